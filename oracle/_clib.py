@@ -1,0 +1,91 @@
+"""ctypes loaders for the oracle's C libraries (test infrastructure only)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_LIB = os.path.join(HERE, "_build", "liboracle.so")
+REF_LIB = os.path.join(HERE, "_ref", "libref_shaders.so")
+REFERENCE_ROOT = os.environ.get("RDV_REFERENCE_ROOT", "/root/reference")
+
+_oracle = None
+_ref = None
+
+
+def build_oracle(verbose: bool = False) -> None:
+    """make -C oracle (C restatement) and, when the reference checkout is
+    present, make -C oracle ref (reference shader functions)."""
+    out = None if verbose else subprocess.DEVNULL
+    subprocess.check_call(["make", "-s", "-C", HERE], stdout=out)
+    if os.path.isdir(os.path.join(REFERENCE_ROOT, "src", "rdv", "shaders")):
+        subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF={REFERENCE_ROOT}"], stdout=out)
+
+
+def oracle_lib() -> ctypes.CDLL:
+    global _oracle
+    if _oracle is None:
+        if not os.path.exists(ORACLE_LIB):
+            build_oracle()
+        lib = ctypes.CDLL(ORACLE_LIB)
+        lib.oracle_mlp_forward.restype = None
+        lib.oracle_mlp_forward.argtypes = [
+            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+            ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+        ]
+        lib.oracle_round.restype = None
+        lib.oracle_round.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]
+        _oracle = lib
+    return _oracle
+
+
+def ref_lib_available() -> bool:
+    if os.path.exists(REF_LIB):
+        return True
+    if os.path.isdir(os.path.join(REFERENCE_ROOT, "src", "rdv", "shaders")):
+        try:
+            build_oracle()
+        except (OSError, subprocess.CalledProcessError):
+            return False
+        return os.path.exists(REF_LIB)
+    return False
+
+
+def ref_lib() -> ctypes.CDLL:
+    """The reference's own scalar shader functions (see ref_shim/)."""
+    global _ref
+    if _ref is None:
+        if not ref_lib_available():
+            raise FileNotFoundError(
+                f"{REF_LIB} is missing and the reference checkout is not present to build it")
+        lib = ctypes.CDLL(REF_LIB)
+        vp, lg, i32, f32 = ctypes.c_void_p, ctypes.c_long, ctypes.c_int, ctypes.c_float
+        lib.ref_mlp_c1.argtypes = [vp, lg, vp, vp, vp]
+        lib.ref_mlp_small.argtypes = [vp, lg, vp, vp, vp]
+        lib.ref_linear_tensor_op_16_24.argtypes = [vp, i32, vp, vp, vp]
+        lib.ref_relu_tensor_op.argtypes = [vp, i32, i32, vp]
+        lib.ref_conv2d_tensor_op_3x3_16_32_16x16.argtypes = [vp, vp, vp, vp]
+        lib.ref_winograd_fwd.argtypes = [vp, vp]
+        lib.ref_winograd_inv.argtypes = [vp, vp]
+        lib.ref_transmittance_rm.argtypes = [f32, f32, vp, vp, f32, f32, f32]
+        lib.ref_transmittance_rm.restype = f32
+        for name in ("ref_mlp_c1", "ref_mlp_small", "ref_linear_tensor_op_16_24", "ref_relu_tensor_op",
+                     "ref_conv2d_tensor_op_3x3_16_32_16x16", "ref_winograd_fwd", "ref_winograd_inv"):
+            getattr(lib, name).restype = None
+        _ref = lib
+    return _ref
+
+
+def ptr(a) -> int:
+    """Address of a C-contiguous numpy array."""
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def ptr_array(arrays) -> ctypes.Array:
+    arr = (ctypes.c_void_p * len(arrays))()
+    for i, a in enumerate(arrays):
+        arr[i] = ptr(a)
+    return arr

@@ -1,0 +1,174 @@
+"""Volume ray-march oracle (test infrastructure only).
+
+Pieces restated from the reference:
+
+* pinhole rays -- rdv/shaders/rendering/cameras.h:1-20 with the defaults of
+  rdv/domain/rendering.py:24-42 (aspect = W/H, fov = pi/4, no jitter);
+* implicit [-1, 1]^3 box slab test -- rdv/shaders/libraries/math_library.h:48-57;
+* miss rule and entry clamp -- rdv/shaders/volumes/raymarching_transmittance.h:11-19;
+* fixed-step absorption -- rdv/shaders/volumes/raymarching_transmittance_trait.h:1-14
+  (``transmittance_rm``);
+* the MLP as a LinearFast chain (float16 staging, fp32 accumulate), see
+  oracle/mlp.py.
+
+The emission-absorption compositing of BASELINE config 4 (128 uniform samples,
+softplus density, sigmoid colour, front-to-back alpha compositing, RGBA with
+A = 1 - T) has no counterpart in the reference; it follows BASELINE.json's
+config text and its parity is unpinned.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .mlp import stage
+
+
+def orbit_pose(frame: int, n_frames: int = 8, radius: float = 3.0, height: float = 0.5) -> np.ndarray:
+    """Camera k of the orbit around the unit cube: origin (r cos t, h, r sin t),
+    target 0, up +y, as [9] float32 (origin | target | up, the layout
+    Cameras expects, rendering.py:37)."""
+    t = 2.0 * math.pi * frame / n_frames
+    return np.array([radius * math.cos(t), height, radius * math.sin(t), 0, 0, 0, 0, 1, 0], dtype=np.float32)
+
+
+def _normalize(v):
+    return v / np.sqrt(np.sum(v * v, axis=-1, keepdims=True))
+
+
+def camera_rays(pose9, width: int, height: int, aspect: float | None = None, fov: float | None = None,
+                row_begin: int = 0, row_end: int | None = None):
+    """cameras.h:1-20 for every pixel (rows row_begin..row_end) -> origins
+    [R, 3], unit directions [R, 3], float32 arithmetic."""
+    if aspect is None:
+        aspect = width / height
+    if fov is None:
+        fov = math.pi / 4
+    row_end = height if row_end is None else row_end
+    pose = np.asarray(pose9, dtype=np.float32).reshape(3, 3)
+    o, t, n = pose[0], pose[1], pose[2]
+    ys, xs = np.meshgrid(np.arange(row_begin, row_end, dtype=np.float32),
+                         np.arange(width, dtype=np.float32), indexing="ij")
+    px = (xs + np.float32(0.5)) / np.float32(width) * np.float32(2.0) - np.float32(1.0)
+    py = (ys + np.float32(0.5)) / np.float32(height) * np.float32(2.0) - np.float32(1.0)
+    sx = px * np.float32(aspect)
+    sy = py
+    sz = np.float32(1.0 / math.tan(np.float32(fov) * 0.5))
+    zaxis = _normalize(t - o)
+    xaxis = _normalize(np.cross(n, zaxis))
+    yaxis = np.cross(zaxis, xaxis)
+    w = xaxis[None, None, :] * sx[..., None] + yaxis[None, None, :] * sy[..., None] + zaxis * sz
+    w = _normalize(w).astype(np.float32).reshape(-1, 3)
+    origins = np.broadcast_to(o, w.shape).astype(np.float32)
+    return origins, w
+
+
+def ray_box(x: np.ndarray, w: np.ndarray):
+    """math_library.h:48-57: slab test against [-1, 1]^3."""
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.float32(1.0) / w
+        xc = -x * inv
+        s = np.abs(inv)
+        tmin = np.max(xc - s, axis=-1)
+        tmax = np.min(xc + s, axis=-1)
+    return tmin.astype(np.float32), tmax.astype(np.float32)
+
+
+def softplus(v):
+    return np.maximum(v, 0.0) + np.log1p(np.exp(-np.abs(v)))
+
+
+def sigmoid(v):
+    return 1.0 / (1.0 + np.exp(-v))
+
+
+def mlp_eval(points: np.ndarray, layers) -> np.ndarray:
+    """LinearFast chain in float64 on staged operands (see mlp.mlp_forward_f64)."""
+    a = points.astype(np.float32)
+    for l in layers:
+        xs = stage(a, l["math"]).astype(np.float64)
+        ws = stage(l["W"], l["math"]).astype(np.float64)
+        out = xs @ ws.T + l["b"].astype(np.float64)
+        if l["relu"]:
+            out = np.maximum(out, 0.0)
+        a = out.astype(np.float32)
+    return a.astype(np.float64)
+
+
+def render_emission_absorption(pose9, width: int, height: int, n_samples: int, layers,
+                               aspect: float | None = None, fov: float | None = None,
+                               row_begin: int = 0, row_end: int | None = None) -> np.ndarray:
+    """RGBA [rows, width, 4] float64."""
+    row_end = height if row_end is None else row_end
+    o, w = camera_rays(pose9, width, height, aspect, fov, row_begin, row_end)
+    tmin, tmax = ray_box(o, w)
+    hit = ~((tmax <= 0) | (tmin > tmax))
+    tmin = np.maximum(tmin, np.float32(0.0))
+    rgba = np.zeros((o.shape[0], 4), dtype=np.float64)
+    idx = np.nonzero(hit)[0]
+    if idx.size:
+        oh, wh = o[idx], w[idx]
+        t0, t1 = tmin[idx], tmax[idx]
+        dt = (t1 - t0) / np.float32(n_samples)
+        i = np.arange(n_samples, dtype=np.float32)
+        ts = t0[:, None] + (i[None, :] + np.float32(0.5)) * dt[:, None]
+        pts = oh[:, None, :] + ts[..., None] * wh[:, None, :]
+        out = mlp_eval(pts.reshape(-1, 3).astype(np.float32), layers).reshape(idx.size, n_samples, -1)
+        sigma = softplus(out[..., 0])
+        rgb = sigmoid(out[..., 1:4])
+        tau = sigma * dt.astype(np.float64)[:, None]
+        alpha = 1.0 - np.exp(-tau)
+        # T_i = prod_{j<i} (1 - alpha_j) = exp(-sum_{j<i} tau_j)
+        excl = np.concatenate([np.zeros((idx.size, 1)), np.cumsum(tau, axis=1)[:, :-1]], axis=1)
+        T = np.exp(-excl)
+        wgt = T * alpha
+        rgba[idx, :3] = np.sum(wgt[..., None] * rgb, axis=1)
+        rgba[idx, 3] = 1.0 - np.exp(-np.sum(tau, axis=1))
+    return rgba.reshape(row_end - row_begin, width, 4)
+
+
+def transmittance_rm(x, w, d, step_size, density_scale, extinction, safety_cap: int = 4096):
+    """raymarching_transmittance_trait.h:1-14 vectorised over rays:
+    tau accumulates extinction(x) * scale * step while d > 0 (at most
+    safety_cap steps); any ray whose tau exceeds 16 returns 0, else exp(-tau).
+    `extinction` maps [R, 3] float32 positions to [R] float32."""
+    x = np.array(x, dtype=np.float32)
+    w = np.asarray(w, dtype=np.float32)
+    d = np.array(d, dtype=np.float32)
+    tau = np.zeros(x.shape[0], dtype=np.float32)
+    dead = np.zeros(x.shape[0], dtype=bool)  # returned 0 early
+    step = np.float32(step_size)
+    scale = np.float32(density_scale)
+    for _ in range(safety_cap):
+        live = (d > 0) & ~dead
+        if not live.any():
+            break
+        ext = extinction(x[live]).astype(np.float32) * scale
+        tau[live] = tau[live] + ext * step
+        over = np.zeros_like(live)
+        over[live] = tau[live] > 16
+        dead |= over
+        d[live] = d[live] - step
+        x[live] = x[live] + step * w[live]
+    out = np.exp(-tau.astype(np.float64)).astype(np.float32)
+    out[dead] = 0.0
+    return out
+
+
+def raymarching_transmittance(origins, dirs, step_size, density_scale, extinction):
+    """RaymarchingTransmittance.forward (raymarching_transmittance.h:1-21) with
+    the identity transform: slab test, miss -> 1, entry clamp, then
+    transmittance_rm over d = tMax - tMin."""
+    o = np.asarray(origins, dtype=np.float32)
+    w = np.asarray(dirs, dtype=np.float32)
+    tmin, tmax = ray_box(o, w)
+    miss = (tmax <= 0) | (tmin > tmax)
+    tmin = np.maximum(tmin, np.float32(0.0))
+    x = o + w * tmin[:, None]
+    d = tmax - tmin
+    out = np.ones(o.shape[0], dtype=np.float32)
+    hit = ~miss
+    if hit.any():
+        out[hit] = transmittance_rm(x[hit], w[hit], d[hit], step_size, density_scale, extinction)
+    return out

@@ -1,0 +1,65 @@
+// Test infrastructure only (parity checker, never shipped or measured).
+//
+// A minimal C++ stand-in for the handful of GLSL constructs used by the
+// reference shader functions that this directory compiles *from where they
+// lie* in the reference checkout (rdv/shaders/...). Only functions whose
+// bodies are plain scalar/array arithmetic are compiled this way:
+//
+//   maps/linear.h                       Linear.forward (exact fp32 per row)
+//   maps/relu.h                         ReLU.forward
+//   maps/composite.h                    Composite.forward (f(g(x)))
+//   tensors/linear_tensor_op.h          LinearTensorOp.forward (fp32 4x8 tiles)
+//   tensors/relu_tensor_op.h            ReLUTensorOp.forward
+//   tensors/conv2d_tensor_op.h          Conv2DTensorOp.forward (fp32 direct conv)
+//   tensors/conv2d_tensor_op_winograd3x3.h  _winograd_fwd / _winograd_inv
+//   volumes/raymarching_transmittance_trait.h  transmittance_rm
+//
+// Cooperative-matrix code in those files sits behind
+// RDV_COOPERATIVE_MATRIX_SUPPORT, which is never defined here, so only the
+// portable scalar paths are compiled.
+#pragma once
+#include <cmath>
+#include <cstdint>
+
+typedef unsigned int uint;
+
+struct rdv_uvec3 { unsigned x, y, z; };
+
+// Per-"invocation" builtins; the wrappers set them before every call.
+static rdv_uvec3 gl_LocalInvocationID = {0, 0, 0};
+static rdv_uvec3 gl_GlobalInvocationID = {0, 0, 0};
+static rdv_uvec3 gl_WorkGroupID = {0, 0, 0};
+
+// One invocation at a time: the workgroup-uniformity test of
+// cooperative_library.h can never see 32 live lanes, so it reports false and
+// every node takes its independent (per-thread) path, exactly as a partially
+// occupied workgroup does in the reference.
+static inline bool all_thread_sync(uint) { return false; }
+
+struct rdv_vec3 {
+    float x, y, z;
+    rdv_vec3() : x(0), y(0), z(0) {}
+    rdv_vec3(float a, float b, float c) : x(a), y(b), z(c) {}
+};
+static inline rdv_vec3 operator*(float s, rdv_vec3 v) { return rdv_vec3(s * v.x, s * v.y, s * v.z); }
+static inline rdv_vec3 operator*(rdv_vec3 v, float s) { return rdv_vec3(s * v.x, s * v.y, s * v.z); }
+static inline rdv_vec3 operator+(rdv_vec3 a, rdv_vec3 b) { return rdv_vec3(a.x + b.x, a.y + b.y, a.z + b.z); }
+static inline rdv_vec3& operator+=(rdv_vec3& a, rdv_vec3 b) { a.x += b.x; a.y += b.y; a.z += b.z; return a; }
+
+// GLSL max(float, float-literal) - the literal is a double in C++.
+static inline float max(float a, double b) { return a > (float)b ? a : (float)b; }
+static inline float max(double a, float b) { return (float)a > b ? (float)a : b; }
+static inline float max(float a, float b) { return a > b ? a : b; }
+static inline int min(int a, int b) { return a < b ? a : b; }
+
+#define vec3 rdv_vec3
+#define shared static
+#define barrier() ((void)0)
+#define deref(x) (x)
+#define resolve(x) (x)
+#define RDV_CONCAT_(a, b) a##b
+#define RDV_CONCAT(a, b) RDV_CONCAT_(a, b)
+// GLSL parameter qualifiers: arrays decay to pointers, so `out float v[16]`
+// still writes through to the caller.
+#define in
+#define out

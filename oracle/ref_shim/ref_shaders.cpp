@@ -1,0 +1,281 @@
+// Test infrastructure only (parity checker, never shipped or measured).
+//
+// Compiles a few of the reference's own GLSL functions as C++ (see
+// glsl_prelude.hpp for which and why) and exposes them through a small
+// extern "C" surface used by tests/golden/make_golden.py and by the CPU
+// parity tests. The shader files are #included from the reference
+// checkout (REF_SHADERS include path, set by oracle/Makefile); nothing of
+// them is copied into this repository.
+//
+// Node layouts below mirror the field order the reference declares for each
+// node type (rdv/domain/nn.py: _LinearBase.weight/bias/id,
+// LinearTensorOp.x_buf/weight/bias + TensorOperation.shape/result,
+// Conv2DTensorOp.x_buf/weight/bias).
+#include "glsl_prelude.hpp"
+
+// ---------------------------------------------------------------------------
+// Map path: Linear (maps/linear.h), ReLU (maps/relu.h), Composite
+// (maps/composite.h). Every distinct (IN, OUT) specialisation is a distinct
+// node type, exactly like the reference's per-generic GLSL struct, so C++
+// overload resolution plays the role of the megakernel's forward() overloads.
+// ---------------------------------------------------------------------------
+#define DECLARE_LINEAR(NAME, IN_, OUT_)                     \
+    struct NAME { float* weight; float* bias; int id; };
+
+DECLARE_LINEAR(Lin_3_64, 3, 64)
+DECLARE_LINEAR(Lin_64_64, 64, 64)
+DECLARE_LINEAR(Lin_64_4, 64, 4)
+DECLARE_LINEAR(Lin_5_16, 5, 16)
+DECLARE_LINEAR(Lin_16_7, 16, 7)
+struct Relu_64 { int unused; };
+struct Relu_16 { int unused; };
+
+#define RDV_NODE Lin_3_64
+#define IN 3
+#define OUT 64
+#include "maps/linear.h"
+#undef IN
+#undef OUT
+#undef RDV_NODE
+
+#define RDV_NODE Lin_64_64
+#define IN 64
+#define OUT 64
+#include "maps/linear.h"
+#undef IN
+#undef OUT
+#undef RDV_NODE
+
+#define RDV_NODE Lin_64_4
+#define IN 64
+#define OUT 4
+#include "maps/linear.h"
+#undef IN
+#undef OUT
+#undef RDV_NODE
+
+#define RDV_NODE Lin_5_16
+#define IN 5
+#define OUT 16
+#include "maps/linear.h"
+#undef IN
+#undef OUT
+#undef RDV_NODE
+
+#define RDV_NODE Lin_16_7
+#define IN 16
+#define OUT 7
+#include "maps/linear.h"
+#undef IN
+#undef OUT
+#undef RDV_NODE
+
+#define RDV_NODE Relu_64
+#define IN 64
+#define OUT 64
+#include "maps/relu.h"
+#undef IN
+#undef OUT
+#undef RDV_NODE
+
+#define RDV_NODE Relu_16
+#define IN 16
+#define OUT 16
+#include "maps/relu.h"
+#undef IN
+#undef OUT
+#undef RDV_NODE
+
+// `a >> b` builds Composite(f=b, g=a) (rdv/maths/__init__.py Map.__rshift__),
+// so `L0 >> relu >> L1 >> relu >> L2 >> relu >> L3` nests left to right.
+#define DECLARE_COMPOSITE(NAME, F, G, IN_, OUT_, V_)       \
+    struct NAME { F f; G g; };                             \
+
+DECLARE_COMPOSITE(C1_a, Relu_64, Lin_3_64, 3, 64, 64)
+DECLARE_COMPOSITE(C1_b, Lin_64_64, C1_a, 3, 64, 64)
+DECLARE_COMPOSITE(C1_c, Relu_64, C1_b, 3, 64, 64)
+DECLARE_COMPOSITE(C1_d, Lin_64_64, C1_c, 3, 64, 64)
+DECLARE_COMPOSITE(C1_e, Relu_64, C1_d, 3, 64, 64)
+DECLARE_COMPOSITE(C1_f, Lin_64_4, C1_e, 3, 4, 64)
+DECLARE_COMPOSITE(S_a, Relu_16, Lin_5_16, 5, 16, 16)
+DECLARE_COMPOSITE(S_b, Lin_16_7, S_a, 5, 7, 16)
+
+#define IN 3
+#define V 64
+#define OUT 64
+#define RDV_NODE C1_a
+#include "maps/composite.h"
+#undef RDV_NODE
+#define RDV_NODE C1_b
+#include "maps/composite.h"
+#undef RDV_NODE
+#define RDV_NODE C1_c
+#include "maps/composite.h"
+#undef RDV_NODE
+#define RDV_NODE C1_d
+#include "maps/composite.h"
+#undef RDV_NODE
+#define RDV_NODE C1_e
+#include "maps/composite.h"
+#undef RDV_NODE
+#undef OUT
+#define OUT 4
+#define RDV_NODE C1_f
+#include "maps/composite.h"
+#undef RDV_NODE
+#undef OUT
+#undef V
+#undef IN
+
+#define IN 5
+#define V 16
+#define OUT 16
+#define RDV_NODE S_a
+#include "maps/composite.h"
+#undef RDV_NODE
+#undef OUT
+#define OUT 7
+#define RDV_NODE S_b
+#include "maps/composite.h"
+#undef RDV_NODE
+#undef OUT
+#undef V
+#undef IN
+
+// ---------------------------------------------------------------------------
+// TensorOperation path (fp32): LinearTensorOp, ReLUTensorOp, Conv2DTensorOp.
+// ---------------------------------------------------------------------------
+struct LinTO_16_24 { int shape[2]; float* result; float* x_buf; float* weight; float* bias; };
+#define RDV_NODE LinTO_16_24
+#define INF 16
+#define OUTF 24
+#include "tensors/linear_tensor_op.h"
+#undef INF
+#undef OUTF
+#undef RDV_NODE
+
+struct ReluTO { int shape[2]; float* result; float* x_buf; };
+#define RDV_NODE ReluTO
+#include "tensors/relu_tensor_op.h"
+#undef RDV_NODE
+
+struct ConvTO { int shape[2]; float* result; float* x_buf; float* weight; float* bias; };
+#define RDV_NODE ConvTO
+#define KH 3
+#define KW 3
+#define CIN 16
+#define COUT 32
+#define H 16
+#define W 16
+#include "tensors/conv2d_tensor_op.h"
+#undef RDV_NODE
+#undef KH
+#undef KW
+#undef CIN
+#undef COUT
+#undef H
+#undef W
+
+// Winograd transforms: the cooperative-matrix forward() of this file is
+// compiled out (RDV_COOPERATIVE_MATRIX_SUPPORT undefined), leaving the two
+// scalar transforms _winograd_fwd / _winograd_inv.
+struct WinoTO { int unused; };
+#define RDV_NODE WinoTO
+#define CIN 16
+#define COUT 16
+#define H 16
+#define W 16
+#include "tensors/conv2d_tensor_op_winograd3x3.h"
+#undef RDV_NODE
+#undef CIN
+#undef COUT
+#undef H
+#undef W
+
+// Fixed-step transmittance (volumes/raymarching_transmittance_trait.h). The
+// extinction Map is supplied here as an analytic field so the marching rule
+// itself (step, early-out at tau > 16, d > 0 loop guard, safety cap) is what
+// gets pinned.
+struct RmNode { float c0, c1; };
+static float extinction(RmNode node, vec3 x) {
+    return node.c0 + node.c1 * (x.x * x.x + x.y * x.y + x.z * x.z);
+}
+#define RDV_NODE RmNode
+#include "volumes/raymarching_transmittance_trait.h"
+#undef RDV_NODE
+
+// ---------------------------------------------------------------------------
+// extern "C" surface
+// ---------------------------------------------------------------------------
+extern "C" {
+
+// C1 architecture 3->64->64->64->4 with ReLU between,
+// evaluated row by row through the reference's own Composite chain.
+void ref_mlp_c1(const float* x, long n, float* const* W, float* const* b, float* y) {
+    C1_f net;
+    net.f = Lin_64_4{W[3], b[3], 0};
+    net.g.f = Relu_64{0};
+    net.g.g.f = Lin_64_64{W[2], b[2], 1};
+    net.g.g.g.f = Relu_64{0};
+    net.g.g.g.g.f = Lin_64_64{W[1], b[1], 0};
+    net.g.g.g.g.g.f = Relu_64{0};
+    net.g.g.g.g.g.g = Lin_3_64{W[0], b[0], 0};
+    for (long r = 0; r < n; ++r) {
+        float in_row[3] = {x[r * 3 + 0], x[r * 3 + 1], x[r * 3 + 2]};
+        forward(net, in_row, y + r * 4);
+    }
+}
+
+// Small odd-width chain 5->16->ReLU->7.
+void ref_mlp_small(const float* x, long n, float* const* W, float* const* b, float* y) {
+    S_b net;
+    net.f = Lin_16_7{W[1], b[1], 0};
+    net.g.f = Relu_16{0};
+    net.g.g = Lin_5_16{W[0], b[0], 0};
+    for (long r = 0; r < n; ++r) {
+        float in_row[5];
+        for (int k = 0; k < 5; ++k) in_row[k] = x[r * 5 + k];
+        forward(net, in_row, y + r * 7);
+    }
+}
+
+// LinearTensorOp fp32, INF=16, OUTF=24; batch must be a multiple of 4.
+void ref_linear_tensor_op_16_24(const float* x, int batch, const float* Wt, const float* b, float* y) {
+    LinTO_16_24 node;
+    node.shape[0] = batch; node.shape[1] = 24;
+    node.result = y; node.x_buf = const_cast<float*>(x);
+    node.weight = const_cast<float*>(Wt); node.bias = const_cast<float*>(b);
+    int tiles = (batch / 4) * (24 / 8);
+    for (int t = 0; t < tiles; ++t) { gl_GlobalInvocationID.x = t; forward(node); }
+}
+
+void ref_relu_tensor_op(const float* x, int rows, int cols, float* y) {
+    ReluTO node;
+    node.shape[0] = rows; node.shape[1] = cols;
+    node.result = y; node.x_buf = const_cast<float*>(x);
+    int tiles = (rows / 4) * (cols / 8);
+    for (int t = 0; t < tiles; ++t) { gl_GlobalInvocationID.x = t; forward(node); }
+}
+
+// Conv2DTensorOp fp32 'same' 3x3, H=W=16, CIN=16, COUT=32; x [H*W, CIN],
+// weight [3, 3, CIN, COUT].
+void ref_conv2d_tensor_op_3x3_16_32_16x16(const float* x, const float* w, const float* b, float* y) {
+    ConvTO node;
+    node.shape[0] = 16 * 16; node.shape[1] = 32;
+    node.result = y; node.x_buf = const_cast<float*>(x);
+    node.weight = const_cast<float*>(w); node.bias = const_cast<float*>(b);
+    int tiles = (16 * 16 / 4) * (32 / 8);
+    for (int t = 0; t < tiles; ++t) { gl_GlobalInvocationID.x = t; forward(node); }
+}
+
+void ref_winograd_fwd(const float* d, float* V) { _winograd_fwd(const_cast<float*>(d), V); }
+void ref_winograd_inv(const float* M, float* Y) { _winograd_inv(const_cast<float*>(M), Y); }
+
+float ref_transmittance_rm(float c0, float c1, const float* x, const float* w, float d,
+                           float step_size, float density_scale) {
+    RmNode node{c0, c1};
+    return transmittance_rm(node, vec3(x[0], x[1], x[2]), vec3(w[0], w[1], w[2]), d, step_size,
+                            density_scale);
+}
+
+}  // extern "C"

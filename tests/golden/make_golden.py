@@ -1,0 +1,150 @@
+"""Regenerates the golden fixtures in this directory from the reference itself.
+
+Run in a checkout where the reference is present (default /root/reference):
+
+    python tests/golden/make_golden.py
+
+Two sources, both the reference's own code:
+
+* ``oracle/_ref/libref_shaders.so`` -- the reference's scalar GLSL functions
+  (maps/linear.h, relu.h, composite.h, tensors/linear_tensor_op.h,
+  relu_tensor_op.h, conv2d_tensor_op.h, the Winograd transforms, and
+  volumes/raymarching_transmittance_trait.h) compiled as C++ from the
+  reference checkout by ``make -C oracle ref``;
+* ``rdv/domain/nn.py``'s torch helper ``_winograd_transform_weight`` and its
+  ``_WINOGRAD_G`` table, executed from the reference source. The package
+  itself cannot be imported (it needs the external ``vk`` module at import
+  time), so the two definitions are lifted out of the file with ``ast`` and
+  executed on their own.
+
+The fixtures are small ``.npz`` files; the CPU tests compare the oracle's
+restatements against them, so they keep pinning the oracle where the
+reference checkout is absent (e.g. the GPU box).
+"""
+from __future__ import annotations
+
+import ast
+import ctypes
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from oracle._clib import REFERENCE_ROOT, ptr, ptr_array, ref_lib  # noqa: E402
+
+
+def xavier_uniform(rng, out_f, in_f):
+    bound = np.sqrt(6.0 / (in_f + out_f))
+    return rng.uniform(-bound, bound, size=(out_f, in_f)).astype(np.float32)
+
+
+def reference_python_helpers():
+    """Executes _WINOGRAD_G and _winograd_transform_weight from the
+    reference's nn.py in an isolated namespace."""
+    path = os.path.join(REFERENCE_ROOT, "src", "rdv", "domain", "nn.py")
+    tree = ast.parse(open(path).read(), filename=path)
+    wanted = {"_WINOGRAD_G", "_winograd_transform_weight"}
+    body = []
+    for node in tree.body:
+        if isinstance(node, ast.FunctionDef) and node.name in wanted:
+            body.append(node)
+        elif isinstance(node, ast.Assign) and any(getattr(t, "id", None) in wanted for t in node.targets):
+            body.append(node)
+    mod = ast.Module(body=body, type_ignores=[])
+    ns: dict = {}
+    exec(compile(mod, path, "exec"), ns)
+    return ns
+
+
+class _TorchHolder:
+    """Stands in for RDVObject: the helper only calls .as_tensor('torch')."""
+
+    def __init__(self, t):
+        self.t = t
+
+    def as_tensor(self, backend):
+        assert backend == "torch"
+        return self.t
+
+
+def main():
+    lib = ref_lib()
+    rng = np.random.default_rng(20240601)
+    out = {}
+
+    # --- Map chain, BASELINE config-1 architecture (3->64->64->64->4) -------
+    dims = [3, 64, 64, 64, 4]
+    W = [xavier_uniform(rng, dims[i + 1], dims[i]) for i in range(4)]
+    b = [rng.uniform(-0.1, 0.1, size=dims[i + 1]).astype(np.float32) for i in range(4)]
+    x = rng.uniform(-1, 1, size=(96, 3)).astype(np.float32)
+    y = np.zeros((96, 4), dtype=np.float32)
+    lib.ref_mlp_c1(ptr(x), x.shape[0], ptr_array(W), ptr_array(b), ptr(y))
+    np.savez_compressed(os.path.join(HERE, "mlp_c1.npz"), x=x, y=y,
+                        **{f"W{i}": W[i] for i in range(4)}, **{f"b{i}": b[i] for i in range(4)})
+
+    # --- odd widths 5 -> 16 -> ReLU -> 7 -------------------------------------
+    W = [xavier_uniform(rng, 16, 5), xavier_uniform(rng, 7, 16)]
+    b = [rng.uniform(-0.5, 0.5, size=16).astype(np.float32), rng.uniform(-0.5, 0.5, size=7).astype(np.float32)]
+    x = rng.standard_normal((37, 5)).astype(np.float32)
+    y = np.zeros((37, 7), dtype=np.float32)
+    lib.ref_mlp_small(ptr(x), x.shape[0], ptr_array(W), ptr_array(b), ptr(y))
+    np.savez_compressed(os.path.join(HERE, "mlp_small.npz"), x=x, y=y, W0=W[0], W1=W[1], b0=b[0], b1=b[1])
+
+    # --- TensorOperation fp32 ------------------------------------------------
+    x = rng.standard_normal((20, 16)).astype(np.float32)
+    Wt = xavier_uniform(rng, 24, 16)
+    bt = rng.uniform(-0.5, 0.5, size=24).astype(np.float32)
+    y = np.zeros((20, 24), dtype=np.float32)
+    lib.ref_linear_tensor_op_16_24(ptr(x), 20, ptr(Wt), ptr(bt), ptr(y))
+    xr = rng.standard_normal((8, 16)).astype(np.float32)
+    yr = np.zeros_like(xr)
+    lib.ref_relu_tensor_op(ptr(xr), 8, 16, ptr(yr))
+    xc = rng.standard_normal((16 * 16, 16)).astype(np.float32)
+    wc = (rng.standard_normal((3, 3, 16, 32)) * np.sqrt(2.0 / (9 * 16))).astype(np.float32)
+    bc = rng.uniform(-0.1, 0.1, size=32).astype(np.float32)
+    yc = np.zeros((16 * 16, 32), dtype=np.float32)
+    lib.ref_conv2d_tensor_op_3x3_16_32_16x16(ptr(xc), ptr(wc), ptr(bc), ptr(yc))
+    np.savez_compressed(os.path.join(HERE, "tensor_ops.npz"), lin_x=x, lin_W=Wt, lin_b=bt, lin_y=y,
+                        relu_x=xr, relu_y=yr, conv_x=xc, conv_w=wc, conv_b=bc, conv_y=yc)
+
+    # --- Winograd scalar transforms and the filter transform ----------------
+    d = rng.standard_normal((64, 16)).astype(np.float32)
+    V = np.zeros_like(d)
+    for i in range(64):
+        lib.ref_winograd_fwd(ptr(d[i]), ptr(V[i]))
+    M = rng.standard_normal((64, 16)).astype(np.float32)
+    Y = np.zeros((64, 4), dtype=np.float32)
+    for i in range(64):
+        lib.ref_winograd_inv(ptr(M[i]), ptr(Y[i]))
+    import torch
+    ns = reference_python_helpers()
+    wf = (rng.standard_normal((3, 3, 16, 32)) * 0.2).astype(np.float32)
+    U = ns["_winograd_transform_weight"](_TorchHolder(torch.from_numpy(wf)), 16, 32).numpy()
+    np.savez_compressed(os.path.join(HERE, "winograd.npz"), d=d, V=V, M=M, Y=Y, w=wf, U=U,
+                        G=np.array(ns["_WINOGRAD_G"], dtype=np.float64))
+
+    # --- fixed-step transmittance ---------------------------------------------
+    nr = 48
+    xs = rng.uniform(-1, 1, size=(nr, 3)).astype(np.float32)
+    ws = rng.standard_normal((nr, 3)).astype(np.float32)
+    ws /= np.linalg.norm(ws, axis=1, keepdims=True)
+    ds = rng.uniform(0.0, 2.5, size=nr).astype(np.float32)
+    ds[:4] = [0.0, -0.1, 1e-3, 3.0]
+    c0 = rng.uniform(0.0, 3.0, size=nr).astype(np.float32)
+    c1 = rng.uniform(0.0, 8.0, size=nr).astype(np.float32)
+    c0[4:8] = 40.0  # tau crosses 16 -> early return 0
+    T = np.zeros(nr, dtype=np.float32)
+    for i in range(nr):
+        T[i] = lib.ref_transmittance_rm(ctypes.c_float(c0[i]), ctypes.c_float(c1[i]), ptr(xs[i]), ptr(ws[i]),
+                                        ctypes.c_float(ds[i]), ctypes.c_float(0.05), ctypes.c_float(1.0))
+    np.savez_compressed(os.path.join(HERE, "transmittance.npz"), x=xs, w=ws, d=ds, c0=c0, c1=c1, T=T,
+                        step=np.float32(0.05), scale=np.float32(1.0))
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

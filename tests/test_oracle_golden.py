@@ -1,0 +1,144 @@
+"""Pins the CPU oracle against golden vectors produced by the reference's own
+code (tests/golden/make_golden.py). Runs without a GPU."""
+import numpy as np
+import pytest
+
+from oracle import mlp as omlp
+from oracle import raymarch as orm
+from oracle import winograd as owg
+from oracle._clib import ref_lib, ref_lib_available
+
+
+def _layers_from(g, n, relu_last=False, math="f32"):
+    return [{"W": g[f"W{i}"], "b": g[f"b{i}"], "math": math, "relu": (i < n - 1) or relu_last} for i in range(n)]
+
+
+def test_c_oracle_fp32_chain_is_bit_exact_vs_reference_composite(golden):
+    g = golden("mlp_c1.npz")
+    y = omlp.mlp_forward(g["x"], _layers_from(g, 4))
+    np.testing.assert_array_equal(y, g["y"])
+
+
+def test_c_oracle_odd_widths_bit_exact(golden):
+    g = golden("mlp_small.npz")
+    y = omlp.mlp_forward(g["x"], _layers_from(g, 2))
+    np.testing.assert_array_equal(y, g["y"])
+
+
+def test_fp32_oracle_f64_agrees_within_fp32_tolerance(golden):
+    g = golden("mlp_c1.npz")
+    y = omlp.mlp_forward_f64(g["x"], _layers_from(g, 4))
+    assert omlp.within_tolerance(g["y"], y, 1e-5)
+
+
+def test_linear_tensor_op_matches_reference(golden):
+    g = golden("tensor_ops.npz")
+    layers = [{"W": g["lin_W"], "b": g["lin_b"], "math": "f32", "relu": False}]
+    y = omlp.mlp_forward(g["lin_x"], layers)
+    # LinearTensorOp seeds acc with bias and accumulates k ascending in 8-wide
+    # chunks -- the same sequence as the Map path, so bit-exact.
+    np.testing.assert_array_equal(y, g["lin_y"])
+    np.testing.assert_array_equal(np.maximum(g["relu_x"], 0), g["relu_y"])
+
+
+def test_direct_conv_oracle_matches_reference_conv2d_tensor_op(golden):
+    g = golden("tensor_ops.npz")
+    x = g["conv_x"].reshape(1, 16, 16, 16)
+    y = owg.conv3x3_direct(x, g["conv_w"], g["conv_b"]).reshape(256, 32)
+    nw, el = omlp.rel_errors(g["conv_y"], y)
+    assert nw < 1e-6 and el < 1e-5, (nw, el)
+
+
+def test_winograd_scalar_transforms_bit_exact(golden):
+    g = golden("winograd.npz")
+    np.testing.assert_array_equal(owg.winograd_fwd_f23(g["d"]), g["V"])
+    np.testing.assert_array_equal(owg.winograd_inv_f23(g["M"]), g["Y"])
+    # the matrix form used by the batched oracle is the same linear map
+    d = g["d"].astype(np.float64).reshape(-1, 4, 4)
+    V = np.einsum("ij,njk,lk->nil", owg.BT_F23, d, owg.BT_F23).reshape(-1, 16)
+    np.testing.assert_allclose(V, g["V"], rtol=0, atol=1e-5)
+    M = g["M"].astype(np.float64).reshape(-1, 4, 4)
+    Y = np.einsum("pi,nij,qj->npq", owg.AT_F23, M, owg.AT_F23).reshape(-1, 4)
+    np.testing.assert_allclose(Y, g["Y"], rtol=0, atol=1e-5)
+
+
+def test_winograd_filter_transform_matches_reference_torch_helper(golden):
+    g = golden("winograd.npz")
+    np.testing.assert_array_equal(owg.G_F23, g["G"])
+    U = owg.filter_transform(g["w"], "F2x2")
+    np.testing.assert_array_equal(U.reshape(-1).astype(np.float16), g["U"])
+
+
+@pytest.mark.parametrize("variant", ["F2x2", "F4x4"])
+def test_winograd_identity_in_float64(variant):
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((2, 8, 12, 16)).astype(np.float32)
+    w = (rng.standard_normal((3, 3, 16, 8)) * 0.1).astype(np.float32)
+    b = rng.standard_normal(8).astype(np.float32)
+    d = owg.conv3x3_direct(x, w, b)
+    y = owg.conv3x3_winograd(x, w, b, variant, staged=False)
+    np.testing.assert_allclose(y, d, rtol=0, atol=1e-12)
+
+
+def test_toom_cook_reproduces_reference_f23_matrices():
+    AT, G, BT = owg.toom_cook_matrices([0.0, 1.0, -1.0], 2)
+    # same transforms up to the sign convention of the first point's row
+    np.testing.assert_allclose(np.abs(AT), np.abs(owg.AT_F23))
+    np.testing.assert_allclose(np.abs(G), np.abs(owg.G_F23))
+    np.testing.assert_allclose(np.abs(BT), np.abs(owg.BT_F23))
+
+
+def test_transmittance_restatement_matches_reference(golden):
+    g = golden("transmittance.npz")
+    T = np.empty_like(g["T"])
+    for i in range(T.shape[0]):
+        c0, c1 = g["c0"][i], g["c1"][i]
+
+        def ext(p, c0=c0, c1=c1):
+            return np.float32(c0) + np.float32(c1) * np.sum(p * p, axis=-1, dtype=np.float32)
+
+        T[i] = orm.transmittance_rm(g["x"][i:i + 1], g["w"][i:i + 1], g["d"][i:i + 1], g["step"], g["scale"], ext)[0]
+    np.testing.assert_allclose(T, g["T"], rtol=2e-6, atol=1e-7)
+    assert np.all(T[4:8] == 0.0)
+
+
+@pytest.mark.skipif(not ref_lib_available(), reason="reference shader library not built")
+def test_live_reference_library_agrees_with_fixture(golden):
+    """Where oracle/_ref is present, re-run one fixture through it."""
+    g = golden("mlp_small.npz")
+    from oracle._clib import ptr, ptr_array
+
+    y = np.zeros_like(g["y"])
+    ref_lib().ref_mlp_small(ptr(g["x"]), g["x"].shape[0], ptr_array([g["W0"], g["W1"]]),
+                            ptr_array([g["b0"], g["b1"]]), ptr(y))
+    np.testing.assert_array_equal(y, g["y"])
+
+
+def test_fp16_staging_semantics():
+    """LinearFast: products of float16-staged operands summed in fp32 from 0,
+    bias added after; the trailing partial 32-row workgroup runs fp32."""
+    rng = np.random.default_rng(3)
+    layers = [{"W": rng.standard_normal((16, 8)).astype(np.float32), "b": rng.standard_normal(16).astype(np.float32),
+               "math": "f16", "relu": True},
+              {"W": rng.standard_normal((4, 16)).astype(np.float32), "b": rng.standard_normal(4).astype(np.float32),
+               "math": "f16", "relu": False}]
+    x = rng.standard_normal((70, 8)).astype(np.float32)
+    y = omlp.mlp_forward(x, layers, tail_exact=True)
+    ref16 = omlp.mlp_forward_f64(x, layers)
+    f32_layers = [dict(l, math="f32") for l in layers]
+    ref32 = omlp.mlp_forward_f64(x, f32_layers)
+    assert omlp.within_tolerance(y[:64], ref16[:64], 1e-5)
+    assert omlp.within_tolerance(y[64:], ref32[64:], 1e-5)
+    # the f16 rows really differ from exact fp32
+    assert not np.allclose(y[:64], ref32[:64], rtol=1e-6, atol=0)
+
+
+def test_camera_rays_geometry():
+    pose = orm.orbit_pose(0)
+    o, w = orm.camera_rays(pose, 8, 6)
+    assert o.shape == (48, 3) and w.shape == (48, 3)
+    np.testing.assert_allclose(np.linalg.norm(w, axis=1), 1.0, atol=1e-6)
+    # centre of the image looks at the target (the origin)
+    centre = (w[2 * 8 + 3] + w[2 * 8 + 4] + w[3 * 8 + 3] + w[3 * 8 + 4]) / 4
+    to_target = -pose[:3] / np.linalg.norm(pose[:3])
+    assert np.dot(centre / np.linalg.norm(centre), to_target) > 0.99
