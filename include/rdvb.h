@@ -1,0 +1,114 @@
+/*
+ * rdvb -- C ABI of the B200 (sm_100a) implementation of Rendervous's
+ * data-parallel hot path: fused small-MLP evaluation, Winograd 3x3
+ * convolution and the MLP volume ray-march.
+ *
+ * Conventions
+ *  - Every entry point returns an int status: RDVB_OK (0) or a negative
+ *    RDVB_ERR_* code; rdvb_last_error() gives the calling thread's message.
+ *  - Tensor arguments are DEVICE pointers owned by the caller, row-major,
+ *    densely packed. Small descriptor arrays (dims, flags, pointer lists) are
+ *    HOST arrays read before the call returns.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *    stream). Calls are asynchronous and stream-ordered, like the kernels
+ *    they launch; they never synchronize unless documented.
+ *  - The reference dispatches each operator through a Vulkan compute
+ *    "megakernel" and blocks in vk.submit_and_wait
+ *    (rdv/core/_core.py:2799-2886); these entry points replace that
+ *    dispatch for the operators named beside each one.
+ */
+#ifndef RDVB_H
+#define RDVB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RDVB_OK 0
+#define RDVB_ERR_INVALID_ARG (-1)
+#define RDVB_ERR_UNSUPPORTED (-2)
+#define RDVB_ERR_CUDA (-3)
+#define RDVB_ERR_DEVICE_STATUS (-4) /* a kernel reported a bounded-wait timeout */
+
+/* element types */
+#define RDVB_F32 0
+#define RDVB_F16 1
+#define RDVB_BF16 2
+
+/* per-layer flags of the MLP chain: bits 0-1 arithmetic, bit 2 ReLU after */
+#define RDVB_MATH_F32 0  /* Linear: exact fp32 (rdv/shaders/maps/linear.h) */
+#define RDVB_MATH_F16 1  /* LinearFast: float16 operands, fp32 accumulate (maps/linear_fast.h) */
+#define RDVB_MATH_BF16 2 /* bfloat16 operands, fp32 accumulate (B200 extension) */
+#define RDVB_LAYER_RELU 4
+
+/* Winograd variants */
+#define RDVB_WINOGRAD_F2X2 0 /* F(2x2,3x3), the reference's algorithm */
+#define RDVB_WINOGRAD_F4X4 1 /* F(4x4,3x3), B200 extension */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int rdvb_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* rdvb_last_error(void);
+
+/* Synchronizes the current device, then reads (and, if `clear`, resets) the
+ * device status word that kernels set when a bounded wait expires. Returns
+ * RDVB_OK and writes the word to *status (0 = healthy). */
+int rdvb_device_status(int clear, uint32_t* status);
+
+/* ---------------------------------------------------------------- MLP ----
+ * A chain of n_layers affine layers, dims[0] -> dims[1] -> ... -> dims[n],
+ * each y = W x + b with W [dims[l+1], dims[l]] (PyTorch nn.Linear layout) and
+ * b [dims[l+1]], optionally followed by ReLU.
+ *
+ * Replaces: Map.__call__ of a `linear(W,b,f16) >> relu >> ...` Composite
+ * (rdv/maths/__init__.py:1451-1487, Composite :1700-1728, MapEvaluator
+ * :1569-1610; layer arithmetic rdv/shaders/maps/linear.h:15-44 and
+ * linear_fast.h:39-109) and the single-layer TensorOperations
+ * LinearTensorOp{,Fast,Mine,Simple,Small} (rdv/domain/nn.py:377-411,
+ * 541-605, 1153-1411).
+ */
+
+/* Bytes of the packed-weight buffer rdvb_mlp_pack writes for these dims
+ * (0 if the chain cannot use the tensor-core path). */
+int64_t rdvb_mlp_packed_bytes(int n_layers, const int* dims);
+
+/* Converts fp32 weights/biases (device pointers, one per layer) into the
+ * tensor-core image: float16 (operand = RDVB_F16) or bfloat16 (RDVB_BF16)
+ * K-major 128-byte-swizzled blocks, biases padded to 16. `packed` must hold
+ * rdvb_mlp_packed_bytes() bytes, 256-byte aligned. The reference re-reads
+ * fp32 weights at every dispatch (linear_fast.h:81-82); callers that change
+ * weights in place call this again. */
+int rdvb_mlp_pack(int n_layers, const int* dims, const float* const* weights, const float* const* biases,
+                  int operand, void* packed, void* stream);
+
+/* y[n_rows, dims[n]] (fp32) = chain(x[n_rows, dims[0]]).
+ *  x_dtype      RDVB_F32 / RDVB_F16 / RDVB_BF16
+ *  layer_flags  n_layers entries: RDVB_MATH_* | (RDVB_LAYER_RELU)
+ *  input_relu   apply ReLU to x first (a chain that starts with relu)
+ *  tail_exact   1: rows of a trailing partial 32-row group run every layer in
+ *               exact fp32, as the reference's LinearFast falls back when its
+ *               32-lane workgroup is not full (linear_fast.h:44,102-108)
+ *  packed       rdvb_mlp_pack output for the same weights (required when any
+ *               layer is F16/BF16 and the chain fits the tensor-core path;
+ *               may be NULL for all-fp32 chains)
+ *  weights, biases  the fp32 device tensors (used by the CUDA-core path)
+ * Chains whose every layer is F16 (or every layer BF16) with widths <= 128
+ * run on the tcgen05 tensor-core kernel; other chains (widths <= 256) run on
+ * the CUDA-core kernel. */
+int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
+                     const float* const* weights, const float* const* biases, const int* layer_flags,
+                     int input_relu, int tail_exact, const void* packed, float* y, void* stream);
+
+/* y = max(x, 0) over n floats. Replaces ReLUTensorOp
+ * (rdv/domain/nn.py:362-374, rdv/shaders/tensors/relu_tensor_op.h). */
+int rdvb_relu(const float* x, float* y, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RDVB_H */

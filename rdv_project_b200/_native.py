@@ -1,0 +1,93 @@
+"""ctypes binding of librdvb.so (the C ABI declared in include/rdvb.h).
+
+The library is built in-tree by ``rdv_project_b200.csrc.build`` (or
+``__graft_entry__.build()``). There is no fallback: if the library is missing
+or cannot be loaded every operator raises, so a CUDA-less or unbuilt
+environment can never silently compute something else.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "librdvb.so")
+_lib = None
+_lock = threading.Lock()
+
+RDVB_OK = 0
+RDVB_F32, RDVB_F16, RDVB_BF16 = 0, 1, 2
+RDVB_MATH_F32, RDVB_MATH_F16, RDVB_MATH_BF16 = 0, 1, 2
+RDVB_LAYER_RELU = 4
+RDVB_WINOGRAD_F2X2, RDVB_WINOGRAD_F4X4 = 0, 1
+
+_c_int, _c_i64, _vp, _c_u32, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float
+
+# name -> (restype, argtypes); the exported surface of include/rdvb.h
+SIGNATURES = {
+    "rdvb_version": (_c_int, []),
+    "rdvb_last_error": (ctypes.c_char_p, []),
+    "rdvb_device_status": (_c_int, [_c_int, ctypes.POINTER(_c_u32)]),
+    "rdvb_mlp_packed_bytes": (_c_i64, [_c_int, _vp]),
+    "rdvb_mlp_pack": (_c_int, [_c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),
+    "rdvb_mlp_forward": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp]),
+    "rdvb_relu": (_c_int, [_vp, _vp, _c_i64, _vp]),
+}
+
+
+class RdvbError(RuntimeError):
+    """A librdvb call returned an error status."""
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(_LIB_PATH):
+                    raise RdvbError(
+                        f"{_LIB_PATH} is missing: build the CUDA extension first "
+                        "(python -m rdv_project_b200.csrc.build, or __graft_entry__.build())")
+                handle = ctypes.CDLL(_LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(handle, name, None)
+                    if fn is None:
+                        continue
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().rdvb_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    if rc != RDVB_OK:
+        raise RdvbError(f"{what} failed ({rc}): {last_error()}")
+
+
+def device_status(clear: bool = True) -> int:
+    v = _c_u32(0)
+    check(lib().rdvb_device_status(1 if clear else 0, ctypes.byref(v)), "rdvb_device_status")
+    return int(v.value)
+
+
+def int_array(values):
+    arr = (_c_int * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = int(v)
+    return arr
+
+
+def ptr_array(ptrs):
+    arr = (_vp * len(ptrs))()
+    for i, p in enumerate(ptrs):
+        arr[i] = int(p)
+    return arr

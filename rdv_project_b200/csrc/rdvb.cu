@@ -1,0 +1,383 @@
+// C ABI of the rdv B200 hot path (declared in include/rdvb.h). One
+// translation unit: the kernels are included below so that the device status
+// word and the kernels share a module.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "rdvb.h"
+#include "ptx.cuh"
+#include "mlp_tc.cuh"
+#include "mlp_simt.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return RDVB_OK;
+}
+
+struct DeviceInfo {
+    bool init = false;
+    int sm_count = 0;
+    int max_smem_optin = 0;
+    size_t tc_smem_set = 0;
+    size_t simt_smem_set = 0;
+};
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mutex;
+
+int current_device(DeviceInfo** info) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(RDVB_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    DeviceInfo& d = g_dev[dev];
+    if (!d.init) {
+        cudaDeviceProp prop;
+        e = cudaGetDeviceProperties(&prop, dev);
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+        if (prop.major != 10) {
+            return fail(RDVB_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev,
+                        prop.major, prop.minor);
+        }
+        d.sm_count = prop.multiProcessorCount;
+        d.max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+        d.init = true;
+    }
+    *info = &d;
+    return RDVB_OK;
+}
+
+inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// ------------------------------------------------------------- MLP layout
+struct PackLayout {
+    bool ok = false;
+    uint32_t k_pad[rdvb::mlp_tc::kMaxLayers], n_pad[rdvb::mlp_tc::kMaxLayers];
+    uint32_t w_off[rdvb::mlp_tc::kMaxLayers], w_bytes[rdvb::mlp_tc::kMaxLayers];
+    uint32_t b_off[rdvb::mlp_tc::kMaxLayers];
+    uint32_t total_w = 0;      // bytes of all weight blocks
+    uint32_t bias_floats = 0;  // floats of the padded bias block
+    uint32_t bias_byte_off = 0;
+    uint32_t max_w_bytes = 0;
+    int64_t total_bytes = 0;
+};
+
+PackLayout pack_layout(int n_layers, const int* dims) {
+    PackLayout L;
+    if (n_layers < 1 || n_layers > rdvb::mlp_tc::kMaxLayers || dims == nullptr) return L;
+    for (int l = 0; l <= n_layers; ++l)
+        if (dims[l] < 1 || dims[l] > static_cast<int>(rdvb::mlp_tc::kMaxWidth)) return L;
+    uint32_t w = 0, b = 0;
+    for (int l = 0; l < n_layers; ++l) {
+        L.k_pad[l] = round_up(dims[l], 16);
+        L.n_pad[l] = round_up(dims[l + 1], 16);
+        const uint32_t katoms = (L.k_pad[l] + 63) / 64;
+        L.w_off[l] = w;
+        L.w_bytes[l] = L.n_pad[l] * katoms * 128u;
+        L.b_off[l] = b;
+        w += L.w_bytes[l];
+        b += L.n_pad[l];
+        L.max_w_bytes = std::max(L.max_w_bytes, L.w_bytes[l]);
+    }
+    L.total_w = w;
+    L.bias_floats = b;
+    L.bias_byte_off = round_up(w, 256);
+    L.total_bytes = static_cast<int64_t>(L.bias_byte_off) + 4ll * b;
+    L.ok = true;
+    return L;
+}
+
+int check_chain(int n_layers, const int* dims, const int* flags) {
+    if (n_layers < 1 || n_layers > rdvb::mlp_simt::kMaxLayers)
+        return fail(RDVB_ERR_INVALID_ARG, "n_layers must be in [1, %d], got %d", rdvb::mlp_simt::kMaxLayers, n_layers);
+    if (!dims || !flags) return fail(RDVB_ERR_INVALID_ARG, "dims and layer_flags must not be NULL");
+    for (int l = 0; l <= n_layers; ++l)
+        if (dims[l] < 1) return fail(RDVB_ERR_INVALID_ARG, "dims[%d] = %d must be positive", l, dims[l]);
+    for (int l = 0; l < n_layers; ++l) {
+        const int m = flags[l] & 3;
+        if (m > RDVB_MATH_BF16 || (flags[l] & ~7))
+            return fail(RDVB_ERR_INVALID_ARG, "layer_flags[%d] = %d is not a valid flag set", l, flags[l]);
+    }
+    return RDVB_OK;
+}
+
+// --------------------------------------------------- tensor-core launcher
+int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims, const int* flags,
+                  int input_relu, const void* packed, float* y, cudaStream_t stream, DeviceInfo* dev, bool* taken) {
+    using namespace rdvb::mlp_tc;
+    *taken = false;
+    if (n_rows <= 0) return RDVB_OK;
+    PackLayout L = pack_layout(n_layers, dims);
+    if (!L.ok || packed == nullptr) return RDVB_OK;
+    const int math = flags[0] & 3;
+    if (math == RDVB_MATH_F32) return RDVB_OK;
+    for (int l = 1; l < n_layers; ++l)
+        if ((flags[l] & 3) != math) return RDVB_OK;
+    if (!aligned(x, 16) || !aligned(packed, 256) || !aligned(y, 4)) return RDVB_OK;
+
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.x = x;
+    p.y = y;
+    p.wpack = static_cast<const uint8_t*>(packed);
+    p.bpack = reinterpret_cast<const float*>(static_cast<const uint8_t*>(packed) + L.bias_byte_off);
+    p.n_rows = n_rows;
+    p.n_tiles = static_cast<int>((n_rows + kTileM - 1) / kTileM);
+    p.in_dim = dims[0];
+    p.out_dim = dims[n_layers];
+    p.x_dtype = x_dtype;
+    p.relu_in = input_relu ? 1 : 0;
+    p.bf16 = (math == RDVB_MATH_BF16) ? 1 : 0;
+    p.n_layers = n_layers;
+    p.w_total_bytes = L.total_w;
+    p.bias_floats = L.bias_floats;
+    for (int l = 0; l < n_layers; ++l) {
+        p.layer[l].k_pad = L.k_pad[l];
+        p.layer[l].n_pad = L.n_pad[l];
+        p.layer[l].w_off = L.w_off[l];
+        p.layer[l].w_bytes = L.w_bytes[l];
+        p.layer[l].b_off = L.b_off[l];
+        p.layer[l].idesc = rdvb::umma_idesc_f16(L.n_pad[l], p.bf16);
+        p.layer[l].relu = (flags[l] & RDVB_LAYER_RELU) ? 1u : 0u;
+    }
+    const int esize = x_dtype == RDVB_F32 ? 4 : 2;
+    p.x_stage_bytes = round_up(static_cast<uint32_t>(kTileM) * dims[0] * esize, 128);
+    p.off_w = kSlots * kABytes;
+    const uint32_t budget = static_cast<uint32_t>(dev->max_smem_optin);
+    auto total_for = [&](uint32_t wsize) {
+        const uint32_t off_x = p.off_w + wsize;
+        const uint32_t off_bias = off_x + kSlots * p.x_stage_bytes;
+        const uint32_t off_bar = round_up(off_bias + 4u * L.bias_floats, 16);
+        return std::make_pair(off_bar + kBarBlockBytes + 1024u, std::make_pair(off_x, std::make_pair(off_bias, off_bar)));
+    };
+    uint32_t wsize = 0;
+    const uint32_t resident_size = round_up(L.total_w, 1024);
+    if (resident_size <= 96u * 1024u && total_for(resident_size).first <= budget) {
+        p.resident = 1;
+        p.w_stages = 1;
+        wsize = resident_size;
+        p.w_slot_bytes = resident_size;
+    } else {
+        p.resident = 0;
+        p.w_slot_bytes = round_up(L.max_w_bytes, 1024);
+        p.w_stages = 0;
+        for (int st = 3; st >= 2; --st) {
+            if (total_for(st * p.w_slot_bytes).first <= budget) {
+                p.w_stages = st;
+                break;
+            }
+        }
+        if (p.w_stages == 0) return RDVB_OK;  // does not fit: CUDA-core path
+        wsize = p.w_stages * p.w_slot_bytes;
+    }
+    auto t = total_for(wsize);
+    const uint32_t smem = t.first;
+    p.off_x = t.second.first;
+    p.off_bias = t.second.second.first;
+    p.off_bar = t.second.second.second;
+    p.tmem_cols = 256;
+    p.y_vec4 = (p.out_dim % 4 == 0 && aligned(y, 16)) ? 1 : 0;
+
+    if (dev->tc_smem_set < smem) {
+        cudaError_t e = cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(mlp_tc): %s", cudaGetErrorString(e));
+        dev->tc_smem_set = smem;
+    }
+    const int pairs = (p.n_tiles + kSlots - 1) / kSlots;
+    const int grid = std::min(dev->sm_count, pairs);
+    mlp_tc_kernel<<<grid, kThreads, smem, stream>>>(p);
+    *taken = true;
+    return check_launch("mlp_tc_kernel");
+}
+
+int launch_mlp_simt(const void* x, int x_dtype, int64_t row_begin, int64_t row_end, int n_layers, const int* dims,
+                    const float* const* weights, const float* const* biases, const int* flags, bool force_f32,
+                    int input_relu, float* y, cudaStream_t stream, DeviceInfo* dev) {
+    using namespace rdvb::mlp_simt;
+    if (row_end <= row_begin) return RDVB_OK;
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.x = x;
+    p.x_dtype = x_dtype;
+    p.y = y;
+    p.row_begin = row_begin;
+    p.row_end = row_end;
+    p.n_layers = n_layers;
+    p.relu_in = input_relu ? 1 : 0;
+    int maxw = 0;
+    for (int l = 0; l <= n_layers; ++l) maxw = std::max(maxw, dims[l]);
+    if (maxw > kMaxWidth)
+        return fail(RDVB_ERR_UNSUPPORTED, "layer width %d exceeds the CUDA-core path limit %d", maxw, kMaxWidth);
+    p.maxw = maxw;
+    for (int l = 0; l < n_layers; ++l) {
+        if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "weights[%d]/biases[%d] is NULL", l, l);
+        p.layer[l].W = weights[l];
+        p.layer[l].b = biases[l];
+        p.layer[l].K = dims[l];
+        p.layer[l].N = dims[l + 1];
+        p.layer[l].math = force_f32 ? 0 : (flags[l] & 3);
+        p.layer[l].relu = (flags[l] & RDVB_LAYER_RELU) ? 1 : 0;
+    }
+    const size_t smem = (2ull * maxw * kRows + static_cast<size_t>(maxw) * kOch) * sizeof(float);
+    if (smem > static_cast<size_t>(dev->max_smem_optin))
+        return fail(RDVB_ERR_UNSUPPORTED, "CUDA-core MLP path needs %zu bytes of shared memory", smem);
+    if (dev->simt_smem_set < smem) {
+        cudaError_t e =
+            cudaFuncSetAttribute(mlp_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(mlp_simt): %s", cudaGetErrorString(e));
+        dev->simt_smem_set = smem;
+    }
+    const int64_t rows = row_end - row_begin;
+    const int64_t blocks = (rows + kRows - 1) / kRows;
+    if (blocks > 0x7fffffffLL) return fail(RDVB_ERR_UNSUPPORTED, "too many rows (%lld)", (long long)rows);
+    mlp_simt_kernel<<<static_cast<unsigned>(blocks), kRows, smem, stream>>>(p);
+    return check_launch("mlp_simt_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int rdvb_version(void) { return 100; }
+
+const char* rdvb_last_error(void) { return g_last_error.c_str(); }
+
+int rdvb_device_status(int clear, uint32_t* status) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(e));
+    uint32_t v = 0;
+    e = cudaMemcpyFromSymbol(&v, rdvb::g_status, sizeof(v));
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "reading the status word: %s", cudaGetErrorString(e));
+    if (clear && v) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbol(rdvb::g_status, &zero, sizeof(zero));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "clearing the status word: %s", cudaGetErrorString(e));
+    }
+    if (status) *status = v;
+    return RDVB_OK;
+}
+
+int64_t rdvb_mlp_packed_bytes(int n_layers, const int* dims) {
+    PackLayout L = pack_layout(n_layers, dims);
+    return L.ok ? L.total_bytes : 0;
+}
+
+int rdvb_mlp_pack(int n_layers, const int* dims, const float* const* weights, const float* const* biases, int operand,
+                  void* packed, void* stream) {
+    using namespace rdvb::mlp_tc;
+    PackLayout L = pack_layout(n_layers, dims);
+    if (!L.ok) return fail(RDVB_ERR_UNSUPPORTED, "chain not eligible for the tensor-core path (n_layers <= %d, widths <= %u)",
+                           kMaxLayers, kMaxWidth);
+    if (operand != RDVB_F16 && operand != RDVB_BF16)
+        return fail(RDVB_ERR_INVALID_ARG, "operand must be RDVB_F16 or RDVB_BF16");
+    if (!packed || !aligned(packed, 256)) return fail(RDVB_ERR_INVALID_ARG, "packed must be a 256-byte aligned pointer");
+    if (!weights || !biases) return fail(RDVB_ERR_INVALID_ARG, "weights/biases must not be NULL");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    PackParams pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.n_layers = n_layers;
+    pp.bf16 = operand == RDVB_BF16 ? 1 : 0;
+    pp.wpack = static_cast<uint8_t*>(packed);
+    pp.bpack = reinterpret_cast<float*>(static_cast<uint8_t*>(packed) + L.bias_byte_off);
+    uint32_t chunks = 0;
+    for (int l = 0; l < n_layers; ++l) {
+        if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "weights[%d]/biases[%d] is NULL", l, l);
+        PackLayer& pl = pp.layer[l];
+        pl.W = weights[l];
+        pl.b = biases[l];
+        pl.K = dims[l];
+        pl.N = dims[l + 1];
+        pl.n_pad = L.n_pad[l];
+        pl.katoms = (L.k_pad[l] + 63) / 64;
+        pl.w_off = L.w_off[l];
+        pl.b_off = L.b_off[l];
+        chunks += pl.n_pad * pl.katoms * 8;
+    }
+    pp.total_chunks = chunks;
+    const int threads = 256;
+    const int blocks = std::min<int>((chunks + threads - 1) / threads, dev->sm_count * 8);
+    mlp_pack_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(pp);
+    return check_launch("mlp_pack_kernel");
+}
+
+int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
+                     const float* const* weights, const float* const* biases, const int* layer_flags, int input_relu,
+                     int tail_exact, const void* packed, float* y, void* stream) {
+    if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
+    if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16 && x_dtype != RDVB_BF16)
+        return fail(RDVB_ERR_INVALID_ARG, "x_dtype %d is not RDVB_F32/F16/BF16", x_dtype);
+    if (n_rows < 0) return fail(RDVB_ERR_INVALID_ARG, "n_rows must be >= 0");
+    if (n_rows == 0) return RDVB_OK;
+    if (!x || !y) return fail(RDVB_ERR_INVALID_ARG, "x and y must not be NULL");
+    if (!weights || !biases) return fail(RDVB_ERR_INVALID_ARG, "weights/biases must not be NULL");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    bool any_low = false;
+    for (int l = 0; l < n_layers; ++l) any_low |= (layer_flags[l] & 3) != RDVB_MATH_F32;
+    // Rows served by the tensor-core kernel: whole 32-row groups. The rest
+    // (< 32 rows) go to the CUDA-core kernel: in exact fp32 when tail_exact
+    // (the reference's partial-workgroup rule), else with the same staging.
+    const int64_t n_main = (n_rows / 32) * 32;
+    bool taken = false;
+    if (any_low) {
+        if (int rc = launch_mlp_tc(x, x_dtype, n_main, n_layers, dims, layer_flags, input_relu, packed, y, st, dev,
+                                   &taken))
+            return rc;
+    }
+    if (taken) {
+        return launch_mlp_simt(x, x_dtype, n_main, n_rows, n_layers, dims, weights, biases, layer_flags,
+                               tail_exact != 0, input_relu, y, st, dev);
+    }
+    if (any_low && tail_exact) {
+        if (int rc = launch_mlp_simt(x, x_dtype, 0, n_main, n_layers, dims, weights, biases, layer_flags, false,
+                                     input_relu, y, st, dev))
+            return rc;
+        return launch_mlp_simt(x, x_dtype, n_main, n_rows, n_layers, dims, weights, biases, layer_flags, true,
+                               input_relu, y, st, dev);
+    }
+    return launch_mlp_simt(x, x_dtype, 0, n_rows, n_layers, dims, weights, biases, layer_flags, false, input_relu, y,
+                           st, dev);
+}
+
+int rdvb_relu(const float* x, float* y, int64_t n, void* stream) {
+    if (n < 0) return fail(RDVB_ERR_INVALID_ARG, "n must be >= 0");
+    if (n == 0) return RDVB_OK;
+    if (!x || !y) return fail(RDVB_ERR_INVALID_ARG, "x and y must not be NULL");
+    if (!aligned(x, 16) || !aligned(y, 16)) return fail(RDVB_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const int threads = 256;
+    const int64_t want = (n / 4 + threads - 1) / threads;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, dev->sm_count * 16)));
+    rdvb::mlp_simt::relu_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+    return check_launch("relu_kernel");
+}
+
+}  // extern "C"
