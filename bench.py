@@ -1,0 +1,426 @@
+"""Benchmark of the rdv hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c1|c5]
+
+Default workload (the one the headline metric is quoted
+on): fp16 fully-fused MLP 32 -> 128 x 8 hidden -> 16 with ReLU, fp32
+accumulation, 4,194,304 rows ~N(0,1) fp32 per GPU, Kaiming-normal weights,
+zero biases, seeded synthetic data. One step = one forward pass over the whole
+batch. Metric: MLP evals/s = rows x layers / s (layers = 9 weight layers).
+
+* ``value``: device time (CUDA events on the launch stream, max over ranks)
+  with the input already resident in HBM; inputs (537 MB) are larger than
+  the 126 MB L2, so no flush is needed between steps.
+* ``e2e``: the same metric through the public API with host buffers: every
+  step copies the pinned fp32 input host->device (rdv.wrap), runs the map
+  and copies the fp32 result back into pinned host memory.
+* ``roofline``: tensor-pipe bound; achieved = algorithmic FLOPs of one
+  launch / its average duration; peak from MEASURED_PEAKS.json.
+* ``cpu_baseline``: the oracle's torch-CPU restatement (float16-staged
+  operands, fp32 GEMMs, all host threads) on a bounded sample, rank 0 at N=1.
+* ``--impl reference``: the reference path's CPU restatement (the reference
+  itself needs Vulkan, unavailable on this box) timed alone on the host.
+
+Multi-GPU (torchrun): each rank runs its own batch (weak scaling); the only
+cross-rank traffic is the barrier and the max-reduction of the timings.
+``--workload c5`` runs BASELINE config 5 instead (67,108,864 rows split
+across ranks, final NCCL all-gather of the outputs; strong scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MLP evals/sec (points x layers)"
+UNIT = "evals/s"
+
+
+# ----------------------------------------------------------------- workloads
+def c2_spec():
+    return dict(name="c2", dims=[32] + [128] * 8 + [16], rows=4_194_304, math="f16",
+                x_dist="normal", w_init="kaiming_normal",
+                workload="BASELINE config 2: fp16 fully-fused MLP 32->128x8->16, ReLU, fp32 accumulate")
+
+
+def c1_spec():
+    return dict(name="c1", dims=[3, 64, 64, 64, 4], rows=262_144, math="f32", x_dist="uniform",
+                w_init="xavier_uniform", workload="BASELINE config 1: fp32 MLP 3->64->64->64->4, ReLU")
+
+
+def c5_spec():
+    return dict(name="c5", dims=[3, 64, 64, 64, 64, 4], rows=67_108_864, math="f16", x_dist="uniform",
+                w_init="kaiming_normal",
+                workload="BASELINE config 5: fp16 MLP 3->64x4->4 sharded over ranks + NCCL all-gather")
+
+
+def make_weights(spec, seed_base=1000):
+    dims = spec["dims"]
+    layers = []
+    for i in range(len(dims) - 1):
+        g = torch.Generator().manual_seed(seed_base + i)
+        fan_in, fan_out = dims[i], dims[i + 1]
+        if spec["w_init"] == "kaiming_normal":
+            W = torch.randn(fan_out, fan_in, generator=g) * math.sqrt(2.0 / fan_in)
+        else:
+            bound = math.sqrt(6.0 / (fan_in + fan_out))
+            W = (torch.rand(fan_out, fan_in, generator=g) * 2 - 1) * bound
+        layers.append({"W": W.float().contiguous(), "b": torch.zeros(fan_out), "math": spec["math"],
+                       "relu": i < len(dims) - 2})
+    return layers
+
+
+def make_input(spec, rows, seed):
+    g = torch.Generator().manual_seed(seed)
+    if spec["x_dist"] == "normal":
+        return torch.randn(rows, spec["dims"][0], generator=g)
+    return torch.rand(rows, spec["dims"][0], generator=g) * 2 - 1
+
+
+def build_map(rdv, layers, dev):
+    m = None
+    for l in layers:
+        lin = rdv.linear(l["W"].to(dev), l["b"].to(dev), f16=(l["math"] == "f16"))
+        m = lin if m is None else m >> lin
+        if l["relu"]:
+            m = m >> rdv.relu
+    return m
+
+
+def flops_per_row(dims):
+    return 2 * sum(dims[i] * dims[i + 1] for i in range(len(dims) - 1))
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        return self.summary()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic(key):
+    """Per-launch DRAM bytes recorded from an ncu capture in
+    profiles/ncu_traffic.txt (lines: `<key> <bytes>`), or None."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        with open(path) as f:
+            for ln in f:
+                parts = ln.split()
+                if len(parts) >= 2 and parts[0] == key and not ln.startswith("#"):
+                    return float(parts[1])
+    except OSError:
+        return None
+    return None
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(spec, layers, seconds=8.0, chunk=65536):
+    """Oracle torch-CPU restatement (float16-staged operands, fp32 GEMM,
+    all host threads) on a bounded sample of the same workload."""
+    from oracle import mlp as omlp
+
+    lay = omlp.prestage_torch([{"W": l["W"], "b": l["b"], "math": l["math"], "relu": l["relu"]} for l in layers])
+    x = make_input(spec, chunk, seed=12345)
+    omlp.mlp_forward_torch_cpu(x[:1024], lay)
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        omlp.mlp_forward_torch_cpu(x, lay)
+        done += chunk
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= spec["rows"]:
+            break
+    n_layers = len(layers)
+    return {"value": done * n_layers / el, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{done} rows of the workload in {chunk}-row chunks ({el:.1f} s): torch CPU fp32 GEMMs on "
+                      f"float16-staged operands (oracle restatement of the reference path)"}
+
+
+# ---------------------------------------------------------------- reference
+def run_reference(args, spec, world, rank):
+    if rank != 0:
+        return
+    from oracle import mlp as omlp
+
+    layers = make_weights(spec)
+    lay = omlp.prestage_torch([{"W": l["W"], "b": l["b"], "math": l["math"], "relu": l["relu"]} for l in layers])
+    sample = min(spec["rows"], 262_144)
+    x = make_input(spec, sample, seed=0)
+    for _ in range(args.warmup):
+        omlp.mlp_forward_torch_cpu(x, lay)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        omlp.mlp_forward_torch_cpu(x, lay)
+    el = time.perf_counter() - t0
+    n_layers = len(layers)
+    value = sample * n_layers * args.steps / el
+    sample_txt = (f"{sample} of {spec['rows']} rows per step, torch CPU fp32 GEMMs on float16-staged operands, "
+                  f"{torch.get_num_threads()} threads (restatement of the reference path; its Vulkan kernels are "
+                  f"unavailable on this box)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16" if spec["math"] == "f16" else "f32",
+        "data": "synthetic (seeded)", "config": {"workload": spec["workload"], "rows_per_step": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample_txt},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- ours
+def run_ours(args, spec, world, rank, local):
+    import rdv_project_b200 as rdv
+    from rdv_project_b200 import _native as N
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = make_weights(spec)
+    n_layers = len(layers)
+    m = build_map(rdv, layers, dev)
+    sharded = spec["name"] == "c5"
+    if sharded:
+        per_rank = spec["rows"] // world
+        x_host = make_input(spec, spec["rows"], seed=0)[rank * per_rank:(rank + 1) * per_rank].contiguous()
+        y_all = torch.empty(spec["rows"], spec["dims"][-1], device=dev)
+    else:
+        per_rank = spec["rows"]
+        x_host = make_input(spec, per_rank, seed=rank)
+    x_dev = rdv.wrap(x_host.to(dev))
+    stream = torch.cuda.current_stream()
+
+    def step():
+        y = m(x_dev)
+        if sharded:
+            if world > 1:
+                import torch.distributed as dist
+                dist.all_gather_into_tensor(y_all, y.as_tensor("torch"))
+            else:
+                y_all.copy_(y.as_tensor("torch"))
+        return y
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    # quick parity spot-check of the benchmark's own output (sampled rows)
+    idx = np.zeros(0, dtype=np.int64)
+    parity = (None, None)
+    if not args.profile_run:
+        from oracle import mlp as omlp
+        idx = np.random.default_rng(7).choice(per_rank, size=min(per_rank, 2048), replace=False)
+        idx.sort()
+        y_dev = m(x_dev).as_tensor("torch")
+        got = y_dev[torch.from_numpy(idx).to(dev)].cpu().numpy()
+        lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": l["math"], "relu": l["relu"]} for l in layers]
+        ref = omlp.mlp_forward(x_host.numpy()[idx], lay_np)
+        parity = omlp.rel_errors(got, ref)
+
+    # ---- device-timed region ----
+    sampler = ClockSampler(local) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    launches0 = N.launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = N.launch_count() - launches0
+    clocks = sampler.stop() if sampler else None
+    barrier(world)
+    t_dev = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
+
+    # ---- end-to-end through the public API with host buffers ----
+    x_pin = x_host.pin_memory()
+    y_pin = torch.empty(per_rank, spec["dims"][-1]).pin_memory()
+    e2e_steps = 0 if args.profile_run else max(1, min(args.steps, 5))
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        y = m(rdv.wrap(x_pin))
+        y_pin.copy_(y.as_tensor("torch"), non_blocking=True)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
+
+    if rank != 0:
+        return
+    units_per_step = (spec["rows"] if sharded else per_rank * world) * n_layers
+    value = units_per_step * args.steps / t_dev
+    ms = t_dev / args.steps * 1e3
+    peaks, peak_kind = measured_peaks()
+    flops_launch = flops_per_row(spec["dims"]) * per_rank
+    achieved = flops_launch / (t_dev / args.steps) / 1e12
+    key = "bf16_tflops"
+    peak = float(peaks.get(key, 1590.0))
+    traffic = ncu_traffic(f"mlp_tc_{spec['name']}")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+        "dtype": "f16" if spec["math"] == "f16" else "f32", "data": "synthetic (seeded torch.Generator)",
+        "config": {"workload": spec["workload"], "rows_per_gpu": per_rank, "dims": spec["dims"],
+                   "layers": n_layers, "input": "fp32 [rows, %d]" % spec["dims"][0],
+                   "l2": "inputs larger than L2 (%.0f MB per GPU), no flush" % (per_rank * spec["dims"][0] * 4 / 1e6),
+                   "parallelism": f"dp{world}"},
+        "e2e": {"value": units_per_step * e2e_steps / t_e2e if e2e_steps else None, "unit": UNIT,
+                "h2d_bytes_per_step": int(x_pin.numel() * 4), "d2h_bytes_per_step": int(y_pin.numel() * 4)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor" if spec["math"] != "f32" else "fp32-cuda-core", "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_kind} {key}",
+                     "flops_per_launch": flops_launch},
+        "parity": {"rows_checked": int(idx.size), "normwise": parity[0], "elementwise": parity[1]},
+        "clocks": clocks,
+    }
+    if world == 1 and not args.profile_run:
+        line["cpu_baseline"] = cpu_baseline(spec, layers)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c1", "c5"], default="c2")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="rows per GPU instead of the config's (small cases for ncu captures)")
+    ap.add_argument("--profile-run", action="store_true",
+                    help="timed loop only: no parity check, end-to-end leg or CPU baseline")
+    args = ap.parse_args()
+    spec = {"c2": c2_spec, "c1": c1_spec, "c5": c5_spec}[args.workload]()
+    if args.rows:
+        spec["rows"] = args.rows
+        spec["workload"] += f" (reduced to {args.rows} rows)"
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, spec, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, spec, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -51,6 +51,10 @@ extern "C" {
 /* Library version (major*10000 + minor*100 + patch). */
 int rdvb_version(void);
 
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads). Lets a caller count launches inside a timed region. */
+int64_t rdvb_launch_count(void);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* rdvb_last_error(void);
 

@@ -126,6 +126,49 @@ def mlp_forward_blas(x: np.ndarray, layers, input_relu: bool = False) -> np.ndar
     return a
 
 
+def mlp_forward_torch_cpu(x, layers, input_relu: bool = False, threads: int | None = None):
+    """CPU baseline on torch's CPU kernels (the torch/CPU restatement of the
+    reference path): float16/bfloat16 staging by dtype round trip, fp32 GEMM,
+    fp32 bias, ReLU. `layers` entries may carry a pre-staged "_Wt" torch
+    tensor (see prestage_torch). Uses all host threads unless told otherwise."""
+    import torch
+
+    if threads:
+        torch.set_num_threads(threads)
+    a = x if isinstance(x, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    if input_relu:
+        a = torch.relu(a)
+    for l in layers:
+        Wt = l["_Wt"] if "_Wt" in l else _torch_stage(torch.as_tensor(l["W"]), l["math"]).t().contiguous()
+        xs = a if l["math"] == "f32" else _torch_stage(a, l["math"])
+        a = torch.addmm(torch.as_tensor(l["b"]), xs, Wt)
+        if l["relu"]:
+            a.relu_()
+    return a
+
+
+def _torch_stage(t, math):
+    import torch
+
+    if math == "f16":
+        return t.to(torch.float16).to(torch.float32)
+    if math == "bf16":
+        return t.to(torch.bfloat16).to(torch.float32)
+    return t
+
+
+def prestage_torch(layers):
+    import torch
+
+    out = []
+    for l in layers:
+        d = dict(l)
+        d["_Wt"] = _torch_stage(torch.as_tensor(l["W"]), l["math"]).t().contiguous()
+        d["b"] = torch.as_tensor(l["b"])
+        out.append(d)
+    return out
+
+
 def prestage(layers):
     """Caches each layer's staged weight for repeated mlp_forward_blas calls."""
     out = []

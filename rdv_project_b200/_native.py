@@ -26,6 +26,7 @@ _c_int, _c_i64, _vp, _c_u32, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_void_
 # name -> (restype, argtypes); the exported surface of include/rdvb.h
 SIGNATURES = {
     "rdvb_version": (_c_int, []),
+    "rdvb_launch_count": (_c_i64, []),
     "rdvb_last_error": (ctypes.c_char_p, []),
     "rdvb_device_status": (_c_int, [_c_int, ctypes.POINTER(_c_u32)]),
     "rdvb_mlp_packed_bytes": (_c_i64, [_c_int, _vp]),
@@ -77,6 +78,10 @@ def device_status(clear: bool = True) -> int:
     v = _c_u32(0)
     check(lib().rdvb_device_status(1 if clear else 0, ctypes.byref(v)), "rdvb_device_status")
     return int(v.value)
+
+
+def launch_count() -> int:
+    return int(lib().rdvb_launch_count())
 
 
 def int_array(values):

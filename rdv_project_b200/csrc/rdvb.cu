@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -18,6 +19,7 @@
 namespace {
 
 thread_local std::string g_last_error;
+std::atomic<long long> g_launches{0};
 
 int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -32,6 +34,7 @@ int fail(int code, const char* fmt, ...) {
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return RDVB_OK;
 }
 
@@ -263,6 +266,8 @@ int launch_mlp_simt(const void* x, int x_dtype, int64_t row_begin, int64_t row_e
 extern "C" {
 
 int rdvb_version(void) { return 100; }
+
+int64_t rdvb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* rdvb_last_error(void) { return g_last_error.c_str(); }
 
