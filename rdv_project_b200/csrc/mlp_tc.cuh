@@ -3,24 +3,43 @@
 // Replaces the reference's cooperative-matrix Map chain
 // (rdv/shaders/maps/linear_fast.h:39-109 composed by
 // rdv/shaders/maps/composite.h:8-12 and driven one row per thread by
-// rdv/shaders/maps/map_evaluator.h:1-5). Same arithmetic contract: inputs and
-// weights staged as float16 (or bfloat16), products accumulated in fp32,
-// fp32 bias added after, ReLU in fp32 (applied before the next layer's
-// float16 staging), fp32 output.
+// rdv/shaders/maps/map_evaluator.h:1-5). Arithmetic contract: inputs and
+// weights staged as float16 (or bfloat16), products accumulated in fp32, the
+// fp32 bias included in the fp32 accumulation, ReLU applied before the next
+// layer's float16 staging, fp32 output.
 //
-// Design (one persistent CTA per SM, 320 threads):
-//   warps 0-7  epilogue: stage the input tile (fp32 -> f16, SW128 layout),
-//              then per layer read the TMEM accumulator (tcgen05.ld), add
-//              bias, ReLU + convert to f16 and write the next layer's A tile
-//              back into shared memory; the last layer writes fp32 rows.
-//   warp 8     producer: 1-D bulk (TMA) copies of input tiles and of the
+// Bias: the tensor core adds it as one extra K=16 step per layer -- a
+// constant A tile whose first two K columns are 1.0 against a B block whose
+// first two K rows hold the bias split into float16 hi + lo parts
+// (b = hi + lo + r, |r| <= 2^-22 |b|). The sum is fp32 and the products are
+// exact, so the result is the fp32 bias add up to that residual and the
+// order of fp32 additions. This keeps the epilogue to
+// TMEM load -> ReLU + convert -> TMEM store.
+//
+// Design (one persistent CTA per SM, 19 warps):
+//   warps 0-15 epilogue. Warp w owns TMEM lane quadrant (w % 4) -- rows
+//              32*(w%4) .. +31 of every tile -- and, for slot s, the
+//              16-column chunks c with (c + s) % 4 == w / 4 (rotating the
+//              owner by slot spreads narrow layers over all warps). Per layer
+//              it reads its accumulator chunks (tcgen05.ld), applies ReLU
+//              while converting to f16/bf16 (cvt.rn.relu) and writes them
+//              back into TMEM (tcgen05.st) as the next layer's A operand, so
+//              hidden activations never touch shared memory; the last layer
+//              writes fp32 rows to global memory.
+//   warp 16    producer: 1-D bulk (TMA) copies of input tiles and of the
 //              pre-swizzled weight blocks (resident, or streamed per layer
-//              through a ring when they do not fit).
-//   warp 9     MMA issuer: allocates TMEM, one thread issues
-//              tcgen05.mma (M=128, N=layer width, K=16 steps) per layer and
-//              commits completion to mbarriers.
-// Two 128-row tiles ("slots") are in flight so one slot's epilogue overlaps
-// the other slot's MMAs. No activation ever leaves the SM between layers.
+//              through a ring), issued from one event loop.
+//   warp 17    MMA issuer: allocates TMEM; one thread issues tcgen05.mma
+//              (M=128, N=layer width, K=16 steps) per layer -- A from shared
+//              memory for the first layer, from TMEM after -- plus the bias
+//              step, and commits completion to mbarriers.
+//   warp 18    input staging: converts each input tile (x dtype ->
+//              f16/bf16, zero-padded to 16) into the first layer's A tile in
+//              shared memory (K-major, 128B swizzle).
+// SLOTS independent 128-row tiles are in flight per CTA (one TMEM
+// accumulator and one TMEM activation tile each), so the epilogue of one
+// tile overlaps the MMAs of the others. Shared memory only feeds the weights
+// and the first layer's A, well inside its bandwidth.
 #pragma once
 #include "ptx.cuh"
 
@@ -29,24 +48,26 @@ namespace mlp_tc {
 
 constexpr int kMaxLayers = 16;
 constexpr int kTileM = 128;
-constexpr int kSlots = 2;
-constexpr int kEpiWarps = 8;
-constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kMaxSlots = 4;
+constexpr int kEpiWarps = 16;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kStageWarp = 18;
+constexpr int kThreads = 19 * 32;
 constexpr uint32_t kAtomBytes = kTileM * 128;      // one 64-wide K atom of a 128-row tile
-constexpr int kMaxKAtoms = 2;                       // layer width <= 128
-constexpr uint32_t kABytes = kAtomBytes * kMaxKAtoms;
 constexpr int kMaxWStages = 4;
 constexpr uint32_t kMaxWidth = 128;
+constexpr int kColGroups = kEpiWarps / 4;           // 4 column groups
+constexpr int kChunksPerWarp = (kMaxWidth / 16) / kColGroups;  // 2
+constexpr uint32_t kOnesBytes = kTileM * 32;        // constant A tile of the bias step
+constexpr uint32_t kTmemCols = 512;
 
 struct Layer {
-    uint32_t k_pad;   // input width rounded up to 16
-    uint32_t n_pad;   // output width rounded up to 16
-    uint32_t w_off;   // byte offset of the packed block in the weight pack
-    uint32_t w_bytes; // n_pad * katoms * 128
-    uint32_t b_off;   // float offset in the bias pack
+    uint32_t k_pad;    // input width rounded up to 16
+    uint32_t n_pad;    // output width rounded up to 16
+    uint32_t w_off;    // byte offset of the layer block in the weight pack
+    uint32_t w_bytes;  // layer block: SW128 weights + bias block, 1 KB multiple
+    uint32_t bias_off; // byte offset of the bias block inside the layer block
     uint32_t idesc;
     uint32_t relu;
 };
@@ -55,34 +76,36 @@ struct Params {
     const void* x;
     float* y;
     const uint8_t* wpack;
-    const float* bpack;
     long long n_rows;
     int n_tiles;
     int in_dim;
     int out_dim;
     int x_dtype;  // 0 f32, 1 f16, 2 bf16
     int relu_in;
-    int bf16;     // operand type: 0 f16, 1 bf16
     int n_layers;
     int resident;
     int w_stages;
     uint32_t w_slot_bytes;
     uint32_t w_total_bytes;
-    uint32_t bias_floats;
     uint32_t x_stage_bytes;
-    uint32_t off_w, off_x, off_bias, off_bar;
-    uint32_t tmem_cols;
+    uint32_t off_w, off_x, off_ones, off_bar;
+    uint32_t a0_bytes;     // shared-memory A tile of layer 0, per slot
+    uint32_t acc_stride;   // TMEM columns of one slot's fp32 accumulator
+    uint32_t act_base;     // first TMEM column of the activation regions
+    uint32_t act_stride;   // TMEM columns of one slot's 16-bit activation tile
     int y_vec4;
     Layer layer[kMaxLayers];
 };
 
 // Barrier slots in the barrier block.
 enum : int {
-    kBarXFull = 0,
-    kBarXEmpty = kBarXFull + kSlots,
-    kBarAFull = kBarXEmpty + kSlots,
-    kBarAccFull = kBarAFull + kSlots,
-    kBarWFull = kBarAccFull + kSlots,
+    kBarXFull = 0,                             // input tile landed in staging (TMA tx)
+    kBarXEmpty = kBarXFull + kMaxSlots,        // staging buffer consumed
+    kBarA0Full = kBarXEmpty + kMaxSlots,       // layer-0 A tile written
+    kBarA0Empty = kBarA0Full + kMaxSlots,      // layer-0 MMAs done reading it
+    kBarAFull = kBarA0Empty + kMaxSlots,       // epilogue done with a layer of the slot
+    kBarAccFull = kBarAFull + kMaxSlots,       // accumulator ready
+    kBarWFull = kBarAccFull + kMaxSlots,
     kBarWEmpty = kBarWFull + kMaxWStages,
     kBarDrain = kBarWEmpty + kMaxWStages,
     kNumBars = kBarDrain + 1,
@@ -95,23 +118,45 @@ __device__ __forceinline__ float load_x_elem(const uint8_t* xs, int dtype, uint3
     return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(xs)[idx]);
 }
 
-__device__ __forceinline__ uint32_t pack2(float a, float b, int bf16, int relu) {
-    if (bf16) return relu ? pack_bf16x2_relu(a, b) : pack_bf16x2(a, b);
-    return relu ? pack_f16x2_relu(a, b) : pack_f16x2(a, b);
+template <int BF16, bool RELU>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if (BF16) return RELU ? pack_bf16x2_relu(a, b) : pack_bf16x2(a, b);
+    return RELU ? pack_f16x2_relu(a, b) : pack_f16x2(a, b);
+}
+
+template <int BF16>
+__device__ __forceinline__ uint32_t pack2_rt(float a, float b, int relu) {
+    return relu ? pack2<BF16, true>(a, b) : pack2<BF16, false>(a, b);
 }
 
 // Drain wait used on the abort path: ignores the abort flag, keeps its own
 // time limit.
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint32_t* status) {
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
     const uint64_t t0 = global_timer_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, 500000u)) {
         if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
-            atomicOr(status, kStatusTimeoutDrain);
+            atomicOr(&g_status, kStatusTimeoutDrain);
             return;
         }
     }
 }
 
+// Tile index of (round r, slot s) for this CTA, or -1 past the end.
+template <int SLOTS>
+__device__ __forceinline__ int tile_of(int r, int s, int n_tiles) {
+    const int t = (r * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x)) * SLOTS + s;
+    return t < n_tiles ? t : -1;
+}
+
+// One warp's share of a 16-column accumulator chunk -> packed 16-bit
+// activations (8 TMEM columns).
+template <int BF16, bool RELU>
+__device__ __forceinline__ void convert_chunk(const uint32_t (&v)[16], uint32_t (&pk)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pk[i] = pack2<BF16, RELU>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+}
+
+template <int SLOTS, int BF16>
 __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the SW128 atoms.
@@ -119,11 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
     const uint32_t base = (raw_addr + 1023u) & ~1023u;
     uint8_t* const base_ptr = smem_raw + (base - raw_addr);
 
-    const uint32_t a_base = base;                      // kSlots * kABytes
+    const uint32_t a_base = base;  // SLOTS * a0_bytes (layer-0 A tiles)
     const uint32_t w_base = base + p.off_w;
     const uint32_t x_base = base + p.off_x;
-    const float* bias_s = reinterpret_cast<const float*>(base_ptr + p.off_bias);
-    float* bias_w = reinterpret_cast<float*>(base_ptr + p.off_bias);
+    const uint32_t ones_base = base + p.off_ones;
     const uint32_t bar_base = base + p.off_bar;
     auto bar = [&](int i) -> uint32_t { return bar_base + 8u * static_cast<uint32_t>(i); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + p.off_bar + kNumBars * 8);
@@ -133,9 +177,11 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSlots; ++s) {
+        for (int s = 0; s < kMaxSlots; ++s) {
             mbar_init(bar(kBarXFull + s), 1);
-            mbar_init(bar(kBarXEmpty + s), kEpiWarps);
+            mbar_init(bar(kBarXEmpty + s), 1);
+            mbar_init(bar(kBarA0Full + s), 1);
+            mbar_init(bar(kBarA0Empty + s), 1);
             mbar_init(bar(kBarAFull + s), kEpiWarps);
             mbar_init(bar(kBarAccFull + s), 1);
         }
@@ -147,8 +193,18 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
         *abort = 0u;
         fence_mbarrier_init();
     }
+    // Constant A tile of the bias step: every row is [1, 1, 0, ..., 0].
+    if (threadIdx.x < kTileM) {
+        const uint32_t one2 = BF16 ? 0x3F803F80u : 0x3C003C00u;
+        const uint32_t r = threadIdx.x;
+        st_shared_v4(ones_base + k16_plain_offset(r, 0), one2, 0u, 0u, 0u);
+        st_shared_v4(ones_base + k16_plain_offset(r, 8), 0u, 0u, 0u, 0u);
+    }
+    // Layer-0 A tiles start zeroed: chunks past the input width stay zero.
+    for (uint32_t i = threadIdx.x; i < SLOTS * p.a0_bytes / 16; i += kThreads) st_shared_v4(a_base + i * 16, 0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
     if (warp == kMmaWarp) {
-        tmem_alloc(smem_addr(tmem_slot), p.tmem_cols);
+        tmem_alloc(smem_addr(tmem_slot), kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -157,162 +213,124 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
     const uint32_t tmem_base = *tmem_slot;
 
     const int n_layers = p.n_layers;
-    const int G = gridDim.x;
+    const int esize = p.x_dtype == 0 ? 4 : 2;
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            uint32_t xu[kSlots] = {0, 0};
-            uint32_t wcount = 0;
-            const int esize = p.x_dtype == 0 ? 4 : 2;
+            // Two independent copy streams, issued by one thread in an event
+            // loop so neither blocks the other: input tiles (x_empty[s]
+            // gates each slot's staging buffer) and weight blocks (w_empty
+            // gates each ring slot). Both follow the consumers' order.
+            uint32_t xph = 0u, xused = 0u;  // per-slot parity of the next load / slot used
+            uint32_t wcount = 0, q = 0, wph = 0;
             bool ok = true;
+            int xr = 0, xs = 0;  // next input tile to load: (round, slot)
+            int wr = 0, wl = 0;  // next weight block: (round, layer)
+            bool x_done = tile_of<SLOTS>(0, 0, p.n_tiles) < 0;
+            bool w_done = p.resident || x_done;
             if (p.resident) {
                 mbar_arrive_expect_tx(bar(kBarWFull), p.w_total_bytes);
                 for (int l = 0; l < n_layers; ++l)
                     bulk_g2s(w_base + p.layer[l].w_off, p.wpack + p.layer[l].w_off, p.layer[l].w_bytes,
                              bar(kBarWFull));
             }
-            for (int r = 0; ok; ++r) {
-                const int tile0 = (r * G + blockIdx.x) * kSlots;
-                if (tile0 >= p.n_tiles) break;
-                for (int s = 0; s < kSlots && ok; ++s) {
-                    const int t = tile0 + s;
-                    if (t >= p.n_tiles) break;
-                    if (!mbar_wait(bar(kBarXEmpty + s), (xu[s] & 1u) ^ 1u, abort, &g_status, kStatusTimeoutXEmpty)) {
-                        ok = false;
-                        break;
-                    }
-                    long long row0 = static_cast<long long>(t) * kTileM;
+            uint64_t t_last = global_timer_ns();
+            while (!(x_done && w_done)) {
+                bool progressed = false;
+                if (!x_done && mbar_test_wait(bar(kBarXEmpty + xs), ((xph >> xs) & 1u) ^ 1u)) {
+                    const int t = tile_of<SLOTS>(xr, xs, p.n_tiles);
+                    const long long row0 = static_cast<long long>(t) * kTileM;
                     long long rows = p.n_rows - row0;
                     if (rows > kTileM) rows = kTileM;
                     const uint32_t bytes = static_cast<uint32_t>(rows) * p.in_dim * esize;
-                    mbar_arrive_expect_tx(bar(kBarXFull + s), bytes);
-                    bulk_g2s(x_base + s * p.x_stage_bytes,
-                             static_cast<const uint8_t*>(p.x) + row0 * p.in_dim * esize, bytes, bar(kBarXFull + s));
-                    ++xu[s];
-                }
-                if (!p.resident) {
-                    for (int l = 0; l < n_layers && ok; ++l) {
-                        const uint32_t q = wcount % p.w_stages;
-                        const uint32_t ph = (wcount / p.w_stages) & 1u;
-                        if (!mbar_wait(bar(kBarWEmpty + q), ph ^ 1u, abort, &g_status, kStatusTimeoutWEmpty)) {
-                            ok = false;
-                            break;
-                        }
-                        mbar_arrive_expect_tx(bar(kBarWFull + q), p.layer[l].w_bytes);
-                        bulk_g2s(w_base + q * p.w_slot_bytes, p.wpack + p.layer[l].w_off, p.layer[l].w_bytes,
-                                 bar(kBarWFull + q));
-                        ++wcount;
+                    mbar_arrive_expect_tx(bar(kBarXFull + xs), bytes);
+                    bulk_g2s(x_base + xs * p.x_stage_bytes,
+                             static_cast<const uint8_t*>(p.x) + row0 * p.in_dim * esize, bytes, bar(kBarXFull + xs));
+                    xph ^= 1u << xs;
+                    xused |= 1u << xs;
+                    if (++xs == SLOTS) {
+                        xs = 0;
+                        ++xr;
                     }
+                    x_done = tile_of<SLOTS>(xr, xs, p.n_tiles) < 0;
+                    progressed = true;
+                }
+                if (!w_done && mbar_test_wait(bar(kBarWEmpty + q), wph ^ 1u)) {
+                    mbar_arrive_expect_tx(bar(kBarWFull + q), p.layer[wl].w_bytes);
+                    bulk_g2s(w_base + q * p.w_slot_bytes, p.wpack + p.layer[wl].w_off, p.layer[wl].w_bytes,
+                             bar(kBarWFull + q));
+                    ++wcount;
+                    if (++q == static_cast<uint32_t>(p.w_stages)) {
+                        q = 0;
+                        wph ^= 1u;
+                    }
+                    if (++wl == n_layers) {
+                        wl = 0;
+                        ++wr;
+                    }
+                    w_done = tile_of<SLOTS>(wr, 0, p.n_tiles) < 0;
+                    progressed = true;
+                }
+                if (progressed) {
+                    t_last = global_timer_ns();
+                } else if (*abort) {
+                    ok = false;
+                    break;
+                } else if (global_timer_ns() - t_last > RDVB_WAIT_LIMIT_NS) {
+                    *abort = 1u;
+                    atomicOr(&g_status, x_done ? kStatusTimeoutWEmpty : kStatusTimeoutXEmpty);
+                    ok = false;
+                    break;
+                } else {
+                    __nanosleep(128);  // leave the scheduler to the compute warps
                 }
             }
             if (!ok) {
                 // Let every copy this thread started land before the CTA exits.
-                for (int s = 0; s < kSlots; ++s)
-                    if (xu[s]) drain_wait(bar(kBarXFull + s), (xu[s] - 1u) & 1u, &g_status);
+                for (int s = 0; s < SLOTS; ++s)
+                    if ((xused >> s) & 1u) drain_wait(bar(kBarXFull + s), ((xph >> s) & 1u) ^ 1u);
                 if (p.resident) {
-                    drain_wait(bar(kBarWFull), 0u, &g_status);
+                    drain_wait(bar(kBarWFull), 0u);
                 } else {
                     for (uint32_t c = (wcount > (uint32_t)p.w_stages ? wcount - p.w_stages : 0u); c < wcount; ++c)
-                        drain_wait(bar(kBarWFull + c % p.w_stages), (c / p.w_stages) & 1u, &g_status);
+                        drain_wait(bar(kBarWFull + c % p.w_stages), (c / p.w_stages) & 1u);
                 }
             }
         }
-    } else if (warp == kMmaWarp) {
-        if (lane == 0) {
-            uint32_t au[kSlots] = {0, 0};
-            uint32_t wcount = 0;
-            bool ok = true;
-            bool issued = false;
-            if (p.resident) ok = mbar_wait(bar(kBarWFull), 0u, abort, &g_status, kStatusTimeoutWFull);
-            for (int r = 0; ok; ++r) {
-                const int tile0 = (r * G + blockIdx.x) * kSlots;
-                if (tile0 >= p.n_tiles) break;
-                const int nslots = min(kSlots, p.n_tiles - tile0);
-                for (int l = 0; l < n_layers && ok; ++l) {
-                    const Layer& L = p.layer[l];
-                    uint32_t wb;
-                    uint32_t q = 0;
-                    if (p.resident) {
-                        wb = w_base + L.w_off;
-                    } else {
-                        q = wcount % p.w_stages;
-                        if (!mbar_wait(bar(kBarWFull + q), (wcount / p.w_stages) & 1u, abort, &g_status,
-                                       kStatusTimeoutWFull)) {
-                            ok = false;
-                            break;
-                        }
-                        wb = w_base + q * p.w_slot_bytes;
-                    }
-                    for (int s = 0; s < nslots; ++s) {
-                        if (!mbar_wait(bar(kBarAFull + s), au[s] & 1u, abort, &g_status, kStatusTimeoutAFull)) {
-                            ok = false;
-                            break;
-                        }
-                        ++au[s];
-                        tc_fence_after();
-                        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(s) * kMaxWidth;
-                        const uint32_t a_tile = a_base + static_cast<uint32_t>(s) * kABytes;
-                        const uint32_t ksteps = L.k_pad >> 4;
-                        for (uint32_t j = 0; j < ksteps; ++j) {
-                            const uint32_t koff = (j >> 2) * kAtomBytes + (j & 3u) * 32u;
-                            const uint32_t kboff = (j >> 2) * (L.n_pad * 128u) + (j & 3u) * 32u;
-                            umma_f16(d_tmem, umma_desc_sw128(a_tile + koff), umma_desc_sw128(wb + kboff), L.idesc,
-                                     j > 0 ? 1u : 0u);
-                        }
-                        umma_commit(bar(kBarAccFull + s));
-                        issued = true;
-                    }
-                    if (!ok) break;
-                    if (!p.resident) {
-                        umma_commit(bar(kBarWEmpty + q));
-                        ++wcount;
-                    }
-                }
-            }
-            if (!ok && issued) {
-                umma_commit(bar(kBarDrain));
-                drain_wait(bar(kBarDrain), 0u, &g_status);
-            }
-        }
-    } else {
-        // ------------------------------------------------------ epilogue
-        const int et = threadIdx.x;  // 0..255
-        for (uint32_t i = et; i < p.bias_floats; i += kEpiThreads) bias_w[i] = p.bpack[i];
-        named_bar_sync(1, kEpiThreads);
-
-        const int quad = warp & 3;
-        const int grp = warp >> 2;
-        const int row = quad * 32 + lane;
-        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-        uint32_t xf[kSlots] = {0, 0};
-        uint32_t ac[kSlots] = {0, 0};
-        const int esize = p.x_dtype == 0 ? 4 : 2;
+    } else if (warp == kStageWarp) {
+        // ---------------------------------------------- input staging
+        uint32_t xfph = 0u, a0eph = 0u;
         const uint32_t kch0 = p.layer[0].k_pad >> 3;
+        // only chunks holding input columns are rewritten; the rest stay zero
+        const uint32_t kch_in = (static_cast<uint32_t>(p.in_dim) + 7u) >> 3;
+        const bool vec = p.x_dtype == 0 && (p.in_dim & 7) == 0;
         bool ok = true;
-
-        for (int r = 0; ok; ++r) {
-            const int tile0 = (r * G + blockIdx.x) * kSlots;
-            if (tile0 >= p.n_tiles) break;
-            const int nslots = min(kSlots, p.n_tiles - tile0);
-
-            // Stage the input tiles: [rows, in_dim] (x dtype) -> A[s] f16/bf16.
-            for (int s = 0; s < nslots; ++s) {
-                if (!mbar_wait(bar(kBarXFull + s), xf[s] & 1u, abort, &g_status, kStatusTimeoutXFull)) {
+        (void)kch0;
+        for (int r = 0; ok && tile_of<SLOTS>(r, 0, p.n_tiles) >= 0; ++r) {
+            for (int s = 0; s < SLOTS; ++s) {
+                const int t = tile_of<SLOTS>(r, s, p.n_tiles);
+                if (t < 0) break;
+                bool good = mbar_wait(bar(kBarXFull + s), (xfph >> s) & 1u, abort, &g_status, kStatusTimeoutXFull) &&
+                            mbar_wait(bar(kBarA0Empty + s), ((a0eph >> s) & 1u) ^ 1u, abort, &g_status,
+                                      kStatusTimeoutOther);
+                // every lane leaves together, so the warp-wide steps below
+                // never run diverged
+                if (!__all_sync(0xffffffffu, good)) {
                     ok = false;
                     break;
                 }
-                ++xf[s];
-                const long long row0 = static_cast<long long>(tile0 + s) * kTileM;
-                long long rv = p.n_rows - row0;
-                const int rows_valid = rv > kTileM ? kTileM : static_cast<int>(rv);
+                xfph ^= 1u << s;
+                a0eph ^= 1u << s;
+                const long long row0 = static_cast<long long>(t) * kTileM;
+                const long long rv = p.n_rows - row0;
+                const uint32_t rows_valid = rv > kTileM ? static_cast<uint32_t>(kTileM) : static_cast<uint32_t>(rv);
                 const uint8_t* xs = base_ptr + p.off_x + s * p.x_stage_bytes;
-                const uint32_t a_tile = a_base + static_cast<uint32_t>(s) * kABytes;
-                for (uint32_t idx = et; idx < kTileM * kch0; idx += kEpiThreads) {
-                    const uint32_t ri = idx / kch0;
-                    const uint32_t c = idx - ri * kch0;
+                const uint32_t a_tile = a_base + static_cast<uint32_t>(s) * p.a0_bytes;
+                for (uint32_t idx = lane; idx < kTileM * kch_in; idx += 32) {
+                    const uint32_t ri = idx / kch_in;
+                    const uint32_t c = idx - ri * kch_in;
                     float v[8];
-                    if (p.x_dtype == 0 && (p.in_dim & 7) == 0 && ri < (uint32_t)rows_valid &&
-                        c * 8 + 8 <= (uint32_t)p.in_dim) {
+                    if (vec && ri < rows_valid) {
                         const float4* src = reinterpret_cast<const float4*>(xs + (ri * p.in_dim + c * 8) * 4);
                         const float4 u0 = src[0], u1 = src[1];
                         v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
@@ -321,92 +339,185 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
 #pragma unroll
                         for (int e = 0; e < 8; ++e) {
                             const uint32_t k = c * 8 + e;
-                            v[e] = (ri < (uint32_t)rows_valid && k < (uint32_t)p.in_dim)
+                            v[e] = (ri < rows_valid && k < static_cast<uint32_t>(p.in_dim))
                                        ? load_x_elem(xs, p.x_dtype, ri * p.in_dim + k)
                                        : 0.0f;
                         }
                     }
-                    const uint32_t w0 = pack2(v[0], v[1], p.bf16, p.relu_in);
-                    const uint32_t w1 = pack2(v[2], v[3], p.bf16, p.relu_in);
-                    const uint32_t w2 = pack2(v[4], v[5], p.bf16, p.relu_in);
-                    const uint32_t w3 = pack2(v[6], v[7], p.bf16, p.relu_in);
-                    st_shared_v4(a_tile + sw128_offset(ri, c * 8, kTileM), w0, w1, w2, w3);
+                    st_shared_v4(a_tile + sw128_offset(ri, c * 8, kTileM), pack2_rt<BF16>(v[0], v[1], p.relu_in),
+                                 pack2_rt<BF16>(v[2], v[3], p.relu_in), pack2_rt<BF16>(v[4], v[5], p.relu_in),
+                                 pack2_rt<BF16>(v[6], v[7], p.relu_in));
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(bar(kBarXEmpty + s));
-                    mbar_arrive(bar(kBarAFull + s));
+                    mbar_arrive(bar(kBarA0Full + s));
                 }
-                (void)esize;
             }
-            if (!ok) break;
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            uint32_t aph = 0u, a0ph = 0u;  // per-slot parities of the next a_full / a0_full phase
+            uint32_t q = 0, wph = 0;       // weight ring slot and its phase
+            bool ok = true;
+            bool issued = false;
+            const uint64_t ones_desc = umma_desc_k16_plain(ones_base);
+            const uint64_t w_desc_sw = umma_desc_sw128(w_base);     // + (byte offset >> 4)
+            const uint64_t w_desc_plain = umma_desc_k16_plain(w_base);
+            if (p.resident) ok = mbar_wait(bar(kBarWFull), 0u, abort, &g_status, kStatusTimeoutWFull);
+            // Per-slot operand addresses, fixed for the whole kernel.
+            uint32_t d_tm[SLOTS], a_tm[SLOTS];
+            uint64_t a0_desc[SLOTS];
+#pragma unroll
+            for (int s = 0; s < SLOTS; ++s) {
+                d_tm[s] = tmem_base + static_cast<uint32_t>(s) * p.acc_stride;
+                a_tm[s] = tmem_base + p.act_base + static_cast<uint32_t>(s) * p.act_stride;
+                a0_desc[s] = umma_desc_sw128(a_base + static_cast<uint32_t>(s) * p.a0_bytes);
+            }
+            for (int r = 0; ok && tile_of<SLOTS>(r, 0, p.n_tiles) >= 0; ++r) {
+                for (int l = 0; l < n_layers && ok; ++l) {
+                    const uint32_t ksteps = p.layer[l].k_pad >> 4;
+                    const uint32_t n8 = p.layer[l].n_pad * 8u;  // one K atom of B, in 16-byte units
+                    const uint32_t idesc = p.layer[l].idesc;
+                    uint32_t blk;  // byte offset of this layer's block from w_base
+                    if (p.resident) {
+                        blk = p.layer[l].w_off;
+                    } else {
+                        if (!mbar_wait(bar(kBarWFull + q), wph, abort, &g_status, kStatusTimeoutWFull)) {
+                            ok = false;
+                            break;
+                        }
+                        blk = q * p.w_slot_bytes;
+                    }
+                    // B descriptors of this layer's K steps, shared by every slot
+                    const uint64_t b0 = w_desc_sw + (blk >> 4);
+                    uint64_t b_desc[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) b_desc[j] = b0 + (j >> 2) * n8 + (j & 3) * 2;
+                    const uint64_t bias_desc = w_desc_plain + ((blk + p.layer[l].bias_off) >> 4);
+#pragma unroll
+                    for (int s = 0; s < SLOTS; ++s) {
+                        if (tile_of<SLOTS>(r, s, p.n_tiles) < 0) break;
+                        if (l == 0) {
+                            if (!mbar_wait(bar(kBarA0Full + s), (a0ph >> s) & 1u, abort, &g_status,
+                                           kStatusTimeoutXFull)) {
+                                ok = false;
+                                break;
+                            }
+                            a0ph ^= 1u << s;
+                        }
+                        // previous layer's activations written (or, at layer 0,
+                        // the previous round's last accumulator read)
+                        if (l > 0 || r > 0) {
+                            if (!mbar_wait(bar(kBarAFull + s), (aph >> s) & 1u, abort, &g_status,
+                                           kStatusTimeoutAFull)) {
+                                ok = false;
+                                break;
+                            }
+                            aph ^= 1u << s;
+                        }
+                        tc_fence_after();
+                        if (l == 0) {
+                            // input layer: A from the staged shared-memory tile
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (j < static_cast<int>(ksteps))
+                                    umma_f16(d_tm[s], a0_desc[s] + (j >> 2) * (kAtomBytes >> 4) + (j & 3) * 2,
+                                             b_desc[j], idesc, j > 0 ? 1u : 0u);
+                        } else {
+                            // hidden layers: A = previous activations, resident in TMEM
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (j < static_cast<int>(ksteps))
+                                    umma_f16_ts(d_tm[s], a_tm[s] + j * 8u, b_desc[j], idesc, j > 0 ? 1u : 0u);
+                        }
+                        // bias step: ones[128 x 16] x [b_hi; b_lo; 0...]
+                        umma_f16(d_tm[s], ones_desc, bias_desc, idesc, 1u);
+                        if (l == 0) umma_commit(bar(kBarA0Empty + s));
+                        umma_commit(bar(kBarAccFull + s));
+                        issued = true;
+                    }
+                    if (!ok) break;
+                    if (!p.resident) {
+                        umma_commit(bar(kBarWEmpty + q));
+                        if (++q == static_cast<uint32_t>(p.w_stages)) {
+                            q = 0;
+                            wph ^= 1u;
+                        }
+                    }
+                }
+            }
+            if (!ok && issued) {
+                umma_commit(bar(kBarDrain));
+                drain_wait(bar(kBarDrain), 0u);
+            }
+        }
+    } else {
+        // ------------------------------------------------------ epilogue
+        const int quad = warp & 3;
+        const int grp = warp >> 2;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        uint32_t acph = 0u;  // per-slot parity of the next acc_full phase
+        bool ok = true;
 
+        for (int r = 0; ok && tile_of<SLOTS>(r, 0, p.n_tiles) >= 0; ++r) {
             for (int l = 0; l < n_layers && ok; ++l) {
-                const Layer& L = p.layer[l];
                 const bool last = (l == n_layers - 1);
-                const uint32_t nch = L.n_pad >> 4;
-                for (int s = 0; s < nslots; ++s) {
-                    if (!mbar_wait(bar(kBarAccFull + s), ac[s] & 1u, abort, &g_status, kStatusTimeoutAccFull)) {
+                const uint32_t nch = p.layer[l].n_pad >> 4;
+                const bool relu = p.layer[l].relu != 0;
+#pragma unroll
+                for (int s = 0; s < SLOTS; ++s) {
+                    const int t = tile_of<SLOTS>(r, s, p.n_tiles);
+                    if (t < 0) break;
+                    const bool good =
+                        mbar_wait(bar(kBarAccFull + s), (acph >> s) & 1u, abort, &g_status, kStatusTimeoutAccFull);
+                    // tcgen05.ld/st below are warp-collective: leave together
+                    if (!__all_sync(0xffffffffu, good)) {
                         ok = false;
                         break;
                     }
-                    ++ac[s];
+                    acph ^= 1u << s;
                     tc_fence_after();
-                    const uint32_t t_col = tmem_base + lane_off + static_cast<uint32_t>(s) * kMaxWidth;
-                    uint32_t v[4][16];
+                    const uint32_t c0 = static_cast<uint32_t>((grp - s) & 3);  // first chunk owned for this slot
+                    const uint32_t t_col = tmem_base + lane_off + static_cast<uint32_t>(s) * p.acc_stride;
+                    uint32_t v[kChunksPerWarp][16];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t c = grp + 2 * j;
+                    for (int j = 0; j < kChunksPerWarp; ++j) {
+                        const uint32_t c = c0 + kColGroups * j;
                         if (c < nch) tmem_ld16(t_col + c * 16, v[j]);
                     }
                     tmem_wait_ld();
                     if (!last) {
-                        const uint32_t a_tile = a_base + static_cast<uint32_t>(s) * kABytes;
+                        const uint32_t t_act =
+                            tmem_base + lane_off + p.act_base + static_cast<uint32_t>(s) * p.act_stride;
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const uint32_t c = grp + 2 * j;
+                        for (int j = 0; j < kChunksPerWarp; ++j) {
+                            const uint32_t c = c0 + kColGroups * j;
                             if (c < nch) {
-                                const float* bb = bias_s + L.b_off + c * 16;
                                 uint32_t pk[8];
-#pragma unroll
-                                for (int i = 0; i < 16; i += 2) {
-                                    float a0 = __uint_as_float(v[j][i]);
-                                    float a1 = __uint_as_float(v[j][i + 1]);
-                                    add_f32x2(a0, a1, bb[i], bb[i + 1]);
-                                    pk[i >> 1] = pack2(a0, a1, p.bf16, L.relu);
-                                }
-                                // columns c*16 .. c*16+15 of this layer = K chunks 2c, 2c+1 of the next
-                                st_shared_v4(a_tile + sw128_offset(row, c * 16, kTileM), pk[0], pk[1], pk[2], pk[3]);
-                                st_shared_v4(a_tile + sw128_offset(row, c * 16 + 8, kTileM), pk[4], pk[5], pk[6],
-                                             pk[7]);
+                                if (relu) convert_chunk<BF16, true>(v[j], pk);
+                                else convert_chunk<BF16, false>(v[j], pk);
+                                // columns c*16 .. c*16+15 of this layer are K elements
+                                // c*16 .. c*16+15 of the next: 8 packed TMEM columns
+                                tmem_st8(t_act + c * 8, pk);
                             }
                         }
-                        fence_proxy_async_smem();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(bar(kBarAFull + s));
+                        tmem_wait_st();
                     } else {
-                        const long long grow = static_cast<long long>(tile0 + s) * kTileM + row;
+                        const long long grow = static_cast<long long>(t) * kTileM + row;
                         if (grow < p.n_rows) {
                             float* yrow = p.y + grow * p.out_dim;
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const uint32_t c = grp + 2 * j;
+                            for (int j = 0; j < kChunksPerWarp; ++j) {
+                                const uint32_t c = c0 + kColGroups * j;
                                 if (c < nch) {
-                                    const float* bb = bias_s + L.b_off + c * 16;
                                     float o[16];
 #pragma unroll
-                                    for (int i = 0; i < 16; i += 2) {
-                                        float a0 = __uint_as_float(v[j][i]);
-                                        float a1 = __uint_as_float(v[j][i + 1]);
-                                        add_f32x2(a0, a1, bb[i], bb[i + 1]);
-                                        if (L.relu) {
-                                            a0 = fmaxf(a0, 0.0f);
-                                            a1 = fmaxf(a1, 0.0f);
-                                        }
-                                        o[i] = a0;
-                                        o[i + 1] = a1;
+                                    for (int i = 0; i < 16; ++i) {
+                                        const float a = __uint_as_float(v[j][i]);
+                                        o[i] = relu ? fmaxf(a, 0.0f) : a;
                                     }
                                     const int col0 = c * 16;
                                     if (p.y_vec4 && col0 + 16 <= p.out_dim) {
@@ -423,8 +534,12 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                                 }
                             }
                         }
-                        tc_fence_before();
                     }
+                    // activations written (or, after the last layer, the
+                    // accumulator read): the slot's next MMA may proceed
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(kBarAFull + s));
                 }
             }
         }
@@ -434,26 +549,26 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, p.tmem_cols);
+        tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
-// Packs fp32 [N, K] row-major weights (PyTorch nn.Linear layout) of every
-// layer into the K-major SW128 image the kernel copies straight into shared
-// memory (zero padding to n_pad x katoms*64), and the biases into one fp32
-// array padded to n_pad per layer.
+// Packs fp32 [N, K] row-major weights (PyTorch nn.Linear layout) and fp32
+// biases of every layer into the image the kernel copies straight into
+// shared memory: per layer, the K-major SW128 weight block (zero padded to
+// n_pad x katoms*64) followed by the bias block (n_pad rows x 16 K columns,
+// unswizzled core matrices: column 0 = hi part, column 1 = lo part).
 struct PackLayer {
     const float* W;
     const float* b;
-    uint32_t K, N, n_pad, katoms, w_off, b_off;
+    uint32_t K, N, n_pad, katoms, w_off, bias_off;
 };
 struct PackParams {
     PackLayer layer[kMaxLayers];
     int n_layers;
     int bf16;
     uint8_t* wpack;
-    float* bpack;
-    uint32_t total_chunks;  // sum over layers of n_pad * katoms * 8
+    uint32_t total_chunks;  // sum over layers of n_pad * (katoms * 8 + 2) 16-byte chunks
 };
 
 __global__ void mlp_pack_kernel(const __grid_constant__ PackParams p) {
@@ -461,25 +576,40 @@ __global__ void mlp_pack_kernel(const __grid_constant__ PackParams p) {
         uint32_t rem = g;
         int l = 0;
         for (; l < p.n_layers; ++l) {
-            const uint32_t nc = p.layer[l].n_pad * p.layer[l].katoms * 8;
+            const uint32_t nc = p.layer[l].n_pad * (p.layer[l].katoms * 8 + 2);
             if (rem < nc) break;
             rem -= nc;
         }
         const PackLayer& L = p.layer[l];
-        const uint32_t chunks_per_row = L.katoms * 8;
+        const uint32_t chunks_per_row = L.katoms * 8 + 2;
         const uint32_t n = rem / chunks_per_row;
         const uint32_t kc = rem - n * chunks_per_row;
-        uint32_t w[4];
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        uint8_t* dst;
+        if (kc < L.katoms * 8) {
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const uint32_t k0 = kc * 8 + e;
-            const float v0 = (n < L.N && k0 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0] : 0.0f;
-            const float v1 = (n < L.N && k0 + 1 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0 + 1] : 0.0f;
-            w[e >> 1] = p.bf16 ? pack_bf16x2(v0, v1) : pack_f16x2(v0, v1);
+            for (int e = 0; e < 8; e += 2) {
+                const uint32_t k0 = kc * 8 + e;
+                const float v0 = (n < L.N && k0 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0] : 0.0f;
+                const float v1 = (n < L.N && k0 + 1 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0 + 1] : 0.0f;
+                w[e >> 1] = p.bf16 ? pack_bf16x2(v0, v1) : pack_f16x2(v0, v1);
+            }
+            dst = p.wpack + L.w_off + sw128_offset(n, kc * 8, L.n_pad);
+        } else {
+            const uint32_t half = kc - L.katoms * 8;  // K columns 0-7 or 8-15 of the bias block
+            if (half == 0) {
+                const float b = (n < L.N) ? L.b[n] : 0.0f;
+                if (p.bf16) {
+                    const float hi = __bfloat162float(__float2bfloat16_rn(b));
+                    w[0] = pack_bf16x2(hi, b - hi);
+                } else {
+                    const float hi = __half2float(__float2half_rn(b));
+                    w[0] = pack_f16x2(hi, b - hi);
+                }
+            }
+            dst = p.wpack + L.w_off + L.bias_off + k16_plain_offset(n, half * 8);
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.wpack + L.w_off + sw128_offset(n, kc * 8, L.n_pad));
-        *dst = make_uint4(w[0], w[1], w[2], w[3]);
-        if (kc == 0) p.bpack[L.b_off + n] = (n < L.N) ? L.b[n] : 0.0f;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 

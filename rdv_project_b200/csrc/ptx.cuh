@@ -73,14 +73,44 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Same, but the thread may sleep up to `hint_ns` (it resumes as soon as the
+// phase completes), so a waiting warp does not take issue slots from the
+// warps sharing its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Non-blocking test of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Returns false (and
 // raises *abort) if the CTA was aborted or the wait ran past the limit.
+// Each try sleeps up to 0.5 ms, so the abort flag and the time limit are
+// still checked regularly.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort,
                                           uint32_t* status, uint32_t code) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;
         if (*abort) return false;
         if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
             *abort = 1u;
@@ -139,15 +169,28 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (f16 or bf16 inputs,
-// f32 accumulate), issued by one thread.
+// f32 accumulate), issued by one thread. No "memory" clobber: the operands
+// are ordered by the mbarrier waits and tcgen05 fences around the issue, and
+// a clobber would stop the compiler from scheduling descriptor arithmetic
+// around the (volatile, so still in-order) MMA instructions.
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Same with the A operand read from tensor memory (M=128 rows = lanes, 16-bit
+// elements packed two per 32-bit column: one K=16 step spans 8 columns).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive once on `bar` when every previously issued tcgen05 op of this
@@ -168,6 +211,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 8 consecutive 32-bit columns; thread i writes lane (base + i).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+        "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // UMMA shared-memory matrix descriptor for a K-major operand in the
 // canonical 128-byte-swizzled layout: rows of 128 bytes (64 x 16-bit
 // elements), 8-row core groups 1024 bytes apart (SBO), 16-byte chunks
@@ -184,6 +236,24 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     d |= static_cast<uint64_t>(1u) << 46;             // descriptor version (sm_100)
     d |= static_cast<uint64_t>(2u) << 61;             // SWIZZLE_128B
     return d;
+}
+
+// Descriptor for a K-major operand with no swizzle ("interleaved" core
+// matrices): 8 rows x 16 bytes per core matrix stored contiguously, the two
+// 8-element K halves of a K=16 slice 128 bytes apart (LBO), 8-row groups 256
+// bytes apart (SBO). Element (row, k), k < 16, sits at
+// (row/8)*256 + (k/8)*128 + (row%8)*16 + (k%8)*2.
+__device__ __forceinline__ uint64_t umma_desc_k16_plain(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(128u >> 4) << 16;      // LBO
+    d |= static_cast<uint64_t>(256u >> 4) << 32;      // SBO
+    d |= static_cast<uint64_t>(1u) << 46;             // version
+    return d;                                         // layout 0 = no swizzle
+}
+
+__host__ __device__ __forceinline__ uint32_t k16_plain_offset(uint32_t row, uint32_t k) {
+    return (row >> 3) * 256u + (k >> 3) * 128u + (row & 7u) * 16u + (k & 7u) * 2u;
 }
 
 // Instruction descriptor, kind::f16: D f32, A/B f16 (0) or bf16 (1), both

@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -42,7 +43,7 @@ struct DeviceInfo {
     bool init = false;
     int sm_count = 0;
     int max_smem_optin = 0;
-    size_t tc_smem_set = 0;
+    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2] = {};
     size_t simt_smem_set = 0;
 };
 constexpr int kMaxDevices = 64;
@@ -80,35 +81,33 @@ struct PackLayout {
     bool ok = false;
     uint32_t k_pad[rdvb::mlp_tc::kMaxLayers], n_pad[rdvb::mlp_tc::kMaxLayers];
     uint32_t w_off[rdvb::mlp_tc::kMaxLayers], w_bytes[rdvb::mlp_tc::kMaxLayers];
-    uint32_t b_off[rdvb::mlp_tc::kMaxLayers];
-    uint32_t total_w = 0;      // bytes of all weight blocks
-    uint32_t bias_floats = 0;  // floats of the padded bias block
-    uint32_t bias_byte_off = 0;
+    uint32_t bias_off[rdvb::mlp_tc::kMaxLayers];
+    uint32_t total_w = 0;  // bytes of all layer blocks
     uint32_t max_w_bytes = 0;
     int64_t total_bytes = 0;
 };
 
+// Per layer: the K-major SW128 weight block (n_pad rows x katoms*128 bytes)
+// followed by the bias block (n_pad rows x 32 bytes), padded to 1 KB so the
+// next layer block stays 1 KB aligned.
 PackLayout pack_layout(int n_layers, const int* dims) {
     PackLayout L;
     if (n_layers < 1 || n_layers > rdvb::mlp_tc::kMaxLayers || dims == nullptr) return L;
     for (int l = 0; l <= n_layers; ++l)
         if (dims[l] < 1 || dims[l] > static_cast<int>(rdvb::mlp_tc::kMaxWidth)) return L;
-    uint32_t w = 0, b = 0;
+    uint32_t w = 0;
     for (int l = 0; l < n_layers; ++l) {
         L.k_pad[l] = round_up(dims[l], 16);
         L.n_pad[l] = round_up(dims[l + 1], 16);
         const uint32_t katoms = (L.k_pad[l] + 63) / 64;
         L.w_off[l] = w;
-        L.w_bytes[l] = L.n_pad[l] * katoms * 128u;
-        L.b_off[l] = b;
+        L.bias_off[l] = L.n_pad[l] * katoms * 128u;
+        L.w_bytes[l] = round_up(L.bias_off[l] + L.n_pad[l] * 32u, 1024);
         w += L.w_bytes[l];
-        b += L.n_pad[l];
         L.max_w_bytes = std::max(L.max_w_bytes, L.w_bytes[l]);
     }
     L.total_w = w;
-    L.bias_floats = b;
-    L.bias_byte_off = round_up(w, 256);
-    L.total_bytes = static_cast<int64_t>(L.bias_byte_off) + 4ll * b;
+    L.total_bytes = w;
     L.ok = true;
     return L;
 }
@@ -146,73 +145,109 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     p.x = x;
     p.y = y;
     p.wpack = static_cast<const uint8_t*>(packed);
-    p.bpack = reinterpret_cast<const float*>(static_cast<const uint8_t*>(packed) + L.bias_byte_off);
     p.n_rows = n_rows;
     p.n_tiles = static_cast<int>((n_rows + kTileM - 1) / kTileM);
     p.in_dim = dims[0];
     p.out_dim = dims[n_layers];
     p.x_dtype = x_dtype;
     p.relu_in = input_relu ? 1 : 0;
-    p.bf16 = (math == RDVB_MATH_BF16) ? 1 : 0;
+    const int bf16 = (math == RDVB_MATH_BF16) ? 1 : 0;
     p.n_layers = n_layers;
     p.w_total_bytes = L.total_w;
-    p.bias_floats = L.bias_floats;
     for (int l = 0; l < n_layers; ++l) {
         p.layer[l].k_pad = L.k_pad[l];
         p.layer[l].n_pad = L.n_pad[l];
         p.layer[l].w_off = L.w_off[l];
         p.layer[l].w_bytes = L.w_bytes[l];
-        p.layer[l].b_off = L.b_off[l];
-        p.layer[l].idesc = rdvb::umma_idesc_f16(L.n_pad[l], p.bf16);
+        p.layer[l].bias_off = L.bias_off[l];
+        p.layer[l].idesc = rdvb::umma_idesc_f16(L.n_pad[l], bf16);
         p.layer[l].relu = (flags[l] & RDVB_LAYER_RELU) ? 1u : 0u;
     }
     const int esize = x_dtype == RDVB_F32 ? 4 : 2;
     p.x_stage_bytes = round_up(static_cast<uint32_t>(kTileM) * dims[0] * esize, 128);
-    p.off_w = kSlots * kABytes;
+    p.y_vec4 = (p.out_dim % 4 == 0 && aligned(y, 16)) ? 1 : 0;
     const uint32_t budget = static_cast<uint32_t>(dev->max_smem_optin);
-    auto total_for = [&](uint32_t wsize) {
-        const uint32_t off_x = p.off_w + wsize;
-        const uint32_t off_bias = off_x + kSlots * p.x_stage_bytes;
-        const uint32_t off_bar = round_up(off_bias + 4u * L.bias_floats, 16);
-        return std::make_pair(off_bar + kBarBlockBytes + 1024u, std::make_pair(off_x, std::make_pair(off_bias, off_bar)));
-    };
-    uint32_t wsize = 0;
-    const uint32_t resident_size = round_up(L.total_w, 1024);
-    if (resident_size <= 96u * 1024u && total_for(resident_size).first <= budget) {
-        p.resident = 1;
-        p.w_stages = 1;
-        wsize = resident_size;
-        p.w_slot_bytes = resident_size;
-    } else {
-        p.resident = 0;
-        p.w_slot_bytes = round_up(L.max_w_bytes, 1024);
-        p.w_stages = 0;
+
+    // TMEM per slot: the fp32 accumulator (widest layer output) and the
+    // 16-bit activation tile that feeds the next layer (widest hidden input,
+    // two elements per column), both in multiples of 32 columns.
+    uint32_t n_max = 0, act_k_max = 16;
+    for (int l = 0; l < n_layers; ++l) n_max = std::max(n_max, L.n_pad[l]);
+    for (int l = 1; l < n_layers; ++l) act_k_max = std::max(act_k_max, L.k_pad[l]);
+    p.acc_stride = round_up(n_max, 32);
+    p.act_stride = round_up(act_k_max / 2, 32);
+    p.a0_bytes = ((L.k_pad[0] + 63) / 64) * kAtomBytes;
+
+    // Shared-memory plan for a slot count: layer-0 A tiles, weights
+    // (resident when they fit, else a ring of >= 2 layer blocks), one input
+    // staging buffer per slot, biases, barriers. Returns the dynamic smem
+    // bytes (0 = no fit).
+    auto plan = [&](int slots, Params& q) -> uint32_t {
+        if (static_cast<uint32_t>(slots) * (q.acc_stride + q.act_stride) > kTmemCols) return 0;
+        q.act_base = slots * q.acc_stride;
+        q.off_w = slots * q.a0_bytes;
+        auto place = [&](uint32_t wsize) -> uint32_t {
+            q.off_x = q.off_w + wsize;
+            q.off_ones = q.off_x + slots * q.x_stage_bytes;  // 1 KB multiple: x stages are 128 B multiples
+            q.off_ones = round_up(q.off_ones, 1024);
+            q.off_bar = q.off_ones + kOnesBytes;
+            return q.off_bar + kBarBlockBytes + 1024u;
+        };
+        const uint32_t resident_size = round_up(L.total_w, 1024);
+        uint32_t total = place(resident_size);
+        if (total <= budget) {
+            q.resident = 1;
+            q.w_stages = 1;
+            q.w_slot_bytes = resident_size;
+            return total;
+        }
+        q.resident = 0;
+        q.w_slot_bytes = round_up(L.max_w_bytes, 1024);
         for (int st = 3; st >= 2; --st) {
-            if (total_for(st * p.w_slot_bytes).first <= budget) {
-                p.w_stages = st;
-                break;
+            total = place(st * q.w_slot_bytes);
+            if (total <= budget) {
+                q.w_stages = st;
+                return total;
             }
         }
-        if (p.w_stages == 0) return RDVB_OK;  // does not fit: CUDA-core path
-        wsize = p.w_stages * p.w_slot_bytes;
+        return 0;
+    };
+    int slots = 0;
+    uint32_t smem = 0;
+    int forced = 0;
+    if (const char* env = getenv("RDVB_MLP_SLOTS")) forced = atoi(env);
+    for (int sl = kMaxSlots; sl >= 2; --sl) {
+        if (forced && sl != forced) continue;
+        Params q = p;
+        const uint32_t need = plan(sl, q);
+        if (need) {
+            p = q;
+            slots = sl;
+            smem = need;
+            break;
+        }
     }
-    auto t = total_for(wsize);
-    const uint32_t smem = t.first;
-    p.off_x = t.second.first;
-    p.off_bias = t.second.second.first;
-    p.off_bar = t.second.second.second;
-    p.tmem_cols = 256;
-    p.y_vec4 = (p.out_dim % 4 == 0 && aligned(y, 16)) ? 1 : 0;
+    if (!slots) return RDVB_OK;  // does not fit: CUDA-core path
 
-    if (dev->tc_smem_set < smem) {
-        cudaError_t e = cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(mlp_tc): %s", cudaGetErrorString(e));
-        dev->tc_smem_set = smem;
-    }
-    const int pairs = (p.n_tiles + kSlots - 1) / kSlots;
-    const int grid = std::min(dev->sm_count, pairs);
-    mlp_tc_kernel<<<grid, kThreads, smem, stream>>>(p);
+    int rc = RDVB_OK;
+    auto go = [&](auto kernel, int sl) {
+        if (dev->tc_smem_set[sl][bf16] < smem) {
+            cudaError_t e =
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) {
+                rc = fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(mlp_tc<%d>): %s", sl, cudaGetErrorString(e));
+                return;
+            }
+            dev->tc_smem_set[sl][bf16] = smem;
+        }
+        const int groups = (p.n_tiles + sl - 1) / sl;
+        const int grid = std::min(dev->sm_count, groups);
+        kernel<<<grid, kThreads, smem, stream>>>(p);
+    };
+    if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1>, 4) : go(mlp_tc_kernel<4, 0>, 4);
+    else if (slots == 3) bf16 ? go(mlp_tc_kernel<3, 1>, 3) : go(mlp_tc_kernel<3, 0>, 3);
+    else bf16 ? go(mlp_tc_kernel<2, 1>, 2) : go(mlp_tc_kernel<2, 0>, 2);
+    if (rc) return rc;
     *taken = true;
     return check_launch("mlp_tc_kernel");
 }
@@ -308,7 +343,6 @@ int rdvb_mlp_pack(int n_layers, const int* dims, const float* const* weights, co
     pp.n_layers = n_layers;
     pp.bf16 = operand == RDVB_BF16 ? 1 : 0;
     pp.wpack = static_cast<uint8_t*>(packed);
-    pp.bpack = reinterpret_cast<float*>(static_cast<uint8_t*>(packed) + L.bias_byte_off);
     uint32_t chunks = 0;
     for (int l = 0; l < n_layers; ++l) {
         if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "weights[%d]/biases[%d] is NULL", l, l);
@@ -320,8 +354,8 @@ int rdvb_mlp_pack(int n_layers, const int* dims, const float* const* weights, co
         pl.n_pad = L.n_pad[l];
         pl.katoms = (L.k_pad[l] + 63) / 64;
         pl.w_off = L.w_off[l];
-        pl.b_off = L.b_off[l];
-        chunks += pl.n_pad * pl.katoms * 8;
+        pl.bias_off = L.bias_off[l];
+        chunks += pl.n_pad * (pl.katoms * 8 + 2);
     }
     pp.total_chunks = chunks;
     const int threads = 256;

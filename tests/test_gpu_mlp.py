@@ -82,6 +82,24 @@ def test_linearfast_chain_matches_oracle(rdv, cuda_device, dims, n_rows):
     assert rdv.device_status() == 0
 
 
+@pytest.mark.parametrize("slots", [2, 3, 4])
+@pytest.mark.parametrize("dims", [[32] + [128] * 8 + [16], [3, 64, 64, 64, 64, 4]])
+def test_every_slot_count_over_many_rounds(rdv, cuda_device, monkeypatch, slots, dims):
+    """Forces the number of tiles in flight per CTA (RDVB_MLP_SLOTS) on a
+    batch large enough for several rounds per CTA plus a partial last round
+    (streamed weights for the 128-wide chain, resident for the 64-wide one)."""
+    monkeypatch.setenv("RDVB_MLP_SLOTS", str(slots))
+    layers = _layers(dims, "f16", seed=slots * 31 + len(dims))
+    n_rows = 128 * (148 * slots * 2 + 37) + 96
+    x = np.random.default_rng(slots).standard_normal((n_rows, dims[0])).astype(np.float32)
+    m = _build(rdv, layers, cuda_device)
+    y = m(torch.from_numpy(x).to(cuda_device)).as_tensor("torch").cpu().numpy()
+    sel = np.arange(0, n_rows, 13)
+    ref = omlp.mlp_forward(x[sel], layers)
+    _check(y[sel], ref, TOL_F16, TIGHT_F16)
+    assert rdv.device_status() == 0
+
+
 def test_config2_architecture_full_width(rdv, cuda_device):
     dims = [32] + [128] * 8 + [16]
     layers = _layers(dims, "f16", seed=2, bias_scale=0.0)
