@@ -111,6 +111,56 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
  * (rdv/domain/nn.py:362-374, rdv/shaders/tensors/relu_tensor_op.h). */
 int rdvb_relu(const float* x, float* y, int64_t n, void* stream);
 
+/* ----------------------------------------------------------- 3x3 conv ----
+ * 'Same' (zero padding 1), stride-1 3x3 convolution of NHWC tensors,
+ * x [n, h, w, cin] -> y [n, h, w, cout], weights [3, 3, cin, cout]
+ * (channels-last, the reference TensorOp layout), bias [cout].
+ *
+ * Replaces: Conv2DTensorOpWinograd3x3 (rdv/domain/nn.py:1002-1087, kernel
+ * rdv/shaders/tensors/conv2d_tensor_op_winograd3x3.h:95-178, filter
+ * transform _winograd_transform_weight nn.py:522-538), generalised to a batch
+ * of images, odd h/w and cin, cout up to 64 (multiples of 16); the reference
+ * takes one image, even h and w, cin/cout <= 48.
+ */
+
+/* Bytes of the packed filter operand for (variant, cin, cout); 0 if the
+ * combination is not supported. */
+int64_t rdvb_winograd_packed_bytes(int variant, int cin, int cout);
+
+/* Filter transform U = G g G^T of fp32 weights w_33io [3, 3, cin, cout]
+ * (device), computed in fp32 and rounded to float16, like
+ * _winograd_transform_weight (rdv/domain/nn.py:525-538).
+ *  u_plain   optional (may be NULL): the reference's flat float16 array
+ *            [16][cin][cout]
+ *  u_packed  optional (may be NULL): the tensor-core operand consumed by
+ *            rdvb_conv3x3_winograd, rdvb_winograd_packed_bytes() bytes,
+ *            256-byte aligned; requires cin, cout multiples of 16, <= 64
+ * Only RDVB_WINOGRAD_F2X2 is implemented; RDVB_WINOGRAD_F4X4 returns
+ * RDVB_ERR_UNSUPPORTED. */
+int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int variant, void* u_plain,
+                                   void* u_packed, void* stream);
+
+/* Winograd convolution: input transform (fp32, staged float16), one tcgen05
+ * GEMM per transform position (fp32 accumulation), inverse transform and bias
+ * (fp32), fused in one kernel.
+ *  x_dtype   RDVB_F32 or RDVB_F16 (x 16-byte aligned)
+ *  u_packed  rdvb_winograd_filter_transform output for these channels
+ *  bias      [cout] fp32, or NULL for zero
+ *  y_dtype   RDVB_F32 (the reference's output type) or RDVB_F16
+ *            (y 16-byte aligned) */
+int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int cin, int cout,
+                          const void* u_packed, int variant, const float* bias, void* y, int y_dtype,
+                          void* stream);
+
+/* Direct 'same' (padding kh/2, kw/2), stride-1 convolution in fp32 on CUDA
+ * cores: y = bias + sum over (kh, kw, cin) of x * w, one fused multiply-add
+ * per tap. Replaces Conv2DTensorOp (rdv/domain/nn.py:414-469,
+ * rdv/shaders/tensors/conv2d_tensor_op.h:21-87); also the on-device check of
+ * the Winograd path. x RDVB_F32 or RDVB_F16; weight [kh, kw, cin, cout] fp32;
+ * cout a multiple of 8; weight and y 16-byte aligned. */
+int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
+                       const float* weight, const float* bias, float* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -134,11 +134,32 @@ def conv3x3_direct(x_nhwc: np.ndarray, w_33io: np.ndarray, bias: np.ndarray) -> 
     return y
 
 
+def conv2d_direct(x_nhwc: np.ndarray, w_hwio: np.ndarray, bias) -> np.ndarray:
+    """'same' (padding KH//2, KW//2), stride-1 KHxKW cross-correlation in
+    float64, the general form of Conv2DTensorOp (conv2d_tensor_op.h:21-87:
+    pad_h = KH / 2, ih = h + kh - pad_h)."""
+    x = np.asarray(x_nhwc, dtype=np.float64)
+    w = np.asarray(w_hwio, dtype=np.float64)
+    n, H, W, cin = x.shape
+    KH, KW, _, cout = w.shape
+    ph, pw = KH // 2, KW // 2
+    xp = np.zeros((n, H + KH - 1, W + KW - 1, cin), dtype=np.float64)
+    xp[:, ph:ph + H, pw:pw + W, :] = x
+    y = np.zeros((n, H, W, cout), dtype=np.float64)
+    if bias is not None:
+        y += np.asarray(bias, dtype=np.float64)
+    for kh in range(KH):
+        for kw in range(KW):
+            y += np.einsum("nhwc,cd->nhwd", xp[:, kh:kh + H, kw:kw + W, :], w[kh, kw])
+    return y
+
+
 def conv3x3_winograd(x_nhwc: np.ndarray, w_33io: np.ndarray, bias: np.ndarray,
                      variant: str = "F2x2", staged: bool = True) -> np.ndarray:
-    """Winograd convolution with the reference's precision recipe: transforms
-    in fp32 arithmetic (carried here in float64), U and V staged float16 when
-    `staged`, per-position GEMM and inverse transform in float64, + bias.
+    """Winograd convolution with the reference's precision recipe: U and V
+    staged float16 when `staged` (F2x2: V from the reference's fp32 transform
+    in its operation order; F4x4: B^T d B in float64, then float32, then
+    float16), per-position GEMM and inverse transform in float64, + bias.
     H and W must be multiples of the output tile size m."""
     v = VARIANTS[variant]
     m, a = v["m"], v["a"]
@@ -158,9 +179,16 @@ def conv3x3_winograd(x_nhwc: np.ndarray, w_33io: np.ndarray, bias: np.ndarray,
     d = xp[:, idx_h][:, :, :, idx_w]  # n, th, a, tw, a, cin
     d = d.transpose(0, 1, 3, 2, 4, 5)  # n, th, tw, a, a, cin
     BT = v["BT"]
-    V = np.einsum("ij,nxyjkc,lk->nxyilc", BT, d, BT)  # B^T d B
-    if staged:
-        V = stage(V.astype(np.float32), "f16").astype(np.float64)
+    if staged and variant == "F2x2":
+        # the reference's own fp32 transform, in its operation order
+        # (_winograd_fwd, conv2d_tensor_op_winograd3x3.h:59-78), then float16
+        dc = np.ascontiguousarray(d.astype(np.float32).transpose(0, 1, 2, 5, 3, 4)).reshape(-1, 16)
+        V = winograd_fwd_f23(dc).reshape(n, th, tw, cin, 4, 4).transpose(0, 1, 2, 4, 5, 3)
+        V = stage(np.ascontiguousarray(V), "f16").astype(np.float64)
+    else:
+        V = np.einsum("ij,nxyjkc,lk->nxyilc", BT, d, BT)  # B^T d B
+        if staged:
+            V = stage(V.astype(np.float32), "f16").astype(np.float64)
     if staged:
         U = filter_transform(w_33io, variant).astype(np.float64)  # [a*a, cin, cout]
     else:

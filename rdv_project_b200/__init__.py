@@ -13,6 +13,8 @@ from .core import (RDVObject, wrap, profiling, reset_submit_times, profiling_sub
 from .maps import (Map, Identity, X, ReLU, relu, Linear, LinearFast, LinearFastBF16, linear, Composite)
 from .tensor_ops import (TensorOperation, ReLUTensorOp, LinearTensorOp, LinearTensorOpFast, LinearTensorOpMine,
                          LinearTensorOpSimple, LinearTensorOpSmall)
+from .conv import (Conv2DTensorOp, Conv2DTensorOpWinograd3x3, Conv3x3Winograd, conv2d_direct,
+                   _winograd_transform_weight)
 from ._native import RdvbError, device_status
 
 __all__ = [
@@ -20,5 +22,6 @@ __all__ = [
     "Map", "Identity", "X", "ReLU", "relu", "Linear", "LinearFast", "LinearFastBF16", "linear", "Composite",
     "TensorOperation", "ReLUTensorOp", "LinearTensorOp", "LinearTensorOpFast", "LinearTensorOpMine",
     "LinearTensorOpSimple", "LinearTensorOpSmall",
+    "Conv2DTensorOp", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
     "RdvbError", "device_status",
 ]

@@ -33,6 +33,12 @@ SIGNATURES = {
     "rdvb_mlp_pack": (_c_int, [_c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),
     "rdvb_mlp_forward": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp]),
     "rdvb_relu": (_c_int, [_vp, _vp, _c_i64, _vp]),
+    "rdvb_winograd_packed_bytes": (_c_i64, [_c_int, _c_int, _c_int]),
+    "rdvb_winograd_filter_transform": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "rdvb_conv3x3_winograd": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_int, _vp, _vp,
+                                       _c_int, _vp]),
+    "rdvb_conv2d_direct": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
+                                    _vp, _vp]),
 }
 
 

@@ -1,0 +1,195 @@
+"""3x3 convolution operators (the reference's conv TensorOperations,
+rdv/domain/nn.py:414-469 and 1002-1087) and a batched NHWC Winograd
+operator.
+
+* ``Conv2DTensorOp(x, weight, bias, H, W)``: 'same', stride-1 KHxKW
+  convolution in exact fp32 (CUDA cores) -> rdvb_conv2d_direct.
+* ``Conv2DTensorOpWinograd3x3(x, weight, bias, H, W)``: Winograd F(2x2,3x3)
+  -> rdvb_winograd_filter_transform (once, at construction, like the
+  reference's ``_winograd_transform_weight``) + rdvb_conv3x3_winograd.
+  Same inputs, layouts and assertion messages as the reference, except
+  that in/out channels may go up to 64 (reference: 48, a limit of its 48 KB
+  shared-memory budget) and (H/2)*(W/2) need not be a multiple of 32 (the
+  reference's workgroup size; the B200 kernel masks partial blocks).
+* ``Conv3x3Winograd(weight, bias)``: the same kernel on batched NHWC
+  tensors ``[N, H, W, CIN]`` (float32 or float16, any H/W), output float32
+  or float16 -- the form the BASELINE config-3 workload uses.
+* ``_winograd_transform_weight(weight, in_channels, out_channels)``: the
+  reference's helper (nn.py:525-538), computed on the device; returns the
+  flat float16 ``[16 * CIN * COUT]`` buffer.
+
+Inputs of the TensorOperation forms are ``[H*W, channels]`` row-major
+(channels-last, H*W flattened), weights ``[3, 3, CIN, COUT]``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+from .core import RDVObject, _timed, current_device, stream_handle, wrap
+from .tensor_ops import TensorOperation, _as_op_input, _f32_view
+
+_DTYPES = {torch.float32: N.RDVB_F32, torch.float16: N.RDVB_F16}
+MAX_WINOGRAD_CHANNELS = 64
+
+
+def _dev_f32(t) -> torch.Tensor:
+    t = t._tensor if isinstance(t, RDVObject) else torch.as_tensor(t)
+    return t.to(device=current_device(), dtype=torch.float32).contiguous()
+
+
+def _filter_transform(w33io: torch.Tensor, cin: int, cout: int, plain: bool, packed: bool):
+    lib = N.lib()
+    u_plain = torch.empty(16 * cin * cout, dtype=torch.float16, device=w33io.device) if plain else None
+    u_packed = None
+    if packed:
+        nbytes = lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F2X2, cin, cout)
+        if nbytes <= 0:
+            raise N.RdvbError(f"no packed Winograd operand for cin={cin}, cout={cout}")
+        u_packed = torch.empty(int(nbytes), dtype=torch.uint8, device=w33io.device)
+    N.check(lib.rdvb_winograd_filter_transform(
+        w33io.data_ptr(), cin, cout, N.RDVB_WINOGRAD_F2X2,
+        u_plain.data_ptr() if plain else None, u_packed.data_ptr() if packed else None, stream_handle()),
+        "rdvb_winograd_filter_transform")
+    return u_plain, u_packed
+
+
+def _winograd_transform_weight(weight, in_channels: int, out_channels: int) -> torch.Tensor:
+    """U = G g G^T of a [3, 3, CIN, COUT] weight, fp32 arithmetic, stored
+    float16 as a flat [16][CIN][COUT] buffer (rdv/domain/nn.py:525-538)."""
+    w = _dev_f32(weight)
+    assert tuple(w.shape) == (3, 3, in_channels, out_channels), "weight must be [3, 3, in_channels, out_channels]"
+    u_plain, _ = _filter_transform(w, in_channels, out_channels, plain=True, packed=False)
+    return u_plain
+
+
+def _launch_winograd(x: torch.Tensor, n: int, h: int, w: int, cin: int, cout: int, u_packed: torch.Tensor,
+                     bias, y: torch.Tensor) -> None:
+    N.check(N.lib().rdvb_conv3x3_winograd(
+        x.data_ptr(), _DTYPES[x.dtype], n, h, w, cin, cout, u_packed.data_ptr(), N.RDVB_WINOGRAD_F2X2,
+        bias.data_ptr() if bias is not None else None, y.data_ptr(), _DTYPES[y.dtype], stream_handle()),
+        "rdvb_conv3x3_winograd")
+
+
+class Conv2DTensorOp(TensorOperation):
+    """'same'-padded, stride-1 KHxKW convolution in exact fp32
+    (rdv/domain/nn.py:414-469, rdv/shaders/tensors/conv2d_tensor_op.h)."""
+
+    def __init__(self, x, weight, bias, H: int, W: int) -> None:
+        data, shape, upstream = _as_op_input(x)
+        assert len(shape) == 2, "Conv2DTensorOp requires a 2D (H*W, in_channels) input"
+        hw, in_channels = shape
+        assert hw == H * W, f"H*W ({H * W}) must match x's own row count ({hw})"
+        weight = weight if isinstance(weight, RDVObject) else wrap(weight)
+        bias = bias if isinstance(bias, RDVObject) else wrap(bias)
+        assert len(weight.shape) == 4, "weight must be [KH, KW, in_channels, out_channels]"
+        kh, kw, weight_in_channels, out_channels = weight.shape
+        assert weight_in_channels == in_channels, "weight's own in_channels must match x's own trailing dim"
+        assert tuple(bias.shape) == (out_channels,), "bias must be [out_channels]"
+        assert in_channels % 8 == 0, f"in_channels ({in_channels}) must be a multiple of 8"
+        assert out_channels % 8 == 0, f"out_channels ({out_channels}) must be a multiple of 8"
+        self.KH, self.KW, self.CIN, self.COUT, self.H, self.W = kh, kw, in_channels, out_channels, H, W
+        self.x_buf = data
+        self.weight = weight
+        self.bias = bias
+        self._upstream = upstream
+        super().__init__([hw, out_channels])
+
+    def _run(self):
+        x = _f32_view(self.x_buf)
+        w = _f32_view(self.weight)
+        b = _f32_view(self.bias)
+        y = self.result._tensor
+        N.check(N.lib().rdvb_conv2d_direct(
+            x.data_ptr(), N.RDVB_F32, 1, self.H, self.W, self.CIN, self.COUT, self.KH, self.KW, w.data_ptr(),
+            b.data_ptr(), y.data_ptr(), stream_handle()), "rdvb_conv2d_direct")
+
+
+class Conv2DTensorOpWinograd3x3(TensorOperation):
+    """'same'-padded, stride-1 3x3 convolution via Winograd F(2x2, 3x3)
+    (rdv/domain/nn.py:1002-1087). The weight is transformed once, at
+    construction, into U = G g G^T (float16); later in-place weight edits are
+    not seen, as in the reference."""
+
+    _TILE_ROWS = 1
+    _TILE_COLS = 16
+
+    def __init__(self, x, weight, bias, H: int, W: int) -> None:
+        data, shape, upstream = _as_op_input(x)
+        assert len(shape) == 2, "Conv2DTensorOpWinograd3x3 requires a 2D (H*W, in_channels) input"
+        hw, in_channels = shape
+        assert hw == H * W, f"H*W ({H * W}) must match x's own row count ({hw})"
+        weight = weight if isinstance(weight, RDVObject) else wrap(weight)
+        bias = bias if isinstance(bias, RDVObject) else wrap(bias)
+        assert tuple(weight.shape[:2]) == (3, 3), "weight must be [3, 3, in_channels, out_channels]"
+        _, _, weight_in_channels, out_channels = weight.shape
+        assert weight_in_channels == in_channels, "weight's own in_channels must match x's own trailing dim"
+        assert tuple(bias.shape) == (out_channels,), "bias must be [out_channels]"
+        assert H % 2 == 0, f"H ({H}) must be even"
+        assert W % 2 == 0, f"W ({W}) must be even"
+        assert in_channels % 16 == 0, f"in_channels ({in_channels}) must be a multiple of 16"
+        assert out_channels % 16 == 0, f"out_channels ({out_channels}) must be a multiple of 16"
+        assert in_channels <= MAX_WINOGRAD_CHANNELS, \
+            f"in_channels ({in_channels}) must be at most {MAX_WINOGRAD_CHANNELS} (see this op's own docstring)"
+        assert out_channels <= MAX_WINOGRAD_CHANNELS, \
+            f"out_channels ({out_channels}) must be at most {MAX_WINOGRAD_CHANNELS} (see this op's own docstring)"
+        self.CIN, self.COUT, self.H, self.W = in_channels, out_channels, H, W
+        self.x_buf = data
+        self.bias = bias
+        self._upstream = upstream
+        w32 = _f32_view(weight)
+        self.weight_u, self._u_packed = _filter_transform(w32, in_channels, out_channels, plain=True, packed=True)
+        super().__init__([hw, out_channels])
+
+    def _run(self):
+        x = _f32_view(self.x_buf)
+        b = _f32_view(self.bias)
+        _launch_winograd(x, 1, self.H, self.W, self.CIN, self.COUT, self._u_packed, b, self.result._tensor)
+
+
+class Conv3x3Winograd:
+    """Batched NHWC 'same' 3x3 convolution via the fused Winograd F(2x2,3x3)
+    kernel: ``Conv3x3Winograd(weight[3,3,CIN,COUT], bias[COUT] | None)``,
+    then ``conv(x[N,H,W,CIN], out_dtype=torch.float32, out=None)``. x may
+    be float32 or float16; channels are multiples of 16 up to 64."""
+
+    def __init__(self, weight, bias=None) -> None:
+        w = _dev_f32(weight)
+        assert w.dim() == 4 and tuple(w.shape[:2]) == (3, 3), "weight must be [3, 3, in_channels, out_channels]"
+        self.cin, self.cout = int(w.shape[2]), int(w.shape[3])
+        self.bias = _dev_f32(bias) if bias is not None else None
+        if self.bias is not None:
+            assert tuple(self.bias.shape) == (self.cout,), "bias must be [out_channels]"
+        _, self.u_packed = _filter_transform(w, self.cin, self.cout, plain=False, packed=True)
+
+    def __call__(self, x, out_dtype=torch.float32, out: torch.Tensor | None = None) -> torch.Tensor:
+        x = x._tensor if isinstance(x, RDVObject) else x
+        assert x.dim() == 4 and x.shape[3] == self.cin, f"x must be [N, H, W, {self.cin}]"
+        assert x.dtype in _DTYPES, "x must be float32 or float16"
+        if x.device != current_device() or not x.is_contiguous():
+            x = x.to(current_device()).contiguous()
+        n, h, w, _ = (int(v) for v in x.shape)
+        if out is None:
+            out = torch.empty((n, h, w, self.cout), dtype=out_dtype, device=x.device)
+        assert out.shape == (n, h, w, self.cout) and out.dtype in _DTYPES and out.is_contiguous()
+        with _timed():
+            _launch_winograd(x, n, h, w, self.cin, self.cout, self.u_packed, self.bias, out)
+        return out
+
+
+def conv2d_direct(x: torch.Tensor, weight, bias=None) -> torch.Tensor:
+    """fp32 'same' direct convolution of NHWC x [N, H, W, CIN] (float32 or
+    float16) with weight [KH, KW, CIN, COUT]: the on-device check of the
+    Winograd path."""
+    w = _dev_f32(weight)
+    b = _dev_f32(bias) if bias is not None else None
+    x = x.to(current_device()).contiguous()
+    n, h, wd, cin = (int(v) for v in x.shape)
+    kh, kw, wcin, cout = (int(v) for v in w.shape)
+    assert wcin == cin, "weight's own in_channels must match x's own trailing dim"
+    y = torch.empty((n, h, wd, cout), dtype=torch.float32, device=x.device)
+    with _timed():
+        N.check(N.lib().rdvb_conv2d_direct(
+            x.data_ptr(), _DTYPES[x.dtype], n, h, wd, cin, cout, kh, kw, w.data_ptr(),
+            b.data_ptr() if b is not None else None, y.data_ptr(), stream_handle()), "rdvb_conv2d_direct")
+    return y

@@ -101,16 +101,27 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Suspend-time hint of the bounded waits below (nanoseconds).
+#ifndef RDVB_SLEEP_HINT_NS
+#define RDVB_SLEEP_HINT_NS 500000u
+#endif
+#ifndef RDVB_SPIN_TRIES
+#define RDVB_SPIN_TRIES 0
+#endif
+
 // Waits for the phase with the given parity to complete. Returns false (and
 // raises *abort) if the CTA was aborted or the wait ran past the limit.
-// Each try sleeps up to 0.5 ms, so the abort flag and the time limit are
-// still checked regularly.
+// Each try sleeps up to RDVB_SLEEP_HINT_NS, so the abort flag and the time
+// limit are still checked regularly.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort,
                                           uint32_t* status, uint32_t code) {
-    if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;
+#pragma unroll 1
+    for (int i = 0; i < RDVB_SPIN_TRIES; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, RDVB_SLEEP_HINT_NS)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;
+        if (mbar_try_wait_sleep(bar, parity, RDVB_SLEEP_HINT_NS)) return true;
         if (*abort) return false;
         if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
             *abort = 1u;
@@ -118,6 +129,20 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             return false;
         }
     }
+}
+
+// Warp-wide bounded wait: lane 0 waits on the barrier, the outcome is
+// broadcast and the warp re-converges (__syncwarp orders lane 0's acquire
+// before the other lanes' later accesses). One waiting thread per warp
+// instead of 32 keeps the barrier traffic off the shared-memory pipe the
+// tensor core reads its operands through. Call with all 32 lanes.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile uint32_t* abort,
+                                               uint32_t* status, uint32_t code) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, status, code);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    __syncwarp();
+    return ok;
 }
 
 // ------------------------------------------------------- bulk async copies

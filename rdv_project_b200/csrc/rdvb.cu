@@ -16,6 +16,7 @@
 #include "ptx.cuh"
 #include "mlp_tc.cuh"
 #include "mlp_simt.cuh"
+#include "winograd.cuh"
 
 namespace {
 
@@ -45,6 +46,7 @@ struct DeviceInfo {
     int max_smem_optin = 0;
     size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2] = {};
     size_t simt_smem_set = 0;
+    size_t wino_smem_set[2] = {};
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
@@ -417,6 +419,143 @@ int rdvb_relu(const float* x, float* y, int64_t n, void* stream) {
     const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, dev->sm_count * 16)));
     rdvb::mlp_simt::relu_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
     return check_launch("relu_kernel");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------- 3x3 conv
+namespace {
+
+bool wino_channels_ok(int cin, int cout) {
+    using rdvb::wino::kMaxChannels;
+    return cin >= 16 && cout >= 16 && cin % 16 == 0 && cout % 16 == 0 && cin <= kMaxChannels &&
+           cout <= kMaxChannels;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t rdvb_winograd_packed_bytes(int variant, int cin, int cout) {
+    if (variant != RDVB_WINOGRAD_F2X2 || !wino_channels_ok(cin, cout)) return 0;
+    return 16LL * cout * 128;
+}
+
+int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int variant, void* u_plain,
+                                   void* u_packed, void* stream) {
+    if (variant == RDVB_WINOGRAD_F4X4)
+        return fail(RDVB_ERR_UNSUPPORTED, "RDVB_WINOGRAD_F4X4 is not implemented; use RDVB_WINOGRAD_F2X2");
+    if (variant != RDVB_WINOGRAD_F2X2) return fail(RDVB_ERR_INVALID_ARG, "unknown Winograd variant %d", variant);
+    if (cin < 1 || cout < 1) return fail(RDVB_ERR_INVALID_ARG, "cin (%d) and cout (%d) must be positive", cin, cout);
+    if (!w_33io) return fail(RDVB_ERR_INVALID_ARG, "w_33io must not be NULL");
+    if (u_packed) {
+        if (!wino_channels_ok(cin, cout))
+            return fail(RDVB_ERR_UNSUPPORTED, "packed operand needs cin, cout multiples of 16 in [16, %d] (got %d, %d)",
+                        rdvb::wino::kMaxChannels, cin, cout);
+        if (!aligned(u_packed, 256)) return fail(RDVB_ERR_INVALID_ARG, "u_packed must be 256-byte aligned");
+    }
+    if (!u_plain && !u_packed) return RDVB_OK;
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (u_packed) {
+        // the bytes of each 128-byte row past cin are never read; zero them anyway
+        cudaError_t e = cudaMemsetAsync(u_packed, 0, rdvb_winograd_packed_bytes(variant, cin, cout), st);
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
+    const int total = cin * cout;
+    const int threads = 256;
+    const int blocks = std::max(1, std::min((total + threads - 1) / threads, dev->sm_count * 4));
+    rdvb::wino::winograd_f23_filter_kernel<<<blocks, threads, 0, st>>>(
+        w_33io, cin, cout, static_cast<__half*>(u_plain), static_cast<uint8_t*>(u_packed));
+    return check_launch("winograd_f23_filter_kernel");
+}
+
+int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int cin, int cout,
+                          const void* u_packed, int variant, const float* bias, void* y, int y_dtype,
+                          void* stream) {
+    using namespace rdvb::wino;
+    if (variant == RDVB_WINOGRAD_F4X4)
+        return fail(RDVB_ERR_UNSUPPORTED, "RDVB_WINOGRAD_F4X4 is not implemented; use RDVB_WINOGRAD_F2X2");
+    if (variant != RDVB_WINOGRAD_F2X2) return fail(RDVB_ERR_INVALID_ARG, "unknown Winograd variant %d", variant);
+    if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16)
+        return fail(RDVB_ERR_INVALID_ARG, "x_dtype must be RDVB_F32 or RDVB_F16");
+    if (y_dtype != RDVB_F32 && y_dtype != RDVB_F16)
+        return fail(RDVB_ERR_INVALID_ARG, "y_dtype must be RDVB_F32 or RDVB_F16");
+    if (n < 0 || h < 0 || w < 0) return fail(RDVB_ERR_INVALID_ARG, "n, h, w must be >= 0");
+    if (!wino_channels_ok(cin, cout))
+        return fail(RDVB_ERR_UNSUPPORTED, "cin, cout must be multiples of 16 in [16, %d] (got %d, %d)", kMaxChannels,
+                    cin, cout);
+    if (n == 0 || h == 0 || w == 0) return RDVB_OK;
+    if (!x || !y || !u_packed) return fail(RDVB_ERR_INVALID_ARG, "x, y and u_packed must not be NULL");
+    if (!aligned(x, 16) || !aligned(y, 16) || !aligned(u_packed, 16))
+        return fail(RDVB_ERR_INVALID_ARG, "x, y and u_packed must be 16-byte aligned");
+    if (bias && !aligned(bias, 4)) return fail(RDVB_ERR_INVALID_ARG, "bias must be 4-byte aligned");
+    const long long tiles_w = (w + 1) / 2, tiles_h = (h + 1) / 2;
+    const long long n_tiles = static_cast<long long>(n) * tiles_h * tiles_w;
+    if (n_tiles > 0x7fffffffLL - kTileM) return fail(RDVB_ERR_UNSUPPORTED, "too many tiles (%lld)", n_tiles);
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.x = x;
+    p.y = y;
+    p.u_pack = static_cast<const uint8_t*>(u_packed);
+    p.bias = bias;
+    p.h = h;
+    p.w = w;
+    p.cin = cin;
+    p.cout = cout;
+    p.y_f16 = y_dtype == RDVB_F16 ? 1 : 0;
+    p.tiles_w = static_cast<int>(tiles_w);
+    p.tiles_per_img = static_cast<int>(tiles_w * tiles_h);
+    p.n_tiles = static_cast<int>(n_tiles);
+    p.n_blocks = static_cast<int>((n_tiles + kTileM - 1) / kTileM);
+    p.u_bytes = static_cast<uint32_t>(rdvb_winograd_packed_bytes(variant, cin, cout));
+    p.off_a = round_up(p.u_bytes, 1024);
+    p.off_bar = p.off_a + 4 * kATileBytes;
+    p.idesc = rdvb::umma_idesc_f16(static_cast<uint32_t>(cout), 0);
+    const uint32_t smem = p.off_bar + kBarBlockBytes + 1024u;
+    if (smem > static_cast<uint32_t>(dev->max_smem_optin))
+        return fail(RDVB_ERR_UNSUPPORTED, "Winograd kernel needs %u bytes of shared memory", smem);
+    const int xi = x_dtype == RDVB_F16 ? 1 : 0;
+    auto kernel = xi ? winograd_f23_kernel<true> : winograd_f23_kernel<false>;
+    if (dev->wino_smem_set[xi] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(winograd): %s", cudaGetErrorString(e));
+        dev->wino_smem_set[xi] = smem;
+    }
+    const int grid = std::min(dev->sm_count, p.n_blocks);
+    kernel<<<grid, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+    return check_launch("winograd_f23_kernel");
+}
+
+int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
+                       const float* weight, const float* bias, float* y, void* stream) {
+    if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16)
+        return fail(RDVB_ERR_INVALID_ARG, "x_dtype must be RDVB_F32 or RDVB_F16");
+    if (n < 0 || h < 0 || w < 0) return fail(RDVB_ERR_INVALID_ARG, "n, h, w must be >= 0");
+    if (cin < 1 || cout < 8 || cout % 8 != 0)
+        return fail(RDVB_ERR_INVALID_ARG, "cin must be >= 1 and cout a positive multiple of 8 (got %d, %d)", cin, cout);
+    if (kh < 1 || kw < 1) return fail(RDVB_ERR_INVALID_ARG, "kh and kw must be >= 1");
+    if (n == 0 || h == 0 || w == 0) return RDVB_OK;
+    if (!x || !weight || !y) return fail(RDVB_ERR_INVALID_ARG, "x, weight and y must not be NULL");
+    if (!aligned(weight, 16) || !aligned(y, 16))
+        return fail(RDVB_ERR_INVALID_ARG, "weight and y must be 16-byte aligned");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const long long total = static_cast<long long>(n) * h * w * (cout / 8);
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + threads - 1) / threads,
+                                                                               dev->sm_count * 32LL)));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (x_dtype == RDVB_F16)
+        rdvb::wino::conv2d_direct_kernel<true><<<blocks, threads, 0, st>>>(x, weight, bias, y, n, h, w, cin, cout, kh, kw);
+    else
+        rdvb::wino::conv2d_direct_kernel<false><<<blocks, threads, 0, st>>>(x, weight, bias, y, n, h, w, cin, cout, kh,
+                                                                            kw);
+    return check_launch("conv2d_direct_kernel");
 }
 
 }  // extern "C"

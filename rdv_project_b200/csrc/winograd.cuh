@@ -1,0 +1,541 @@
+// Winograd F(2x2, 3x3) convolution (stride 1, zero padding 1) with the
+// input transform, the per-position GEMMs and the output transform fused in
+// one kernel, plus the filter transform and a direct convolution.
+//
+// Replaces Conv2DTensorOpWinograd3x3 (rdv/domain/nn.py:1002-1087,
+// rdv/shaders/tensors/conv2d_tensor_op_winograd3x3.h:95-178) and extends it
+// to batched NHWC tensors and to 64 channels. Same arithmetic contract: the
+// input transform V = B^T d B in fp32 (same operation order as
+// _winograd_fwd, :59-78), V staged float16; the filter transform U = G g G^T
+// in fp32, staged float16 (nn.py:525-538); products of float16 operands
+// accumulated in fp32 on the tensor core; bias added in fp32 (:164-174).
+//
+// The inverse transform Y_ij = sum_uv A^T[i][u] A^T[j][v] M_uv (coefficients
+// 0/+1/-1) runs on the tensor core as well: each output position (i, j) of
+// the 2x2 tile has its own TMEM accumulator, and every nonzero term adds
+// +-V_uv * U_uv to it (the sign is the MMA's negate-B bit), 36 position-GEMMs
+// per block of tiles instead of 16 plus a CUDA-core inverse. The tensor
+// core has the headroom; the CUDA cores, whose registers would otherwise hold
+// the 2x2 x COUT partial outputs of every tile, are left free to transform
+// and prefetch the input.
+//
+// Design (one persistent CTA per SM, 16 warps):
+//   * U for all 16 positions stays resident in shared memory (K-major,
+//     128-byte swizzle), loaded once by one bulk copy.
+//   * A CTA walks blocks of 128 Winograd tiles (raster order over
+//     (image, tile row, tile column)), each block as 4 "rows" u of the 4x4
+//     transform domain. For a row, every thread loads its two (tile,
+//     8-channel chunk) items' input (16 x 16-byte loads in flight), forms the
+//     first (row) pass of B^T d B, then for v = 0..3 waits until the GEMMs of
+//     the previous row released V tile v, writes V_uv (float16) and arrives;
+//     thread 0 issues position (u, v)'s GEMMs as soon as all warps arrived.
+//     So the transform of row r + 1 overlaps the GEMMs of row r, position by
+//     position.
+//   * TMEM: the 4 accumulators (i, j) of a block, COUT columns each, double
+//     buffered across blocks (512 columns). After a block's last GEMM, warp w
+//     reads tiles 32*(w%4)..+31 (its lane quadrant) x channels 16*(w/4)..+15,
+//     adds the bias and stores, while the next block's GEMMs run.
+// HBM traffic is the input read (halo re-reads hit L1/L2) plus the output
+// write, the operator's roofline.
+#pragma once
+#include "ptx.cuh"
+
+namespace rdvb {
+namespace wino {
+
+constexpr int kTileM = 128;         // Winograd tiles per block (GEMM M)
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxChannels = 64;    // CIN, COUT: multiples of 16, at most 64
+constexpr uint32_t kATileBytes = kTileM * 128;  // one position's V tile (128-byte rows)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kDCols = 4 * kMaxChannels;   // one block's 4 output accumulators
+
+struct Params {
+    const void* x;          // [N, H, W, CIN] NHWC, float32 or float16
+    void* y;                // [N, H, W, COUT] NHWC, float32 or float16
+    const uint8_t* u_pack;  // 16 blocks of (COUT rows x 128 B), K-major SW128
+    const float* bias;      // [COUT] or null
+    int h, w, cin, cout;
+    int y_f16;
+    int tiles_w, tiles_per_img;
+    int n_tiles;
+    int n_blocks;
+    uint32_t u_bytes;       // 16 * cout * 128
+    uint32_t off_a, off_bar;
+    uint32_t idesc;         // M = 128, N = COUT, f16 x f16 -> f32
+};
+
+enum : int {
+    kBarUFull = 0,
+    kBarAFull = 1,       // + v: V tile v written (16 warp arrivals)
+    kBarAEmpty = 5,      // + v: the GEMMs reading V tile v are done (commit)
+    kBarDFull = 9,       // + half: a block's accumulators are final (commit)
+    kBarDrain = 11,
+    kNumBars = 12,
+};
+constexpr uint32_t kBarBlockBytes = kNumBars * 8 + 16;
+constexpr uint32_t kNegateB = 1u << 14;  // instruction-descriptor bit: negate the B operand
+
+// A^T of F(2, 3) = [[1, 1, 1, 0], [0, 1, -1, -1]] (the reference's
+// _winograd_inv, :80-93).
+__host__ __device__ constexpr int at_coef(int i, int u) {
+    return i == 0 ? (u < 3 ? 1 : 0) : (u == 0 ? 0 : (u == 1 ? 1 : -1));
+}
+
+// One transform item: a Winograd tile of the current block and an 8-channel
+// chunk of its input.
+struct Item {
+    long long e0;      // element offset of patch (row 0, col 0), channel chunk start
+    uint32_t rmask;    // bit k: patch row k inside the image (0 if no item)
+    uint32_t cmask;    // bit c: patch column c inside the image
+    uint32_t soff;     // byte offset of (tile row, chunk) inside a V tile
+};
+
+// Item `idx` (tile row idx / (CIN/8) of block `blk`, chunk idx % (CIN/8)).
+// Returns false when the block has no such item. Tiles past the end get an
+// all-invalid patch, so their V rows are written as zeros.
+__device__ __forceinline__ bool make_item(const Params& p, int blk, int idx, Item& it) {
+    const int cch = p.cin >> 3;
+    it.rmask = 0;
+    it.cmask = 0;
+    it.e0 = 0;
+    it.soff = 0;
+    if (idx >= kTileM * cch) return false;
+    const int tr = idx / cch, ck = idx - tr * cch;
+    it.soff = sw128_offset(static_cast<uint32_t>(tr), static_cast<uint32_t>(ck * 8), kTileM);
+    const int t = blk * kTileM + tr;
+    if (t < p.n_tiles) {
+        const int img = t / p.tiles_per_img;
+        const int rem = t - img * p.tiles_per_img;
+        const int ty = rem / p.tiles_w, tx = rem - ty * p.tiles_w;
+        const int gh0 = 2 * ty - 1, gw0 = 2 * tx - 1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (gh0 + k >= 0 && gh0 + k < p.h) it.rmask |= 1u << k;
+            if (gw0 + k >= 0 && gw0 + k < p.w) it.cmask |= 1u << k;
+        }
+        it.e0 = ((static_cast<long long>(img) * p.h + gh0) * p.w + gw0) * p.cin + ck * 8;
+    }
+    return true;
+}
+
+__device__ __forceinline__ void h8_to_f32(const uint4& q, float (&v)[8]) {
+    const __half2* h2 = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h2[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+    }
+}
+
+// Row pairs and signs of B^T (the reference's _winograd_fwd, :59-78): the
+// first pass of domain row u is m = d_k0 + t_u * d_k1 (one rounding, so
+// fma(t, b, a) is the reference's a - b / a + b exactly), times s_u:
+//   u = 0: d0 - d2      u = 1: d1 + d2      u = 2: d2 - d1 = -(d1 - d2)
+//   u = 3: d1 - d3.
+// The same holds for the second pass over columns v. The factor s = -1 of
+// u = 2 and v = 2 is not applied to V (float16 rounding is symmetric, so
+// -fp16(x) == fp16(-x)); it flips the sign of the position's GEMMs instead.
+__host__ __device__ constexpr int bt_k0(int u) { return u == 0 ? 0 : 1; }
+__host__ __device__ constexpr int bt_k1(int u) { return u == 0 ? 2 : (u == 3 ? 3 : 2); }
+__host__ __device__ constexpr float bt_t(int u) { return u == 1 ? 1.0f : -1.0f; }
+__host__ __device__ constexpr int bt_s(int u) { return u == 2 ? -1 : 1; }
+
+// m for both items of the thread (domain row u): all 16 loads of a float16
+// input are issued before the first use.
+template <bool X16>
+__device__ __forceinline__ void first_pass(const Params& p, const Item (&it)[2], long long row_stride, int u,
+                                           float (&m)[2][4][8]) {
+    const int k0 = bt_k0(u), k1 = bt_k1(u);
+    const float t = bt_t(u);
+    const long long o0 = k0 * row_stride, o1 = k1 * row_stride;
+    if constexpr (X16) {
+        const __half* x = static_cast<const __half*>(p.x);
+        uint4 ra[2][4], rb[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const bool v0 = (it[i].rmask >> k0) & 1u, v1 = (it[i].rmask >> k1) & 1u;
+#pragma unroll
+            for (int col = 0; col < 4; ++col) {
+                const bool vc = (it[i].cmask >> col) & 1u;
+                const long long ec = it[i].e0 + static_cast<long long>(col) * p.cin;
+                ra[i][col] = (vc && v0) ? __ldg(reinterpret_cast<const uint4*>(x + ec + o0)) : make_uint4(0u, 0u, 0u, 0u);
+                rb[i][col] = (vc && v1) ? __ldg(reinterpret_cast<const uint4*>(x + ec + o1)) : make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int col = 0; col < 4; ++col) {
+                float a[8], b[8];
+                h8_to_f32(ra[i][col], a);
+                h8_to_f32(rb[i][col], b);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) m[i][col][e] = fmaf(t, b[e], a[e]);
+            }
+    } else {
+        const float* x = static_cast<const float*>(p.x);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const bool v0 = (it[i].rmask >> k0) & 1u, v1 = (it[i].rmask >> k1) & 1u;
+#pragma unroll
+            for (int col = 0; col < 4; ++col) {
+                const bool vc = (it[i].cmask >> col) & 1u;
+                const long long ec = it[i].e0 + static_cast<long long>(col) * p.cin;
+                const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4* pa = reinterpret_cast<const float4*>(x + ec + o0);
+                const float4* pb = reinterpret_cast<const float4*>(x + ec + o1);
+                const float4 a0 = (vc && v0) ? __ldg(pa) : z, a1 = (vc && v0) ? __ldg(pa + 1) : z;
+                const float4 b0 = (vc && v1) ? __ldg(pb) : z, b1 = (vc && v1) ? __ldg(pb + 1) : z;
+                const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) m[i][col][e] = fmaf(t, b[e], a[e]);
+            }
+        }
+    }
+}
+
+// Second (column) pass for domain column V of one item (without the factor
+// s_V), float16, into V tile V.
+template <int V>
+__device__ __forceinline__ void store_v(const float (&m)[4][8], uint32_t dst) {
+    constexpr int c0 = bt_k0(V), c1 = bt_k1(V);
+    constexpr float t = bt_t(V);
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2)
+        pk[e >> 1] = pack_f16x2(fmaf(t, m[c1][e], m[c0][e]), fmaf(t, m[c1][e + 1], m[c0][e + 1]));
+    st_shared_v4(dst, pk[0], pk[1], pk[2], pk[3]);
+}
+
+// The GEMMs of domain position (u, v): for every output position (i, j)
+// with a nonzero coefficient c = A^T[i][u] * A^T[j][v], D_ij += c * s_u * s_v
+// * V'_uv * U_uv (V' as stored). The first contribution to D_ij in a block
+// comes from (u, v) = (i, j) (A^T[1][0] = 0) and overwrites it.
+// Fully unrolled, every descriptor in its own register: an MMA's operand
+// registers are read after issue, so recomputing one in a loop would stall
+// the issuing thread until the previous MMA has consumed it.
+__device__ __forceinline__ void issue_position(int u, int v, uint32_t d_base, uint64_t ad, uint64_t bd,
+                                               uint32_t idesc, uint32_t ksteps) {
+    const int s = bt_s(u) * bt_s(v);
+    uint64_t a[4], b[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        a[k] = ad + 2 * k;
+        b[k] = bd + 2 * k;
+    }
+    const uint32_t id_neg = idesc | kNegateB;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int i = q >> 1, j = q & 1;
+        const int c = at_coef(i, u) * at_coef(j, v) * s;
+        if (c == 0) continue;
+        const uint32_t acc0 = (u == i && v == j) ? 0u : 1u;
+        const uint32_t d = d_base + static_cast<uint32_t>(q * kMaxChannels);
+        const uint32_t id = c > 0 ? idesc : id_neg;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (k < static_cast<int>(ksteps)) umma_f16(d, a[k], b[k], id, k == 0 ? acc0 : 1u);
+    }
+}
+
+// D_ij + bias of this lane's tile (channels 16*grp..+15) to the output.
+// The TMEM loads are warp-collective: every lane runs them, only lanes with
+// a valid tile store.
+__device__ __forceinline__ void store_block(const Params& p, int t, bool valid, int grp, uint32_t td) {
+    const int tt = valid ? t : 0;
+    const int img = tt / p.tiles_per_img;
+    const int rem = tt - img * p.tiles_per_img;
+    const int ty = rem / p.tiles_w, tx = rem - ty * p.tiles_w;
+    float b[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) b[c] = p.bias ? __ldg(p.bias + 16 * grp + c) : 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t r[16];
+        tmem_ld16(td + static_cast<uint32_t>(q * kMaxChannels), r);
+        tmem_wait_ld();
+        const int oh = 2 * ty + (q >> 1), ow = 2 * tx + (q & 1);
+        if (!valid || oh >= p.h || ow >= p.w) continue;  // past the end; odd h or w
+        const long long o = ((static_cast<long long>(img) * p.h + oh) * p.w + ow) * p.cout + 16 * grp;
+        float y[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) y[c] = __uint_as_float(r[c]) + b[c];
+        if (!p.y_f16) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4)
+                dst[c4] = make_float4(y[4 * c4], y[4 * c4 + 1], y[4 * c4 + 2], y[4 * c4 + 3]);
+        } else {
+            uint32_t pk[8];
+#pragma unroll
+            for (int c = 0; c < 16; c += 2) pk[c >> 1] = pack_f16x2(y[c], y[c + 1]);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.y) + o);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+    }
+}
+
+struct RowCtx {
+    const Params* p;
+    Item it[2];
+    bool has[2];
+    long long row_stride;
+    uint32_t a_base, bar_base, d_base, ksteps, idesc;
+    uint64_t a_desc0, u_desc0, u_pos;
+    int r, u, bl, lane;
+    bool issuer;
+    volatile uint32_t* abort;
+    __device__ __forceinline__ uint32_t bar(int i) const { return bar_base + 8u * static_cast<uint32_t>(i); }
+};
+
+// Thread 0: once every warp has written V tile v of the current row, issue
+// position (u, v)'s GEMMs and commit the tile's release (and, after the
+// block's last position, the accumulators). One shared copy of this code,
+// so the issuing thread's instructions stay cached.
+__device__ __noinline__ bool issue_after_full(uint32_t bar_base, volatile uint32_t* abort, int r, int u, int v,
+                                              int bl, uint32_t d_base, uint64_t a_desc0, uint64_t u_desc0,
+                                              uint64_t u_pos, uint32_t idesc, uint32_t ksteps) {
+    auto bar = [&](int i) { return bar_base + 8u * static_cast<uint32_t>(i); };
+    bool ok = true;
+    if (r == 0 && v == 0) ok = mbar_wait(bar(kBarUFull), 0u, abort, &g_status, kStatusTimeoutWFull);
+    if (ok) ok = mbar_wait(bar(kBarAFull + v), r & 1, abort, &g_status, kStatusTimeoutAFull);
+    if (!ok) return false;
+    tc_fence_after();
+    issue_position(u, v, d_base, a_desc0 + static_cast<uint64_t>(v) * (kATileBytes >> 4),
+                   u_desc0 + static_cast<uint64_t>(u * 4 + v) * u_pos, idesc, ksteps);
+    umma_commit(bar(kBarAEmpty + v));
+    if (u == 3 && v == 3) umma_commit(bar(kBarDFull + (bl & 1)));
+    return true;
+}
+
+// Domain column V of the current row: wait until V tile V is free, write
+// it, and let thread 0 issue its GEMMs.
+template <int V>
+__device__ __forceinline__ bool do_position(const RowCtx& c, const float (&m)[2][4][8]) {
+    if (!mbar_wait_warp(c.bar(kBarAEmpty + V), (c.r & 1) ^ 1, c.abort, &g_status, kStatusTimeoutXEmpty))
+        return false;
+    if (c.has[0]) store_v<V>(m[0], c.a_base + V * kATileBytes + c.it[0].soff);
+    if (c.has[1]) store_v<V>(m[1], c.a_base + V * kATileBytes + c.it[1].soff);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (c.lane == 0) mbar_arrive(c.bar(kBarAFull + V));
+    bool ok = true;
+    if (c.issuer)
+        ok = issue_after_full(c.bar_base, c.abort, c.r, c.u, V, c.bl, c.d_base, c.a_desc0, c.u_desc0, c.u_pos, c.idesc,
+                              c.ksteps);
+    return __all_sync(0xffffffffu, ok);
+}
+
+template <bool X16>
+__device__ __forceinline__ bool do_row(const RowCtx& c) {
+    float m[2][4][8];
+    first_pass<X16>(*c.p, c.it, c.row_stride, c.u, m);
+    return do_position<0>(c, m) && do_position<1>(c, m) && do_position<2>(c, m) && do_position<3>(c, m);
+}
+
+template <bool X16>
+__global__ void __launch_bounds__(kThreads, 1) winograd_f23_kernel(const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_addr(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t* const base_ptr = smem_raw + (base - raw_addr);
+    const uint32_t u_base = base;  // U at offset 0
+    RowCtx c;
+    c.p = &p;
+    c.a_base = base + p.off_a;
+    c.bar_base = base + p.off_bar;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + p.off_bar + kNumBars * 8);
+    c.abort = reinterpret_cast<volatile uint32_t*>(base_ptr + p.off_bar + kNumBars * 8 + 4);
+
+    const int warp = threadIdx.x >> 5;
+    c.lane = threadIdx.x & 31;
+    c.issuer = threadIdx.x == 0;
+    if (threadIdx.x == 0) {
+        mbar_init(c.bar(kBarUFull), 1);
+        for (int v = 0; v < 4; ++v) {
+            mbar_init(c.bar(kBarAFull + v), kWarps);
+            mbar_init(c.bar(kBarAEmpty + v), 1);
+        }
+        mbar_init(c.bar(kBarDFull), 1);
+        mbar_init(c.bar(kBarDFull + 1), 1);
+        mbar_init(c.bar(kBarDrain), 1);
+        *c.abort = 0u;
+        fence_mbarrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_addr(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    if (c.issuer) {
+        mbar_arrive_expect_tx(c.bar(kBarUFull), p.u_bytes);
+        bulk_g2s(u_base, p.u_pack, p.u_bytes, c.bar(kBarUFull));
+    }
+    // blocks blockIdx.x, blockIdx.x + gridDim.x, ...; 4 domain rows each
+    const int n_mine = blockIdx.x < p.n_blocks ? (p.n_blocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int rows = 4 * n_mine;
+
+    const int quad = warp & 3;
+    const int grp = warp >> 2;
+    const bool has_cols = 16 * grp < p.cout;
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + 16u * grp;
+    c.row_stride = static_cast<long long>(p.w) * p.cin;
+    c.a_desc0 = umma_desc_sw128(c.a_base);
+    c.u_desc0 = umma_desc_sw128(u_base);
+    c.ksteps = static_cast<uint32_t>(p.cin) >> 4;
+    c.u_pos = static_cast<uint64_t>(p.cout) * 8u;  // one position of U, in 16-byte units
+    c.idesc = p.idesc;
+
+    // a finished block's accumulators: + bias, to the output
+    auto epilogue = [&](int bl) -> bool {
+        const uint32_t half = bl & 1;
+        if (!mbar_wait_warp(c.bar(kBarDFull + half), (bl >> 1) & 1, c.abort, &g_status, kStatusTimeoutAccFull))
+            return false;
+        tc_fence_after();
+        if (has_cols) {
+            const int t = (blockIdx.x + bl * gridDim.x) * kTileM + quad * 32 + c.lane;
+            store_block(p, t, t < p.n_tiles, grp, t_lane + half * kDCols);
+        }
+        tc_fence_before();
+        return true;
+    };
+
+    bool ok = true;
+    for (int r = 0; ok && r < rows; ++r) {
+        const int u = r & 3;
+        c.r = r;
+        c.bl = r >> 2;
+        if (u == 0) {
+            const int blk = blockIdx.x + c.bl * gridDim.x;
+            c.has[0] = make_item(p, blk, threadIdx.x, c.it[0]);
+            c.has[1] = make_item(p, blk, threadIdx.x + kThreads, c.it[1]);
+        }
+        c.d_base = tmem_base + (c.bl & 1) * kDCols;
+        c.u = u;
+        ok = do_row<X16>(c);
+        // the previous block's outputs, while this block's GEMMs run
+        if (ok && u == 0 && c.bl > 0) ok = epilogue(c.bl - 1);
+    }
+    if (ok && rows > 0) ok = epilogue(n_mine - 1);
+    if (!ok) *c.abort = 1u;
+
+    // Let every issued MMA finish before TMEM is released (immediate unless
+    // the CTA aborted with GEMMs in flight).
+    if (c.issuer) {
+        umma_commit(c.bar(kBarDrain));
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait_sleep(c.bar(kBarDrain), 0u, 500000u))
+            if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
+                atomicOr(&g_status, kStatusTimeoutDrain);
+                break;
+            }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// U = G g G^T per (cin, cout) filter in fp32 -- G g first, then (G g) G^T,
+// each a left-to-right sum of exact products (G holds 0, 1/2 and 1), as the
+// reference's torch expression computes it (nn.py:533-538) -- staged float16.
+// Written as the reference's flat [16][CIN][COUT] array (u_plain, optional)
+// and as 16 K-major SW128 operand blocks of COUT rows (u_pack, optional).
+__global__ void winograd_f23_filter_kernel(const float* __restrict__ w33io, int cin, int cout,
+                                           __half* __restrict__ u_plain, uint8_t* __restrict__ u_pack) {
+    const int total = cin * cout;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+        const int ci = idx / cout, co = idx - ci * cout;
+        float g[3][3];
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) g[kh][kw] = w33io[((kh * 3 + kw) * cin + ci) * cout + co];
+        constexpr float G[4][3] = {{1.0f, 0.0f, 0.0f}, {0.5f, 0.5f, 0.5f}, {0.5f, -0.5f, 0.5f}, {0.0f, 0.0f, 1.0f}};
+        float t[4][3];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+                t[a][c] = __fadd_rn(__fadd_rn(__fmul_rn(G[a][0], g[0][c]), __fmul_rn(G[a][1], g[1][c])),
+                                    __fmul_rn(G[a][2], g[2][c]));
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const float uv = __fadd_rn(__fadd_rn(__fmul_rn(t[a][0], G[b][0]), __fmul_rn(t[a][1], G[b][1])),
+                                           __fmul_rn(t[a][2], G[b][2]));
+                const int pos = a * 4 + b;
+                const __half hv = __float2half_rn(uv);
+                if (u_plain) u_plain[(static_cast<size_t>(pos) * cin + ci) * cout + co] = hv;
+                if (u_pack)
+                    *reinterpret_cast<__half*>(u_pack + static_cast<size_t>(pos) * cout * 128 +
+                                               sw128_offset(co, ci, cout)) = hv;
+            }
+    }
+}
+
+// 'Same' (zero padding KH/2, KW/2), stride-1 direct convolution in fp32:
+// acc = bias; acc += x * w over (kh, kw, cin) in that order, one fused
+// multiply-add per tap (Conv2DTensorOp, rdv/shaders/tensors/conv2d_tensor_op.h:21-87).
+// One thread per (pixel, 8 output channels). x float32 or float16.
+template <bool X16>
+__global__ void conv2d_direct_kernel(const void* __restrict__ x, const float* __restrict__ wt,
+                                     const float* __restrict__ bias, float* __restrict__ y, int n, int h, int w,
+                                     int cin, int cout, int kh_n, int kw_n) {
+    const int chunks = cout >> 3;
+    const long long total = static_cast<long long>(n) * h * w * chunks;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long pix = idx / chunks;
+        const int c0 = static_cast<int>(idx - pix * chunks) * 8;
+        const int ow = static_cast<int>(pix % w);
+        const long long t = pix / w;
+        const int oh = static_cast<int>(t % h);
+        const long long img = t / h;
+        float acc[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = bias ? bias[c0 + c] : 0.0f;
+        for (int kh = 0; kh < kh_n; ++kh) {
+            const int ih = oh + kh - kh_n / 2;
+            if (ih < 0 || ih >= h) continue;
+            for (int kw = 0; kw < kw_n; ++kw) {
+                const int iw = ow + kw - kw_n / 2;
+                if (iw < 0 || iw >= w) continue;
+                const long long xin = ((img * h + ih) * w + iw) * cin;
+                const float* wk = wt + static_cast<long long>(kh * kw_n + kw) * cin * cout + c0;
+                for (int k = 0; k < cin; ++k) {
+                    const float xv = X16 ? __half2float(static_cast<const __half*>(x)[xin + k])
+                                         : static_cast<const float*>(x)[xin + k];
+                    const float4 wa = __ldg(reinterpret_cast<const float4*>(wk + static_cast<long long>(k) * cout));
+                    const float4 wb =
+                        __ldg(reinterpret_cast<const float4*>(wk + static_cast<long long>(k) * cout + 4));
+                    acc[0] = fmaf(xv, wa.x, acc[0]);
+                    acc[1] = fmaf(xv, wa.y, acc[1]);
+                    acc[2] = fmaf(xv, wa.z, acc[2]);
+                    acc[3] = fmaf(xv, wa.w, acc[3]);
+                    acc[4] = fmaf(xv, wb.x, acc[4]);
+                    acc[5] = fmaf(xv, wb.y, acc[5]);
+                    acc[6] = fmaf(xv, wb.z, acc[6]);
+                    acc[7] = fmaf(xv, wb.w, acc[7]);
+                }
+            }
+        }
+        float4* dst = reinterpret_cast<float4*>(y + pix * cout + c0);
+        dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+}  // namespace wino
+}  // namespace rdvb
