@@ -161,6 +161,45 @@ int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int c
 int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
                        const float* weight, const float* bias, float* y, void* stream);
 
+/* ---------------------------------------------------------- ray-march ----
+ * Pinhole camera rays through a volume whose density and colour come from an
+ * MLP, rendered front to back.
+ *
+ * Replaces: the reference's Cameras grid (rdv/domain/rendering.py:10-42,
+ * rdv/shaders/rendering/cameras.h:1-20), its implicit [-1,1]^3 box
+ * (rdv/shaders/libraries/math_library.h:48-57, miss rule and entry clamp of
+ * rdv/shaders/volumes/raymarching_transmittance.h:11-19) and the per-sample
+ * MLP evaluation of a Cameras >> RaymarchingTransmittance(extinction=mlp)
+ * sensor (rdv/domain/volumes.py:124-141). The emission-absorption
+ * compositing (softplus density, sigmoid colour, RGBA with A = 1 - T) has no
+ * reference counterpart; it follows the BASELINE volume-render workload.
+ */
+
+/* Cameras: out [n_cameras, height, width, 6] = (origin, unit direction) of
+ * each pixel-centre ray; poses [n_cameras, 9] = origin | target | up (device).
+ * aspect <= 0 means width / height, fov <= 0 means pi / 4 (the reference's
+ * defaults). */
+int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, float* out,
+                     void* stream);
+
+/* Workspace bytes rdvb_raymarch_render needs for a width x height image. */
+int64_t rdvb_raymarch_workspace_bytes(int width, int height);
+
+/* Renders rows [row_begin, row_end) of a width x height image from the camera
+ * pose9 (HOST array: origin | target | up): every ray is clipped to the
+ * [-1,1]^3 box and sampled at n_samples (must be 128) midpoints
+ * t_i = t0 + (i + 1/2)(t1 - t0)/n; the MLP (dims[0] = 3 -> dims[n] = 4, all
+ * layers RDVB_MATH_F16 or all RDVB_MATH_BF16, `packed` from rdvb_mlp_pack)
+ * gives (o0, o1, o2, o3) per sample; sigma = softplus(o0), rgb = sigmoid(o1..3),
+ * alpha_i = 1 - exp(-sigma_i dt), C = sum T_i alpha_i rgb_i with
+ * T_i = prod_{j<i} (1 - alpha_j). rgba [(row_end-row_begin) * width, 4] fp32,
+ * 16-byte aligned: (C, 1 - T_n); rays that miss the box get 0. One fused
+ * tensor-core kernel evaluates and composites every ray that hits; workspace
+ * (rdvb_raymarch_workspace_bytes, 256-byte aligned) holds the hit list. */
+int rdvb_raymarch_render(const float* pose9, int width, int height, float fov, float aspect, int n_samples,
+                         int n_layers, const int* dims, const int* layer_flags, const void* packed, int row_begin,
+                         int row_end, void* workspace, size_t workspace_bytes, float* rgba, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

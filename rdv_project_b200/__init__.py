@@ -15,6 +15,7 @@ from .tensor_ops import (TensorOperation, ReLUTensorOp, LinearTensorOp, LinearTe
                          LinearTensorOpSimple, LinearTensorOpSmall)
 from .conv import (Conv2DTensorOp, Conv2DTensorOpWinograd3x3, Conv3x3Winograd, conv2d_direct,
                    _winograd_transform_weight)
+from .rendering import Cameras, VolumeRenderer
 from ._native import RdvbError, device_status
 
 __all__ = [
@@ -23,5 +24,6 @@ __all__ = [
     "TensorOperation", "ReLUTensorOp", "LinearTensorOp", "LinearTensorOpFast", "LinearTensorOpMine",
     "LinearTensorOpSimple", "LinearTensorOpSmall",
     "Conv2DTensorOp", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
+    "Cameras", "VolumeRenderer",
     "RdvbError", "device_status",
 ]

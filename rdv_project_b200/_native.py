@@ -39,6 +39,10 @@ SIGNATURES = {
                                        _c_int, _vp]),
     "rdvb_conv2d_direct": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
                                     _vp, _vp]),
+    "rdvb_camera_rays": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_f, _c_f, _vp, _vp]),
+    "rdvb_raymarch_workspace_bytes": (_c_i64, [_c_int, _c_int]),
+    "rdvb_raymarch_render": (_c_int, [_vp, _c_int, _c_int, _c_f, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int, _c_int,
+                                      _vp, ctypes.c_size_t, _vp, _vp]),
 }
 
 
@@ -94,6 +98,13 @@ def int_array(values):
     arr = (_c_int * len(values))()
     for i, v in enumerate(values):
         arr[i] = int(v)
+    return arr
+
+
+def float_array(values):
+    arr = (_c_f * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = float(v)
     return arr
 
 

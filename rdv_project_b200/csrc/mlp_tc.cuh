@@ -72,6 +72,17 @@ struct Layer {
     uint32_t relu;
 };
 
+// Volume ray-march mode: one 128-row tile is one ray's 128 samples.
+struct RayParams {
+    const int* hit_list;   // pixel index (within the rendered band) of every ray that hits the box
+    const int* n_hits;     // number of entries of hit_list (device)
+    float* rgba;           // [band rows * width, 4]
+    float org[3];          // camera origin
+    float xa[3], ya[3], za[3];  // camera basis (cameras.h: xaxis, yaxis, zaxis)
+    float aspect, sz;      // sx = p.x * aspect; sz = 1 / tan(fov / 2)
+    int width, height, row_begin;
+};
+
 struct Params {
     const void* x;
     float* y;
@@ -94,7 +105,9 @@ struct Params {
     uint32_t act_base;     // first TMEM column of the activation regions
     uint32_t act_stride;   // TMEM columns of one slot's 16-bit activation tile
     int y_vec4;
+    uint32_t off_ray;      // ray mode: compositing scratch (4 column groups x 4 quadrants x 4 floats)
     Layer layer[kMaxLayers];
+    RayParams ray;
 };
 
 // Barrier slots in the barrier block.
@@ -108,8 +121,10 @@ enum : int {
     kBarWFull = kBarAccFull + kMaxSlots,
     kBarWEmpty = kBarWFull + kMaxWStages,
     kBarDrain = kBarWEmpty + kMaxWStages,
-    kNumBars = kBarDrain + 1,
+    kBarComp = kBarDrain + 1,                  // ray mode: per column group, 4 quadrant partials written
+    kNumBars = kBarComp + 4,
 };
+constexpr uint32_t kRayScratchBytes = 4 * 4 * 4 * 4;
 constexpr uint32_t kBarBlockBytes = kNumBars * 8 + 16;  // + tmem base + abort word
 
 __device__ __forceinline__ float load_x_elem(const uint8_t* xs, int dtype, uint32_t idx) {
@@ -156,7 +171,39 @@ __device__ __forceinline__ void convert_chunk(const uint32_t (&v)[16], uint32_t 
     for (int i = 0; i < 8; ++i) pk[i] = pack2<BF16, RELU>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
 }
 
-template <int SLOTS, int BF16>
+// Pinhole ray of pixel `pix` of the band (cameras.h:1-20: pixel centre,
+// p in [-1, 1], w = normalize(xaxis * p.x * aspect + yaxis * p.y + zaxis *
+// sz)) and its [-1, 1]^3 slab interval (math_library.h:48-57), entry clamped
+// to 0 (raymarching_transmittance.h:11-19). Returns false on a miss.
+__device__ __forceinline__ bool ray_setup(const RayParams& rp, int pix, float (&o)[3], float (&w)[3], float& t0,
+                                          float& t1) {
+    const int py = rp.row_begin + pix / rp.width, px = pix - (pix / rp.width) * rp.width;
+    const float fx = (static_cast<float>(px) + 0.5f) / static_cast<float>(rp.width) * 2.0f - 1.0f;
+    const float fy = (static_cast<float>(py) + 0.5f) / static_cast<float>(rp.height) * 2.0f - 1.0f;
+    const float sx = fx * rp.aspect, sy = fy;
+    float d[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) d[c] = rp.xa[c] * sx + rp.ya[c] * sy + rp.za[c] * rp.sz;
+    const float inv_len = 1.0f / sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+    float tmin = -INFINITY, tmax = INFINITY;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        o[c] = rp.org[c];
+        w[c] = d[c] * inv_len;
+        const float inv = 1.0f / w[c];
+        const float xc = -o[c] * inv, sc = fabsf(inv);
+        tmin = fmaxf(tmin, xc - sc);
+        tmax = fminf(tmax, xc + sc);
+    }
+    t0 = fmaxf(tmin, 0.0f);
+    t1 = tmax;
+    return !(tmax <= 0.0f || tmin > tmax);
+}
+
+__device__ __forceinline__ float softplus_f(float v) { return fmaxf(v, 0.0f) + log1pf(expf(-fabsf(v))); }
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+template <int SLOTS, int BF16, bool RAY>
 __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the SW128 atoms.
@@ -190,6 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
             mbar_init(bar(kBarWEmpty + q), 1);
         }
         mbar_init(bar(kBarDrain), 1);
+        for (int g = 0; g < 4; ++g) mbar_init(bar(kBarComp + g), 4);
         *abort = 0u;
         fence_mbarrier_init();
     }
@@ -214,6 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
 
     const int n_layers = p.n_layers;
     const int esize = p.x_dtype == 0 ? 4 : 2;
+    // ray mode: the hit list's length is produced on the device
+    const int n_tiles = RAY ? *p.ray.n_hits : p.n_tiles;
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
@@ -226,8 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
             bool ok = true;
             int xr = 0, xs = 0;  // next input tile to load: (round, slot)
             int wr = 0, wl = 0;  // next weight block: (round, layer)
-            bool x_done = tile_of<SLOTS>(0, 0, p.n_tiles) < 0;
-            bool w_done = p.resident || x_done;
+            const bool no_tiles = tile_of<SLOTS>(0, 0, n_tiles) < 0;
+            bool x_done = RAY || no_tiles;  // ray mode: samples are generated, not loaded
+            bool w_done = p.resident || no_tiles;
             if (p.resident) {
                 mbar_arrive_expect_tx(bar(kBarWFull), p.w_total_bytes);
                 for (int l = 0; l < n_layers; ++l)
@@ -238,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
             while (!(x_done && w_done)) {
                 bool progressed = false;
                 if (!x_done && mbar_test_wait(bar(kBarXEmpty + xs), ((xph >> xs) & 1u) ^ 1u)) {
-                    const int t = tile_of<SLOTS>(xr, xs, p.n_tiles);
+                    const int t = tile_of<SLOTS>(xr, xs, n_tiles);
                     const long long row0 = static_cast<long long>(t) * kTileM;
                     long long rows = p.n_rows - row0;
                     if (rows > kTileM) rows = kTileM;
@@ -252,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                         xs = 0;
                         ++xr;
                     }
-                    x_done = tile_of<SLOTS>(xr, xs, p.n_tiles) < 0;
+                    x_done = tile_of<SLOTS>(xr, xs, n_tiles) < 0;
                     progressed = true;
                 }
                 if (!w_done && mbar_test_wait(bar(kBarWEmpty + q), wph ^ 1u)) {
@@ -268,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                         wl = 0;
                         ++wr;
                     }
-                    w_done = tile_of<SLOTS>(wr, 0, p.n_tiles) < 0;
+                    w_done = tile_of<SLOTS>(wr, 0, n_tiles) < 0;
                     progressed = true;
                 }
                 if (progressed) {
@@ -306,10 +357,36 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
         const bool vec = p.x_dtype == 0 && (p.in_dim & 7) == 0;
         bool ok = true;
         (void)kch0;
-        for (int r = 0; ok && tile_of<SLOTS>(r, 0, p.n_tiles) >= 0; ++r) {
+        for (int r = 0; ok && tile_of<SLOTS>(r, 0, n_tiles) >= 0; ++r) {
             for (int s = 0; s < SLOTS; ++s) {
-                const int t = tile_of<SLOTS>(r, s, p.n_tiles);
+                const int t = tile_of<SLOTS>(r, s, n_tiles);
                 if (t < 0) break;
+                if constexpr (RAY) {
+                    // sample i of the ray at t_i = t0 + (i + 1/2) * dt, dt = (t1 - t0) / 128,
+                    // as float16/bfloat16 (x, y, z, 0...) in the layer-0 A tile
+                    const bool good = mbar_wait(bar(kBarA0Empty + s), ((a0eph >> s) & 1u) ^ 1u, abort, &g_status,
+                                                kStatusTimeoutOther);
+                    if (!__all_sync(0xffffffffu, good)) {
+                        ok = false;
+                        break;
+                    }
+                    a0eph ^= 1u << s;
+                    float o[3], w[3], t0, t1;
+                    ray_setup(p.ray, __ldg(p.ray.hit_list + t), o, w, t0, t1);
+                    const float dt = (t1 - t0) / static_cast<float>(kTileM);
+                    const uint32_t a_tile = a_base + static_cast<uint32_t>(s) * p.a0_bytes;
+#pragma unroll
+                    for (int k = 0; k < kTileM / 32; ++k) {
+                        const uint32_t ri = static_cast<uint32_t>(k * 32 + lane);
+                        const float ts = t0 + (static_cast<float>(ri) + 0.5f) * dt;
+                        st_shared_v4(a_tile + sw128_offset(ri, 0, kTileM), pack2_rt<BF16>(o[0] + ts * w[0], o[1] + ts * w[1], 0),
+                                     pack2_rt<BF16>(o[2] + ts * w[2], 0.0f, 0), 0u, 0u);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(kBarA0Full + s));
+                    continue;
+                }
                 bool good = mbar_wait(bar(kBarXFull + s), (xfph >> s) & 1u, abort, &g_status, kStatusTimeoutXFull) &&
                             mbar_wait(bar(kBarA0Empty + s), ((a0eph >> s) & 1u) ^ 1u, abort, &g_status,
                                       kStatusTimeoutOther);
@@ -375,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                 a_tm[s] = tmem_base + p.act_base + static_cast<uint32_t>(s) * p.act_stride;
                 a0_desc[s] = umma_desc_sw128(a_base + static_cast<uint32_t>(s) * p.a0_bytes);
             }
-            for (int r = 0; ok && tile_of<SLOTS>(r, 0, p.n_tiles) >= 0; ++r) {
+            for (int r = 0; ok && tile_of<SLOTS>(r, 0, n_tiles) >= 0; ++r) {
                 for (int l = 0; l < n_layers && ok; ++l) {
                     const uint32_t ksteps = p.layer[l].k_pad >> 4;
                     const uint32_t n8 = p.layer[l].n_pad * 8u;  // one K atom of B, in 16-byte units
@@ -398,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                     const uint64_t bias_desc = w_desc_plain + ((blk + p.layer[l].bias_off) >> 4);
 #pragma unroll
                     for (int s = 0; s < SLOTS; ++s) {
-                        if (tile_of<SLOTS>(r, s, p.n_tiles) < 0) break;
+                        if (tile_of<SLOTS>(r, s, n_tiles) < 0) break;
                         if (l == 0) {
                             if (!mbar_wait(bar(kBarA0Full + s), (a0ph >> s) & 1u, abort, &g_status,
                                            kStatusTimeoutXFull)) {
@@ -460,16 +537,17 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
         const int row = quad * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
         uint32_t acph = 0u;  // per-slot parity of the next acc_full phase
+        uint32_t comp_ph = 0u;  // ray mode: parity of this group's next compositing phase
         bool ok = true;
 
-        for (int r = 0; ok && tile_of<SLOTS>(r, 0, p.n_tiles) >= 0; ++r) {
+        for (int r = 0; ok && tile_of<SLOTS>(r, 0, n_tiles) >= 0; ++r) {
             for (int l = 0; l < n_layers && ok; ++l) {
                 const bool last = (l == n_layers - 1);
                 const uint32_t nch = p.layer[l].n_pad >> 4;
                 const bool relu = p.layer[l].relu != 0;
 #pragma unroll
                 for (int s = 0; s < SLOTS; ++s) {
-                    const int t = tile_of<SLOTS>(r, s, p.n_tiles);
+                    const int t = tile_of<SLOTS>(r, s, n_tiles);
                     if (t < 0) break;
                     const bool good =
                         mbar_wait(bar(kBarAccFull + s), (acph >> s) & 1u, abort, &g_status, kStatusTimeoutAccFull);
@@ -505,6 +583,70 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                             }
                         }
                         tmem_wait_st();
+                    } else if constexpr (RAY) {
+                        // Front-to-back emission-absorption compositing of the
+                        // ray's 128 samples (rows = samples in order): the warps
+                        // owning columns 0..15 (sigma, r, g, b) each scan their
+                        // quadrant's 32 samples with shuffles; quadrant 0 of the
+                        // group chains the 4 partials.
+                        if (c0 == 0) {
+                            const int pix = __ldg(p.ray.hit_list + t);
+                            float o[3], w[3], t0, t1;
+                            ray_setup(p.ray, pix, o, w, t0, t1);
+                            const float dt = (t1 - t0) / static_cast<float>(kTileM);
+                            const float tau = softplus_f(__uint_as_float(v[0][0])) * dt;
+                            const float alpha = -expm1f(-tau);
+                            float incl = tau;
+#pragma unroll
+                            for (int d = 1; d < 32; d <<= 1) {
+                                const float nb = __shfl_up_sync(0xffffffffu, incl, d);
+                                if (lane >= d) incl += nb;
+                            }
+                            float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+                            if (lane == 0) excl = 0.0f;
+                            const float wgt = expf(-excl) * alpha;  // T_i * alpha_i within the quadrant
+                            float cr = wgt * sigmoid_f(__uint_as_float(v[0][1]));
+                            float cg = wgt * sigmoid_f(__uint_as_float(v[0][2]));
+                            float cb = wgt * sigmoid_f(__uint_as_float(v[0][3]));
+#pragma unroll
+                            for (int d = 16; d > 0; d >>= 1) {
+                                cr += __shfl_xor_sync(0xffffffffu, cr, d);
+                                cg += __shfl_xor_sync(0xffffffffu, cg, d);
+                                cb += __shfl_xor_sync(0xffffffffu, cb, d);
+                            }
+                            const float tau_q = __shfl_sync(0xffffffffu, incl, 31);
+                            float* scr = reinterpret_cast<float*>(base_ptr + p.off_ray) + grp * 16;
+                            if (lane == 0) {
+                                scr[quad * 4 + 0] = cr;
+                                scr[quad * 4 + 1] = cg;
+                                scr[quad * 4 + 2] = cb;
+                                scr[quad * 4 + 3] = tau_q;
+                                mbar_arrive(bar(kBarComp + grp));
+                            }
+                            if (quad == 0) {
+                                // the 4 partials of this ray, chained front to back
+                                bool got = true;
+                                if (lane == 0) {
+                                    got = mbar_wait(bar(kBarComp + grp), comp_ph, abort, &g_status,
+                                                    kStatusTimeoutOther);
+                                    if (got) {
+                                        float rr = 0.0f, gg = 0.0f, bb = 0.0f, tsum = 0.0f;
+#pragma unroll
+                                        for (int q = 0; q < 4; ++q) {
+                                            const float tr = expf(-tsum);
+                                            rr += tr * scr[q * 4 + 0];
+                                            gg += tr * scr[q * 4 + 1];
+                                            bb += tr * scr[q * 4 + 2];
+                                            tsum += scr[q * 4 + 3];
+                                        }
+                                        reinterpret_cast<float4*>(p.ray.rgba)[pix] =
+                                            make_float4(rr, gg, bb, -expm1f(-tsum));
+                                    }
+                                }
+                                comp_ph ^= 1u;
+                                if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) ok = false;
+                            }
+                        }
                     } else {
                         const long long grow = static_cast<long long>(t) * kTileM + row;
                         if (grow < p.n_rows) {

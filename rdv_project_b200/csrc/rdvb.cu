@@ -17,6 +17,7 @@
 #include "mlp_tc.cuh"
 #include "mlp_simt.cuh"
 #include "winograd.cuh"
+#include "raymarch.cuh"
 
 namespace {
 
@@ -44,7 +45,7 @@ struct DeviceInfo {
     bool init = false;
     int sm_count = 0;
     int max_smem_optin = 0;
-    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2] = {};
+    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2][2] = {};  // [slots][bf16][ray]
     size_t simt_smem_set = 0;
     size_t wino_smem_set[2] = {};
 };
@@ -129,18 +130,23 @@ int check_chain(int n_layers, const int* dims, const int* flags) {
 }
 
 // --------------------------------------------------- tensor-core launcher
+// Launches the tcgen05 fused-MLP kernel on rows [0, n_rows) of x, or, with
+// `ray` set, in ray-march mode (tiles = the rays of ray->hit_list, count on
+// the device). Sets *taken when the chain fits the kernel and it launched.
 int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims, const int* flags,
-                  int input_relu, const void* packed, float* y, cudaStream_t stream, DeviceInfo* dev, bool* taken) {
+                  int input_relu, const void* packed, float* y, cudaStream_t stream, DeviceInfo* dev, bool* taken,
+                  const rdvb::mlp_tc::RayParams* ray = nullptr) {
     using namespace rdvb::mlp_tc;
     *taken = false;
-    if (n_rows <= 0) return RDVB_OK;
+    if (!ray && n_rows <= 0) return RDVB_OK;
     PackLayout L = pack_layout(n_layers, dims);
     if (!L.ok || packed == nullptr) return RDVB_OK;
     const int math = flags[0] & 3;
     if (math == RDVB_MATH_F32) return RDVB_OK;
     for (int l = 1; l < n_layers; ++l)
         if ((flags[l] & 3) != math) return RDVB_OK;
-    if (!aligned(x, 16) || !aligned(packed, 256) || !aligned(y, 4)) return RDVB_OK;
+    if (!aligned(packed, 256)) return RDVB_OK;
+    if (!ray && (!aligned(x, 16) || !aligned(y, 4))) return RDVB_OK;
 
     Params p;
     memset(&p, 0, sizeof(p));
@@ -166,7 +172,8 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
         p.layer[l].relu = (flags[l] & RDVB_LAYER_RELU) ? 1u : 0u;
     }
     const int esize = x_dtype == RDVB_F32 ? 4 : 2;
-    p.x_stage_bytes = round_up(static_cast<uint32_t>(kTileM) * dims[0] * esize, 128);
+    p.x_stage_bytes = ray ? 0u : round_up(static_cast<uint32_t>(kTileM) * dims[0] * esize, 128);
+    if (ray) p.ray = *ray;
     p.y_vec4 = (p.out_dim % 4 == 0 && aligned(y, 16)) ? 1 : 0;
     const uint32_t budget = static_cast<uint32_t>(dev->max_smem_optin);
 
@@ -193,7 +200,8 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
             q.off_ones = q.off_x + slots * q.x_stage_bytes;  // 1 KB multiple: x stages are 128 B multiples
             q.off_ones = round_up(q.off_ones, 1024);
             q.off_bar = q.off_ones + kOnesBytes;
-            return q.off_bar + kBarBlockBytes + 1024u;
+            q.off_ray = round_up(q.off_bar + kBarBlockBytes, 16);
+            return q.off_ray + kRayScratchBytes + 1024u;
         };
         const uint32_t resident_size = round_up(L.total_w, 1024);
         uint32_t total = place(resident_size);
@@ -232,23 +240,32 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     if (!slots) return RDVB_OK;  // does not fit: CUDA-core path
 
     int rc = RDVB_OK;
+    const int ri = ray ? 1 : 0;
     auto go = [&](auto kernel, int sl) {
-        if (dev->tc_smem_set[sl][bf16] < smem) {
+        if (dev->tc_smem_set[sl][bf16][ri] < smem) {
             cudaError_t e =
                 cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
             if (e != cudaSuccess) {
                 rc = fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(mlp_tc<%d>): %s", sl, cudaGetErrorString(e));
                 return;
             }
-            dev->tc_smem_set[sl][bf16] = smem;
+            dev->tc_smem_set[sl][bf16][ri] = smem;
         }
+        // ray mode: the tile count is only known on the device; a CTA with
+        // no tile exits after loading the weights
         const int groups = (p.n_tiles + sl - 1) / sl;
-        const int grid = std::min(dev->sm_count, groups);
+        const int grid = ray ? dev->sm_count : std::min(dev->sm_count, groups);
         kernel<<<grid, kThreads, smem, stream>>>(p);
     };
-    if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1>, 4) : go(mlp_tc_kernel<4, 0>, 4);
-    else if (slots == 3) bf16 ? go(mlp_tc_kernel<3, 1>, 3) : go(mlp_tc_kernel<3, 0>, 3);
-    else bf16 ? go(mlp_tc_kernel<2, 1>, 2) : go(mlp_tc_kernel<2, 0>, 2);
+    if (ray) {
+        if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1, true>, 4) : go(mlp_tc_kernel<4, 0, true>, 4);
+        else if (slots == 3) bf16 ? go(mlp_tc_kernel<3, 1, true>, 3) : go(mlp_tc_kernel<3, 0, true>, 3);
+        else bf16 ? go(mlp_tc_kernel<2, 1, true>, 2) : go(mlp_tc_kernel<2, 0, true>, 2);
+    } else {
+        if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1, false>, 4) : go(mlp_tc_kernel<4, 0, false>, 4);
+        else if (slots == 3) bf16 ? go(mlp_tc_kernel<3, 1, false>, 3) : go(mlp_tc_kernel<3, 0, false>, 3);
+        else bf16 ? go(mlp_tc_kernel<2, 1, false>, 2) : go(mlp_tc_kernel<2, 0, false>, 2);
+    }
     if (rc) return rc;
     *taken = true;
     return check_launch("mlp_tc_kernel");
@@ -556,6 +573,121 @@ int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin,
         rdvb::wino::conv2d_direct_kernel<false><<<blocks, threads, 0, st>>>(x, weight, bias, y, n, h, w, cin, cout, kh,
                                                                             kw);
     return check_launch("conv2d_direct_kernel");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------- ray-march
+namespace {
+
+struct Vec3 {
+    float x, y, z;
+};
+Vec3 v_sub(Vec3 a, Vec3 b) { return {a.x - b.x, a.y - b.y, a.z - b.z}; }
+Vec3 v_cross(Vec3 a, Vec3 b) { return {a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x}; }
+Vec3 v_norm(Vec3 a) {
+    const float l = std::sqrt(a.x * a.x + a.y * a.y + a.z * a.z);
+    return {a.x / l, a.y / l, a.z / l};
+}
+
+constexpr float kDefaultFov = 0.78539816339744830962f;  // pi / 4 (rendering.py:33)
+
+}  // namespace
+
+extern "C" {
+
+int64_t rdvb_raymarch_workspace_bytes(int width, int height) {
+    if (width < 1 || height < 1) return 0;
+    return 256 + static_cast<int64_t>(width) * height * 4;
+}
+
+int rdvb_raymarch_render(const float* pose9, int width, int height, float fov, float aspect, int n_samples,
+                         int n_layers, const int* dims, const int* layer_flags, const void* packed, int row_begin,
+                         int row_end, void* workspace, size_t workspace_bytes, float* rgba, void* stream) {
+    using namespace rdvb::mlp_tc;
+    if (!pose9 || !dims || !layer_flags) return fail(RDVB_ERR_INVALID_ARG, "pose9, dims and layer_flags must not be NULL");
+    if (width < 1 || height < 1) return fail(RDVB_ERR_INVALID_ARG, "width and height must be positive");
+    if (row_begin < 0 || row_end > height || row_begin > row_end)
+        return fail(RDVB_ERR_INVALID_ARG, "rows [%d, %d) are not inside [0, %d)", row_begin, row_end, height);
+    if (n_samples != kTileM)
+        return fail(RDVB_ERR_UNSUPPORTED, "n_samples must be %d (one tensor-core tile per ray), got %d", kTileM,
+                    n_samples);
+    if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
+    if (dims[0] != 3 || dims[n_layers] != 4)
+        return fail(RDVB_ERR_INVALID_ARG, "the MLP must map 3 -> 4 (density, r, g, b); got %d -> %d", dims[0],
+                    dims[n_layers]);
+    const int math = layer_flags[0] & 3;
+    if (math == RDVB_MATH_F32) return fail(RDVB_ERR_UNSUPPORTED, "ray-march MLP layers must be RDVB_MATH_F16 or _BF16");
+    for (int l = 1; l < n_layers; ++l)
+        if ((layer_flags[l] & 3) != math) return fail(RDVB_ERR_UNSUPPORTED, "all layers must use the same arithmetic");
+    PackLayout L = pack_layout(n_layers, dims);
+    if (!L.ok) return fail(RDVB_ERR_UNSUPPORTED, "MLP widths must be <= %u", kMaxWidth);
+    if (!packed || !aligned(packed, 256)) return fail(RDVB_ERR_INVALID_ARG, "packed must be a 256-byte aligned pointer");
+    if (!rgba || !aligned(rgba, 16)) return fail(RDVB_ERR_INVALID_ARG, "rgba must be a 16-byte aligned pointer");
+    const long long n_pix = static_cast<long long>(row_end - row_begin) * width;
+    if (n_pix == 0) return RDVB_OK;
+    const int64_t need = 256 + n_pix * 4;
+    if (!workspace || !aligned(workspace, 256) || static_cast<int64_t>(workspace_bytes) < need)
+        return fail(RDVB_ERR_INVALID_ARG, "workspace must be 256-byte aligned and hold %lld bytes", (long long)need);
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    // camera (cameras.h:1-20): look-at basis, computed once in fp32
+    if (!(fov > 0.0f)) fov = kDefaultFov;
+    if (!(aspect > 0.0f)) aspect = static_cast<float>(width) / static_cast<float>(height);
+    const Vec3 o{pose9[0], pose9[1], pose9[2]}, t{pose9[3], pose9[4], pose9[5]}, n{pose9[6], pose9[7], pose9[8]};
+    const Vec3 z = v_norm(v_sub(t, o));
+    const Vec3 xa = v_norm(v_cross(n, z));
+    const Vec3 ya = v_cross(z, xa);
+    RayParams rp;
+    memset(&rp, 0, sizeof(rp));
+    rp.org[0] = o.x; rp.org[1] = o.y; rp.org[2] = o.z;
+    rp.xa[0] = xa.x; rp.xa[1] = xa.y; rp.xa[2] = xa.z;
+    rp.ya[0] = ya.x; rp.ya[1] = ya.y; rp.ya[2] = ya.z;
+    rp.za[0] = z.x; rp.za[1] = z.y; rp.za[2] = z.z;
+    rp.aspect = aspect;
+    rp.sz = 1.0f / std::tan(fov * 0.5f);
+    rp.width = width;
+    rp.height = height;
+    rp.row_begin = row_begin;
+    int* n_hits = static_cast<int*>(workspace);
+    int* hit_list = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + 256);
+    rp.hit_list = hit_list;
+    rp.n_hits = n_hits;
+    rp.rgba = rgba;
+
+    cudaError_t e = cudaMemsetAsync(n_hits, 0, sizeof(int), st);
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((n_pix + threads - 1) / threads,
+                                                                                   dev->sm_count * 16LL)));
+    rdvb::ray::ray_compact_kernel<<<blocks, threads, 0, st>>>(rp, static_cast<int>(n_pix), hit_list, n_hits, rgba);
+    if (int rc = check_launch("ray_compact_kernel")) return rc;
+    bool taken = false;
+    if (int rc = launch_mlp_tc(nullptr, RDVB_F32, 0, n_layers, dims, layer_flags, 0, packed, nullptr, st, dev, &taken,
+                               &rp))
+        return rc;
+    if (!taken) return fail(RDVB_ERR_UNSUPPORTED, "MLP does not fit the tensor-core kernel");
+    return RDVB_OK;
+}
+
+int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, float* out,
+                     void* stream) {
+    if (n_cameras < 0 || width < 0 || height < 0) return fail(RDVB_ERR_INVALID_ARG, "sizes must be >= 0");
+    if (n_cameras == 0 || width == 0 || height == 0) return RDVB_OK;
+    if (!poses || !out) return fail(RDVB_ERR_INVALID_ARG, "poses and out must not be NULL");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    if (!(fov > 0.0f)) fov = kDefaultFov;
+    if (!(aspect > 0.0f)) aspect = static_cast<float>(width) / static_cast<float>(height);
+    const long long total = static_cast<long long>(n_cameras) * width * height;
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + threads - 1) / threads,
+                                                                                   dev->sm_count * 16LL)));
+    rdvb::ray::camera_rays_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        poses, n_cameras, width, height, aspect, fov, out);
+    return check_launch("camera_rays_kernel");
 }
 
 }  // extern "C"
