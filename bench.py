@@ -286,8 +286,10 @@ def run_ours(args, spec, world, rank, local):
     m = build_map(rdv, layers, dev)
     sharded = spec["name"] == "c5"
     if sharded:
-        per_rank = spec["rows"] // world
-        x_host = make_input(spec, spec["rows"], seed=0)[rank * per_rank:(rank + 1) * per_rank].contiguous()
+        from rdv_project_b200.sharding import all_gather_rows, shard_range
+        rb, re_ = shard_range(spec["rows"], world, rank)
+        per_rank = re_ - rb
+        x_host = make_input(spec, spec["rows"], seed=0)[rb:re_].contiguous()
         y_all = torch.empty(spec["rows"], spec["dims"][-1], device=dev)
     else:
         per_rank = spec["rows"]
@@ -299,8 +301,7 @@ def run_ours(args, spec, world, rank, local):
         y = m(x_dev)
         if sharded:
             if world > 1:
-                import torch.distributed as dist
-                dist.all_gather_into_tensor(y_all, y.as_tensor("torch"))
+                all_gather_rows(y.as_tensor("torch"), spec["rows"], out=y_all)
             else:
                 y_all.copy_(y.as_tensor("torch"))
         return y
@@ -388,7 +389,324 @@ def run_ours(args, spec, world, rank, local):
     }
     if world == 1 and not args.profile_run:
         line["cpu_baseline"] = cpu_baseline(spec, layers)
+        if spec["name"] == "c2" and not args.no_secondary:
+            # the other BASELINE configs, device-timed on this GPU in the same run
+            line["secondary"] = {
+                "c1": mlp_summary(c1_spec()),
+                "c3": run_c3(args, 1, 0, local, summary=True),
+                "c4": run_c4(args, 1, 0, local, summary=True),
+                "c5": mlp_summary(c5_spec()),
+            }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------- config 3: Winograd conv
+C3_SHAPE = (8, 256, 256, 64)  # NHWC float16 input, 64 output channels
+
+
+def c3_data():
+    x = torch.randn(C3_SHAPE, generator=torch.Generator().manual_seed(0)).half()
+    w = torch.randn((64, 64, 3, 3), generator=torch.Generator().manual_seed(1000)) * math.sqrt(2.0 / 576)
+    return x, w.permute(2, 3, 1, 0).contiguous(), torch.zeros(64)  # weight -> [3, 3, CIN, COUT]
+
+
+def c3_bytes(n_img, out_bytes=4):
+    _, h, w, c = C3_SHAPE
+    return n_img * h * w * c * (2 + out_bytes) + 16 * 64 * 64 * 2
+
+
+def time_steps(fn, steps, flush=None, stream=None):
+    """Sum of per-step CUDA-event times (s) on `stream`, L2 flushed between
+    steps (outside the timed intervals) when `flush` is given."""
+    stream = stream or torch.cuda.current_stream()
+    total = 0.0
+    for i in range(steps):
+        if flush is not None:
+            flush.fill_(i & 0xFF)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        total += e0.elapsed_time(e1) / 1e3
+    return total
+
+
+def run_c3(args, world, rank, local, summary=False):
+    import rdv_project_b200 as rdv
+    from rdv_project_b200 import _native as N
+    from rdv_project_b200.sharding import all_gather_rows, shard_range
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    x_all, w33io, b = c3_data()
+    ib, ie = shard_range(C3_SHAPE[0], world, rank)
+    n_img = ie - ib
+    x_host = x_all[ib:ie].contiguous()
+    x = x_host.to(dev)
+    conv = rdv.Conv3x3Winograd(w33io, b)
+    y = torch.empty(x.shape[:3] + (64,), dtype=torch.float32, device=dev)
+    y_all = torch.empty(C3_SHAPE[:3] + (64,), dtype=torch.float32, device=dev) if world > 1 else None
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    def step():
+        conv(x, out=y)
+        if world > 1:
+            all_gather_rows(y, C3_SHAPE[0], out=y_all)
+
+    steps = 5 if summary else args.steps
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    parity = (None, None)
+    if not args.profile_run:
+        ref = rdv.conv2d_direct(x[:1], w33io, b)
+        d = (y[:1].double() - ref.double()).abs()
+        r = ref.double()
+        parity = ((d.max() / r.abs().max()).item(), (d / (r.abs() + r.pow(2).mean().sqrt())).max().item())
+    sampler = ClockSampler(local) if (rank == 0 and not summary) else None
+    barrier(world)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    l0 = N.launch_count()
+    t_kernel = time_steps(lambda: conv(x, out=y), steps, flush)
+    t_step = time_steps(step, steps, flush)
+    launches = N.launch_count() - l0
+    clocks = sampler.stop() if sampler else None
+    t_kernel = max_over_ranks(t_kernel, world)
+    t_step = max_over_ranks(t_step, world)
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = c3_bytes(n_img) / (t_kernel / steps) / 1e9
+    value = c3_bytes(C3_SHAPE[0]) * steps / t_step / 1e9
+    if summary:
+        return {"workload": "BASELINE config 3: Winograd F(2x2,3x3) 8x256x256x64 fp16 -> 64 fp32",
+                "metric": "Winograd GB/s", "value": value, "ms_per_step": t_step / steps * 1e3,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                             "frac": achieved / hbm, "peak_source": f"{peak_kind} hbm_gbs"},
+                "parity_vs_direct": {"normwise": parity[0], "elementwise": parity[1]}}
+    # end to end through the public API with host buffers
+    x_pin = x_host.pin_memory()
+    y_pin = torch.empty(y.shape, dtype=torch.float32).pin_memory()
+    e2e_steps = 0 if args.profile_run else max(1, min(args.steps, 5))
+
+    def e2e_step():
+        yy = conv(x_pin.to(dev, non_blocking=True))
+        y_pin.copy_(yy, non_blocking=True)
+
+    t_e2e = max_over_ranks(time_steps(e2e_step, e2e_steps, flush), world) if e2e_steps else None
+    if rank != 0:
+        return None
+    line = {
+        "metric": "Winograd GB/s", "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": t_step / steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded torch.Generator)",
+        "config": {"workload": "BASELINE config 3: Winograd F(2x2,3x3) conv, stride 1, pad 1, NHWC fp16 "
+                               "8x256x256x64 -> 64 (fp32 out), Kaiming-normal weights",
+                   "images_per_gpu": n_img, "algorithmic_bytes_per_step": c3_bytes(C3_SHAPE[0]),
+                   "l2": "flushed between steps (256 MB write, outside the timed intervals)",
+                   "parallelism": f"images split over {world} rank(s), NCCL all-gather of the outputs"},
+        "e2e": {"value": c3_bytes(C3_SHAPE[0]) * e2e_steps / t_e2e / 1e9 if e2e_steps else None, "unit": "GB/s",
+                "h2d_bytes_per_step": int(x_pin.numel() * 2), "d2h_bytes_per_step": int(y_pin.numel() * 4)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": ncu_traffic("winograd_f23_c3"), "peak_source": f"{peak_kind} hbm_gbs",
+                     "bytes_per_launch": c3_bytes(n_img)},
+        "parity": {"against": "on-device fp32 direct conv, image 0", "normwise": parity[0], "elementwise": parity[1]},
+        "clocks": clocks,
+    }
+    if world == 1 and not args.profile_run:
+        line["cpu_baseline"] = c3_cpu_baseline(x_all, w33io, b)
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def c3_cpu_baseline(x_all, w33io, b, seconds=6.0):
+    """torch CPU fp32 conv2d (the direct convolution the reference's op
+    approximates) on float16-rounded images, all host threads."""
+    import torch.nn.functional as F
+
+    wt = w33io.permute(3, 2, 0, 1).contiguous()  # -> [COUT, CIN, 3, 3]
+    done, t0 = 0, time.perf_counter()
+    while True:
+        xi = x_all[done % x_all.shape[0]:done % x_all.shape[0] + 1].float().permute(0, 3, 1, 2)
+        F.conv2d(xi, wt, b, padding=1)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= x_all.shape[0]:
+            break
+    return {"value": c3_bytes(done) / el / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{done} of {x_all.shape[0]} images ({el:.1f} s), torch CPU fp32 conv2d on float16-rounded "
+                      f"input, algorithmic bytes of those images per second"}
+
+
+# ------------------------------------------------------- config 4: ray-march
+C4 = dict(width=1920, height=1080, dims=[3, 64, 64, 4], samples=128)
+
+
+def c4_layers():
+    spec = dict(dims=C4["dims"], math="f16", w_init="kaiming_normal")
+    return make_weights(spec)
+
+
+def run_c4(args, world, rank, local, summary=False):
+    import rdv_project_b200 as rdv
+    from rdv_project_b200 import _native as N
+    from rdv_project_b200.sharding import all_gather_rows, shard_range
+    from oracle import raymarch as orm
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = c4_layers()
+    ren = rdv.VolumeRenderer(build_map(rdv, layers, dev))
+    W, H = C4["width"], C4["height"]
+    pose = torch.from_numpy(orm.orbit_pose(0))
+    rb, re_ = shard_range(H, world, rank)
+    band = torch.empty((re_ - rb, W, 4), device=dev)
+    img = torch.empty((H, W, 4), device=dev) if world > 1 else None
+
+    def render():
+        ren.render(pose, W, H, row_begin=rb, row_end=re_, out=band)
+
+    def step():
+        render()
+        if world > 1:
+            all_gather_rows(band, H, out=img)
+
+    steps = 5 if summary else args.steps
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    hits = int(ren._ws[dev.index][:4].view(torch.int32).item())
+    parity = (None, None)
+    if not args.profile_run and rb <= 537 < re_ - 2:
+        got = band[537 - rb:540 - rb].cpu().numpy()
+        lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
+        ref = orm.render_emission_absorption(pose.numpy(), W, H, 128, lay_np, row_begin=537, row_end=540)
+        from oracle import mlp as omlp
+        parity = omlp.rel_errors(got, ref)
+    sampler = ClockSampler(local) if (rank == 0 and not summary) else None
+    barrier(world)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    l0 = N.launch_count()
+    t_kernel = time_steps(render, steps)
+    t_step = time_steps(step, steps)
+    launches = N.launch_count() - l0
+    clocks = sampler.stop() if sampler else None
+    t_kernel = max_over_ranks(t_kernel, world)
+    t_step = max_over_ranks(t_step, world)
+    peaks, peak_kind = measured_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    flops_sample = flops_per_row(C4["dims"])
+    achieved = hits * 128 * flops_sample / (t_kernel / steps) / 1e12
+    fps = steps / t_step
+    if summary:
+        return {"workload": "BASELINE config 4: ray-march 1920x1080, 128 samples/ray, MLP 3-64-64-4 fp16",
+                "metric": "frames/s", "value": fps, "ms_per_frame": t_step / steps * 1e3, "rays_hit": hits,
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "peak_source": f"{peak_kind} bf16_tflops",
+                             "note": "flops of the samples of rays that hit the box"},
+                "parity_vs_oracle_rows_537_539": {"normwise": parity[0], "elementwise": parity[1]}}
+    if rank != 0:
+        return None
+    line = {
+        "metric": "ray-march frames/s", "value": fps, "unit": "frames/s", "n_gpus": world, "steps": steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": t_step / steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded weights, orbit pose 0)",
+        "config": {"workload": "BASELINE config 4: volume ray-march 1920x1080, one pinhole ray per pixel, 128 "
+                               "uniform samples per ray, MLP 3-64-64-4 fp16 (softplus density, sigmoid RGB), "
+                               "front-to-back compositing",
+                   "rays_hit_box_rank0": hits, "samples_per_frame_evaluated_rank0": hits * 128,
+                   "l2": "weights only are reused; the RGBA output is written once",
+                   "parallelism": f"row bands over {world} rank(s), NCCL all-gather of the image"},
+        "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 36,
+                "d2h_bytes_per_step": int(H * W * 16)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": f"{peak_kind} bf16_tflops",
+                     "flops_per_launch": hits * 128 * flops_sample},
+        "parity": {"against": "oracle render of rows 537-539", "normwise": parity[0], "elementwise": parity[1]},
+        "clocks": clocks,
+    }
+    if not args.profile_run:
+        # end to end: host pose in, RGBA image back to pinned host memory
+        out_pin = torch.empty((re_ - rb, W, 4)).pin_memory()
+
+        def e2e_step():
+            render()
+            out_pin.copy_(band, non_blocking=True)
+
+        t_e2e = time_steps(e2e_step, max(1, min(args.steps, 5)))
+        line["e2e"] = {"value": max(1, min(args.steps, 5)) / t_e2e, "unit": "frames/s", "h2d_bytes_per_step": 36,
+                       "d2h_bytes_per_step": int(out_pin.numel() * 4)}
+        if world == 1:
+            line["cpu_baseline"] = c4_cpu_baseline(layers)
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def c4_cpu_baseline(layers, rows=4):
+    """Oracle restatement (numpy, float16-staged MLP) on a band of full-width
+    rows through the middle of the image, extrapolated to frames/s."""
+    from oracle import raymarch as orm
+
+    lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
+    t0 = time.perf_counter()
+    orm.render_emission_absorption(orm.orbit_pose(0), C4["width"], C4["height"], 128, lay_np, row_begin=538,
+                                   row_end=538 + rows)
+    el = time.perf_counter() - t0
+    return {"value": rows / el / C4["height"], "unit": "frames/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} full-width rows through the cube ({el:.1f} s, numpy/BLAS), extrapolated to 1080 rows "
+                      f"(the middle rows hit the box more than the frame average, so this favours the CPU)"}
+
+
+def run_reference_c34(args):
+    """Reference arm for configs 3 and 4: the CPU restatement of the
+    reference path on the host cores (rank 0 only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    if args.workload == "c3":
+        x_all, w33io, b = c3_data()
+        cb = c3_cpu_baseline(x_all, w33io, b, seconds=max(5.0, float(args.steps)))
+        metric, unit = "Winograd GB/s", "GB/s"
+    else:
+        cb = c4_cpu_baseline(c4_layers())
+        metric, unit = "ray-march frames/s", "frames/s"
+    line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32" if args.workload == "c3" else "f16",
+            "data": "synthetic (seeded)", "config": {"workload": f"BASELINE config {args.workload[1]}"},
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def mlp_summary(spec, steps=5):
+    """Device-timed MLP evals/s of another MLP config on this GPU (inputs
+    resident in HBM), for the secondary section of the headline line."""
+    import rdv_project_b200 as rdv
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = make_weights(spec)
+    m = build_map(rdv, layers, dev)
+    x = rdv.wrap(make_input(spec, spec["rows"], seed=0).to(dev))
+    for _ in range(3):
+        m(x)
+    torch.cuda.synchronize()
+    t = time_steps(lambda: m(x), steps)
+    peaks, peak_kind = measured_peaks()
+    achieved = flops_per_row(spec["dims"]) * spec["rows"] / (t / steps) / 1e12
+    out = {"workload": spec["workload"], "metric": METRIC, "value": spec["rows"] * len(layers) * steps / t,
+           "ms_per_step": t / steps * 1e3, "rows": spec["rows"]}
+    if spec["math"] != "f32":
+        peak = float(peaks.get("bf16_tflops", 1590.0))
+        out["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                           "frac": achieved / peak, "peak_source": f"{peak_kind} bf16_tflops"}
+    else:
+        out["achieved_tflops_fp32"] = achieved
+    return out
 
 
 def main():
@@ -397,12 +715,27 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1", "c5"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows per GPU instead of the config's (small cases for ncu captures)")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="headline line only (skip the other configs' device-timed summaries)")
     ap.add_argument("--profile-run", action="store_true",
                     help="timed loop only: no parity check, end-to-end leg or CPU baseline")
     args = ap.parse_args()
+    if args.workload in ("c3", "c4"):
+        if args.impl == "reference":
+            run_reference_c34(args)
+            return
+        world, rank, local = dist_setup(args.gpus)
+        try:
+            (run_c3 if args.workload == "c3" else run_c4)(args, world, rank, local)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.barrier()
+                dist.destroy_process_group()
+        return
     spec = {"c2": c2_spec, "c1": c1_spec, "c5": c5_spec}[args.workload]()
     if args.rows:
         spec["rows"] = args.rows

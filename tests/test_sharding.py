@@ -1,0 +1,75 @@
+"""Host-side multi-rank logic (CPU, gloo, world size 2): shard ranges and the
+final all-gather of row blocks. The per-rank compute here is a CPU stand-in
+(an affine map on torch CPU tensors); the GPU path runs the same functions
+with NCCL and the CUDA kernels (bench.py --gpus N)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from rdv_project_b200.sharding import all_gather_rows, shard_range, shard_sizes, sharded_map
+
+
+def test_shard_ranges_partition():
+    for n in [0, 1, 7, 64, 1000, 1080, 67_108_864]:
+        for world in [1, 2, 3, 4, 8]:
+            ranges = [shard_range(n, world, r) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == n
+            for (b0, e0), (b1, e1) in zip(ranges, ranges[1:]):
+                assert e0 == b1
+            sizes = shard_sizes(n, world)
+            assert max(sizes) - min(sizes) <= 1 and sum(sizes) == n
+    assert shard_range(1080, 8, 3) == (405, 540)
+    with pytest.raises(ValueError):
+        shard_range(10, 2, 2)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class _AffineStandIn:
+    """CPU stand-in for a Map: [rows, 3] -> [rows, 4]."""
+
+    IN, OUT = 3, 4
+
+    def __init__(self):
+        g = torch.Generator().manual_seed(5)
+        self.W = torch.randn(4, 3, generator=g)
+        self.b = torch.randn(4, generator=g)
+
+    def __call__(self, x):
+        return x @ self.W.T + self.b
+
+
+def _worker(rank, world, port, n):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        x = torch.arange(n * 3, dtype=torch.float32).reshape(n, 3) / 7.0
+        m = _AffineStandIn()
+        full = sharded_map(m, x)
+        torch.testing.assert_close(full, m(x))
+        # the gather of bare blocks, e.g. image row bands [rows, width, 4]
+        b, e = shard_range(n, world, rank)
+        band = torch.full((e - b, 2, 4), float(rank))
+        img = all_gather_rows(band, n)
+        for r in range(world):
+            rb, re = shard_range(n, world, r)
+            assert torch.all(img[rb:re] == r)
+        with pytest.raises(ValueError):
+            all_gather_rows(torch.zeros(e - b + 1, 4), n)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [8, 7, 1])
+def test_sharded_map_and_gather_gloo_world2(n):
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    mp.spawn(_worker, args=(2, _free_port(), n), nprocs=2, join=True)
