@@ -82,7 +82,8 @@ int64_t rdvb_mlp_packed_bytes(int n_layers, const int* dims);
 
 /* Converts fp32 weights/biases (device pointers, one per layer) into the
  * tensor-core image: float16 (operand = RDVB_F16) or bfloat16 (RDVB_BF16)
- * K-major 128-byte-swizzled blocks, biases padded to 16. `packed` must hold
+ * K-major 128-byte-swizzled weight blocks, then the fp32 biases of every
+ * layer (added to the fp32 accumulator, as the reference does). `packed` must hold
  * rdvb_mlp_packed_bytes() bytes, 256-byte aligned. The reference re-reads
  * fp32 weights at every dispatch (linear_fast.h:81-82); callers that change
  * weights in place call this again. */

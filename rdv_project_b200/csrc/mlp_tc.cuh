@@ -5,34 +5,31 @@
 // rdv/shaders/maps/composite.h:8-12 and driven one row per thread by
 // rdv/shaders/maps/map_evaluator.h:1-5). Arithmetic contract: inputs and
 // weights staged as float16 (or bfloat16), products accumulated in fp32, the
-// fp32 bias included in the fp32 accumulation, ReLU applied before the next
-// layer's float16 staging, fp32 output.
-//
-// Bias: the tensor core adds it as one extra K=16 step per layer -- a
-// constant A tile whose first two K columns are 1.0 against a B block whose
-// first two K rows hold the bias split into float16 hi + lo parts
-// (b = hi + lo + r, |r| <= 2^-22 |b|). The sum is fp32 and the products are
-// exact, so the result is the fp32 bias add up to that residual and the
-// order of fp32 additions. This keeps the epilogue to
-// TMEM load -> ReLU + convert -> TMEM store.
+// fp32 bias added to the fp32 accumulator (the reference's order: products
+// first, then + b), ReLU applied before the next layer's float16 staging,
+// fp32 output. The epilogue does the bias add (TMEM load -> + b -> ReLU +
+// convert -> TMEM store): the single MMA-issuing thread is the kernel's
+// serial resource, so it issues only the K steps.
 //
 // Design (one persistent CTA per SM, 19 warps):
 //   warps 0-15 epilogue. Warp w owns TMEM lane quadrant (w % 4) -- rows
-//              32*(w%4) .. +31 of every tile -- and, for slot s, the
-//              16-column chunks c with (c + s) % 4 == w / 4 (rotating the
-//              owner by slot spreads narrow layers over all warps). Per layer
-//              it reads its accumulator chunks (tcgen05.ld), applies ReLU
-//              while converting to f16/bf16 (cvt.rn.relu) and writes them
+//              32*(w%4) .. +31 of every tile. Warp group g = w / 4 owns slot
+//              g % SLOTS and, of that slot's 16-column chunks, every
+//              (4/SLOTS)-th one starting at g / SLOTS: the slots' epilogues
+//              run concurrently, each warp waiting only on its own slot. Per
+//              layer it reads its accumulator chunks (tcgen05.ld), applies
+//              ReLU while converting to f16/bf16 (cvt.rn.relu) and writes them
 //              back into TMEM (tcgen05.st) as the next layer's A operand, so
 //              hidden activations never touch shared memory; the last layer
-//              writes fp32 rows to global memory.
+//              writes fp32 rows to global memory (or, in ray mode, composites
+//              the ray's samples into one RGBA pixel).
 //   warp 16    producer: 1-D bulk (TMA) copies of input tiles and of the
 //              pre-swizzled weight blocks (resident, or streamed per layer
 //              through a ring), issued from one event loop.
 //   warp 17    MMA issuer: allocates TMEM; one thread issues tcgen05.mma
 //              (M=128, N=layer width, K=16 steps) per layer -- A from shared
-//              memory for the first layer, from TMEM after -- plus the bias
-//              step, and commits completion to mbarriers.
+//              memory for the first layer, from TMEM after -- and commits
+//              completion to mbarriers.
 //   warp 18    input staging: converts each input tile (x dtype ->
 //              f16/bf16, zero-padded to 16) into the first layer's A tile in
 //              shared memory (K-major, 128B swizzle).
@@ -57,17 +54,14 @@ constexpr int kThreads = 19 * 32;
 constexpr uint32_t kAtomBytes = kTileM * 128;      // one 64-wide K atom of a 128-row tile
 constexpr int kMaxWStages = 4;
 constexpr uint32_t kMaxWidth = 128;
-constexpr int kColGroups = kEpiWarps / 4;           // 4 column groups
-constexpr int kChunksPerWarp = (kMaxWidth / 16) / kColGroups;  // 2
-constexpr uint32_t kOnesBytes = kTileM * 32;        // constant A tile of the bias step
 constexpr uint32_t kTmemCols = 512;
 
 struct Layer {
     uint32_t k_pad;    // input width rounded up to 16
     uint32_t n_pad;    // output width rounded up to 16
     uint32_t w_off;    // byte offset of the layer block in the weight pack
-    uint32_t w_bytes;  // layer block: SW128 weights + bias block, 1 KB multiple
-    uint32_t bias_off; // byte offset of the bias block inside the layer block
+    uint32_t w_bytes;  // layer block: SW128 weights, 1 KB multiple
+    uint32_t b_idx;    // first element of the layer's fp32 bias in the bias block
     uint32_t idesc;
     uint32_t relu;
 };
@@ -99,7 +93,9 @@ struct Params {
     uint32_t w_slot_bytes;
     uint32_t w_total_bytes;
     uint32_t x_stage_bytes;
-    uint32_t off_w, off_x, off_ones, off_bar;
+    uint32_t off_w, off_x, off_bias, off_bar;
+    uint32_t bias_bytes;   // fp32 biases of every layer (n_pad each), 16-byte multiple
+    uint32_t bias_gofs;    // their byte offset in the weight pack
     uint32_t a0_bytes;     // shared-memory A tile of layer 0, per slot
     uint32_t acc_stride;   // TMEM columns of one slot's fp32 accumulator
     uint32_t act_base;     // first TMEM column of the activation regions
@@ -121,8 +117,9 @@ enum : int {
     kBarWFull = kBarAccFull + kMaxSlots,
     kBarWEmpty = kBarWFull + kMaxWStages,
     kBarDrain = kBarWEmpty + kMaxWStages,
-    kBarComp = kBarDrain + 1,                  // ray mode: per column group, 4 quadrant partials written
-    kNumBars = kBarComp + 4,
+    kBarComp = kBarDrain + 1,                  // ray mode: per slot, 4 quadrant partials written
+    kBarBias = kBarComp + 4,                   // fp32 biases landed (TMA tx)
+    kNumBars = kBarBias + 1,
 };
 constexpr uint32_t kRayScratchBytes = 4 * 4 * 4 * 4;
 constexpr uint32_t kBarBlockBytes = kNumBars * 8 + 16;  // + tmem base + abort word
@@ -161,6 +158,24 @@ template <int SLOTS>
 __device__ __forceinline__ int tile_of(int r, int s, int n_tiles) {
     const int t = (r * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x)) * SLOTS + s;
     return t < n_tiles ? t : -1;
+}
+
+// + fp32 bias of the chunk's 16 columns (shared memory, broadcast to all
+// lanes), in place on the raw accumulator words.
+__device__ __forceinline__ void add_bias16(uint32_t (&v)[16], const float* b) {
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 bb = b4[q];
+        float x0 = __uint_as_float(v[4 * q]), x1 = __uint_as_float(v[4 * q + 1]);
+        float x2 = __uint_as_float(v[4 * q + 2]), x3 = __uint_as_float(v[4 * q + 3]);
+        add_f32x2(x0, x1, bb.x, bb.y);
+        add_f32x2(x2, x3, bb.z, bb.w);
+        v[4 * q] = __float_as_uint(x0);
+        v[4 * q + 1] = __float_as_uint(x1);
+        v[4 * q + 2] = __float_as_uint(x2);
+        v[4 * q + 3] = __float_as_uint(x3);
+    }
 }
 
 // One warp's share of a 16-column accumulator chunk -> packed 16-bit
@@ -205,6 +220,7 @@ __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf
 
 template <int SLOTS, int BF16, bool RAY>
 __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_constant__ Params p) {
+    static_assert(SLOTS == 2 || SLOTS == 4, "the epilogue splits 4 warp groups evenly over the slots");
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the SW128 atoms.
     const uint32_t raw_addr = smem_addr(smem_raw);
@@ -214,7 +230,6 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
     const uint32_t a_base = base;  // SLOTS * a0_bytes (layer-0 A tiles)
     const uint32_t w_base = base + p.off_w;
     const uint32_t x_base = base + p.off_x;
-    const uint32_t ones_base = base + p.off_ones;
     const uint32_t bar_base = base + p.off_bar;
     auto bar = [&](int i) -> uint32_t { return bar_base + 8u * static_cast<uint32_t>(i); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + p.off_bar + kNumBars * 8);
@@ -229,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
             mbar_init(bar(kBarXEmpty + s), 1);
             mbar_init(bar(kBarA0Full + s), 1);
             mbar_init(bar(kBarA0Empty + s), 1);
-            mbar_init(bar(kBarAFull + s), kEpiWarps);
+            mbar_init(bar(kBarAFull + s), kEpiWarps / SLOTS);  // the warps owning the slot
             mbar_init(bar(kBarAccFull + s), 1);
         }
         for (int q = 0; q < kMaxWStages; ++q) {
@@ -238,15 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
         }
         mbar_init(bar(kBarDrain), 1);
         for (int g = 0; g < 4; ++g) mbar_init(bar(kBarComp + g), 4);
+        mbar_init(bar(kBarBias), 1);
         *abort = 0u;
         fence_mbarrier_init();
-    }
-    // Constant A tile of the bias step: every row is [1, 1, 0, ..., 0].
-    if (threadIdx.x < kTileM) {
-        const uint32_t one2 = BF16 ? 0x3F803F80u : 0x3C003C00u;
-        const uint32_t r = threadIdx.x;
-        st_shared_v4(ones_base + k16_plain_offset(r, 0), one2, 0u, 0u, 0u);
-        st_shared_v4(ones_base + k16_plain_offset(r, 8), 0u, 0u, 0u, 0u);
     }
     // Layer-0 A tiles start zeroed: chunks past the input width stay zero.
     for (uint32_t i = threadIdx.x; i < SLOTS * p.a0_bytes / 16; i += kThreads) st_shared_v4(a_base + i * 16, 0u, 0u, 0u, 0u);
@@ -279,6 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
             const bool no_tiles = tile_of<SLOTS>(0, 0, n_tiles) < 0;
             bool x_done = RAY || no_tiles;  // ray mode: samples are generated, not loaded
             bool w_done = p.resident || no_tiles;
+            // fp32 biases of every layer, read by the epilogue
+            mbar_arrive_expect_tx(bar(kBarBias), p.bias_bytes);
+            bulk_g2s(base + p.off_bias, p.wpack + p.bias_gofs, p.bias_bytes, bar(kBarBias));
             if (p.resident) {
                 mbar_arrive_expect_tx(bar(kBarWFull), p.w_total_bytes);
                 for (int l = 0; l < n_layers; ++l)
@@ -347,6 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                         drain_wait(bar(kBarWFull + c % p.w_stages), (c / p.w_stages) & 1u);
                 }
             }
+            // the bias copy is waited for by the epilogue only when the CTA has tiles
+            drain_wait(bar(kBarBias), 0u);
         }
     } else if (warp == kStageWarp) {
         // ---------------------------------------------- input staging
@@ -439,9 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
             uint32_t q = 0, wph = 0;       // weight ring slot and its phase
             bool ok = true;
             bool issued = false;
-            const uint64_t ones_desc = umma_desc_k16_plain(ones_base);
             const uint64_t w_desc_sw = umma_desc_sw128(w_base);     // + (byte offset >> 4)
-            const uint64_t w_desc_plain = umma_desc_k16_plain(w_base);
             if (p.resident) ok = mbar_wait(bar(kBarWFull), 0u, abort, &g_status, kStatusTimeoutWFull);
             // Per-slot operand addresses, fixed for the whole kernel.
             uint32_t d_tm[SLOTS], a_tm[SLOTS];
@@ -472,7 +484,6 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                     uint64_t b_desc[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) b_desc[j] = b0 + (j >> 2) * n8 + (j & 3) * 2;
-                    const uint64_t bias_desc = w_desc_plain + ((blk + p.layer[l].bias_off) >> 4);
 #pragma unroll
                     for (int s = 0; s < SLOTS; ++s) {
                         if (tile_of<SLOTS>(r, s, n_tiles) < 0) break;
@@ -509,8 +520,6 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                                 if (j < static_cast<int>(ksteps))
                                     umma_f16_ts(d_tm[s], a_tm[s] + j * 8u, b_desc[j], idesc, j > 0 ? 1u : 0u);
                         }
-                        // bias step: ones[128 x 16] x [b_hi; b_lo; 0...]
-                        umma_f16(d_tm[s], ones_desc, bias_desc, idesc, 1u);
                         if (l == 0) umma_commit(bar(kBarA0Empty + s));
                         umma_commit(bar(kBarAccFull + s));
                         issued = true;
@@ -536,153 +545,163 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
         const int grp = warp >> 2;
         const int row = quad * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-        uint32_t acph = 0u;  // per-slot parity of the next acc_full phase
-        uint32_t comp_ph = 0u;  // ray mode: parity of this group's next compositing phase
+        // Warp group grp owns slot grp % SLOTS and, of that slot's 16-column
+        // chunks, every kGroupsPerSlot-th one starting at grp / SLOTS, so the
+        // slots' epilogues run concurrently and a warp only ever waits on its
+        // own slot's accumulator.
+        constexpr int kGroupsPerSlot = 4 / SLOTS;
+        const int s = grp % SLOTS;
+        const uint32_t sub = static_cast<uint32_t>(grp / SLOTS);
+        const uint32_t t_col = tmem_base + lane_off + static_cast<uint32_t>(s) * p.acc_stride;
+        const uint32_t t_act = tmem_base + lane_off + p.act_base + static_cast<uint32_t>(s) * p.act_stride;
+        uint32_t acph = 0u;     // parity of the slot's next acc_full phase
+        uint32_t comp_ph = 0u;  // ray mode: parity of the slot's next compositing phase
         bool ok = true;
+        const float* bias_smem = reinterpret_cast<const float*>(base_ptr + p.off_bias);
+        if (tile_of<SLOTS>(0, s, n_tiles) >= 0) {
+            const bool got = mbar_wait(bar(kBarBias), 0u, abort, &g_status, kStatusTimeoutWFull);
+            ok = __all_sync(0xffffffffu, got);
+        }
 
-        for (int r = 0; ok && tile_of<SLOTS>(r, 0, n_tiles) >= 0; ++r) {
+        for (int r = 0; ok; ++r) {
+            const int t = tile_of<SLOTS>(r, s, n_tiles);
+            if (t < 0) break;
             for (int l = 0; l < n_layers && ok; ++l) {
                 const bool last = (l == n_layers - 1);
                 const uint32_t nch = p.layer[l].n_pad >> 4;
                 const bool relu = p.layer[l].relu != 0;
-#pragma unroll
-                for (int s = 0; s < SLOTS; ++s) {
-                    const int t = tile_of<SLOTS>(r, s, n_tiles);
-                    if (t < 0) break;
-                    const bool good =
-                        mbar_wait(bar(kBarAccFull + s), (acph >> s) & 1u, abort, &g_status, kStatusTimeoutAccFull);
-                    // tcgen05.ld/st below are warp-collective: leave together
-                    if (!__all_sync(0xffffffffu, good)) {
-                        ok = false;
-                        break;
-                    }
-                    acph ^= 1u << s;
-                    tc_fence_after();
-                    const uint32_t c0 = static_cast<uint32_t>((grp - s) & 3);  // first chunk owned for this slot
-                    const uint32_t t_col = tmem_base + lane_off + static_cast<uint32_t>(s) * p.acc_stride;
-                    uint32_t v[kChunksPerWarp][16];
-#pragma unroll
-                    for (int j = 0; j < kChunksPerWarp; ++j) {
-                        const uint32_t c = c0 + kColGroups * j;
-                        if (c < nch) tmem_ld16(t_col + c * 16, v[j]);
-                    }
-                    tmem_wait_ld();
-                    if (!last) {
-                        const uint32_t t_act =
-                            tmem_base + lane_off + p.act_base + static_cast<uint32_t>(s) * p.act_stride;
-#pragma unroll
-                        for (int j = 0; j < kChunksPerWarp; ++j) {
-                            const uint32_t c = c0 + kColGroups * j;
-                            if (c < nch) {
-                                uint32_t pk[8];
-                                if (relu) convert_chunk<BF16, true>(v[j], pk);
-                                else convert_chunk<BF16, false>(v[j], pk);
-                                // columns c*16 .. c*16+15 of this layer are K elements
-                                // c*16 .. c*16+15 of the next: 8 packed TMEM columns
-                                tmem_st8(t_act + c * 8, pk);
-                            }
-                        }
-                        tmem_wait_st();
-                    } else if constexpr (RAY) {
-                        // Front-to-back emission-absorption compositing of the
-                        // ray's 128 samples (rows = samples in order): the warps
-                        // owning columns 0..15 (sigma, r, g, b) each scan their
-                        // quadrant's 32 samples with shuffles; quadrant 0 of the
-                        // group chains the 4 partials.
-                        if (c0 == 0) {
-                            const int pix = __ldg(p.ray.hit_list + t);
-                            float o[3], w[3], t0, t1;
-                            ray_setup(p.ray, pix, o, w, t0, t1);
-                            const float dt = (t1 - t0) / static_cast<float>(kTileM);
-                            const float tau = softplus_f(__uint_as_float(v[0][0])) * dt;
-                            const float alpha = -expm1f(-tau);
-                            float incl = tau;
-#pragma unroll
-                            for (int d = 1; d < 32; d <<= 1) {
-                                const float nb = __shfl_up_sync(0xffffffffu, incl, d);
-                                if (lane >= d) incl += nb;
-                            }
-                            float excl = __shfl_up_sync(0xffffffffu, incl, 1);
-                            if (lane == 0) excl = 0.0f;
-                            const float wgt = expf(-excl) * alpha;  // T_i * alpha_i within the quadrant
-                            float cr = wgt * sigmoid_f(__uint_as_float(v[0][1]));
-                            float cg = wgt * sigmoid_f(__uint_as_float(v[0][2]));
-                            float cb = wgt * sigmoid_f(__uint_as_float(v[0][3]));
-#pragma unroll
-                            for (int d = 16; d > 0; d >>= 1) {
-                                cr += __shfl_xor_sync(0xffffffffu, cr, d);
-                                cg += __shfl_xor_sync(0xffffffffu, cg, d);
-                                cb += __shfl_xor_sync(0xffffffffu, cb, d);
-                            }
-                            const float tau_q = __shfl_sync(0xffffffffu, incl, 31);
-                            float* scr = reinterpret_cast<float*>(base_ptr + p.off_ray) + grp * 16;
-                            if (lane == 0) {
-                                scr[quad * 4 + 0] = cr;
-                                scr[quad * 4 + 1] = cg;
-                                scr[quad * 4 + 2] = cb;
-                                scr[quad * 4 + 3] = tau_q;
-                                mbar_arrive(bar(kBarComp + grp));
-                            }
-                            if (quad == 0) {
-                                // the 4 partials of this ray, chained front to back
-                                bool got = true;
-                                if (lane == 0) {
-                                    got = mbar_wait(bar(kBarComp + grp), comp_ph, abort, &g_status,
-                                                    kStatusTimeoutOther);
-                                    if (got) {
-                                        float rr = 0.0f, gg = 0.0f, bb = 0.0f, tsum = 0.0f;
-#pragma unroll
-                                        for (int q = 0; q < 4; ++q) {
-                                            const float tr = expf(-tsum);
-                                            rr += tr * scr[q * 4 + 0];
-                                            gg += tr * scr[q * 4 + 1];
-                                            bb += tr * scr[q * 4 + 2];
-                                            tsum += scr[q * 4 + 3];
-                                        }
-                                        reinterpret_cast<float4*>(p.ray.rgba)[pix] =
-                                            make_float4(rr, gg, bb, -expm1f(-tsum));
-                                    }
-                                }
-                                comp_ph ^= 1u;
-                                if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) ok = false;
-                            }
-                        }
-                    } else {
-                        const long long grow = static_cast<long long>(t) * kTileM + row;
-                        if (grow < p.n_rows) {
-                            float* yrow = p.y + grow * p.out_dim;
-#pragma unroll
-                            for (int j = 0; j < kChunksPerWarp; ++j) {
-                                const uint32_t c = c0 + kColGroups * j;
-                                if (c < nch) {
-                                    float o[16];
-#pragma unroll
-                                    for (int i = 0; i < 16; ++i) {
-                                        const float a = __uint_as_float(v[j][i]);
-                                        o[i] = relu ? fmaxf(a, 0.0f) : a;
-                                    }
-                                    const int col0 = c * 16;
-                                    if (p.y_vec4 && col0 + 16 <= p.out_dim) {
-                                        float4* dst = reinterpret_cast<float4*>(yrow + col0);
-                                        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
-                                        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
-                                        dst[2] = make_float4(o[8], o[9], o[10], o[11]);
-                                        dst[3] = make_float4(o[12], o[13], o[14], o[15]);
-                                    } else {
-#pragma unroll
-                                        for (int i = 0; i < 16; ++i)
-                                            if (col0 + i < p.out_dim) yrow[col0 + i] = o[i];
-                                    }
-                                }
-                            }
-                        }
-                    }
-                    // activations written (or, after the last layer, the
-                    // accumulator read): the slot's next MMA may proceed
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(bar(kBarAFull + s));
+                const float* bias_l = bias_smem + p.layer[l].b_idx;
+                const bool good = mbar_wait(bar(kBarAccFull + s), acph, abort, &g_status, kStatusTimeoutAccFull);
+                // tcgen05.ld/st below are warp-collective: leave together
+                if (!__all_sync(0xffffffffu, good)) {
+                    ok = false;
+                    break;
                 }
+                acph ^= 1u;
+                tc_fence_after();
+                if (!last) {
+                    // two chunks per round trip: columns c*16..c*16+15 of this
+                    // layer are K elements c*16.. of the next, 8 packed columns
+                    for (uint32_t c = sub; c < nch; c += 2 * kGroupsPerSlot) {
+                        const uint32_t c2 = c + kGroupsPerSlot;
+                        uint32_t v0[16], v1[16];
+                        tmem_ld16(t_col + c * 16, v0);
+                        if (c2 < nch) tmem_ld16(t_col + c2 * 16, v1);
+                        tmem_wait_ld();
+                        add_bias16(v0, bias_l + c * 16);
+                        if (c2 < nch) add_bias16(v1, bias_l + c2 * 16);
+                        uint32_t pk[8];
+                        if (relu) convert_chunk<BF16, true>(v0, pk);
+                        else convert_chunk<BF16, false>(v0, pk);
+                        tmem_st8(t_act + c * 8, pk);
+                        if (c2 < nch) {
+                            if (relu) convert_chunk<BF16, true>(v1, pk);
+                            else convert_chunk<BF16, false>(v1, pk);
+                            tmem_st8(t_act + c2 * 8, pk);
+                        }
+                    }
+                    tmem_wait_st();
+                } else if constexpr (RAY) {
+                    // Front-to-back emission-absorption compositing of the
+                    // ray's 128 samples (rows = samples in order): the warps
+                    // owning columns 0..15 (sigma, r, g, b) each scan their
+                    // quadrant's 32 samples with shuffles; quadrant 0 chains
+                    // the 4 partials.
+                    if (sub == 0) {
+                        uint32_t v0[16];
+                        tmem_ld16(t_col, v0);
+                        tmem_wait_ld();
+                        add_bias16(v0, bias_l);
+                        const int pix = __ldg(p.ray.hit_list + t);
+                        float o[3], w[3], t0, t1;
+                        ray_setup(p.ray, pix, o, w, t0, t1);
+                        const float dt = (t1 - t0) / static_cast<float>(kTileM);
+                        const float tau = softplus_f(__uint_as_float(v0[0])) * dt;
+                        const float alpha = -expm1f(-tau);
+                        float incl = tau;
+#pragma unroll
+                        for (int d = 1; d < 32; d <<= 1) {
+                            const float nb = __shfl_up_sync(0xffffffffu, incl, d);
+                            if (lane >= d) incl += nb;
+                        }
+                        float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+                        if (lane == 0) excl = 0.0f;
+                        const float wgt = expf(-excl) * alpha;  // T_i * alpha_i within the quadrant
+                        float cr = wgt * sigmoid_f(__uint_as_float(v0[1]));
+                        float cg = wgt * sigmoid_f(__uint_as_float(v0[2]));
+                        float cb = wgt * sigmoid_f(__uint_as_float(v0[3]));
+#pragma unroll
+                        for (int d = 16; d > 0; d >>= 1) {
+                            cr += __shfl_xor_sync(0xffffffffu, cr, d);
+                            cg += __shfl_xor_sync(0xffffffffu, cg, d);
+                            cb += __shfl_xor_sync(0xffffffffu, cb, d);
+                        }
+                        const float tau_q = __shfl_sync(0xffffffffu, incl, 31);
+                        float* scr = reinterpret_cast<float*>(base_ptr + p.off_ray) + s * 16;
+                        if (lane == 0) {
+                            scr[quad * 4 + 0] = cr;
+                            scr[quad * 4 + 1] = cg;
+                            scr[quad * 4 + 2] = cb;
+                            scr[quad * 4 + 3] = tau_q;
+                            mbar_arrive(bar(kBarComp + s));
+                        }
+                        if (quad == 0) {
+                            // the 4 partials of this ray, chained front to back
+                            bool got = true;
+                            if (lane == 0) {
+                                got = mbar_wait(bar(kBarComp + s), comp_ph, abort, &g_status, kStatusTimeoutOther);
+                                if (got) {
+                                    float rr = 0.0f, gg = 0.0f, bb = 0.0f, tsum = 0.0f;
+#pragma unroll
+                                    for (int q = 0; q < 4; ++q) {
+                                        const float tr = expf(-tsum);
+                                        rr += tr * scr[q * 4 + 0];
+                                        gg += tr * scr[q * 4 + 1];
+                                        bb += tr * scr[q * 4 + 2];
+                                        tsum += scr[q * 4 + 3];
+                                    }
+                                    reinterpret_cast<float4*>(p.ray.rgba)[pix] = make_float4(rr, gg, bb, -expm1f(-tsum));
+                                }
+                            }
+                            comp_ph ^= 1u;
+                            if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) ok = false;
+                        }
+                    }
+                } else {
+                    const long long grow = static_cast<long long>(t) * kTileM + row;
+                    float* yrow = p.y + grow * p.out_dim;
+                    for (uint32_t c = sub; c < nch; c += kGroupsPerSlot) {
+                        uint32_t v0[16];
+                        tmem_ld16(t_col + c * 16, v0);
+                        tmem_wait_ld();
+                        add_bias16(v0, bias_l + c * 16);
+                        if (grow < p.n_rows) {
+                            float o[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float a = __uint_as_float(v0[i]);
+                                o[i] = relu ? fmaxf(a, 0.0f) : a;
+                            }
+                            const int col0 = c * 16;
+                            if (p.y_vec4 && col0 + 16 <= p.out_dim) {
+                                float4* dst = reinterpret_cast<float4*>(yrow + col0);
+                                dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+                                dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+                                dst[2] = make_float4(o[8], o[9], o[10], o[11]);
+                                dst[3] = make_float4(o[12], o[13], o[14], o[15]);
+                            } else {
+#pragma unroll
+                                for (int i = 0; i < 16; ++i)
+                                    if (col0 + i < p.out_dim) yrow[col0 + i] = o[i];
+                            }
+                        }
+                    }
+                }
+                // activations written (or, after the last layer, the
+                // accumulator read): the slot's next MMA may proceed
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarAFull + s));
             }
         }
     }
@@ -697,61 +716,61 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
 
 // Packs fp32 [N, K] row-major weights (PyTorch nn.Linear layout) and fp32
 // biases of every layer into the image the kernel copies straight into
-// shared memory: per layer, the K-major SW128 weight block (zero padded to
-// n_pad x katoms*64) followed by the bias block (n_pad rows x 16 K columns,
-// unswizzled core matrices: column 0 = hi part, column 1 = lo part).
+// shared memory: per layer the K-major SW128 weight block (zero padded to
+// n_pad x katoms*64, float16 or bfloat16), then one block holding every
+// layer's fp32 bias zero padded to n_pad.
 struct PackLayer {
     const float* W;
     const float* b;
-    uint32_t K, N, n_pad, katoms, w_off, bias_off;
+    uint32_t K, N, n_pad, katoms, w_off, b_idx;
 };
 struct PackParams {
     PackLayer layer[kMaxLayers];
     int n_layers;
     int bf16;
     uint8_t* wpack;
-    uint32_t total_chunks;  // sum over layers of n_pad * (katoms * 8 + 2) 16-byte chunks
+    uint32_t bias_gofs;     // byte offset of the bias block
+    uint32_t w_chunks;      // 16-byte weight chunks of all layers
+    uint32_t total_chunks;  // + 4-float bias chunks
 };
 
 __global__ void mlp_pack_kernel(const __grid_constant__ PackParams p) {
     for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < p.total_chunks; g += gridDim.x * blockDim.x) {
+        if (g >= p.w_chunks) {
+            // bias chunk: 4 consecutive entries of the padded bias block
+            const uint32_t e0 = (g - p.w_chunks) * 4;
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t e = e0 + k;
+                int l = 0;
+                while (l + 1 < p.n_layers && e >= p.layer[l + 1].b_idx) ++l;
+                const uint32_t n = e - p.layer[l].b_idx;
+                v[k] = (n < p.layer[l].N) ? p.layer[l].b[n] : 0.0f;
+            }
+            *reinterpret_cast<float4*>(p.wpack + p.bias_gofs + e0 * 4) = make_float4(v[0], v[1], v[2], v[3]);
+            continue;
+        }
         uint32_t rem = g;
         int l = 0;
         for (; l < p.n_layers; ++l) {
-            const uint32_t nc = p.layer[l].n_pad * (p.layer[l].katoms * 8 + 2);
+            const uint32_t nc = p.layer[l].n_pad * p.layer[l].katoms * 8;
             if (rem < nc) break;
             rem -= nc;
         }
         const PackLayer& L = p.layer[l];
-        const uint32_t chunks_per_row = L.katoms * 8 + 2;
+        const uint32_t chunks_per_row = L.katoms * 8;
         const uint32_t n = rem / chunks_per_row;
         const uint32_t kc = rem - n * chunks_per_row;
-        uint32_t w[4] = {0u, 0u, 0u, 0u};
-        uint8_t* dst;
-        if (kc < L.katoms * 8) {
+        uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-                const uint32_t k0 = kc * 8 + e;
-                const float v0 = (n < L.N && k0 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0] : 0.0f;
-                const float v1 = (n < L.N && k0 + 1 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0 + 1] : 0.0f;
-                w[e >> 1] = p.bf16 ? pack_bf16x2(v0, v1) : pack_f16x2(v0, v1);
-            }
-            dst = p.wpack + L.w_off + sw128_offset(n, kc * 8, L.n_pad);
-        } else {
-            const uint32_t half = kc - L.katoms * 8;  // K columns 0-7 or 8-15 of the bias block
-            if (half == 0) {
-                const float b = (n < L.N) ? L.b[n] : 0.0f;
-                if (p.bf16) {
-                    const float hi = __bfloat162float(__float2bfloat16_rn(b));
-                    w[0] = pack_bf16x2(hi, b - hi);
-                } else {
-                    const float hi = __half2float(__float2half_rn(b));
-                    w[0] = pack_f16x2(hi, b - hi);
-                }
-            }
-            dst = p.wpack + L.w_off + L.bias_off + k16_plain_offset(n, half * 8);
+        for (int e = 0; e < 8; e += 2) {
+            const uint32_t k0 = kc * 8 + e;
+            const float v0 = (n < L.N && k0 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0] : 0.0f;
+            const float v1 = (n < L.N && k0 + 1 < L.K) ? L.W[static_cast<size_t>(n) * L.K + k0 + 1] : 0.0f;
+            w[e >> 1] = p.bf16 ? pack_bf16x2(v0, v1) : pack_f16x2(v0, v1);
         }
-        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(p.wpack + L.w_off + sw128_offset(n, kc * 8, L.n_pad)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 

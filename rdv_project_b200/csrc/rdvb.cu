@@ -84,33 +84,37 @@ struct PackLayout {
     bool ok = false;
     uint32_t k_pad[rdvb::mlp_tc::kMaxLayers], n_pad[rdvb::mlp_tc::kMaxLayers];
     uint32_t w_off[rdvb::mlp_tc::kMaxLayers], w_bytes[rdvb::mlp_tc::kMaxLayers];
-    uint32_t bias_off[rdvb::mlp_tc::kMaxLayers];
+    uint32_t b_idx[rdvb::mlp_tc::kMaxLayers];
     uint32_t total_w = 0;  // bytes of all layer blocks
     uint32_t max_w_bytes = 0;
+    uint32_t bias_gofs = 0, bias_bytes = 0;
     int64_t total_bytes = 0;
 };
 
-// Per layer: the K-major SW128 weight block (n_pad rows x katoms*128 bytes)
-// followed by the bias block (n_pad rows x 32 bytes), padded to 1 KB so the
-// next layer block stays 1 KB aligned.
+// Per layer the K-major SW128 weight block (n_pad rows x katoms*128 bytes, a
+// 1 KB multiple since n_pad is a multiple of 16), then one fp32 bias block
+// for all layers (n_pad entries each).
 PackLayout pack_layout(int n_layers, const int* dims) {
     PackLayout L;
     if (n_layers < 1 || n_layers > rdvb::mlp_tc::kMaxLayers || dims == nullptr) return L;
     for (int l = 0; l <= n_layers; ++l)
         if (dims[l] < 1 || dims[l] > static_cast<int>(rdvb::mlp_tc::kMaxWidth)) return L;
-    uint32_t w = 0;
+    uint32_t w = 0, nb = 0;
     for (int l = 0; l < n_layers; ++l) {
         L.k_pad[l] = round_up(dims[l], 16);
         L.n_pad[l] = round_up(dims[l + 1], 16);
         const uint32_t katoms = (L.k_pad[l] + 63) / 64;
         L.w_off[l] = w;
-        L.bias_off[l] = L.n_pad[l] * katoms * 128u;
-        L.w_bytes[l] = round_up(L.bias_off[l] + L.n_pad[l] * 32u, 1024);
+        L.w_bytes[l] = round_up(L.n_pad[l] * katoms * 128u, 1024);
+        L.b_idx[l] = nb;
+        nb += L.n_pad[l];
         w += L.w_bytes[l];
         L.max_w_bytes = std::max(L.max_w_bytes, L.w_bytes[l]);
     }
     L.total_w = w;
-    L.total_bytes = w;
+    L.bias_gofs = w;
+    L.bias_bytes = round_up(nb * 4u, 16);
+    L.total_bytes = static_cast<int64_t>(w) + L.bias_bytes;
     L.ok = true;
     return L;
 }
@@ -162,12 +166,14 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     const int bf16 = (math == RDVB_MATH_BF16) ? 1 : 0;
     p.n_layers = n_layers;
     p.w_total_bytes = L.total_w;
+    p.bias_gofs = L.bias_gofs;
+    p.bias_bytes = L.bias_bytes;
     for (int l = 0; l < n_layers; ++l) {
         p.layer[l].k_pad = L.k_pad[l];
         p.layer[l].n_pad = L.n_pad[l];
         p.layer[l].w_off = L.w_off[l];
         p.layer[l].w_bytes = L.w_bytes[l];
-        p.layer[l].bias_off = L.bias_off[l];
+        p.layer[l].b_idx = L.b_idx[l];
         p.layer[l].idesc = rdvb::umma_idesc_f16(L.n_pad[l], bf16);
         p.layer[l].relu = (flags[l] & RDVB_LAYER_RELU) ? 1u : 0u;
     }
@@ -197,9 +203,8 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
         q.off_w = slots * q.a0_bytes;
         auto place = [&](uint32_t wsize) -> uint32_t {
             q.off_x = q.off_w + wsize;
-            q.off_ones = q.off_x + slots * q.x_stage_bytes;  // 1 KB multiple: x stages are 128 B multiples
-            q.off_ones = round_up(q.off_ones, 1024);
-            q.off_bar = q.off_ones + kOnesBytes;
+            q.off_bias = round_up(q.off_x + slots * q.x_stage_bytes, 16);
+            q.off_bar = round_up(q.off_bias + q.bias_bytes, 16);
             q.off_ray = round_up(q.off_bar + kBarBlockBytes, 16);
             return q.off_ray + kRayScratchBytes + 1024u;
         };
@@ -226,7 +231,7 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     uint32_t smem = 0;
     int forced = 0;
     if (const char* env = getenv("RDVB_MLP_SLOTS")) forced = atoi(env);
-    for (int sl = kMaxSlots; sl >= 2; --sl) {
+    for (int sl = kMaxSlots; sl >= 2; sl /= 2) {  // 4 or 2: the epilogue splits its warp groups evenly
         if (forced && sl != forced) continue;
         Params q = p;
         const uint32_t need = plan(sl, q);
@@ -259,11 +264,9 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     };
     if (ray) {
         if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1, true>, 4) : go(mlp_tc_kernel<4, 0, true>, 4);
-        else if (slots == 3) bf16 ? go(mlp_tc_kernel<3, 1, true>, 3) : go(mlp_tc_kernel<3, 0, true>, 3);
         else bf16 ? go(mlp_tc_kernel<2, 1, true>, 2) : go(mlp_tc_kernel<2, 0, true>, 2);
     } else {
         if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1, false>, 4) : go(mlp_tc_kernel<4, 0, false>, 4);
-        else if (slots == 3) bf16 ? go(mlp_tc_kernel<3, 1, false>, 3) : go(mlp_tc_kernel<3, 0, false>, 3);
         else bf16 ? go(mlp_tc_kernel<2, 1, false>, 2) : go(mlp_tc_kernel<2, 0, false>, 2);
     }
     if (rc) return rc;
@@ -373,10 +376,12 @@ int rdvb_mlp_pack(int n_layers, const int* dims, const float* const* weights, co
         pl.n_pad = L.n_pad[l];
         pl.katoms = (L.k_pad[l] + 63) / 64;
         pl.w_off = L.w_off[l];
-        pl.bias_off = L.bias_off[l];
-        chunks += pl.n_pad * (pl.katoms * 8 + 2);
+        pl.b_idx = L.b_idx[l];
+        chunks += pl.n_pad * pl.katoms * 8;
     }
-    pp.total_chunks = chunks;
+    pp.bias_gofs = L.bias_gofs;
+    pp.w_chunks = chunks;
+    pp.total_chunks = chunks + L.bias_bytes / 16;
     const int threads = 256;
     const int blocks = std::min<int>((chunks + threads - 1) / threads, dev->sm_count * 8);
     mlp_pack_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(pp);
