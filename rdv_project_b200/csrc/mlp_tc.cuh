@@ -11,7 +11,7 @@
 // convert -> TMEM store): the single MMA-issuing thread is the kernel's
 // serial resource, so it issues only the K steps.
 //
-// Design (one persistent CTA per SM, 19 warps):
+// Design (one persistent CTA per SM, 20 warps):
 //   warps 0-15 epilogue. Warp w owns TMEM lane quadrant (w % 4) -- rows
 //              32*(w%4) .. +31 of every tile. Warp group g = w / 4 owns slot
 //              g % SLOTS and, of that slot's 16-column chunks, every
@@ -26,7 +26,8 @@
 //   warp 16    producer: 1-D bulk (TMA) copies of input tiles and of the
 //              pre-swizzled weight blocks (resident, or streamed per layer
 //              through a ring), issued from one event loop.
-//   warp 17    MMA issuer: allocates TMEM; one thread issues tcgen05.mma
+//   warps 17, 19  MMA issuers (even / odd slots; warp 17 allocates TMEM):
+//              one thread each issues tcgen05.mma
 //              (M=128, N=layer width, K=16 steps) per layer -- A from shared
 //              memory for the first layer, from TMEM after -- and commits
 //              completion to mbarriers.
@@ -48,9 +49,14 @@ constexpr int kTileM = 128;
 constexpr int kMaxSlots = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kProducerWarp = 16;
-constexpr int kMmaWarp = 17;
+constexpr int kMmaWarp = 17;        // issues the MMAs of the even slots; allocates TMEM
+constexpr int kMmaWarp2 = 19;       // issues the MMAs of the odd slots
+constexpr int kMaxIssuers = 2;
+// CTA size for ISSUERS MMA-issuing warps: 16 epilogue + producer + MMA +
+// staging (+ the second issuer). Streamed-weight chains run 19 warps, which
+// leaves their register-heavy epilogue the larger budget.
+__host__ __device__ constexpr int cta_threads(int issuers) { return (18 + issuers) * 32; }
 constexpr int kStageWarp = 18;
-constexpr int kThreads = 19 * 32;
 constexpr uint32_t kAtomBytes = kTileM * 128;      // one 64-wide K atom of a 128-row tile
 constexpr int kMaxWStages = 4;
 constexpr uint32_t kMaxWidth = 128;
@@ -116,8 +122,8 @@ enum : int {
     kBarAccFull = kBarAFull + kMaxSlots,       // accumulator ready
     kBarWFull = kBarAccFull + kMaxSlots,
     kBarWEmpty = kBarWFull + kMaxWStages,
-    kBarDrain = kBarWEmpty + kMaxWStages,
-    kBarComp = kBarDrain + 1,                  // ray mode: per slot, 4 quadrant partials written
+    kBarDrain = kBarWEmpty + kMaxWStages,      // + issuer
+    kBarComp = kBarDrain + kMaxIssuers,        // ray mode: per slot, 4 quadrant partials written
     kBarBias = kBarComp + 4,                   // fp32 biases landed (TMA tx)
     kNumBars = kBarBias + 1,
 };
@@ -218,8 +224,8 @@ __device__ __forceinline__ bool ray_setup(const RayParams& rp, int pix, float (&
 __device__ __forceinline__ float softplus_f(float v) { return fmaxf(v, 0.0f) + log1pf(expf(-fabsf(v))); }
 __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-template <int SLOTS, int BF16, bool RAY>
-__global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_constant__ Params p) {
+template <int SLOTS, int BF16, bool RAY, int ISSUERS>
+__global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const __grid_constant__ Params p) {
     static_assert(SLOTS == 2 || SLOTS == 4, "the epilogue splits 4 warp groups evenly over the slots");
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the SW128 atoms.
@@ -249,16 +255,16 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
         }
         for (int q = 0; q < kMaxWStages; ++q) {
             mbar_init(bar(kBarWFull + q), 1);
-            mbar_init(bar(kBarWEmpty + q), 1);
+            mbar_init(bar(kBarWEmpty + q), 1);  // streamed weights: a single issuer
         }
-        mbar_init(bar(kBarDrain), 1);
+        for (int i = 0; i < kMaxIssuers; ++i) mbar_init(bar(kBarDrain + i), 1);
         for (int g = 0; g < 4; ++g) mbar_init(bar(kBarComp + g), 4);
         mbar_init(bar(kBarBias), 1);
         *abort = 0u;
         fence_mbarrier_init();
     }
     // Layer-0 A tiles start zeroed: chunks past the input width stay zero.
-    for (uint32_t i = threadIdx.x; i < SLOTS * p.a0_bytes / 16; i += kThreads) st_shared_v4(a_base + i * 16, 0u, 0u, 0u, 0u);
+    for (uint32_t i = threadIdx.x; i < SLOTS * p.a0_bytes / 16; i += cta_threads(ISSUERS)) st_shared_v4(a_base + i * 16, 0u, 0u, 0u, 0u);
     fence_proxy_async_smem();
     if (warp == kMmaWarp) {
         tmem_alloc(smem_addr(tmem_slot), kTmemCols);
@@ -447,7 +453,14 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                 }
             }
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == kMmaWarp || (ISSUERS > 1 && warp == kMmaWarp2)) {
+        // With resident weights the slots are independent and two issuing
+        // threads split them by parity (a slot-layer's wait, K-step MMAs and
+        // commits are a few hundred cycles of one thread's time, so this
+        // halves the serial issue path). Streamed weights keep one issuer,
+        // whose in-order walk over the slots releases each ring block.
+        const int mi = warp == kMmaWarp ? 0 : 1;
+        constexpr int n_iss = ISSUERS;  // the host launches 2 only with resident weights
         if (lane == 0) {
             uint32_t aph = 0u, a0ph = 0u;  // per-slot parities of the next a_full / a0_full phase
             uint32_t q = 0, wph = 0;       // weight ring slot and its phase
@@ -486,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                     for (int j = 0; j < 8; ++j) b_desc[j] = b0 + (j >> 2) * n8 + (j & 3) * 2;
 #pragma unroll
                     for (int s = 0; s < SLOTS; ++s) {
+                        if (s % n_iss != mi) continue;
                         if (tile_of<SLOTS>(r, s, n_tiles) < 0) break;
                         if (l == 0) {
                             if (!mbar_wait(bar(kBarA0Full + s), (a0ph >> s) & 1u, abort, &g_status,
@@ -535,8 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_tc_kernel(const __grid_consta
                 }
             }
             if (!ok && issued) {
-                umma_commit(bar(kBarDrain));
-                drain_wait(bar(kBarDrain), 0u);
+                umma_commit(bar(kBarDrain + mi));
+                drain_wait(bar(kBarDrain + mi), 0u);
             }
         }
     } else {

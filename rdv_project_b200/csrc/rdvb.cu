@@ -45,7 +45,7 @@ struct DeviceInfo {
     bool init = false;
     int sm_count = 0;
     int max_smem_optin = 0;
-    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2][2] = {};  // [slots][bf16][ray]
+    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2][2][3] = {};  // [slots][bf16][ray][issuers]
     size_t simt_smem_set = 0;
     size_t wino_smem_set[2] = {};
 };
@@ -246,29 +246,35 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
 
     int rc = RDVB_OK;
     const int ri = ray ? 1 : 0;
+    // two MMA-issuing warps when the weights are resident (the slots are then
+    // independent); one in-order issuer for streamed weights
+    const int iss = p.resident ? 2 : 1;
     auto go = [&](auto kernel, int sl) {
-        if (dev->tc_smem_set[sl][bf16][ri] < smem) {
+        if (dev->tc_smem_set[sl][bf16][ri][iss] < smem) {
             cudaError_t e =
                 cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
             if (e != cudaSuccess) {
                 rc = fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(mlp_tc<%d>): %s", sl, cudaGetErrorString(e));
                 return;
             }
-            dev->tc_smem_set[sl][bf16][ri] = smem;
+            dev->tc_smem_set[sl][bf16][ri][iss] = smem;
         }
         // ray mode: the tile count is only known on the device; a CTA with
         // no tile exits after loading the weights
         const int groups = (p.n_tiles + sl - 1) / sl;
         const int grid = ray ? dev->sm_count : std::min(dev->sm_count, groups);
-        kernel<<<grid, kThreads, smem, stream>>>(p);
+        kernel<<<grid, cta_threads(iss), smem, stream>>>(p);
     };
+#define RDVB_GO(S, B, R)                                                         \
+    (iss == 2 ? go(mlp_tc_kernel<S, B, R, 2>, S) : go(mlp_tc_kernel<S, B, R, 1>, S))
     if (ray) {
-        if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1, true>, 4) : go(mlp_tc_kernel<4, 0, true>, 4);
-        else bf16 ? go(mlp_tc_kernel<2, 1, true>, 2) : go(mlp_tc_kernel<2, 0, true>, 2);
+        if (slots == 4) bf16 ? RDVB_GO(4, 1, true) : RDVB_GO(4, 0, true);
+        else bf16 ? RDVB_GO(2, 1, true) : RDVB_GO(2, 0, true);
     } else {
-        if (slots == 4) bf16 ? go(mlp_tc_kernel<4, 1, false>, 4) : go(mlp_tc_kernel<4, 0, false>, 4);
-        else bf16 ? go(mlp_tc_kernel<2, 1, false>, 2) : go(mlp_tc_kernel<2, 0, false>, 2);
+        if (slots == 4) bf16 ? RDVB_GO(4, 1, false) : RDVB_GO(4, 0, false);
+        else bf16 ? RDVB_GO(2, 1, false) : RDVB_GO(2, 0, false);
     }
+#undef RDVB_GO
     if (rc) return rc;
     *taken = true;
     return check_launch("mlp_tc_kernel");
