@@ -59,8 +59,9 @@ int64_t rdvb_launch_count(void);
 const char* rdvb_last_error(void);
 
 /* Synchronizes the current device, then reads (and, if `clear`, resets) the
- * device status word that kernels set when a bounded wait expires. Returns
- * RDVB_OK and writes the word to *status (0 = healthy). */
+ * device status word that kernels set when a bounded wait expires, and writes
+ * it to *status. Returns RDVB_OK when the word is 0, RDVB_ERR_DEVICE_STATUS
+ * when it is not. */
 int rdvb_device_status(int clear, uint32_t* status);
 
 /* ---------------------------------------------------------------- MLP ----

@@ -84,9 +84,16 @@ def check(rc: int, what: str) -> None:
         raise RdvbError(f"{what} failed ({rc}): {last_error()}")
 
 
+RDVB_ERR_DEVICE_STATUS = -4
+
+
 def device_status(clear: bool = True) -> int:
+    """Synchronizes the device and returns the bounded-wait status word
+    (0 = healthy; bits name the wait that expired)."""
     v = _c_u32(0)
-    check(lib().rdvb_device_status(1 if clear else 0, ctypes.byref(v)), "rdvb_device_status")
+    rc = lib().rdvb_device_status(1 if clear else 0, ctypes.byref(v))
+    if rc != RDVB_ERR_DEVICE_STATUS:
+        check(rc, "rdvb_device_status")
     return int(v.value)
 
 

@@ -346,6 +346,7 @@ int rdvb_device_status(int clear, uint32_t* status) {
         if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "clearing the status word: %s", cudaGetErrorString(e));
     }
     if (status) *status = v;
+    if (v) return fail(RDVB_ERR_DEVICE_STATUS, "a kernel's bounded wait expired (status 0x%x)", v);
     return RDVB_OK;
 }
 
