@@ -109,6 +109,24 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
                      const float* const* weights, const float* const* biases, const int* layer_flags,
                      int input_relu, int tail_exact, const void* packed, float* y, void* stream);
 
+/* Allocation-free rdvb_mlp_forward (no reference counterpart: the reference
+ * re-stages weights inside every dispatch). Same arguments minus `packed`:
+ * the packed weight image is written into a static device array of
+ * rdvb_mlp_static_capacity() bytes (256 KiB) owned by the library, so the
+ * call allocates nothing. It is for callers that cannot allocate device
+ * memory (hosts driving the C ABI over buffers they do not own, loops that
+ * forbid allocation between calls). Chains whose packed image exceeds the
+ * capacity return RDVB_ERR_UNSUPPORTED. Nothing needs to start zeroed: each
+ * call rewrites every byte the kernel reads. The array is shared by all
+ * callers on a device: two calls whose work overlaps on the device (other
+ * streams, other threads) race on it, so order them (one stream, or events).
+ * The array's address is looked up (cudaGetSymbolAddress) on the first call
+ * on each device; make that first call before any stream capture. */
+int64_t rdvb_mlp_static_capacity(void);
+int rdvb_mlp_forward_static(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
+                            const float* const* weights, const float* const* biases, const int* layer_flags,
+                            int input_relu, int tail_exact, float* y, void* stream);
+
 /* y = max(x, 0) over n floats. Replaces ReLUTensorOp
  * (rdv/domain/nn.py:362-374, rdv/shaders/tensors/relu_tensor_op.h). */
 int rdvb_relu(const float* x, float* y, int64_t n, void* stream);

@@ -32,6 +32,8 @@ SIGNATURES = {
     "rdvb_mlp_packed_bytes": (_c_i64, [_c_int, _vp]),
     "rdvb_mlp_pack": (_c_int, [_c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),
     "rdvb_mlp_forward": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp]),
+    "rdvb_mlp_static_capacity": (_c_i64, []),
+    "rdvb_mlp_forward_static": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp]),
     "rdvb_relu": (_c_int, [_vp, _vp, _c_i64, _vp]),
     "rdvb_winograd_packed_bytes": (_c_i64, [_c_int, _c_int, _c_int]),
     "rdvb_winograd_filter_transform": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp]),

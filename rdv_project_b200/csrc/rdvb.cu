@@ -703,3 +703,73 @@ int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, f
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------- allocation-free MLP
+// A variant of rdvb_mlp_forward for callers that cannot allocate device
+// memory for the packed weight image: hosts that drive the library through
+// the C ABI from memory they do not own (a foreign runtime's buffers, an
+// embedding with no CUDA allocator of its own), or a hot loop whose caller
+// forbids allocation between calls. The image lives in a file-scope static
+// device array instead.
+namespace {
+
+constexpr size_t kStaticPackBytes = 256 * 1024;  // holds chains up to ~256 KB of packed weights + biases
+__device__ __align__(256) uint8_t g_static_pack[kStaticPackBytes];
+
+void* g_static_pack_ptr[kMaxDevices] = {};
+std::mutex g_static_pack_mutex;
+
+// Address of g_static_pack on the current device, looked up once per device
+// (with that device current).
+int static_pack_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(RDVB_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_static_pack_mutex);
+    if (!g_static_pack_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_static_pack);
+        if (e != cudaSuccess)
+            return fail(RDVB_ERR_CUDA, "cudaGetSymbolAddress(static pack): %s", cudaGetErrorString(e));
+        g_static_pack_ptr[dev] = p;
+    }
+    *out = g_static_pack_ptr[dev];
+    return RDVB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t rdvb_mlp_static_capacity(void) { return static_cast<int64_t>(kStaticPackBytes); }
+
+int rdvb_mlp_forward_static(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
+                            const float* const* weights, const float* const* biases, const int* layer_flags,
+                            int input_relu, int tail_exact, float* y, void* stream) {
+    if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
+    const int math = layer_flags[0] & 3;
+    bool uniform = true;
+    for (int l = 1; l < n_layers; ++l) uniform &= (layer_flags[l] & 3) == math;
+    void* packed = nullptr;
+    // a packed image is used only by chains the tensor-core kernel takes:
+    // every layer float16 or every layer bfloat16, widths <= 128
+    if (uniform && math != RDVB_MATH_F32 && n_rows >= 32) {
+        const int64_t need = rdvb_mlp_packed_bytes(n_layers, dims);
+        if (need > 0) {
+            if (need > static_cast<int64_t>(kStaticPackBytes))
+                return fail(RDVB_ERR_UNSUPPORTED,
+                            "packed weights need %lld bytes; rdvb_mlp_forward_static holds at most %lld "
+                            "(use rdvb_mlp_pack + rdvb_mlp_forward with a caller buffer)",
+                            (long long)need, (long long)kStaticPackBytes);
+            if (int rc = static_pack_address(&packed)) return rc;
+            if (int rc = rdvb_mlp_pack(n_layers, dims, weights, biases,
+                                       math == RDVB_MATH_BF16 ? RDVB_BF16 : RDVB_F16, packed, stream))
+                return rc;
+        }
+    }
+    return rdvb_mlp_forward(x, x_dtype, n_rows, n_layers, dims, weights, biases, layer_flags, input_relu, tail_exact,
+                            packed, y, stream);
+}
+
+}  // extern "C"
