@@ -325,11 +325,13 @@ def run_ours(args, spec, world, rank, local):
 
     # ---- device-timed region ----
     sampler = ClockSampler(local) if rank == 0 else None
-    barrier(world)
-    torch.cuda.synchronize()
+    # the sampler starts (and warms up) before the barrier, so every rank
+    # enters the timed loop together
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
     launches0 = N.launch_count()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
@@ -465,12 +467,14 @@ def run_c3(args, world, rank, local, summary=False):
         r = ref.double()
         parity = ((d.max() / r.abs().max()).item(), (d / (r.abs() + r.pow(2).mean().sqrt())).max().item())
     sampler = ClockSampler(local) if (rank == 0 and not summary) else None
-    barrier(world)
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
     l0 = N.launch_count()
     t_kernel = time_steps(lambda: conv(x, out=y), steps, flush)
+    barrier(world)  # ranks enter the collective loop together
     t_step = time_steps(step, steps, flush)
     launches = N.launch_count() - l0
     clocks = sampler.stop() if sampler else None
@@ -586,12 +590,14 @@ def run_c4(args, world, rank, local, summary=False):
         from oracle import mlp as omlp
         parity = omlp.rel_errors(got, ref)
     sampler = ClockSampler(local) if (rank == 0 and not summary) else None
-    barrier(world)
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
     l0 = N.launch_count()
     t_kernel = time_steps(render, steps)
+    barrier(world)  # ranks enter the collective loop together
     t_step = time_steps(step, steps)
     launches = N.launch_count() - l0
     clocks = sampler.stop() if sampler else None
