@@ -540,7 +540,7 @@ int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int c
     p.tiles_w = static_cast<int>(tiles_w);
     p.tiles_per_img = static_cast<int>(tiles_w * tiles_h);
     p.n_tiles = static_cast<int>(n_tiles);
-    p.n_blocks = static_cast<int>((n_tiles + kTileM - 1) / kTileM);
+    p.n_blocks = static_cast<int>((n_tiles + kBlockTiles - 1) / kBlockTiles);
     p.u_bytes = static_cast<uint32_t>(rdvb_winograd_packed_bytes(variant, cin, cout));
     p.off_a = round_up(p.u_bytes, 1024);
     p.off_bar = p.off_a + 4 * kATileBytes;

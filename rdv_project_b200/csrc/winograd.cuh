@@ -22,19 +22,20 @@
 // Design (one persistent CTA per SM, 16 warps):
 //   * U for all 16 positions stays resident in shared memory (K-major,
 //     128-byte swizzle), loaded once by one bulk copy.
-//   * A CTA walks blocks of 128 Winograd tiles (raster order over
+//   * A CTA walks blocks of 120 Winograd tiles (raster order over
 //     (image, tile row, tile column)), each block as 4 "rows" u of the 4x4
-//     transform domain. For a row, every thread loads its two (tile,
-//     8-channel chunk) items' input (16 x 16-byte loads in flight), forms the
-//     first (row) pass of B^T d B, then for v = 0..3 waits until the GEMMs of
-//     the previous row released V tile v, writes V_uv (float16) and arrives;
-//     thread 0 issues position (u, v)'s GEMMs as soon as all warps arrived.
-//     So the transform of row r + 1 overlaps the GEMMs of row r, position by
-//     position.
+//     transform domain. Warps 0-14 (480 threads, two (tile, 8-channel)
+//     items each) load a row's input (16 x 16-byte loads in flight), form
+//     the first (row) pass of B^T d B, then for v = 0..3 wait until the
+//     GEMMs of the previous row released V tile v, write V_uv (float16) and
+//     arrive. Warp 15 only issues: once all 15 warps wrote V tile v it issues
+//     position (u, v)'s GEMMs (M = 128; V rows 120-127 are not used), so the
+//     transform of row r + 1 overlaps the GEMMs of row r, position by position.
 //   * TMEM: the 4 accumulators (i, j) of a block, COUT columns each, double
 //     buffered across blocks (512 columns). After a block's last GEMM, warp w
-//     reads tiles 32*(w%4)..+31 (its lane quadrant) x channels 16*(w/4)..+15,
-//     adds the bias and stores, while the next block's GEMMs run.
+//     of 0-14 reads lane quadrant w%4 x channels 16*(w/4)..+15 (warp 3 also
+//     channels 48-63 of quadrant 3), adds the bias and stores, while the
+//     next block's GEMMs run.
 // HBM traffic is the input read (halo re-reads hit L1/L2) plus the output
 // write, the operator's roofline.
 #pragma once
@@ -43,7 +44,11 @@
 namespace rdvb {
 namespace wino {
 
-constexpr int kTileM = 128;         // Winograd tiles per block (GEMM M)
+constexpr int kTileM = 128;         // GEMM M: rows of a V tile and TMEM lanes
+constexpr int kBlockTiles = 120;    // Winograd tiles per block (V rows 120-127 are unused)
+constexpr int kXWarps = 15;         // transform + epilogue warps: 480 threads x 2 items = 120 tiles x 8 chunks
+constexpr int kXThreads = kXWarps * 32;
+constexpr int kIssueWarp = 15;      // the MMA-issuing warp
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxChannels = 64;    // CIN, COUT: multiples of 16, at most 64
@@ -101,10 +106,10 @@ __device__ __forceinline__ bool make_item(const Params& p, int blk, int idx, Ite
     it.cmask = 0;
     it.e0 = 0;
     it.soff = 0;
-    if (idx >= kTileM * cch) return false;
+    if (idx >= kBlockTiles * cch) return false;
     const int tr = idx / cch, ck = idx - tr * cch;
     it.soff = sw128_offset(static_cast<uint32_t>(tr), static_cast<uint32_t>(ck * 8), kTileM);
-    const int t = blk * kTileM + tr;
+    const int t = blk * kBlockTiles + tr;
     if (t < p.n_tiles) {
         const int img = t / p.tiles_per_img;
         const int rem = t - img * p.tiles_per_img;
@@ -285,36 +290,14 @@ struct RowCtx {
     Item it[2];
     bool has[2];
     long long row_stride;
-    uint32_t a_base, bar_base, d_base, ksteps, idesc;
-    uint64_t a_desc0, u_desc0, u_pos;
-    int r, u, bl, lane;
-    bool issuer;
+    uint32_t a_base, bar_base;
+    int r, u, lane;
     volatile uint32_t* abort;
     __device__ __forceinline__ uint32_t bar(int i) const { return bar_base + 8u * static_cast<uint32_t>(i); }
 };
 
-// Thread 0: once every warp has written V tile v of the current row, issue
-// position (u, v)'s GEMMs and commit the tile's release (and, after the
-// block's last position, the accumulators). One shared copy of this code,
-// so the issuing thread's instructions stay cached.
-__device__ __noinline__ bool issue_after_full(uint32_t bar_base, volatile uint32_t* abort, int r, int u, int v,
-                                              int bl, uint32_t d_base, uint64_t a_desc0, uint64_t u_desc0,
-                                              uint64_t u_pos, uint32_t idesc, uint32_t ksteps) {
-    auto bar = [&](int i) { return bar_base + 8u * static_cast<uint32_t>(i); };
-    bool ok = true;
-    if (r == 0 && v == 0) ok = mbar_wait(bar(kBarUFull), 0u, abort, &g_status, kStatusTimeoutWFull);
-    if (ok) ok = mbar_wait(bar(kBarAFull + v), r & 1, abort, &g_status, kStatusTimeoutAFull);
-    if (!ok) return false;
-    tc_fence_after();
-    issue_position(u, v, d_base, a_desc0 + static_cast<uint64_t>(v) * (kATileBytes >> 4),
-                   u_desc0 + static_cast<uint64_t>(u * 4 + v) * u_pos, idesc, ksteps);
-    umma_commit(bar(kBarAEmpty + v));
-    if (u == 3 && v == 3) umma_commit(bar(kBarDFull + (bl & 1)));
-    return true;
-}
-
-// Domain column V of the current row: wait until V tile V is free, write
-// it, and let thread 0 issue its GEMMs.
+// Domain column V of the current row: wait until the GEMMs of the previous
+// row released V tile V, write it (float16), signal the issuing warp.
 template <int V>
 __device__ __forceinline__ bool do_position(const RowCtx& c, const float (&m)[2][4][8]) {
     if (!mbar_wait_warp(c.bar(kBarAEmpty + V), (c.r & 1) ^ 1, c.abort, &g_status, kStatusTimeoutXEmpty))
@@ -324,11 +307,7 @@ __device__ __forceinline__ bool do_position(const RowCtx& c, const float (&m)[2]
     fence_proxy_async_smem();
     __syncwarp();
     if (c.lane == 0) mbar_arrive(c.bar(kBarAFull + V));
-    bool ok = true;
-    if (c.issuer)
-        ok = issue_after_full(c.bar_base, c.abort, c.r, c.u, V, c.bl, c.d_base, c.a_desc0, c.u_desc0, c.u_pos, c.idesc,
-                              c.ksteps);
-    return __all_sync(0xffffffffu, ok);
+    return true;
 }
 
 template <bool X16>
@@ -354,11 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_kernel(const __grid_
 
     const int warp = threadIdx.x >> 5;
     c.lane = threadIdx.x & 31;
-    c.issuer = threadIdx.x == 0;
     if (threadIdx.x == 0) {
         mbar_init(c.bar(kBarUFull), 1);
         for (int v = 0; v < 4; ++v) {
-            mbar_init(c.bar(kBarAFull + v), kWarps);
+            mbar_init(c.bar(kBarAFull + v), kXWarps);
             mbar_init(c.bar(kBarAEmpty + v), 1);
         }
         mbar_init(c.bar(kBarDFull), 1);
@@ -375,69 +353,93 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_kernel(const __grid_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    if (c.issuer) {
-        mbar_arrive_expect_tx(c.bar(kBarUFull), p.u_bytes);
-        bulk_g2s(u_base, p.u_pack, p.u_bytes, c.bar(kBarUFull));
-    }
     // blocks blockIdx.x, blockIdx.x + gridDim.x, ...; 4 domain rows each
     const int n_mine = blockIdx.x < p.n_blocks ? (p.n_blocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int rows = 4 * n_mine;
-
-    const int quad = warp & 3;
-    const int grp = warp >> 2;
-    const bool has_cols = 16 * grp < p.cout;
-    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + 16u * grp;
-    c.row_stride = static_cast<long long>(p.w) * p.cin;
-    c.a_desc0 = umma_desc_sw128(c.a_base);
-    c.u_desc0 = umma_desc_sw128(u_base);
-    c.ksteps = static_cast<uint32_t>(p.cin) >> 4;
-    c.u_pos = static_cast<uint64_t>(p.cout) * 8u;  // one position of U, in 16-byte units
-    c.idesc = p.idesc;
-
-    // a finished block's accumulators: + bias, to the output
-    auto epilogue = [&](int bl) -> bool {
-        const uint32_t half = bl & 1;
-        if (!mbar_wait_warp(c.bar(kBarDFull + half), (bl >> 1) & 1, c.abort, &g_status, kStatusTimeoutAccFull))
-            return false;
-        tc_fence_after();
-        if (has_cols) {
-            const int t = (blockIdx.x + bl * gridDim.x) * kTileM + quad * 32 + c.lane;
-            store_block(p, t, t < p.n_tiles, grp, t_lane + half * kDCols);
-        }
-        tc_fence_before();
-        return true;
-    };
-
     bool ok = true;
-    for (int r = 0; ok && r < rows; ++r) {
-        const int u = r & 3;
-        c.r = r;
-        c.bl = r >> 2;
-        if (u == 0) {
-            const int blk = blockIdx.x + c.bl * gridDim.x;
-            c.has[0] = make_item(p, blk, threadIdx.x, c.it[0]);
-            c.has[1] = make_item(p, blk, threadIdx.x + kThreads, c.it[1]);
-        }
-        c.d_base = tmem_base + (c.bl & 1) * kDCols;
-        c.u = u;
-        ok = do_row<X16>(c);
-        // the previous block's outputs, while this block's GEMMs run
-        if (ok && u == 0 && c.bl > 0) ok = epilogue(c.bl - 1);
-    }
-    if (ok && rows > 0) ok = epilogue(n_mine - 1);
-    if (!ok) *c.abort = 1u;
 
-    // Let every issued MMA finish before TMEM is released (immediate unless
-    // the CTA aborted with GEMMs in flight).
-    if (c.issuer) {
-        umma_commit(c.bar(kBarDrain));
-        const uint64_t t0 = global_timer_ns();
-        while (!mbar_try_wait_sleep(c.bar(kBarDrain), 0u, 500000u))
-            if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
-                atomicOr(&g_status, kStatusTimeoutDrain);
-                break;
+    if (warp == kIssueWarp) {
+        // ----------------------------------------------------- MMA issuer
+        if (c.lane == 0) {
+            mbar_arrive_expect_tx(c.bar(kBarUFull), p.u_bytes);
+            bulk_g2s(u_base, p.u_pack, p.u_bytes, c.bar(kBarUFull));
+            ok = mbar_wait(c.bar(kBarUFull), 0u, c.abort, &g_status, kStatusTimeoutWFull);
+            const uint64_t u_desc0 = umma_desc_sw128(u_base);
+            const uint64_t u_pos = static_cast<uint64_t>(p.cout) * 8u;  // one position of U, 16-byte units
+            const uint32_t ksteps = static_cast<uint32_t>(p.cin) >> 4;
+            uint64_t a_desc[4];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) a_desc[v] = umma_desc_sw128(c.a_base + v * kATileBytes);
+            for (int r = 0; ok && r < rows; ++r) {
+                const int u = r & 3, bl = r >> 2;
+                const uint32_t d_base = tmem_base + (bl & 1) * kDCols;
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    if (!mbar_wait(c.bar(kBarAFull + v), r & 1, c.abort, &g_status, kStatusTimeoutAFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_position(u, v, d_base, a_desc[v], u_desc0 + static_cast<uint64_t>(u * 4 + v) * u_pos,
+                                   p.idesc, ksteps);
+                    umma_commit(c.bar(kBarAEmpty + v));  // V tile v may be rewritten
+                    if (u == 3 && v == 3) umma_commit(c.bar(kBarDFull + (bl & 1)));
+                }
             }
+            if (!ok) *c.abort = 1u;
+            // every issued MMA completes before TMEM is released
+            umma_commit(c.bar(kBarDrain));
+            const uint64_t t0 = global_timer_ns();
+            while (!mbar_try_wait_sleep(c.bar(kBarDrain), 0u, 500000u))
+                if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
+                    atomicOr(&g_status, kStatusTimeoutDrain);
+                    break;
+                }
+        }
+    } else {
+        // ------------------------------------------- transform + epilogue
+        // Epilogue share: (lane quadrant, 16-channel group) pairs w and, for
+        // warp 3, pair 15 (quadrant 3, channels 48-63).
+        const int quad = warp & 3;
+        const long long blk_tiles = kBlockTiles;
+        c.row_stride = static_cast<long long>(p.w) * p.cin;
+        auto epilogue = [&](int bl) -> bool {
+            const uint32_t half = bl & 1;
+            if (!mbar_wait_warp(c.bar(kBarDFull + half), (bl >> 1) & 1, c.abort, &g_status, kStatusTimeoutAccFull))
+                return false;
+            tc_fence_after();
+            const int row = quad * 32 + c.lane;
+            const int t = static_cast<int>((blockIdx.x + static_cast<long long>(bl) * gridDim.x) * blk_tiles) + row;
+            const bool valid = row < kBlockTiles && t < p.n_tiles;
+            for (int pr = warp; pr < 16; pr += 12) {  // warp 3: pairs 3 and 15
+                const int grp = pr >> 2;
+                if (16 * grp < p.cout)
+                    store_block(p, t, valid, grp,
+                                tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + 16u * grp + half * kDCols);
+                if (warp != 3) break;
+            }
+            tc_fence_before();
+            return true;
+        };
+        const int xt = threadIdx.x;  // 0 .. 479
+        for (int r = 0; ok && r < rows; ++r) {
+            const int u = r & 3;
+            const int bl = r >> 2;
+            c.r = r;
+            c.u = u;
+            if (u == 0) {
+                const int blk = blockIdx.x + bl * gridDim.x;
+                c.has[0] = make_item(p, blk, xt, c.it[0]);
+                c.has[1] = make_item(p, blk, xt + kXThreads, c.it[1]);
+            }
+            ok = do_row<X16>(c);
+            // the previous block's outputs, while this block's GEMMs run
+            if (ok && u == 0 && bl > 0) ok = epilogue(bl - 1);
+        }
+        if (ok && rows > 0) ok = epilogue(n_mine - 1);
+        if (!ok) *c.abort = 1u;
     }
+
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
