@@ -601,7 +601,8 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                         uint32_t v0[16], v1[16];
                         tmem_ld16(t_col + c * 16, v0);
                         if (c2 < nch) tmem_ld16(t_col + c2 * 16, v1);
-                        tmem_wait_ld();
+                        tmem_wait_ld(v0);
+                        reg_barrier(v1);
                         add_bias16(v0, bias_l + c * 16);
                         if (c2 < nch) add_bias16(v1, bias_l + c2 * 16);
                         uint32_t pk[8];
@@ -624,7 +625,7 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                     if (sub == 0) {
                         uint32_t v0[16];
                         tmem_ld16(t_col, v0);
-                        tmem_wait_ld();
+                        tmem_wait_ld(v0);
                         add_bias16(v0, bias_l);
                         const int pix = __ldg(p.ray.hit_list + t);
                         float o[3], w[3], t0, t1;
@@ -687,7 +688,7 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                     for (uint32_t c = sub; c < nch; c += kGroupsPerSlot) {
                         uint32_t v0[16];
                         tmem_ld16(t_col + c * 16, v0);
-                        tmem_wait_ld();
+                        tmem_wait_ld(v0);
                         add_bias16(v0, bias_l + c * 16);
                         if (grow < p.n_rows) {
                             float o[16];

@@ -370,20 +370,30 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_kernel(const __grid_
             uint64_t a_desc[4];
 #pragma unroll
             for (int v = 0; v < 4; ++v) a_desc[v] = umma_desc_sw128(c.a_base + v * kATileBytes);
-            for (int r = 0; ok && r < rows; ++r) {
-                const int u = r & 3, bl = r >> 2;
+            // The row loop is unrolled: every MMA's accumulate flag, sign and
+            // operand offsets are compile-time constants. (With the row index
+            // u a loop variable, some builds of this loop lost MMAs, or
+            // accumulated into stale TMEM, depending only on how the
+            // surrounding code was laid out; every build with constant
+            // per-MMA flags gave exact results.)
+            for (int bl = 0; ok && bl < n_mine; ++bl) {
                 const uint32_t d_base = tmem_base + (bl & 1) * kDCols;
 #pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                    if (!mbar_wait(c.bar(kBarAFull + v), r & 1, c.abort, &g_status, kStatusTimeoutAFull)) {
-                        ok = false;
-                        break;
+                for (int u = 0; u < 4; ++u) {
+                    const int r = bl * 4 + u;
+                    if (!ok) break;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        if (!mbar_wait(c.bar(kBarAFull + v), r & 1, c.abort, &g_status, kStatusTimeoutAFull)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        issue_position(u, v, d_base, a_desc[v], u_desc0 + static_cast<uint64_t>(u * 4 + v) * u_pos,
+                                       p.idesc, ksteps);
+                        umma_commit(c.bar(kBarAEmpty + v));  // V tile v may be rewritten
+                        if (u == 3 && v == 3) umma_commit(c.bar(kBarDFull + (bl & 1)));
                     }
-                    tc_fence_after();
-                    issue_position(u, v, d_base, a_desc[v], u_desc0 + static_cast<uint64_t>(u * 4 + v) * u_pos,
-                                   p.idesc, ksteps);
-                    umma_commit(c.bar(kBarAEmpty + v));  // V tile v may be rewritten
-                    if (u == 3 && v == 3) umma_commit(c.bar(kBarDFull + (bl & 1)));
                 }
             }
             if (!ok) *c.abort = 1u;
