@@ -220,6 +220,30 @@ int rdvb_raymarch_render(const float* pose9, int width, int height, float fov, f
                          int n_layers, const int* dims, const int* layer_flags, const void* packed, int row_begin,
                          int row_end, void* workspace, size_t workspace_bytes, float* rgba, void* stream);
 
+/* Workspace bytes rdvb_transmittance_rm needs (a ray counter). */
+int64_t rdvb_transmittance_workspace_bytes(void);
+
+/* RaymarchingTransmittance (rdv/domain/volumes.py:124-141;
+ * rdv/shaders/volumes/raymarching_transmittance.h:1-21 and
+ * raymarching_transmittance_trait.h:1-14; replaces the Map[6, 1] dispatch of
+ * Map.__call__, rdv/maths/__init__.py:1451-1487, for this node):
+ * out[i] = transmittance along ray i of rays [n_rays, 6] (origin, direction;
+ * fp32, device). The ray is taken to object space by the node transform
+ * (transform: HOST mat4x3, 12 floats column-major -- 3x3 part, then the
+ * origin; NULL = identity), clipped to the [-1, 1]^3 box (misses give 1),
+ * then marched in fixed steps of step_size from the entry point: tau +=
+ * extinction(x) * density_scale * step_size, 0 as soon as tau > 16, else
+ * exp(-tau) once the segment (or 4096 steps) is used up.
+ * The extinction is the chain of n_layers Linear / LinearFast layers (dims[0]
+ * = 3, dims[n_layers] = 1, widths <= 128; weights[l] [dims[l+1], dims[l]] and
+ * biases[l] fp32 device; layer_flags as rdvb_mlp_forward; input_relu applies
+ * a ReLU to the position first). workspace: 256-byte aligned,
+ * rdvb_transmittance_workspace_bytes() bytes. */
+int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transform, float step_size,
+                          float density_scale, int n_layers, const int* dims, const float* const* weights,
+                          const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+                          size_t workspace_bytes, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,7 +5,9 @@ Pieces restated from the reference:
 * pinhole rays -- rdv/shaders/rendering/cameras.h:1-20 with the defaults of
   rdv/domain/rendering.py:24-42 (aspect = W/H, fov = pi/4, no jitter);
 * implicit [-1, 1]^3 box slab test -- rdv/shaders/libraries/math_library.h:48-57;
-* miss rule and entry clamp -- rdv/shaders/volumes/raymarching_transmittance.h:11-19;
+* object-space transform, miss rule and entry clamp --
+  rdv/shaders/volumes/raymarching_transmittance.h:1-21 (x <- L (x - O),
+  w <- L w with L the inverse of the node's 3x3 part, O its origin);
 * fixed-step absorption -- rdv/shaders/volumes/raymarching_transmittance_trait.h:1-14
   (``transmittance_rm``);
 * the MLP as a LinearFast chain (float16 staging, fp32 accumulate), see
@@ -156,12 +158,36 @@ def transmittance_rm(x, w, d, step_size, density_scale, extinction, safety_cap: 
     return out
 
 
-def raymarching_transmittance(origins, dirs, step_size, density_scale, extinction):
-    """RaymarchingTransmittance.forward (raymarching_transmittance.h:1-21) with
-    the identity transform: slab test, miss -> 1, entry clamp, then
-    transmittance_rm over d = tMax - tMin."""
+def object_space(origins, dirs, transform=None):
+    """raymarching_transmittance.h:4-9: x <- L (x - O), w <- L w, where
+    transform is the node's mat4x3 (12 floats, column-major: three columns of
+    the 3x3 part, then the origin O) and L the 3x3 inverse (formed in float64,
+    rounded to float32). Each component is ((L_i0 v_0 + L_i1 v_1) + L_i2 v_2)
+    with every product and sum rounded to float32."""
     o = np.asarray(origins, dtype=np.float32)
     w = np.asarray(dirs, dtype=np.float32)
+    if transform is None:
+        return o.copy(), w.copy()
+    t = np.asarray(transform, dtype=np.float64).reshape(-1)
+    M = t[:9].reshape(3, 3).T  # M[row, col]; the flat layout is column-major
+    O = t[9:12].astype(np.float32)
+    L = np.linalg.inv(M).astype(np.float32)
+
+    def apply(v):
+        out = np.empty_like(v)
+        for i in range(3):
+            acc = (L[i, 0] * v[:, 0]).astype(np.float32) + (L[i, 1] * v[:, 1]).astype(np.float32)
+            out[:, i] = acc.astype(np.float32) + (L[i, 2] * v[:, 2]).astype(np.float32)
+        return out
+
+    return apply((o - O).astype(np.float32)), apply(w)
+
+
+def raymarching_transmittance(origins, dirs, step_size, density_scale, extinction, transform=None):
+    """RaymarchingTransmittance.forward (raymarching_transmittance.h:1-21):
+    object-space transform, slab test, miss -> 1, entry clamp, then
+    transmittance_rm over d = tMax - tMin."""
+    o, w = object_space(origins, dirs, transform)
     tmin, tmax = ray_box(o, w)
     miss = (tmax <= 0) | (tmin > tmax)
     tmin = np.maximum(tmin, np.float32(0.0))
@@ -172,3 +198,12 @@ def raymarching_transmittance(origins, dirs, step_size, density_scale, extinctio
     if hit.any():
         out[hit] = transmittance_rm(x[hit], w[hit], d[hit], step_size, density_scale, extinction)
     return out
+
+
+def mlp_extinction(layers, input_relu: bool = False):
+    """extinction(x) of a Linear / LinearFast chain 3 -> ... -> 1 (layers as
+    mlp_eval): [R, 3] float32 -> [R] float32."""
+    def ext(p):
+        a = np.maximum(p, np.float32(0.0)) if input_relu else p
+        return mlp_eval(np.asarray(a, dtype=np.float32), layers)[:, 0].astype(np.float32)
+    return ext

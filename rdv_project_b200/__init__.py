@@ -16,6 +16,7 @@ from .tensor_ops import (TensorOperation, ReLUTensorOp, LinearTensorOp, LinearTe
 from .conv import (Conv2DTensorOp, Conv2DTensorOpWinograd3x3, Conv3x3Winograd, conv2d_direct,
                    _winograd_transform_weight)
 from .rendering import Cameras, VolumeRenderer
+from .volumes import RaymarchingTransmittance
 from ._native import RdvbError, device_status
 
 __all__ = [
@@ -24,6 +25,6 @@ __all__ = [
     "TensorOperation", "ReLUTensorOp", "LinearTensorOp", "LinearTensorOpFast", "LinearTensorOpMine",
     "LinearTensorOpSimple", "LinearTensorOpSmall",
     "Conv2DTensorOp", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
-    "Cameras", "VolumeRenderer",
+    "Cameras", "VolumeRenderer", "RaymarchingTransmittance",
     "RdvbError", "device_status",
 ]

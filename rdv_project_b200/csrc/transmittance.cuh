@@ -1,0 +1,234 @@
+// RaymarchingTransmittance: fixed-step absorption march with an MLP
+// extinction, one persistent thread per ray.
+//
+// Per ray (x, w) -- rdv/shaders/volumes/raymarching_transmittance.h:1-21:
+//   x <- L (x - O), w <- L w   (L = inverse of the node transform's 3x3
+//                               part, O its translation; L is formed on the
+//                               host)
+//   slab test against [-1, 1]^3 (rdv/shaders/libraries/math_library.h:48-57);
+//   a ray with tMax <= 0 or tMin > tMax returns 1;
+//   tMin <- max(0, tMin), x <- x + w tMin, d <- tMax - tMin, then
+//   rdv/shaders/volumes/raymarching_transmittance_trait.h:1-14:
+//     tau = 0; while d > 0 (at most 4096 steps):
+//       tau += extinction(x) * scale * step; tau > 16 -> return 0;
+//       d -= step; x += step * w
+//     return exp(-tau)
+// The march arithmetic is written with explicit round-to-nearest products
+// and sums (no contraction into FMAs), so the step count, the positions and
+// the early exit follow the reference's fp32 operations one for one.
+//
+// The extinction is a chain of Linear (exact fp32: acc = b, acc += x W in
+// ascending k, rdv/shaders/maps/linear.h:28-31) or LinearFast layers
+// (float16 / bfloat16 staged operands, fp32 accumulation, bias after,
+// rdv/shaders/maps/linear_fast.h:61-98) with optional ReLUs, 3 inputs and 1
+// output. All layers' weights are staged once per CTA into shared memory as
+// [K][chunk] blocks (one broadcast 16-byte load feeds 4 FMAs); activations
+// live in shared memory transposed ([feature][thread]), conflict free.
+//
+// Rays are handed out by one global counter: a thread whose ray finished
+// takes the next one, so the lanes of a warp stay busy although rays march
+// different numbers of steps.
+#pragma once
+#include "ptx.cuh"
+
+namespace rdvb {
+namespace trm {
+
+constexpr int kThreads = 128;    // rays in flight per CTA
+constexpr int kMaxLayers = 8;
+constexpr int kMaxWidth = 128;
+constexpr int kSafety = 4096;    // raymarching_transmittance_trait.h:4
+
+struct Layer {
+    const float* W;  // [N, K] fp32 (the caller's layout)
+    const float* b;  // [N] fp32
+    int K, N;
+    int chunk;     // 4 or 32 outputs per weight block
+    int w_off;     // float offset of this layer's blocks in the shared weight image
+    int b_off;     // float offset of its bias
+    int math;      // 0 f32 exact, 1 f16 staging, 2 bf16 staging
+    int relu;
+};
+
+struct Params {
+    const float* rays;      // [n_rays, 6] (x, w)
+    float* out;             // [n_rays]
+    long long n_rays;
+    int* counter;           // next ray index (0 at launch)
+    float L[9];             // row-major 3x3: x_obj[i] = sum_j L[3 i + j] (x - O)[j]
+    float O[3];
+    float step, scale;
+    int n_layers;
+    int input_relu;
+    int maxw;               // widest activation (>= 3)
+    int w_floats;           // floats of the shared weight image (weight blocks, then biases)
+    Layer layer[kMaxLayers];
+};
+
+__device__ __forceinline__ float stage_val(float v, int math) {
+    if (math == 1) return __half2float(__float2half_rn(v));
+    if (math == 2) return __bfloat162float(__float2bfloat16_rn(v));
+    return v;
+}
+
+// One chunk of CH outputs of layer L for this thread: acc over ascending k.
+template <int CH>
+__device__ __forceinline__ void chunk_eval(const Layer& L, const float* __restrict__ wsm, const float* __restrict__ bsm,
+                                           const float* ain, int o0, float (&acc)[CH]) {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) acc[j] = (L.math == 0 && o0 + j < L.N) ? bsm[L.b_off + o0 + j] : 0.0f;
+    const float* wb = wsm + L.w_off + o0 * L.K;  // block of outputs o0..o0+CH-1: [K][CH]
+    for (int k = 0; k < L.K; ++k) {
+        const float a = ain[k * kThreads];
+        const float4* wr = reinterpret_cast<const float4*>(wb + k * CH);
+#pragma unroll
+        for (int j4 = 0; j4 < CH / 4; ++j4) {
+            const float4 w = wr[j4];
+            acc[4 * j4 + 0] = fmaf(a, w.x, acc[4 * j4 + 0]);
+            acc[4 * j4 + 1] = fmaf(a, w.y, acc[4 * j4 + 1]);
+            acc[4 * j4 + 2] = fmaf(a, w.z, acc[4 * j4 + 2]);
+            acc[4 * j4 + 3] = fmaf(a, w.w, acc[4 * j4 + 3]);
+        }
+    }
+}
+
+// Finishes a chunk: bias after (staged layers), ReLU, staging for the next
+// layer's operands; writes outputs o0.. into aout (the thread's column).
+template <int CH>
+__device__ __forceinline__ void chunk_store(const Layer& L, const float* __restrict__ bsm, int next_math, int o0,
+                                            const float (&acc)[CH], float* aout) {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+        const int o = o0 + j;
+        if (o < L.N) {
+            float v = acc[j];
+            if (L.math != 0) v += bsm[L.b_off + o];
+            if (L.relu) v = fmaxf(v, 0.0f);
+            aout[o * kThreads] = stage_val(v, next_math);
+        }
+    }
+}
+
+// extinction(x) for this thread: the chain on the 3-vector x.
+__device__ __forceinline__ float extinction(const Params& p, const float* __restrict__ wsm,
+                                            const float* __restrict__ bsm, float* act0, float* act1,
+                                            const float (&x)[3]) {
+    const int m0 = p.layer[0].math;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        float v = x[k];
+        if (p.input_relu) v = fmaxf(v, 0.0f);
+        act0[k * kThreads] = stage_val(v, m0);
+    }
+    float* ain = act0;
+    float* aout = act1;
+    for (int l = 0; l < p.n_layers; ++l) {
+        const Layer L = p.layer[l];
+        const int next_math = l + 1 < p.n_layers ? p.layer[l + 1].math : 0;
+        if (L.chunk == 4) {
+            for (int o0 = 0; o0 < L.N; o0 += 4) {
+                float acc[4];
+                chunk_eval<4>(L, wsm, bsm, ain, o0, acc);
+                chunk_store<4>(L, bsm, next_math, o0, acc, aout);
+            }
+        } else {
+            for (int o0 = 0; o0 < L.N; o0 += 32) {
+                float acc[32];
+                chunk_eval<32>(L, wsm, bsm, ain, o0, acc);
+                chunk_store<32>(L, bsm, next_math, o0, acc, aout);
+            }
+        }
+        float* t = ain;
+        ain = aout;
+        aout = t;
+    }
+    return ain[0];
+}
+
+__global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_constant__ Params p) {
+    extern __shared__ float sm[];
+    float* wsm = sm;                                   // weight blocks, then biases
+    float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
+    float* act1 = act0 + p.maxw * kThreads;
+    // stage every layer once: block of outputs o0..o0+CH-1 as [K][CH], values
+    // rounded to the layer's operand format, zero beyond N
+    for (int l = 0; l < p.n_layers; ++l) {
+        const Layer L = p.layer[l];
+        const int nb = (L.N + L.chunk - 1) / L.chunk;
+        for (int i = threadIdx.x; i < nb * L.chunk * L.K; i += kThreads) {
+            const int blk = i / (L.chunk * L.K), rem = i - blk * L.chunk * L.K;
+            const int k = rem / L.chunk, j = rem - k * L.chunk;
+            const int o = blk * L.chunk + j;
+            wsm[L.w_off + i] = o < L.N ? stage_val(L.W[static_cast<size_t>(o) * L.K + k], L.math) : 0.0f;
+        }
+        for (int i = threadIdx.x; i < L.N; i += kThreads) wsm[L.b_off + i] = L.b[i];
+    }
+    __syncthreads();
+    const float* bsm = wsm;  // b_off values index the same image
+
+    long long ray = -1;
+    float x[3], w[3], d = 0.0f, tau = 0.0f;
+    int steps = 0;
+    while (true) {
+        if (ray < 0) {
+            ray = atomicAdd(p.counter, 1);
+            if (ray >= p.n_rays) break;
+            const float* r = p.rays + ray * 6;
+            float xr[3], wr[3];
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                xr[k] = __fsub_rn(r[k], p.O[k]);
+                wr[k] = r[3 + k];
+            }
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                x[i] = __fadd_rn(__fadd_rn(__fmul_rn(p.L[3 * i], xr[0]), __fmul_rn(p.L[3 * i + 1], xr[1])),
+                                 __fmul_rn(p.L[3 * i + 2], xr[2]));
+                w[i] = __fadd_rn(__fadd_rn(__fmul_rn(p.L[3 * i], wr[0]), __fmul_rn(p.L[3 * i + 1], wr[1])),
+                                 __fmul_rn(p.L[3 * i + 2], wr[2]));
+            }
+            float tmin = -INFINITY, tmax = INFINITY;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                const float inv = __fdiv_rn(1.0f, w[k]);
+                const float xc = __fmul_rn(-x[k], inv);
+                const float s = fabsf(inv);
+                tmin = fmaxf(tmin, __fsub_rn(xc, s));
+                tmax = fminf(tmax, __fadd_rn(xc, s));
+            }
+            if (tmax <= 0.0f || tmin > tmax) {  // the ray misses the volume: fully transparent
+                p.out[ray] = 1.0f;
+                ray = -1;
+                continue;
+            }
+            tmin = fmaxf(0.0f, tmin);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(w[k], tmin));
+            d = __fsub_rn(tmax, tmin);
+            tau = 0.0f;
+            steps = 0;
+            if (!(d > 0.0f)) {
+                p.out[ray] = 1.0f;  // exp(-0)
+                ray = -1;
+                continue;
+            }
+        }
+        const float e = __fmul_rn(extinction(p, wsm, bsm, act0, act1, x), p.scale);
+        tau = __fadd_rn(tau, __fmul_rn(e, p.step));
+        if (tau > 16.0f) {
+            p.out[ray] = 0.0f;
+            ray = -1;
+            continue;
+        }
+        d = __fsub_rn(d, p.step);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(p.step, w[k]));
+        if (!(d > 0.0f) || ++steps >= kSafety) {
+            p.out[ray] = expf(-tau);
+            ray = -1;
+        }
+    }
+}
+
+}  // namespace trm
+}  // namespace rdvb

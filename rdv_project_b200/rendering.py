@@ -48,6 +48,10 @@ class Cameras:
         self.fov = fov
         self.pixel_jitter = 0
 
+    def __rshift__(self, m):
+        """Camera grid composed with a Map[6, k] (e.g. RaymarchingTransmittance)."""
+        return _CameraGrid(self, m)
+
     def __call__(self) -> RDVObject:
         dev = current_device()
         poses = self.poses._tensor.to(device=dev, dtype=torch.float32).contiguous()
@@ -57,6 +61,19 @@ class Cameras:
                                              float(self.aspect_ratio), float(self.fov), out.data_ptr(),
                                              stream_handle()), "rdvb_camera_rays")
         return RDVObject(out)
+
+
+class _CameraGrid:
+    """``cameras >> m``: m evaluated on every ray of the grid ->
+    ``[num_cameras, height, width, m.OUT]``."""
+
+    def __init__(self, cameras: Cameras, m) -> None:
+        assert m.IN is None or m.IN == 6, "a camera grid produces 6 values per ray (origin, direction)"
+        self.cameras = cameras
+        self.map = m
+
+    def __call__(self) -> RDVObject:
+        return self.map(self.cameras())
 
 
 class VolumeRenderer:

@@ -1,0 +1,95 @@
+"""Volume nodes of the hot path.
+
+``RaymarchingTransmittance(extinction, transform=None, step_size=0.002,
+density_scale=1.0)`` mirrors rdv/domain/volumes.py:124-141: a ``Map[6, 1]``
+from a ray (origin, direction) to the transmittance of the fixed-step
+absorption march through the node's [-1, 1]^3 box
+(rdv/shaders/volumes/raymarching_transmittance.h:1-21,
+raymarching_transmittance_trait.h:1-14). ``extinction`` is a ``Map[3, 1]``
+(the reference casts it so, volumes.py:16) built from ``Linear`` /
+``LinearFast`` / ``ReLU``; ``transform`` is the node's ``mat4x3`` (four
+columns: the 3x3 part, then the origin; default identity). Calling the node on
+rays ``[..., 6]`` returns ``[..., 1]`` float32, one persistent CUDA thread
+per ray marching it exactly like the reference's loop (rdvb_transmittance_rm).
+
+``Cameras(...) >> node`` composes a camera grid with the node; calling the
+composition returns ``[num_cameras, height, width, 1]``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+from .core import RDVObject, _timed, current_device, stream_handle, wrap
+from .maps import Map, _lower
+
+_IDENTITY = (1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0)
+
+
+def _mat4x3(transform) -> tuple:
+    """12 floats, column-major (the reference's mat4x3 constructor order)."""
+    if transform is None:
+        return _IDENTITY
+    t = torch.as_tensor(transform, dtype=torch.float64).detach().cpu()
+    if t.shape == (4, 3):      # four columns of vec3
+        t = t.reshape(-1)
+    assert t.numel() == 12, "transform must be a mat4x3 (12 values, column-major)"
+    return tuple(float(v) for v in t.reshape(-1))
+
+
+class RaymarchingTransmittance(Map):
+    """Map[6, 1]: ray -> transmittance through the extinction field."""
+
+    IN = 6
+    OUT = 1
+
+    def __init__(self, extinction: Map, transform=None, step_size: float = 0.002, density_scale: float = 1.0):
+        ext = extinction
+        if ext.__is_generic__:
+            ext = ext._bind(in_size=3, out_size=1)
+        assert ext.IN == 3 and ext.OUT == 1, "extinction must be a Map[3, 1]"
+        self.extinction = ext
+        self.step_size = float(step_size)
+        self.transform = _mat4x3(transform)
+        self.density_scale = float(density_scale)
+        self._state = {}
+
+    def _ops(self):
+        raise NotImplementedError("RaymarchingTransmittance is evaluated by its own kernel, not a fused MLP chain")
+
+    def _device_state(self, dev):
+        st = self._state.get(dev.index)
+        if st is None:
+            input_relu, layers, relus = _lower(self.extinction)
+            if not layers:
+                raise NotImplementedError("the extinction needs at least one Linear layer")
+            st = {
+                "input_relu": int(input_relu),
+                "layers": layers,
+                "dims": [3] + [l.OUT for l in layers],
+                "flags": [l._math | (N.RDVB_LAYER_RELU if r else 0) for l, r in zip(layers, relus)],
+                "ws": torch.empty(int(N.lib().rdvb_transmittance_workspace_bytes()), dtype=torch.uint8, device=dev),
+            }
+            self._state[dev.index] = st
+        st["W"] = [l._fp32(l.weight, dev) for l in st["layers"]]
+        st["b"] = [l._fp32(l.bias, dev) for l in st["layers"]]
+        return st
+
+    def __call__(self, rays):
+        dev = current_device()
+        rt = rays._tensor if isinstance(rays, RDVObject) else wrap(rays)._tensor
+        assert rt.shape[-1] == 6, f"input's last dimension ({rt.shape[-1]}) must match the map's IN (6)"
+        lead = list(rt.shape[:-1])
+        r2 = rt.reshape(-1, 6)
+        if r2.device != dev or r2.dtype != torch.float32 or not r2.is_contiguous():
+            r2 = r2.to(device=dev, dtype=torch.float32).contiguous()
+        out = torch.empty(lead + [1], dtype=torch.float32, device=dev)
+        st = self._device_state(dev)
+        n = len(st["layers"])
+        with _timed():
+            N.check(N.lib().rdvb_transmittance_rm(
+                r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.step_size, self.density_scale, n,
+                N.int_array(st["dims"]), N.ptr_array([w.data_ptr() for w in st["W"]]),
+                N.ptr_array([b.data_ptr() for b in st["b"]]), N.int_array(st["flags"]), st["input_relu"],
+                st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(), stream_handle()), "rdvb_transmittance_rm")
+        return RDVObject(out)
