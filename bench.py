@@ -398,6 +398,7 @@ def run_ours(args, spec, world, rank, local):
                 "c3": run_c3(args, 1, 0, local, summary=True),
                 "c4": run_c4(args, 1, 0, local, summary=True),
                 "c5": mlp_summary(c5_spec()),
+                "transmittance": trm_summary(),
             }
     print(json.dumps(line), flush=True)
 
@@ -687,6 +688,44 @@ def run_reference_c34(args):
             "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------- RaymarchingTransmittance
+TRM = dict(width=1920, height=1080, dims=[3, 64, 64, 1], step=0.01, scale=1.0)
+
+
+def trm_summary(steps=3):
+    """Device-timed RaymarchingTransmittance over the config-4 camera's rays
+    (orbit pose 0, 1920x1080), extinction ReLU(MLP 3->64->64->1) with
+    LinearFast layers (Kaiming-normal, seeded), step 0.01, density scale 1."""
+    import rdv_project_b200 as rdv
+    from oracle import raymarch as orm
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    spec = dict(dims=TRM["dims"], math="f16", w_init="kaiming_normal")
+    layers = make_weights(spec)
+    for l in layers:
+        l["relu"] = True  # ReLU after every layer: extinction >= 0
+    node = rdv.RaymarchingTransmittance(build_map(rdv, layers, dev), step_size=TRM["step"],
+                                        density_scale=TRM["scale"])
+    cams = rdv.Cameras(TRM["width"], TRM["height"], torch.from_numpy(orm.orbit_pose(0)[None]))
+    rays = cams().as_tensor("torch").reshape(-1, 6)
+    for _ in range(2):
+        node(rays)
+    torch.cuda.synchronize()
+    t = time_steps(lambda: node(rays), steps)
+    evals = node.last_evaluations()
+    d = TRM["dims"]
+    flop = 2 * sum(d[i] * d[i + 1] for i in range(len(d) - 1))
+    achieved = evals * flop / (t / steps) / 1e12  # MLP flops of the evaluated steps (padded widths not counted)
+    peaks, peak_kind = measured_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    return {"workload": "RaymarchingTransmittance, 1920x1080 camera rays (orbit pose 0), extinction "
+                        "ReLU(MLP 3->64->64->1) LinearFast (tensor-core march), step 0.01",
+            "metric": "extinction evaluations/s", "value": evals * steps / t, "ms_per_step": t / steps * 1e3,
+            "evaluations_per_step": evals, "rays": int(rays.shape[0]),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_kind} bf16_tflops"}}
 
 
 def mlp_summary(spec, steps=5):

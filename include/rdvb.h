@@ -220,8 +220,13 @@ int rdvb_raymarch_render(const float* pose9, int width, int height, float fov, f
                          int n_layers, const int* dims, const int* layer_flags, const void* packed, int row_begin,
                          int row_end, void* workspace, size_t workspace_bytes, float* rgba, void* stream);
 
-/* Workspace bytes rdvb_transmittance_rm needs (a ray counter). */
-int64_t rdvb_transmittance_workspace_bytes(void);
+/* Workspace bytes rdvb_transmittance_rm needs for n_rays rays and this
+ * extinction chain: 256 for exact fp32 chains (CUDA-core march); for float16
+ * / bfloat16 chains (tensor-core march) also the packed weights and the
+ * per-batch ray and chunk records (about 110 MB at most). Bytes 8-15 hold
+ * (uint64) the number of extinction evaluations of the last call, readable
+ * once it completed. */
+int64_t rdvb_transmittance_workspace_bytes(int64_t n_rays, int n_layers, const int* dims, const int* layer_flags);
 
 /* RaymarchingTransmittance (rdv/domain/volumes.py:124-141;
  * rdv/shaders/volumes/raymarching_transmittance.h:1-21 and
@@ -238,7 +243,11 @@ int64_t rdvb_transmittance_workspace_bytes(void);
  * = 3, dims[n_layers] = 1, widths <= 128; weights[l] [dims[l+1], dims[l]] and
  * biases[l] fp32 device; layer_flags as rdvb_mlp_forward; input_relu applies
  * a ReLU to the position first). workspace: 256-byte aligned,
- * rdvb_transmittance_workspace_bytes() bytes. */
+ * rdvb_transmittance_workspace_bytes() bytes. Exact fp32 chains march one
+ * ray per CUDA thread exactly like the reference's loop; float16 / bfloat16
+ * chains evaluate every step of a ray in 128-step chunks on the tensor cores
+ * (fused MLP kernel) and combine the chunks in step order -- same result,
+ * steps past an early exit are evaluated too. */
 int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transform, float step_size,
                           float density_scale, int n_layers, const int* dims, const float* const* weights,
                           const float* const* biases, const int* layer_flags, int input_relu, void* workspace,

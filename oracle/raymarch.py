@@ -130,11 +130,12 @@ def render_emission_absorption(pose9, width: int, height: int, n_samples: int, l
     return rgba.reshape(row_end - row_begin, width, 4)
 
 
-def transmittance_rm(x, w, d, step_size, density_scale, extinction, safety_cap: int = 4096):
+def transmittance_rm(x, w, d, step_size, density_scale, extinction, safety_cap: int = 4096, counts=None):
     """raymarching_transmittance_trait.h:1-14 vectorised over rays:
     tau accumulates extinction(x) * scale * step while d > 0 (at most
     safety_cap steps); any ray whose tau exceeds 16 returns 0, else exp(-tau).
-    `extinction` maps [R, 3] float32 positions to [R] float32."""
+    `extinction` maps [R, 3] float32 positions to [R] float32. `counts`, if
+    given ([R] int64), receives each ray's number of extinction evaluations."""
     x = np.array(x, dtype=np.float32)
     w = np.asarray(w, dtype=np.float32)
     d = np.array(d, dtype=np.float32)
@@ -147,6 +148,8 @@ def transmittance_rm(x, w, d, step_size, density_scale, extinction, safety_cap: 
         if not live.any():
             break
         ext = extinction(x[live]).astype(np.float32) * scale
+        if counts is not None:
+            counts[live] += 1
         tau[live] = tau[live] + ext * step
         over = np.zeros_like(live)
         over[live] = tau[live] > 16
@@ -183,10 +186,12 @@ def object_space(origins, dirs, transform=None):
     return apply((o - O).astype(np.float32)), apply(w)
 
 
-def raymarching_transmittance(origins, dirs, step_size, density_scale, extinction, transform=None):
+def raymarching_transmittance(origins, dirs, step_size, density_scale, extinction, transform=None,
+                              return_evaluations: bool = False):
     """RaymarchingTransmittance.forward (raymarching_transmittance.h:1-21):
     object-space transform, slab test, miss -> 1, entry clamp, then
-    transmittance_rm over d = tMax - tMin."""
+    transmittance_rm over d = tMax - tMin. With return_evaluations, also the
+    total number of extinction evaluations."""
     o, w = object_space(origins, dirs, transform)
     tmin, tmax = ray_box(o, w)
     miss = (tmax <= 0) | (tmin > tmax)
@@ -195,8 +200,11 @@ def raymarching_transmittance(origins, dirs, step_size, density_scale, extinctio
     d = tmax - tmin
     out = np.ones(o.shape[0], dtype=np.float32)
     hit = ~miss
+    counts = np.zeros(int(hit.sum()), dtype=np.int64)
     if hit.any():
-        out[hit] = transmittance_rm(x[hit], w[hit], d[hit], step_size, density_scale, extinction)
+        out[hit] = transmittance_rm(x[hit], w[hit], d[hit], step_size, density_scale, extinction, counts=counts)
+    if return_evaluations:
+        return out, int(counts.sum())
     return out
 
 

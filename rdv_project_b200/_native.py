@@ -45,7 +45,7 @@ SIGNATURES = {
     "rdvb_raymarch_workspace_bytes": (_c_i64, [_c_int, _c_int]),
     "rdvb_raymarch_render": (_c_int, [_vp, _c_int, _c_int, _c_f, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int, _c_int,
                                       _vp, ctypes.c_size_t, _vp, _vp]),
-    "rdvb_transmittance_workspace_bytes": (_c_i64, []),
+    "rdvb_transmittance_workspace_bytes": (_c_i64, [_c_i64, _c_int, _vp, _vp]),
     "rdvb_transmittance_rm": (_c_int, [_vp, _c_i64, _vp, _c_f, _c_f, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
                                        ctypes.c_size_t, _vp, _vp]),
 }

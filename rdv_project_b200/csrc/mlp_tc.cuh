@@ -72,10 +72,33 @@ struct Layer {
     uint32_t relu;
 };
 
-// Volume ray-march mode: one 128-row tile is one ray's 128 samples.
+// Transmittance march (RaymarchingTransmittance): a ray's entry point and
+// object-space direction, its step count (the reference's d > 0 loop, at
+// most 4096) and the index of its first 128-step chunk in the chunk list.
+struct MarchRay {
+    float x[3];
+    float w[3];
+    int n_steps;
+    int base;
+};
+
+// Kernel modes (template argument RAY): rows of x, volume render, transmittance march.
+constexpr int kModeRows = 0;
+constexpr int kModeRender = 1;
+constexpr int kModeMarch = 2;
+
+// Volume ray-march modes. Render (march = 0): one 128-row tile is one ray's
+// 128 samples, composited into an RGBA pixel. Transmittance (march = 1):
+// one tile is 128 consecutive steps of one ray; the tile's result is the sum
+// of its steps' extinction * scale * step and the largest prefix of that sum.
 struct RayParams {
-    const int* hit_list;   // pixel index (within the rendered band) of every ray that hits the box
+    const int* hit_list;   // render: pixel index (within the band) of every ray that hits the box;
+                           // march: ray index of every chunk
     const int* n_hits;     // number of entries of hit_list (device)
+    int march;
+    const MarchRay* rec;   // march: per-ray records
+    float2* chunk_out;     // march: (sum, largest prefix) per chunk
+    float step, scale;     // march: step size, density scale
     float* rgba;           // [band rows * width, 4]
     float org[3];          // camera origin
     float xa[3], ya[3], za[3];  // camera basis (cameras.h: xaxis, yaxis, zaxis)
@@ -224,7 +247,7 @@ __device__ __forceinline__ bool ray_setup(const RayParams& rp, int pix, float (&
 __device__ __forceinline__ float softplus_f(float v) { return fmaxf(v, 0.0f) + log1pf(expf(-fabsf(v))); }
 __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-template <int SLOTS, int BF16, bool RAY, int ISSUERS>
+template <int SLOTS, int BF16, int RAY, int ISSUERS>
 __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const __grid_constant__ Params p) {
     static_assert(SLOTS == 2 || SLOTS == 4, "the epilogue splits 4 warp groups evenly over the slots");
     extern __shared__ uint8_t smem_raw[];
@@ -391,6 +414,28 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                         break;
                     }
                     a0eph ^= 1u << s;
+                    if constexpr (RAY == kModeMarch) {
+                        // step k = 128 c + i of the ray at x_e + (k * step) * w
+                        const int ray = __ldg(p.ray.hit_list + t);
+                        const MarchRay& mr = p.ray.rec[ray];
+                        const int c = t - __ldg(&mr.base);
+                        const float xe0 = __ldg(&mr.x[0]), xe1 = __ldg(&mr.x[1]), xe2 = __ldg(&mr.x[2]);
+                        const float w0 = __ldg(&mr.w[0]), w1 = __ldg(&mr.w[1]), w2 = __ldg(&mr.w[2]);
+                        const uint32_t a_tile = a_base + static_cast<uint32_t>(s) * p.a0_bytes;
+#pragma unroll
+                        for (int k = 0; k < kTileM / 32; ++k) {
+                            const uint32_t ri = static_cast<uint32_t>(k * 32 + lane);
+                            const float tk = __fmul_rn(static_cast<float>(c * kTileM + static_cast<int>(ri)), p.ray.step);
+                            st_shared_v4(a_tile + sw128_offset(ri, 0, kTileM),
+                                         pack2_rt<BF16>(__fadd_rn(xe0, __fmul_rn(tk, w0)), __fadd_rn(xe1, __fmul_rn(tk, w1)),
+                                                        p.relu_in),
+                                         pack2_rt<BF16>(__fadd_rn(xe2, __fmul_rn(tk, w2)), 0.0f, p.relu_in), 0u, 0u);
+                        }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(bar(kBarA0Full + s));
+                        continue;
+                    }
                     float o[3], w[3], t0, t1;
                     ray_setup(p.ray, __ldg(p.ray.hit_list + t), o, w, t0, t1);
                     const float dt = (t1 - t0) / static_cast<float>(kTileM);
@@ -617,12 +662,63 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                     }
                     tmem_wait_st();
                 } else if constexpr (RAY) {
-                    // Front-to-back emission-absorption compositing of the
-                    // ray's 128 samples (rows = samples in order): the warps
-                    // owning columns 0..15 (sigma, r, g, b) each scan their
-                    // quadrant's 32 samples with shuffles; quadrant 0 chains
-                    // the 4 partials.
-                    if (sub == 0) {
+                    if constexpr (RAY == kModeMarch) {
+                        if (sub == 0) {
+                            // transmittance: tau_i = extinction_i * scale * step for
+                            // the chunk's valid steps (0 past the ray's end); each
+                            // quadrant scans its 32 steps, quadrant 0 chains the 4
+                            // (sum, largest prefix) partials in step order
+                            uint32_t v0[16];
+                            tmem_ld16(t_col, v0);
+                            tmem_wait_ld(v0);
+                            add_bias16(v0, bias_l);
+                            const int ray = __ldg(p.ray.hit_list + t);
+                            const MarchRay& mr = p.ray.rec[ray];
+                            const int c = t - __ldg(&mr.base);
+                            float e = __uint_as_float(v0[0]);
+                            if (relu) e = fmaxf(e, 0.0f);
+                            const bool valid = c * kTileM + row < __ldg(&mr.n_steps);
+                            const float tau = valid ? __fmul_rn(__fmul_rn(e, p.ray.scale), p.ray.step) : 0.0f;
+                            float incl = tau;
+    #pragma unroll
+                            for (int d = 1; d < 32; d <<= 1) {
+                                const float nb = __shfl_up_sync(0xffffffffu, incl, d);
+                                if (lane >= d) incl += nb;
+                            }
+                            float pmax = valid ? incl : -INFINITY;
+    #pragma unroll
+                            for (int d = 16; d > 0; d >>= 1) pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, d));
+                            const float sum_q = __shfl_sync(0xffffffffu, incl, 31);
+                            float* scr = reinterpret_cast<float*>(base_ptr + p.off_ray) + s * 16;
+                            if (lane == 0) {
+                                scr[quad * 4 + 0] = sum_q;
+                                scr[quad * 4 + 1] = pmax;
+                                mbar_arrive(bar(kBarComp + s));
+                            }
+                            if (quad == 0) {
+                                bool got = true;
+                                if (lane == 0) {
+                                    got = mbar_wait(bar(kBarComp + s), comp_ph, abort, &g_status, kStatusTimeoutOther);
+                                    if (got) {
+                                        float sum = 0.0f, best = -INFINITY;
+    #pragma unroll
+                                        for (int q = 0; q < 4; ++q) {
+                                            best = fmaxf(best, sum + scr[q * 4 + 1]);
+                                            sum += scr[q * 4 + 0];
+                                        }
+                                        p.ray.chunk_out[t] = make_float2(sum, best);
+                                    }
+                                }
+                                comp_ph ^= 1u;
+                                if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) ok = false;
+                            }
+                        }
+                    } else if (sub == 0) {
+                        // render: front-to-back emission-absorption
+                        // compositing of the ray's 128 samples (rows = samples
+                        // in order): the warps owning columns 0..15 (sigma, r,
+                        // g, b) each scan their quadrant's 32 samples with
+                        // shuffles; quadrant 0 chains the 4 partials.
                         uint32_t v0[16];
                         tmem_ld16(t_col, v0);
                         tmem_wait_ld(v0);

@@ -47,7 +47,7 @@ struct DeviceInfo {
     bool init = false;
     int sm_count = 0;
     int max_smem_optin = 0;
-    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2][2][3] = {};  // [slots][bf16][ray][issuers]
+    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2][3][3] = {};  // [slots][bf16][mode][issuers]
     size_t simt_smem_set = 0;
     size_t wino_smem_set[2] = {};
     size_t trm_smem_set = 0;
@@ -248,7 +248,7 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     if (!slots) return RDVB_OK;  // does not fit: CUDA-core path
 
     int rc = RDVB_OK;
-    const int ri = ray ? 1 : 0;
+    const int ri = ray ? (ray->march ? kModeMarch : kModeRender) : kModeRows;
     // two MMA-issuing warps when the weights are resident (the slots are then
     // independent); one in-order issuer for streamed weights
     const int iss = p.resident ? 2 : 1;
@@ -271,11 +271,16 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
 #define RDVB_GO(S, B, R)                                                         \
     (iss == 2 ? go(mlp_tc_kernel<S, B, R, 2>, S) : go(mlp_tc_kernel<S, B, R, 1>, S))
     if (ray) {
-        if (slots == 4) bf16 ? RDVB_GO(4, 1, true) : RDVB_GO(4, 0, true);
-        else bf16 ? RDVB_GO(2, 1, true) : RDVB_GO(2, 0, true);
+        if (ri == kModeMarch) {
+            if (slots == 4) bf16 ? RDVB_GO(4, 1, kModeMarch) : RDVB_GO(4, 0, kModeMarch);
+            else bf16 ? RDVB_GO(2, 1, kModeMarch) : RDVB_GO(2, 0, kModeMarch);
+        } else {
+            if (slots == 4) bf16 ? RDVB_GO(4, 1, kModeRender) : RDVB_GO(4, 0, kModeRender);
+            else bf16 ? RDVB_GO(2, 1, kModeRender) : RDVB_GO(2, 0, kModeRender);
+        }
     } else {
-        if (slots == 4) bf16 ? RDVB_GO(4, 1, false) : RDVB_GO(4, 0, false);
-        else bf16 ? RDVB_GO(2, 1, false) : RDVB_GO(2, 0, false);
+        if (slots == 4) bf16 ? RDVB_GO(4, 1, kModeRows) : RDVB_GO(4, 0, kModeRows);
+        else bf16 ? RDVB_GO(2, 1, kModeRows) : RDVB_GO(2, 0, kModeRows);
     }
 #undef RDVB_GO
     if (rc) return rc;
@@ -687,7 +692,42 @@ int rdvb_raymarch_render(const float* pose9, int width, int height, float fov, f
     return RDVB_OK;
 }
 
-int64_t rdvb_transmittance_workspace_bytes(void) { return 256; }
+namespace {
+constexpr int64_t kMarchBatch = 1 << 18;  // rays per tensor-core march batch
+constexpr int64_t kMarchChunks = (rdvb::trm::kSafety + rdvb::mlp_tc::kTileM - 1) / rdvb::mlp_tc::kTileM;
+
+// The tensor-core march takes chains whose layers all stage float16 (or all
+// bfloat16) and that fit the fused kernel; exact fp32 chains run on the
+// CUDA cores.
+bool march_on_tensor_cores(int n_layers, const int* dims, const int* flags) {
+    const int math = flags[0] & 3;
+    if (math == RDVB_MATH_F32) return false;
+    for (int l = 1; l < n_layers; ++l)
+        if ((flags[l] & 3) != math) return false;
+    return pack_layout(n_layers, dims).ok;
+}
+
+struct MarchWorkspace {
+    int64_t packed_off, rec_off, list_off, out_off, total;
+};
+
+MarchWorkspace march_workspace(int64_t n_rays, int n_layers, const int* dims) {
+    MarchWorkspace m;
+    const int64_t batch = std::max<int64_t>(1, std::min(n_rays, kMarchBatch));
+    m.packed_off = 256;
+    m.rec_off = m.packed_off + ((rdvb_mlp_packed_bytes(n_layers, dims) + 255) / 256) * 256;
+    m.list_off = m.rec_off + batch * static_cast<int64_t>(sizeof(rdvb::mlp_tc::MarchRay));
+    m.out_off = m.list_off + ((batch * kMarchChunks * 4 + 255) / 256) * 256;
+    m.total = m.out_off + batch * kMarchChunks * 8;
+    return m;
+}
+}  // namespace
+
+int64_t rdvb_transmittance_workspace_bytes(int64_t n_rays, int n_layers, const int* dims, const int* layer_flags) {
+    if (n_rays < 0 || n_layers < 1 || n_layers > rdvb::trm::kMaxLayers || !dims || !layer_flags) return 0;
+    if (!march_on_tensor_cores(n_layers, dims, layer_flags)) return 256;
+    return march_workspace(n_rays, n_layers, dims).total;
+}
 
 int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transform, float step_size,
                           float density_scale, int n_layers, const int* dims, const float* const* weights,
@@ -714,8 +754,10 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
     if (n_rays == 0) return RDVB_OK;
     if (!rays || !out) return fail(RDVB_ERR_INVALID_ARG, "rays and out must not be NULL");
     if (!aligned(rays, 4) || !aligned(out, 4)) return fail(RDVB_ERR_INVALID_ARG, "rays and out must be 4-byte aligned");
-    if (!workspace || !aligned(workspace, 256) || workspace_bytes < 256)
-        return fail(RDVB_ERR_INVALID_ARG, "workspace must be 256-byte aligned and hold 256 bytes");
+    const bool tc = march_on_tensor_cores(n_layers, dims, layer_flags);
+    const int64_t need = tc ? march_workspace(n_rays, n_layers, dims).total : 256;
+    if (!workspace || !aligned(workspace, 256) || static_cast<int64_t>(workspace_bytes) < need)
+        return fail(RDVB_ERR_INVALID_ARG, "workspace must be 256-byte aligned and hold %lld bytes", (long long)need);
     DeviceInfo* dev = nullptr;
     if (int rc = current_device(&dev)) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -726,6 +768,7 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
     p.out = out;
     p.n_rays = n_rays;
     p.counter = static_cast<int*>(workspace);
+    p.evaluations = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + 8);
     p.step = step_size;
     p.scale = density_scale;
     p.n_layers = n_layers;
@@ -755,6 +798,68 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
     inv[2][2] = (M[0][0] * M[1][1] - M[0][1] * M[1][0]) / det;
     for (int r = 0; r < 3; ++r)
         for (int c = 0; c < 3; ++c) p.L[3 * r + c] = static_cast<float>(inv[r][c]);
+    if (tc) {
+        // tensor-core march: pack the chain into the workspace, then per
+        // batch of rays: setup -> fused MLP over the chunks -> combine
+        using rdvb::mlp_tc::MarchRay;
+        using rdvb::mlp_tc::RayParams;
+        const MarchWorkspace m = march_workspace(n_rays, n_layers, dims);
+        uint8_t* ws = static_cast<uint8_t*>(workspace);
+        const int math = layer_flags[0] & 3;
+        if (int rc = rdvb_mlp_pack(n_layers, dims, weights, biases, math == RDVB_MATH_BF16 ? RDVB_BF16 : RDVB_F16,
+                                   ws + m.packed_off, stream))
+            return rc;
+        cudaError_t e = cudaMemsetAsync(ws, 0, 16, st);
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+        int* n_chunks = reinterpret_cast<int*>(ws);
+        unsigned long long* evals = reinterpret_cast<unsigned long long*>(ws + 8);
+        MarchRay* rec = reinterpret_cast<MarchRay*>(ws + m.rec_off);
+        int* list = reinterpret_cast<int*>(ws + m.list_off);
+        float2* cout2 = reinterpret_cast<float2*>(ws + m.out_off);
+        for (int64_t b0 = 0; b0 < n_rays; b0 += kMarchBatch) {
+            const int nb = static_cast<int>(std::min<int64_t>(kMarchBatch, n_rays - b0));
+            e = cudaMemsetAsync(n_chunks, 0, sizeof(int), st);
+            if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+            SetupParams sp;
+            memset(&sp, 0, sizeof(sp));
+            sp.rays = rays + b0 * 6;
+            sp.out = out + b0;
+            sp.n = nb;
+            memcpy(sp.L, p.L, sizeof(sp.L));
+            memcpy(sp.O, p.O, sizeof(sp.O));
+            sp.step = step_size;
+            sp.rec = rec;
+            sp.chunk_list = list;
+            sp.n_chunks = n_chunks;
+            const int threads = 256;
+            const int blocks = static_cast<int>(std::min<int64_t>((nb + threads - 1) / threads, dev->sm_count * 8LL));
+            trm_setup_kernel<<<blocks, threads, 0, st>>>(sp);
+            if (int rc = check_launch("trm_setup_kernel")) return rc;
+            RayParams rp;
+            memset(&rp, 0, sizeof(rp));
+            rp.hit_list = list;
+            rp.n_hits = n_chunks;
+            rp.march = 1;
+            rp.rec = rec;
+            rp.chunk_out = cout2;
+            rp.step = step_size;
+            rp.scale = density_scale;
+            bool taken = false;
+            if (int rc = launch_mlp_tc(nullptr, RDVB_F32, 0, n_layers, dims, layer_flags, input_relu, ws + m.packed_off,
+                                       nullptr, st, dev, &taken, &rp))
+                return rc;
+            if (!taken) return fail(RDVB_ERR_UNSUPPORTED, "extinction MLP does not fit the tensor-core kernel");
+            CombineParams cp;
+            cp.rec = rec;
+            cp.chunk_out = cout2;
+            cp.out = out + b0;
+            cp.n = nb;
+            cp.evaluations = evals;
+            trm_combine_kernel<<<blocks, threads, 0, st>>>(cp);
+            if (int rc = check_launch("trm_combine_kernel")) return rc;
+        }
+        return RDVB_OK;
+    }
     int off = 0;
     for (int l = 0; l < n_layers; ++l) {
         Layer& L = p.layer[l];
@@ -789,7 +894,7 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
     per_sm = std::max(per_sm, 1);
     const long long want = (n_rays + kThreads - 1) / kThreads;
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * dev->sm_count * per_sm)));
-    e = cudaMemsetAsync(p.counter, 0, sizeof(int), st);
+    e = cudaMemsetAsync(workspace, 0, 16, st);
     if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
     transmittance_kernel<<<grid, kThreads, smem, st>>>(p);
     return check_launch("transmittance_kernel");

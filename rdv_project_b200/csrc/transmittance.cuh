@@ -29,7 +29,7 @@
 // takes the next one, so the lanes of a warp stay busy although rays march
 // different numbers of steps.
 #pragma once
-#include "ptx.cuh"
+#include "mlp_tc.cuh"
 
 namespace rdvb {
 namespace trm {
@@ -54,7 +54,8 @@ struct Params {
     const float* rays;      // [n_rays, 6] (x, w)
     float* out;             // [n_rays]
     long long n_rays;
-    int* counter;           // next ray index (0 at launch)
+    int* counter;                   // next ray index (0 at launch)
+    unsigned long long* evaluations; // extinction evaluations of the launch (0 at launch)
     float L[9];             // row-major 3x3: x_obj[i] = sum_j L[3 i + j] (x - O)[j]
     float O[3];
     float step, scale;
@@ -145,6 +146,41 @@ __device__ __forceinline__ float extinction(const Params& p, const float* __rest
     return ain[0];
 }
 
+// raymarching_transmittance.h:4-19 for one ray r = (x, w): object space,
+// slab test, entry clamp. Returns false on a miss; else the entry point x,
+// the object-space direction w and d = tMax - tMin.
+__device__ __forceinline__ bool march_entry(const float* __restrict__ r, const float (&L)[9], const float (&O)[3],
+                                            float (&x)[3], float (&w)[3], float& d) {
+    float xr[3], wr[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        xr[k] = __fsub_rn(r[k], O[k]);
+        wr[k] = r[3 + k];
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        x[i] = __fadd_rn(__fadd_rn(__fmul_rn(L[3 * i], xr[0]), __fmul_rn(L[3 * i + 1], xr[1])),
+                         __fmul_rn(L[3 * i + 2], xr[2]));
+        w[i] = __fadd_rn(__fadd_rn(__fmul_rn(L[3 * i], wr[0]), __fmul_rn(L[3 * i + 1], wr[1])),
+                         __fmul_rn(L[3 * i + 2], wr[2]));
+    }
+    float tmin = -INFINITY, tmax = INFINITY;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float inv = __fdiv_rn(1.0f, w[k]);
+        const float xc = __fmul_rn(-x[k], inv);
+        const float s = fabsf(inv);
+        tmin = fmaxf(tmin, __fsub_rn(xc, s));
+        tmax = fminf(tmax, __fadd_rn(xc, s));
+    }
+    if (tmax <= 0.0f || tmin > tmax) return false;
+    tmin = fmaxf(0.0f, tmin);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(w[k], tmin));
+    d = __fsub_rn(tmax, tmin);
+    return true;
+}
+
 __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_constant__ Params p) {
     extern __shared__ float sm[];
     float* wsm = sm;                                   // weight blocks, then biases
@@ -173,38 +209,11 @@ __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_co
         if (ray < 0) {
             ray = atomicAdd(p.counter, 1);
             if (ray >= p.n_rays) break;
-            const float* r = p.rays + ray * 6;
-            float xr[3], wr[3];
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                xr[k] = __fsub_rn(r[k], p.O[k]);
-                wr[k] = r[3 + k];
-            }
-#pragma unroll
-            for (int i = 0; i < 3; ++i) {
-                x[i] = __fadd_rn(__fadd_rn(__fmul_rn(p.L[3 * i], xr[0]), __fmul_rn(p.L[3 * i + 1], xr[1])),
-                                 __fmul_rn(p.L[3 * i + 2], xr[2]));
-                w[i] = __fadd_rn(__fadd_rn(__fmul_rn(p.L[3 * i], wr[0]), __fmul_rn(p.L[3 * i + 1], wr[1])),
-                                 __fmul_rn(p.L[3 * i + 2], wr[2]));
-            }
-            float tmin = -INFINITY, tmax = INFINITY;
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                const float inv = __fdiv_rn(1.0f, w[k]);
-                const float xc = __fmul_rn(-x[k], inv);
-                const float s = fabsf(inv);
-                tmin = fmaxf(tmin, __fsub_rn(xc, s));
-                tmax = fminf(tmax, __fadd_rn(xc, s));
-            }
-            if (tmax <= 0.0f || tmin > tmax) {  // the ray misses the volume: fully transparent
-                p.out[ray] = 1.0f;
+            if (!march_entry(p.rays + ray * 6, p.L, p.O, x, w, d)) {
+                p.out[ray] = 1.0f;  // the ray misses the volume: fully transparent
                 ray = -1;
                 continue;
             }
-            tmin = fmaxf(0.0f, tmin);
-#pragma unroll
-            for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(w[k], tmin));
-            d = __fsub_rn(tmax, tmin);
             tau = 0.0f;
             steps = 0;
             if (!(d > 0.0f)) {
@@ -214,19 +223,122 @@ __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_co
             }
         }
         const float e = __fmul_rn(extinction(p, wsm, bsm, act0, act1, x), p.scale);
+        ++steps;
         tau = __fadd_rn(tau, __fmul_rn(e, p.step));
+        bool done = false;
+        float result = 0.0f;
         if (tau > 16.0f) {
-            p.out[ray] = 0.0f;
-            ray = -1;
-            continue;
-        }
-        d = __fsub_rn(d, p.step);
+            done = true;
+        } else {
+            d = __fsub_rn(d, p.step);
 #pragma unroll
-        for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(p.step, w[k]));
-        if (!(d > 0.0f) || ++steps >= kSafety) {
-            p.out[ray] = expf(-tau);
+            for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(p.step, w[k]));
+            if (!(d > 0.0f) || steps >= kSafety) {
+                done = true;
+                result = expf(-tau);
+            }
+        }
+        if (done) {
+            p.out[ray] = result;
+            atomicAdd(p.evaluations, static_cast<unsigned long long>(steps));
             ray = -1;
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core path (float16 / bfloat16 extinction chains): rays in batches.
+//   trm_setup_kernel   one thread per ray: entry point, the exact step count
+//                      of the reference's loop (d -= step while d > 0, at
+//                      most 4096 steps), and a contiguous run of ceil(n/128)
+//                      chunk-list entries (warp-aggregated append);
+//   mlp_tc_kernel      (ray mode, march = 1) one 128-step chunk per tile:
+//                      the extinction MLP on tcgen05 and the chunk's (sum,
+//                      largest prefix) of tau;
+//   trm_combine_kernel one thread per ray: the chunks in step order -- 0 as
+//                      soon as tau + prefix > 16, else exp(-tau).
+// Every step of a ray is evaluated, also past an early exit; the result is
+// the reference's.
+struct SetupParams {
+    const float* rays;  // batch [n, 6]
+    float* out;         // batch [n]
+    int n;
+    float L[9];
+    float O[3];
+    float step;
+    mlp_tc::MarchRay* rec;
+    int* chunk_list;
+    int* n_chunks;
+};
+
+__global__ void trm_setup_kernel(const __grid_constant__ SetupParams p) {
+    const int lane = threadIdx.x & 31;
+    for (int base0 = blockIdx.x * blockDim.x; base0 < p.n; base0 += gridDim.x * blockDim.x) {
+        const int i = base0 + threadIdx.x;
+        int nch = 0;
+        mlp_tc::MarchRay mr;
+        if (i < p.n) {
+            float x[3], w[3], d = 0.0f;
+            int n = 0;
+            if (march_entry(p.rays + static_cast<long long>(i) * 6, p.L, p.O, x, w, d)) {
+                while (d > 0.0f && n < kSafety) {
+                    d = __fsub_rn(d, p.step);
+                    ++n;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                mr.x[k] = x[k];
+                mr.w[k] = w[k];
+            }
+            mr.n_steps = n;
+            nch = (n + mlp_tc::kTileM - 1) / mlp_tc::kTileM;
+            if (n == 0) p.out[i] = 1.0f;  // miss, or an empty segment: exp(-0)
+        }
+        // warp-aggregated append of each ray's chunk run
+        int incl = nch;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int nb = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += nb;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        int wbase = 0;
+        if (lane == 0 && total) wbase = atomicAdd(p.n_chunks, total);
+        wbase = __shfl_sync(0xffffffffu, wbase, 0);
+        if (i < p.n) {
+            mr.base = wbase + incl - nch;
+            p.rec[i] = mr;
+            for (int c = 0; c < nch; ++c) p.chunk_list[mr.base + c] = i;
+        }
+    }
+}
+
+struct CombineParams {
+    const mlp_tc::MarchRay* rec;
+    const float2* chunk_out;
+    float* out;
+    int n;
+    unsigned long long* evaluations;
+};
+
+__global__ void trm_combine_kernel(const __grid_constant__ CombineParams p) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += gridDim.x * blockDim.x) {
+        const int n = p.rec[i].n_steps;
+        if (n == 0) continue;
+        const int base = p.rec[i].base;
+        const int nch = (n + mlp_tc::kTileM - 1) / mlp_tc::kTileM;
+        float tau = 0.0f, T = -1.0f;
+        for (int c = 0; c < nch; ++c) {
+            const float2 r = p.chunk_out[base + c];
+            if (tau + r.y > 16.0f) {
+                T = 0.0f;
+                break;
+            }
+            tau += r.x;
+        }
+        p.out[i] = T < 0.0f ? expf(-tau) : T;
+        atomicAdd(p.evaluations, static_cast<unsigned long long>(n));
     }
 }
 

@@ -9,8 +9,10 @@ raymarching_transmittance_trait.h:1-14). ``extinction`` is a ``Map[3, 1]``
 (the reference casts it so, volumes.py:16) built from ``Linear`` /
 ``LinearFast`` / ``ReLU``; ``transform`` is the node's ``mat4x3`` (four
 columns: the 3x3 part, then the origin; default identity). Calling the node on
-rays ``[..., 6]`` returns ``[..., 1]`` float32, one persistent CUDA thread
-per ray marching it exactly like the reference's loop (rdvb_transmittance_rm).
+rays ``[..., 6]`` returns ``[..., 1]`` float32 (rdvb_transmittance_rm): exact
+fp32 chains march one ray per CUDA thread like the reference's loop;
+float16 / bfloat16 (LinearFast) chains evaluate the steps in 128-step chunks
+with the fused tensor-core MLP kernel.
 
 ``Cameras(...) >> node`` composes a camera grid with the node; calling the
 composition returns ``[num_cameras, height, width, 1]``.
@@ -68,7 +70,7 @@ class RaymarchingTransmittance(Map):
                 "layers": layers,
                 "dims": [3] + [l.OUT for l in layers],
                 "flags": [l._math | (N.RDVB_LAYER_RELU if r else 0) for l, r in zip(layers, relus)],
-                "ws": torch.empty(int(N.lib().rdvb_transmittance_workspace_bytes()), dtype=torch.uint8, device=dev),
+                "ws": None,
             }
             self._state[dev.index] = st
         st["W"] = [l._fp32(l.weight, dev) for l in st["layers"]]
@@ -86,6 +88,10 @@ class RaymarchingTransmittance(Map):
         out = torch.empty(lead + [1], dtype=torch.float32, device=dev)
         st = self._device_state(dev)
         n = len(st["layers"])
+        need = int(N.lib().rdvb_transmittance_workspace_bytes(r2.shape[0], n, N.int_array(st["dims"]),
+                                                              N.int_array(st["flags"])))
+        if st["ws"] is None or st["ws"].numel() < need:
+            st["ws"] = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
         with _timed():
             N.check(N.lib().rdvb_transmittance_rm(
                 r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.step_size, self.density_scale, n,
@@ -93,3 +99,11 @@ class RaymarchingTransmittance(Map):
                 N.ptr_array([b.data_ptr() for b in st["b"]]), N.int_array(st["flags"]), st["input_relu"],
                 st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(), stream_handle()), "rdvb_transmittance_rm")
         return RDVObject(out)
+
+    def last_evaluations(self) -> int:
+        """Extinction evaluations (march steps) of the last call on this
+        device; synchronises with it."""
+        st = self._state.get(current_device().index)
+        if st is None or st["ws"] is None:
+            return 0
+        return int(st["ws"][8:16].view(torch.int64).item())

@@ -95,9 +95,15 @@ def test_fp32_chain_matches_oracle(rdv, cuda_device, dims, step, scale, final_re
     # the field also takes negative values (tau may fall), as any Map may
     layers = _layers(dims, "f32", seed=len(dims), final_relu=final_relu)
     rays = _rays(1536, seed=1)
-    got = _run(rdv, layers, rays, cuda_device, step_size=step, density_scale=scale)
-    ref = _oracle(layers, rays, step, scale)
+    node = rdv.RaymarchingTransmittance(_chain(rdv, layers, cuda_device), step_size=step, density_scale=scale)
+    got = node(torch.from_numpy(rays).to(cuda_device)).as_tensor("torch")[:, 0].cpu().numpy()
+    ref, evals = orm.raymarching_transmittance(rays[:, :3], rays[:, 3:], step, scale, orm.mlp_extinction(layers),
+                                               return_evaluations=True)
     _check(got, ref, TOL_F32)
+    # same number of march steps (positions, d and the exits follow the same fp32 operations)
+    # (a ray whose tau ends within rounding of 16 may exit on one side only)
+    flips = np.any((got == 0.0) != (ref == 0.0))
+    assert node.last_evaluations() == evals or flips, (node.last_evaluations(), evals)
     # the march outcomes themselves agree: misses give exactly 1, early exits exactly 0
     assert np.array_equal(got == 1.0, ref == 1.0)
     assert np.sum((got == 0.0) != (ref == 0.0)) <= 2  # a tau within rounding of 16 may exit on one side only
@@ -109,6 +115,32 @@ def test_staged_chain_matches_oracle(rdv, cuda_device, math_):
     rays = _rays(2048, seed=2)
     got = _run(rdv, layers, rays, cuda_device, step_size=0.01, density_scale=1.5)
     ref = _oracle(layers, rays, 0.01, 1.5)
+    _check(got, ref, TOL_F16)
+
+
+def test_tensor_core_march_step_count_and_batches(rdv, cuda_device):
+    """float16 chains run the chunked tensor-core march: every step of a ray
+    is evaluated (Σ of the reference loop's step counts, no early exit), and
+    more rays than one batch (262,144) are processed in order."""
+    layers = _layers((3, 16, 1), "f16", seed=11, final_relu=True)
+    rays = _rays(300_000, seed=12)
+    node = rdv.RaymarchingTransmittance(_chain(rdv, layers, cuda_device), step_size=0.05, density_scale=1.0)
+    got = node(torch.from_numpy(rays).to(cuda_device)).as_tensor("torch")[:, 0].cpu().numpy()
+    ref = _oracle(layers, rays, 0.05, 1.0)
+    _check(got, ref, TOL_F16)
+    _, steps = orm.raymarching_transmittance(rays[:, :3], rays[:, 3:], 0.05, 0.0, orm.mlp_extinction(layers),
+                                             return_evaluations=True)
+    assert node.last_evaluations() == steps
+
+
+def test_mixed_precision_chain_runs_on_cuda_cores(rdv, cuda_device):
+    """A chain mixing exact and float16 layers takes the CUDA-core march with
+    float16 staging of the LinearFast layer's operands."""
+    layers = _layers((3, 32, 1), "f32", seed=13, final_relu=True)
+    layers[1]["math"] = "f16"
+    rays = _rays(1024, seed=14)
+    got = _run(rdv, layers, rays, cuda_device, step_size=0.02, density_scale=2.0)
+    ref = _oracle(layers, rays, 0.02, 2.0)
     _check(got, ref, TOL_F16)
 
 
