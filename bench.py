@@ -398,7 +398,7 @@ def run_ours(args, spec, world, rank, local):
                 "c3": run_c3(args, 1, 0, local, summary=True),
                 "c4": run_c4(args, 1, 0, local, summary=True),
                 "c5": mlp_summary(c5_spec()),
-                "transmittance": trm_summary(),
+                "transmittance": run_trm(args, 1, 0, local, summary=True),
             }
     print(json.dumps(line), flush=True)
 
@@ -678,13 +678,18 @@ def run_reference_c34(args):
         x_all, w33io, b = c3_data()
         cb = c3_cpu_baseline(x_all, w33io, b, seconds=max(5.0, float(args.steps)))
         metric, unit = "Winograd GB/s", "GB/s"
+    elif args.workload == "trm":
+        cb = trm_cpu_baseline(trm_layers())
+        metric, unit = "extinction evaluations/s", "evaluations/s"
     else:
         cb = c4_cpu_baseline(c4_layers())
         metric, unit = "ray-march frames/s", "frames/s"
     line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32" if args.workload == "c3" else "f16",
-            "data": "synthetic (seeded)", "config": {"workload": f"BASELINE config {args.workload[1]}"},
+            "data": "synthetic (seeded)",
+            "config": {"workload": "RaymarchingTransmittance" if args.workload == "trm"
+                       else f"BASELINE config {args.workload[1]}"},
             "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -694,38 +699,161 @@ def run_reference_c34(args):
 TRM = dict(width=1920, height=1080, dims=[3, 64, 64, 1], step=0.01, scale=1.0)
 
 
-def trm_summary(steps=3):
-    """Device-timed RaymarchingTransmittance over the config-4 camera's rays
-    (orbit pose 0, 1920x1080), extinction ReLU(MLP 3->64->64->1) with
-    LinearFast layers (Kaiming-normal, seeded), step 0.01, density scale 1."""
-    import rdv_project_b200 as rdv
-    from oracle import raymarch as orm
-
-    dev = torch.device("cuda", torch.cuda.current_device())
+def trm_layers():
     spec = dict(dims=TRM["dims"], math="f16", w_init="kaiming_normal")
     layers = make_weights(spec)
     for l in layers:
         l["relu"] = True  # ReLU after every layer: extinction >= 0
+    return layers
+
+
+def trm_flop():
+    d = TRM["dims"]
+    return 2 * sum(d[i] * d[i + 1] for i in range(len(d) - 1))
+
+
+def trm_rays():
+    from oracle import raymarch as orm
+
+    o, w = orm.camera_rays(orm.orbit_pose(0), TRM["width"], TRM["height"])
+    return torch.from_numpy(np.concatenate([o, w], axis=1).astype(np.float32))
+
+
+def run_trm(args, world, rank, local, summary=False):
+    """RaymarchingTransmittance (the reference's absorption sensor) over the
+    config-4 camera's rays, extinction ReLU(MLP 3->64->64->1) with LinearFast
+    layers (Kaiming-normal, seeded), step 0.01, density scale 1. Rays are
+    split in contiguous ranges over the ranks, one all-gather of T."""
+    import rdv_project_b200 as rdv
+    from rdv_project_b200 import _native as N
+    from rdv_project_b200.sharding import all_gather_rows, shard_range
+    from oracle import mlp as omlp
+    from oracle import raymarch as orm
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = trm_layers()
     node = rdv.RaymarchingTransmittance(build_map(rdv, layers, dev), step_size=TRM["step"],
                                         density_scale=TRM["scale"])
-    cams = rdv.Cameras(TRM["width"], TRM["height"], torch.from_numpy(orm.orbit_pose(0)[None]))
-    rays = cams().as_tensor("torch").reshape(-1, 6)
-    for _ in range(2):
-        node(rays)
+    rays_all = trm_rays()
+    n_all = rays_all.shape[0]
+    rb, re_ = shard_range(n_all, world, rank)
+    rays_host = rays_all[rb:re_].contiguous()
+    rays = rays_host.to(dev)
+    T_all = torch.empty((n_all, 1), device=dev) if world > 1 else None
+    state = {}
+
+    def march():
+        state["T"] = node(rays).as_tensor("torch")
+
+    def step():
+        march()
+        if world > 1:
+            all_gather_rows(state["T"], n_all, out=T_all)
+
+    steps = 3 if summary else args.steps
+    for _ in range(max(args.warmup, 3)):
+        step()
     torch.cuda.synchronize()
-    t = time_steps(lambda: node(rays), steps)
-    evals = node.last_evaluations()
-    d = TRM["dims"]
-    flop = 2 * sum(d[i] * d[i + 1] for i in range(len(d) - 1))
-    achieved = evals * flop / (t / steps) / 1e12  # MLP flops of the evaluated steps (padded widths not counted)
+    evals_rank = node.last_evaluations()
+    parity = (None, None)
+    if not args.profile_run:
+        mid = (TRM["height"] // 2) * TRM["width"]
+        if rb <= mid and mid + 2048 <= re_:
+            got = state["T"][mid - rb:mid - rb + 2048, 0].cpu().numpy()
+            lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
+            sample = rays_all[mid:mid + 2048].numpy()
+            ref = orm.raymarching_transmittance(sample[:, :3], sample[:, 3:], TRM["step"], TRM["scale"],
+                                                orm.mlp_extinction(lay_np))
+            parity = omlp.rel_errors(got, ref)
+    sampler = ClockSampler(local) if (rank == 0 and not summary) else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    l0 = N.launch_count()
+    t_kernel = time_steps(march, steps)
+    barrier(world)
+    t_step = time_steps(step, steps)
+    launches = N.launch_count() - l0
+    clocks = sampler.stop() if sampler else None
+    evals_total = evals_rank
+    if world > 1:
+        import torch.distributed as dist
+        tv = torch.tensor([evals_rank], dtype=torch.float64, device=dev)
+        dist.all_reduce(tv)
+        evals_total = int(tv.item())
+    t_kernel = max_over_ranks(t_kernel, world)
+    t_step = max_over_ranks(t_step, world)
     peaks, peak_kind = measured_peaks()
     peak = float(peaks.get("bf16_tflops", 1590.0))
-    return {"workload": "RaymarchingTransmittance, 1920x1080 camera rays (orbit pose 0), extinction "
-                        "ReLU(MLP 3->64->64->1) LinearFast (tensor-core march), step 0.01",
-            "metric": "extinction evaluations/s", "value": evals * steps / t, "ms_per_step": t / steps * 1e3,
-            "evaluations_per_step": evals, "rays": int(rays.shape[0]),
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "peak_source": f"{peak_kind} bf16_tflops"}}
+    achieved = evals_rank * trm_flop() / (t_kernel / steps) / 1e12  # rank 0's launches
+    value = evals_total * steps / t_step
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_source": f"{peak_kind} bf16_tflops",
+            "note": "MLP flops of the evaluated steps over the call's three launches (setup, fused MLP, combine)"}
+    if summary:
+        return {"workload": "RaymarchingTransmittance, 1920x1080 camera rays (orbit pose 0), extinction "
+                            "ReLU(MLP 3->64->64->1) LinearFast (tensor-core march), step 0.01",
+                "metric": "extinction evaluations/s", "value": value, "ms_per_step": t_step / steps * 1e3,
+                "evaluations_per_step": evals_total, "rays": n_all, "roofline": roof,
+                "parity_vs_oracle_2048_rays": {"normwise": parity[0], "elementwise": parity[1]}}
+    if rank != 0:
+        return None
+    roof["traffic"] = ncu_traffic("mlp_tc_march_trm")
+    roof["flops_per_launch"] = evals_rank * trm_flop()
+    line = {
+        "metric": "extinction evaluations/s", "value": value, "unit": "evaluations/s", "n_gpus": world,
+        "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": t_step / steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded weights, orbit pose 0 camera rays)",
+        "config": {"workload": "RaymarchingTransmittance (rdv/domain/volumes.py:124-141) over 1920x1080 pinhole "
+                               "rays, extinction ReLU(MLP 3->64->64->1) LinearFast, step 0.01, density scale 1",
+                   "rays": n_all, "evaluations_per_step": evals_total,
+                   "l2": "rays (12 MB) stay in L2 between steps; the work is the MLP per step",
+                   "parallelism": f"ray ranges over {world} rank(s), NCCL all-gather of T"},
+        "e2e": None,
+        "gpu_launches": int(launches),
+        "roofline": roof,
+        "parity": {"against": "oracle march of 2048 rays through the image middle", "normwise": parity[0],
+                   "elementwise": parity[1]},
+        "clocks": clocks,
+    }
+    if not args.profile_run:
+        # end to end: rays from pinned host memory, T back to pinned host memory
+        rays_pin = rays_host.pin_memory()
+        T_pin = torch.empty((re_ - rb, 1)).pin_memory()
+
+        def e2e_step():
+            rays.copy_(rays_pin, non_blocking=True)
+            march()
+            T_pin.copy_(state["T"], non_blocking=True)
+
+        k = max(1, min(args.steps, 5))
+        t_e2e = max_over_ranks(time_steps(e2e_step, k), world)
+        line["e2e"] = {"value": evals_total * k / t_e2e, "unit": "evaluations/s",
+                       "h2d_bytes_per_step": int(rays_pin.numel() * 4), "d2h_bytes_per_step": int(T_pin.numel() * 4)}
+        if world == 1:
+            line["cpu_baseline"] = trm_cpu_baseline(layers)
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def trm_cpu_baseline(layers, n=65536):
+    """Oracle restatement (numpy, the reference's per-step loop with early
+    exit, float16-staged MLP) on n rays through the image middle."""
+    from oracle import raymarch as orm
+
+    lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
+    rays = trm_rays()
+    mid = (TRM["height"] // 2) * TRM["width"]
+    sample = rays[mid:mid + n].numpy()
+    t0 = time.perf_counter()
+    _, evals = orm.raymarching_transmittance(sample[:, :3], sample[:, 3:], TRM["step"], TRM["scale"],
+                                             orm.mlp_extinction(lay_np), return_evaluations=True)
+    el = time.perf_counter() - t0
+    return {"value": evals / el, "unit": "evaluations/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} rays through the image middle ({evals} evaluations, {el:.1f} s, numpy/BLAS)"}
 
 
 def mlp_summary(spec, steps=5):
@@ -760,7 +888,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5", "trm"], default="c2")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows per GPU instead of the config's (small cases for ncu captures)")
     ap.add_argument("--no-secondary", action="store_true",
@@ -768,13 +896,13 @@ def main():
     ap.add_argument("--profile-run", action="store_true",
                     help="timed loop only: no parity check, end-to-end leg or CPU baseline")
     args = ap.parse_args()
-    if args.workload in ("c3", "c4"):
+    if args.workload in ("c3", "c4", "trm"):
         if args.impl == "reference":
             run_reference_c34(args)
             return
         world, rank, local = dist_setup(args.gpus)
         try:
-            (run_c3 if args.workload == "c3" else run_c4)(args, world, rank, local)
+            {"c3": run_c3, "c4": run_c4, "trm": run_trm}[args.workload](args, world, rank, local)
         finally:
             if world > 1:
                 import torch.distributed as dist
