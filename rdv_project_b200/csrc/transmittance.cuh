@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_co
     long long ray = -1;
     float x[3], w[3], d = 0.0f, tau = 0.0f;
     int steps = 0;
+    unsigned long long my_evals = 0;  // this thread's evaluations, added once at the end
     while (true) {
         if (ray < 0) {
             ray = atomicAdd(p.counter, 1);
@@ -240,10 +241,11 @@ __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_co
         }
         if (done) {
             p.out[ray] = result;
-            atomicAdd(p.evaluations, static_cast<unsigned long long>(steps));
+            my_evals += static_cast<unsigned long long>(steps);
             ray = -1;
         }
     }
+    if (my_evals) atomicAdd(p.evaluations, my_evals);
 }
 
 // ---------------------------------------------------------------------------
@@ -323,22 +325,29 @@ struct CombineParams {
 };
 
 __global__ void trm_combine_kernel(const __grid_constant__ CombineParams p) {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += gridDim.x * blockDim.x) {
-        const int n = p.rec[i].n_steps;
-        if (n == 0) continue;
-        const int base = p.rec[i].base;
-        const int nch = (n + mlp_tc::kTileM - 1) / mlp_tc::kTileM;
-        float tau = 0.0f, T = -1.0f;
-        for (int c = 0; c < nch; ++c) {
-            const float2 r = p.chunk_out[base + c];
-            if (tau + r.y > 16.0f) {
-                T = 0.0f;
-                break;
+    for (int base0 = blockIdx.x * blockDim.x; base0 < p.n; base0 += gridDim.x * blockDim.x) {
+        const int i = base0 + threadIdx.x;
+        unsigned n = 0;
+        if (i < p.n) {
+            n = static_cast<unsigned>(p.rec[i].n_steps);
+            if (n > 0) {
+                const int base = p.rec[i].base;
+                const int nch = (static_cast<int>(n) + mlp_tc::kTileM - 1) / mlp_tc::kTileM;
+                float tau = 0.0f, T = -1.0f;
+                for (int c = 0; c < nch; ++c) {
+                    const float2 r = p.chunk_out[base + c];
+                    if (tau + r.y > 16.0f) {
+                        T = 0.0f;
+                        break;
+                    }
+                    tau += r.x;
+                }
+                p.out[i] = T < 0.0f ? expf(-tau) : T;
             }
-            tau += r.x;
         }
-        p.out[i] = T < 0.0f ? expf(-tau) : T;
-        atomicAdd(p.evaluations, static_cast<unsigned long long>(n));
+        // one atomic per warp for the evaluation count
+        const unsigned warp_n = __reduce_add_sync(0xffffffffu, n);
+        if ((threadIdx.x & 31) == 0 && warp_n) atomicAdd(p.evaluations, static_cast<unsigned long long>(warp_n));
     }
 }
 
