@@ -99,7 +99,7 @@ class Conv2DTensorOp(TensorOperation):
         x = _f32_view(self.x_buf)
         w = _f32_view(self.weight)
         b = _f32_view(self.bias)
-        y = self.result._tensor
+        y = self._result._tensor
         N.check(N.lib().rdvb_conv2d_direct(
             x.data_ptr(), N.RDVB_F32, 1, self.H, self.W, self.CIN, self.COUT, self.KH, self.KW, w.data_ptr(),
             b.data_ptr(), y.data_ptr(), stream_handle()), "rdvb_conv2d_direct")
@@ -144,7 +144,7 @@ class Conv2DTensorOpWinograd3x3(TensorOperation):
     def _run(self):
         x = _f32_view(self.x_buf)
         b = _f32_view(self.bias)
-        _launch_winograd(x, 1, self.H, self.W, self.CIN, self.COUT, self._u_packed, b, self.result._tensor)
+        _launch_winograd(x, 1, self.H, self.W, self.CIN, self.COUT, self._u_packed, b, self._result._tensor)
 
 
 class Conv3x3Winograd:

@@ -9,6 +9,17 @@ upstream op in dependency order, ``as_type(backend)`` returns the result.
 Inputs are aliased, so an in-place edit of a leaf tensor followed by
 ``evaluate_chain()`` recomputes the pipeline, as in the reference.
 
+``evaluate_chain()`` runs each maximal run of linear / ReLU ops that feed
+only one another and share one arithmetic (all exact fp32, or all float16
+operands fitting the tensor-core kernel) as ONE fused rdvb_mlp_forward
+launch: the run's last op gets its result, the ops inside the run are
+marked stale and materialise on first use (``result``, ``as_type``, a
+downstream ``evaluate()`` or their own ``evaluate_chain()``). The fused
+launch computes the same values as the per-op dispatches: the fp32
+accumulator + bias of each layer is rounded once to the next layer's
+float16 operand either way (ReLU first), and exact fp32 layers keep their
+summation order.
+
 Operators and the kernels behind them:
 
 * ``ReLUTensorOp`` -> rdvb_relu.
@@ -49,6 +60,7 @@ class TensorOperation:
     _shape = None
     _upstream = None
     _extra_upstreams = ()
+    _stale = False
 
     def __init__(self, shape):
         cls = type(self)
@@ -58,22 +70,34 @@ class TensorOperation:
         self._shape = list(shape)
         self.shape = list(shape)
         dev = current_device()
-        self.result = RDVObject(torch.empty(self._shape, dtype=torch.float32, device=dev))
-        self._output_t = self.result
+        self._result = RDVObject(torch.empty(self._shape, dtype=torch.float32, device=dev))
+        self._output_t = self._result
         self.evaluate()
 
+    @property
+    def result(self) -> RDVObject:
+        if self._stale:
+            self.evaluate_chain()
+        return self._result
+
     def as_type(self, backend):
+        if self._stale:
+            self.evaluate_chain()
         return self._output_t.as_tensor(backend).reshape(self._shape)
 
     def evaluate(self):
+        for up in (self._upstream, *self._extra_upstreams):
+            if up is not None and up._stale:
+                up.evaluate_chain()
         with _timed():
             self._run()
+        self._stale = False
 
     def evaluate_chain(self):
         ops = []
         _collect_tensor_ops(self, set(), ops)
-        for op in ops:
-            op.evaluate()
+        with _timed():
+            _run_chain_fused(ops, self)
 
     def _run(self):  # pragma: no cover - abstract
         raise NotImplementedError
@@ -100,6 +124,103 @@ def _collect_tensor_ops(node, seen_ids, out):
     out.append(node)
 
 
+def _fusable(op) -> bool:
+    return isinstance(op, (_LinearOpBase, ReLUTensorOp))
+
+
+def _linear_math(run):
+    maths = {op._math for op in run if isinstance(op, _LinearOpBase)}
+    return maths.pop() if len(maths) == 1 else None
+
+
+def _tc_eligible(dims) -> bool:
+    return N.lib().rdvb_mlp_packed_bytes(len(dims) - 1, N.int_array(dims)) > 0
+
+
+def _run_chain_fused(ops, final) -> None:
+    """Dispatches `ops` (dependency order) with each fusable run as one
+    launch; see the module docstring."""
+    consumers = {id(op): 0 for op in ops}
+    for op in ops:
+        for up in (op._upstream, *op._extra_upstreams):
+            if up is not None and id(up) in consumers:
+                consumers[id(up)] += 1
+    i = 0
+    while i < len(ops):
+        run = [ops[i]]
+        if _fusable(ops[i]):
+            j = i
+            while j + 1 < len(ops):
+                a, b = ops[j], ops[j + 1]
+                if not (_fusable(b) and b._upstream is a and not b._extra_upstreams and consumers[id(a)] == 1
+                        and a is not final):
+                    break
+                cand = run + [b]
+                if _linear_math(cand) is None and any(isinstance(o, _LinearOpBase) for o in cand):
+                    break
+                run = cand
+                j += 1
+        if not _launch_fused(run):
+            for op in run:
+                op._run()
+                op._stale = False
+        i += len(run)
+
+
+def _launch_fused(run) -> bool:
+    """One rdvb_mlp_forward for a run of >= 2 ops holding >= 1 linear op;
+    False when the run is dispatched op by op instead."""
+    linears = [op for op in run if isinstance(op, _LinearOpBase)]
+    if len(run) < 2 or not linears or len(linears) > 16:
+        return False
+    input_relu = 0
+    layers = []  # [op, relu_after]
+    for op in run:
+        if isinstance(op, _LinearOpBase):
+            layers.append([op, False])
+        elif layers:
+            layers[-1][1] = True
+        else:
+            input_relu = 1
+    math = _linear_math(run)
+    dims = [layers[0][0].weight.shape[1]] + [op.weight.shape[0] for op, _ in layers]
+    if math != N.RDVB_MATH_F32 and not _tc_eligible(dims):
+        return False  # would run on the CUDA cores with a different summation order
+    first = run[0]
+    x = _f32_view(first.x_buf)
+    Ws, bs = [], []
+    for op, _ in layers:
+        W, b = op._prepare_weights()
+        Ws.append(W)
+        bs.append(b)
+    flags = [op._math | (N.RDVB_LAYER_RELU if relu else 0) for op, relu in layers]
+    last = run[-1]
+    packed = None
+    if math != N.RDVB_MATH_F32:
+        key = tuple((w.data_ptr(), w._version, b.data_ptr(), b._version) for w, b in zip(Ws, bs))
+        cache = last.__dict__.setdefault("_fused_pack", {})
+        packed = cache.get(key)
+        if packed is None:
+            lib = N.lib()
+            nbytes = lib.rdvb_mlp_packed_bytes(len(layers), N.int_array(dims))
+            packed = torch.empty(int(nbytes), dtype=torch.uint8, device=x.device)
+            N.check(lib.rdvb_mlp_pack(len(layers), N.int_array(dims), N.ptr_array([w.data_ptr() for w in Ws]),
+                                      N.ptr_array([b.data_ptr() for b in bs]), N.RDVB_F16, packed.data_ptr(),
+                                      stream_handle()), "rdvb_mlp_pack")
+            cache.clear()
+            cache[key] = packed
+    y = last._result._tensor
+    N.check(N.lib().rdvb_mlp_forward(
+        x.data_ptr(), N.RDVB_F32, x.shape[0], len(layers), N.int_array(dims),
+        N.ptr_array([w.data_ptr() for w in Ws]), N.ptr_array([b.data_ptr() for b in bs]), N.int_array(flags),
+        input_relu, 0, packed.data_ptr() if packed is not None else None, y.data_ptr(), stream_handle()),
+        "rdvb_mlp_forward")
+    for op in run[:-1]:
+        op._stale = True
+    last._stale = False
+    return True
+
+
 def _f32_view(obj: RDVObject) -> torch.Tensor:
     t = obj._tensor
     dev = current_device()
@@ -119,7 +240,7 @@ class ReLUTensorOp(TensorOperation):
 
     def _run(self):
         x = _f32_view(self.x_buf)
-        y = self.result._tensor
+        y = self._result._tensor
         N.check(N.lib().rdvb_relu(x.data_ptr(), y.data_ptr(), y.numel(), stream_handle()), "rdvb_relu")
 
 
@@ -180,7 +301,7 @@ class _LinearOpBase(TensorOperation):
     def _run(self):
         W, b = self._prepare_weights()
         x = _f32_view(self.x_buf)
-        y = self.result._tensor
+        y = self._result._tensor
         rc = N.lib().rdvb_mlp_forward(
             x.data_ptr(), N.RDVB_F32, x.shape[0], 1, N.int_array([W.shape[1], W.shape[0]]),
             N.ptr_array([W.data_ptr()]), N.ptr_array([b.data_ptr()]), N.int_array([self._math]), 0, 0,
