@@ -399,6 +399,7 @@ def run_ours(args, spec, world, rank, local):
                 "c4": run_c4(args, 1, 0, local, summary=True),
                 "c5": mlp_summary(c5_spec()),
                 "transmittance": run_trm(args, 1, 0, local, summary=True),
+                "tensor_op_chain": chain_summary(),
             }
     print(json.dumps(line), flush=True)
 
@@ -854,6 +855,46 @@ def trm_cpu_baseline(layers, n=65536):
     el = time.perf_counter() - t0
     return {"value": evals / el, "unit": "evaluations/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{n} rays through the image middle ({evals} evaluations, {el:.1f} s, numpy/BLAS)"}
+
+
+def chain_summary(rows=1 << 20, steps=3):
+    """TensorOperation pipeline of the config-2 architecture
+    (LinearTensorOpSmall / ReLUTensorOp, 17 ops) on `rows` rows: one dispatch
+    per op (each op reads and writes its fp32 result in HBM) against
+    evaluate_chain(), which runs the pipeline as one fused launch."""
+    import rdv_project_b200 as rdv
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    spec = c2_spec()
+    layers = make_weights(spec)
+    cur = make_input(spec, rows, seed=0).to(dev)
+    ops = []
+    for l in layers:
+        cur = rdv.LinearTensorOpSmall(cur, l["W"].to(dev), l["b"].to(dev))
+        ops.append(cur)
+        if l["relu"]:
+            cur = rdv.ReLUTensorOp(cur)
+            ops.append(cur)
+    final = ops[-1]
+
+    def per_op():
+        for op in ops:
+            op.evaluate()
+
+    for _ in range(2):
+        per_op()
+    torch.cuda.synchronize()
+    t_ops = time_steps(per_op, steps)
+    ref = final.as_type("torch").clone()
+    for _ in range(2):
+        final.evaluate_chain()
+    torch.cuda.synchronize()
+    t_fused = time_steps(final.evaluate_chain, steps)
+    same = bool(torch.equal(final.as_type("torch"), ref))
+    return {"workload": f"config-2 architecture as {len(ops)} TensorOperations (LinearTensorOpSmall, "
+                        f"ReLUTensorOp), {rows} rows",
+            "per_op_ms": t_ops / steps * 1e3, "evaluate_chain_ms": t_fused / steps * 1e3,
+            "speedup": t_ops / t_fused, "bit_identical": same}
 
 
 def mlp_summary(spec, steps=5):

@@ -189,6 +189,39 @@ __device__ __forceinline__ int tile_of(int r, int s, int n_tiles) {
     return t < n_tiles ? t : -1;
 }
 
+// Exactly KS K-step MMAs of one layer for one slot: A from the slot's
+// shared-memory tile (SS) or from its TMEM activations (TS). The MMAs are
+// straight-line code selected by a switch on the layer's K steps: in a fixed
+// 8-step unrolled loop, a step skipped by its runtime condition measured
+// about as expensive for the issuing thread as an issued MMA (~140 cycles),
+// up to ~500 cycles per layer of a narrow chain.
+template <int KS>
+__device__ __forceinline__ void issue_ks(bool ts, uint32_t d, uint64_t a0_desc, uint32_t a_tm,
+                                         const uint64_t (&b)[8], uint32_t idesc) {
+    if (ts) {
+#pragma unroll
+        for (int j = 0; j < KS; ++j) umma_f16_ts(d, a_tm + j * 8u, b[j], idesc, j > 0 ? 1u : 0u);
+    } else {
+#pragma unroll
+        for (int j = 0; j < KS; ++j)
+            umma_f16(d, a0_desc + (j >> 2) * (kAtomBytes >> 4) + (j & 3) * 2, b[j], idesc, j > 0 ? 1u : 0u);
+    }
+}
+
+__device__ __forceinline__ void issue_layer(uint32_t ksteps, bool ts, uint32_t d, uint64_t a0_desc, uint32_t a_tm,
+                                            const uint64_t (&b)[8], uint32_t idesc) {
+    switch (ksteps) {
+        case 1: issue_ks<1>(ts, d, a0_desc, a_tm, b, idesc); break;
+        case 2: issue_ks<2>(ts, d, a0_desc, a_tm, b, idesc); break;
+        case 3: issue_ks<3>(ts, d, a0_desc, a_tm, b, idesc); break;
+        case 4: issue_ks<4>(ts, d, a0_desc, a_tm, b, idesc); break;
+        case 5: issue_ks<5>(ts, d, a0_desc, a_tm, b, idesc); break;
+        case 6: issue_ks<6>(ts, d, a0_desc, a_tm, b, idesc); break;
+        case 7: issue_ks<7>(ts, d, a0_desc, a_tm, b, idesc); break;
+        default: issue_ks<8>(ts, d, a0_desc, a_tm, b, idesc); break;
+    }
+}
+
 // + fp32 bias of the chunk's 16 columns (shared memory, broadcast to all
 // lanes), in place on the raw accumulator words.
 __device__ __forceinline__ void add_bias16(uint32_t (&v)[16], const float* b) {
@@ -565,15 +598,21 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                             aph ^= 1u << s;
                         }
                         tc_fence_after();
-                        if (l == 0) {
-                            // input layer: A from the staged shared-memory tile
+                        // input layer: A from the staged shared-memory tile; hidden
+                        // layers: A = previous activations, resident in TMEM.
+                        // Resident-weight chains (two issuers, mostly narrow
+                        // layers) issue exactly ksteps MMAs; the streamed-weight
+                        // kernel keeps the fixed 8-step loop, which measured
+                        // faster for its 8-step layers.
+                        if constexpr (ISSUERS == 2) {
+                            issue_layer(ksteps, l > 0, d_tm[s], a0_desc[s], a_tm[s], b_desc, idesc);
+                        } else if (l == 0) {
 #pragma unroll
                             for (int j = 0; j < 8; ++j)
                                 if (j < static_cast<int>(ksteps))
                                     umma_f16(d_tm[s], a0_desc[s] + (j >> 2) * (kAtomBytes >> 4) + (j & 3) * 2,
                                              b_desc[j], idesc, j > 0 ? 1u : 0u);
                         } else {
-                            // hidden layers: A = previous activations, resident in TMEM
 #pragma unroll
                             for (int j = 0; j < 8; ++j)
                                 if (j < static_cast<int>(ksteps))
