@@ -181,6 +181,33 @@ int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int c
 int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
                        const float* weight, const float* bias, float* y, void* stream);
 
+/* The same convolution with the operands rounded first: math RDVB_MATH_F16 /
+ * RDVB_MATH_BF16 rounds x and w to float16 / bfloat16 (products exact in
+ * fp32, fp32 accumulation), RDVB_MATH_F32 is rdvb_conv2d_direct. bias_first:
+ * the bias seeds the accumulator (Conv2DTensorOpSimple, Simple3x3, Window3x3:
+ * rdv/domain/nn.py:669-999, rdv/shaders/tensors/conv2d_tensor_op_simple.h,
+ * conv2d_tensor_op_simple3x3.h, conv2d_tensor_op_window3x3.h) or, with 0, is
+ * added after the sum (Conv2DTensorOpFast: nn.py:608-666,
+ * conv2d_tensor_op_fast.h). */
+int rdvb_conv2d_direct_staged(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
+                              const float* weight, const float* bias, int math, int bias_first, float* y,
+                              void* stream);
+
+/* 2x2 average pool, stride 2 (Downsample2xTensorOp, rdv/domain/nn.py:1090-1107,
+ * rdv/shaders/tensors/downsample2x_tensor_op.h): x [h, w, c] fp32 -> y
+ * [h/2, w/2, c], each output ((x00 + x01) + x10) + x11, times 0.25. h, w even;
+ * c a multiple of 8; x, y 16-byte aligned. */
+int rdvb_downsample2x(const float* x, int h, int w, int c, float* y, void* stream);
+
+/* Nearest-neighbour 2x upsample (Upsample2xTensorOp, nn.py:1110-1124,
+ * rdv/shaders/tensors/upsample2x_tensor_op.h): x [h, w, c] -> y [2h, 2w, c]. */
+int rdvb_upsample2x(const float* x, int h, int w, int c, float* y, void* stream);
+
+/* Channel concatenation (ConcatTensorOp, nn.py:1127-1150,
+ * rdv/shaders/tensors/concat_tensor_op.h): x1 [rows, c1] | x2 [rows, c2] ->
+ * y [rows, c1 + c2]; c1, c2 multiples of 8; 16-byte aligned pointers. */
+int rdvb_concat_channels(const float* x1, int c1, const float* x2, int c2, int64_t rows, float* y, void* stream);
+
 /* ---------------------------------------------------------- ray-march ----
  * Pinhole camera rays through a volume whose density and colour come from an
  * MLP, rendered front to back.

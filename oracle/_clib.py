@@ -71,8 +71,12 @@ def ref_lib() -> ctypes.CDLL:
         lib.ref_winograd_inv.argtypes = [vp, vp]
         lib.ref_transmittance_rm.argtypes = [f32, f32, vp, vp, f32, f32, f32]
         lib.ref_transmittance_rm.restype = f32
+        lib.ref_downsample2x.argtypes = [vp, i32, i32, i32, vp]
+        lib.ref_upsample2x.argtypes = [vp, i32, i32, i32, vp]
+        lib.ref_concat.argtypes = [vp, i32, vp, i32, i32, vp]
         for name in ("ref_mlp_c1", "ref_mlp_small", "ref_linear_tensor_op_16_24", "ref_relu_tensor_op",
-                     "ref_conv2d_tensor_op_3x3_16_32_16x16", "ref_winograd_fwd", "ref_winograd_inv"):
+                     "ref_conv2d_tensor_op_3x3_16_32_16x16", "ref_winograd_fwd", "ref_winograd_inv",
+                     "ref_downsample2x", "ref_upsample2x", "ref_concat"):
             getattr(lib, name).restype = None
         _ref = lib
     return _ref

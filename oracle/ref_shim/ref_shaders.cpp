@@ -176,6 +176,27 @@ struct ConvTO { int shape[2]; float* result; float* x_buf; float* weight; float*
 #undef H
 #undef W
 
+// Resampling and concatenation (tensors/downsample2x_tensor_op.h,
+// upsample2x_tensor_op.h, concat_tensor_op.h): one 4x8 tile per invocation.
+// (each reference megakernel holds one op's code; conv2d_tensor_op.h's
+// helper macro is dropped so these files' own local variable of that name
+// compile.)
+#undef col_blocks
+struct DownTO { int shape[2]; float* result; float* x_buf; int W; };
+#define RDV_NODE DownTO
+#include "tensors/downsample2x_tensor_op.h"
+#undef RDV_NODE
+
+struct UpTO { int shape[2]; float* result; float* x_buf; int W; };
+#define RDV_NODE UpTO
+#include "tensors/upsample2x_tensor_op.h"
+#undef RDV_NODE
+
+struct CatTO { int shape[2]; float* result; float* x1_buf; float* x2_buf; int C1; };
+#define RDV_NODE CatTO
+#include "tensors/concat_tensor_op.h"
+#undef RDV_NODE
+
 // Winograd transforms: the cooperative-matrix forward() of this file is
 // compiled out (RDV_COOPERATIVE_MATRIX_SUPPORT undefined), leaving the two
 // scalar transforms _winograd_fwd / _winograd_inv.
@@ -265,6 +286,34 @@ void ref_conv2d_tensor_op_3x3_16_32_16x16(const float* x, const float* w, const 
     node.result = y; node.x_buf = const_cast<float*>(x);
     node.weight = const_cast<float*>(w); node.bias = const_cast<float*>(b);
     int tiles = (16 * 16 / 4) * (32 / 8);
+    for (int t = 0; t < tiles; ++t) { gl_GlobalInvocationID.x = t; forward(node); }
+}
+
+// Downsample2xTensorOp: x [h*w, c] -> y [(h/2)*(w/2), c]; (h/2)*(w/2) a
+// multiple of 4, c a multiple of 8.
+void ref_downsample2x(const float* x, int h, int w, int c, float* y) {
+    DownTO node;
+    node.shape[0] = (h / 2) * (w / 2); node.shape[1] = c;
+    node.result = y; node.x_buf = const_cast<float*>(x); node.W = w / 2;
+    int tiles = (node.shape[0] / 4) * (c / 8);
+    for (int t = 0; t < tiles; ++t) { gl_GlobalInvocationID.x = t; forward(node); }
+}
+
+// Upsample2xTensorOp: x [h*w, c] -> y [(2h)*(2w), c].
+void ref_upsample2x(const float* x, int h, int w, int c, float* y) {
+    UpTO node;
+    node.shape[0] = (2 * h) * (2 * w); node.shape[1] = c;
+    node.result = y; node.x_buf = const_cast<float*>(x); node.W = 2 * w;
+    int tiles = (node.shape[0] / 4) * (c / 8);
+    for (int t = 0; t < tiles; ++t) { gl_GlobalInvocationID.x = t; forward(node); }
+}
+
+// ConcatTensorOp: x1 [rows, c1] | x2 [rows, c2] -> y [rows, c1 + c2].
+void ref_concat(const float* x1, int c1, const float* x2, int c2, int rows, float* y) {
+    CatTO node;
+    node.shape[0] = rows; node.shape[1] = c1 + c2;
+    node.result = y; node.x1_buf = const_cast<float*>(x1); node.x2_buf = const_cast<float*>(x2); node.C1 = c1;
+    int tiles = (rows / 4) * ((c1 + c2) / 8);
     for (int t = 0; t < tiles; ++t) { gl_GlobalInvocationID.x = t; forward(node); }
 }
 

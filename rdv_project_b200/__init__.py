@@ -12,8 +12,10 @@ Every operator launches hand-written sm_100a kernels from the in-tree
 from .core import (RDVObject, wrap, profiling, reset_submit_times, profiling_submit_times)
 from .maps import (Map, Identity, X, ReLU, relu, Linear, LinearFast, LinearFastBF16, linear, Composite)
 from .tensor_ops import (TensorOperation, ReLUTensorOp, LinearTensorOp, LinearTensorOpFast, LinearTensorOpMine,
-                         LinearTensorOpSimple, LinearTensorOpSmall)
-from .conv import (Conv2DTensorOp, Conv2DTensorOpWinograd3x3, Conv3x3Winograd, conv2d_direct,
+                         LinearTensorOpSimple, LinearTensorOpSmall, Downsample2xTensorOp, Upsample2xTensorOp,
+                         ConcatTensorOp)
+from .conv import (Conv2DTensorOp, Conv2DTensorOpFast, Conv2DTensorOpSimple, Conv2DTensorOpSimple3x3,
+                   Conv2DTensorOpWindow3x3, Conv2DTensorOpWinograd3x3, Conv3x3Winograd, conv2d_direct,
                    _winograd_transform_weight)
 from .rendering import Cameras, VolumeRenderer
 from .volumes import RaymarchingTransmittance
@@ -23,8 +25,9 @@ __all__ = [
     "RDVObject", "wrap", "profiling", "reset_submit_times", "profiling_submit_times",
     "Map", "Identity", "X", "ReLU", "relu", "Linear", "LinearFast", "LinearFastBF16", "linear", "Composite",
     "TensorOperation", "ReLUTensorOp", "LinearTensorOp", "LinearTensorOpFast", "LinearTensorOpMine",
-    "LinearTensorOpSimple", "LinearTensorOpSmall",
-    "Conv2DTensorOp", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
+    "LinearTensorOpSimple", "LinearTensorOpSmall", "Downsample2xTensorOp", "Upsample2xTensorOp", "ConcatTensorOp",
+    "Conv2DTensorOp", "Conv2DTensorOpFast", "Conv2DTensorOpSimple", "Conv2DTensorOpSimple3x3",
+    "Conv2DTensorOpWindow3x3", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
     "Cameras", "VolumeRenderer", "RaymarchingTransmittance",
     "RdvbError", "device_status",
 ]

@@ -41,6 +41,11 @@ SIGNATURES = {
                                        _c_int, _vp]),
     "rdvb_conv2d_direct": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
                                     _vp, _vp]),
+    "rdvb_conv2d_direct_staged": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                           _vp, _vp, _c_int, _c_int, _vp, _vp]),
+    "rdvb_downsample2x": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp]),
+    "rdvb_upsample2x": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp]),
+    "rdvb_concat_channels": (_c_int, [_vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "rdvb_camera_rays": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_f, _c_f, _vp, _vp]),
     "rdvb_raymarch_workspace_bytes": (_c_i64, [_c_int, _c_int]),
     "rdvb_raymarch_render": (_c_int, [_vp, _c_int, _c_int, _c_f, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int, _c_int,

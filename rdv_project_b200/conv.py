@@ -4,6 +4,12 @@ operator.
 
 * ``Conv2DTensorOp(x, weight, bias, H, W)``: 'same', stride-1 KHxKW
   convolution in exact fp32 (CUDA cores) -> rdvb_conv2d_direct.
+* ``Conv2DTensorOpFast`` / ``Conv2DTensorOpSimple`` / ``Conv2DTensorOpSimple3x3``
+  / ``Conv2DTensorOpWindow3x3(x, weight, bias, H, W)`` (nn.py:608-999): the
+  reference's tensor-core direct convolutions -- x and weight rounded to
+  float16, fp32 accumulation, the bias seeding the accumulator (Simple*,
+  Window3x3) or added after (Fast) -> rdvb_conv2d_direct_staged, with each
+  op's own shape assertions.
 * ``Conv2DTensorOpWinograd3x3(x, weight, bias, H, W)``: Winograd F(2x2,3x3)
   -> rdvb_winograd_filter_transform (once, at construction, like the
   reference's ``_winograd_transform_weight``) + rdvb_conv3x3_winograd.
@@ -27,7 +33,7 @@ import torch
 
 from . import _native as N
 from .core import RDVObject, _timed, current_device, stream_handle, wrap
-from .tensor_ops import TensorOperation, _as_op_input, _f32_view
+from .tensor_ops import TensorOperation, _as_op_input, _f32_view, _max_subgroups
 
 _DTYPES = {torch.float32: N.RDVB_F32, torch.float16: N.RDVB_F16}
 MAX_WINOGRAD_CHANNELS = 64
@@ -103,6 +109,128 @@ class Conv2DTensorOp(TensorOperation):
         N.check(N.lib().rdvb_conv2d_direct(
             x.data_ptr(), N.RDVB_F32, 1, self.H, self.W, self.CIN, self.COUT, self.KH, self.KW, w.data_ptr(),
             b.data_ptr(), y.data_ptr(), stream_handle()), "rdvb_conv2d_direct")
+
+
+class _StagedConv(TensorOperation):
+    """Shared body of the reference's tensor-core direct convolutions:
+    x [H*W, in_channels], weight [KH, KW, in_channels, out_channels], bias
+    [out_channels]; x and weight rounded to float16, fp32 accumulation over
+    (kh, kw, cin), the bias seeding the accumulator or added after
+    (rdvb_conv2d_direct_staged)."""
+
+    _TILE_ROWS = 32
+    _TILE_COLS = 16
+    _bias_first = True
+    _name = "Conv2DTensorOp"
+
+    def _check(self, x, weight, bias, H, W, fixed_3x3=False):
+        data, shape, upstream = _as_op_input(x)
+        assert len(shape) == 2, f"{self._name} requires a 2D (H*W, in_channels) input"
+        hw, in_channels = shape
+        assert hw == H * W, f"H*W ({H * W}) must match x's own row count ({hw})"
+        weight = weight if isinstance(weight, RDVObject) else wrap(weight)
+        bias = bias if isinstance(bias, RDVObject) else wrap(bias)
+        if fixed_3x3:
+            assert tuple(weight.shape[:2]) == (3, 3), "weight must be [3, 3, in_channels, out_channels]"
+        else:
+            assert len(weight.shape) == 4, "weight must be [KH, KW, in_channels, out_channels]"
+        kh, kw, weight_in_channels, out_channels = weight.shape
+        assert weight_in_channels == in_channels, "weight's own in_channels must match x's own trailing dim"
+        assert tuple(bias.shape) == (out_channels,), "bias must be [out_channels]"
+        return data, upstream, hw, in_channels, out_channels, kh, kw, weight, bias
+
+    def _setup(self, data, upstream, hw, cin, cout, kh, kw, weight, bias, H, W):
+        self.KH, self.KW, self.CIN, self.COUT, self.H, self.W = kh, kw, cin, cout, H, W
+        self.x_buf = data
+        self.weight = weight
+        self.bias = bias
+        self._upstream = upstream
+        TensorOperation.__init__(self, [hw, cout])
+
+    def _run(self):
+        x = _f32_view(self.x_buf)
+        w = _f32_view(self.weight)
+        b = _f32_view(self.bias)
+        y = self._result._tensor
+        N.check(N.lib().rdvb_conv2d_direct_staged(
+            x.data_ptr(), N.RDVB_F32, 1, self.H, self.W, self.CIN, self.COUT, self.KH, self.KW, w.data_ptr(),
+            b.data_ptr(), N.RDVB_MATH_F16, int(self._bias_first), y.data_ptr(), stream_handle()),
+            "rdvb_conv2d_direct_staged")
+
+
+class Conv2DTensorOpFast(_StagedConv):
+    """'same'-padded, stride-1 KHxKW convolution with float16 operands and
+    fp32 accumulation, bias added after the sum (rdv/domain/nn.py:608-666,
+    rdv/shaders/tensors/conv2d_tensor_op_fast.h)."""
+
+    _bias_first = False
+    _name = "Conv2DTensorOpFast"
+
+    def __init__(self, x, weight, bias, H: int, W: int) -> None:
+        data, up, hw, cin, cout, kh, kw, weight, bias = self._check(x, weight, bias, H, W)
+        assert cin % 16 == 0, f"in_channels ({cin}) must be a multiple of 16"
+        assert cout % 16 == 0, f"out_channels ({cout}) must be a multiple of 16"
+        self._setup(data, up, hw, cin, cout, kh, kw, weight, bias, H, W)
+
+
+class Conv2DTensorOpSimple(_StagedConv):
+    """'same'-padded, stride-1 KHxKW convolution with float16 operands, the
+    fp32 accumulator seeded with the bias (rdv/domain/nn.py:669-754,
+    rdv/shaders/tensors/conv2d_tensor_op_simple.h)."""
+
+    _name = "Conv2DTensorOpSimple"
+
+    def __init__(self, x, weight, bias, H: int, W: int) -> None:
+        data, up, hw, cin, cout, kh, kw, weight, bias = self._check(x, weight, bias, H, W)
+        assert hw % 32 == 0, f"H*W ({hw}) must be a multiple of 32"
+        assert cin % 16 == 0, f"in_channels ({cin}) must be a multiple of 16"
+        assert cout % 16 == 0, f"out_channels ({cout}) must be a multiple of 16"
+        self._setup(data, up, hw, cin, cout, kh, kw, weight, bias, H, W)
+
+
+class Conv2DTensorOpSimple3x3(_StagedConv):
+    """'same'-padded, stride-1 3x3 convolution with float16 operands, the
+    fp32 accumulator seeded with the bias (rdv/domain/nn.py:757-848,
+    rdv/shaders/tensors/conv2d_tensor_op_simple3x3.h)."""
+
+    _name = "Conv2DTensorOpSimple3x3"
+
+    def __init__(self, x, weight, bias, H: int, W: int) -> None:
+        data, up, hw, cin, cout, kh, kw, weight, bias = self._check(x, weight, bias, H, W, fixed_3x3=True)
+        assert hw % 32 == 0, f"H*W ({hw}) must be a multiple of 32"
+        assert cin % 16 == 0, f"in_channels ({cin}) must be a multiple of 16"
+        assert cout % 16 == 0, f"out_channels ({cout}) must be a multiple of 16"
+        # the reference's subgroups-per-tile choice (nn.py:830-838); the B200
+        # kernel does not use it
+        tap_k = 9 * cin
+        self.SPT = _max_subgroups(fixed_bytes=32 * tap_k * 2, per_subgroup_bytes=16 * tap_k * 2,
+                                  divides=lambda s: cout % (16 * s) == 0)
+        self._setup(data, up, hw, cin, cout, kh, kw, weight, bias, H, W)
+
+
+class Conv2DTensorOpWindow3x3(_StagedConv):
+    """'same'-padded, stride-1 3x3 convolution over 8x8 output windows with
+    float16 operands, the fp32 accumulator seeded with the bias
+    (rdv/domain/nn.py:851-999, rdv/shaders/tensors/conv2d_tensor_op_window3x3.h).
+    The reference's separate zero-padding pass into a temporary buffer is not
+    needed here: the kernel skips taps outside the image."""
+
+    _TILE_ROWS = 1
+    _TILE_COLS = 16
+    _WIN = 8
+    _name = "Conv2DTensorOpWindow3x3"
+
+    def __init__(self, x, weight, bias, H: int, W: int) -> None:
+        data, up, hw, cin, cout, kh, kw, weight, bias = self._check(x, weight, bias, H, W, fixed_3x3=True)
+        assert H % self._WIN == 0, f"H ({H}) must be a multiple of {self._WIN}"
+        assert W % self._WIN == 0, f"W ({W}) must be a multiple of {self._WIN}"
+        assert cin % 16 == 0, f"in_channels ({cin}) must be a multiple of 16"
+        assert cout % 16 == 0, f"out_channels ({cout}) must be a multiple of 16"
+        assert cin <= 64, f"in_channels ({cin}) must be at most 64 (see this op's own docstring)"
+        fetch = self._WIN + 2
+        shared_bytes = (fetch * fetch * cin + 16 * 9 * cin) * 2 + 64 * 16 * 2 + 64 * 16 * 4
+        assert shared_bytes <= 49152, f"in_channels ({cin}) needs {shared_bytes} bytes of shared memory (48KB budget)"
+        self._setup(data, up, hw, cin, cout, kh, kw, weight, bias, H, W)
 
 
 class Conv2DTensorOpWinograd3x3(TensorOperation):

@@ -20,6 +20,7 @@
 #include "winograd.cuh"
 #include "raymarch.cuh"
 #include "transmittance.cuh"
+#include "resample.cuh"
 
 namespace {
 
@@ -568,10 +569,13 @@ int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int c
     return check_launch("winograd_f23_kernel");
 }
 
-int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
-                       const float* weight, const float* bias, float* y, void* stream) {
+int rdvb_conv2d_direct_staged(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
+                              const float* weight, const float* bias, int math, int bias_first, float* y,
+                              void* stream) {
     if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16)
         return fail(RDVB_ERR_INVALID_ARG, "x_dtype must be RDVB_F32 or RDVB_F16");
+    if (math != RDVB_MATH_F32 && math != RDVB_MATH_F16 && math != RDVB_MATH_BF16)
+        return fail(RDVB_ERR_INVALID_ARG, "math must be RDVB_MATH_F32, _F16 or _BF16");
     if (n < 0 || h < 0 || w < 0) return fail(RDVB_ERR_INVALID_ARG, "n, h, w must be >= 0");
     if (cin < 1 || cout < 8 || cout % 8 != 0)
         return fail(RDVB_ERR_INVALID_ARG, "cin must be >= 1 and cout a positive multiple of 8 (got %d, %d)", cin, cout);
@@ -587,12 +591,78 @@ int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin,
     const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + threads - 1) / threads,
                                                                                dev->sm_count * 32LL)));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (x_dtype == RDVB_F16)
-        rdvb::wino::conv2d_direct_kernel<true><<<blocks, threads, 0, st>>>(x, weight, bias, y, n, h, w, cin, cout, kh, kw);
-    else
-        rdvb::wino::conv2d_direct_kernel<false><<<blocks, threads, 0, st>>>(x, weight, bias, y, n, h, w, cin, cout, kh,
-                                                                            kw);
+    using rdvb::wino::conv2d_direct_kernel;
+    const bool x16 = x_dtype == RDVB_F16;
+    const bool bf = bias_first != 0;
+#define RDVB_CONV(X, M, B) conv2d_direct_kernel<X, M, B><<<blocks, threads, 0, st>>>(x, weight, bias, y, n, h, w, cin, cout, kh, kw)
+    if (math == RDVB_MATH_F32) {
+        x16 ? RDVB_CONV(true, 0, true) : RDVB_CONV(false, 0, true);
+    } else if (math == RDVB_MATH_F16) {
+        if (bf) x16 ? RDVB_CONV(true, 1, true) : RDVB_CONV(false, 1, true);
+        else x16 ? RDVB_CONV(true, 1, false) : RDVB_CONV(false, 1, false);
+    } else {
+        if (bf) x16 ? RDVB_CONV(true, 2, true) : RDVB_CONV(false, 2, true);
+        else x16 ? RDVB_CONV(true, 2, false) : RDVB_CONV(false, 2, false);
+    }
+#undef RDVB_CONV
     return check_launch("conv2d_direct_kernel");
+}
+
+int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
+                       const float* weight, const float* bias, float* y, void* stream) {
+    return rdvb_conv2d_direct_staged(x, x_dtype, n, h, w, cin, cout, kh, kw, weight, bias, RDVB_MATH_F32, 1, y,
+                                     stream);
+}
+
+namespace {
+int resample_grid(long long items, DeviceInfo* dev) {
+    return static_cast<int>(std::max<long long>(1, std::min<long long>((items + 255) / 256, dev->sm_count * 16LL)));
+}
+int check_rows_channels(const void* a, const void* b, int c) {
+    if (c < 8 || c % 8 != 0) return fail(RDVB_ERR_INVALID_ARG, "channels must be a positive multiple of 8 (got %d)", c);
+    if (!a || !b) return fail(RDVB_ERR_INVALID_ARG, "x and y must not be NULL");
+    if (!aligned(a, 16) || !aligned(b, 16)) return fail(RDVB_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
+    return RDVB_OK;
+}
+}  // namespace
+
+int rdvb_downsample2x(const float* x, int h, int w, int c, float* y, void* stream) {
+    if (h < 0 || w < 0 || h % 2 || w % 2) return fail(RDVB_ERR_INVALID_ARG, "h and w must be even and >= 0");
+    if (h == 0 || w == 0) return RDVB_OK;
+    if (int rc = check_rows_channels(x, y, c)) return rc;
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const long long items = static_cast<long long>(h / 2) * (w / 2) * (c / 8);
+    rdvb::resample::downsample2x_kernel<<<resample_grid(items, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, y, h, w, c);
+    return check_launch("downsample2x_kernel");
+}
+
+int rdvb_upsample2x(const float* x, int h, int w, int c, float* y, void* stream) {
+    if (h < 0 || w < 0) return fail(RDVB_ERR_INVALID_ARG, "h and w must be >= 0");
+    if (h == 0 || w == 0) return RDVB_OK;
+    if (int rc = check_rows_channels(x, y, c)) return rc;
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const long long items = 4LL * h * w * (c / 8);
+    rdvb::resample::upsample2x_kernel<<<resample_grid(items, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, y, h, w, c);
+    return check_launch("upsample2x_kernel");
+}
+
+int rdvb_concat_channels(const float* x1, int c1, const float* x2, int c2, int64_t rows, float* y, void* stream) {
+    if (rows < 0) return fail(RDVB_ERR_INVALID_ARG, "rows must be >= 0");
+    if (c1 < 8 || c1 % 8 || c2 < 8 || c2 % 8)
+        return fail(RDVB_ERR_INVALID_ARG, "c1 and c2 must be positive multiples of 8 (got %d, %d)", c1, c2);
+    if (rows == 0) return RDVB_OK;
+    if (int rc = check_rows_channels(x1, y, c1 + c2)) return rc;
+    if (!x2 || !aligned(x2, 16)) return fail(RDVB_ERR_INVALID_ARG, "x2 must be a 16-byte aligned pointer");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const long long items = rows * ((c1 + c2) / 8);
+    rdvb::resample::concat_kernel<<<resample_grid(items, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x1, x2, y, rows, c1, c2);
+    return check_launch("concat_kernel");
 }
 
 }  // extern "C"

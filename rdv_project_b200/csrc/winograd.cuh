@@ -497,11 +497,27 @@ __global__ void winograd_f23_filter_kernel(const float* __restrict__ w33io, int 
     }
 }
 
-// 'Same' (zero padding KH/2, KW/2), stride-1 direct convolution in fp32:
-// acc = bias; acc += x * w over (kh, kw, cin) in that order, one fused
-// multiply-add per tap (Conv2DTensorOp, rdv/shaders/tensors/conv2d_tensor_op.h:21-87).
+// Operand staging of the direct convolution: 0 exact fp32, 1 float16,
+// 2 bfloat16 (round to nearest even, value kept in fp32).
+template <int MATH>
+__device__ __forceinline__ float conv_stage(float v) {
+    if constexpr (MATH == 1) return __half2float(__float2half_rn(v));
+    if constexpr (MATH == 2) return __bfloat162float(__float2bfloat16_rn(v));
+    return v;
+}
+
+// 'Same' (zero padding KH/2, KW/2), stride-1 direct convolution: acc over
+// (kh, kw, cin) in that order, one fused multiply-add per tap, fp32
+// accumulation. MATH 0 is Conv2DTensorOp's exact fp32 arithmetic (acc =
+// bias first, rdv/shaders/tensors/conv2d_tensor_op.h:21-87); MATH 1 / 2
+// round x and w to float16 / bfloat16 first (products exact in fp32), the
+// reference's tensor-core conv ops: bias seeding the accumulator
+// (BIAS_FIRST: Conv2DTensorOpSimple, Simple3x3, Window3x3 --
+// conv2d_tensor_op_simple.h:108-117, conv2d_tensor_op_simple3x3.h:98-102,
+// conv2d_tensor_op_window3x3.h:160-165) or added after the sum
+// (Conv2DTensorOpFast, conv2d_tensor_op_fast.h:100-104).
 // One thread per (pixel, 8 output channels). x float32 or float16.
-template <bool X16>
+template <bool X16, int MATH, bool BIAS_FIRST>
 __global__ void conv2d_direct_kernel(const void* __restrict__ x, const float* __restrict__ wt,
                                      const float* __restrict__ bias, float* __restrict__ y, int n, int h, int w,
                                      int cin, int cout, int kh_n, int kw_n) {
@@ -517,7 +533,7 @@ __global__ void conv2d_direct_kernel(const void* __restrict__ x, const float* __
         const long long img = t / h;
         float acc[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) acc[c] = bias ? bias[c0 + c] : 0.0f;
+        for (int c = 0; c < 8; ++c) acc[c] = (bias && BIAS_FIRST) ? bias[c0 + c] : 0.0f;
         for (int kh = 0; kh < kh_n; ++kh) {
             const int ih = oh + kh - kh_n / 2;
             if (ih < 0 || ih >= h) continue;
@@ -527,21 +543,25 @@ __global__ void conv2d_direct_kernel(const void* __restrict__ x, const float* __
                 const long long xin = ((img * h + ih) * w + iw) * cin;
                 const float* wk = wt + static_cast<long long>(kh * kw_n + kw) * cin * cout + c0;
                 for (int k = 0; k < cin; ++k) {
-                    const float xv = X16 ? __half2float(static_cast<const __half*>(x)[xin + k])
-                                         : static_cast<const float*>(x)[xin + k];
+                    const float xv = conv_stage<MATH>(X16 ? __half2float(static_cast<const __half*>(x)[xin + k])
+                                                          : static_cast<const float*>(x)[xin + k]);
                     const float4 wa = __ldg(reinterpret_cast<const float4*>(wk + static_cast<long long>(k) * cout));
                     const float4 wb =
                         __ldg(reinterpret_cast<const float4*>(wk + static_cast<long long>(k) * cout + 4));
-                    acc[0] = fmaf(xv, wa.x, acc[0]);
-                    acc[1] = fmaf(xv, wa.y, acc[1]);
-                    acc[2] = fmaf(xv, wa.z, acc[2]);
-                    acc[3] = fmaf(xv, wa.w, acc[3]);
-                    acc[4] = fmaf(xv, wb.x, acc[4]);
-                    acc[5] = fmaf(xv, wb.y, acc[5]);
-                    acc[6] = fmaf(xv, wb.z, acc[6]);
-                    acc[7] = fmaf(xv, wb.w, acc[7]);
+                    acc[0] = fmaf(xv, conv_stage<MATH>(wa.x), acc[0]);
+                    acc[1] = fmaf(xv, conv_stage<MATH>(wa.y), acc[1]);
+                    acc[2] = fmaf(xv, conv_stage<MATH>(wa.z), acc[2]);
+                    acc[3] = fmaf(xv, conv_stage<MATH>(wa.w), acc[3]);
+                    acc[4] = fmaf(xv, conv_stage<MATH>(wb.x), acc[4]);
+                    acc[5] = fmaf(xv, conv_stage<MATH>(wb.y), acc[5]);
+                    acc[6] = fmaf(xv, conv_stage<MATH>(wb.z), acc[6]);
+                    acc[7] = fmaf(xv, conv_stage<MATH>(wb.w), acc[7]);
                 }
             }
+        }
+        if (bias && !BIAS_FIRST) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] += bias[c0 + c];
         }
         float4* dst = reinterpret_cast<float4*>(y + pix * cout + c0);
         dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);

@@ -29,6 +29,9 @@ Operators and the kernels behind them:
   converts its weight to float16 once at construction (nn.py:1297,
   ``_cast_fp16``), so like the reference it does not see later in-place
   weight edits; the others re-read the fp32 weight when it has changed.
+* ``Downsample2xTensorOp(x, H, W)`` (2x2 average pool), ``Upsample2xTensorOp(x,
+  H, W)`` (nearest 2x), ``ConcatTensorOp(g1, g2)`` (channel concat)
+  -> rdvb_downsample2x / rdvb_upsample2x / rdvb_concat_channels.
 * Convolutions live in ``conv.py``.
 """
 from __future__ import annotations
@@ -392,3 +395,74 @@ class LinearTensorOpSmall(_LinearOpBase):
         assert inf <= 128, f"in_features ({inf}) must be at most 128 (see this op's own docstring)"
         assert outf <= 128, f"out_features ({outf}) must be at most 128 (see this op's own docstring)"
         self._setup(data, weight, bias, up, batch, outf)
+
+
+class Downsample2xTensorOp(TensorOperation):
+    """2x2 average pool, stride 2, over a flattened [H*W, C] input
+    (rdv/domain/nn.py:1090-1107, rdv/shaders/tensors/downsample2x_tensor_op.h)."""
+
+    def __init__(self, x, H: int, W: int) -> None:
+        data, shape, upstream = _as_op_input(x)
+        assert len(shape) == 2, "Downsample2xTensorOp requires a 2D (H*W, C) input"
+        hw, channels = shape
+        assert hw == H * W, f"H*W ({H * W}) must match x's own row count ({hw})"
+        assert H % 2 == 0 and W % 2 == 0, "Downsample2xTensorOp requires even H and W"
+        self.x_buf = data
+        self.H_in, self.W_in = H, W
+        self.W = W // 2  # output width
+        self._upstream = upstream
+        super().__init__([(H // 2) * (W // 2), channels])
+
+    def _run(self):
+        x = _f32_view(self.x_buf)
+        y = self._result._tensor
+        N.check(N.lib().rdvb_downsample2x(x.data_ptr(), self.H_in, self.W_in, y.shape[1], y.data_ptr(),
+                                          stream_handle()), "rdvb_downsample2x")
+
+
+class Upsample2xTensorOp(TensorOperation):
+    """Nearest-neighbour 2x upsample over a flattened [H*W, C] input
+    (rdv/domain/nn.py:1110-1124, rdv/shaders/tensors/upsample2x_tensor_op.h)."""
+
+    def __init__(self, x, H: int, W: int) -> None:
+        data, shape, upstream = _as_op_input(x)
+        assert len(shape) == 2, "Upsample2xTensorOp requires a 2D (H*W, C) input"
+        hw, channels = shape
+        assert hw == H * W, f"H*W ({H * W}) must match x's own row count ({hw})"
+        self.x_buf = data
+        self.H_in, self.W_in = H, W
+        self.W = W * 2  # output width
+        self._upstream = upstream
+        super().__init__([(H * 2) * (W * 2), channels])
+
+    def _run(self):
+        x = _f32_view(self.x_buf)
+        y = self._result._tensor
+        N.check(N.lib().rdvb_upsample2x(x.data_ptr(), self.H_in, self.W_in, y.shape[1], y.data_ptr(),
+                                        stream_handle()), "rdvb_upsample2x")
+
+
+class ConcatTensorOp(TensorOperation):
+    """Channel concat of two ops/tensors sharing the H*W leading dim
+    (rdv/domain/nn.py:1127-1150, rdv/shaders/tensors/concat_tensor_op.h)."""
+
+    def __init__(self, g1, g2) -> None:
+        data1, shape1, up1 = _as_op_input(g1)
+        data2, shape2, up2 = _as_op_input(g2)
+        assert len(shape1) == 2 and len(shape2) == 2, "ConcatTensorOp requires 2D (H*W, C) inputs"
+        assert shape1[0] == shape2[0], "g1/g2 must share the same H*W leading dim"
+        assert shape1[1] % 8 == 0, f"g1's own channels ({shape1[1]}) must be a multiple of 8"
+        assert shape2[1] % 8 == 0, f"g2's own channels ({shape2[1]}) must be a multiple of 8"
+        self.x1_buf = data1
+        self.x2_buf = data2
+        self.C1 = shape1[1]
+        self._upstream = up1
+        self._extra_upstreams = (up2,) if up2 is not None else ()
+        super().__init__([shape1[0], shape1[1] + shape2[1]])
+
+    def _run(self):
+        x1 = _f32_view(self.x1_buf)
+        x2 = _f32_view(self.x2_buf)
+        y = self._result._tensor
+        N.check(N.lib().rdvb_concat_channels(x1.data_ptr(), x1.shape[1], x2.data_ptr(), x2.shape[1], y.shape[0],
+                                             y.data_ptr(), stream_handle()), "rdvb_concat_channels")

@@ -143,6 +143,19 @@ def main():
                                         ctypes.c_float(ds[i]), ctypes.c_float(0.05), ctypes.c_float(1.0))
     np.savez_compressed(os.path.join(HERE, "transmittance.npz"), x=xs, w=ws, d=ds, c0=c0, c1=c1, T=T,
                         step=np.float32(0.05), scale=np.float32(1.0))
+    # --- resampling / concatenation tensor ops -------------------------------
+    xs = rng.standard_normal((8 * 12, 16)).astype(np.float32)
+    down = np.zeros((4 * 6, 16), dtype=np.float32)
+    lib.ref_downsample2x(ptr(xs), 8, 12, 16, ptr(down))
+    xu = rng.standard_normal((4 * 6, 8)).astype(np.float32)
+    up = np.zeros((8 * 12, 8), dtype=np.float32)
+    lib.ref_upsample2x(ptr(xu), 4, 6, 8, ptr(up))
+    x1 = rng.standard_normal((20, 16)).astype(np.float32)
+    x2 = rng.standard_normal((20, 8)).astype(np.float32)
+    cat = np.zeros((20, 24), dtype=np.float32)
+    lib.ref_concat(ptr(x1), 16, ptr(x2), 8, 20, ptr(cat))
+    np.savez_compressed(os.path.join(HERE, "resample.npz"), down_x=xs, down_y=down, up_x=xu, up_y=up,
+                        cat_x1=x1, cat_x2=x2, cat_y=cat)
     print("golden fixtures written to", HERE)
 
 

@@ -5,6 +5,7 @@ import pytest
 
 from oracle import mlp as omlp
 from oracle import raymarch as orm
+from oracle import tensors as oten
 from oracle import winograd as owg
 from oracle._clib import ref_lib, ref_lib_available
 
@@ -142,3 +143,10 @@ def test_camera_rays_geometry():
     centre = (w[2 * 8 + 3] + w[2 * 8 + 4] + w[3 * 8 + 3] + w[3 * 8 + 4]) / 4
     to_target = -pose[:3] / np.linalg.norm(pose[:3])
     assert np.dot(centre / np.linalg.norm(centre), to_target) > 0.99
+
+
+def test_resample_and_concat_restatements_bit_exact_vs_reference(golden):
+    g = golden("resample.npz")
+    np.testing.assert_array_equal(oten.downsample2x(g["down_x"], 8, 12), g["down_y"])
+    np.testing.assert_array_equal(oten.upsample2x(g["up_x"], 4, 6), g["up_y"])
+    np.testing.assert_array_equal(oten.concat(g["cat_x1"], g["cat_x2"]), g["cat_y"])
