@@ -193,6 +193,22 @@ int rdvb_conv2d_direct_staged(const void* x, int x_dtype, int n, int h, int w, i
                               const float* weight, const float* bias, int math, int bias_first, float* y,
                               void* stream);
 
+/* The reference's tensor-core convolutions on tcgen05 (implicit GEMM, one
+ * M=128 x N=cout MMA per tap and 16 input channels, fp32 accumulation in
+ * TMEM, bias added in the epilogue). Eligible shapes: cin 16..64 and cout
+ * 16..256, multiples of 16, kh*kw <= 25, the taps' weights fitting shared
+ * memory; rdvb_conv_tc_packed_bytes returns 0 otherwise.
+ *  rdvb_conv_tc_pack: weight [kh, kw, cin, cout] fp32 (device) -> wpack
+ *    (256-byte aligned, rdvb_conv_tc_packed_bytes bytes) as float16
+ *    (operand RDVB_F16) or bfloat16 (RDVB_BF16).
+ *  rdvb_conv2d_tc: x [n*h*w, cin] (RDVB_F32 or RDVB_F16, 16-byte aligned)
+ *    -> y [n*h*w, cout] fp32 (16-byte aligned), 'same' padding, stride 1. */
+int64_t rdvb_conv_tc_packed_bytes(int kh, int kw, int cin, int cout);
+int rdvb_conv_tc_pack(const float* weight, int kh, int kw, int cin, int cout, int operand, void* wpack,
+                      void* stream);
+int rdvb_conv2d_tc(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
+                   const void* wpack, int operand, const float* bias, float* y, void* stream);
+
 /* 2x2 average pool, stride 2 (Downsample2xTensorOp, rdv/domain/nn.py:1090-1107,
  * rdv/shaders/tensors/downsample2x_tensor_op.h): x [h, w, c] fp32 -> y
  * [h/2, w/2, c], each output ((x00 + x01) + x10) + x11, times 0.25. h, w even;

@@ -115,8 +115,9 @@ class _StagedConv(TensorOperation):
     """Shared body of the reference's tensor-core direct convolutions:
     x [H*W, in_channels], weight [KH, KW, in_channels, out_channels], bias
     [out_channels]; x and weight rounded to float16, fp32 accumulation over
-    (kh, kw, cin), the bias seeding the accumulator or added after
-    (rdvb_conv2d_direct_staged)."""
+    (kh, kw, cin). Runs as a tcgen05 implicit GEMM (rdvb_conv2d_tc) when
+    the shape fits it, else on the CUDA cores (rdvb_conv2d_direct_staged,
+    the bias seeding the accumulator or added after as the op does)."""
 
     _TILE_ROWS = 32
     _TILE_COLS = 16
@@ -147,11 +148,37 @@ class _StagedConv(TensorOperation):
         self._upstream = upstream
         TensorOperation.__init__(self, [hw, cout])
 
+    def _packed(self, w: torch.Tensor):
+        """float16 weight image of the tensor-core kernel (re-packed after an
+        in-place weight edit), or None when the shape is outside its limits."""
+        lib = N.lib()
+        nbytes = lib.rdvb_conv_tc_packed_bytes(self.KH, self.KW, self.CIN, self.COUT)
+        if nbytes <= 0:
+            return None
+        key = (w.data_ptr(), self.weight._tensor._version)
+        if getattr(self, "_wpack_key", None) != key:
+            if getattr(self, "_wpack", None) is None:
+                self._wpack = torch.empty(int(nbytes), dtype=torch.uint8, device=w.device)
+            N.check(lib.rdvb_conv_tc_pack(w.data_ptr(), self.KH, self.KW, self.CIN, self.COUT, N.RDVB_F16,
+                                          self._wpack.data_ptr(), stream_handle()), "rdvb_conv_tc_pack")
+            self._wpack_key = key
+        return self._wpack
+
     def _run(self):
         x = _f32_view(self.x_buf)
         w = _f32_view(self.weight)
         b = _f32_view(self.bias)
         y = self._result._tensor
+        wpack = self._packed(w)
+        if wpack is not None:
+            # tcgen05 implicit GEMM: fp32 accumulation from zero, bias in the
+            # epilogue (equal to the bias-seeded sum within fp32 rounding)
+            N.check(N.lib().rdvb_conv2d_tc(
+                x.data_ptr(), N.RDVB_F32, 1, self.H, self.W, self.CIN, self.COUT, self.KH, self.KW,
+                wpack.data_ptr(), N.RDVB_F16, b.data_ptr(), y.data_ptr(), stream_handle()), "rdvb_conv2d_tc")
+            return
+        # shapes outside the tensor-core kernel's limits (cin > 64, cout > 256,
+        # more taps than fit shared memory): the same arithmetic on CUDA cores
         N.check(N.lib().rdvb_conv2d_direct_staged(
             x.data_ptr(), N.RDVB_F32, 1, self.H, self.W, self.CIN, self.COUT, self.KH, self.KW, w.data_ptr(),
             b.data_ptr(), N.RDVB_MATH_F16, int(self._bias_first), y.data_ptr(), stream_handle()),

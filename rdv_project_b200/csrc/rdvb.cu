@@ -21,6 +21,7 @@
 #include "raymarch.cuh"
 #include "transmittance.cuh"
 #include "resample.cuh"
+#include "conv_tc.cuh"
 
 namespace {
 
@@ -52,6 +53,7 @@ struct DeviceInfo {
     size_t simt_smem_set = 0;
     size_t wino_smem_set[2] = {};
     size_t trm_smem_set = 0;
+    size_t conv_tc_smem_set = 0;
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
@@ -606,6 +608,96 @@ int rdvb_conv2d_direct_staged(const void* x, int x_dtype, int n, int h, int w, i
     }
 #undef RDVB_CONV
     return check_launch("conv2d_direct_kernel");
+}
+
+namespace {
+// Shared-memory bytes of conv_tc_kernel for these shapes (0: not eligible).
+uint32_t conv_tc_smem(int kh, int kw, int cin, int cout, int budget) {
+    using namespace rdvb::convtc;
+    if (kh < 1 || kw < 1 || kh * kw > kMaxTaps) return 0;
+    if (cin < 16 || cin % 16 || cin > kMaxCin || cout < 16 || cout % 16 || cout > kMaxCout) return 0;
+    const uint32_t w_bytes = static_cast<uint32_t>(kh * kw) * cout * 128u;
+    const uint32_t off_a = (w_bytes + 1023u) & ~1023u;
+    const uint32_t total = off_a + kRing * kATileBytes + kBarBlockBytes + 1024u;
+    return total <= static_cast<uint32_t>(budget) ? total : 0u;
+}
+}  // namespace
+
+int64_t rdvb_conv_tc_packed_bytes(int kh, int kw, int cin, int cout) {
+    DeviceInfo* dev = nullptr;
+    const int budget = current_device(&dev) == RDVB_OK ? dev->max_smem_optin : 232448;
+    if (!conv_tc_smem(kh, kw, cin, cout, budget)) return 0;
+    return static_cast<int64_t>(kh) * kw * cout * 128;
+}
+
+int rdvb_conv_tc_pack(const float* weight, int kh, int kw, int cin, int cout, int operand, void* wpack,
+                      void* stream) {
+    if (operand != RDVB_F16 && operand != RDVB_BF16) return fail(RDVB_ERR_INVALID_ARG, "operand must be RDVB_F16 or RDVB_BF16");
+    if (rdvb_conv_tc_packed_bytes(kh, kw, cin, cout) <= 0)
+        return fail(RDVB_ERR_UNSUPPORTED, "%dx%d x %d -> %d is outside the tensor-core convolution's limits", kh, kw,
+                    cin, cout);
+    if (!weight || !wpack || !aligned(wpack, 256))
+        return fail(RDVB_ERR_INVALID_ARG, "weight must be set and wpack 256-byte aligned");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const long long total = static_cast<long long>(kh) * kw * cout * 64;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, dev->sm_count * 8LL));
+    rdvb::convtc::conv_tc_pack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        weight, kh * kw, cin, cout, operand == RDVB_BF16 ? 1 : 0, static_cast<uint8_t*>(wpack));
+    return check_launch("conv_tc_pack_kernel");
+}
+
+int rdvb_conv2d_tc(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
+                   const void* wpack, int operand, const float* bias, float* y, void* stream) {
+    using namespace rdvb::convtc;
+    if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16)
+        return fail(RDVB_ERR_INVALID_ARG, "x_dtype must be RDVB_F32 or RDVB_F16");
+    if (operand != RDVB_F16 && operand != RDVB_BF16) return fail(RDVB_ERR_INVALID_ARG, "operand must be RDVB_F16 or RDVB_BF16");
+    if (n < 0 || h < 0 || w < 0) return fail(RDVB_ERR_INVALID_ARG, "n, h, w must be >= 0");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const uint32_t smem = conv_tc_smem(kh, kw, cin, cout, dev->max_smem_optin);
+    if (!smem)
+        return fail(RDVB_ERR_UNSUPPORTED, "%dx%d x %d -> %d is outside the tensor-core convolution's limits", kh, kw,
+                    cin, cout);
+    const long long n_pix = static_cast<long long>(n) * h * w;
+    if (n_pix == 0) return RDVB_OK;
+    if (n_pix > (static_cast<long long>(0x7fffffff) - 1) * kTileM)
+        return fail(RDVB_ERR_UNSUPPORTED, "too many pixels (%lld)", n_pix);
+    if (!x || !y || !wpack) return fail(RDVB_ERR_INVALID_ARG, "x, y and wpack must not be NULL");
+    if (!aligned(x, 16) || !aligned(y, 16) || !aligned(wpack, 256))
+        return fail(RDVB_ERR_INVALID_ARG, "x and y must be 16-byte and wpack 256-byte aligned");
+    if (bias && !aligned(bias, 4)) return fail(RDVB_ERR_INVALID_ARG, "bias must be 4-byte aligned");
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.x = x;
+    p.y = y;
+    p.wpack = static_cast<const uint8_t*>(wpack);
+    p.bias = bias;
+    p.n_pix = n_pix;
+    p.h = h;
+    p.w = w;
+    p.cin = cin;
+    p.cout = cout;
+    p.kh = kh;
+    p.kw = kw;
+    p.taps = kh * kw;
+    p.x_f16 = x_dtype == RDVB_F16 ? 1 : 0;
+    p.bf16 = operand == RDVB_BF16 ? 1 : 0;
+    p.n_blocks = static_cast<int>((n_pix + kTileM - 1) / kTileM);
+    p.w_bytes = static_cast<uint32_t>(p.taps) * cout * 128u;
+    p.off_a = (p.w_bytes + 1023u) & ~1023u;
+    p.off_bar = p.off_a + kRing * kATileBytes;
+    p.idesc = rdvb::umma_idesc_f16(static_cast<uint32_t>(cout), p.bf16);
+    if (dev->conv_tc_smem_set < smem) {
+        cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(conv_tc): %s", cudaGetErrorString(e));
+        dev->conv_tc_smem_set = smem;
+    }
+    const int grid = std::min(dev->sm_count, p.n_blocks);
+    conv_tc_kernel<<<grid, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+    return check_launch("conv_tc_kernel");
 }
 
 int rdvb_conv2d_direct(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,

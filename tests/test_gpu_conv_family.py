@@ -119,3 +119,64 @@ def test_resample_large_and_unet_style_chain(rdv, cuda_device):
     nw, el = omlp.rel_errors(got[:, c:], oten.upsample2x(conv2, h // 2, w // 2))
     assert nw <= 1e-4 and el <= 1e-4
     assert rdv.device_status() == 0
+
+
+def _tc_conv(N, x, wt, b, n, h, w, operand):
+    cin, cout = wt.shape[2], wt.shape[3]
+    kh, kw = wt.shape[0], wt.shape[1]
+    lib = N.lib()
+    nbytes = lib.rdvb_conv_tc_packed_bytes(kh, kw, cin, cout)
+    assert nbytes > 0
+    wp = torch.empty(int(nbytes), dtype=torch.uint8, device=x.device)
+    N.check(lib.rdvb_conv_tc_pack(wt.data_ptr(), kh, kw, cin, cout, operand, wp.data_ptr(), None), "pack")
+    y = torch.full((n * h * w, cout), float("nan"), device=x.device)
+    N.check(lib.rdvb_conv2d_tc(x.data_ptr(), N.RDVB_F16 if x.dtype == torch.float16 else N.RDVB_F32, n, h, w, cin,
+                               cout, kh, kw, wp.data_ptr(), operand, b.data_ptr(), y.data_ptr(), None), "conv_tc")
+    return y
+
+
+@pytest.mark.parametrize("n,h,w,cin,cout,kh,kw,operand", [
+    (1, 160, 160, 16, 16, 3, 3, "f16"),    # 200 blocks: several per CTA, both accumulator halves
+    (2, 37, 53, 64, 128, 3, 3, "f16"),     # ragged last block, two images
+    (3, 24, 24, 32, 32, 5, 5, "bf16"),     # 25 taps, bfloat16 operands
+    (1, 64, 64, 48, 256, 1, 1, "f16"),     # 1x1, widest output
+])
+def test_tensor_core_conv_matches_oracle(rdv, cuda_device, n, h, w, cin, cout, kh, kw, operand):
+    import rdv_project_b200._native as N
+    from oracle import winograd as owg
+    from oracle.mlp import stage
+
+    g = torch.Generator().manual_seed(n * 100 + cin)
+    x = torch.randn(n * h * w, cin, generator=g)
+    wt = torch.randn(kh, kw, cin, cout, generator=g) * (2.0 / (kh * kw * cin)) ** 0.5
+    b = torch.randn(cout, generator=g) * 0.1
+    op = N.RDVB_F16 if operand == "f16" else N.RDVB_BF16
+    xd, wd, bd = x.to(cuda_device), wt.to(cuda_device), b.to(cuda_device)  # alive while the kernels run
+    y = _tc_conv(N, xd, wd, bd, n, h, w, op)
+    torch.cuda.synchronize()
+    xs = stage(x.numpy(), operand).reshape(n, h, w, cin)
+    ref = owg.conv2d_direct(xs, stage(wt.numpy(), operand), b.numpy()).reshape(n * h * w, cout)
+    got = y.cpu().numpy()
+    assert not np.isnan(got).any()
+    nw, el = omlp.rel_errors(got, ref)
+    assert nw <= 1e-4 and el <= 1e-4, (nw, el)
+    # the CUDA-core kernel on the same staged operands agrees to fp32 rounding
+    if operand == "f16" and n == 1:
+        y2 = torch.empty_like(y)
+        N.check(N.lib().rdvb_conv2d_direct_staged(
+            xd.data_ptr(), N.RDVB_F32, n, h, w, cin, cout, kh, kw, wd.data_ptr(), bd.data_ptr(), N.RDVB_MATH_F16, 0,
+            y2.data_ptr(), None), "staged")
+        torch.testing.assert_close(y, y2, rtol=2e-5, atol=2e-5)
+    assert rdv.device_status() == 0
+
+
+def test_shapes_outside_tensor_core_limits_take_cuda_cores(rdv, cuda_device):
+    import rdv_project_b200._native as N
+
+    assert N.lib().rdvb_conv_tc_packed_bytes(3, 3, 96, 32) == 0   # cin > 64
+    assert N.lib().rdvb_conv_tc_packed_bytes(7, 7, 16, 16) == 0   # 49 taps
+    x, wt, b = _data(16, 16, 96, 32, seed=9)
+    op = rdv.Conv2DTensorOpFast(x.to(cuda_device), wt.to(cuda_device), b.to(cuda_device), 16, 16)
+    ref = oten.conv2d_staged(x.numpy(), wt.numpy(), b.numpy(), 16, 16, "f16")
+    nw, el = omlp.rel_errors(op.as_type("torch").cpu().numpy(), ref)
+    assert nw <= 1e-4 and el <= 1e-4
