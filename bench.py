@@ -400,6 +400,7 @@ def run_ours(args, spec, world, rank, local):
                 "c5": mlp_summary(c5_spec()),
                 "transmittance": run_trm(args, 1, 0, local, summary=True),
                 "tensor_op_chain": chain_summary(),
+                "conv_family": conv_family_summary(),
             }
     print(json.dumps(line), flush=True)
 
@@ -895,6 +896,48 @@ def chain_summary(rows=1 << 20, steps=3):
                         f"ReLUTensorOp), {rows} rows",
             "per_op_ms": t_ops / steps * 1e3, "evaluate_chain_ms": t_fused / steps * 1e3,
             "speedup": t_ops / t_fused, "bit_identical": same}
+
+
+def conv_family_summary(steps=5):
+    """The reference's tensor-core direct convolution (Conv2DTensorOpSimple3x3
+    arithmetic: float16 operands, fp32 accumulation) at config 3's shape
+    (8x256x256x64 -> 64, 3x3), on the tcgen05 implicit-GEMM kernel and on the
+    CUDA-core kernel with the same staged operands, L2 flushed between steps."""
+    from rdv_project_b200 import _native as N
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    x_h, w33io, b = c3_data()
+    n, h, w, c = C3_SHAPE
+    x = x_h.reshape(n * h * w, c).to(dev)
+    wt, bd = w33io.to(dev), b.to(dev)
+    lib = N.lib()
+    wp = torch.empty(int(lib.rdvb_conv_tc_packed_bytes(3, 3, c, c)), dtype=torch.uint8, device=dev)
+    N.check(lib.rdvb_conv_tc_pack(wt.data_ptr(), 3, 3, c, c, N.RDVB_F16, wp.data_ptr(), None), "rdvb_conv_tc_pack")
+    y = torch.empty(n * h * w, c, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def tc():
+        N.check(lib.rdvb_conv2d_tc(x.data_ptr(), N.RDVB_F16, n, h, w, c, c, 3, 3, wp.data_ptr(), N.RDVB_F16,
+                                   bd.data_ptr(), y.data_ptr(), None), "rdvb_conv2d_tc")
+
+    def cuda_cores():
+        N.check(lib.rdvb_conv2d_direct_staged(x.data_ptr(), N.RDVB_F16, n, h, w, c, c, 3, 3, wt.data_ptr(),
+                                              bd.data_ptr(), N.RDVB_MATH_F16, 1, y.data_ptr(), None),
+                "rdvb_conv2d_direct_staged")
+
+    out = {"workload": "3x3 direct conv, float16 operands / fp32 accumulation, 8x256x256x64 -> 64 (config 3 shape)"}
+    flops = 2 * n * h * w * c * c * 9
+    for name, fn, k in (("tensor_core", tc, steps), ("cuda_cores", cuda_cores, 1)):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        t = time_steps(fn, k, flush=flush) / k
+        out[name] = {"ms": t * 1e3, "tflops": flops / t / 1e12}
+    peaks, peak_kind = measured_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    out["roofline"] = {"bound": "tensor", "achieved": out["tensor_core"]["tflops"], "peak": peak, "unit": "TFLOP/s",
+                       "frac": out["tensor_core"]["tflops"] / peak, "peak_source": f"{peak_kind} bf16_tflops"}
+    return out
 
 
 def mlp_summary(spec, steps=5):
