@@ -794,6 +794,24 @@ def run_trm(args, world, rank, local, summary=False):
     roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_source": f"{peak_kind} bf16_tflops",
             "note": "MLP flops of the evaluated steps over the call's three launches (setup, fused MLP, combine)"}
+    e2e = None
+    if not args.profile_run and not summary:
+        # end to end on every rank: its rays from pinned host memory, its T
+        # back to pinned host memory; max over ranks
+        rays_pin = rays_host.pin_memory()
+        T_pin = torch.empty((re_ - rb, 1)).pin_memory()
+
+        def e2e_step():
+            rays.copy_(rays_pin, non_blocking=True)
+            march()
+            T_pin.copy_(state["T"], non_blocking=True)
+
+        k = max(1, min(args.steps, 5))
+        barrier(world)
+        t_e2e = max_over_ranks(time_steps(e2e_step, k), world)
+        e2e = {"value": evals_total * k / t_e2e, "unit": "evaluations/s",
+               "h2d_bytes_per_step": int(rays_pin.numel() * 4) * world,
+               "d2h_bytes_per_step": int(T_pin.numel() * 4) * world}
     if summary:
         return {"workload": "RaymarchingTransmittance, 1920x1080 camera rays (orbit pose 0), extinction "
                             "ReLU(MLP 3->64->64->1) LinearFast (tensor-core march), step 0.01",
@@ -821,22 +839,10 @@ def run_trm(args, world, rank, local, summary=False):
                    "elementwise": parity[1]},
         "clocks": clocks,
     }
-    if not args.profile_run:
-        # end to end: rays from pinned host memory, T back to pinned host memory
-        rays_pin = rays_host.pin_memory()
-        T_pin = torch.empty((re_ - rb, 1)).pin_memory()
-
-        def e2e_step():
-            rays.copy_(rays_pin, non_blocking=True)
-            march()
-            T_pin.copy_(state["T"], non_blocking=True)
-
-        k = max(1, min(args.steps, 5))
-        t_e2e = max_over_ranks(time_steps(e2e_step, k), world)
-        line["e2e"] = {"value": evals_total * k / t_e2e, "unit": "evaluations/s",
-                       "h2d_bytes_per_step": int(rays_pin.numel() * 4), "d2h_bytes_per_step": int(T_pin.numel() * 4)}
-        if world == 1:
-            line["cpu_baseline"] = trm_cpu_baseline(layers)
+    if e2e is not None:
+        line["e2e"] = e2e
+    if not args.profile_run and world == 1:
+        line["cpu_baseline"] = trm_cpu_baseline(layers)
     print(json.dumps(line), flush=True)
     return line
 
