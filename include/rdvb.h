@@ -209,6 +209,16 @@ int rdvb_conv_tc_pack(const float* weight, int kh, int kw, int cin, int cout, in
 int rdvb_conv2d_tc(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
                    const void* wpack, int operand, const float* bias, float* y, void* stream);
 
+/* TensorSampler (rdv/maths/__init__.py:2050-2083,
+ * rdv/shaders/samplers/tensor_sampler.h): y[i] = multilinear (linear) or
+ * nearest lookup of t [shape[0], ..., shape[in_dim-1], out_dim] fp32 at
+ * x[i] in [-1, 1]^in_dim (x [n, in_dim] fp32; coordinate in_dim-1-d runs
+ * along dimension d). clamp: corners outside t take the clamped index (else
+ * they contribute 0); aligned: -1/+1 at the first/last cell centres (else at
+ * the outer edges). in_dim 1..3; y [n, out_dim] fp32. */
+int rdvb_tensor_sampler(const float* t, int in_dim, const int* shape, int out_dim, const float* x, int64_t n,
+                        int clamp, int aligned, int linear, float* y, void* stream);
+
 /* 2x2 average pool, stride 2 (Downsample2xTensorOp, rdv/domain/nn.py:1090-1107,
  * rdv/shaders/tensors/downsample2x_tensor_op.h): x [h, w, c] fp32 -> y
  * [h/2, w/2, c], each output ((x00 + x01) + x10) + x11, times 0.25. h, w even;

@@ -49,3 +49,71 @@ def conv2d_staged(x_hw_c: np.ndarray, w_hwio: np.ndarray, bias, h: int, w: int, 
     xs = stage(np.asarray(x_hw_c, dtype=np.float32), math).reshape(1, h, w, cin)
     ws = stage(np.asarray(w_hwio, dtype=np.float32), math)
     return conv2d_direct(xs, ws, bias).reshape(h * w, -1)
+
+
+def tensor_sampler(t: np.ndarray, x: np.ndarray, clamp: bool = True, aligned: bool = False,
+                   linear: bool = True) -> np.ndarray:
+    """TensorSampler (rdv/shaders/samplers/tensor_sampler.h, IN = 1..3)
+    restated in float32, vectorised over points: t [D0, .., D(IN-1), OUT],
+    x [n, IN] -> [n, OUT]. Dimension d is addressed by x[:, IN-1-d]; corner
+    weights and the innermost mix(l, r, a) = l (1 - a) + r a in the
+    reference's order, out-of-range corners clamped or dropped."""
+    t = np.asarray(t, dtype=np.float32)
+    x = np.asarray(x, dtype=np.float32)
+    IN = t.ndim - 1
+    dims = t.shape[:IN]
+    one, half = np.float32(1.0), np.float32(0.5)
+    ac = np.float32(1.0 if aligned else 0.0)
+    lo, alpha, lo_in, hi_in, clo, chi = [], [], [], [], [], []
+    for d in range(IN):
+        g = np.float32(dims[d])
+        idx = ((x[:, IN - 1 - d] * (g - ac) + g) * half - half).astype(np.float32)
+        l = np.floor(idx).astype(np.int64)
+        h = l + 1
+        lo.append(l)
+        alpha.append((idx - l.astype(np.float32)).astype(np.float32))
+        lo_in.append(clamp | ((l >= 0) & (l < dims[d])))
+        hi_in.append(clamp | ((h >= 0) & (h < dims[d])))
+        clo.append(np.clip(l, 0, dims[d] - 1))
+        chi.append(np.clip(h, 0, dims[d] - 1))
+    n = x.shape[0]
+    out_dim = t.shape[-1]
+    if not linear:
+        idx = [lo[d] + (alpha[d] >= half) for d in range(IN)]
+        inside = np.ones(n, dtype=bool)
+        for d in range(IN):
+            inside &= (idx[d] >= 0) & (idx[d] < dims[d])
+            idx[d] = np.clip(idx[d], 0, dims[d] - 1)
+        y = t[tuple(idx)]
+        if not clamp:
+            y = np.where(inside[:, None], y, np.float32(0.0))
+        return y.astype(np.float32)
+
+    def pair(outer_idx, left_ok, right_ok, rest, y):
+        L = IN - 1
+        left = t[tuple(outer_idx + [clo[L]])]
+        right = t[tuple(outer_idx + [chi[L]])]
+        a = alpha[L][:, None]
+        r = rest[:, None]
+        both = (left * (one - a) + right * a).astype(np.float32)
+        add = np.where((left_ok & right_ok)[:, None], (r * both).astype(np.float32),
+                       np.where(left_ok[:, None], ((r * (one - a)).astype(np.float32) * left).astype(np.float32),
+                                np.where(right_ok[:, None], ((r * a).astype(np.float32) * right).astype(np.float32),
+                                         np.float32(0.0))))
+        return (y + add).astype(np.float32)
+
+    y = np.zeros((n, out_dim), dtype=np.float32)
+    if IN == 1:
+        return pair([], lo_in[0], hi_in[0], np.ones(n, np.float32), y)
+    if IN == 2:
+        y = pair([clo[0]], lo_in[0] & lo_in[1], lo_in[0] & hi_in[1], (one - alpha[0]).astype(np.float32), y)
+        return pair([chi[0]], hi_in[0] & lo_in[1], hi_in[0] & hi_in[1], alpha[0], y)
+    a0, a1 = alpha[0], alpha[1]
+    y = pair([clo[0], clo[1]], lo_in[0] & lo_in[1] & lo_in[2], lo_in[0] & lo_in[1] & hi_in[2],
+             ((one - a0) * (one - a1)).astype(np.float32), y)
+    y = pair([clo[0], chi[1]], lo_in[0] & hi_in[1] & lo_in[2], lo_in[0] & hi_in[1] & hi_in[2],
+             ((one - a0) * a1).astype(np.float32), y)
+    y = pair([chi[0], chi[1]], hi_in[0] & hi_in[1] & lo_in[2], hi_in[0] & hi_in[1] & hi_in[2],
+             (a0 * a1).astype(np.float32), y)
+    return pair([chi[0], clo[1]], hi_in[0] & lo_in[1] & lo_in[2], hi_in[0] & lo_in[1] & hi_in[2],
+                (a0 * (one - a1)).astype(np.float32), y)

@@ -47,6 +47,7 @@ SIGNATURES = {
     "rdvb_conv_tc_pack": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_conv2d_tc": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_int,
                                 _vp, _vp, _vp]),
+    "rdvb_tensor_sampler": (_c_int, [_vp, _c_int, _vp, _c_int, _vp, _c_i64, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_downsample2x": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_upsample2x": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_concat_channels": (_c_int, [_vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),

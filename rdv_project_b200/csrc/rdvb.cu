@@ -22,6 +22,7 @@
 #include "transmittance.cuh"
 #include "resample.cuh"
 #include "conv_tc.cuh"
+#include "sampler.cuh"
 
 namespace {
 
@@ -717,6 +718,39 @@ int check_rows_channels(const void* a, const void* b, int c) {
     return RDVB_OK;
 }
 }  // namespace
+
+int rdvb_tensor_sampler(const float* t, int in_dim, const int* shape, int out_dim, const float* x, int64_t n,
+                        int clamp, int aligned, int linear, float* y, void* stream) {
+    if (in_dim < 1 || in_dim > 3) return fail(RDVB_ERR_UNSUPPORTED, "in_dim must be 1, 2 or 3 (got %d)", in_dim);
+    if (!shape) return fail(RDVB_ERR_INVALID_ARG, "shape must not be NULL");
+    for (int d = 0; d < in_dim; ++d)
+        if (shape[d] < 1) return fail(RDVB_ERR_INVALID_ARG, "shape[%d] = %d must be positive", d, shape[d]);
+    if (out_dim < 1) return fail(RDVB_ERR_INVALID_ARG, "out_dim must be positive");
+    if (n < 0) return fail(RDVB_ERR_INVALID_ARG, "n must be >= 0");
+    if (n == 0) return RDVB_OK;
+    if (!t || !x || !y) return fail(RDVB_ERR_INVALID_ARG, "t, x and y must not be NULL");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    rdvb::sampler::Params p;
+    memset(&p, 0, sizeof(p));
+    p.t = t;
+    p.x = x;
+    p.y = y;
+    p.n = n;
+    p.out = out_dim;
+    for (int d = 0; d < in_dim; ++d) p.dim[d] = shape[d];
+    p.clamp = clamp ? 1 : 0;
+    p.aligned = aligned ? 1 : 0;
+    p.linear = linear ? 1 : 0;
+    const long long total = n * out_dim;
+    const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + 255) / 256,
+                                                                               dev->sm_count * 16LL)));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (in_dim == 1) rdvb::sampler::tensor_sampler_kernel<1><<<blocks, 256, 0, st>>>(p);
+    else if (in_dim == 2) rdvb::sampler::tensor_sampler_kernel<2><<<blocks, 256, 0, st>>>(p);
+    else rdvb::sampler::tensor_sampler_kernel<3><<<blocks, 256, 0, st>>>(p);
+    return check_launch("tensor_sampler_kernel");
+}
 
 int rdvb_downsample2x(const float* x, int h, int w, int c, float* y, void* stream) {
     if (h < 0 || w < 0 || h % 2 || w % 2) return fail(RDVB_ERR_INVALID_ARG, "h and w must be even and >= 0");

@@ -1,0 +1,129 @@
+// TensorSampler (rdv/maths/__init__.py:2050-2083,
+// rdv/shaders/samplers/tensor_sampler.h): multilinear or nearest lookup of a
+// dense fp32 tensor t [D0, ..., D(IN-1), OUT] at points x in [-1, 1]^IN.
+// Dimension i of t is addressed by coordinate x[IN-1-i] (the last
+// coordinate runs along the first dimension, as torch's grid_sample).
+//   index_f = (x * (D - a) + D) * 0.5 - 0.5   (a = 1 when aligned: -1/+1 at
+//             the first/last cell centres; a = 0: at the outer edges)
+//   lo = floor(index_f), hi = lo + 1, alpha = index_f - lo
+//   linear:  corner weights (1 - alpha, alpha) per dimension, the innermost
+//            pair blended as mix(left, right, alpha) = left (1 - alpha) +
+//            right alpha, times the product of the outer weights, added in
+//            the reference's corner order; a corner outside the tensor
+//            contributes 0 unless clamp (then its index is clamped)
+//   nearest: lo + (alpha >= 0.5); outside -> 0 unless clamp.
+// One thread per (point, channel); every product and sum is rounded
+// separately, in the reference's order.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace rdvb {
+namespace sampler {
+
+struct Params {
+    const float* t;
+    const float* x;   // [n, IN]
+    float* y;         // [n, OUT]
+    long long n;
+    int out;
+    int dim[3];
+    int clamp, aligned, linear;
+};
+
+__device__ __forceinline__ float mixf(float a, float b, float t) {
+    return __fadd_rn(__fmul_rn(a, __fsub_rn(1.0f, t)), __fmul_rn(b, t));
+}
+
+// dst += rest * blend of the pair (left, right) at offset `off` and `off + d`
+// along the innermost dimension, with the inside flags of both corners.
+__device__ __forceinline__ float blend_pair(const float* __restrict__ t, long long off, long long d, bool left_in,
+                                            bool right_in, float xw, float rest, float dst) {
+    if (!left_in && !right_in) return dst;
+    const float l = __ldg(t + off), r = __ldg(t + off + d);
+    if (left_in && right_in) return __fadd_rn(dst, __fmul_rn(rest, mixf(l, r, xw)));
+    if (left_in) return __fadd_rn(dst, __fmul_rn(__fmul_rn(rest, __fsub_rn(1.0f, xw)), l));
+    return __fadd_rn(dst, __fmul_rn(__fmul_rn(rest, xw), r));
+}
+
+__device__ __forceinline__ void coord(float xc, int dim, float ac, bool border, int& lo, int& clo, int& chi,
+                                      float& alpha, bool& lo_in, bool& hi_in) {
+    const float g = static_cast<float>(dim);
+    const float index_f = __fsub_rn(__fmul_rn(__fadd_rn(__fmul_rn(xc, __fsub_rn(g, ac)), g), 0.5f), 0.5f);
+    lo = static_cast<int>(floorf(index_f));
+    const int hi = lo + 1;
+    alpha = __fsub_rn(index_f, static_cast<float>(lo));
+    lo_in = border || (lo >= 0 && lo < dim);
+    hi_in = border || (hi >= 0 && hi < dim);
+    clo = min(max(lo, 0), dim - 1);
+    chi = min(max(hi, 0), dim - 1);
+}
+
+template <int IN>
+__global__ void tensor_sampler_kernel(const __grid_constant__ Params p) {
+    const long long total = p.n * p.out;
+    const float ac = p.aligned ? 1.0f : 0.0f;
+    const bool border = p.clamp != 0;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long i = idx / p.out;
+        const int k = static_cast<int>(idx - i * p.out);
+        int lo[IN], clo[IN], chi[IN];
+        float alpha[IN];
+        bool lo_in[IN], hi_in[IN];
+#pragma unroll
+        for (int d = 0; d < IN; ++d)
+            coord(__ldg(p.x + i * IN + (IN - 1 - d)), p.dim[d], ac, border, lo[d], clo[d], chi[d], alpha[d],
+                  lo_in[d], hi_in[d]);
+        // element strides of the spatial dimensions
+        long long st[IN];
+        st[IN - 1] = p.out;
+#pragma unroll
+        for (int d = IN - 2; d >= 0; --d) st[d] = st[d + 1] * p.dim[d + 1];
+        float out = 0.0f;
+        if (!p.linear) {
+            bool inside = true;
+            long long off = k;
+#pragma unroll
+            for (int d = 0; d < IN; ++d) {
+                int id = lo[d] + (alpha[d] >= 0.5f ? 1 : 0);
+                inside = inside && id >= 0 && id < p.dim[d];
+                id = min(max(id, 0), p.dim[d] - 1);
+                off += id * st[d];
+            }
+            if (border || inside) out = __ldg(p.t + off);
+            p.y[idx] = out;
+            continue;
+        }
+        const int L = IN - 1;  // innermost (fastest) dimension
+        const long long dl = static_cast<long long>(chi[L] - clo[L]) * st[L];
+        if constexpr (IN == 1) {
+            out = blend_pair(p.t, clo[0] * st[0] + k, dl, lo_in[0], hi_in[0], alpha[0], 1.0f, out);
+        } else if constexpr (IN == 2) {
+            const long long base = clo[0] * st[0] + clo[1] * st[1] + k;
+            const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st[0];
+            out = blend_pair(p.t, base, dl, lo_in[0] && lo_in[1], lo_in[0] && hi_in[1], alpha[1],
+                             __fsub_rn(1.0f, alpha[0]), out);
+            out = blend_pair(p.t, base + d0, dl, hi_in[0] && lo_in[1], hi_in[0] && hi_in[1], alpha[1], alpha[0], out);
+        } else {
+            long long ptr = clo[0] * st[0] + clo[1] * st[1] + clo[2] * st[2] + k;
+            const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st[0];
+            const long long d1 = static_cast<long long>(chi[1] - clo[1]) * st[1];
+            const float a0 = alpha[0], a1 = alpha[1];
+            out = blend_pair(p.t, ptr, dl, lo_in[0] && lo_in[1] && lo_in[2], lo_in[0] && lo_in[1] && hi_in[2],
+                             alpha[2], __fmul_rn(__fsub_rn(1.0f, a0), __fsub_rn(1.0f, a1)), out);
+            ptr += d1;
+            out = blend_pair(p.t, ptr, dl, lo_in[0] && hi_in[1] && lo_in[2], lo_in[0] && hi_in[1] && hi_in[2],
+                             alpha[2], __fmul_rn(__fsub_rn(1.0f, a0), a1), out);
+            ptr += d0;
+            out = blend_pair(p.t, ptr, dl, hi_in[0] && hi_in[1] && lo_in[2], hi_in[0] && hi_in[1] && hi_in[2],
+                             alpha[2], __fmul_rn(a0, a1), out);
+            ptr -= d1;
+            out = blend_pair(p.t, ptr, dl, hi_in[0] && lo_in[1] && lo_in[2], hi_in[0] && lo_in[1] && hi_in[2],
+                             alpha[2], __fmul_rn(a0, __fsub_rn(1.0f, a1)), out);
+        }
+        p.y[idx] = out;
+    }
+}
+
+}  // namespace sampler
+}  // namespace rdvb

@@ -174,6 +174,50 @@ def linear(weight, bias, f16: bool = False):
     return (LinearFast if f16 else Linear)(weight, bias)
 
 
+class TensorSampler(Map):
+    """Multilinear (linear=True) or nearest lookup of a dense fp32 tensor
+    t [D0, ..., D(IN-1), OUT] at points in [-1, 1]^IN
+    (rdv/maths/__init__.py:2050-2083, rdv/shaders/samplers/tensor_sampler.h):
+    clamp clamps out-of-range corners (else they contribute 0), aligned ties
+    -1/+1 to the first/last cell centres (else to the outer edges), as
+    torch's grid_sample. IN is 1, 2 or 3. Composed before a Linear chain
+    (``sampler >> mlp``) it is the chain's input encoding: one sampler
+    launch, then the fused MLP on its output."""
+
+    def __init__(self, t, clamp: bool = True, aligned: bool = False, linear: bool = True) -> None:
+        t = t if isinstance(t, RDVObject) else wrap(t)
+        n = len(t.shape)
+        assert 2 <= n <= 4, "TensorSampler supports 1- to 3-dimensional grids (a [D0, ..., OUT] tensor)"
+        self.t = t
+        self.IN = n - 1
+        self.OUT = t.shape[n - 1]
+        self.clamp = 1 if clamp else 0
+        self.aligned = 1 if aligned else 0
+        self.linear = 1 if linear else 0
+
+    def _sample(self, x2d: torch.Tensor, y2d: torch.Tensor) -> None:
+        t = self.t._tensor
+        if t.device != x2d.device or t.dtype != torch.float32 or not t.is_contiguous():
+            t = t.to(device=x2d.device, dtype=torch.float32).contiguous()
+        N.check(N.lib().rdvb_tensor_sampler(
+            t.data_ptr(), self.IN, N.int_array(list(t.shape[:self.IN])), self.OUT, x2d.data_ptr(), x2d.shape[0],
+            self.clamp, self.aligned, self.linear, y2d.data_ptr(), stream_handle()), "rdvb_tensor_sampler")
+
+    def __call__(self, *args, **kwargs):
+        if len(args) != 1:
+            raise TypeError("a Map is called with exactly one input tensor")
+        x, = args
+        xt = x._tensor if isinstance(x, RDVObject) else wrap(x)._tensor
+        assert xt.shape[-1] == self.IN, f"input's last dimension ({xt.shape[-1]}) must match the map's IN ({self.IN})"
+        dev = current_device()
+        x2d = xt.reshape(-1, self.IN).to(device=dev, dtype=torch.float32).contiguous()
+        out = torch.empty(list(xt.shape[:-1]) + [self.OUT], dtype=torch.float32, device=dev)
+        with _timed():
+            if x2d.shape[0]:
+                self._sample(x2d, out.view(-1, self.OUT))
+        return RDVObject(out)
+
+
 class Composite(Map):
     """f(g(x)); g's OUT must match f's IN."""
 
@@ -223,6 +267,8 @@ def _lower(m: Map):
     layers = []
     relus = []
     for op in m._ops():
+        if isinstance(op, TensorSampler):
+            raise NotImplementedError("a TensorSampler must come first in the chain (its input encoding)")
         if isinstance(op, _LinearBase):
             layers.append(op)
             relus.append(False)
@@ -244,13 +290,19 @@ def _weights_key(layers):
 
 
 class _ChainPlan:
-    """Per-device lowered chain: fp32 weight views, flags and (for
-    float16/bfloat16 chains) the packed tensor-core weight image."""
+    """Per-device lowered chain: an optional leading TensorSampler (the
+    input encoding), fp32 weight views, flags and (for float16/bfloat16
+    chains) the packed tensor-core weight image."""
 
     def __init__(self, m: Map, dev):
-        self.input_relu, self.layers, self.relus = _lower(m)
+        ops = m._ops()
+        self.prologue = ops[0] if ops and isinstance(ops[0], TensorSampler) else None
+        rest = m
+        if self.prologue is not None:
+            rest = _compose_ops(ops[1:])
+        self.input_relu, self.layers, self.relus = _lower(rest) if rest is not None else (False, [], [])
         self.dev = dev
-        self.dims = [m.IN] + [l.OUT for l in self.layers]
+        self.dims = [self.prologue.OUT if self.prologue is not None else m.IN] + [l.OUT for l in self.layers]
         self.flags = [l._math | (N.RDVB_LAYER_RELU if r else 0) for l, r in zip(self.layers, self.relus)]
         self.packed = None
         self.packed_key = None
@@ -284,12 +336,27 @@ class _ChainPlan:
 _DTYPES = {torch.float32: N.RDVB_F32, torch.float16: N.RDVB_F16, torch.bfloat16: N.RDVB_BF16}
 
 
+def _compose_ops(ops):
+    """Composite of the ops (applied first to last), or None if empty."""
+    m = None
+    for op in ops:
+        m = op if m is None else Composite(op, m)
+    return m
+
+
 def run_chain(plan: _ChainPlan, x2d: torch.Tensor, y2d: torch.Tensor, tail_exact: bool) -> None:
     """Launches the lowered chain on [rows, IN] -> [rows, OUT] (device tensors)."""
     plan.refresh()
     rows = x2d.shape[0]
     if rows == 0:
         return
+    if plan.prologue is not None:
+        feats = torch.empty(rows, plan.prologue.OUT, dtype=torch.float32, device=x2d.device)
+        xs = x2d if x2d.dtype == torch.float32 else x2d.float()
+        plan.prologue._sample(xs.contiguous(), feats if plan.layers or plan.input_relu else y2d)
+        if not plan.layers and not plan.input_relu:
+            return
+        x2d = feats
     if not plan.layers:
         if plan.input_relu:
             N.check(N.lib().rdvb_relu(x2d.data_ptr(), y2d.data_ptr(), x2d.numel(), stream_handle()), "rdvb_relu")

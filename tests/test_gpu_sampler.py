@@ -1,0 +1,71 @@
+"""GPU parity of TensorSampler (rdv/maths/__init__.py:2050-2083) against the
+oracle restatement (oracle/tensors.tensor_sampler, itself checked against
+torch's grid_sample on CPU), alone and as the input encoding of a fused MLP
+chain (sampler >> LinearFast ...). The sampler is fp32 arithmetic in the
+reference's order: 1e-5; the chain runs float16 operands: 1e-2."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import mlp as omlp
+from oracle import tensors as oten
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rdv():
+    import rdv_project_b200 as rdv
+    return rdv
+
+
+@pytest.mark.parametrize("shape", [(37, 5), (9, 13, 8), (6, 7, 5, 16), (32, 32, 32, 4)])
+@pytest.mark.parametrize("clamp,aligned,linear", [(True, False, True), (False, True, True), (True, True, False),
+                                                  (False, False, False)])
+def test_sampler_matches_oracle(rdv, cuda_device, shape, clamp, aligned, linear):
+    rng = np.random.default_rng(len(shape) * 7 + clamp + 2 * aligned + 4 * linear)
+    t = rng.standard_normal(shape).astype(np.float32)
+    in_dim = len(shape) - 1
+    x = rng.uniform(-1.25, 1.25, size=(4000, in_dim)).astype(np.float32)
+    s = rdv.TensorSampler(torch.from_numpy(t).to(cuda_device), clamp=clamp, aligned=aligned, linear=linear)
+    got = s(torch.from_numpy(x).to(cuda_device)).as_tensor("torch").cpu().numpy()
+    ref = oten.tensor_sampler(t, x, clamp, aligned, linear)
+    nw, el = omlp.rel_errors(got, ref)
+    assert nw <= 1e-5 and el <= 1e-5, (nw, el)
+
+
+def test_sampler_feeds_fused_mlp(rdv, cuda_device):
+    rng = np.random.default_rng(3)
+    grid = rng.standard_normal((16, 16, 16, 16)).astype(np.float32)
+    dims = [16, 64, 64, 4]
+    layers = [{"W": (rng.standard_normal((dims[i + 1], dims[i])) * np.sqrt(2.0 / dims[i])).astype(np.float32),
+               "b": (rng.standard_normal(dims[i + 1]) * 0.1).astype(np.float32), "math": "f16", "relu": i < 2}
+              for i in range(3)]
+    m = rdv.TensorSampler(torch.from_numpy(grid).to(cuda_device))
+    for l in layers:
+        m = m >> rdv.linear(torch.from_numpy(l["W"]).to(cuda_device), torch.from_numpy(l["b"]).to(cuda_device),
+                            f16=True)
+        if l["relu"]:
+            m = m >> rdv.relu
+    x = rng.uniform(-1, 1, size=(5000, 3)).astype(np.float32)
+    got = m(rdv.wrap(torch.from_numpy(x).to(cuda_device))).as_tensor("torch").cpu().numpy()
+    feats = oten.tensor_sampler(grid, x)
+    ref = omlp.mlp_forward(feats, layers, tail_exact=True)
+    nw, el = omlp.rel_errors(got, ref)
+    assert nw <= 1e-2 and el <= 1e-2, (nw, el)
+    assert got.shape == (5000, 4)
+
+
+def test_sampler_shapes_and_empty(rdv, cuda_device):
+    t = torch.randn(4, 5, 3, device=cuda_device)
+    s = rdv.TensorSampler(t)
+    assert (s.IN, s.OUT) == (2, 3)
+    out = s(torch.zeros(0, 2, device=cuda_device)).as_tensor("torch")
+    assert tuple(out.shape) == (0, 3)
+    out = s(torch.zeros(2, 7, 2, device=cuda_device)).as_tensor("torch")
+    assert tuple(out.shape) == (2, 7, 3)
+    # the centre of a 1-cell-per-axis grid returns that cell
+    one = torch.arange(6.0, device=cuda_device).reshape(1, 1, 6)
+    v = rdv.TensorSampler(one)(torch.zeros(1, 2, device=cuda_device)).as_tensor("torch")
+    assert torch.equal(v.cpu(), torch.arange(6.0).reshape(1, 6))
+    assert rdv.device_status() == 0

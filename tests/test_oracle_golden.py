@@ -150,3 +150,26 @@ def test_resample_and_concat_restatements_bit_exact_vs_reference(golden):
     np.testing.assert_array_equal(oten.downsample2x(g["down_x"], 8, 12), g["down_y"])
     np.testing.assert_array_equal(oten.upsample2x(g["up_x"], 4, 6), g["up_y"])
     np.testing.assert_array_equal(oten.concat(g["cat_x1"], g["cat_x2"]), g["cat_y"])
+
+
+@pytest.mark.parametrize("in_dim", [2, 3])
+@pytest.mark.parametrize("clamp,aligned,linear", [(True, False, True), (False, False, True), (True, True, True),
+                                                  (False, True, True), (True, False, False), (False, True, False)])
+def test_tensor_sampler_restatement_matches_torch_grid_sample(in_dim, clamp, aligned, linear):
+    """The reference documents TensorSampler as torch's grid_sample
+    (align_corners = aligned, padding border / zeros = clamp); the
+    restatement is checked against it on points spilling past the borders."""
+    import torch
+    import torch.nn.functional as F
+
+    rng = np.random.default_rng(in_dim * 10 + clamp + 2 * aligned + 4 * linear)
+    shape = (5, 7, 4) if in_dim == 2 else (4, 6, 5, 3)
+    t = rng.standard_normal(shape).astype(np.float32)
+    x = rng.uniform(-1.3, 1.3, size=(500, in_dim)).astype(np.float32)
+    got = oten.tensor_sampler(t, x, clamp, aligned, linear)
+    tt = torch.from_numpy(t).permute(in_dim, *range(in_dim)).unsqueeze(0)
+    grid = torch.from_numpy(x).reshape((1, 500) + (1,) * (in_dim - 1) + (in_dim,))
+    ref = F.grid_sample(tt, grid, mode="bilinear" if linear else "nearest",
+                        padding_mode="border" if clamp else "zeros", align_corners=aligned)
+    ref = ref.reshape(t.shape[-1], 500).T.numpy()
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
