@@ -183,7 +183,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int q_warps = quad == 3 ? 3 : 4;
         const int q_index = warp >> 2;
         const int n_chunks = p.cout >> 4;
-        int pix_img[kMaxItems], pix_oh[kMaxItems], pix_ow[kMaxItems];
+        // per item, fixed over the taps: the input element offset of the
+        // pixel's own position and channel chunk, its row / column, and the
+        // item's offset inside an A tile
+        long long item_e[kMaxItems];
+        int pix_oh[kMaxItems], pix_ow[kMaxItems];
+        uint32_t item_soff[kMaxItems];
         bool pix_ok[kMaxItems];
 
         auto epilogue = [&](int bl) -> bool {
@@ -221,18 +226,23 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             for (int i = 0; i < kMaxItems; ++i) {
                 const int item = xt + i * kXThreads;
                 pix_ok[i] = false;
-                pix_img[i] = pix_oh[i] = pix_ow[i] = 0;
+                pix_oh[i] = pix_ow[i] = 0;
+                item_e[i] = 0;
+                item_soff[i] = 0;
                 if (item < items) {
-                    const long long pix = blk * kTileM + item / cch;
+                    const int r = item / cch, c = item - (item / cch) * cch;
+                    item_soff[i] = sw128_offset(static_cast<uint32_t>(r), static_cast<uint32_t>(c * 8), kTileM);
+                    const long long pix = blk * kTileM + r;
                     if (pix < p.n_pix) {
                         pix_ok[i] = true;
                         pix_ow[i] = static_cast<int>(pix % p.w);
                         const long long rest = pix / p.w;
                         pix_oh[i] = static_cast<int>(rest % p.h);
-                        pix_img[i] = static_cast<int>(rest / p.h);
+                        item_e[i] = pix * p.cin + c * 8;  // NHWC: the pixel's own element offset
                     }
                 }
             }
+            int dh = -(p.kh / 2), dw = -(p.kw / 2);  // tap offsets, row-major over (kh, kw)
             for (int t = 0; ok && t < taps; ++t) {
                 const int g = bl * taps + t;
                 const int s = g % kRing;
@@ -241,18 +251,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                     ok = false;
                     break;
                 }
-                const int dh = t / p.kw - p.kh / 2, dw = t % p.kw - p.kw / 2;
+                const long long shift = dh * row_stride + static_cast<long long>(dw) * p.cin;
                 const uint32_t a_tile = a_base + static_cast<uint32_t>(s) * kATileBytes;
 #pragma unroll
                 for (int i = 0; i < kMaxItems; ++i) {
                     const int item = xt + i * kXThreads;
                     if (item >= items) break;
-                    const int r = item / cch, c = item - (item / cch) * cch;
                     uint32_t q0 = 0u, q1 = 0u, q2 = 0u, q3 = 0u;
                     const int ih = pix_oh[i] + dh, iw = pix_ow[i] + dw;
                     if (pix_ok[i] && ih >= 0 && ih < p.h && iw >= 0 && iw < p.w) {
-                        const long long e = (static_cast<long long>(pix_img[i]) * p.h + ih) * row_stride +
-                                            static_cast<long long>(iw) * p.cin + c * 8;
+                        const long long e = item_e[i] + shift;
                         if (p.x_f16) {
                             const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + e));
                             if (p.bf16) {
@@ -271,8 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                             q2 = pack2(b.x, b.y, p.bf16); q3 = pack2(b.z, b.w, p.bf16);
                         }
                     }
-                    st_shared_v4(a_tile + sw128_offset(static_cast<uint32_t>(r), static_cast<uint32_t>(c * 8), kTileM),
-                                 q0, q1, q2, q3);
+                    st_shared_v4(a_tile + item_soff[i], q0, q1, q2, q3);
+                }
+                if (++dw > p.kw - 1 - p.kw / 2) {
+                    dw = -(p.kw / 2);
+                    ++dh;
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
