@@ -12,17 +12,16 @@
 //   * every tap's weights stay resident in shared memory (K-major,
 //     128-byte swizzle, one COUT x 128-byte block per tap), loaded once by
 //     one bulk copy;
-//   * warps 0-14 stage the A tile of each (block, tap) into a ring of 4
+//   * warps 0-10 stage the A tile of each (block, tap) into a ring of 4
 //     shared-memory tiles (fp32 or fp16 input -> f16/bf16), waiting until
 //     the GEMM that last read the tile released it;
 //   * warp 15 issues, per tap, CIN/16 MMAs (M = 128, N = COUT) into the
 //     block's TMEM accumulator once the tap's tile is written; the first
 //     tap's MMAs and the others are separate code paths, so every MMA's
 //     accumulate flag is a compile-time constant;
-//   * accumulators are double buffered across blocks; after the first tap
-//     of block b is staged, warps 0-14 add the bias to block b-1's
-//     accumulator and store it (lane quadrant x 16-column chunks), while
-//     block b's GEMMs run.
+//   * accumulators are double buffered across blocks; warps 11-14 (one per
+//     TMEM lane quadrant) add the bias to each finished block and store it
+//     while the next block's GEMMs run, then free the half for block b + 2.
 // Every wait is bounded (ptx.cuh) and reports through the status word.
 #pragma once
 #include "ptx.cuh"
@@ -31,8 +30,9 @@ namespace rdvb {
 namespace convtc {
 
 constexpr int kTileM = 128;
-constexpr int kXWarps = 15;
+constexpr int kXWarps = 11;                       // staging warps 0-10
 constexpr int kXThreads = kXWarps * 32;
+constexpr int kEpiWarp0 = 11;                     // epilogue warps 11-14, one per TMEM lane quadrant
 constexpr int kIssueWarp = 15;
 constexpr int kThreads = 16 * 32;
 constexpr int kRing = 4;                          // A tiles in flight
@@ -41,7 +41,7 @@ constexpr int kMaxCin = 64;
 constexpr int kMaxCout = 256;                     // two accumulators of COUT columns in 512
 constexpr int kMaxTaps = 25;
 constexpr uint32_t kTmemCols = 512;
-constexpr int kMaxItems = 3;                      // (pixel, 8-channel) items per staging thread: 128 * 8 / 480
+constexpr int kMaxItems = 3;                      // (pixel, 8-channel) items per staging thread: 128 * 8 / 352
 
 struct Params {
     const void* x;            // [N*H*W, CIN] float32 or float16
@@ -62,8 +62,9 @@ enum : int {
     kBarAFull = 1,              // + ring slot: A tile written (one arrival per staging warp)
     kBarAEmpty = 1 + kRing,     // + ring slot: the GEMMs reading it are done (commit)
     kBarDFull = 1 + 2 * kRing,  // + half: a block's accumulator is final (commit)
-    kBarDrain = 3 + 2 * kRing,
-    kNumBars = 4 + 2 * kRing,
+    kBarDEmpty = 3 + 2 * kRing, // + half: the epilogue read it (one arrival per epilogue warp)
+    kBarDrain = 5 + 2 * kRing,
+    kNumBars = 6 + 2 * kRing,
 };
 constexpr uint32_t kBarBlockBytes = kNumBars * 8 + 16;
 
@@ -112,6 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         }
         mbar_init(bar(kBarDFull), 1);
         mbar_init(bar(kBarDFull + 1), 1);
+        mbar_init(bar(kBarDEmpty), 4);
+        mbar_init(bar(kBarDEmpty + 1), 4);
         mbar_init(bar(kBarDrain), 1);
         *abort = 0u;
         fence_mbarrier_init();
@@ -142,6 +145,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             bool issued = false;
             for (int bl = 0; ok && bl < n_mine; ++bl) {
                 const uint32_t d = tmem_base + (bl & 1) * d_cols;
+                // the accumulator half was read out by the epilogue of block bl - 2
+                if (bl >= 2 && !mbar_wait(bar(kBarDEmpty + (bl & 1)), ((bl >> 1) - 1) & 1, abort, &g_status,
+                                          kStatusTimeoutOther)) {
+                    ok = false;
+                    break;
+                }
                 for (int t = 0; t < taps; ++t) {
                     const int g = bl * taps + t;
                     const int s = g % kRing;
@@ -171,35 +180,23 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                     }
             }
         }
-    } else {
-        // ------------------------------------------ staging + epilogue
-        const int xt = threadIdx.x;  // 0 .. kXThreads - 1
-        const int cch = p.cin >> 3;  // 8-channel chunks per pixel
-        const int items = kTileM * cch;
-        const long long row_stride = static_cast<long long>(p.w) * p.cin;
+    } else if (warp >= kEpiWarp0) {
+        // -------------------------------------------------------- epilogue
+        // Warp (11 + q) % 4 = its TMEM lane quadrant: every 16-column chunk
+        // of its 32 pixels, + bias, to the output; then the half is free.
         const int quad = warp & 3;
-        // epilogue: this quadrant's 16-column chunks, split over its warps
-        // (quadrants 0-2: warps q, q+4, q+8, q+12; quadrant 3: 3, 7, 11)
-        const int q_warps = quad == 3 ? 3 : 4;
-        const int q_index = warp >> 2;
         const int n_chunks = p.cout >> 4;
-        // per item, fixed over the taps: the input element offset of the
-        // pixel's own position and channel chunk, its row / column, and the
-        // item's offset inside an A tile
-        long long item_e[kMaxItems];
-        int pix_oh[kMaxItems], pix_ow[kMaxItems];
-        uint32_t item_soff[kMaxItems];
-        bool pix_ok[kMaxItems];
-
-        auto epilogue = [&](int bl) -> bool {
+        for (int bl = 0; ok && bl < n_mine; ++bl) {
             const uint32_t half = bl & 1;
-            if (!mbar_wait_warp(bar(kBarDFull + half), (bl >> 1) & 1, abort, &g_status, kStatusTimeoutAccFull))
-                return false;
+            if (!mbar_wait_warp(bar(kBarDFull + half), (bl >> 1) & 1, abort, &g_status, kStatusTimeoutAccFull)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
             const long long pix = (static_cast<long long>(blockIdx.x) + static_cast<long long>(bl) * gridDim.x) *
                                       kTileM + quad * 32 + lane;
             const bool valid = pix < p.n_pix;
-            for (int c = q_index; c < n_chunks; c += q_warps) {
+            for (int c = 0; c < n_chunks; ++c) {
                 uint32_t r[16];
                 tmem_ld16(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + half * d_cols + 16u * c, r);
                 tmem_wait_ld(r);
@@ -216,8 +213,23 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 }
             }
             tc_fence_before();
-            return true;
-        };
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarDEmpty + half));
+        }
+        if (!ok) *abort = 1u;
+    } else {
+        // ------------------------------------------------------- staging
+        const int xt = threadIdx.x;  // 0 .. kXThreads - 1
+        const int cch = p.cin >> 3;  // 8-channel chunks per pixel
+        const int items = kTileM * cch;
+        const long long row_stride = static_cast<long long>(p.w) * p.cin;
+        // per item, fixed over the taps: the input element offset of the
+        // pixel's own position and channel chunk, its row / column, and the
+        // item's offset inside an A tile
+        long long item_e[kMaxItems];
+        int pix_oh[kMaxItems], pix_ow[kMaxItems];
+        uint32_t item_soff[kMaxItems];
+        bool pix_ok[kMaxItems];
 
         for (int bl = 0; ok && bl < n_mine; ++bl) {
             const long long blk = static_cast<long long>(blockIdx.x) + static_cast<long long>(bl) * gridDim.x;
@@ -288,11 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarAFull + s));
-                // the previous block's outputs, while this block's GEMMs run
-                if (t == 0 && bl > 0) ok = epilogue(bl - 1);
             }
         }
-        if (ok && n_mine > 0) ok = epilogue(n_mine - 1);
         if (!ok) *abort = 1u;
     }
 
