@@ -71,6 +71,10 @@ def ref_lib() -> ctypes.CDLL:
         lib.ref_winograd_inv.argtypes = [vp, vp]
         lib.ref_transmittance_rm.argtypes = [f32, f32, vp, vp, f32, f32, f32]
         lib.ref_transmittance_rm.restype = f32
+        lib.ref_random_sequence.argtypes = [vp, i32, i32, vp]
+        lib.ref_random_sequence.restype = None
+        lib.ref_transmittance_rt.argtypes = [f32, f32, vp, i32, i32, i32, vp, i32, vp, vp, f32, f32]
+        lib.ref_transmittance_rt.restype = f32
         lib.ref_downsample2x.argtypes = [vp, i32, i32, i32, vp]
         lib.ref_upsample2x.argtypes = [vp, i32, i32, i32, vp]
         lib.ref_concat.argtypes = [vp, i32, vp, i32, i32, vp]

@@ -215,3 +215,169 @@ def mlp_extinction(layers, input_relu: bool = False):
         a = np.maximum(p, np.float32(0.0)) if input_relu else p
         return mlp_eval(np.asarray(a, dtype=np.float32), layers)[:, 0].astype(np.float32)
     return ext
+
+
+# ---------------------------------------------------------------------------
+# Ratio tracking (RatiotrackingTransmittance, rdv/domain/volumes.py:144-170)
+# ---------------------------------------------------------------------------
+# The reference's generator (rdv/shaders/libraries/random_library.h:7-44):
+# three Tausworthe components and one LCG, combined by XOR; random() keeps
+# the low 23 bits as the mantissa of a float in [1, 2) and subtracts 1. Each
+# invocation starts from the dispatch's seeds spawned by its index
+# (random_library.h:256-268, index = gl_GlobalInvocationID.x for a Map
+# dispatch, i.e. the row). States are [R, 4] uint32 arrays.
+_TAUS = ((13, 19, 12, 4294967294), (2, 25, 4, 4294967288), (3, 11, 17, 4294967280))
+
+
+def random_step(state: np.ndarray) -> None:
+    """random_step (random_library.h:13-19), in place."""
+    for c, (s1, s2, s3, m) in enumerate(_TAUS):
+        z = state[:, c]
+        b = ((z << np.uint32(s1)) ^ z) >> np.uint32(s2)
+        state[:, c] = ((z & np.uint32(m)) << np.uint32(s3)) ^ b
+    state[:, 3] = state[:, 3] * np.uint32(1664525) + np.uint32(1013904223)
+
+
+def random_spawn(seeds, index: np.ndarray) -> np.ndarray:
+    """random_spawn (random_library.h:44-49) of the dispatch seeds for each
+    invocation index: the per-thread initial state."""
+    s = np.asarray(seeds, dtype=np.uint32).reshape(4)
+    i = np.asarray(index, dtype=np.int64).astype(np.uint32)  # two's complement, as GLSL's int -> uint
+    with np.errstate(over="ignore"):
+        st = np.stack([s[0] ^ (i ^ np.uint32(17)), s[1] ^ (i * np.uint32(123111171)), s[2] ^ (i + np.uint32(11)),
+                       s[3] ^ (i ^ (s[0] + np.uint32(13) * s[1]))], axis=1).astype(np.uint32)
+    random_step(st)
+    return st
+
+
+def random_draw(state: np.ndarray) -> np.ndarray:
+    """random() (random_library.h:27-34) for every row of state, in place."""
+    random_step(state)
+    v = state[:, 0] ^ state[:, 1] ^ state[:, 2] ^ state[:, 3]
+    return ((v & np.uint32(0x007FFFFF)) | np.uint32(0x3F800000)).view(np.float32) - np.float32(1.0)
+
+
+def voxel_majorant(grid: np.ndarray, x: np.ndarray, w: np.ndarray):
+    """VoxelMajorantField.forward (rdv/shaders/volumes/voxel_majorant_field.h):
+    grid [D, H, W] (z, y, x) float32; x, w [R, 3] object space. Returns the
+    cell's majorant and the distance along w to the cell's exit."""
+    dims = np.array([grid.shape[2], grid.shape[1], grid.shape[0]], dtype=np.int64)
+    f = dims.astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        pos = (x * np.float32(0.5) + np.float32(0.5)) * f
+        cell = np.clip(np.trunc(pos).astype(np.int64), 0, dims - 1)
+        vs = np.float32(2.0) / f
+        bmin = cell.astype(np.float32) * vs - np.float32(1.0)
+        bmax = bmin + vs
+        t0 = (bmin - x) / w
+        t1 = (bmax - x) / w
+        # GLSL max(a, b) = a < b ? b : a, min(a, b) = b < a ? b : a
+        texit = np.where(t0 < t1, t1, t0)
+        dist = np.where(texit[:, 1] < texit[:, 0], texit[:, 1], texit[:, 0])
+        dist = np.where(texit[:, 2] < dist, texit[:, 2], dist)
+    value = grid[cell[:, 2], cell[:, 1], cell[:, 0]]
+    return value.astype(np.float32), dist.astype(np.float32)
+
+
+def _log_f32(v: np.ndarray) -> np.ndarray:
+    """float32 log, correctly rounded (evaluated in float64)."""
+    return np.log(v.astype(np.float64)).astype(np.float32)
+
+
+def transmittance_rt(x, w, d, density_scale, extinction, majorant, state, counts=None):
+    """transmittance_rt (rdv/shaders/volumes/ratiotracking_transmittance_trait.h)
+    vectorised over rays in lock step, every operation in float32:
+
+        T = 1; for (safety < 1024 while d > 0):
+            maj = max(majorant(x, w, dist), 1e-12); dist = max(dist, 1e-6)
+            dt = min(dist, -log(1 - random()) / (maj * density_scale))
+            d -= dt; x += dt w
+            dt >= dist -> next iteration (left the majorant's cell)
+            d <= 0 -> return T
+            T *= 1 - extinction(x) / maj
+            T < 0.05: random() >= T -> return 0, else T = 1 (Russian roulette)
+        return T
+
+    `state` ([R, 4] uint32, each ray's generator) advances in place.
+    `majorant(x, w)` returns (value, distance); `extinction` maps [n, 3] to [n]."""
+    x = np.array(x, dtype=np.float32)
+    w = np.asarray(w, dtype=np.float32)
+    d = np.array(d, dtype=np.float32)
+    n = x.shape[0]
+    T = np.ones(n, dtype=np.float32)
+    out = np.ones(n, dtype=np.float32)
+    running = np.ones(n, dtype=bool)
+    ds = np.float32(density_scale)
+    for _ in range(1024):
+        ended = running & ~(d > 0)   # the loop condition failed: return T
+        out[ended] = T[ended]
+        running &= ~ended
+        act = np.nonzero(running)[0]
+        if act.size == 0:
+            break
+        maj, dist = majorant(x[act], w[act])
+        maj = np.where(maj < np.float32(1e-12), np.float32(1e-12), maj).astype(np.float32)
+        dist = np.where(dist < np.float32(1e-6), np.float32(1e-6), dist).astype(np.float32)
+        st = state[act]
+        u = random_draw(st)
+        with np.errstate(divide="ignore"):
+            q = (-_log_f32(np.float32(1.0) - u)) / (maj * ds)
+        dt = np.where(q < dist, q, dist).astype(np.float32)
+        d[act] = d[act] - dt
+        x[act] = x[act] + dt[:, None] * w[act]
+        moved_out = dt >= dist
+        reached = ~moved_out & (d[act] <= 0)
+        done = act[reached]
+        out[done] = T[done]
+        running[done] = False
+        coll = ~moved_out & ~reached
+        ci = act[coll]
+        if ci.size:
+            sigma = np.asarray(extinction(x[ci]), dtype=np.float32)
+            if counts is not None:
+                counts[ci] += 1
+            T[ci] = T[ci] * (np.float32(1.0) - sigma / maj[coll])
+            low = T[ci] < np.float32(0.05)
+            if low.any():
+                li = np.nonzero(coll)[0][low]   # positions inside act
+                sub = st[li]
+                u2 = random_draw(sub)
+                st[li] = sub
+                rays = act[li]
+                killed = u2 >= T[rays]
+                out[rays[killed]] = 0.0
+                running[rays[killed]] = False
+                T[rays[~killed]] = 1.0
+        state[act] = st
+    out[running] = T[running]
+    return out
+
+
+def ratiotracking_transmittance(origins, dirs, density_scale, extinction, grid, seeds, transform=None,
+                                index=None, return_evaluations: bool = False):
+    """RatiotrackingTransmittance.forward
+    (rdv/shaders/volumes/ratiotracking_transmittance.h): object space, slab
+    test, miss -> 1, entry clamp, then transmittance_rt over d = tMax - tMin
+    with ray r's generator spawned from `seeds` by index[r] (default r) and
+    a VoxelMajorantField over `grid` [D, H, W]."""
+    o, w = object_space(origins, dirs, transform)
+    tmin, tmax = ray_box(o, w)
+    miss = (tmax <= 0) | (tmin > tmax)
+    tmin = np.maximum(tmin, np.float32(0.0))
+    x = o + w * tmin[:, None]
+    d = tmax - tmin
+    n = o.shape[0]
+    out = np.ones(n, dtype=np.float32)
+    idx = np.arange(n) if index is None else np.asarray(index)
+    hit = np.nonzero(~miss)[0]
+    counts = np.zeros(hit.size, dtype=np.int64)
+    g = np.asarray(grid, dtype=np.float32)
+    if g.ndim == 4:
+        g = g[..., 0]
+    if hit.size:
+        state = random_spawn(seeds, idx[hit])
+        out[hit] = transmittance_rt(x[hit], w[hit], d[hit], density_scale, extinction,
+                                    lambda xx, ww: voxel_majorant(g, xx, ww), state, counts=counts)
+    if return_evaluations:
+        return out, int(counts.sum())
+    return out

@@ -36,15 +36,61 @@ static rdv_uvec3 gl_WorkGroupID = {0, 0, 0};
 // occupied workgroup does in the reference.
 static inline bool all_thread_sync(uint) { return false; }
 
+struct rdv_vec2 {
+    float x, y;
+    rdv_vec2() : x(0), y(0) {}
+    rdv_vec2(float a, float b) : x(a), y(b) {}
+};
 struct rdv_vec3 {
     float x, y, z;
     rdv_vec3() : x(0), y(0), z(0) {}
     rdv_vec3(float a, float b, float c) : x(a), y(b), z(c) {}
+    rdv_vec3(rdv_vec2 a, float c) : x(a.x), y(a.y), z(c) {}
 };
 static inline rdv_vec3 operator*(float s, rdv_vec3 v) { return rdv_vec3(s * v.x, s * v.y, s * v.z); }
 static inline rdv_vec3 operator*(rdv_vec3 v, float s) { return rdv_vec3(s * v.x, s * v.y, s * v.z); }
 static inline rdv_vec3 operator+(rdv_vec3 a, rdv_vec3 b) { return rdv_vec3(a.x + b.x, a.y + b.y, a.z + b.z); }
 static inline rdv_vec3& operator+=(rdv_vec3& a, rdv_vec3 b) { a.x += b.x; a.y += b.y; a.z += b.z; return a; }
+
+// More GLSL vector types, for libraries/random_library.h (the Taus + LCG
+// generator and its samplers): only the operations that file uses.
+struct rdv_vec4 {
+    float x, y, z, w;
+    rdv_vec4() : x(0), y(0), z(0), w(0) {}
+    rdv_vec4(float a, float b, float c, float d) : x(a), y(b), z(c), w(d) {}
+    rdv_vec4(rdv_vec2 a, rdv_vec2 b) : x(a.x), y(a.y), z(b.x), w(b.y) {}
+};
+struct rdv_uvec4 {
+    uint x, y, z, w;
+    rdv_uvec4() : x(0), y(0), z(0), w(0) {}
+    // GLSL's uvec4(int, ...) converts each component (two's complement wrap)
+    rdv_uvec4(long long a, long long b, long long c, long long d)
+        : x((uint)a), y((uint)b), z((uint)c), w((uint)d) {}
+};
+static inline rdv_uvec4 operator^(rdv_uvec4 a, rdv_uvec4 b) {
+    rdv_uvec4 r; r.x = a.x ^ b.x; r.y = a.y ^ b.y; r.z = a.z ^ b.z; r.w = a.w ^ b.w; return r;
+}
+static inline rdv_uvec4 operator+(rdv_uvec4 a, int s) {
+    rdv_uvec4 r; r.x = a.x + (uint)s; r.y = a.y + (uint)s; r.z = a.z + (uint)s; r.w = a.w + (uint)s; return r;
+}
+static inline float uintBitsToFloat(uint v) { float f; __builtin_memcpy(&f, &v, 4); return f; }
+static inline uint floatBitsToUint(float f) { uint v; __builtin_memcpy(&v, &f, 4); return v; }
+static inline rdv_uvec4 floatBitsToUint(rdv_vec4 v) {
+    rdv_uvec4 r; r.x = floatBitsToUint(v.x); r.y = floatBitsToUint(v.y); r.z = floatBitsToUint(v.z);
+    r.w = floatBitsToUint(v.w); return r;
+}
+static inline rdv_vec2 operator*(float s, rdv_vec2 v) { return rdv_vec2(s * v.x, s * v.y); }
+static inline rdv_vec2 operator*(rdv_vec2 a, rdv_vec2 b) { return rdv_vec2(a.x * b.x, a.y * b.y); }
+static inline rdv_vec2 operator+(rdv_vec2 a, rdv_vec2 b) { return rdv_vec2(a.x + b.x, a.y + b.y); }
+static inline rdv_vec4 operator*(rdv_vec4 a, rdv_vec4 b) { return rdv_vec4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w); }
+static inline rdv_vec4 operator+(rdv_vec4 a, rdv_vec4 b) { return rdv_vec4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+static inline rdv_vec3 operator*(rdv_vec3 a, rdv_vec3 b) { return rdv_vec3(a.x * b.x, a.y * b.y, a.z * b.z); }
+static inline rdv_vec3 operator*(double s, rdv_vec3 v) { return (float)s * v; }
+static inline float dot(rdv_vec3 a, rdv_vec3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+// GLSL's float log: C++ would widen `1.0 - random()` and evaluate in double.
+static inline float rdv_log(double v) { return std::log((float)v); }
+static inline float min(float a, double b) { return a < (float)b ? a : (float)b; }
+static inline float max(int a, double b) { return (float)a > (float)b ? (float)a : (float)b; }
 
 // GLSL max(float, float-literal) - the literal is a double in C++.
 static inline float max(float a, double b) { return a > (float)b ? a : (float)b; }

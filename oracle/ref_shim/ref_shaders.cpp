@@ -225,6 +225,64 @@ static float extinction(RmNode node, vec3 x) {
 #include "volumes/raymarching_transmittance_trait.h"
 #undef RDV_NODE
 
+// Ratio tracking (volumes/ratiotracking_transmittance_trait.h) with the
+// reference's own Taus + LCG generator (libraries/random_library.h). The
+// Makefile compiles a copy of random_library.h written into _ref/gen whose
+// only change is `inout uvec4 x` -> `uvec4& x` (GLSL inout parameters are
+// references; no macro can express that). The extinction is the analytic
+// field above; the majorant is a voxel grid looked up as
+// volumes/voxel_majorant_field.h does, restated here because that file's
+// GLSL array constructors do not compile as C++.
+#define vec2 rdv_vec2
+#define vec4 rdv_vec4
+#define uvec4 rdv_uvec4
+#define uvec3 rdv_uvec3
+#define layout(...)
+#define uniform static struct
+#define pi 3.1415926535897932384626433832795
+#define two_pi 6.283185307179586476925286766559
+#define log(x) rdv_log(x)
+#define random rdv_random  // stdlib's long random(void) has the same name
+static float min(float a, float b) { return a < b ? a : b; }
+// math_library.h's create_ortho_basis is only used by the direction
+// samplers, which the tracking loop never calls.
+static void create_ortho_basis(vec3, vec3& T, vec3& B) { T = vec3(1, 0, 0); B = vec3(0, 0, 1); }
+#define RDV_NODE rdv_random_init
+#include "random_library.h"
+#undef RDV_NODE
+
+struct RtNode {
+    float c0, c1;       // extinction c0 + c1 |x|^2, as RmNode
+    const float* grid;  // majorant voxels [D, H, W] (z, y, x)
+    int gd, gh, gw;
+};
+static float extinction(RtNode node, vec3 x) {
+    return node.c0 + node.c1 * (x.x * x.x + x.y * x.y + x.z * x.z);
+}
+static float majorant(RtNode node, vec3 x, vec3 w, float& distance) {
+    const int dim[3] = {node.gw, node.gh, node.gd};
+    const float xs[3] = {x.x, x.y, x.z}, ws[3] = {w.x, w.y, w.z};
+    int cell[3];
+    float texit[3];
+    for (int k = 0; k < 3; ++k) {
+        int c = (int)((xs[k] * 0.5f + 0.5f) * (float)dim[k]);
+        c = c < 0 ? 0 : (c > dim[k] - 1 ? dim[k] - 1 : c);
+        cell[k] = c;
+        const float vs = 2.0f / (float)dim[k];
+        const float bmin = (float)c * vs - 1.0f;
+        const float bmax = bmin + vs;
+        const float t0 = (bmin - xs[k]) / ws[k], t1 = (bmax - xs[k]) / ws[k];
+        texit[k] = t0 > t1 ? t0 : t1;
+    }
+    distance = min(min(texit[0], texit[1]), texit[2]);
+    return node.grid[((long)cell[2] * node.gh + cell[1]) * node.gw + cell[0]];
+}
+#define RDV_NODE RtNode
+#include "volumes/ratiotracking_transmittance_trait.h"
+#undef RDV_NODE
+#undef log
+#undef random
+
 // ---------------------------------------------------------------------------
 // extern "C" surface
 // ---------------------------------------------------------------------------
@@ -325,6 +383,25 @@ float ref_transmittance_rm(float c0, float c1, const float* x, const float* w, f
     RmNode node{c0, c1};
     return transmittance_rm(node, vec3(x[0], x[1], x[2]), vec3(w[0], w[1], w[2]), d, step_size,
                             density_scale);
+}
+
+// The per-thread generator state of invocation `index` (random_library.h's
+// init: the dispatch seeds spawned by the thread index), then n draws of
+// random().
+void ref_random_sequence(const unsigned* seeds, int index, int n, float* dst) {
+    random_seeds.seeds = uvec4(seeds[0], seeds[1], seeds[2], seeds[3]);
+    rdv_random_init(rdv_uvec3{(unsigned)index, 0u, 0u});
+    for (int i = 0; i < n; ++i) dst[i] = rdv_random();
+}
+
+// transmittance_rt for one ray segment (entry point x, direction w, length
+// d) on invocation `index`'s generator.
+float ref_transmittance_rt(float c0, float c1, const float* grid, int gd, int gh, int gw, const unsigned* seeds,
+                           int index, const float* x, const float* w, float d, float density_scale) {
+    random_seeds.seeds = uvec4(seeds[0], seeds[1], seeds[2], seeds[3]);
+    rdv_random_init(rdv_uvec3{(unsigned)index, 0u, 0u});
+    RtNode node{c0, c1, grid, gd, gh, gw};
+    return transmittance_rt(node, vec3(x[0], x[1], x[2]), vec3(w[0], w[1], w[2]), d, density_scale);
 }
 
 }  // extern "C"

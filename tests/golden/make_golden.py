@@ -8,8 +8,9 @@ Two sources, both the reference's own code:
 
 * ``oracle/_ref/libref_shaders.so`` -- the reference's scalar GLSL functions
   (maps/linear.h, relu.h, composite.h, tensors/linear_tensor_op.h,
-  relu_tensor_op.h, conv2d_tensor_op.h, the Winograd transforms, and
-  volumes/raymarching_transmittance_trait.h) compiled as C++ from the
+  relu_tensor_op.h, conv2d_tensor_op.h, the Winograd transforms,
+  volumes/raymarching_transmittance_trait.h, libraries/random_library.h and
+  volumes/ratiotracking_transmittance_trait.h) compiled as C++ from the
   reference checkout by ``make -C oracle ref``;
 * ``rdv/domain/nn.py``'s torch helper ``_winograd_transform_weight`` and its
   ``_WINOGRAD_G`` table, executed from the reference source. The package
@@ -156,6 +157,36 @@ def main():
     lib.ref_concat(ptr(x1), 16, ptr(x2), 8, 20, ptr(cat))
     np.savez_compressed(os.path.join(HERE, "resample.npz"), down_x=xs, down_y=down, up_x=xu, up_y=up,
                         cat_x1=x1, cat_x2=x2, cat_y=cat)
+    # --- ratio tracking: the generator and transmittance_rt -------------------
+    # random_library.h's per-invocation state (seeds spawned by the index)
+    # and its first 64 draws; then transmittance_rt over ray segments with
+    # the analytic extinction c0 + c1 |x|^2 and a 4x5x6 voxel majorant, for
+    # three media (dense: mostly Russian roulette; medium; thin).
+    seeds = np.array([777, 31337, 4242, 99991], dtype=np.uint32)
+    rng_index = np.array([0, 1, 2, 31, 1000, 65535, 123456789, 2 ** 31 - 1], dtype=np.int64)
+    rng_draws = np.zeros((rng_index.size, 64), dtype=np.float32)
+    for i, idx in enumerate(rng_index):
+        lib.ref_random_sequence(ptr(seeds), int(idx), 64, ptr(rng_draws[i]))
+    nr = 96
+    media = np.array([[1.5, 2.0, 1.0, 1.3], [0.2, 0.5, 1.0, 1.0], [0.05, 0.3, 3.0, 0.7]], dtype=np.float32)
+    rt_x = rng.uniform(-0.999, 0.999, size=(len(media), nr, 3)).astype(np.float32)
+    rt_w = rng.standard_normal((len(media), nr, 3)).astype(np.float32)
+    rt_w /= np.linalg.norm(rt_w, axis=2, keepdims=True)
+    rt_d = rng.uniform(0.0, 2.5, size=(len(media), nr)).astype(np.float32)
+    rt_d[:, :3] = [0.0, -0.1, 1e-4]
+    rt_index = rng.integers(0, 1 << 20, size=(len(media), nr)).astype(np.int64)
+    grids = np.zeros((len(media), 4, 5, 6), dtype=np.float32)
+    rt_T = np.zeros((len(media), nr), dtype=np.float32)
+    for m, (c0m, c1m, gscale, dsm) in enumerate(media):
+        grids[m] = (rng.uniform(0.5, 1.5, size=(4, 5, 6)) * (c0m + 3 * c1m) * gscale).astype(np.float32)
+        for i in range(nr):
+            rt_T[m, i] = lib.ref_transmittance_rt(
+                ctypes.c_float(c0m), ctypes.c_float(c1m), ptr(grids[m]), 4, 5, 6, ptr(seeds), int(rt_index[m, i]),
+                ptr(np.ascontiguousarray(rt_x[m, i])), ptr(np.ascontiguousarray(rt_w[m, i])),
+                ctypes.c_float(rt_d[m, i]), ctypes.c_float(dsm))
+    np.savez_compressed(os.path.join(HERE, "ratiotracking.npz"), seeds=seeds, rng_index=rng_index,
+                        rng_draws=rng_draws, media=media, x=rt_x, w=rt_w, d=rt_d, index=rt_index, grids=grids,
+                        T=rt_T)
     print("golden fixtures written to", HERE)
 
 

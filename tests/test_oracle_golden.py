@@ -103,6 +103,38 @@ def test_transmittance_restatement_matches_reference(golden):
     assert np.all(T[4:8] == 0.0)
 
 
+def test_generator_restatement_is_bit_exact(golden):
+    """random_spawn + random() of the oracle against the reference's own
+    random_library.h (64 draws for 8 invocation indices)."""
+    g = golden("ratiotracking.npz")
+    st = orm.random_spawn(g["seeds"], g["rng_index"])
+    draws = np.stack([orm.random_draw(st) for _ in range(64)], axis=1)
+    np.testing.assert_array_equal(draws, g["rng_draws"])
+    assert np.all((draws >= 0) & (draws < 1))
+
+
+def test_ratiotracking_restatement_matches_reference(golden):
+    """transmittance_rt over the fixture's ray segments: the same random
+    draws, collisions and Russian-roulette outcomes as the reference's own
+    loop (which evaluates 1 - sigma / maj in double, so values may differ
+    in the last bits)."""
+    g = golden("ratiotracking.npz")
+    for m, (c0, c1, _, ds) in enumerate(g["media"]):
+        def ext(p, c0=c0, c1=c1):
+            return (np.float32(c0) + np.float32(c1) * ((p[:, 0] * p[:, 0] + p[:, 1] * p[:, 1]) + p[:, 2] * p[:, 2])
+                    ).astype(np.float32)
+
+        grid = g["grids"][m]
+        state = orm.random_spawn(g["seeds"], g["index"][m])
+        T = orm.transmittance_rt(g["x"][m], g["w"][m], g["d"][m], ds, ext,
+                                 lambda x, w: orm.voxel_majorant(grid, x, w), state)
+        ref = g["T"][m]
+        np.testing.assert_allclose(T, ref, rtol=0, atol=1e-6)
+        np.testing.assert_array_equal(T == 0, ref == 0)
+        np.testing.assert_array_equal(T == 1, ref == 1)
+    assert (g["T"] == 0).any() and ((g["T"] > 0) & (g["T"] < 1)).any()
+
+
 @pytest.mark.skipif(not ref_lib_available(), reason="reference shader library not built")
 def test_live_reference_library_agrees_with_fixture(golden):
     """Where oracle/_ref is present, re-run one fixture through it."""
