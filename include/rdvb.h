@@ -306,6 +306,34 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
                           const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
                           size_t workspace_bytes, float* out, void* stream);
 
+/* RatiotrackingTransmittance (rdv/domain/volumes.py:144-170;
+ * rdv/shaders/volumes/ratiotracking_transmittance.h and
+ * ratiotracking_transmittance_trait.h) with a VoxelMajorantField
+ * (volumes.py:196-212, rdv/shaders/volumes/voxel_majorant_field.h):
+ * out[i] = the ratio-tracking estimate of the transmittance along ray i of
+ * rays [n_rays, 6]. Object space, box clip and misses as
+ * rdvb_transmittance_rm; then from the entry point, at most 1024 times while
+ * the segment lasts: free-flight step dt = min(cell exit distance,
+ * -log(1 - random()) / (majorant * density_scale)); on a collision inside the
+ * cell T *= 1 - extinction(x) / majorant, and below 0.05 Russian roulette
+ * (random() >= T gives 0, else T = 1).
+ * majorant: fp32 device grid [D, H, W] (z, y, x; the Grid[3, 1]'s tensor
+ * without its channel), majorant_dims = {D, H, W} (host); the cell of x is
+ * clamp(int((x * 0.5 + 0.5) * (W, H, D)), 0, dims - 1).
+ * seeds: 4 host uint32, the dispatch's generator seeds (the reference draws
+ * them per dispatch, core/_common.py:66-75); ray i draws from the seeds
+ * spawned by index i (libraries/random_library.h:44-49, :256-268), the
+ * Taus + LCG generator of random_library.h:7-34.
+ * The extinction chain as rdvb_transmittance_rm (any Linear / LinearFast /
+ * ReLU chain 3 -> ... -> 1, evaluated on the CUDA cores). workspace: 256
+ * bytes, 256-byte aligned; bytes 8-15 hold the number of extinction
+ * evaluations of the call. */
+int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
+                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int n_layers,
+                          const int* dims, const float* const* weights, const float* const* biases,
+                          const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, float* out,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,7 +18,7 @@ from .conv import (Conv2DTensorOp, Conv2DTensorOpFast, Conv2DTensorOpSimple, Con
                    Conv2DTensorOpWindow3x3, Conv2DTensorOpWinograd3x3, Conv3x3Winograd, conv2d_direct,
                    _winograd_transform_weight)
 from .rendering import Cameras, VolumeRenderer
-from .volumes import RaymarchingTransmittance
+from .volumes import RaymarchingTransmittance, RatiotrackingTransmittance, TensorGrid, VoxelMajorantField
 from ._native import RdvbError, device_status
 
 __all__ = [
@@ -29,6 +29,7 @@ __all__ = [
     "LinearTensorOpSimple", "LinearTensorOpSmall", "Downsample2xTensorOp", "Upsample2xTensorOp", "ConcatTensorOp",
     "Conv2DTensorOp", "Conv2DTensorOpFast", "Conv2DTensorOpSimple", "Conv2DTensorOpSimple3x3",
     "Conv2DTensorOpWindow3x3", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
-    "Cameras", "VolumeRenderer", "RaymarchingTransmittance",
+    "Cameras", "VolumeRenderer", "RaymarchingTransmittance", "RatiotrackingTransmittance", "TensorGrid",
+    "VoxelMajorantField",
     "RdvbError", "device_status",
 ]

@@ -58,6 +58,8 @@ SIGNATURES = {
     "rdvb_transmittance_workspace_bytes": (_c_i64, [_c_i64, _c_int, _vp, _vp]),
     "rdvb_transmittance_rm": (_c_int, [_vp, _c_i64, _vp, _c_f, _c_f, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
                                        ctypes.c_size_t, _vp, _vp]),
+    "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int,
+                                       _vp, ctypes.c_size_t, _vp, _vp]),
 }
 
 
@@ -127,6 +129,13 @@ def float_array(values):
     arr = (_c_f * len(values))()
     for i, v in enumerate(values):
         arr[i] = float(v)
+    return arr
+
+
+def uint32_array(values):
+    arr = (_c_u32 * len(values))()
+    for i, v in enumerate(values):
+        arr[i] = int(v) & 0xFFFFFFFF
     return arr
 
 

@@ -54,6 +54,7 @@ struct DeviceInfo {
     size_t simt_smem_set = 0;
     size_t wino_smem_set[2] = {};
     size_t trm_smem_set = 0;
+    size_t rt_smem_set = 0;
     size_t conv_tc_smem_set = 0;
 };
 constexpr int kMaxDevices = 64;
@@ -919,6 +920,87 @@ MarchWorkspace march_workspace(int64_t n_rays, int n_layers, const int* dims) {
 }
 }  // namespace
 
+namespace {
+// Object-space transform of the volume nodes: L = inverse of the 3x3 part
+// of the node's mat4x3 (columns M[0..2]), O = M[3]
+// (raymarching_transmittance.h:4-8, ratiotracking_transmittance.h:4-8);
+// identity when NULL. The inverse is formed in double, rounded to float.
+int trm_object_space(const float* transform, rdvb::trm::Params& p) {
+    double M[3][3] = {{1, 0, 0}, {0, 1, 0}, {0, 0, 1}};  // M[row][col]
+    if (transform) {
+        for (int c = 0; c < 3; ++c)
+            for (int r = 0; r < 3; ++r) M[r][c] = transform[3 * c + r];
+        for (int r = 0; r < 3; ++r) p.O[r] = transform[9 + r];
+    }
+    const double det = M[0][0] * (M[1][1] * M[2][2] - M[1][2] * M[2][1]) -
+                       M[0][1] * (M[1][0] * M[2][2] - M[1][2] * M[2][0]) +
+                       M[0][2] * (M[1][0] * M[2][1] - M[1][1] * M[2][0]);
+    if (!(std::fabs(det) > 0.0)) return fail(RDVB_ERR_INVALID_ARG, "the transform's 3x3 part is singular");
+    double inv[3][3];
+    inv[0][0] = (M[1][1] * M[2][2] - M[1][2] * M[2][1]) / det;
+    inv[0][1] = (M[0][2] * M[2][1] - M[0][1] * M[2][2]) / det;
+    inv[0][2] = (M[0][1] * M[1][2] - M[0][2] * M[1][1]) / det;
+    inv[1][0] = (M[1][2] * M[2][0] - M[1][0] * M[2][2]) / det;
+    inv[1][1] = (M[0][0] * M[2][2] - M[0][2] * M[2][0]) / det;
+    inv[1][2] = (M[0][2] * M[1][0] - M[0][0] * M[1][2]) / det;
+    inv[2][0] = (M[1][0] * M[2][1] - M[1][1] * M[2][0]) / det;
+    inv[2][1] = (M[0][1] * M[2][0] - M[0][0] * M[2][1]) / det;
+    inv[2][2] = (M[0][0] * M[1][1] - M[0][1] * M[1][0]) / det;
+    for (int r = 0; r < 3; ++r)
+        for (int c = 0; c < 3; ++c) p.L[3 * r + c] = static_cast<float>(inv[r][c]);
+    return RDVB_OK;
+}
+
+// The CUDA-core march kernels: the chain's shared-memory weight image, then
+// one launch of as many persistent 128-thread CTAs as fit (rays handed out
+// by the counter at the start of the workspace).
+int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const float* const* weights,
+                      const float* const* biases, const int* layer_flags, void* workspace, DeviceInfo* dev,
+                      cudaStream_t st, bool ratio_tracking) {
+    using namespace rdvb::trm;
+    int off = 0;
+    for (int l = 0; l < n_layers; ++l) {
+        Layer& L = p.layer[l];
+        L.W = weights[l];
+        L.b = biases[l];
+        L.K = dims[l];
+        L.N = dims[l + 1];
+        L.chunk = L.N <= 4 ? 4 : 32;
+        L.math = layer_flags[l] & 3;
+        L.relu = (layer_flags[l] & RDVB_LAYER_RELU) ? 1 : 0;
+        L.w_off = off;
+        off += ((L.N + L.chunk - 1) / L.chunk) * L.chunk * L.K;
+    }
+    for (int l = 0; l < n_layers; ++l) {
+        p.layer[l].b_off = off;
+        off += (dims[l + 1] + 3) & ~3;
+    }
+    p.w_floats = off;
+    const size_t smem = static_cast<size_t>((off + 3) & ~3) * 4 + static_cast<size_t>(2 * p.maxw) * kThreads * 4;
+    if (smem > static_cast<size_t>(dev->max_smem_optin))
+        return fail(RDVB_ERR_UNSUPPORTED, "the extinction MLP needs %zu bytes of shared memory", smem);
+    auto kernel = ratio_tracking ? ratiotracking_kernel : transmittance_kernel;
+    size_t& smem_set = ratio_tracking ? dev->rt_smem_set : dev->trm_smem_set;
+    if (smem_set < smem) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(march): %s", cudaGetErrorString(e));
+        smem_set = smem;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s",
+                                      cudaGetErrorString(e));
+    per_sm = std::max(per_sm, 1);
+    const long long want = (p.n_rays + kThreads - 1) / kThreads;
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * dev->sm_count * per_sm)));
+    e = cudaMemsetAsync(workspace, 0, 16, st);
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    kernel<<<grid, kThreads, smem, st>>>(p);
+    return check_launch(ratio_tracking ? "ratiotracking_kernel" : "transmittance_kernel");
+}
+}  // namespace
+
+
 int64_t rdvb_transmittance_workspace_bytes(int64_t n_rays, int n_layers, const int* dims, const int* layer_flags) {
     if (n_rays < 0 || n_layers < 1 || n_layers > rdvb::trm::kMaxLayers || !dims || !layer_flags) return 0;
     if (!march_on_tensor_cores(n_layers, dims, layer_flags)) return 256;
@@ -970,30 +1052,7 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
     p.n_layers = n_layers;
     p.input_relu = input_relu ? 1 : 0;
     p.maxw = maxw;
-    // object-space transform: L = inverse of the 3x3 part (columns M[0..2]),
-    // O = M[3] (raymarching_transmittance.h:4-8); identity when NULL
-    double M[3][3] = {{1, 0, 0}, {0, 1, 0}, {0, 0, 1}};  // M[row][col]
-    if (transform) {
-        for (int c = 0; c < 3; ++c)
-            for (int r = 0; r < 3; ++r) M[r][c] = transform[3 * c + r];
-        for (int r = 0; r < 3; ++r) p.O[r] = transform[9 + r];
-    }
-    const double det = M[0][0] * (M[1][1] * M[2][2] - M[1][2] * M[2][1]) -
-                       M[0][1] * (M[1][0] * M[2][2] - M[1][2] * M[2][0]) +
-                       M[0][2] * (M[1][0] * M[2][1] - M[1][1] * M[2][0]);
-    if (!(std::fabs(det) > 0.0)) return fail(RDVB_ERR_INVALID_ARG, "the transform's 3x3 part is singular");
-    double inv[3][3];
-    inv[0][0] = (M[1][1] * M[2][2] - M[1][2] * M[2][1]) / det;
-    inv[0][1] = (M[0][2] * M[2][1] - M[0][1] * M[2][2]) / det;
-    inv[0][2] = (M[0][1] * M[1][2] - M[0][2] * M[1][1]) / det;
-    inv[1][0] = (M[1][2] * M[2][0] - M[1][0] * M[2][2]) / det;
-    inv[1][1] = (M[0][0] * M[2][2] - M[0][2] * M[2][0]) / det;
-    inv[1][2] = (M[0][2] * M[1][0] - M[0][0] * M[1][2]) / det;
-    inv[2][0] = (M[1][0] * M[2][1] - M[1][1] * M[2][0]) / det;
-    inv[2][1] = (M[0][1] * M[2][0] - M[0][0] * M[2][1]) / det;
-    inv[2][2] = (M[0][0] * M[1][1] - M[0][1] * M[1][0]) / det;
-    for (int r = 0; r < 3; ++r)
-        for (int c = 0; c < 3; ++c) p.L[3 * r + c] = static_cast<float>(inv[r][c]);
+    if (int rc = trm_object_space(transform, p)) return rc;
     if (tc) {
         // tensor-core march: pack the chain into the workspace, then per
         // batch of rays: setup -> fused MLP over the chunks -> combine
@@ -1056,44 +1115,64 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
         }
         return RDVB_OK;
     }
-    int off = 0;
-    for (int l = 0; l < n_layers; ++l) {
-        Layer& L = p.layer[l];
-        L.W = weights[l];
-        L.b = biases[l];
-        L.K = dims[l];
-        L.N = dims[l + 1];
-        L.chunk = L.N <= 4 ? 4 : 32;
-        L.math = layer_flags[l] & 3;
-        L.relu = (layer_flags[l] & RDVB_LAYER_RELU) ? 1 : 0;
-        L.w_off = off;
-        off += ((L.N + L.chunk - 1) / L.chunk) * L.chunk * L.K;
+    return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev, st, false);
+}
+
+int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
+                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int n_layers,
+                          const int* dims, const float* const* weights, const float* const* biases,
+                          const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, float* out,
+                          void* stream) {
+    using namespace rdvb::trm;
+    if (n_rays < 0) return fail(RDVB_ERR_INVALID_ARG, "n_rays must be >= 0");
+    if (n_layers < 1 || n_layers > kMaxLayers)
+        return fail(RDVB_ERR_INVALID_ARG, "n_layers must be in [1, %d], got %d", kMaxLayers, n_layers);
+    if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
+    if (dims[0] != 3 || dims[n_layers] != 1)
+        return fail(RDVB_ERR_INVALID_ARG, "the extinction must map 3 -> 1, got %d -> %d", dims[0], dims[n_layers]);
+    if (!weights || !biases) return fail(RDVB_ERR_INVALID_ARG, "weights and biases must not be NULL");
+    int maxw = 3;
+    for (int l = 0; l <= n_layers; ++l) {
+        if (dims[l] > kMaxWidth) return fail(RDVB_ERR_UNSUPPORTED, "widths must be <= %d, got %d", kMaxWidth, dims[l]);
+        maxw = std::max(maxw, dims[l]);
     }
-    for (int l = 0; l < n_layers; ++l) {
-        p.layer[l].b_off = off;
-        off += (dims[l + 1] + 3) & ~3;
-    }
-    p.w_floats = off;
-    const size_t smem = static_cast<size_t>((off + 3) & ~3) * 4 + static_cast<size_t>(2 * maxw) * kThreads * 4;
-    if (smem > static_cast<size_t>(dev->max_smem_optin))
-        return fail(RDVB_ERR_UNSUPPORTED, "the extinction MLP needs %zu bytes of shared memory", smem);
-    if (dev->trm_smem_set < smem) {
-        cudaError_t e = cudaFuncSetAttribute(transmittance_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(transmittance): %s", cudaGetErrorString(e));
-        dev->trm_smem_set = smem;
-    }
-    int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, transmittance_kernel, kThreads, smem);
-    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s",
-                                      cudaGetErrorString(e));
-    per_sm = std::max(per_sm, 1);
-    const long long want = (n_rays + kThreads - 1) / kThreads;
-    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * dev->sm_count * per_sm)));
-    e = cudaMemsetAsync(workspace, 0, 16, st);
-    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    transmittance_kernel<<<grid, kThreads, smem, st>>>(p);
-    return check_launch("transmittance_kernel");
+    for (int l = 0; l < n_layers; ++l)
+        if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "layer %d has a NULL weight or bias", l);
+    if (!majorant_dims || !seeds) return fail(RDVB_ERR_INVALID_ARG, "majorant_dims and seeds must not be NULL");
+    for (int k = 0; k < 3; ++k)
+        if (majorant_dims[k] < 1)
+            return fail(RDVB_ERR_INVALID_ARG, "majorant_dims must be positive, got %d", majorant_dims[k]);
+    if (1LL * majorant_dims[0] * majorant_dims[1] * majorant_dims[2] > (1LL << 31))
+        return fail(RDVB_ERR_UNSUPPORTED, "the majorant grid must have at most 2^31 cells");
+    if (n_rays > 0x7fffffffLL - (1LL << 24))
+        return fail(RDVB_ERR_UNSUPPORTED, "at most %lld rays per call", 0x7fffffffLL - (1LL << 24));
+    if (n_rays == 0) return RDVB_OK;
+    if (!rays || !out || !majorant) return fail(RDVB_ERR_INVALID_ARG, "rays, majorant and out must not be NULL");
+    if (!aligned(rays, 4) || !aligned(out, 4) || !aligned(majorant, 4))
+        return fail(RDVB_ERR_INVALID_ARG, "rays, majorant and out must be 4-byte aligned");
+    if (!workspace || !aligned(workspace, 256) || workspace_bytes < 256)
+        return fail(RDVB_ERR_INVALID_ARG, "workspace must be 256-byte aligned and hold 256 bytes");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.rays = rays;
+    p.out = out;
+    p.n_rays = n_rays;
+    p.counter = static_cast<int*>(workspace);
+    p.evaluations = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + 8);
+    p.scale = density_scale;
+    p.n_layers = n_layers;
+    p.input_relu = input_relu ? 1 : 0;
+    p.maxw = maxw;
+    p.maj = majorant;
+    p.mdim[0] = majorant_dims[2];  // x: W
+    p.mdim[1] = majorant_dims[1];  // y: H
+    p.mdim[2] = majorant_dims[0];  // z: D
+    for (int k = 0; k < 4; ++k) p.seeds[k] = seeds[k];
+    if (int rc = trm_object_space(transform, p)) return rc;
+    return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev,
+                             static_cast<cudaStream_t>(stream), true);
 }
 
 int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, float* out,

@@ -64,6 +64,10 @@ struct Params {
     int maxw;               // widest activation (>= 3)
     int w_floats;           // floats of the shared weight image (weight blocks, then biases)
     Layer layer[kMaxLayers];
+    // ratiotracking_kernel only
+    const float* maj;       // majorant voxels [D, H, W] (z, y, x)
+    int mdim[3];            // W, H, D: cells along x, y, z
+    unsigned seeds[4];      // the dispatch's generator seeds
 };
 
 __device__ __forceinline__ float stage_val(float v, int math) {
@@ -181,13 +185,10 @@ __device__ __forceinline__ bool march_entry(const float* __restrict__ r, const f
     return true;
 }
 
-__global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_constant__ Params p) {
-    extern __shared__ float sm[];
-    float* wsm = sm;                                   // weight blocks, then biases
-    float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
-    float* act1 = act0 + p.maxw * kThreads;
-    // stage every layer once: block of outputs o0..o0+CH-1 as [K][CH], values
-    // rounded to the layer's operand format, zero beyond N
+// Stages every layer once into shared memory: block of outputs o0..o0+CH-1
+// as [K][CH], values rounded to the layer's operand format, zero beyond N;
+// then the biases.
+__device__ __forceinline__ void stage_chain(const Params& p, float* wsm) {
     for (int l = 0; l < p.n_layers; ++l) {
         const Layer L = p.layer[l];
         const int nb = (L.N + L.chunk - 1) / L.chunk;
@@ -200,6 +201,14 @@ __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_co
         for (int i = threadIdx.x; i < L.N; i += kThreads) wsm[L.b_off + i] = L.b[i];
     }
     __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_constant__ Params p) {
+    extern __shared__ float sm[];
+    float* wsm = sm;                                   // weight blocks, then biases
+    float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
+    float* act1 = act0 + p.maxw * kThreads;
+    stage_chain(p, wsm);
     const float* bsm = wsm;  // b_off values index the same image
 
     long long ray = -1;
@@ -244,6 +253,129 @@ __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_co
             my_evals += static_cast<unsigned long long>(steps);
             ray = -1;
         }
+    }
+    if (my_evals) atomicAdd(p.evaluations, my_evals);
+}
+
+// ---------------------------------------------------------------------------
+// RatiotrackingTransmittance (rdv/shaders/volumes/ratiotracking_transmittance.h,
+// ratiotracking_transmittance_trait.h): majorant-based ratio tracking with
+// Russian roulette, one persistent thread per ray.
+//
+// Generator: rdv/shaders/libraries/random_library.h:7-49 -- three
+// Tausworthe components and an LCG, XOR-combined; random() = the low 23
+// bits as a mantissa in [1, 2), minus 1. Ray r draws from the dispatch
+// seeds spawned by its row index r (the reference's per-invocation init,
+// random_library.h:256-268, with gl_GlobalInvocationID.x = row), so every
+// ray's sequence is independent of scheduling.
+// Majorant: VoxelMajorantField (rdv/shaders/volumes/voxel_majorant_field.h)
+// over a [D, H, W] grid: the cell holding x, and the distance along w to
+// that cell's exit.
+// The loop (at most 1024 iterations):
+//   maj = max(majorant, 1e-12), dist = max(exit distance, 1e-6)
+//   dt = min(dist, -log(1 - random()) / (maj * density_scale))
+//   d -= dt, x += dt w;  dt >= dist -> next cell;  d <= 0 -> done
+//   T *= 1 - extinction(x) / maj;  T < 0.05 -> roulette: random() >= T
+//   returns 0, else T = 1.
+// Every operation is a separately rounded fp32 operation (no contraction);
+// log is CUDA's logf.
+struct Rng {
+    unsigned x, y, z, w;
+};
+
+__device__ __forceinline__ unsigned taus_step(unsigned z, int s1, int s2, int s3, unsigned m) {
+    const unsigned b = ((z << s1) ^ z) >> s2;
+    return ((z & m) << s3) ^ b;
+}
+
+__device__ __forceinline__ void rng_step(Rng& r) {
+    r.x = taus_step(r.x, 13, 19, 12, 4294967294u);
+    r.y = taus_step(r.y, 2, 25, 4, 4294967288u);
+    r.z = taus_step(r.z, 3, 11, 17, 4294967280u);
+    r.w = 1664525u * r.w + 1013904223u;
+}
+
+__device__ __forceinline__ float rng_uniform(Rng& r) {
+    rng_step(r);
+    const unsigned v = r.x ^ r.y ^ r.z ^ r.w;
+    return __fsub_rn(__uint_as_float((v & 0x007FFFFFu) | 0x3F800000u), 1.0f);
+}
+
+// random_spawn(seeds, index): the index's int arithmetic wraps, as unsigned.
+__device__ __forceinline__ Rng rng_spawn(const unsigned (&s)[4], unsigned index) {
+    Rng r;
+    r.x = s[0] ^ (index ^ 17u);
+    r.y = s[1] ^ (index * 123111171u);
+    r.z = s[2] ^ (index + 11u);
+    r.w = s[3] ^ (index ^ (s[0] + 13u * s[1]));
+    rng_step(r);
+    return r;
+}
+
+__device__ __forceinline__ float voxel_majorant(const Params& p, const float (&x)[3], const float (&w)[3],
+                                                float& dist) {
+    int cell[3];
+    float texit[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float f = static_cast<float>(p.mdim[k]);
+        int c = static_cast<int>(__fmul_rn(__fadd_rn(__fmul_rn(x[k], 0.5f), 0.5f), f));  // toward zero
+        c = min(max(c, 0), p.mdim[k] - 1);
+        cell[k] = c;
+        const float vs = __fdiv_rn(2.0f, f);
+        const float bmin = __fsub_rn(__fmul_rn(static_cast<float>(c), vs), 1.0f);
+        const float bmax = __fadd_rn(bmin, vs);
+        const float t0 = __fdiv_rn(__fsub_rn(bmin, x[k]), w[k]);
+        const float t1 = __fdiv_rn(__fsub_rn(bmax, x[k]), w[k]);
+        texit[k] = t0 < t1 ? t1 : t0;  // GLSL max
+    }
+    dist = texit[1] < texit[0] ? texit[1] : texit[0];  // GLSL min
+    dist = texit[2] < dist ? texit[2] : dist;
+    return __ldg(p.maj + (static_cast<long long>(cell[2]) * p.mdim[1] + cell[1]) * p.mdim[0] + cell[0]);
+}
+
+constexpr int kRtSafety = 1024;  // ratiotracking_transmittance_trait.h's loop cap
+
+__global__ void __launch_bounds__(kThreads) ratiotracking_kernel(const __grid_constant__ Params p) {
+    extern __shared__ float sm[];
+    float* wsm = sm;
+    float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
+    float* act1 = act0 + p.maxw * kThreads;
+    stage_chain(p, wsm);
+    const float* bsm = wsm;
+    unsigned long long my_evals = 0;
+    while (true) {
+        const long long ray = atomicAdd(p.counter, 1);
+        if (ray >= p.n_rays) break;
+        float x[3], w[3], d = 0.0f;
+        float T = 1.0f;  // a ray that misses the volume is fully transparent
+        if (march_entry(p.rays + ray * 6, p.L, p.O, x, w, d)) {
+            Rng r = rng_spawn(p.seeds, static_cast<unsigned>(ray));
+            for (int safety = 0; d > 0.0f && safety < kRtSafety; ++safety) {
+                float dist;
+                float maj = voxel_majorant(p, x, w, dist);
+                maj = maj < 1e-12f ? 1e-12f : maj;
+                dist = dist < 1e-6f ? 1e-6f : dist;
+                const float q = __fdiv_rn(-logf(__fsub_rn(1.0f, rng_uniform(r))), __fmul_rn(maj, p.scale));
+                const float dt = q < dist ? q : dist;  // free-flight distance
+                d = __fsub_rn(d, dt);
+#pragma unroll
+                for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(dt, w[k]));
+                if (dt >= dist) continue;  // left the majorant's cell
+                if (d <= 0.0f) break;      // reached the end without a collision
+                const float sigma = extinction(p, wsm, bsm, act0, act1, x);
+                ++my_evals;
+                T = __fmul_rn(T, __fsub_rn(1.0f, __fdiv_rn(sigma, maj)));
+                if (T < 0.05f) {
+                    if (rng_uniform(r) >= T) {
+                        T = 0.0f;
+                        break;
+                    }
+                    T = 1.0f;  // Russian roulette survivor
+                }
+            }
+        }
+        p.out[ray] = T;
     }
     if (my_evals) atomicAdd(p.evaluations, my_evals);
 }

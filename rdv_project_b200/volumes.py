@@ -14,10 +14,23 @@ fp32 chains march one ray per CUDA thread like the reference's loop;
 float16 / bfloat16 (LinearFast) chains evaluate the steps in 128-step chunks
 with the fused tensor-core MLP kernel.
 
-``Cameras(...) >> node`` composes a camera grid with the node; calling the
+``RatiotrackingTransmittance(extinction, majorant, transform=None,
+density_scale=1.0)`` mirrors rdv/domain/volumes.py:144-170: the same
+``Map[6, 1]`` estimated by majorant-based ratio tracking with Russian
+roulette (rdv/shaders/volumes/ratiotracking_transmittance.h and
+ratiotracking_transmittance_trait.h), one CUDA thread per ray
+(rdvb_transmittance_rt). ``majorant`` is a ``VoxelMajorantField`` (or, as
+in the reference's ``_as_majorant_field``, a bare ``TensorGrid`` / tensor
+``[D, H, W, 1]`` wrapped as one). Each call draws fresh generator seeds, as
+the reference does per dispatch; ``node(rays, seeds=(s0, s1, s2, s3))``
+fixes them for a reproducible estimate.
+
+``Cameras(...) >> node`` composes a camera grid with either node; calling the
 composition returns ``[num_cameras, height, width, 1]``.
 """
 from __future__ import annotations
+
+import random as _random
 
 import torch
 
@@ -107,3 +120,84 @@ class RaymarchingTransmittance(Map):
         if st is None or st["ws"] is None:
             return 0
         return int(st["ws"][8:16].view(torch.int64).item())
+
+
+class TensorGrid:
+    """Grid[IN, OUT] over a tensor whose last dimension is OUT (the
+    reference's TensorGrid, rdv/maths/__init__.py:487-505; IN = ndim - 1,
+    addressed row-major, rdv/shaders/grids/tensor_grid.h)."""
+
+    def __init__(self, data):
+        t = data._tensor if isinstance(data, RDVObject) else torch.as_tensor(data)
+        assert t.dim() >= 2, "a TensorGrid needs at least one index dimension and the OUT dimension"
+        self.data = t
+        self.IN = t.dim() - 1
+        self.OUT = t.shape[-1]
+        self.shape = list(t.shape[:-1])
+
+
+class VoxelMajorantField:
+    """Map[6, 2] (rdv/domain/volumes.py:196-212,
+    rdv/shaders/volumes/voxel_majorant_field.h): for an object-space
+    position and direction, the majorant of the voxel holding the position
+    and the distance along the direction to that voxel's exit. ``grid`` is a
+    Grid[3, 1] over [-1, 1]^3: a TensorGrid, or its tensor [D, H, W, 1]."""
+
+    def __init__(self, grid):
+        if not isinstance(grid, TensorGrid):
+            grid = TensorGrid(grid)
+        assert grid.IN == 3 and grid.OUT == 1, "the majorant grid must be a Grid[3, 1]"
+        self.grid = grid
+
+
+def _as_majorant_field(majorant) -> VoxelMajorantField:
+    """volumes.py:227-242: a field as given, a Grid[3, 1] wrapped as a voxel field."""
+    if isinstance(majorant, VoxelMajorantField):
+        return majorant
+    if isinstance(majorant, (TensorGrid, torch.Tensor, RDVObject)):
+        return VoxelMajorantField(majorant)
+    raise NotImplementedError("majorant must be a VoxelMajorantField or a Grid[3, 1]")
+
+
+def _draw_seeds():
+    """Per-dispatch seeds as the reference draws them: 4 integers in
+    [128, 2^30) (core/_common.py:66-75)."""
+    return tuple(_random.randint(128, (1 << 30) - 1) for _ in range(4))
+
+
+class RatiotrackingTransmittance(RaymarchingTransmittance):
+    """Map[6, 1]: ray -> ratio-tracking estimate of the transmittance."""
+
+    def __init__(self, extinction: Map, majorant, transform=None, density_scale: float = 1.0):
+        super().__init__(extinction, transform=transform, density_scale=density_scale)
+        del self.step_size
+        self.majorant = _as_majorant_field(majorant)
+        self.last_seeds = None
+
+    def __call__(self, rays, seeds=None):
+        dev = current_device()
+        rt = rays._tensor if isinstance(rays, RDVObject) else wrap(rays)._tensor
+        assert rt.shape[-1] == 6, f"input's last dimension ({rt.shape[-1]}) must match the map's IN (6)"
+        lead = list(rt.shape[:-1])
+        r2 = rt.reshape(-1, 6)
+        if r2.device != dev or r2.dtype != torch.float32 or not r2.is_contiguous():
+            r2 = r2.to(device=dev, dtype=torch.float32).contiguous()
+        out = torch.empty(lead + [1], dtype=torch.float32, device=dev)
+        st = self._device_state(dev)
+        g = self.majorant.grid.data
+        if g.device != dev or g.dtype != torch.float32 or not g.is_contiguous():
+            g = g.to(device=dev, dtype=torch.float32).contiguous()
+        seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
+        assert len(seeds) == 4, "seeds must be 4 integers"
+        self.last_seeds = seeds
+        if st["ws"] is None:
+            st["ws"] = torch.empty(256, dtype=torch.uint8, device=dev)
+        n = len(st["layers"])
+        with _timed():
+            N.check(N.lib().rdvb_transmittance_rt(
+                r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.density_scale, g.data_ptr(),
+                N.int_array(list(g.shape[:3])), N.uint32_array(seeds), n, N.int_array(st["dims"]),
+                N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
+                N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
+                stream_handle()), "rdvb_transmittance_rt")
+        return RDVObject(out)
