@@ -401,6 +401,7 @@ def run_ours(args, spec, world, rank, local):
                 "transmittance": run_trm(args, 1, 0, local, summary=True),
                 "tensor_op_chain": chain_summary(),
                 "conv_family": conv_family_summary(),
+                "ratiotracking": ratiotracking_summary(),
             }
     print(json.dumps(line), flush=True)
 
@@ -862,6 +863,67 @@ def trm_cpu_baseline(layers, n=65536):
     el = time.perf_counter() - t0
     return {"value": evals / el, "unit": "evaluations/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{n} rays through the image middle ({evals} evaluations, {el:.1f} s, numpy/BLAS)"}
+
+
+def trm_majorant(layers, cells=16, sub=4, margin=1.3):
+    """Voxel majorant [cells^3, 1] of the extinction chain: the largest value
+    on a sub^3 lattice of every cell (faces included), times margin, + 0.05."""
+    from oracle import mlp as omlp
+
+    lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
+    k = cells * (sub - 1) + 1
+    ax = np.linspace(-1, 1, k, dtype=np.float32)
+    Z, Y, X = np.meshgrid(ax, ax, ax, indexing="ij")
+    v = omlp.mlp_forward_f64(np.stack([X, Y, Z], -1).reshape(-1, 3), lay_np)[:, 0].reshape(k, k, k)
+    g = np.zeros((cells, cells, cells), dtype=np.float32)
+    s = sub - 1
+    for a in range(cells):
+        for b in range(cells):
+            blk = v[a * s:a * s + sub, b * s:b * s + sub, :]
+            for c in range(cells):
+                g[a, b, c] = max(float(blk[:, :, c * s:c * s + sub].max()), 0.0) * margin + 0.05
+    return torch.from_numpy(g[..., None]), lay_np
+
+
+def ratiotracking_summary(steps=3):
+    """RatiotrackingTransmittance over the config-4 camera's rays (1920x1080,
+    orbit pose 0), extinction ReLU(MLP 3->64->64->1) LinearFast (the
+    transmittance workload's chain), a 16^3 voxel majorant of it, density
+    scale 1, fixed seeds; CUDA-core kernel, one thread per ray. The oracle
+    restatement on 65,536 middle rays is the CPU figure."""
+    import rdv_project_b200 as rdv
+    from oracle import raymarch as orm
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = trm_layers()
+    grid, lay_np = trm_majorant(layers)
+    ext = build_map(rdv, layers, dev)
+    node = rdv.RatiotrackingTransmittance(ext, grid.to(dev), density_scale=TRM["scale"])
+    rays = trm_rays().to(dev)
+    seeds = (1234567, 7654321, 1357911, 2468024)
+    for _ in range(2):
+        node(rays, seeds=seeds)
+    torch.cuda.synchronize()
+    t = time_steps(lambda: node(rays, seeds=seeds), steps) / steps
+    evals = node.last_evaluations()
+    flop = trm_flop() * evals
+    nominal = 148 * 128 * 2 * 1.965e9 / 1e12
+    n_cpu = 65536
+    mid = (TRM["height"] // 2) * TRM["width"]
+    sample = trm_rays()[mid:mid + n_cpu].numpy()
+    t0 = time.perf_counter()
+    _, ev_cpu = orm.ratiotracking_transmittance(sample[:, :3], sample[:, 3:], TRM["scale"],
+                                                orm.mlp_extinction(lay_np), grid.numpy(), seeds,
+                                                index=np.arange(mid, mid + n_cpu), return_evaluations=True)
+    el = time.perf_counter() - t0
+    return {"workload": "RatiotrackingTransmittance, 1920x1080 rays (config-4 camera), ReLU(MLP 3->64->64->1) "
+                        "LinearFast extinction, 16^3 voxel majorant",
+            "ms": t * 1e3, "rays_per_s": rays.shape[0] / t, "evaluations": evals, "evaluations_per_s": evals / t,
+            "roofline": {"bound": "fp32 CUDA-core FMA", "achieved": flop / t / 1e12, "unit": "TFLOP/s",
+                         "peak": nominal, "frac": flop / t / 1e12 / nominal,
+                         "peak_source": "nominal: 148 SMs x 128 lanes x 2 x 1.965 GHz"},
+            "cpu_baseline": {"value": ev_cpu / el, "unit": "evaluations/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": f"{n_cpu} middle rays ({ev_cpu} evaluations, {el:.1f} s)"}}
 
 
 def chain_summary(rows=1 << 20, steps=3):

@@ -1169,6 +1169,7 @@ int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transf
     p.mdim[0] = majorant_dims[2];  // x: W
     p.mdim[1] = majorant_dims[1];  // y: H
     p.mdim[2] = majorant_dims[0];  // z: D
+    for (int k = 0; k < 3; ++k) p.mvs[k] = 2.0f / static_cast<float>(p.mdim[k]);
     for (int k = 0; k < 4; ++k) p.seeds[k] = seeds[k];
     if (int rc = trm_object_space(transform, p)) return rc;
     return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev,

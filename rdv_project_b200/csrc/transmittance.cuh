@@ -67,6 +67,7 @@ struct Params {
     // ratiotracking_kernel only
     const float* maj;       // majorant voxels [D, H, W] (z, y, x)
     int mdim[3];            // W, H, D: cells along x, y, z
+    float mvs[3];           // voxel sizes 2 / mdim (fp32 division, as the reference's vec3(2.0) / dim)
     unsigned seeds[4];      // the dispatch's generator seeds
 };
 
@@ -322,7 +323,7 @@ __device__ __forceinline__ float voxel_majorant(const Params& p, const float (&x
         int c = static_cast<int>(__fmul_rn(__fadd_rn(__fmul_rn(x[k], 0.5f), 0.5f), f));  // toward zero
         c = min(max(c, 0), p.mdim[k] - 1);
         cell[k] = c;
-        const float vs = __fdiv_rn(2.0f, f);
+        const float vs = p.mvs[k];
         const float bmin = __fsub_rn(__fmul_rn(static_cast<float>(c), vs), 1.0f);
         const float bmax = __fadd_rn(bmin, vs);
         const float t0 = __fdiv_rn(__fsub_rn(bmin, x[k]), w[k]);
@@ -336,6 +337,13 @@ __device__ __forceinline__ float voxel_majorant(const Params& p, const float (&x
 
 constexpr int kRtSafety = 1024;  // ratiotracking_transmittance_trait.h's loop cap
 
+// Work is warp-coherent: each lane advances its own ray (free flights across
+// majorant cells, taking the next ray when one ends) until it reaches a
+// collision; then the whole warp evaluates the extinction MLP together, each
+// lane on its own collision point (lanes without rays left evaluate a dummy
+// point and discard it), and applies the collision. The MLP -- nearly all of
+// the arithmetic -- thus runs with the lanes converged instead of once per
+// colliding lane.
 __global__ void __launch_bounds__(kThreads) ratiotracking_kernel(const __grid_constant__ Params p) {
     extern __shared__ float sm[];
     float* wsm = sm;
@@ -344,38 +352,65 @@ __global__ void __launch_bounds__(kThreads) ratiotracking_kernel(const __grid_co
     stage_chain(p, wsm);
     const float* bsm = wsm;
     unsigned long long my_evals = 0;
+    long long ray = -1;  // -1: take the next ray; -2: none left
+    float x[3] = {0.0f, 0.0f, 0.0f}, w[3] = {0.0f, 0.0f, 0.0f}, d = 0.0f, T = 1.0f, maj = 1.0f;
+    int safety = 0;
+    Rng r = {0u, 0u, 0u, 0u};
     while (true) {
-        const long long ray = atomicAdd(p.counter, 1);
-        if (ray >= p.n_rays) break;
-        float x[3], w[3], d = 0.0f;
-        float T = 1.0f;  // a ray that misses the volume is fully transparent
-        if (march_entry(p.rays + ray * 6, p.L, p.O, x, w, d)) {
-            Rng r = rng_spawn(p.seeds, static_cast<unsigned>(ray));
-            for (int safety = 0; d > 0.0f && safety < kRtSafety; ++safety) {
-                float dist;
-                float maj = voxel_majorant(p, x, w, dist);
-                maj = maj < 1e-12f ? 1e-12f : maj;
-                dist = dist < 1e-6f ? 1e-6f : dist;
-                const float q = __fdiv_rn(-logf(__fsub_rn(1.0f, rng_uniform(r))), __fmul_rn(maj, p.scale));
-                const float dt = q < dist ? q : dist;  // free-flight distance
-                d = __fsub_rn(d, dt);
+        bool pending = false;  // a collision at x waits for its extinction
+        while (ray != -2 && !pending) {
+            if (ray < 0) {
+                ray = atomicAdd(p.counter, 1);
+                if (ray >= p.n_rays) {
+                    ray = -2;
+                    break;
+                }
+                if (!march_entry(p.rays + ray * 6, p.L, p.O, x, w, d)) {
+                    p.out[ray] = 1.0f;  // the ray misses the volume: fully transparent
+                    ray = -1;
+                    continue;
+                }
+                T = 1.0f;
+                safety = 0;
+                r = rng_spawn(p.seeds, static_cast<unsigned>(ray));
+            }
+            if (!(d > 0.0f) || safety >= kRtSafety) {  // the loop condition
+                p.out[ray] = T;
+                ray = -1;
+                continue;
+            }
+            ++safety;
+            float dist;
+            maj = voxel_majorant(p, x, w, dist);
+            maj = maj < 1e-12f ? 1e-12f : maj;
+            dist = dist < 1e-6f ? 1e-6f : dist;
+            const float q = __fdiv_rn(-logf(__fsub_rn(1.0f, rng_uniform(r))), __fmul_rn(maj, p.scale));
+            const float dt = q < dist ? q : dist;  // free-flight distance
+            d = __fsub_rn(d, dt);
 #pragma unroll
-                for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(dt, w[k]));
-                if (dt >= dist) continue;  // left the majorant's cell
-                if (d <= 0.0f) break;      // reached the end without a collision
-                const float sigma = extinction(p, wsm, bsm, act0, act1, x);
-                ++my_evals;
-                T = __fmul_rn(T, __fsub_rn(1.0f, __fdiv_rn(sigma, maj)));
-                if (T < 0.05f) {
-                    if (rng_uniform(r) >= T) {
-                        T = 0.0f;
-                        break;
-                    }
+            for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(dt, w[k]));
+            if (dt >= dist) continue;  // left the majorant's cell
+            if (d <= 0.0f) {           // reached the end without a collision
+                p.out[ray] = T;
+                ray = -1;
+                continue;
+            }
+            pending = true;
+        }
+        if (!__any_sync(0xffffffffu, pending)) break;  // no lane has rays left
+        const float sigma = extinction(p, wsm, bsm, act0, act1, x);
+        if (pending) {
+            ++my_evals;
+            T = __fmul_rn(T, __fsub_rn(1.0f, __fdiv_rn(sigma, maj)));
+            if (T < 0.05f) {
+                if (rng_uniform(r) >= T) {
+                    p.out[ray] = 0.0f;
+                    ray = -1;
+                } else {
                     T = 1.0f;  // Russian roulette survivor
                 }
             }
         }
-        p.out[ray] = T;
     }
     if (my_evals) atomicAdd(p.evaluations, my_evals);
 }
