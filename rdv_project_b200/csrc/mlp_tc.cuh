@@ -26,8 +26,9 @@
 //   warp 16    producer: 1-D bulk (TMA) copies of input tiles and of the
 //              pre-swizzled weight blocks (resident, or streamed per layer
 //              through a ring), issued from one event loop.
-//   warps 17, 19  MMA issuers (even / odd slots; warp 17 allocates TMEM):
-//              one thread each issues tcgen05.mma
+//   warps 17, 19 (+ 20, 21)  MMA issuers (with 4 slots and resident
+//              weights one per slot, else even / odd slots; warp 17
+//              allocates TMEM): one thread each issues tcgen05.mma
 //              (M=128, N=layer width, K=16 steps) per layer -- A from shared
 //              memory for the first layer, from TMEM after -- and commits
 //              completion to mbarriers.
@@ -51,9 +52,13 @@ constexpr int kEpiWarps = 16;
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;        // issues the MMAs of the even slots; allocates TMEM
 constexpr int kMmaWarp2 = 19;       // issues the MMAs of the odd slots
-constexpr int kMaxIssuers = 2;
+constexpr int kMaxIssuers = 4;      // with 4: warps 17, 19, 20, 21, one slot each
+// Issuer number of an MMA-issuing warp (-1 for other warps).
+__host__ __device__ constexpr int issuer_index(int warp) {
+    return warp == kMmaWarp ? 0 : (warp == kMmaWarp2 ? 1 : (warp >= 20 ? warp - 18 : -1));
+}
 // CTA size for ISSUERS MMA-issuing warps: 16 epilogue + producer + MMA +
-// staging (+ the second issuer). Streamed-weight chains run 19 warps, which
+// staging (+ the other issuers). Streamed-weight chains run 19 warps, which
 // leaves their register-heavy epilogue the larger budget.
 __host__ __device__ constexpr int cta_threads(int issuers) { return (18 + issuers) * 32; }
 constexpr int kStageWarp = 18;
@@ -531,14 +536,17 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                 }
             }
         }
-    } else if (warp == kMmaWarp || (ISSUERS > 1 && warp == kMmaWarp2)) {
-        // With resident weights the slots are independent and two issuing
-        // threads split them by parity (a slot-layer's wait, K-step MMAs and
-        // commits are a few hundred cycles of one thread's time, so this
-        // halves the serial issue path). Streamed weights keep one issuer,
-        // whose in-order walk over the slots releases each ring block.
-        const int mi = warp == kMmaWarp ? 0 : 1;
-        constexpr int n_iss = ISSUERS;  // the host launches 2 only with resident weights
+    } else if (warp == kMmaWarp || (ISSUERS > 1 && warp == kMmaWarp2) || (ISSUERS > 2 && warp >= 20)) {
+        // With resident weights the slots are independent and the issuing
+        // threads split them (slot s goes to issuer s % ISSUERS): a
+        // slot-layer's wait, K-step MMAs and commit are a few hundred cycles
+        // of one thread's time, and an issuer walking its slots in order
+        // waits on a slot that is behind while another is ready. Measured on
+        // width-64 chains: 2 issuers -> 4 (one per slot) takes config 5 from
+        // 6.3 to 5.5 ms. Streamed weights keep one issuer, whose in-order
+        // walk over the slots releases each ring block.
+        const int mi = issuer_index(warp);
+        constexpr int n_iss = ISSUERS;  // the host launches 2 or 4 only with resident weights
         if (lane == 0) {
             uint32_t aph = 0u, a0ph = 0u;  // per-slot parities of the next a_full / a0_full phase
             uint32_t q = 0, wph = 0;       // weight ring slot and its phase
@@ -604,7 +612,7 @@ __global__ void __launch_bounds__(cta_threads(ISSUERS), 1) mlp_tc_kernel(const _
                         // layers) issue exactly ksteps MMAs; the streamed-weight
                         // kernel keeps the fixed 8-step loop, which measured
                         // faster for its 8-step layers.
-                        if constexpr (ISSUERS == 2) {
+                        if constexpr (ISSUERS >= 2) {
                             issue_layer(ksteps, l > 0, d_tm[s], a0_desc[s], a_tm[s], b_desc, idesc);
                         } else if (l == 0) {
 #pragma unroll

@@ -50,7 +50,7 @@ struct DeviceInfo {
     bool init = false;
     int sm_count = 0;
     int max_smem_optin = 0;
-    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2][3][3] = {};  // [slots][bf16][mode][issuers]
+    size_t tc_smem_set[rdvb::mlp_tc::kMaxSlots + 1][2][3][rdvb::mlp_tc::kMaxIssuers + 1] = {};  // [slots][bf16][mode][issuers]
     size_t simt_smem_set = 0;
     size_t wino_smem_set[2] = {};
     size_t trm_smem_set = 0;
@@ -256,7 +256,13 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     const int ri = ray ? (ray->march ? kModeMarch : kModeRender) : kModeRows;
     // two MMA-issuing warps when the weights are resident (the slots are then
     // independent); one in-order issuer for streamed weights
-    const int iss = p.resident ? 2 : 1;
+    // MMA-issuing warps: with resident weights the slots are independent --
+    // one issuer per slot for 4 slots (an issuer never waits on a slot that
+    // is behind while another is ready), two for 2 slots; one in-order issuer
+    // for streamed weights. RDVB_MLP_ISSUERS=2 keeps two issuers for 4 slots.
+    int iss = p.resident ? (slots == 4 ? 4 : 2) : 1;
+    if (const char* env = getenv("RDVB_MLP_ISSUERS"))
+        if (atoi(env) == 2 && iss == 4) iss = 2;
     auto go = [&](auto kernel, int sl) {
         if (dev->tc_smem_set[sl][bf16][ri][iss] < smem) {
             cudaError_t e =
@@ -275,18 +281,20 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     };
 #define RDVB_GO(S, B, R)                                                         \
     (iss == 2 ? go(mlp_tc_kernel<S, B, R, 2>, S) : go(mlp_tc_kernel<S, B, R, 1>, S))
+#define RDVB_GO4(B, R) (iss == 4 ? go(mlp_tc_kernel<4, B, R, 4>, 4) : RDVB_GO(4, B, R))
     if (ray) {
         if (ri == kModeMarch) {
-            if (slots == 4) bf16 ? RDVB_GO(4, 1, kModeMarch) : RDVB_GO(4, 0, kModeMarch);
+            if (slots == 4) bf16 ? RDVB_GO4(1, kModeMarch) : RDVB_GO4(0, kModeMarch);
             else bf16 ? RDVB_GO(2, 1, kModeMarch) : RDVB_GO(2, 0, kModeMarch);
         } else {
-            if (slots == 4) bf16 ? RDVB_GO(4, 1, kModeRender) : RDVB_GO(4, 0, kModeRender);
+            if (slots == 4) bf16 ? RDVB_GO4(1, kModeRender) : RDVB_GO4(0, kModeRender);
             else bf16 ? RDVB_GO(2, 1, kModeRender) : RDVB_GO(2, 0, kModeRender);
         }
     } else {
-        if (slots == 4) bf16 ? RDVB_GO(4, 1, kModeRows) : RDVB_GO(4, 0, kModeRows);
+        if (slots == 4) bf16 ? RDVB_GO4(1, kModeRows) : RDVB_GO4(0, kModeRows);
         else bf16 ? RDVB_GO(2, 1, kModeRows) : RDVB_GO(2, 0, kModeRows);
     }
+#undef RDVB_GO4
 #undef RDVB_GO
     if (rc) return rc;
     *taken = true;
