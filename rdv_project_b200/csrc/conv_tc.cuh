@@ -24,6 +24,7 @@
 //     while the next block's GEMMs run, then free the half for block b + 2.
 // Every wait is bounded (ptx.cuh) and reports through the status word.
 #pragma once
+#include <cuda.h>  // CUtensorMap (the type only; the map is encoded on the host)
 #include "ptx.cuh"
 
 namespace rdvb {
@@ -308,6 +309,212 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// TMA-fed variant for float16 input with 64 channels and float16 operands
+// (the input needs no conversion, so the copy engine stages it directly):
+// a block is an 8-row x 16-column rectangle of output pixels of one image,
+// and tap (dh, dw)'s A tile is the input box {64 channels, 16 columns, 8
+// rows, 1 image} at (0, w0 + dw, h0 + dh, n), loaded by one thread with the
+// 128-byte swizzle the MMA reads; the copy zero-fills the box where it
+// leaves the image, which is the convolution's 'same' padding.
+//   warp 0: producer (weights once, then one box per (block, tap) into a
+//           ring of up to 6 tiles)
+//   warp 1: MMA issuer (allocates TMEM)
+//   warps 2-5: epilogue, one per TMEM lane quadrant: + bias, store the
+//           block's in-image pixels; then frees the accumulator half.
+constexpr int kTmaThreads = 6 * 32;
+constexpr int kTmaMaxRing = 6;
+constexpr int kBoxW = 16, kBoxH = 8;
+
+struct TmaParams {
+    CUtensorMap tmap;         // x [N, H, W, 64] float16: dims {64, W, H, N}, box {64, 16, 8, 1}, SWIZZLE_128B
+    float* y;                 // [N*H*W, COUT] float32
+    const uint8_t* wpack;     // per tap: COUT rows x 128 bytes, K-major SW128
+    const float* bias;        // [COUT] or null
+    int n, h, w, cout, kh, kw, taps;
+    int blocks_w, blocks_h, n_blocks;
+    int ring;                 // A tiles in flight (2..6)
+    uint32_t w_bytes, off_a, off_bar, idesc;
+};
+
+enum : int {
+    kTBarWFull = 0,
+    kTBarFull = 1,                            // + ring slot: the box landed (TMA tx)
+    kTBarEmpty = 1 + kTmaMaxRing,             // + ring slot: the GEMMs reading it are done (commit)
+    kTBarDFull = 1 + 2 * kTmaMaxRing,         // + half
+    kTBarDEmpty = 3 + 2 * kTmaMaxRing,        // + half (one arrival per epilogue warp)
+    kTBarDrain = 5 + 2 * kTmaMaxRing,
+    kTNumBars = 6 + 2 * kTmaMaxRing,
+};
+constexpr uint32_t kTBarBlockBytes = kTNumBars * 8 + 16;
+
+__device__ __forceinline__ void tma_block_origin(const TmaParams& p, int blk, int& img, int& h0, int& w0) {
+    const int per_img = p.blocks_w * p.blocks_h;
+    img = blk / per_img;
+    const int rem = blk - img * per_img;
+    const int hb = rem / p.blocks_w;
+    h0 = hb * kBoxH;
+    w0 = (rem - hb * p.blocks_w) * kBoxW;
+}
+
+__global__ void __launch_bounds__(kTmaThreads, 1) conv_tc_tma_kernel(const __grid_constant__ TmaParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_addr(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t* const base_ptr = smem_raw + (base - raw_addr);
+    const uint32_t w_base = base;
+    const uint32_t a_base = base + p.off_a;
+    const uint32_t bar_base = base + p.off_bar;
+    auto bar = [&](int i) -> uint32_t { return bar_base + 8u * static_cast<uint32_t>(i); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + p.off_bar + kTNumBars * 8);
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(base_ptr + p.off_bar + kTNumBars * 8 + 4);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int R = p.ring;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar(kTBarWFull), 1);
+        for (int s = 0; s < kTmaMaxRing; ++s) {
+            mbar_init(bar(kTBarFull + s), 1);
+            mbar_init(bar(kTBarEmpty + s), 1);
+        }
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(bar(kTBarDFull + h), 1);
+            mbar_init(bar(kTBarDEmpty + h), 4);
+        }
+        mbar_init(bar(kTBarDrain), 1);
+        *abort = 0u;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int n_mine = blockIdx.x < p.n_blocks ? (p.n_blocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int taps = p.taps;
+    const uint32_t d_cols = static_cast<uint32_t>(p.cout);
+    bool ok = true;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        if (lane == 0) {
+            mbar_arrive_expect_tx(bar(kTBarWFull), p.w_bytes);
+            bulk_g2s(w_base, p.wpack, p.w_bytes, bar(kTBarWFull));
+            int g = 0;
+            for (int bl = 0; ok && bl < n_mine; ++bl) {
+                int img, h0, w0;
+                tma_block_origin(p, static_cast<int>(blockIdx.x) + bl * static_cast<int>(gridDim.x), img, h0, w0);
+                int dh = -(p.kh / 2), dw = -(p.kw / 2);
+                for (int t = 0; t < taps; ++t, ++g) {
+                    const int s = g % R;
+                    if (!mbar_wait(bar(kTBarEmpty + s), ((g / R) & 1) ^ 1, abort, &g_status, kStatusTimeoutXEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(bar(kTBarFull + s), kATileBytes);
+                    tma_load_4d(a_base + static_cast<uint32_t>(s) * kATileBytes, &p.tmap, 0, w0 + dw, h0 + dh, img,
+                                bar(kTBarFull + s));
+                    if (++dw > p.kw - 1 - p.kw / 2) {
+                        dw = -(p.kw / 2);
+                        ++dh;
+                    }
+                }
+            }
+            if (!ok) *abort = 1u;
+            // every copy this thread started lands before the CTA exits
+            for (int k = (g > R ? g - R : 0); k < g; ++k) drain_wait(bar(kTBarFull + k % R), (k / R) & 1);
+            drain_wait(bar(kTBarWFull), 0u);
+        }
+    } else if (warp == 1) {
+        // --------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            ok = mbar_wait(bar(kTBarWFull), 0u, abort, &g_status, kStatusTimeoutWFull);
+            const uint64_t w_desc0 = umma_desc_sw128(w_base);
+            const uint64_t a_desc0 = umma_desc_sw128(a_base);
+            const uint64_t tap_step = static_cast<uint64_t>(p.cout) * 8u;  // one tap block, 16-byte units
+            bool issued = false;
+            int g = 0;
+            for (int bl = 0; ok && bl < n_mine; ++bl) {
+                const uint32_t d = tmem_base + (bl & 1) * d_cols;
+                if (bl >= 2 && !mbar_wait(bar(kTBarDEmpty + (bl & 1)), ((bl >> 1) - 1) & 1, abort, &g_status,
+                                          kStatusTimeoutOther)) {
+                    ok = false;
+                    break;
+                }
+                for (int t = 0; t < taps; ++t, ++g) {
+                    const int s = g % R;
+                    if (!mbar_wait(bar(kTBarFull + s), (g / R) & 1, abort, &g_status, kStatusTimeoutAFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(s) * (kATileBytes >> 4);
+                    const uint64_t b_desc = w_desc0 + static_cast<uint64_t>(t) * tap_step;
+                    if (t == 0) issue_tap_ks<4, true>(d, a_desc, b_desc, p.idesc);
+                    else issue_tap_ks<4, false>(d, a_desc, b_desc, p.idesc);
+                    issued = true;
+                    umma_commit(bar(kTBarEmpty + s));  // the tile may be reloaded
+                    if (t == taps - 1) umma_commit(bar(kTBarDFull + (bl & 1)));
+                }
+            }
+            if (!ok) *abort = 1u;
+            if (issued) {
+                umma_commit(bar(kTBarDrain));
+                drain_wait(bar(kTBarDrain), 0u);
+            }
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;  // TMEM lane = pixel (r / 16, r % 16) of the block
+        const int n_chunks = p.cout >> 4;
+        for (int bl = 0; ok && bl < n_mine; ++bl) {
+            const uint32_t half = bl & 1;
+            if (!mbar_wait_warp(bar(kTBarDFull + half), (bl >> 1) & 1, abort, &g_status, kStatusTimeoutAccFull)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            int img, h0, w0;
+            tma_block_origin(p, static_cast<int>(blockIdx.x) + bl * static_cast<int>(gridDim.x), img, h0, w0);
+            const int oh = h0 + r / kBoxW, ow = w0 + r % kBoxW;
+            const bool valid = oh < p.h && ow < p.w;
+            const long long pix = (static_cast<long long>(img) * p.h + oh) * p.w + ow;
+            for (int c = 0; c < n_chunks; ++c) {
+                uint32_t v[16];
+                tmem_ld16(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + half * d_cols + 16u * c, v);
+                tmem_wait_ld(v);
+                if (valid) {
+                    float o[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        o[i] = __uint_as_float(v[i]) + (p.bias ? __ldg(p.bias + 16 * c + i) : 0.0f);
+                    float4* dst = reinterpret_cast<float4*>(p.y + pix * p.cout + 16 * c);
+                    dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+                    dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+                    dst[2] = make_float4(o[8], o[9], o[10], o[11]);
+                    dst[3] = make_float4(o[12], o[13], o[14], o[15]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kTBarDEmpty + half));
+        }
+        if (!ok) *abort = 1u;
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
     }

@@ -175,18 +175,6 @@ __device__ __forceinline__ uint32_t pack2_rt(float a, float b, int relu) {
     return relu ? pack2<BF16, true>(a, b) : pack2<BF16, false>(a, b);
 }
 
-// Drain wait used on the abort path: ignores the abort flag, keeps its own
-// time limit.
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
-    const uint64_t t0 = global_timer_ns();
-    while (!mbar_try_wait_sleep(bar, parity, 500000u)) {
-        if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
-            atomicOr(&g_status, kStatusTimeoutDrain);
-            return;
-        }
-    }
-}
-
 // Tile index of (round r, slot s) for this CTA, or -1 past the end.
 template <int SLOTS>
 __device__ __forceinline__ int tile_of(int r, int s, int n_tiles) {

@@ -145,6 +145,18 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
     return ok;
 }
 
+// Drain wait used on the abort path: ignores the abort flag, keeps its own
+// time limit.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait_sleep(bar, parity, 500000u)) {
+        if (global_timer_ns() - t0 > RDVB_WAIT_LIMIT_NS) {
+            atomicOr(&g_status, kStatusTimeoutDrain);
+            return;
+        }
+    }
+}
+
 // ------------------------------------------------------- bulk async copies
 // Global -> shared 1-D bulk copy (TMA engine), completion counted on `bar`
 // in bytes. dst/src 16-byte aligned, bytes a multiple of 16. No multicast.
@@ -152,6 +164,20 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+// Global -> shared tiled 4-D tensor copy (TMA) of the box at coordinates
+// (c0 innermost .. c3) of `tmap` (a kernel-parameter tensor map), completion
+// counted on `bar` in bytes (the whole box; out-of-range elements are
+// zero-filled). c0 * element size must be a multiple of 16 bytes; the other
+// coordinates may be negative or past the end. No multicast.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
 }
 

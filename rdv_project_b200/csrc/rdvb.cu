@@ -2,6 +2,7 @@
 // translation unit: the kernels are included below so that the device status
 // word and the kernels share a module.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -56,6 +57,7 @@ struct DeviceInfo {
     size_t trm_smem_set = 0;
     size_t rt_smem_set = 0;
     size_t conv_tc_smem_set = 0;
+    size_t conv_tma_smem_set = 0;
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
@@ -657,6 +659,85 @@ int rdvb_conv_tc_pack(const float* weight, int kh, int kw, int cin, int cout, in
     return check_launch("conv_tc_pack_kernel");
 }
 
+namespace {
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library); null when the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// The TMA-fed kernel for float16 input with 64 channels and float16
+// operands. Returns RDVB_OK with *taken = false when the shapes or the
+// driver do not allow it (the caller then stages on the CUDA cores).
+int launch_conv_tc_tma(const void* x, int n, int h, int w, int cout, int kh, int kw, const void* wpack,
+                       const float* bias, float* y, cudaStream_t stream, DeviceInfo* dev, bool* taken) {
+    using namespace rdvb::convtc;
+    *taken = false;
+    if (const char* env = getenv("RDVB_CONV_TMA"))
+        if (atoi(env) == 0) return RDVB_OK;
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return RDVB_OK;
+    const long long blocks_w = (w + kBoxW - 1) / kBoxW, blocks_h = (h + kBoxH - 1) / kBoxH;
+    const long long n_blocks = static_cast<long long>(n) * blocks_w * blocks_h;
+    if (n_blocks > 0x7fffffffLL) return RDVB_OK;
+    const uint32_t w_bytes = static_cast<uint32_t>(kh * kw) * cout * 128u;
+    const uint32_t off_a = (w_bytes + 1023u) & ~1023u;
+    const long long room = static_cast<long long>(dev->max_smem_optin) - off_a - kTBarBlockBytes - 1024;
+    const int ring = static_cast<int>(std::min<long long>(kTmaMaxRing, room > 0 ? room / kATileBytes : 0));
+    if (ring < 2) return RDVB_OK;
+    TmaParams p;
+    memset(&p, 0, sizeof(p));
+    const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
+                                static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[3] = {64 * 2, static_cast<cuuint64_t>(w) * 128, static_cast<cuuint64_t>(h) * w * 128};
+    const cuuint32_t box[4] = {64, kBoxW, kBoxH, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (enc(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return RDVB_OK;
+    p.y = y;
+    p.wpack = static_cast<const uint8_t*>(wpack);
+    p.bias = bias;
+    p.n = n;
+    p.h = h;
+    p.w = w;
+    p.cout = cout;
+    p.kh = kh;
+    p.kw = kw;
+    p.taps = kh * kw;
+    p.blocks_w = static_cast<int>(blocks_w);
+    p.blocks_h = static_cast<int>(blocks_h);
+    p.n_blocks = static_cast<int>(n_blocks);
+    p.ring = ring;
+    p.w_bytes = w_bytes;
+    p.off_a = off_a;
+    p.off_bar = off_a + static_cast<uint32_t>(ring) * kATileBytes;
+    p.idesc = rdvb::umma_idesc_f16(static_cast<uint32_t>(cout), 0);
+    const size_t smem = p.off_bar + kTBarBlockBytes + 1024;
+    if (dev->conv_tma_smem_set < smem) {
+        cudaError_t e = cudaFuncSetAttribute(conv_tc_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(conv_tc_tma): %s", cudaGetErrorString(e));
+        dev->conv_tma_smem_set = smem;
+    }
+    const int grid = static_cast<int>(std::min<long long>(dev->sm_count, n_blocks));
+    conv_tc_tma_kernel<<<grid, kTmaThreads, smem, stream>>>(p);
+    *taken = true;
+    return check_launch("conv_tc_tma_kernel");
+}
+}  // namespace
+
 int rdvb_conv2d_tc(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
                    const void* wpack, int operand, const float* bias, float* y, void* stream) {
     using namespace rdvb::convtc;
@@ -678,6 +759,13 @@ int rdvb_conv2d_tc(const void* x, int x_dtype, int n, int h, int w, int cin, int
     if (!aligned(x, 16) || !aligned(y, 16) || !aligned(wpack, 256))
         return fail(RDVB_ERR_INVALID_ARG, "x and y must be 16-byte and wpack 256-byte aligned");
     if (bias && !aligned(bias, 4)) return fail(RDVB_ERR_INVALID_ARG, "bias must be 4-byte aligned");
+    if (x_dtype == RDVB_F16 && operand == RDVB_F16 && cin == 64) {
+        bool taken = false;
+        if (int rc = launch_conv_tc_tma(x, n, h, w, cout, kh, kw, wpack, bias, y, static_cast<cudaStream_t>(stream),
+                                        dev, &taken))
+            return rc;
+        if (taken) return RDVB_OK;
+    }
     Params p;
     memset(&p, 0, sizeof(p));
     p.x = x;

@@ -180,3 +180,40 @@ def test_shapes_outside_tensor_core_limits_take_cuda_cores(rdv, cuda_device):
     ref = oten.conv2d_staged(x.numpy(), wt.numpy(), b.numpy(), 16, 16, "f16")
     nw, el = omlp.rel_errors(op.as_type("torch").cpu().numpy(), ref)
     assert nw <= 1e-4 and el <= 1e-4
+
+
+@pytest.mark.parametrize("n,h,w,cout,kh,kw", [
+    (1, 40, 48, 64, 3, 3),      # whole 8x16 blocks
+    (2, 37, 53, 128, 3, 3),     # ragged blocks at the bottom and right edges, two images
+    (1, 24, 32, 32, 5, 5),      # 25 taps, halo of 2
+    (3, 9, 17, 256, 1, 1),      # 1x1, widest output, one-row-deep blocks
+])
+def test_tma_fed_conv_matches_oracle_and_staging_kernel(rdv, cuda_device, monkeypatch, n, h, w, cout, kh, kw):
+    """float16 input with 64 channels and float16 operands runs the TMA-fed
+    kernel (input boxes loaded by the copy engine, border zero-filled); it
+    must agree with the oracle and with the staging kernel on the same data."""
+    import rdv_project_b200._native as N
+    from oracle import winograd as owg
+    from oracle.mlp import stage
+
+    cin = 64
+    g = torch.Generator().manual_seed(h * 1000 + w)
+    x = torch.randn(n * h * w, cin, generator=g).half()
+    wt = torch.randn(kh, kw, cin, cout, generator=g) * (2.0 / (kh * kw * cin)) ** 0.5
+    b = torch.randn(cout, generator=g) * 0.1
+    xd, wd, bd = x.to(cuda_device), wt.to(cuda_device), b.to(cuda_device)
+    launches = N.launch_count()
+    y = _tc_conv(N, xd, wd, bd, n, h, w, N.RDVB_F16)
+    torch.cuda.synchronize()
+    ref = owg.conv2d_direct(x.float().numpy().reshape(n, h, w, cin), stage(wt.numpy(), "f16"),
+                            b.numpy()).reshape(n * h * w, cout)
+    got = y.cpu().numpy()
+    assert not np.isnan(got).any()
+    nw, el = omlp.rel_errors(got, ref)
+    assert nw <= 1e-4 and el <= 1e-4, (nw, el)
+    monkeypatch.setenv("RDVB_CONV_TMA", "0")
+    y2 = _tc_conv(N, xd, wd, bd, n, h, w, N.RDVB_F16)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y, y2, rtol=2e-5, atol=2e-5)
+    assert N.launch_count() > launches
+    assert rdv.device_status() == 0
