@@ -322,13 +322,17 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
 // rows, 1 image} at (0, w0 + dw, h0 + dh, n), loaded by one thread with the
 // 128-byte swizzle the MMA reads; the copy zero-fills the box where it
 // leaves the image, which is the convolution's 'same' padding.
-//   warp 0: producer (weights once, then one box per (block, tap) into a
-//           ring of up to 6 tiles)
-//   warp 1: MMA issuer (allocates TMEM)
-//   warps 2-5: epilogue, one per TMEM lane quadrant: + bias, store the
-//           block's in-image pixels; then frees the accumulator half.
-constexpr int kTmaThreads = 6 * 32;
-constexpr int kTmaMaxRing = 6;
+// Two independent streams, even and odd blocks, each with its producer, its
+// half of the tile ring and its MMA issuer (one thread's waits, issues and
+// commits per tap bound a single stream), sharing the weights and the
+// epilogue; stream i accumulates into TMEM half i. Every ring barrier has
+// one producer and one consumer, so parity waits stay within one phase.
+//   warps 0, 7: producers of streams 0 and 1 (warp 0 also loads the weights)
+//   warps 1, 6: MMA issuers of streams 0 and 1 (warp 1 allocates TMEM)
+//   warps 2-5: epilogue, one per TMEM lane quadrant, blocks in order: + bias,
+//           store the block's in-image pixels; then frees the accumulator half.
+constexpr int kTmaThreads = 8 * 32;
+constexpr int kTmaMaxRing = 10;           // both streams' tiles
 constexpr int kBoxW = 16, kBoxH = 8;
 
 struct TmaParams {
@@ -338,7 +342,7 @@ struct TmaParams {
     const float* bias;        // [COUT] or null
     int n, h, w, cout, kh, kw, taps;
     int blocks_w, blocks_h, n_blocks;
-    int ring;                 // A tiles in flight (2..6)
+    int ring;                 // A tiles per stream (1..5); stream i uses slots [i * ring, (i + 1) * ring)
     uint32_t w_bytes, off_a, off_bar, idesc;
 };
 
@@ -348,8 +352,8 @@ enum : int {
     kTBarEmpty = 1 + kTmaMaxRing,             // + ring slot: the GEMMs reading it are done (commit)
     kTBarDFull = 1 + 2 * kTmaMaxRing,         // + half
     kTBarDEmpty = 3 + 2 * kTmaMaxRing,        // + half (one arrival per epilogue warp)
-    kTBarDrain = 5 + 2 * kTmaMaxRing,
-    kTNumBars = 6 + 2 * kTmaMaxRing,
+    kTBarDrain = 5 + 2 * kTmaMaxRing,         // + issuer
+    kTNumBars = 7 + 2 * kTmaMaxRing,
 };
 constexpr uint32_t kTBarBlockBytes = kTNumBars * 8 + 16;
 
@@ -388,6 +392,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) conv_tc_tma_kernel(const __gri
             mbar_init(bar(kTBarDEmpty + h), 4);
         }
         mbar_init(bar(kTBarDrain), 1);
+        mbar_init(bar(kTBarDrain + 1), 1);
         *abort = 0u;
         fence_mbarrier_init();
     }
@@ -404,18 +409,21 @@ __global__ void __launch_bounds__(kTmaThreads, 1) conv_tc_tma_kernel(const __gri
     const uint32_t d_cols = static_cast<uint32_t>(p.cout);
     bool ok = true;
 
-    if (warp == 0) {
-        // ------------------------------------------------------ producer
+    if (warp == 0 || warp == 7) {
+        // ----------------------------------------------------- producers
+        const int mi = warp == 0 ? 0 : 1;  // blocks mi, mi + 2, ...
         if (lane == 0) {
-            mbar_arrive_expect_tx(bar(kTBarWFull), p.w_bytes);
-            bulk_g2s(w_base, p.wpack, p.w_bytes, bar(kTBarWFull));
-            int g = 0;
-            for (int bl = 0; ok && bl < n_mine; ++bl) {
+            if (mi == 0) {
+                mbar_arrive_expect_tx(bar(kTBarWFull), p.w_bytes);
+                bulk_g2s(w_base, p.wpack, p.w_bytes, bar(kTBarWFull));
+            }
+            int g = 0;  // this stream's load count
+            for (int bl = mi; ok && bl < n_mine; bl += 2) {
                 int img, h0, w0;
                 tma_block_origin(p, static_cast<int>(blockIdx.x) + bl * static_cast<int>(gridDim.x), img, h0, w0);
                 int dh = -(p.kh / 2), dw = -(p.kw / 2);
                 for (int t = 0; t < taps; ++t, ++g) {
-                    const int s = g % R;
+                    const int s = mi * R + g % R;
                     if (!mbar_wait(bar(kTBarEmpty + s), ((g / R) & 1) ^ 1, abort, &g_status, kStatusTimeoutXEmpty)) {
                         ok = false;
                         break;
@@ -431,27 +439,28 @@ __global__ void __launch_bounds__(kTmaThreads, 1) conv_tc_tma_kernel(const __gri
             }
             if (!ok) *abort = 1u;
             // every copy this thread started lands before the CTA exits
-            for (int k = (g > R ? g - R : 0); k < g; ++k) drain_wait(bar(kTBarFull + k % R), (k / R) & 1);
-            drain_wait(bar(kTBarWFull), 0u);
+            for (int k = (g > R ? g - R : 0); k < g; ++k) drain_wait(bar(kTBarFull + mi * R + k % R), (k / R) & 1);
+            if (mi == 0) drain_wait(bar(kTBarWFull), 0u);
         }
-    } else if (warp == 1) {
-        // --------------------------------------------------- MMA issuer
+    } else if (warp == 1 || warp == 6) {
+        // -------------------------------------------------- MMA issuers
+        const int mi = warp == 1 ? 0 : 1;  // blocks mi, mi + 2, ... into accumulator half mi
         if (lane == 0) {
             ok = mbar_wait(bar(kTBarWFull), 0u, abort, &g_status, kStatusTimeoutWFull);
             const uint64_t w_desc0 = umma_desc_sw128(w_base);
             const uint64_t a_desc0 = umma_desc_sw128(a_base);
             const uint64_t tap_step = static_cast<uint64_t>(p.cout) * 8u;  // one tap block, 16-byte units
             bool issued = false;
-            int g = 0;
-            for (int bl = 0; ok && bl < n_mine; ++bl) {
+            for (int bl = mi; ok && bl < n_mine; bl += 2) {
                 const uint32_t d = tmem_base + (bl & 1) * d_cols;
                 if (bl >= 2 && !mbar_wait(bar(kTBarDEmpty + (bl & 1)), ((bl >> 1) - 1) & 1, abort, &g_status,
                                           kStatusTimeoutOther)) {
                     ok = false;
                     break;
                 }
+                int g = (bl >> 1) * taps;  // the stream's load index of this block's first tap
                 for (int t = 0; t < taps; ++t, ++g) {
-                    const int s = g % R;
+                    const int s = mi * R + g % R;
                     if (!mbar_wait(bar(kTBarFull + s), (g / R) & 1, abort, &g_status, kStatusTimeoutAFull)) {
                         ok = false;
                         break;
@@ -468,8 +477,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) conv_tc_tma_kernel(const __gri
             }
             if (!ok) *abort = 1u;
             if (issued) {
-                umma_commit(bar(kTBarDrain));
-                drain_wait(bar(kTBarDrain), 0u);
+                umma_commit(bar(kTBarDrain + mi));
+                drain_wait(bar(kTBarDrain + mi), 0u);
             }
         }
     } else {
