@@ -343,7 +343,7 @@ struct TmaParams {
     int n, h, w, cout, kh, kw, taps;
     int blocks_w, blocks_h, n_blocks;
     int ring;                 // A tiles per stream (1..5); stream i uses slots [i * ring, (i + 1) * ring)
-    uint32_t w_bytes, off_a, off_bar, idesc;
+    uint32_t w_bytes, off_a, off_bar, off_bias, idesc;
 };
 
 enum : int {
@@ -486,6 +486,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1) conv_tc_tma_kernel(const __gri
         const int quad = warp & 3;
         const int r = quad * 32 + lane;  // TMEM lane = pixel (r / 16, r % 16) of the block
         const int n_chunks = p.cout >> 4;
+        // the bias once into shared memory (zeros without one)
+        float* bias_s = reinterpret_cast<float*>(base_ptr + p.off_bias);
+        for (int i = threadIdx.x - 64; i < p.cout; i += 128) bias_s[i] = p.bias ? __ldg(p.bias + i) : 0.0f;
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
         for (int bl = 0; ok && bl < n_mine; ++bl) {
             const uint32_t half = bl & 1;
             if (!mbar_wait_warp(bar(kTBarDFull + half), (bl >> 1) & 1, abort, &g_status, kStatusTimeoutAccFull)) {
@@ -497,21 +501,34 @@ __global__ void __launch_bounds__(kTmaThreads, 1) conv_tc_tma_kernel(const __gri
             tma_block_origin(p, static_cast<int>(blockIdx.x) + bl * static_cast<int>(gridDim.x), img, h0, w0);
             const int oh = h0 + r / kBoxW, ow = w0 + r % kBoxW;
             const bool valid = oh < p.h && ow < p.w;
-            const long long pix = (static_cast<long long>(img) * p.h + oh) * p.w + ow;
-            for (int c = 0; c < n_chunks; ++c) {
-                uint32_t v[16];
-                tmem_ld16(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + half * d_cols + 16u * c, v);
-                tmem_wait_ld(v);
+            float* yrow = p.y + ((static_cast<long long>(img) * p.h + oh) * p.w + ow) * p.cout;
+            const uint32_t t0 = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + half * d_cols;
+            // up to 4 chunks (64 columns) per TMEM round trip
+            for (int c0 = 0; c0 < n_chunks; c0 += 4) {
+                uint32_t v[4][16];
+                tmem_ld16(t0 + 16u * c0, v[0]);
+                if (c0 + 1 < n_chunks) tmem_ld16(t0 + 16u * (c0 + 1), v[1]);
+                if (c0 + 2 < n_chunks) tmem_ld16(t0 + 16u * (c0 + 2), v[2]);
+                if (c0 + 3 < n_chunks) tmem_ld16(t0 + 16u * (c0 + 3), v[3]);
+                tmem_wait_ld(v[0]);
+                reg_barrier(v[1]);
+                reg_barrier(v[2]);
+                reg_barrier(v[3]);
                 if (valid) {
-                    float o[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        o[i] = __uint_as_float(v[i]) + (p.bias ? __ldg(p.bias + 16 * c + i) : 0.0f);
-                    float4* dst = reinterpret_cast<float4*>(p.y + pix * p.cout + 16 * c);
-                    dst[0] = make_float4(o[0], o[1], o[2], o[3]);
-                    dst[1] = make_float4(o[4], o[5], o[6], o[7]);
-                    dst[2] = make_float4(o[8], o[9], o[10], o[11]);
-                    dst[3] = make_float4(o[12], o[13], o[14], o[15]);
+                    for (int k = 0; k < 4; ++k) {
+                        const int c = c0 + k;
+                        if (c >= n_chunks) break;
+                        const float4* b4 = reinterpret_cast<const float4*>(bias_s + 16 * c);
+                        float4* dst = reinterpret_cast<float4*>(yrow + 16 * c);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float4 b = b4[q];
+                            dst[q] = make_float4(__uint_as_float(v[k][4 * q]) + b.x, __uint_as_float(v[k][4 * q + 1]) + b.y,
+                                                 __uint_as_float(v[k][4 * q + 2]) + b.z,
+                                                 __uint_as_float(v[k][4 * q + 3]) + b.w);
+                        }
+                    }
                 }
             }
             tc_fence_before();

@@ -692,7 +692,7 @@ int launch_conv_tc_tma(const void* x, int n, int h, int w, int cout, int kh, int
     if (n_blocks > 0x7fffffffLL) return RDVB_OK;
     const uint32_t w_bytes = static_cast<uint32_t>(kh * kw) * cout * 128u;
     const uint32_t off_a = (w_bytes + 1023u) & ~1023u;
-    const long long room = static_cast<long long>(dev->max_smem_optin) - off_a - kTBarBlockBytes - 1024;
+    const long long room = static_cast<long long>(dev->max_smem_optin) - off_a - kTBarBlockBytes - 16 - cout * 4 - 1024;
     // tiles per stream (two streams)
     const int ring = static_cast<int>(std::min<long long>(kTmaMaxRing / 2, room > 0 ? room / (2 * kATileBytes) : 0));
     if (ring < 2) return RDVB_OK;
@@ -725,7 +725,8 @@ int launch_conv_tc_tma(const void* x, int n, int h, int w, int cout, int kh, int
     p.off_a = off_a;
     p.off_bar = off_a + static_cast<uint32_t>(2 * ring) * kATileBytes;
     p.idesc = rdvb::umma_idesc_f16(static_cast<uint32_t>(cout), 0);
-    const size_t smem = p.off_bar + kTBarBlockBytes + 1024;
+    p.off_bias = (p.off_bar + kTBarBlockBytes + 15u) & ~15u;
+    const size_t smem = p.off_bias + static_cast<size_t>(cout) * 4 + 1024;
     if (dev->conv_tma_smem_set < smem) {
         cudaError_t e = cudaFuncSetAttribute(conv_tc_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
