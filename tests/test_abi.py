@@ -74,3 +74,52 @@ def test_validation_before_any_device_work(lib):
                                   N.int_array([3, 64, 64, 4]), N.int_array([5, 5, 1]), None, 0, 8, None, 0, None,
                                   None)
     assert rc == -2 and "n_samples" in N.last_error()
+
+
+def test_ratio_tracking_validation_before_any_device_work(lib):
+    import rdv_project_b200._native as N
+
+    dims, flags = N.int_array([3, 16, 1]), N.int_array([1, 1])
+    seeds = N.uint32_array([1, 2, 3, 4])
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 2, dims, None, None,
+                                   flags, 0, None, 256, None, None)
+    assert rc == -1 and "weights" in N.last_error()
+    w = N.ptr_array([1, 1])
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 2, dims, w, w, flags,
+                                   0, None, 256, None, None)
+    assert rc == -1 and "majorant_dims" in N.last_error()
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), None, 2, dims, w, w, flags,
+                                   0, None, 256, None, None)
+    assert rc == -1 and "seeds" in N.last_error()
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 2,
+                                   N.int_array([3, 16, 2]), w, w, flags, 0, None, 256, None, None)
+    assert rc == -1 and "3 -> 1" in N.last_error()
+    # nothing to do: no device needed
+    assert lib.rdvb_transmittance_rt(None, 0, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 2, dims, w, w, flags,
+                                     0, None, 256, None, None) == 0
+
+
+def test_volume_nodes_host_side():
+    """Argument handling of the volume nodes that needs no device: seeds as
+    the reference draws them, majorant wrapping, TensorGrid shapes."""
+    import torch
+
+    import rdv_project_b200 as rdv
+    from rdv_project_b200 import volumes
+
+    for _ in range(50):
+        s = volumes._draw_seeds()
+        assert len(s) == 4 and all(128 <= v < (1 << 30) for v in s)
+    g = rdv.TensorGrid(torch.ones(4, 5, 6, 1))
+    assert (g.IN, g.OUT, g.shape) == (3, 1, [4, 5, 6])
+    f = volumes._as_majorant_field(torch.ones(2, 2, 2, 1))
+    assert isinstance(f, rdv.VoxelMajorantField) and f.grid.shape == [2, 2, 2]
+    assert volumes._as_majorant_field(f) is f
+    with pytest.raises(AssertionError, match="Grid\\[3, 1\\]"):
+        rdv.VoxelMajorantField(torch.ones(4, 4, 2))
+    with pytest.raises(NotImplementedError):
+        volumes._as_majorant_field(3.0)
+    ext = rdv.linear(torch.randn(1, 3), torch.zeros(1))
+    node = rdv.RatiotrackingTransmittance(ext, torch.ones(1, 1, 1, 1), density_scale=2.0)
+    assert node.IN == 6 and node.OUT == 1 and node.density_scale == 2.0
+    assert not hasattr(node, "step_size")
