@@ -58,6 +58,7 @@ struct DeviceInfo {
     size_t rt_smem_set = 0;
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
+    size_t wino_tma_smem_set = 0;
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
@@ -523,6 +524,29 @@ int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int v
     return check_launch("winograd_f23_filter_kernel");
 }
 
+namespace {
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library); null when the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// The TMA-fed Winograd kernel for float16 input with 64 channels. Returns
+// RDVB_OK with *taken = false when the driver or the shapes do not allow it.
+int launch_winograd_tma(const void* x, int n, int h, int w, int cout, const void* u_packed, const float* bias,
+                        void* y, int y_f16, cudaStream_t stream, DeviceInfo* dev, bool* taken);
+}  // namespace
+
 int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int cin, int cout,
                           const void* u_packed, int variant, const float* bias, void* y, int y_dtype,
                           void* stream) {
@@ -548,6 +572,13 @@ int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int c
     if (n_tiles > 0x7fffffffLL - kTileM) return fail(RDVB_ERR_UNSUPPORTED, "too many tiles (%lld)", n_tiles);
     DeviceInfo* dev = nullptr;
     if (int rc = current_device(&dev)) return rc;
+    if (x_dtype == RDVB_F16 && cin == 64) {
+        bool taken = false;
+        if (int rc = launch_winograd_tma(x, n, h, w, cout, u_packed, bias, y, y_dtype == RDVB_F16 ? 1 : 0,
+                                         static_cast<cudaStream_t>(stream), dev, &taken))
+            return rc;
+        if (taken) return RDVB_OK;
+    }
 
     Params p;
     memset(&p, 0, sizeof(p));
@@ -582,6 +613,62 @@ int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int c
     kernel<<<grid, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
     return check_launch("winograd_f23_kernel");
 }
+
+namespace {
+int launch_winograd_tma(const void* x, int n, int h, int w, int cout, const void* u_packed, const float* bias,
+                        void* y, int y_f16, cudaStream_t stream, DeviceInfo* dev, bool* taken) {
+    using namespace rdvb::wino;
+    *taken = false;
+    if (const char* env = getenv("RDVB_WINO_TMA"))
+        if (atoi(env) == 0) return RDVB_OK;
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return RDVB_OK;
+    const long long tiles_h = (h + 1) / 2, tiles_w = (w + 1) / 2;
+    const long long blocks_h = (tiles_h + kTBlockTR - 1) / kTBlockTR, blocks_w = (tiles_w + kTBlockTC - 1) / kTBlockTC;
+    const long long n_blocks = static_cast<long long>(n) * blocks_h * blocks_w;
+    if (n_blocks > 0x7fffffffLL) return RDVB_OK;
+    TmaParams p;
+    memset(&p, 0, sizeof(p));
+    const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
+                                static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[3] = {128, static_cast<cuuint64_t>(w) * 128, static_cast<cuuint64_t>(h) * w * 128};
+    const cuuint32_t box[4] = {64, kTBoxW, kTBoxH, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (enc(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return RDVB_OK;
+    p.y = y;
+    p.u_pack = static_cast<const uint8_t*>(u_packed);
+    p.bias = bias;
+    p.h = h;
+    p.w = w;
+    p.cout = cout;
+    p.y_f16 = y_f16;
+    p.tiles_h = static_cast<int>(tiles_h);
+    p.tiles_w = static_cast<int>(tiles_w);
+    p.blocks_h = static_cast<int>(blocks_h);
+    p.blocks_w = static_cast<int>(blocks_w);
+    p.n_blocks = static_cast<int>(n_blocks);
+    p.u_pos_bytes = static_cast<uint32_t>(cout) * 128u;
+    p.off_v = kTBoxBytes;
+    p.off_u = p.off_v + 4 * kATileBytes;
+    p.off_bar = p.off_u + kURing * p.u_pos_bytes;
+    p.idesc = rdvb::umma_idesc_f16(static_cast<uint32_t>(cout), 0);
+    const uint32_t smem = p.off_bar + kTBarBlockBytes + 1024u;
+    if (smem > static_cast<uint32_t>(dev->max_smem_optin)) return RDVB_OK;
+    if (dev->wino_tma_smem_set < smem) {
+        cudaError_t e = cudaFuncSetAttribute(winograd_f23_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(winograd_tma): %s", cudaGetErrorString(e));
+        dev->wino_tma_smem_set = smem;
+    }
+    const int grid = static_cast<int>(std::min<long long>(dev->sm_count, n_blocks));
+    winograd_f23_tma_kernel<<<grid, kThreads, smem, stream>>>(p);
+    *taken = true;
+    return check_launch("winograd_f23_tma_kernel");
+}
+}  // namespace
 
 int rdvb_conv2d_direct_staged(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, int kh, int kw,
                               const float* weight, const float* bias, int math, int bias_first, float* y,
@@ -660,22 +747,6 @@ int rdvb_conv_tc_pack(const float* weight, int kh, int kw, int cin, int cout, in
 }
 
 namespace {
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
-// against the driver library); null when the driver does not provide it.
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    });
-    return fn;
-}
-
 // The TMA-fed kernel for float16 input with 64 channels and float16
 // operands. Returns RDVB_OK with *taken = false when the shapes or the
 // driver do not allow it (the caller then stages on the CUDA cores).

@@ -39,6 +39,7 @@
 // HBM traffic is the input read (halo re-reads hit L1/L2) plus the output
 // write, the operator's roofline.
 #pragma once
+#include <cuda.h>  // CUtensorMap (the type only; the map is encoded on the host)
 #include "ptx.cuh"
 
 namespace rdvb {
@@ -448,6 +449,312 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_kernel(const __grid_
         }
         if (ok && rows > 0) ok = epilogue(n_mine - 1);
         if (!ok) *c.abort = 1u;
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// TMA-fed variant (float16 input with 64 channels). A block is a rectangle
+// of 8 x 15 Winograd tiles (16 x 30 output pixels) of one image; its whole
+// input halo -- 18 rows x 32 columns x 64 channels, the top/left padding
+// row and column included -- is ONE tensor-map copy into shared memory
+// (72 KB), zero-filled where it leaves the image, so the transform needs no
+// masks and reads its patches from shared memory instead of waiting on
+// global loads. U is streamed per domain position from L2 through a ring of
+// 4 blocks (one position of U is COUT x 128 B), which leaves room for the
+// input box beside the 4 V tiles. The MMA-issuing thread also issues the
+// copies: the next block's box as soon as every transform warp has written
+// V(3, 0) of this block (after its last read of the box), and U of
+// position P + 3 after position P's MMAs (into the slot of P - 1, whose
+// MMAs have completed). Issue order, accumulate flags and signs, the V
+// tiles and the epilogue are those of winograd_f23_kernel.
+constexpr int kTBlockTR = 8, kTBlockTC = 15;    // tiles per block: rows x columns (120)
+constexpr int kTBoxW = 2 * kTBlockTC + 2;       // 32 input columns
+constexpr int kTBoxH = 2 * kTBlockTR + 2;       // 18 input rows
+constexpr uint32_t kTBoxBytes = 64u * 2u * kTBoxW * kTBoxH;  // 73,728
+constexpr int kURing = 4;
+
+struct TmaParams {
+    CUtensorMap tmap;       // x [N, H, W, 64] float16: dims {64, W, H, N}, box {64, 32, 18, 1}, no swizzle
+    void* y;                // [N, H, W, COUT] float32 or float16
+    const uint8_t* u_pack;  // 16 blocks of (COUT rows x 128 B), K-major SW128
+    const float* bias;      // [COUT] or null
+    int h, w, cout, y_f16;
+    int tiles_h, tiles_w, blocks_h, blocks_w, n_blocks;
+    uint32_t u_pos_bytes;   // COUT * 128: one position of U
+    uint32_t off_v, off_u, off_bar;
+    uint32_t idesc;
+};
+
+enum : int {
+    kTBarXFull = 0,                 // the block's input box landed (TMA tx)
+    kTBarAFull = 1,                 // + v: V tile v written (15 warp arrivals)
+    kTBarAEmpty = 5,                // + v: the GEMMs reading V tile v are done (commit)
+    kTBarUFull = 9,                 // + ring slot: U block landed (tx)
+    kTBarUEmpty = 9 + kURing,       // + ring slot: the GEMMs reading it are done (commit)
+    kTBarDFull = 9 + 2 * kURing,    // + half
+    kTBarDrain = 11 + 2 * kURing,
+    kTNumBars = 12 + 2 * kURing,
+};
+constexpr uint32_t kTBarBlockBytes = kTNumBars * 8 + 16;
+
+__device__ __forceinline__ void tma_wino_block(const TmaParams& p, int blk, int& img, int& by, int& bx) {
+    const int per_img = p.blocks_h * p.blocks_w;
+    img = blk / per_img;
+    const int rem = blk - img * per_img;
+    by = rem / p.blocks_w;
+    bx = rem - by * p.blocks_w;
+}
+
+// First pass of domain row u for both items of the thread, from the box:
+// m = d_k0 + t_u * d_k1 per patch column (rows k0(u), k1(u) of the patch).
+__device__ __forceinline__ void first_pass_smem(uint32_t box, const uint32_t (&poff)[2], int u,
+                                                float (&m)[2][4][8]) {
+    const int k0 = bt_k0(u), k1 = bt_k1(u);
+    const float t = bt_t(u);
+    const uint32_t o0 = static_cast<uint32_t>(k0 * kTBoxW * 128), o1 = static_cast<uint32_t>(k1 * kTBoxW * 128);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int col = 0; col < 4; ++col) {
+            uint4 qa, qb;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(qa.x), "=r"(qa.y), "=r"(qa.z), "=r"(qa.w)
+                         : "r"(box + poff[i] + o0 + col * 128u));
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(qb.x), "=r"(qb.y), "=r"(qb.z), "=r"(qb.w)
+                         : "r"(box + poff[i] + o1 + col * 128u));
+            float a[8], b[8];
+            h8_to_f32(qa, a);
+            h8_to_f32(qb, b);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) m[i][col][e] = fmaf(t, b[e], a[e]);
+        }
+}
+
+// D_ij + bias of this lane's tile (block row `row` < 120) for 16 channels
+// of group grp: the 4 output positions of the 2x2 tile.
+__device__ __forceinline__ void store_block_tma(const TmaParams& p, int img, int by, int bx, int row, int grp,
+                                                uint32_t td) {
+    const bool in_block = row < kTBlockTR * kTBlockTC;
+    const int ty = by * kTBlockTR + (in_block ? row / kTBlockTC : 0);
+    const int tx = bx * kTBlockTC + (in_block ? row % kTBlockTC : 0);
+    float b[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) b[c] = p.bias ? __ldg(p.bias + 16 * grp + c) : 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t r[16];
+        tmem_ld16(td + static_cast<uint32_t>(q * kMaxChannels), r);
+        tmem_wait_ld();
+        const int oh = 2 * ty + (q >> 1), ow = 2 * tx + (q & 1);
+        if (!in_block || oh >= p.h || ow >= p.w) continue;
+        const long long o = ((static_cast<long long>(img) * p.h + oh) * p.w + ow) * p.cout + 16 * grp;
+        float y[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) y[c] = __uint_as_float(r[c]) + b[c];
+        if (!p.y_f16) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4)
+                dst[c4] = make_float4(y[4 * c4], y[4 * c4 + 1], y[4 * c4 + 2], y[4 * c4 + 3]);
+        } else {
+            uint32_t pk[8];
+#pragma unroll
+            for (int c = 0; c < 16; c += 2) pk[c >> 1] = pack_f16x2(y[c], y[c + 1]);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.y) + o);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) winograd_f23_tma_kernel(const __grid_constant__ TmaParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_addr(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t* const base_ptr = smem_raw + (base - raw_addr);
+    const uint32_t box = base;  // the input box at offset 0
+    const uint32_t v_base = base + p.off_v;
+    const uint32_t u_base = base + p.off_u;
+    const uint32_t bar_base = base + p.off_bar;
+    auto bar = [&](int i) -> uint32_t { return bar_base + 8u * static_cast<uint32_t>(i); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + p.off_bar + kTNumBars * 8);
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(base_ptr + p.off_bar + kTNumBars * 8 + 4);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar(kTBarXFull), 1);
+        for (int v = 0; v < 4; ++v) {
+            mbar_init(bar(kTBarAFull + v), kXWarps);
+            mbar_init(bar(kTBarAEmpty + v), 1);
+        }
+        for (int q = 0; q < kURing; ++q) {
+            mbar_init(bar(kTBarUFull + q), 1);
+            mbar_init(bar(kTBarUEmpty + q), 1);
+        }
+        mbar_init(bar(kTBarDFull), 1);
+        mbar_init(bar(kTBarDFull + 1), 1);
+        mbar_init(bar(kTBarDrain), 1);
+        *abort = 0u;
+        fence_mbarrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_addr(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int n_mine = blockIdx.x < p.n_blocks ? (p.n_blocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    bool ok = true;
+
+    if (warp == kIssueWarp) {
+        // ------------------------------------ MMA issuer and copy producer
+        if (lane == 0) {
+            const int n_pos = 16 * n_mine;
+            int x_issued = 0, u_issued = 0;  // copies started (input boxes, U blocks)
+            auto load_box = [&](int bl) {
+                int img, by, bx;
+                tma_wino_block(p, static_cast<int>(blockIdx.x) + bl * static_cast<int>(gridDim.x), img, by, bx);
+                mbar_arrive_expect_tx(bar(kTBarXFull), kTBoxBytes);
+                tma_load_4d(box, &p.tmap, 0, 2 * kTBlockTC * bx - 1, 2 * kTBlockTR * by - 1, img, bar(kTBarXFull));
+                ++x_issued;
+            };
+            auto load_u = [&](int pos) {
+                const int q = pos % kURing;
+                mbar_arrive_expect_tx(bar(kTBarUFull + q), p.u_pos_bytes);
+                bulk_g2s(u_base + static_cast<uint32_t>(q) * p.u_pos_bytes, p.u_pack + (pos % 16) * p.u_pos_bytes,
+                         p.u_pos_bytes, bar(kTBarUFull + q));
+                ++u_issued;
+            };
+            if (n_mine > 0) load_box(0);
+            for (int pos = 0; pos < 3 && pos < n_pos; ++pos) load_u(pos);
+            const uint64_t v_desc0 = umma_desc_sw128(v_base);
+            const uint64_t u_desc0 = umma_desc_sw128(u_base);
+            const uint64_t u_step = static_cast<uint64_t>(p.u_pos_bytes >> 4);
+            const uint32_t ksteps = 4;  // CIN = 64
+            uint64_t a_desc[4];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) a_desc[v] = v_desc0 + static_cast<uint64_t>(v) * (kATileBytes >> 4);
+            // Unrolled over the domain rows, like winograd_f23_kernel: every
+            // MMA's accumulate flag and sign is a compile-time constant.
+            for (int bl = 0; ok && bl < n_mine; ++bl) {
+                const uint32_t d_base = tmem_base + (bl & 1) * kDCols;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int r = bl * 4 + u;
+                    if (!ok) break;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const int pos = r * 4 + v;
+                        if (!mbar_wait(bar(kTBarAFull + v), r & 1, abort, &g_status, kStatusTimeoutAFull)) {
+                            ok = false;
+                            break;
+                        }
+                        // every transform warp has written V(3, 0): none reads the box again
+                        if (u == 3 && v == 0 && bl + 1 < n_mine) load_box(bl + 1);
+                        const int q = pos % kURing;
+                        if (!mbar_wait(bar(kTBarUFull + q), (pos / kURing) & 1, abort, &g_status,
+                                       kStatusTimeoutWFull)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        issue_position(u, v, d_base, a_desc[v], u_desc0 + static_cast<uint64_t>(q) * u_step, p.idesc,
+                                       ksteps);
+                        umma_commit(bar(kTBarAEmpty + v));  // V tile v may be rewritten
+                        umma_commit(bar(kTBarUEmpty + q));  // U slot q may be reloaded
+                        if (u == 3 && v == 3) umma_commit(bar(kTBarDFull + (bl & 1)));
+                        // U of position pos + 3 into the slot of pos - 1 once its GEMMs are done
+                        if (pos + 3 < n_pos) {
+                            if (pos >= 1 && !mbar_wait(bar(kTBarUEmpty + (pos - 1) % kURing), ((pos - 1) / kURing) & 1,
+                                                       abort, &g_status, kStatusTimeoutOther)) {
+                                ok = false;
+                                break;
+                            }
+                            load_u(pos + 3);
+                        }
+                    }
+                }
+            }
+            if (!ok) *abort = 1u;
+            // every issued MMA completes before TMEM is released, every copy
+            // lands before the CTA exits
+            umma_commit(bar(kTBarDrain));
+            drain_wait(bar(kTBarDrain), 0u);
+            if (x_issued > 0) drain_wait(bar(kTBarXFull), (x_issued - 1) & 1);
+            for (int k = (u_issued > kURing ? u_issued - kURing : 0); k < u_issued; ++k)
+                drain_wait(bar(kTBarUFull + k % kURing), (k / kURing) & 1);
+        }
+    } else {
+        // ------------------------------------------- transform + epilogue
+        const int quad = warp & 3;
+        auto epilogue = [&](int bl) -> bool {
+            const uint32_t half = bl & 1;
+            if (!mbar_wait_warp(bar(kTBarDFull + half), (bl >> 1) & 1, abort, &g_status, kStatusTimeoutAccFull))
+                return false;
+            tc_fence_after();
+            int img, by, bx;
+            tma_wino_block(p, static_cast<int>(blockIdx.x) + bl * static_cast<int>(gridDim.x), img, by, bx);
+            const int row = quad * 32 + lane;
+            for (int pr = warp; pr < 16; pr += 12) {  // warp 3: pairs 3 and 15
+                const int grp = pr >> 2;
+                if (16 * grp < p.cout)
+                    store_block_tma(p, img, by, bx, row, grp,
+                                    tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + 16u * grp + half * kDCols);
+                if (warp != 3) break;
+            }
+            tc_fence_before();
+            return true;
+        };
+        // this thread's two (tile, 8-channel chunk) items: byte offset of the
+        // patch's (row 0, col 0) in the box, and of the tile row in a V tile
+        const int xt = threadIdx.x;  // 0 .. 479
+        uint32_t poff[2], soff[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int idx = xt + i * kXThreads;
+            const int tr = idx >> 3, ck = idx & 7;  // block tile 0..119, channel chunk
+            const int trow = tr / kTBlockTC, tcol = tr - trow * kTBlockTC;
+            poff[i] = static_cast<uint32_t>(((2 * trow) * kTBoxW + 2 * tcol) * 128 + ck * 16);
+            soff[i] = sw128_offset(static_cast<uint32_t>(tr), static_cast<uint32_t>(ck * 8), kTileM);
+        }
+        RowCtx c;
+        c.p = nullptr;
+        c.has[0] = c.has[1] = true;
+        c.it[0].soff = soff[0];
+        c.it[1].soff = soff[1];
+        c.a_base = v_base;
+        c.bar_base = bar_base;
+        c.abort = abort;
+        c.lane = lane;
+        for (int bl = 0; ok && bl < n_mine; ++bl) {
+            // the block's input box
+            if (!mbar_wait_warp(bar(kTBarXFull), bl & 1, abort, &g_status, kStatusTimeoutXFull)) {
+                ok = false;
+                break;
+            }
+            for (int u = 0; ok && u < 4; ++u) {
+                c.r = bl * 4 + u;
+                c.u = u;
+                float m[2][4][8];
+                first_pass_smem(box, poff, u, m);
+                ok = do_position<0>(c, m) && do_position<1>(c, m) && do_position<2>(c, m) && do_position<3>(c, m);
+                // the previous block's outputs, while this block's GEMMs run
+                if (ok && u == 0 && bl > 0) ok = epilogue(bl - 1);
+            }
+        }
+        if (ok && n_mine > 0) ok = epilogue(n_mine - 1);
+        if (!ok) *abort = 1u;
     }
 
     tc_fence_before();

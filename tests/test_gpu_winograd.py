@@ -197,3 +197,30 @@ def test_errors_and_empty(rdv, cuda_device):
         rdv.Conv2DTensorOpWinograd3x3(torch.zeros(15 * 8, 16), torch.zeros(3, 3, 16, 16), torch.zeros(16), 15, 8)
     with pytest.raises(AssertionError, match=r"in_channels \(80\) must be at most 64"):
         rdv.Conv2DTensorOpWinograd3x3(torch.zeros(64, 80), torch.zeros(3, 3, 80, 16), torch.zeros(16), 8, 8)
+
+
+@pytest.mark.parametrize("shape,cout", [((3, 37, 61), 64), ((1, 1, 1), 64), ((2, 17, 31), 32),
+                                        ((8, 128, 128), 64), ((1, 33, 100), 48)])
+def test_tma_fed_kernel_equals_global_load_kernel(rdv, cuda_device, monkeypatch, shape, cout):
+    """float16 input with 64 channels takes the TMA-fed kernel (the block's
+    input halo as one box, zero-filled at the border): the same transform
+    arithmetic and GEMMs as the global-load kernel, so the outputs are
+    bit-identical; both agree with the oracle. (8, 128, 128): 320 blocks,
+    more than one per CTA, so the input box and the U ring wrap."""
+    n, h, wd = shape
+    rng = np.random.default_rng(h * 7 + wd + cout)
+    x = rng.standard_normal((n, h, wd, 64)).astype(np.float16).astype(np.float32)
+    w, b = _weights(rng, 64, cout)
+    conv = rdv.Conv3x3Winograd(torch.from_numpy(w), torch.from_numpy(b))
+    xt = torch.from_numpy(x).to(cuda_device).half()
+    y_tma = conv(xt)
+    y16_tma = conv(xt, out_dtype=torch.float16)
+    monkeypatch.setenv("RDVB_WINO_TMA", "0")
+    y_ref = conv(xt)
+    y16_ref = conv(xt, out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    assert torch.equal(y_tma, y_ref)
+    assert torch.equal(y16_tma, y16_ref)
+    if n * h * wd <= 20000:
+        _check(y_tma.cpu().numpy(), _oracle_staged(x, w, b), TIGHT)
+    assert rdv.device_status() == 0
