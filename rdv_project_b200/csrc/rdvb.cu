@@ -664,7 +664,7 @@ int launch_winograd_tma(const void* x, int n, int h, int w, int cout, const void
         dev->wino_tma_smem_set = smem;
     }
     const int grid = static_cast<int>(std::min<long long>(dev->sm_count, n_blocks));
-    winograd_f23_tma_kernel<<<grid, kThreads, smem, stream>>>(p);
+    winograd_f23_tma_kernel<<<grid, kTWThreads, smem, stream>>>(p);
     *taken = true;
     return check_launch("winograd_f23_tma_kernel");
 }

@@ -472,13 +472,19 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_kernel(const __grid_
 // copies: the next block's box as soon as every transform warp has written
 // V(3, 0) of this block (after its last read of the box), and U of
 // position P + 3 after position P's MMAs (into the slot of P - 1, whose
-// MMAs have completed). Issue order, accumulate flags and signs, the V
-// tiles and the epilogue are those of winograd_f23_kernel.
+// MMAs have completed). Four epilogue warps (16-19, one per TMEM lane
+// quadrant) add the bias and store each finished block while the transform
+// warps go on with the next one (the output stores, issued by the transform
+// warps, were the longest part of a block), then free the accumulator half
+// for block b + 2. Issue order, accumulate flags and signs and the V tiles
+// are those of winograd_f23_kernel.
 constexpr int kTBlockTR = 8, kTBlockTC = 15;    // tiles per block: rows x columns (120)
 constexpr int kTBoxW = 2 * kTBlockTC + 2;       // 32 input columns
 constexpr int kTBoxH = 2 * kTBlockTR + 2;       // 18 input rows
 constexpr uint32_t kTBoxBytes = 64u * 2u * kTBoxW * kTBoxH;  // 73,728
 constexpr int kURing = 4;
+constexpr int kTEpiWarp0 = 16;                 // epilogue warps 16-19
+constexpr int kTWThreads = 20 * 32;
 
 struct TmaParams {
     CUtensorMap tmap;       // x [N, H, W, 64] float16: dims {64, W, H, N}, box {64, 32, 18, 1}, no swizzle
@@ -500,7 +506,8 @@ enum : int {
     kTBarUEmpty = 9 + kURing,       // + ring slot: the GEMMs reading it are done (commit)
     kTBarDFull = 9 + 2 * kURing,    // + half
     kTBarDrain = 11 + 2 * kURing,
-    kTNumBars = 12 + 2 * kURing,
+    kTBarDEmpty = 12 + 2 * kURing,  // + half: the epilogue read it (4 warp arrivals)
+    kTNumBars = 14 + 2 * kURing,
 };
 constexpr uint32_t kTBarBlockBytes = kTNumBars * 8 + 16;
 
@@ -575,7 +582,7 @@ __device__ __forceinline__ void store_block_tma(const TmaParams& p, int img, int
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) winograd_f23_tma_kernel(const __grid_constant__ TmaParams p) {
+__global__ void __launch_bounds__(kTWThreads, 1) winograd_f23_tma_kernel(const __grid_constant__ TmaParams p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_addr(smem_raw);
     const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -602,6 +609,8 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_tma_kernel(const __g
         }
         mbar_init(bar(kTBarDFull), 1);
         mbar_init(bar(kTBarDFull + 1), 1);
+        mbar_init(bar(kTBarDEmpty), 4);
+        mbar_init(bar(kTBarDEmpty + 1), 4);
         mbar_init(bar(kTBarDrain), 1);
         *abort = 0u;
         fence_mbarrier_init();
@@ -649,6 +658,12 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_tma_kernel(const __g
             // MMA's accumulate flag and sign is a compile-time constant.
             for (int bl = 0; ok && bl < n_mine; ++bl) {
                 const uint32_t d_base = tmem_base + (bl & 1) * kDCols;
+                // the accumulator half was read out by the epilogue of block bl - 2
+                if (bl >= 2 && !mbar_wait(bar(kTBarDEmpty + (bl & 1)), ((bl >> 1) - 1) & 1, abort, &g_status,
+                                          kStatusTimeoutOther)) {
+                    ok = false;
+                    break;
+                }
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int r = bl * 4 + u;
@@ -695,27 +710,31 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_tma_kernel(const __g
             for (int k = (u_issued > kURing ? u_issued - kURing : 0); k < u_issued; ++k)
                 drain_wait(bar(kTBarUFull + k % kURing), (k / kURing) & 1);
         }
-    } else {
-        // ------------------------------------------- transform + epilogue
+    } else if (warp >= kTEpiWarp0) {
+        // -------------------------------------------------------- epilogue
+        // Warp (16 + q) owns TMEM lane quadrant q: tiles 32 q .. 32 q + 31 of
+        // the block, every 16-channel group; then frees the half.
         const int quad = warp & 3;
-        auto epilogue = [&](int bl) -> bool {
+        const int row = quad * 32 + lane;
+        for (int bl = 0; ok && bl < n_mine; ++bl) {
             const uint32_t half = bl & 1;
-            if (!mbar_wait_warp(bar(kTBarDFull + half), (bl >> 1) & 1, abort, &g_status, kStatusTimeoutAccFull))
-                return false;
+            if (!mbar_wait_warp(bar(kTBarDFull + half), (bl >> 1) & 1, abort, &g_status, kStatusTimeoutAccFull)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
             int img, by, bx;
             tma_wino_block(p, static_cast<int>(blockIdx.x) + bl * static_cast<int>(gridDim.x), img, by, bx);
-            const int row = quad * 32 + lane;
-            for (int pr = warp; pr < 16; pr += 12) {  // warp 3: pairs 3 and 15
-                const int grp = pr >> 2;
-                if (16 * grp < p.cout)
-                    store_block_tma(p, img, by, bx, row, grp,
-                                    tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + 16u * grp + half * kDCols);
-                if (warp != 3) break;
-            }
+            for (int grp = 0; 16 * grp < p.cout; ++grp)
+                store_block_tma(p, img, by, bx, row, grp,
+                                tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + 16u * grp + half * kDCols);
             tc_fence_before();
-            return true;
-        };
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kTBarDEmpty + half));
+        }
+        if (!ok) *abort = 1u;
+    } else {
+        // -------------------------------------------------------- transform
         // this thread's two (tile, 8-channel chunk) items: byte offset of the
         // patch's (row 0, col 0) in the box, and of the tile row in a V tile
         const int xt = threadIdx.x;  // 0 .. 479
@@ -749,11 +768,8 @@ __global__ void __launch_bounds__(kThreads, 1) winograd_f23_tma_kernel(const __g
                 float m[2][4][8];
                 first_pass_smem(box, poff, u, m);
                 ok = do_position<0>(c, m) && do_position<1>(c, m) && do_position<2>(c, m) && do_position<3>(c, m);
-                // the previous block's outputs, while this block's GEMMs run
-                if (ok && u == 0 && bl > 0) ok = epilogue(bl - 1);
             }
         }
-        if (ok && n_mine > 0) ok = epilogue(n_mine - 1);
         if (!ok) *abort = 1u;
     }
 
