@@ -255,6 +255,15 @@ int rdvb_concat_channels(const float* x1, int c1, const float* x2, int c2, int64
 int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, float* out,
                      void* stream);
 
+/* Cameras with pixel_jitter (rdv/domain/rendering.py:24-42, jitter=True;
+ * rdv/shaders/rendering/cameras.h:7): as rdvb_camera_rays, but the ray of
+ * pixel i = (camera, row, column) flattened passes through (column + r0,
+ * row + r1) instead of the pixel centre, r0 and r1 the first two draws of
+ * the reference generator (random_library.h:7-34) started from the 4 host
+ * seeds spawned by index i (random_library.h:44-49, :256-268). */
+int rdvb_camera_rays_jittered(const float* poses, int n_cameras, int width, int height, float aspect, float fov,
+                              const uint32_t* seeds, float* out, void* stream);
+
 /* Workspace bytes rdvb_raymarch_render needs for a width x height image. */
 int64_t rdvb_raymarch_workspace_bytes(int width, int height);
 
@@ -323,14 +332,17 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
  * seeds: 4 host uint32, the dispatch's generator seeds (the reference draws
  * them per dispatch, core/_common.py:66-75); ray i draws from the seeds
  * spawned by index i (libraries/random_library.h:44-49, :256-268), the
- * Taus + LCG generator of random_library.h:7-34.
+ * Taus + LCG generator of random_library.h:7-34. draws_before (0..64):
+ * draws of each ray's generator already taken upstream in the same
+ * invocation -- 2 when the rays come from a jittered Cameras grid composed
+ * with the node (cameras.h:7 draws the pixel offset first), else 0.
  * The extinction chain as rdvb_transmittance_rm (any Linear / LinearFast /
  * ReLU chain 3 -> ... -> 1, evaluated on the CUDA cores). workspace: 256
  * bytes, 256-byte aligned; bytes 8-15 hold the number of extinction
  * evaluations of the call. */
 int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
-                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int n_layers,
-                          const int* dims, const float* const* weights, const float* const* biases,
+                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int draws_before,
+                          int n_layers, const int* dims, const float* const* weights, const float* const* biases,
                           const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, float* out,
                           void* stream);
 

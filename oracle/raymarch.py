@@ -40,9 +40,12 @@ def _normalize(v):
 
 
 def camera_rays(pose9, width: int, height: int, aspect: float | None = None, fov: float | None = None,
-                row_begin: int = 0, row_end: int | None = None):
+                row_begin: int = 0, row_end: int | None = None, jitter_seeds=None, camera_index: int = 0):
     """cameras.h:1-20 for every pixel (rows row_begin..row_end) -> origins
-    [R, 3], unit directions [R, 3], float32 arithmetic."""
+    [R, 3], unit directions [R, 3], float32 arithmetic. With jitter_seeds
+    (pixel_jitter, cameras.h:7) the sub-pixel point is (random(), random())
+    of the pixel's generator -- the seeds spawned by its flat index
+    (camera_index * height + row) * width + column -- instead of the centre."""
     if aspect is None:
         aspect = width / height
     if fov is None:
@@ -52,8 +55,15 @@ def camera_rays(pose9, width: int, height: int, aspect: float | None = None, fov
     o, t, n = pose[0], pose[1], pose[2]
     ys, xs = np.meshgrid(np.arange(row_begin, row_end, dtype=np.float32),
                          np.arange(width, dtype=np.float32), indexing="ij")
-    px = (xs + np.float32(0.5)) / np.float32(width) * np.float32(2.0) - np.float32(1.0)
-    py = (ys + np.float32(0.5)) / np.float32(height) * np.float32(2.0) - np.float32(1.0)
+    if jitter_seeds is None:
+        jx = jy = np.float32(0.5)
+    else:
+        flat = ((camera_index * height + ys.astype(np.int64)) * width + xs.astype(np.int64)).reshape(-1)
+        st = random_spawn(jitter_seeds, flat)
+        jx = random_draw(st).reshape(xs.shape)
+        jy = random_draw(st).reshape(xs.shape)
+    px = (xs + jx) / np.float32(width) * np.float32(2.0) - np.float32(1.0)
+    py = (ys + jy) / np.float32(height) * np.float32(2.0) - np.float32(1.0)
     sx = px * np.float32(aspect)
     sy = py
     sz = np.float32(1.0 / math.tan(np.float32(fov) * 0.5))
@@ -354,12 +364,14 @@ def transmittance_rt(x, w, d, density_scale, extinction, majorant, state, counts
 
 
 def ratiotracking_transmittance(origins, dirs, density_scale, extinction, grid, seeds, transform=None,
-                                index=None, return_evaluations: bool = False):
+                                index=None, return_evaluations: bool = False, draws_before: int = 0):
     """RatiotrackingTransmittance.forward
     (rdv/shaders/volumes/ratiotracking_transmittance.h): object space, slab
     test, miss -> 1, entry clamp, then transmittance_rt over d = tMax - tMin
     with ray r's generator spawned from `seeds` by index[r] (default r) and
-    a VoxelMajorantField over `grid` [D, H, W]."""
+    a VoxelMajorantField over `grid` [D, H, W]. draws_before: draws of each
+    ray's generator already taken in the same invocation (2 after a jittered
+    camera, cameras.h:7)."""
     o, w = object_space(origins, dirs, transform)
     tmin, tmax = ray_box(o, w)
     miss = (tmax <= 0) | (tmin > tmax)
@@ -376,6 +388,8 @@ def ratiotracking_transmittance(origins, dirs, density_scale, extinction, grid, 
         g = g[..., 0]
     if hit.size:
         state = random_spawn(seeds, idx[hit])
+        for _ in range(draws_before):
+            random_step(state)
         out[hit] = transmittance_rt(x[hit], w[hit], d[hit], density_scale, extinction,
                                     lambda xx, ww: voxel_majorant(g, xx, ww), state, counts=counts)
     if return_evaluations:

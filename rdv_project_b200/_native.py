@@ -52,14 +52,15 @@ SIGNATURES = {
     "rdvb_upsample2x": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_concat_channels": (_c_int, [_vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "rdvb_camera_rays": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_f, _c_f, _vp, _vp]),
+    "rdvb_camera_rays_jittered": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_f, _c_f, _vp, _vp, _vp]),
     "rdvb_raymarch_workspace_bytes": (_c_i64, [_c_int, _c_int]),
     "rdvb_raymarch_render": (_c_int, [_vp, _c_int, _c_int, _c_f, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int, _c_int,
                                       _vp, ctypes.c_size_t, _vp, _vp]),
     "rdvb_transmittance_workspace_bytes": (_c_i64, [_c_i64, _c_int, _vp, _vp]),
     "rdvb_transmittance_rm": (_c_int, [_vp, _c_i64, _vp, _c_f, _c_f, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
                                        ctypes.c_size_t, _vp, _vp]),
-    "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int,
-                                       _vp, ctypes.c_size_t, _vp, _vp]),
+    "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp,
+                                       _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
 }
 
 

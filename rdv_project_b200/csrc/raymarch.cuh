@@ -3,6 +3,7 @@
 // mode (mlp_tc.cuh, RAY = true), which evaluates the MLP on each ray's 128
 // samples and composites front to back.
 #pragma once
+#include "rng.cuh"
 #include "mlp_tc.cuh"
 
 namespace rdvb {
@@ -33,8 +34,14 @@ __global__ void ray_compact_kernel(const __grid_constant__ mlp_tc::RayParams rp,
 // Cameras (rdv/domain/rendering.py:10-42, rdv/shaders/rendering/cameras.h:1-20):
 // out[cam, y, x] = (origin, unit direction) of the pixel-centre ray, 6 floats.
 // poses [ncam, 9] = origin | target | up.
+// Cameras grid evaluation (rdv/shaders/rendering/cameras.h:1-20). Pixel i =
+// (camera, row, column) flattened. Without jitter the ray passes through the
+// pixel centre; with jitter (pixel_jitter != 0) through (column + random(),
+// row + random()), the two draws of pixel i's own generator (the dispatch
+// seeds spawned by i; the x offset is drawn first).
 __global__ void camera_rays_kernel(const float* __restrict__ poses, int ncam, int width, int height, float aspect,
-                                   float fov, float* __restrict__ out) {
+                                   float fov, int jitter, uint4 seeds, float* __restrict__ out) {
+    const unsigned sd[4] = {seeds.x, seeds.y, seeds.z, seeds.w};
     const long long total = static_cast<long long>(ncam) * height * width;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -51,8 +58,14 @@ __global__ void camera_rays_kernel(const float* __restrict__ poses, int ncam, in
         const float xl = 1.0f / sqrtf(xa[0] * xa[0] + xa[1] * xa[1] + xa[2] * xa[2]);
         xa[0] *= xl; xa[1] *= xl; xa[2] *= xl;
         const float ya[3] = {z[1] * xa[2] - z[2] * xa[1], z[2] * xa[0] - z[0] * xa[2], z[0] * xa[1] - z[1] * xa[0]};
-        const float px = (static_cast<float>(x) + 0.5f) / static_cast<float>(width) * 2.0f - 1.0f;
-        const float py = (static_cast<float>(y) + 0.5f) / static_cast<float>(height) * 2.0f - 1.0f;
+        float jx = 0.5f, jy = 0.5f;
+        if (jitter) {
+            Rng r = rng_spawn(sd, static_cast<unsigned>(i));
+            jx = rng_uniform(r);
+            jy = rng_uniform(r);
+        }
+        const float px = (static_cast<float>(x) + jx) / static_cast<float>(width) * 2.0f - 1.0f;
+        const float py = (static_cast<float>(y) + jy) / static_cast<float>(height) * 2.0f - 1.0f;
         const float sx = px * aspect, sy = py, sz = 1.0f / tanf(fov * 0.5f);
         float w[3];
 #pragma unroll

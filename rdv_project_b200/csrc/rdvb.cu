@@ -1288,11 +1288,13 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
 }
 
 int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
-                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int n_layers,
-                          const int* dims, const float* const* weights, const float* const* biases,
+                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int draws_before,
+                          int n_layers, const int* dims, const float* const* weights, const float* const* biases,
                           const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, float* out,
                           void* stream) {
     using namespace rdvb::trm;
+    if (draws_before < 0 || draws_before > 64)
+        return fail(RDVB_ERR_INVALID_ARG, "draws_before must be in [0, 64], got %d", draws_before);
     if (n_rays < 0) return fail(RDVB_ERR_INVALID_ARG, "n_rays must be >= 0");
     if (n_layers < 1 || n_layers > kMaxLayers)
         return fail(RDVB_ERR_INVALID_ARG, "n_layers must be in [1, %d], got %d", kMaxLayers, n_layers);
@@ -1340,14 +1342,17 @@ int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transf
     p.mdim[2] = majorant_dims[0];  // z: D
     for (int k = 0; k < 3; ++k) p.mvs[k] = 2.0f / static_cast<float>(p.mdim[k]);
     for (int k = 0; k < 4; ++k) p.seeds[k] = seeds[k];
+    p.draws_before = draws_before;
     if (int rc = trm_object_space(transform, p)) return rc;
     return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev,
                              static_cast<cudaStream_t>(stream), true);
 }
 
-int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, float* out,
-                     void* stream) {
+namespace {
+int camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, int jitter,
+                const uint32_t* seeds, float* out, void* stream) {
     if (n_cameras < 0 || width < 0 || height < 0) return fail(RDVB_ERR_INVALID_ARG, "sizes must be >= 0");
+    if (jitter && !seeds) return fail(RDVB_ERR_INVALID_ARG, "seeds must not be NULL");
     if (n_cameras == 0 || width == 0 || height == 0) return RDVB_OK;
     if (!poses || !out) return fail(RDVB_ERR_INVALID_ARG, "poses and out must not be NULL");
     DeviceInfo* dev = nullptr;
@@ -1358,9 +1363,21 @@ int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, f
     const int threads = 256;
     const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + threads - 1) / threads,
                                                                                    dev->sm_count * 16LL)));
+    const uint4 sd = jitter ? make_uint4(seeds[0], seeds[1], seeds[2], seeds[3]) : make_uint4(0u, 0u, 0u, 0u);
     rdvb::ray::camera_rays_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-        poses, n_cameras, width, height, aspect, fov, out);
+        poses, n_cameras, width, height, aspect, fov, jitter ? 1 : 0, sd, out);
     return check_launch("camera_rays_kernel");
+}
+}  // namespace
+
+int rdvb_camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, float* out,
+                     void* stream) {
+    return camera_rays(poses, n_cameras, width, height, aspect, fov, 0, nullptr, out, stream);
+}
+
+int rdvb_camera_rays_jittered(const float* poses, int n_cameras, int width, int height, float aspect, float fov,
+                              const uint32_t* seeds, float* out, void* stream) {
+    return camera_rays(poses, n_cameras, width, height, aspect, fov, 1, seeds, out, stream);
 }
 
 }  // extern "C"

@@ -30,6 +30,7 @@
 // different numbers of steps.
 #pragma once
 #include "mlp_tc.cuh"
+#include "rng.cuh"
 
 namespace rdvb {
 namespace trm {
@@ -69,6 +70,7 @@ struct Params {
     int mdim[3];            // W, H, D: cells along x, y, z
     float mvs[3];           // voxel sizes 2 / mdim (fp32 division, as the reference's vec3(2.0) / dim)
     unsigned seeds[4];      // the dispatch's generator seeds
+    int draws_before;       // draws of each ray's generator already used upstream (a jittered camera: 2)
 };
 
 __device__ __forceinline__ float stage_val(float v, int math) {
@@ -280,39 +282,6 @@ __global__ void __launch_bounds__(kThreads) transmittance_kernel(const __grid_co
 //   returns 0, else T = 1.
 // Every operation is a separately rounded fp32 operation (no contraction);
 // log is CUDA's logf.
-struct Rng {
-    unsigned x, y, z, w;
-};
-
-__device__ __forceinline__ unsigned taus_step(unsigned z, int s1, int s2, int s3, unsigned m) {
-    const unsigned b = ((z << s1) ^ z) >> s2;
-    return ((z & m) << s3) ^ b;
-}
-
-__device__ __forceinline__ void rng_step(Rng& r) {
-    r.x = taus_step(r.x, 13, 19, 12, 4294967294u);
-    r.y = taus_step(r.y, 2, 25, 4, 4294967288u);
-    r.z = taus_step(r.z, 3, 11, 17, 4294967280u);
-    r.w = 1664525u * r.w + 1013904223u;
-}
-
-__device__ __forceinline__ float rng_uniform(Rng& r) {
-    rng_step(r);
-    const unsigned v = r.x ^ r.y ^ r.z ^ r.w;
-    return __fsub_rn(__uint_as_float((v & 0x007FFFFFu) | 0x3F800000u), 1.0f);
-}
-
-// random_spawn(seeds, index): the index's int arithmetic wraps, as unsigned.
-__device__ __forceinline__ Rng rng_spawn(const unsigned (&s)[4], unsigned index) {
-    Rng r;
-    r.x = s[0] ^ (index ^ 17u);
-    r.y = s[1] ^ (index * 123111171u);
-    r.z = s[2] ^ (index + 11u);
-    r.w = s[3] ^ (index ^ (s[0] + 13u * s[1]));
-    rng_step(r);
-    return r;
-}
-
 __device__ __forceinline__ float voxel_majorant(const Params& p, const float (&x)[3], const float (&w)[3],
                                                 float& dist) {
     int cell[3];
@@ -373,6 +342,7 @@ __global__ void __launch_bounds__(kThreads) ratiotracking_kernel(const __grid_co
                 T = 1.0f;
                 safety = 0;
                 r = rng_spawn(p.seeds, static_cast<unsigned>(ray));
+                for (int k = 0; k < p.draws_before; ++k) rng_step(r);
             }
             if (!(d > 0.0f) || safety >= kRtSafety) {  // the loop condition
                 p.out[ray] = T;

@@ -4,8 +4,13 @@
   mirrors the reference's pinhole ray grid (rdv/domain/rendering.py:10-42,
   rdv/shaders/rendering/cameras.h:1-20): ``poses`` is ``[num_cameras, 9]``
   (origin | target | up); calling it returns ``[num_cameras, height, width,
-  6]`` float32 (origin, unit direction) -> rdvb_camera_rays. Pixel jitter
-  (random sub-pixel offsets) is not implemented.
+  6]`` float32 (origin, unit direction) -> rdvb_camera_rays. With
+  ``jitter=True`` every pixel's ray passes through a random point of the
+  pixel instead of its centre: the first two draws of the pixel's own
+  generator (the reference's Taus + LCG, started from the call's seeds
+  spawned by the flat pixel index) -> rdvb_camera_rays_jittered. Each call
+  draws fresh seeds, as the reference does per dispatch; ``cameras(seeds=...)``
+  fixes them.
 * ``VolumeRenderer(mlp, n_samples=128)`` renders the BASELINE volume
   workload: rays of a pinhole camera clipped to the reference's implicit
   [-1, 1]^3 box (rdv/shaders/libraries/math_library.h:48-57), 128 midpoint
@@ -39,27 +44,37 @@ class Cameras:
         if not isinstance(poses, RDVObject):
             poses = wrap(poses)
         assert poses.shape[1] == 9, "poses must be a [num_cameras, 9] tensor (ori | target | up)"
-        if jitter:
-            raise NotImplementedError("pixel jitter is not supported by this build")
         self.shape = [poses.shape[0], height, width]
         self.width, self.height = width, height
         self.poses = poses
         self.aspect_ratio = aspect_ratio
         self.fov = fov
-        self.pixel_jitter = 0
+        self.pixel_jitter = 1 if jitter else 0
+        self.last_seeds = None
 
     def __rshift__(self, m):
         """Camera grid composed with a Map[6, k] (e.g. RaymarchingTransmittance)."""
         return _CameraGrid(self, m)
 
-    def __call__(self) -> RDVObject:
+    def __call__(self, seeds=None) -> RDVObject:
         dev = current_device()
         poses = self.poses._tensor.to(device=dev, dtype=torch.float32).contiguous()
         out = torch.empty(self.shape + [6], dtype=torch.float32, device=dev)
         with _timed():
-            N.check(N.lib().rdvb_camera_rays(poses.data_ptr(), self.shape[0], self.width, self.height,
-                                             float(self.aspect_ratio), float(self.fov), out.data_ptr(),
-                                             stream_handle()), "rdvb_camera_rays")
+            if self.pixel_jitter:
+                from .volumes import _draw_seeds
+
+                seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
+                assert len(seeds) == 4, "seeds must be 4 integers"
+                self.last_seeds = seeds
+                N.check(N.lib().rdvb_camera_rays_jittered(
+                    poses.data_ptr(), self.shape[0], self.width, self.height, float(self.aspect_ratio),
+                    float(self.fov), N.uint32_array(seeds), out.data_ptr(), stream_handle()),
+                    "rdvb_camera_rays_jittered")
+            else:
+                N.check(N.lib().rdvb_camera_rays(poses.data_ptr(), self.shape[0], self.width, self.height,
+                                                 float(self.aspect_ratio), float(self.fov), out.data_ptr(),
+                                                 stream_handle()), "rdvb_camera_rays")
         return RDVObject(out)
 
 
@@ -72,8 +87,19 @@ class _CameraGrid:
         self.cameras = cameras
         self.map = m
 
-    def __call__(self) -> RDVObject:
-        return self.map(self.cameras())
+    def __call__(self, seeds=None) -> RDVObject:
+        """One dispatch of the composition. A node that draws random numbers
+        (RatiotrackingTransmittance) continues each pixel's generator after
+        the camera's draws, as the reference's single per-thread state does:
+        the same seeds, 2 draws already taken when the camera jitters."""
+        from .volumes import RatiotrackingTransmittance, _draw_seeds
+
+        if isinstance(self.map, RatiotrackingTransmittance):
+            seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
+            rays = self.cameras(seeds=seeds) if self.cameras.pixel_jitter else self.cameras()
+            return self.map(rays, seeds=seeds, draws_before=2 if self.cameras.pixel_jitter else 0)
+        rays = self.cameras(seeds=seeds) if self.cameras.pixel_jitter else self.cameras()
+        return self.map(rays)
 
 
 class VolumeRenderer:

@@ -174,7 +174,7 @@ class RatiotrackingTransmittance(RaymarchingTransmittance):
         self.majorant = _as_majorant_field(majorant)
         self.last_seeds = None
 
-    def __call__(self, rays, seeds=None):
+    def __call__(self, rays, seeds=None, draws_before: int = 0):
         dev = current_device()
         rt = rays._tensor if isinstance(rays, RDVObject) else wrap(rays)._tensor
         assert rt.shape[-1] == 6, f"input's last dimension ({rt.shape[-1]}) must match the map's IN (6)"
@@ -196,7 +196,8 @@ class RatiotrackingTransmittance(RaymarchingTransmittance):
         with _timed():
             N.check(N.lib().rdvb_transmittance_rt(
                 r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.density_scale, g.data_ptr(),
-                N.int_array(list(g.shape[:3])), N.uint32_array(seeds), n, N.int_array(st["dims"]),
+                N.int_array(list(g.shape[:3])), N.uint32_array(seeds), int(draws_before), n,
+                N.int_array(st["dims"]),
                 N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
                 N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
                 stream_handle()), "rdvb_transmittance_rt")

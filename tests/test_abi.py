@@ -29,7 +29,8 @@ def declared_functions():
 def test_header_declares_the_path(lib):
     names = declared_functions()
     for required in ["rdvb_mlp_forward", "rdvb_mlp_pack", "rdvb_conv3x3_winograd", "rdvb_winograd_filter_transform",
-                     "rdvb_raymarch_render", "rdvb_camera_rays", "rdvb_last_error", "rdvb_device_status"]:
+                     "rdvb_raymarch_render", "rdvb_camera_rays", "rdvb_camera_rays_jittered", "rdvb_last_error",
+                     "rdvb_device_status"]:
         assert required in names
 
 
@@ -81,21 +82,24 @@ def test_ratio_tracking_validation_before_any_device_work(lib):
 
     dims, flags = N.int_array([3, 16, 1]), N.int_array([1, 1])
     seeds = N.uint32_array([1, 2, 3, 4])
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 2, dims, None, None,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 0, 2, dims, None, None,
                                    flags, 0, None, 256, None, None)
     assert rc == -1 and "weights" in N.last_error()
     w = N.ptr_array([1, 1])
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 2, dims, w, w, flags,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 0, 2, dims, w, w, flags,
                                    0, None, 256, None, None)
     assert rc == -1 and "majorant_dims" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), None, 2, dims, w, w, flags,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), None, 0, 2, dims, w, w, flags,
                                    0, None, 256, None, None)
     assert rc == -1 and "seeds" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 2,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 0, 2,
                                    N.int_array([3, 16, 2]), w, w, flags, 0, None, 256, None, None)
     assert rc == -1 and "3 -> 1" in N.last_error()
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), seeds, -1, 2, dims, w, w, flags,
+                                   0, None, 256, None, None)
+    assert rc == -1 and "draws_before" in N.last_error()
     # nothing to do: no device needed
-    assert lib.rdvb_transmittance_rt(None, 0, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 2, dims, w, w, flags,
+    assert lib.rdvb_transmittance_rt(None, 0, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 0, 2, dims, w, w, flags,
                                      0, None, 256, None, None) == 0
 
 

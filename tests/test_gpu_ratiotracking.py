@@ -184,3 +184,45 @@ def test_empty_and_camera_composition(rdv, cuda_device):
     assert np.all(np.isfinite(v)) and (v < 1).any() and (v == 1).any()
     assert rdv.device_status() == 0
 
+
+
+def test_jittered_cameras_vs_oracle(rdv, cuda_device):
+    """Cameras(jitter=True) (cameras.h:7): each pixel's ray passes through
+    (column + r0, row + r1), the first two draws of the pixel's generator
+    (seeds spawned by the flat pixel index over all cameras)."""
+    poses = np.stack([orm.orbit_pose(0), orm.orbit_pose(3)]).astype(np.float32)
+    cams = rdv.Cameras(24, 16, torch.from_numpy(poses), jitter=True)
+    rays = cams(seeds=SEEDS).as_tensor("torch").cpu().numpy()
+    assert rays.shape == (2, 16, 24, 6)
+    centre = rdv.Cameras(24, 16, torch.from_numpy(poses))().as_tensor("torch").cpu().numpy()
+    for c in range(2):
+        o, w = orm.camera_rays(poses[c], 24, 16, jitter_seeds=SEEDS, camera_index=c)
+        np.testing.assert_allclose(rays[c].reshape(-1, 6)[:, :3], o, rtol=0, atol=1e-6)
+        np.testing.assert_allclose(rays[c].reshape(-1, 6)[:, 3:], w, rtol=0, atol=1e-5)
+    assert np.abs(rays[..., 3:] - centre[..., 3:]).max() > 1e-3          # off-centre
+    again = cams(seeds=SEEDS).as_tensor("torch").cpu().numpy()
+    assert np.array_equal(rays, again)
+    fresh = cams().as_tensor("torch").cpu().numpy()                       # new seeds per call
+    assert cams.last_seeds != SEEDS and not np.array_equal(rays, fresh)
+
+
+def test_jittered_cameras_composed_with_ratio_tracking(rdv, cuda_device):
+    """Cameras(jitter=True) >> RatiotrackingTransmittance: as in the
+    reference's single per-thread generator, ratio tracking continues each
+    pixel's sequence after the camera's two draws (draws_before = 2)."""
+    layers = _layers([3, 32, 1], "f32", seed=31)
+    grid = _majorant(layers, (2, 2, 2))
+    pose = orm.orbit_pose(1)
+    cams = rdv.Cameras(40, 30, torch.from_numpy(pose[None]), jitter=True)
+    node = rdv.RatiotrackingTransmittance(_chain(rdv, layers, cuda_device), torch.from_numpy(grid).to(cuda_device),
+                                          density_scale=1.2)
+    img = (cams >> node)(seeds=SEEDS).as_tensor("torch").cpu().numpy()
+    assert img.shape == (1, 30, 40, 1)
+    o, w = orm.camera_rays(pose, 40, 30, jitter_seeds=SEEDS)
+    ref = orm.ratiotracking_transmittance(o, w, 1.2, _extinction(layers), grid, SEEDS, draws_before=2)
+    got = img.reshape(-1)
+    _agree(got, ref)
+    # without the skip the estimates would be those of other random numbers
+    other = orm.ratiotracking_transmittance(o, w, 1.2, _extinction(layers), grid, SEEDS, draws_before=0)
+    assert np.mean(np.abs(got - other) > 1e-3) > 0.05
+    assert rdv.device_status() == 0
