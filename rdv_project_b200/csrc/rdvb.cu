@@ -56,6 +56,7 @@ struct DeviceInfo {
     size_t wino_smem_set[2] = {};
     size_t trm_smem_set = 0;
     size_t rt_smem_set = 0;
+    size_t rt_wide_smem_set = 0;
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
     size_t wino_tma_smem_set = 0;
@@ -1145,26 +1146,35 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
         off += (dims[l + 1] + 3) & ~3;
     }
     p.w_floats = off;
-    const size_t smem = static_cast<size_t>((off + 3) & ~3) * 4 + static_cast<size_t>(2 * p.maxw) * kThreads * 4;
+    // ratio tracking: 384 rays per CTA when their activation columns fit
+    // (chains at most 64 wide), 128 otherwise -- the per-ray activations
+    // bound how many warps an SM holds
+    const size_t w_bytes = static_cast<size_t>((off + 3) & ~3) * 4;
+    const bool wide = ratio_tracking &&
+                      w_bytes + static_cast<size_t>(2 * p.maxw) * kRtWideThreads * 4 <=
+                          static_cast<size_t>(dev->max_smem_optin);
+    const int threads = wide ? kRtWideThreads : kThreads;
+    const size_t smem = w_bytes + static_cast<size_t>(2 * p.maxw) * threads * 4;
     if (smem > static_cast<size_t>(dev->max_smem_optin))
         return fail(RDVB_ERR_UNSUPPORTED, "the extinction MLP needs %zu bytes of shared memory", smem);
-    auto kernel = ratio_tracking ? ratiotracking_kernel : transmittance_kernel;
-    size_t& smem_set = ratio_tracking ? dev->rt_smem_set : dev->trm_smem_set;
+    auto kernel = !ratio_tracking ? transmittance_kernel
+                                  : (wide ? ratiotracking_kernel<kRtWideThreads> : ratiotracking_kernel<kThreads>);
+    size_t& smem_set = !ratio_tracking ? dev->trm_smem_set : (wide ? dev->rt_wide_smem_set : dev->rt_smem_set);
     if (smem_set < smem) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(march): %s", cudaGetErrorString(e));
         smem_set = smem;
     }
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
     if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s",
                                       cudaGetErrorString(e));
     per_sm = std::max(per_sm, 1);
-    const long long want = (p.n_rays + kThreads - 1) / kThreads;
+    const long long want = (p.n_rays + threads - 1) / threads;
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * dev->sm_count * per_sm)));
     e = cudaMemsetAsync(workspace, 0, 16, st);
     if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    kernel<<<grid, kThreads, smem, st>>>(p);
+    kernel<<<grid, threads, smem, st>>>(p);
     return check_launch(ratio_tracking ? "ratiotracking_kernel" : "transmittance_kernel");
 }
 }  // namespace

@@ -35,7 +35,8 @@
 namespace rdvb {
 namespace trm {
 
-constexpr int kThreads = 128;    // rays in flight per CTA
+constexpr int kThreads = 128;    // rays in flight per CTA (transmittance_kernel)
+constexpr int kRtWideThreads = 384;  // ratiotracking_kernel when the chain is at most 64 wide
 constexpr int kMaxLayers = 8;
 constexpr int kMaxWidth = 128;
 constexpr int kSafety = 4096;    // raymarching_transmittance_trait.h:4
@@ -80,14 +81,14 @@ __device__ __forceinline__ float stage_val(float v, int math) {
 }
 
 // One chunk of CH outputs of layer L for this thread: acc over ascending k.
-template <int CH>
+template <int CH, int T = kThreads>
 __device__ __forceinline__ void chunk_eval(const Layer& L, const float* __restrict__ wsm, const float* __restrict__ bsm,
                                            const float* ain, int o0, float (&acc)[CH]) {
 #pragma unroll
     for (int j = 0; j < CH; ++j) acc[j] = (L.math == 0 && o0 + j < L.N) ? bsm[L.b_off + o0 + j] : 0.0f;
     const float* wb = wsm + L.w_off + o0 * L.K;  // block of outputs o0..o0+CH-1: [K][CH]
     for (int k = 0; k < L.K; ++k) {
-        const float a = ain[k * kThreads];
+        const float a = ain[k * T];
         const float4* wr = reinterpret_cast<const float4*>(wb + k * CH);
 #pragma unroll
         for (int j4 = 0; j4 < CH / 4; ++j4) {
@@ -102,7 +103,7 @@ __device__ __forceinline__ void chunk_eval(const Layer& L, const float* __restri
 
 // Finishes a chunk: bias after (staged layers), ReLU, staging for the next
 // layer's operands; writes outputs o0.. into aout (the thread's column).
-template <int CH>
+template <int CH, int T = kThreads>
 __device__ __forceinline__ void chunk_store(const Layer& L, const float* __restrict__ bsm, int next_math, int o0,
                                             const float (&acc)[CH], float* aout) {
 #pragma unroll
@@ -112,12 +113,14 @@ __device__ __forceinline__ void chunk_store(const Layer& L, const float* __restr
             float v = acc[j];
             if (L.math != 0) v += bsm[L.b_off + o];
             if (L.relu) v = fmaxf(v, 0.0f);
-            aout[o * kThreads] = stage_val(v, next_math);
+            aout[o * T] = stage_val(v, next_math);
         }
     }
 }
 
-// extinction(x) for this thread: the chain on the 3-vector x.
+// extinction(x) for this thread: the chain on the 3-vector x. T: threads of
+// the CTA, the stride of the [feature][thread] activation columns.
+template <int T = kThreads>
 __device__ __forceinline__ float extinction(const Params& p, const float* __restrict__ wsm,
                                             const float* __restrict__ bsm, float* act0, float* act1,
                                             const float (&x)[3]) {
@@ -126,7 +129,7 @@ __device__ __forceinline__ float extinction(const Params& p, const float* __rest
     for (int k = 0; k < 3; ++k) {
         float v = x[k];
         if (p.input_relu) v = fmaxf(v, 0.0f);
-        act0[k * kThreads] = stage_val(v, m0);
+        act0[k * T] = stage_val(v, m0);
     }
     float* ain = act0;
     float* aout = act1;
@@ -136,14 +139,14 @@ __device__ __forceinline__ float extinction(const Params& p, const float* __rest
         if (L.chunk == 4) {
             for (int o0 = 0; o0 < L.N; o0 += 4) {
                 float acc[4];
-                chunk_eval<4>(L, wsm, bsm, ain, o0, acc);
-                chunk_store<4>(L, bsm, next_math, o0, acc, aout);
+                chunk_eval<4, T>(L, wsm, bsm, ain, o0, acc);
+                chunk_store<4, T>(L, bsm, next_math, o0, acc, aout);
             }
         } else {
             for (int o0 = 0; o0 < L.N; o0 += 32) {
                 float acc[32];
-                chunk_eval<32>(L, wsm, bsm, ain, o0, acc);
-                chunk_store<32>(L, bsm, next_math, o0, acc, aout);
+                chunk_eval<32, T>(L, wsm, bsm, ain, o0, acc);
+                chunk_store<32, T>(L, bsm, next_math, o0, acc, aout);
             }
         }
         float* t = ain;
@@ -191,17 +194,18 @@ __device__ __forceinline__ bool march_entry(const float* __restrict__ r, const f
 // Stages every layer once into shared memory: block of outputs o0..o0+CH-1
 // as [K][CH], values rounded to the layer's operand format, zero beyond N;
 // then the biases.
+template <int T = kThreads>
 __device__ __forceinline__ void stage_chain(const Params& p, float* wsm) {
     for (int l = 0; l < p.n_layers; ++l) {
         const Layer L = p.layer[l];
         const int nb = (L.N + L.chunk - 1) / L.chunk;
-        for (int i = threadIdx.x; i < nb * L.chunk * L.K; i += kThreads) {
+        for (int i = threadIdx.x; i < nb * L.chunk * L.K; i += T) {
             const int blk = i / (L.chunk * L.K), rem = i - blk * L.chunk * L.K;
             const int k = rem / L.chunk, j = rem - k * L.chunk;
             const int o = blk * L.chunk + j;
             wsm[L.w_off + i] = o < L.N ? stage_val(L.W[static_cast<size_t>(o) * L.K + k], L.math) : 0.0f;
         }
-        for (int i = threadIdx.x; i < L.N; i += kThreads) wsm[L.b_off + i] = L.b[i];
+        for (int i = threadIdx.x; i < L.N; i += T) wsm[L.b_off + i] = L.b[i];
     }
     __syncthreads();
 }
@@ -313,12 +317,13 @@ constexpr int kRtSafety = 1024;  // ratiotracking_transmittance_trait.h's loop c
 // point and discard it), and applies the collision. The MLP -- nearly all of
 // the arithmetic -- thus runs with the lanes converged instead of once per
 // colliding lane.
-__global__ void __launch_bounds__(kThreads) ratiotracking_kernel(const __grid_constant__ Params p) {
+template <int NT>
+__global__ void __launch_bounds__(NT) ratiotracking_kernel(const __grid_constant__ Params p) {
     extern __shared__ float sm[];
     float* wsm = sm;
     float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
-    float* act1 = act0 + p.maxw * kThreads;
-    stage_chain(p, wsm);
+    float* act1 = act0 + p.maxw * NT;
+    stage_chain<NT>(p, wsm);
     const float* bsm = wsm;
     unsigned long long my_evals = 0;
     long long ray = -1;  // -1: take the next ray; -2: none left
@@ -368,7 +373,7 @@ __global__ void __launch_bounds__(kThreads) ratiotracking_kernel(const __grid_co
             pending = true;
         }
         if (!__any_sync(0xffffffffu, pending)) break;  // no lane has rays left
-        const float sigma = extinction(p, wsm, bsm, act0, act1, x);
+        const float sigma = extinction<NT>(p, wsm, bsm, act0, act1, x);
         if (pending) {
             ++my_evals;
             T = __fmul_rn(T, __fsub_rn(1.0f, __fdiv_rn(sigma, maj)));
