@@ -698,7 +698,7 @@ def run_reference_c34(args):
     print(json.dumps(line), flush=True)
 
 
-# ------------------------------- RaymarchingTransmittance
+# ------------------------------- RaymarchingTransmittance (the reference's absorption sensor)
 TRM = dict(width=1920, height=1080, dims=[3, 64, 64, 1], step=0.01, scale=1.0)
 
 

@@ -1,6 +1,7 @@
 """Regenerates the golden fixtures in this directory from the reference itself.
 
-Run in a checkout where the reference is present (default /root/reference):
+Run where the reference checkout is present (its path: RDV_REFERENCE_ROOT, else
+the default in oracle/_clib.py):
 
     python tests/golden/make_golden.py
 
