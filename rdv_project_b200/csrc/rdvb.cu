@@ -57,6 +57,7 @@ struct DeviceInfo {
     size_t trm_smem_set = 0;
     size_t rt_smem_set = 0;
     size_t rt_wide_smem_set = 0;
+    size_t rows_smem_set[2] = {0, 0};
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
     size_t wino_tma_smem_set = 0;
@@ -305,6 +306,75 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
     return check_launch("mlp_tc_kernel");
 }
 
+// The persistent rows kernel of the chain evaluator (transmittance.cuh) when
+// the chain fits it: at most 8 layers, widths <= 128, weights + activation
+// columns within shared memory. *taken = false otherwise.
+int launch_chain_rows(const void* x, int x_dtype, int64_t row_begin, int64_t row_end, int n_layers, const int* dims,
+                      const float* const* weights, const float* const* biases, const int* flags, bool force_f32,
+                      int input_relu, float* y, cudaStream_t stream, DeviceInfo* dev, bool* taken) {
+    using namespace rdvb::trm;
+    *taken = false;
+    if (const char* env = getenv("RDVB_SIMT_PERSISTENT"))
+        if (atoi(env) == 0) return RDVB_OK;
+    if (n_layers > kMaxLayers) return RDVB_OK;
+    int maxw = 0;
+    for (int l = 0; l <= n_layers; ++l) maxw = std::max(maxw, dims[l]);
+    if (maxw > kMaxWidth) return RDVB_OK;
+    for (int l = 0; l < n_layers; ++l)
+        if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "weights[%d]/biases[%d] is NULL", l, l);
+    Params p;
+    memset(&p, 0, sizeof(p));
+    int off = 0;
+    for (int l = 0; l < n_layers; ++l) {
+        Layer& L = p.layer[l];
+        L.W = weights[l];
+        L.b = biases[l];
+        L.K = dims[l];
+        L.N = dims[l + 1];
+        L.chunk = L.N <= 4 ? 4 : 32;
+        L.math = force_f32 ? 0 : (flags[l] & 3);
+        L.relu = (flags[l] & RDVB_LAYER_RELU) ? 1 : 0;
+        L.w_off = off;
+        off += ((L.N + L.chunk - 1) / L.chunk) * L.chunk * L.K;
+    }
+    for (int l = 0; l < n_layers; ++l) {
+        p.layer[l].b_off = off;
+        off += (dims[l + 1] + 3) & ~3;
+    }
+    p.w_floats = off;
+    p.n_layers = n_layers;
+    p.input_relu = input_relu ? 1 : 0;
+    p.maxw = maxw;
+    p.x = x;
+    p.x_dtype = x_dtype;
+    p.y = y;
+    p.row_begin = row_begin;
+    p.row_end = row_end;
+    const size_t w_bytes = static_cast<size_t>((off + 3) & ~3) * 4;
+    const size_t budget = static_cast<size_t>(dev->max_smem_optin);
+    const bool wide = w_bytes + static_cast<size_t>(2 * maxw) * 256 * 4 <= budget;
+    const int threads = wide ? 256 : kThreads;
+    const size_t smem = w_bytes + static_cast<size_t>(2 * maxw) * threads * 4;
+    if (smem > budget) return RDVB_OK;
+    auto kernel = wide ? chain_rows_kernel<256> : chain_rows_kernel<kThreads>;
+    size_t& smem_set = dev->rows_smem_set[wide ? 1 : 0];
+    if (smem_set < smem) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(chain_rows): %s", cudaGetErrorString(e));
+        smem_set = smem;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+    if (e != cudaSuccess)
+        return fail(RDVB_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s", cudaGetErrorString(e));
+    per_sm = std::max(per_sm, 1);
+    const long long want = (row_end - row_begin + threads - 1) / threads;
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * dev->sm_count * per_sm)));
+    kernel<<<grid, threads, smem, stream>>>(p);
+    *taken = true;
+    return check_launch("chain_rows_kernel");
+}
+
 int launch_mlp_simt(const void* x, int x_dtype, int64_t row_begin, int64_t row_end, int n_layers, const int* dims,
                     const float* const* weights, const float* const* biases, const int* flags, bool force_f32,
                     int input_relu, float* y, cudaStream_t stream, DeviceInfo* dev) {
@@ -332,6 +402,13 @@ int launch_mlp_simt(const void* x, int x_dtype, int64_t row_begin, int64_t row_e
         p.layer[l].N = dims[l + 1];
         p.layer[l].math = force_f32 ? 0 : (flags[l] & 3);
         p.layer[l].relu = (flags[l] & RDVB_LAYER_RELU) ? 1 : 0;
+    }
+    {
+        bool taken = false;
+        if (int rc = launch_chain_rows(x, x_dtype, row_begin, row_end, n_layers, dims, weights, biases, flags,
+                                       force_f32, input_relu, y, stream, dev, &taken))
+            return rc;
+        if (taken) return RDVB_OK;
     }
     const size_t smem = (2ull * maxw * kRows + static_cast<size_t>(maxw) * kOch) * sizeof(float);
     if (smem > static_cast<size_t>(dev->max_smem_optin))

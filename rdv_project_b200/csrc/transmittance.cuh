@@ -72,6 +72,11 @@ struct Params {
     float mvs[3];           // voxel sizes 2 / mdim (fp32 division, as the reference's vec3(2.0) / dim)
     unsigned seeds[4];      // the dispatch's generator seeds
     int draws_before;       // draws of each ray's generator already used upstream (a jittered camera: 2)
+    // chain_rows_kernel only
+    const void* x;          // [rows, IN] float32 / float16 / bfloat16
+    int x_dtype;            // 0 f32, 1 f16, 2 bf16
+    float* y;               // [rows, OUT]
+    long long row_begin, row_end;
 };
 
 __device__ __forceinline__ float stage_val(float v, int math) {
@@ -118,19 +123,12 @@ __device__ __forceinline__ void chunk_store(const Layer& L, const float* __restr
     }
 }
 
-// extinction(x) for this thread: the chain on the 3-vector x. T: threads of
-// the CTA, the stride of the [feature][thread] activation columns.
+// The chain on this thread's activation column act0 (the input, already
+// staged for layer 0); returns the column holding the last layer's outputs.
+// T: threads of the CTA, the stride of the [feature][thread] columns.
 template <int T = kThreads>
-__device__ __forceinline__ float extinction(const Params& p, const float* __restrict__ wsm,
-                                            const float* __restrict__ bsm, float* act0, float* act1,
-                                            const float (&x)[3]) {
-    const int m0 = p.layer[0].math;
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        float v = x[k];
-        if (p.input_relu) v = fmaxf(v, 0.0f);
-        act0[k * T] = stage_val(v, m0);
-    }
+__device__ __forceinline__ const float* eval_chain(const Params& p, const float* __restrict__ wsm,
+                                                   const float* __restrict__ bsm, float* act0, float* act1) {
     float* ain = act0;
     float* aout = act1;
     for (int l = 0; l < p.n_layers; ++l) {
@@ -153,7 +151,22 @@ __device__ __forceinline__ float extinction(const Params& p, const float* __rest
         ain = aout;
         aout = t;
     }
-    return ain[0];
+    return ain;
+}
+
+// extinction(x) for this thread: the chain on the 3-vector x.
+template <int T = kThreads>
+__device__ __forceinline__ float extinction(const Params& p, const float* __restrict__ wsm,
+                                            const float* __restrict__ bsm, float* act0, float* act1,
+                                            const float (&x)[3]) {
+    const int m0 = p.layer[0].math;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        float v = x[k];
+        if (p.input_relu) v = fmaxf(v, 0.0f);
+        act0[k * T] = stage_val(v, m0);
+    }
+    return eval_chain<T>(p, wsm, bsm, act0, act1)[0];
 }
 
 // raymarching_transmittance.h:4-19 for one ray r = (x, w): object space,
@@ -388,6 +401,46 @@ __global__ void __launch_bounds__(NT) ratiotracking_kernel(const __grid_constant
         }
     }
     if (my_evals) atomicAdd(p.evaluations, my_evals);
+}
+
+// ---------------------------------------------------------------------------
+// Rows mode of the same evaluator: the CUDA-core MLP (exact fp32 Linear
+// chains, chains that mix precisions, the fp32 tail rows of LinearFast
+// chains), y[row] = chain(x[row]) for row_begin <= row < row_end. Persistent
+// CTAs of NT rows stage the chain's weights into shared memory once and then
+// walk the rows; every thread evaluates its row in its own activation
+// column, so no barrier follows the staging. The arithmetic is that of
+// mlp_simt_kernel: bias first and FMAs in ascending k for exact layers,
+// staged operands with the bias after for LinearFast layers.
+template <int NT>
+__global__ void __launch_bounds__(NT) chain_rows_kernel(const __grid_constant__ Params p) {
+    extern __shared__ float sm[];
+    float* wsm = sm;
+    float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
+    float* act1 = act0 + p.maxw * NT;
+    stage_chain<NT>(p, wsm);
+    const float* bsm = wsm;
+    const int in0 = p.layer[0].K, m0 = p.layer[0].math;
+    const int outd = p.layer[p.n_layers - 1].N;
+    for (long long base = p.row_begin + static_cast<long long>(blockIdx.x) * NT; base < p.row_end;
+         base += static_cast<long long>(gridDim.x) * NT) {
+        const long long row = base + threadIdx.x;
+        const bool valid = row < p.row_end;
+        for (int k = 0; k < in0; ++k) {
+            float v = 0.0f;
+            if (valid) {
+                const long long i = row * in0 + k;
+                if (p.x_dtype == 0) v = static_cast<const float*>(p.x)[i];
+                else if (p.x_dtype == 1) v = __half2float(static_cast<const __half*>(p.x)[i]);
+                else v = __bfloat162float(static_cast<const __nv_bfloat16*>(p.x)[i]);
+                if (p.input_relu) v = fmaxf(v, 0.0f);
+            }
+            act0[k * NT] = stage_val(v, m0);
+        }
+        const float* out = eval_chain<NT>(p, wsm, bsm, act0, act1);
+        if (valid)
+            for (int o = 0; o < outd; ++o) p.y[row * outd + o] = out[o * NT];
+    }
 }
 
 // ---------------------------------------------------------------------------
