@@ -57,7 +57,7 @@ struct DeviceInfo {
     size_t trm_smem_set = 0;
     size_t rt_smem_set = 0;
     size_t rt_wide_smem_set = 0;
-    size_t rows_smem_set[2] = {0, 0};
+    size_t rows_smem_set = 0;
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
     size_t wino_tma_smem_set = 0;
@@ -352,16 +352,16 @@ int launch_chain_rows(const void* x, int x_dtype, int64_t row_begin, int64_t row
     p.row_end = row_end;
     const size_t w_bytes = static_cast<size_t>((off + 3) & ~3) * 4;
     const size_t budget = static_cast<size_t>(dev->max_smem_optin);
-    const bool wide = w_bytes + static_cast<size_t>(2 * maxw) * 256 * 4 <= budget;
-    const int threads = wide ? 256 : kThreads;
+    // 128-row CTAs, several per SM where shared memory allows: on a 262,144-row
+    // 3-64-64-64-4 chain they beat one 256-row CTA per SM and two rows per thread.
+    const int threads = kThreads;
     const size_t smem = w_bytes + static_cast<size_t>(2 * maxw) * threads * 4;
     if (smem > budget) return RDVB_OK;
-    auto kernel = wide ? chain_rows_kernel<256> : chain_rows_kernel<kThreads>;
-    size_t& smem_set = dev->rows_smem_set[wide ? 1 : 0];
-    if (smem_set < smem) {
+    auto kernel = chain_rows_kernel<kThreads>;
+    if (dev->rows_smem_set < smem) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(chain_rows): %s", cudaGetErrorString(e));
-        smem_set = smem;
+        dev->rows_smem_set = smem;
     }
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
