@@ -95,13 +95,15 @@ __device__ __forceinline__ void chunk_eval(const Layer& L, const float* __restri
     for (int k = 0; k < L.K; ++k) {
         const float a = ain[k * T];
         const float4* wr = reinterpret_cast<const float4*>(wb + k * CH);
+        float4 wk[CH / 4];  // the step's operands first, then its FMAs
+#pragma unroll
+        for (int j4 = 0; j4 < CH / 4; ++j4) wk[j4] = wr[j4];
 #pragma unroll
         for (int j4 = 0; j4 < CH / 4; ++j4) {
-            const float4 w = wr[j4];
-            acc[4 * j4 + 0] = fmaf(a, w.x, acc[4 * j4 + 0]);
-            acc[4 * j4 + 1] = fmaf(a, w.y, acc[4 * j4 + 1]);
-            acc[4 * j4 + 2] = fmaf(a, w.z, acc[4 * j4 + 2]);
-            acc[4 * j4 + 3] = fmaf(a, w.w, acc[4 * j4 + 3]);
+            acc[4 * j4 + 0] = fmaf(a, wk[j4].x, acc[4 * j4 + 0]);
+            acc[4 * j4 + 1] = fmaf(a, wk[j4].y, acc[4 * j4 + 1]);
+            acc[4 * j4 + 2] = fmaf(a, wk[j4].z, acc[4 * j4 + 2]);
+            acc[4 * j4 + 3] = fmaf(a, wk[j4].w, acc[4 * j4 + 3]);
         }
     }
 }
