@@ -44,17 +44,28 @@ def _dev_f32(t) -> torch.Tensor:
     return t.to(device=current_device(), dtype=torch.float32).contiguous()
 
 
-def _filter_transform(w33io: torch.Tensor, cin: int, cout: int, plain: bool, packed: bool):
+_VARIANTS = {"F2x2": (N.RDVB_WINOGRAD_F2X2, 16), "F4x4": (N.RDVB_WINOGRAD_F4X4, 36)}
+
+
+def _variant(name: str) -> int:
+    if name not in _VARIANTS:
+        raise ValueError(f"Winograd variant must be one of {sorted(_VARIANTS)} (got {name!r})")
+    return _VARIANTS[name][0]
+
+
+def _filter_transform(w33io: torch.Tensor, cin: int, cout: int, plain: bool, packed: bool, variant: str = "F2x2"):
     lib = N.lib()
-    u_plain = torch.empty(16 * cin * cout, dtype=torch.float16, device=w33io.device) if plain else None
+    code = _variant(variant)
+    positions = _VARIANTS[variant][1]
+    u_plain = torch.empty(positions * cin * cout, dtype=torch.float16, device=w33io.device) if plain else None
     u_packed = None
     if packed:
-        nbytes = lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F2X2, cin, cout)
+        nbytes = lib.rdvb_winograd_packed_bytes(code, cin, cout)
         if nbytes <= 0:
-            raise N.RdvbError(f"no packed Winograd operand for cin={cin}, cout={cout}")
+            raise N.RdvbError(f"no packed Winograd {variant} operand for cin={cin}, cout={cout}")
         u_packed = torch.empty(int(nbytes), dtype=torch.uint8, device=w33io.device)
     N.check(lib.rdvb_winograd_filter_transform(
-        w33io.data_ptr(), cin, cout, N.RDVB_WINOGRAD_F2X2,
+        w33io.data_ptr(), cin, cout, code,
         u_plain.data_ptr() if plain else None, u_packed.data_ptr() if packed else None, stream_handle()),
         "rdvb_winograd_filter_transform")
     return u_plain, u_packed
@@ -70,9 +81,9 @@ def _winograd_transform_weight(weight, in_channels: int, out_channels: int) -> t
 
 
 def _launch_winograd(x: torch.Tensor, n: int, h: int, w: int, cin: int, cout: int, u_packed: torch.Tensor,
-                     bias, y: torch.Tensor) -> None:
+                     bias, y: torch.Tensor, variant: str = "F2x2") -> None:
     N.check(N.lib().rdvb_conv3x3_winograd(
-        x.data_ptr(), _DTYPES[x.dtype], n, h, w, cin, cout, u_packed.data_ptr(), N.RDVB_WINOGRAD_F2X2,
+        x.data_ptr(), _DTYPES[x.dtype], n, h, w, cin, cout, u_packed.data_ptr(), _variant(variant),
         bias.data_ptr() if bias is not None else None, y.data_ptr(), _DTYPES[y.dtype], stream_handle()),
         "rdvb_conv3x3_winograd")
 
@@ -303,19 +314,26 @@ class Conv2DTensorOpWinograd3x3(TensorOperation):
 
 
 class Conv3x3Winograd:
-    """Batched NHWC 'same' 3x3 convolution via the fused Winograd F(2x2,3x3)
-    kernel: ``Conv3x3Winograd(weight[3,3,CIN,COUT], bias[COUT] | None)``,
+    """Batched NHWC 'same' 3x3 convolution via Winograd:
+    ``Conv3x3Winograd(weight[3,3,CIN,COUT], bias[COUT] | None, variant="F2x2")``,
     then ``conv(x[N,H,W,CIN], out_dtype=torch.float32, out=None)``. x may
-    be float32 or float16; channels are multiples of 16 up to 64."""
+    be float32 or float16.
 
-    def __init__(self, weight, bias=None) -> None:
+    variant "F2x2": the fused tcgen05 kernel, channels multiples of 16 up to
+    64 (the reference operator's transform). variant "F4x4": F(4x4,3x3) on
+    CUDA cores, channels 1..128 (a B200 extension; with float16 staging its
+    error against the direct convolution is ~6x that of F(2x2))."""
+
+    def __init__(self, weight, bias=None, variant: str = "F2x2") -> None:
         w = _dev_f32(weight)
         assert w.dim() == 4 and tuple(w.shape[:2]) == (3, 3), "weight must be [3, 3, in_channels, out_channels]"
         self.cin, self.cout = int(w.shape[2]), int(w.shape[3])
+        _variant(variant)
+        self.variant = variant
         self.bias = _dev_f32(bias) if bias is not None else None
         if self.bias is not None:
             assert tuple(self.bias.shape) == (self.cout,), "bias must be [out_channels]"
-        _, self.u_packed = _filter_transform(w, self.cin, self.cout, plain=False, packed=True)
+        _, self.u_packed = _filter_transform(w, self.cin, self.cout, plain=False, packed=True, variant=variant)
 
     def __call__(self, x, out_dtype=torch.float32, out: torch.Tensor | None = None) -> torch.Tensor:
         x = x._tensor if isinstance(x, RDVObject) else x
@@ -328,7 +346,7 @@ class Conv3x3Winograd:
             out = torch.empty((n, h, w, self.cout), dtype=out_dtype, device=x.device)
         assert out.shape == (n, h, w, self.cout) and out.dtype in _DTYPES and out.is_contiguous()
         with _timed():
-            _launch_winograd(x, n, h, w, self.cin, self.cout, self.u_packed, self.bias, out)
+            _launch_winograd(x, n, h, w, self.cin, self.cout, self.u_packed, self.bias, out, self.variant)
         return out
 
 

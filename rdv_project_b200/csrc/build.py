@@ -18,7 +18,7 @@ ROOT = os.path.dirname(PKG)
 LIB_DIR = os.path.join(PKG, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "librdvb.so")
 SOURCES = ["rdvb.cu"]
-HEADERS = ["ptx.cuh", "rng.cuh", "mlp_tc.cuh", "mlp_simt.cuh", "winograd.cuh", "raymarch.cuh", "transmittance.cuh",
+HEADERS = ["ptx.cuh", "rng.cuh", "mlp_tc.cuh", "mlp_simt.cuh", "winograd.cuh", "winograd_f43.cuh", "raymarch.cuh", "transmittance.cuh",
            "resample.cuh", "conv_tc.cuh", "sampler.cuh"]
 
 

@@ -19,6 +19,7 @@
 #include "mlp_tc.cuh"
 #include "mlp_simt.cuh"
 #include "winograd.cuh"
+#include "winograd_f43.cuh"
 #include "raymarch.cuh"
 #include "transmittance.cuh"
 #include "resample.cuh"
@@ -61,6 +62,7 @@ struct DeviceInfo {
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
     size_t wino_tma_smem_set = 0;
+    size_t wino43_smem_set[2] = {};
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
@@ -563,22 +565,99 @@ bool wino_channels_ok(int cin, int cout) {
            cout <= kMaxChannels;
 }
 
+bool wino43_channels_ok(int cin, int cout) {
+    using rdvb::wino43::kMaxChannels;
+    return cin >= 1 && cout >= 1 && cin <= kMaxChannels && cout <= kMaxChannels;
+}
+
+// F(4x4,3x3) on CUDA cores (winograd_f43.cuh); arguments validated by the caller
+// except the variant-specific ones.
+int conv3x3_winograd_f43(const void* x, int x_dtype, int n, int h, int w, int cin, int cout, const void* u,
+                         const float* bias, void* y, int y_dtype, cudaStream_t stream) {
+    using namespace rdvb::wino43;
+    if (!wino43_channels_ok(cin, cout))
+        return fail(RDVB_ERR_UNSUPPORTED, "F4X4 needs cin, cout in [1, %d] (got %d, %d)", kMaxChannels, cin, cout);
+    if (n == 0 || h == 0 || w == 0) return RDVB_OK;
+    if (!x || !y || !u) return fail(RDVB_ERR_INVALID_ARG, "x, y and u_packed must not be NULL");
+    const uintptr_t xa = x_dtype == RDVB_F16 ? 2 : 4, ya = y_dtype == RDVB_F16 ? 2 : 4;
+    if (!aligned(x, xa) || !aligned(y, ya) || !aligned(u, 2) || (bias && !aligned(bias, 4)))
+        return fail(RDVB_ERR_INVALID_ARG, "x, y, u_packed and bias must be aligned to their element size");
+    const long long tiles_h = (h + kM - 1) / kM, tiles_w = (w + kM - 1) / kM;
+    if (tiles_h * tiles_w > 0x7fffffffLL) return fail(RDVB_ERR_UNSUPPORTED, "image too large (%d x %d)", h, w);
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.x = x;
+    p.y = y;
+    p.u = static_cast<const __half*>(u);
+    p.bias = bias;
+    p.h = h;
+    p.w = w;
+    p.cin = cin;
+    p.cout = cout;
+    p.y_f16 = y_dtype == RDVB_F16 ? 1 : 0;
+    p.tiles_w = static_cast<int>(tiles_w);
+    p.tiles_per_img = static_cast<int>(tiles_h * tiles_w);
+    p.n_tiles = static_cast<long long>(n) * p.tiles_per_img;
+    const size_t smem = static_cast<size_t>(kBlockTiles) * kPos * cin * sizeof(__half);
+    const int xi = x_dtype == RDVB_F16 ? 1 : 0;
+    auto kernel = xi ? winograd_f43_kernel<true> : winograd_f43_kernel<false>;
+    if (dev->wino43_smem_set[xi] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(winograd_f43): %s", cudaGetErrorString(e));
+        dev->wino43_smem_set[xi] = smem;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
+    if (e != cudaSuccess)
+        return fail(RDVB_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s", cudaGetErrorString(e));
+    const long long blocks = (p.n_tiles + kBlockTiles - 1) / kBlockTiles;
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(blocks, 1LL * dev->sm_count * std::max(per_sm, 1))));
+    kernel<<<grid, kThreads, smem, stream>>>(p);
+    return check_launch("winograd_f43_kernel");
+}
+
 }  // namespace
 
 extern "C" {
 
 int64_t rdvb_winograd_packed_bytes(int variant, int cin, int cout) {
+    if (variant == RDVB_WINOGRAD_F4X4)
+        return wino43_channels_ok(cin, cout) ? 36LL * cin * cout * static_cast<int64_t>(sizeof(__half)) : 0;
     if (variant != RDVB_WINOGRAD_F2X2 || !wino_channels_ok(cin, cout)) return 0;
     return 16LL * cout * 128;
 }
 
 int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int variant, void* u_plain,
                                    void* u_packed, void* stream) {
-    if (variant == RDVB_WINOGRAD_F4X4)
-        return fail(RDVB_ERR_UNSUPPORTED, "RDVB_WINOGRAD_F4X4 is not implemented; use RDVB_WINOGRAD_F2X2");
-    if (variant != RDVB_WINOGRAD_F2X2) return fail(RDVB_ERR_INVALID_ARG, "unknown Winograd variant %d", variant);
+    if (variant != RDVB_WINOGRAD_F2X2 && variant != RDVB_WINOGRAD_F4X4)
+        return fail(RDVB_ERR_INVALID_ARG, "unknown Winograd variant %d", variant);
     if (cin < 1 || cout < 1) return fail(RDVB_ERR_INVALID_ARG, "cin (%d) and cout (%d) must be positive", cin, cout);
     if (!w_33io) return fail(RDVB_ERR_INVALID_ARG, "w_33io must not be NULL");
+    if (variant == RDVB_WINOGRAD_F4X4) {
+        // the packed operand of F(4x4) is the plain [36][cin][cout] float16 array
+        if (!wino43_channels_ok(cin, cout))
+            return fail(RDVB_ERR_UNSUPPORTED, "F4X4 needs cin, cout in [1, %d] (got %d, %d)",
+                        rdvb::wino43::kMaxChannels, cin, cout);
+        if ((u_plain && !aligned(u_plain, 2)) || (u_packed && !aligned(u_packed, 2)))
+            return fail(RDVB_ERR_INVALID_ARG, "u_plain and u_packed must be 2-byte aligned");
+        if (!u_plain && !u_packed) return RDVB_OK;
+        DeviceInfo* dev = nullptr;
+        if (int rc = current_device(&dev)) return rc;
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const long long total = static_cast<long long>(cin) * cout;
+        const int threads = 256;
+        const int blocks = static_cast<int>(std::max<long long>(
+            1, std::min<long long>((total + threads - 1) / threads, 4LL * dev->sm_count)));
+        for (void* dst : {u_plain, u_packed}) {
+            if (!dst) continue;
+            rdvb::wino43::winograd_f43_filter_kernel<<<blocks, threads, 0, st>>>(w_33io, cin, cout,
+                                                                                 static_cast<__half*>(dst));
+            if (int rc = check_launch("winograd_f43_filter_kernel")) return rc;
+        }
+        return RDVB_OK;
+    }
     if (u_packed) {
         if (!wino_channels_ok(cin, cout))
             return fail(RDVB_ERR_UNSUPPORTED, "packed operand needs cin, cout multiples of 16 in [16, %d] (got %d, %d)",
@@ -629,14 +708,16 @@ int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int c
                           const void* u_packed, int variant, const float* bias, void* y, int y_dtype,
                           void* stream) {
     using namespace rdvb::wino;
-    if (variant == RDVB_WINOGRAD_F4X4)
-        return fail(RDVB_ERR_UNSUPPORTED, "RDVB_WINOGRAD_F4X4 is not implemented; use RDVB_WINOGRAD_F2X2");
-    if (variant != RDVB_WINOGRAD_F2X2) return fail(RDVB_ERR_INVALID_ARG, "unknown Winograd variant %d", variant);
+    if (variant != RDVB_WINOGRAD_F2X2 && variant != RDVB_WINOGRAD_F4X4)
+        return fail(RDVB_ERR_INVALID_ARG, "unknown Winograd variant %d", variant);
     if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16)
         return fail(RDVB_ERR_INVALID_ARG, "x_dtype must be RDVB_F32 or RDVB_F16");
     if (y_dtype != RDVB_F32 && y_dtype != RDVB_F16)
         return fail(RDVB_ERR_INVALID_ARG, "y_dtype must be RDVB_F32 or RDVB_F16");
     if (n < 0 || h < 0 || w < 0) return fail(RDVB_ERR_INVALID_ARG, "n, h, w must be >= 0");
+    if (variant == RDVB_WINOGRAD_F4X4)
+        return conv3x3_winograd_f43(x, x_dtype, n, h, w, cin, cout, u_packed, bias, y, y_dtype,
+                                    static_cast<cudaStream_t>(stream));
     if (!wino_channels_ok(cin, cout))
         return fail(RDVB_ERR_UNSUPPORTED, "cin, cout must be multiples of 16 in [16, %d] (got %d, %d)", kMaxChannels,
                     cin, cout);

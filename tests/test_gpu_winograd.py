@@ -177,7 +177,7 @@ def test_errors_and_empty(rdv, cuda_device):
     lib = N.lib()
     assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F2X2, 64, 64) == 16 * 64 * 128
     assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F2X2, 80, 64) == 0
-    assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F4X4, 64, 64) == 0
+    assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F4X4, 64, 64) == 36 * 64 * 64 * 2
     dummy = torch.zeros(1 << 16, device=cuda_device)
     # n = 0: nothing to do, no launch
     before = N.launch_count()
@@ -185,8 +185,8 @@ def test_errors_and_empty(rdv, cuda_device):
                                       N.RDVB_WINOGRAD_F2X2, None, dummy.data_ptr(), N.RDVB_F32, None), "empty")
     assert N.launch_count() == before
     rc = lib.rdvb_conv3x3_winograd(dummy.data_ptr(), N.RDVB_F32, 1, 8, 8, 16, 16, dummy.data_ptr(),
-                                   N.RDVB_WINOGRAD_F4X4, None, dummy.data_ptr(), N.RDVB_F32, None)
-    assert rc == -2 and "F4X4" in N.last_error()
+                                   7, None, dummy.data_ptr(), N.RDVB_F32, None)
+    assert rc == -1 and "variant" in N.last_error()
     rc = lib.rdvb_conv3x3_winograd(dummy.data_ptr(), N.RDVB_F32, 1, 8, 8, 24, 16, dummy.data_ptr(),
                                    N.RDVB_WINOGRAD_F2X2, None, dummy.data_ptr(), N.RDVB_F32, None)
     assert rc == -2 and "multiples of 16" in N.last_error()
