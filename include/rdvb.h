@@ -155,8 +155,10 @@ int64_t rdvb_winograd_packed_bytes(int variant, int cin, int cout);
  *  u_packed  optional (may be NULL): the tensor-core operand consumed by
  *            rdvb_conv3x3_winograd, rdvb_winograd_packed_bytes() bytes,
  *            256-byte aligned; requires cin, cout multiples of 16, <= 64
- * Only RDVB_WINOGRAD_F2X2 is implemented; RDVB_WINOGRAD_F4X4 returns
- * RDVB_ERR_UNSUPPORTED. */
+ * RDVB_WINOGRAD_F4X4 (a B200 extension): U = G g G^T with the 6x3 Toom-Cook
+ * G of the points {0, 1, -1, 2, -1/2, inf}; u_plain and u_packed are both
+ * the plain float16 array [36][cin][cout] (2-byte aligned), cin and cout in
+ * [1, 128]. */
 int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int variant, void* u_plain,
                                    void* u_packed, void* stream);
 
@@ -167,7 +169,10 @@ int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int v
  *  u_packed  rdvb_winograd_filter_transform output for these channels
  *  bias      [cout] fp32, or NULL for zero
  *  y_dtype   RDVB_F32 (the reference's output type) or RDVB_F16
- *            (y 16-byte aligned) */
+ *            (y 16-byte aligned)
+ * variant RDVB_WINOGRAD_F4X4: the same recipe with 6x6 transforms and the 36
+ * per-position reductions on CUDA cores (fp32), one fused kernel; cin, cout
+ * in [1, 128]; x, y aligned to their element size. */
 int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int cin, int cout,
                           const void* u_packed, int variant, const float* bias, void* y, int y_dtype,
                           void* stream);
