@@ -600,7 +600,9 @@ int conv3x3_winograd_f43(const void* x, int x_dtype, int n, int h, int w, int ci
     p.tiles_w = static_cast<int>(tiles_w);
     p.tiles_per_img = static_cast<int>(tiles_h * tiles_w);
     p.n_tiles = static_cast<long long>(n) * p.tiles_per_img;
-    const size_t smem = static_cast<size_t>(kBlockTiles) * kPos * cin * sizeof(__half);
+    const size_t smem = smem_bytes(cin, cout);
+    if (smem > static_cast<size_t>(dev->max_smem_optin))
+        return fail(RDVB_ERR_UNSUPPORTED, "F4X4 kernel needs %zu bytes of shared memory", smem);
     const int xi = x_dtype == RDVB_F16 ? 1 : 0;
     auto kernel = xi ? winograd_f43_kernel<true> : winograd_f43_kernel<false>;
     if (dev->wino43_smem_set[xi] < smem) {

@@ -19,13 +19,19 @@
 // outside the image); partial tiles at the bottom/right edges store only
 // their in-image outputs.
 //
-// winograd_f43_kernel: persistent CTAs of 256 threads walk blocks of 16
-// tiles. Phase 1, items (tile, ci): the 6x6 patch is loaded (consecutive
-// threads read consecutive channels) and transformed, V written float16 to
-// shared memory [tile][36][cin]. Phase 2, items (tile, co): 36 fp32
-// accumulators over ci (V broadcast from shared memory, U coalesced over co
-// from global memory / L2), then the inverse transform, bias and the store
-// (coalesced over co). Two block barriers per block of tiles.
+// winograd_f43_kernel: persistent CTAs of 256 threads walk blocks of 8
+// tiles, three phases per block separated by block barriers:
+//   1. items (tile, ci): the 6x6 patch is loaded (consecutive threads read
+//      consecutive channels) and transformed; V is written float16 to shared
+//      memory as [36][cin][8 tiles], so one 16-byte load gives a (position,
+//      channel)'s V for all 8 tiles;
+//   2. items (position q, output-channel pair): 8 tiles x 2 channels of fp32
+//      accumulators over ascending ci -- per ci one 16-byte V load and two
+//      float16 U loads (coalesced over output channels, from L2) feed 16
+//      FMAs; M written to shared memory as [36][8 tiles][cout] fp32;
+//   3. items (tile, co): the 36 M values, the inverse transform, bias and the
+//      store (coalesced over co).
+// Shared memory: 576 cin + 1152 cout bytes (221,184 at 128/128 channels).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -37,7 +43,7 @@ namespace wino43 {
 constexpr int kA = 6;             // transform size m + r - 1
 constexpr int kM = 4;             // output tile size
 constexpr int kPos = kA * kA;     // 36 transform positions
-constexpr int kBlockTiles = 16;   // tiles per block of a CTA
+constexpr int kBlockTiles = 8;    // tiles per block of a CTA (one 16-byte V load)
 constexpr int kThreads = 256;
 constexpr int kMaxChannels = 128;
 
@@ -103,10 +109,19 @@ __device__ __forceinline__ float load_x(const void* x, long long i) {
     else return static_cast<const float*>(x)[i];
 }
 
+// Shared-memory bytes of winograd_f43_kernel for (cin, cout).
+inline size_t smem_bytes(int cin, int cout) {
+    return static_cast<size_t>(kPos) * kBlockTiles * (static_cast<size_t>(cin) * sizeof(__half) +
+                                                      static_cast<size_t>(cout) * sizeof(float));
+}
+
 template <bool XF16>
 __global__ void __launch_bounds__(kThreads) winograd_f43_kernel(const __grid_constant__ Params p) {
-    extern __shared__ __half vsm[];  // [kBlockTiles][36][cin]
+    extern __shared__ __align__(16) unsigned char smem_raw[];
     const int cin = p.cin, cout = p.cout;
+    __half* vsm = reinterpret_cast<__half*>(smem_raw);  // [36][cin][kBlockTiles]
+    float* msm = reinterpret_cast<float*>(smem_raw + static_cast<size_t>(kPos) * cin * kBlockTiles * sizeof(__half));
+    const int n_pairs = (cout + 1) / 2;
     for (long long t0 = static_cast<long long>(blockIdx.x) * kBlockTiles; t0 < p.n_tiles;
          t0 += static_cast<long long>(gridDim.x) * kBlockTiles) {
         // Phase 1: V = B^T d B of (tile, ci), staged float16.
@@ -146,7 +161,7 @@ __global__ void __launch_bounds__(kThreads) winograd_f43_kernel(const __grid_con
                         if (kBT[a][r] != 0.0f) s = fmaf(kBT[a][r], d[r][c], s);
                     t[a][c] = s;
                 }
-            __half* vt = vsm + static_cast<size_t>(tl) * kPos * cin + ci;
+            __half* vt = vsm + static_cast<size_t>(ci) * kBlockTiles + tl;
 #pragma unroll
             for (int a = 0; a < kA; ++a)
 #pragma unroll
@@ -155,26 +170,49 @@ __global__ void __launch_bounds__(kThreads) winograd_f43_kernel(const __grid_con
 #pragma unroll
                     for (int c = 0; c < kA; ++c)
                         if (kBT[b][c] != 0.0f) s = fmaf(t[a][c], kBT[b][c], s);
-                    vt[(a * kA + b) * cin] = __float2half_rn(s);
+                    vt[static_cast<size_t>(a * kA + b) * cin * kBlockTiles] = __float2half_rn(s);
                 }
         }
         __syncthreads();
-        // Phase 2: M = sum over ci of V * U per position, Y = A^T M A + bias.
+        // Phase 2: M[q][tile][co] = sum over ascending ci of V * U.
+        for (int it = threadIdx.x; it < kPos * n_pairs; it += kThreads) {
+            const int q = it / n_pairs, co = 2 * (it - q * n_pairs);
+            const bool two = co + 1 < cout;
+            float acc[kBlockTiles][2];
+#pragma unroll
+            for (int t = 0; t < kBlockTiles; ++t) acc[t][0] = acc[t][1] = 0.0f;
+            const uint4* vq = reinterpret_cast<const uint4*>(vsm + static_cast<size_t>(q) * cin * kBlockTiles);
+            const __half* uq = p.u + static_cast<size_t>(q) * cin * cout + co;
+            for (int ci = 0; ci < cin; ++ci) {
+                const uint4 vv = vq[ci];
+                const float u0 = __half2float(uq[static_cast<size_t>(ci) * cout]);
+                const float u1 = two ? __half2float(uq[static_cast<size_t>(ci) * cout + 1]) : 0.0f;
+                const __half2* vh = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+                for (int t2 = 0; t2 < kBlockTiles / 2; ++t2) {
+                    const float2 f = __half22float2(vh[t2]);
+                    acc[2 * t2][0] = fmaf(f.x, u0, acc[2 * t2][0]);
+                    acc[2 * t2][1] = fmaf(f.x, u1, acc[2 * t2][1]);
+                    acc[2 * t2 + 1][0] = fmaf(f.y, u0, acc[2 * t2 + 1][0]);
+                    acc[2 * t2 + 1][1] = fmaf(f.y, u1, acc[2 * t2 + 1][1]);
+                }
+            }
+            float* mq = msm + static_cast<size_t>(q) * kBlockTiles * cout + co;
+#pragma unroll
+            for (int t = 0; t < kBlockTiles; ++t) {
+                mq[static_cast<size_t>(t) * cout] = acc[t][0];
+                if (two) mq[static_cast<size_t>(t) * cout + 1] = acc[t][1];
+            }
+        }
+        __syncthreads();
+        // Phase 3: Y = A^T M A + bias for (tile, co).
         for (int it = threadIdx.x; it < kBlockTiles * cout; it += kThreads) {
             const int tl = it / cout, co = it - tl * cout;
             const long long tile = t0 + tl;
             if (tile >= p.n_tiles) continue;
             float m[kPos];
 #pragma unroll
-            for (int q = 0; q < kPos; ++q) m[q] = 0.0f;
-            const __half* vt = vsm + static_cast<size_t>(tl) * kPos * cin;
-            const __half* ut = p.u + co;
-            for (int ci = 0; ci < cin; ++ci) {
-#pragma unroll
-                for (int q = 0; q < kPos; ++q)
-                    m[q] = fmaf(__half2float(vt[q * cin + ci]),
-                                __half2float(ut[(static_cast<size_t>(q) * cin + ci) * cout]), m[q]);
-            }
+            for (int q = 0; q < kPos; ++q) m[q] = msm[(static_cast<size_t>(q) * kBlockTiles + tl) * cout + co];
             float s[kM][kA];  // A^T M
 #pragma unroll
             for (int i = 0; i < kM; ++i)
