@@ -98,7 +98,7 @@ def test_f4x4_matches_oracle(rdv, cuda_device, cin, cout, xdt, shape):
 
 
 def test_f4x4_many_blocks_per_cta_and_f16_output(rdv, cuda_device):
-    # 8 * 32 * 32 = 8192 tiles = 512 blocks of 16: more than one block per CTA
+    # 8 * 32 * 32 = 8192 tiles = 1024 blocks of 8: several blocks per CTA
     rng = np.random.default_rng(5)
     x = rng.standard_normal((8, 128, 128, 16)).astype(np.float16).astype(np.float32)
     w, b = _weights(rng, 16, 16)
