@@ -261,8 +261,6 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
 
     int rc = RDVB_OK;
     const int ri = ray ? (ray->march ? kModeMarch : kModeRender) : kModeRows;
-    // two MMA-issuing warps when the weights are resident (the slots are then
-    // independent); one in-order issuer for streamed weights
     // MMA-issuing warps: with resident weights the slots are independent --
     // one issuer per slot for 4 slots (an issuer never waits on a slot that
     // is behind while another is ready), two for 2 slots; one in-order issuer
