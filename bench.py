@@ -1,30 +1,37 @@
 """Benchmark of the rdv hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c1|c5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c5|c2|c1|c3|c4|trm]
 
-Default workload (the one the headline metric is quoted
-on): fp16 fully-fused MLP 32 -> 128 x 8 hidden -> 16 with ReLU, fp32
-accumulation, 4,194,304 rows ~N(0,1) fp32 per GPU, Kaiming-normal weights,
-zero biases, seeded synthetic data. One step = one forward pass over the whole
-batch. Metric: MLP evals/s = rows x layers / s (layers = 9 weight layers).
+Default workload (the configuration the metric "MLP
+evals/sec at 1/2/4/8 B200" is defined across): fp16 MLP 3 -> 64 x 4 hidden
+-> 4 with ReLU, fp32 accumulation, 67,108,864 rows ~U[-1,1]^3 fp32 split
+evenly over the ranks, Kaiming-normal weights, zero biases, seeded synthetic
+data, and a final NCCL all-gather of the fp32 outputs so every rank holds
+the whole [67,108,864, 4] result. One step = one forward pass over the whole
+batch plus the all-gather. Metric: MLP evals/s = rows x layers / s (5 weight
+layers).
 
 * ``value``: device time (CUDA events on the launch stream, max over ranks)
-  with the input already resident in HBM; inputs (537 MB) are larger than
-  the 126 MB L2, so no flush is needed between steps.
-* ``e2e``: the same metric through the public API with host buffers: every
-  step copies the pinned fp32 input host->device (rdv.wrap), runs the map
-  and copies the fp32 result back into pinned host memory.
-* ``roofline``: tensor-pipe bound; achieved = algorithmic FLOPs of one
-  launch / its average duration; peak from MEASURED_PEAKS.json.
+  with the input resident in HBM (805 MB > 126 MB L2, no flush). At N > 1
+  the rows are cut into slabs split evenly over the ranks; the all-gather of
+  slab k runs on NCCL's stream while slab k + 1 computes
+  (sharding.sharded_map_overlapped).
+* ``e2e``: the same metric through the public API from pinned host memory:
+  each rank streams its rows in and its results out on copy streams while
+  the kernels and the all-gather run (h2d/d2h bytes are whole-job figures).
+* ``roofline``: tensor-pipe bound; achieved = algorithmic FLOPs of the
+  rank's launches / their CUDA-event time; peak from MEASURED_PEAKS.json.
 * ``cpu_baseline``: the oracle's torch-CPU restatement (float16-staged
   operands, fp32 GEMMs, all host threads) on a bounded sample, rank 0 at N=1.
+* ``secondary`` (N=1): compact device-timed figures of the other BASELINE
+  configs and the secondary operators from the same run.
 * ``--impl reference``: the reference path's CPU restatement (the reference
-  itself needs Vulkan, unavailable on this box) timed alone on the host.
+  itself needs Vulkan, unavailable on this box) timed alone on the host's
+  cores, rank 0 only.
 
-Multi-GPU (torchrun): each rank runs its own batch (weak scaling); the only
-cross-rank traffic is the barrier and the max-reduction of the timings.
-``--workload c5`` runs BASELINE config 5 instead (67,108,864 rows split
-across ranks, final NCCL all-gather of the outputs; strong scaling).
+``--workload c2`` runs BASELINE config 2 (4,194,304 rows per GPU, weak
+scaling); c1, c3, c4 and trm run the other configs with their own metrics.
 """
 from __future__ import annotations
 
@@ -198,8 +205,12 @@ def dist_setup(n_gpus):
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
+        # NCCL on a high-priority stream: the overlapped all-gather's CTAs are
+        # dispatched ahead of the next slab's kernel when SMs free up
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), pg_options=opts)
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
@@ -220,11 +231,21 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
+def host_threads() -> int:
+    """All of the host's cores for the CPU legs (torchrun sets
+    OMP_NUM_THREADS=1 in every rank; the CPU figures are taken on rank 0 with
+    the whole host)."""
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
 def cpu_baseline(spec, layers, seconds=8.0, chunk=65536):
     """Oracle torch-CPU restatement (float16-staged operands, fp32 GEMM,
     all host threads) on a bounded sample of the same workload."""
     from oracle import mlp as omlp
 
+    cores = host_threads()
     lay = omlp.prestage_torch([{"W": l["W"], "b": l["b"], "math": l["math"], "relu": l["relu"]} for l in layers])
     x = make_input(spec, chunk, seed=12345)
     omlp.mlp_forward_torch_cpu(x[:1024], lay)
@@ -237,9 +258,20 @@ def cpu_baseline(spec, layers, seconds=8.0, chunk=65536):
         if el >= seconds or done >= spec["rows"]:
             break
     n_layers = len(layers)
-    return {"value": done * n_layers / el, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{done} rows of the workload in {chunk}-row chunks ({el:.1f} s): torch CPU fp32 GEMMs on "
-                      f"float16-staged operands (oracle restatement of the reference path)"}
+    return {"value": done * n_layers / el, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{done} rows in {chunk}-row chunks ({el:.1f} s), torch CPU, f16-staged operands"}
+
+
+def mlp_config(spec, world):
+    """The `config` object of an MLP workload line; both arms print the same
+    one for the same (workload, N)."""
+    sharded = spec["name"] == "c5"
+    rows_per_gpu = spec["rows"] // world if sharded else spec["rows"]
+    cfg = {"workload": spec["workload"], "dims": spec["dims"], "rows_per_gpu": rows_per_gpu,
+           "rows_total": spec["rows"] if sharded else spec["rows"] * world,
+           "l2": "inputs larger than L2, no flush",
+           "parallelism": f"dp{world}" + ("+allgather" if sharded and world > 1 else "")}
+    return cfg
 
 
 # ---------------------------------------------------------------- reference
@@ -248,6 +280,7 @@ def run_reference(args, spec, world, rank):
         return
     from oracle import mlp as omlp
 
+    cores = host_threads()
     layers = make_weights(spec)
     lay = omlp.prestage_torch([{"W": l["W"], "b": l["b"], "math": l["math"], "relu": l["relu"]} for l in layers])
     sample = min(spec["rows"], 262_144)
@@ -261,15 +294,15 @@ def run_reference(args, spec, world, rank):
     n_layers = len(layers)
     value = sample * n_layers * args.steps / el
     sample_txt = (f"{sample} of {spec['rows']} rows per step, torch CPU fp32 GEMMs on float16-staged operands, "
-                  f"{torch.get_num_threads()} threads (restatement of the reference path; its Vulkan kernels are "
-                  f"unavailable on this box)")
+                  f"{cores} threads (restatement of the reference path; its Vulkan kernels are unavailable on "
+                  f"this box)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16" if spec["math"] == "f16" else "f32",
-        "data": "synthetic (seeded)", "config": {"workload": spec["workload"], "rows_per_step": sample},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": sample_txt},
+        "higher_is_better": True, "scaling": "strong" if spec["name"] == "c5" else "weak", "vs_baseline": None,
+        "dtype": "f16" if spec["math"] == "f16" else "f32",
+        "data": "synthetic (seeded torch.Generator)", "config": mlp_config(spec, args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample_txt},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -279,46 +312,47 @@ def run_reference(args, spec, world, rank):
 def run_ours(args, spec, world, rank, local):
     import rdv_project_b200 as rdv
     from rdv_project_b200 import _native as N
+    from rdv_project_b200.sharding import piece_bounds, sharded_map_overlapped
 
     dev = torch.device("cuda", torch.cuda.current_device())
     layers = make_weights(spec)
     n_layers = len(layers)
     m = build_map(rdv, layers, dev)
     sharded = spec["name"] == "c5"
+    out_dim = spec["dims"][-1]
+    chunks = args.chunks if args.chunks else (8 if world > 1 else 1)
+    reserve = args.reserve_ctas if world > 1 else 0
     if sharded:
-        from rdv_project_b200.sharding import all_gather_rows, shard_range
-        rb, re_ = shard_range(spec["rows"], world, rank)
-        per_rank = re_ - rb
-        x_host = make_input(spec, spec["rows"], seed=0)[rb:re_].contiguous()
-        y_all = torch.empty(spec["rows"], spec["dims"][-1], device=dev)
+        n = spec["rows"]
+        x_host = make_input(spec, n, seed=0)
+        pieces = piece_bounds(n, world, rank, chunks)
+        rows_rank = sum(e - b for b, e in pieces)
     else:
-        per_rank = spec["rows"]
-        x_host = make_input(spec, per_rank, seed=rank)
-    x_dev = rdv.wrap(x_host.to(dev))
+        n = spec["rows"]
+        x_host = make_input(spec, n, seed=rank)
+        pieces = [(0, n)]
+        rows_rank = n
+    x_dev = x_host.to(dev)
+    y_all = torch.empty(n, out_dim, device=dev)
     stream = torch.cuda.current_stream()
 
     def step():
-        y = m(x_dev)
         if sharded:
-            if world > 1:
-                all_gather_rows(y.as_tensor("torch"), spec["rows"], out=y_all)
-            else:
-                y_all.copy_(y.as_tensor("torch"))
-        return y
+            sharded_map_overlapped(m, x_dev, out=y_all, chunks=chunks, reserve_ctas=reserve)
+        else:
+            rdv.maps.evaluate_into(m, x_dev, y_all)
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
 
-    # quick parity spot-check of the benchmark's own output (sampled rows)
-    idx = np.zeros(0, dtype=np.int64)
+    # parity spot-check of the benchmark's own output against the oracle
+    # (2048 sampled rows of the gathered result)
     parity = (None, None)
     if not args.profile_run:
         from oracle import mlp as omlp
-        idx = np.random.default_rng(7).choice(per_rank, size=min(per_rank, 2048), replace=False)
-        idx.sort()
-        y_dev = m(x_dev).as_tensor("torch")
-        got = y_dev[torch.from_numpy(idx).to(dev)].cpu().numpy()
+        idx = np.sort(np.random.default_rng(7).choice(n, size=min(n, 2048), replace=False))
+        got = y_all[torch.from_numpy(idx).to(dev)].cpu().numpy()
         lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": l["math"], "relu": l["relu"]} for l in layers]
         ref = omlp.mlp_forward(x_host.numpy()[idx], lay_np)
         parity = omlp.rel_errors(got, ref)
@@ -345,65 +379,105 @@ def run_ours(args, spec, world, rank, local):
     barrier(world)
     t_dev = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
 
-    # ---- end-to-end through the public API with host buffers ----
-    x_pin = x_host.pin_memory()
-    y_pin = torch.empty(per_rank, spec["dims"][-1]).pin_memory()
-    e2e_steps = 0 if args.profile_run else max(1, min(args.steps, 5))
-    barrier(world)
+    # kernel-only time of this rank's launches (no collective), for the roofline
+    def kernels_only():
+        for b, e in pieces:
+            rdv.maps.evaluate_into(m, x_dev[b:e], y_all[b:e])
+
     torch.cuda.synchronize()
     ev0.record(stream)
-    for _ in range(e2e_steps):
-        y = m(rdv.wrap(x_pin))
-        y_pin.copy_(y.as_tensor("torch"), non_blocking=True)
+    for _ in range(args.steps):
+        kernels_only()
     ev1.record(stream)
     torch.cuda.synchronize()
-    t_e2e = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
+    t_kern = ev0.elapsed_time(ev1) / 1e3
+    barrier(world)
+
+    # ---- end-to-end through the public API with pinned host buffers ----
+    e2e_steps = 0 if args.profile_run else max(1, min(args.steps, 5))
+    t_e2e = None
+    if e2e_steps:
+        x_pin = x_host.pin_memory()
+        y_pin = torch.empty(n, out_dim).pin_memory()
+        e2e_chunks = args.e2e_chunks
+
+        def e2e_step():
+            if sharded:
+                sharded_map_overlapped(m, x_host=x_pin, y_host=y_pin, out=y_all, chunks=max(e2e_chunks, chunks),
+                                       reserve_ctas=reserve)
+            else:
+                sharded_map_overlapped(m, x_host=x_pin, y_host=y_pin, out=y_all, chunks=e2e_chunks, shard=False)
+
+        e2e_step()
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        t_e2e = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
 
     if rank != 0:
         return
-    units_per_step = (spec["rows"] if sharded else per_rank * world) * n_layers
+    units_per_step = (n if sharded else n * world) * n_layers
     value = units_per_step * args.steps / t_dev
     ms = t_dev / args.steps * 1e3
     peaks, peak_kind = measured_peaks()
-    flops_launch = flops_per_row(spec["dims"]) * per_rank
-    achieved = flops_launch / (t_dev / args.steps) / 1e12
+    flops_launch = flops_per_row(spec["dims"]) * rows_rank
+    achieved = flops_launch / (t_kern / args.steps) / 1e12
     key = "bf16_tflops"
     peak = float(peaks.get(key, 1590.0))
     traffic = ncu_traffic(f"mlp_tc_{spec['name']}")
+    rows_io = n if sharded else n * world
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong" if sharded else "weak", "vs_baseline": None,
         "dtype": "f16" if spec["math"] == "f16" else "f32", "data": "synthetic (seeded torch.Generator)",
-        "config": {"workload": spec["workload"], "rows_per_gpu": per_rank, "dims": spec["dims"],
-                   "layers": n_layers, "input": "fp32 [rows, %d]" % spec["dims"][0],
-                   "l2": "inputs larger than L2 (%.0f MB per GPU), no flush" % (per_rank * spec["dims"][0] * 4 / 1e6),
-                   "parallelism": f"dp{world}"},
+        "config": mlp_config(spec, world),
         "e2e": {"value": units_per_step * e2e_steps / t_e2e if e2e_steps else None, "unit": UNIT,
-                "h2d_bytes_per_step": int(x_pin.numel() * 4), "d2h_bytes_per_step": int(y_pin.numel() * 4)},
+                "h2d_bytes_per_step": int(rows_io * spec["dims"][0] * 4),
+                "d2h_bytes_per_step": int(rows_io * out_dim * 4)},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor" if spec["math"] != "f32" else "fp32-cuda-core", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": f"{peak_kind} {key}",
-                     "flops_per_launch": flops_launch},
-        "parity": {"rows_checked": int(idx.size), "normwise": parity[0], "elementwise": parity[1]},
+                     "peak_source": f"{peak_kind} {key}", "flops_per_launch": flops_launch,
+                     "kernel_ms": t_kern / args.steps * 1e3},
+        "parity": {"rows": 2048, "normwise": parity[0], "elementwise": parity[1]},
         "clocks": clocks,
     }
+    if sharded and world > 1:
+        line["overlap"] = {"chunks": chunks, "reserve_ctas": reserve}
     if world == 1 and not args.profile_run:
         line["cpu_baseline"] = cpu_baseline(spec, layers)
-        if spec["name"] == "c2" and not args.no_secondary:
-            # the other BASELINE configs, device-timed on this GPU in the same run
-            line["secondary"] = {
-                "c1": mlp_summary(c1_spec()),
-                "c3": run_c3(args, 1, 0, local, summary=True),
-                "c4": run_c4(args, 1, 0, local, summary=True),
-                "c5": mlp_summary(c5_spec()),
-                "transmittance": run_trm(args, 1, 0, local, summary=True),
-                "tensor_op_chain": chain_summary(),
-                "conv_family": conv_family_summary(),
-                "ratiotracking": ratiotracking_summary(),
-            }
+        if not args.no_secondary:
+            line["secondary"] = secondary_summaries(args, local, spec["name"])
     print(json.dumps(line), flush=True)
+
+
+def _r(v, nd=4):
+    """Rounded number for the compact secondary section."""
+    if v is None:
+        return None
+    return float(f"{v:.{nd}g}")
+
+
+def secondary_summaries(args, local, headline):
+    """Compact device-timed figures of the other configs and operators on
+    this GPU (one object per workload: value, unit, ms, roofline fraction,
+    parity against the oracle). Prose descriptions are in DESIGN.md."""
+    out = {}
+    for name, spec_fn in (("c2", c2_spec), ("c5", c5_spec), ("c1", c1_spec)):
+        if name != headline:
+            out[name] = mlp_summary(spec_fn())
+    out["c3"] = run_c3(args, 1, 0, local, summary=True)
+    out["c4"] = run_c4(args, 1, 0, local, summary=True)
+    out["trm"] = run_trm(args, 1, 0, local, summary=True)
+    out["rt"] = ratiotracking_summary()
+    out["chain"] = chain_summary()
+    out["conv_tc"] = conv_family_summary()
+    return out
 
 
 # ------------------------------------------------- config 3: Winograd conv
@@ -466,10 +540,7 @@ def run_c3(args, world, rank, local, summary=False):
     torch.cuda.synchronize()
     parity = (None, None)
     if not args.profile_run:
-        ref = rdv.conv2d_direct(x[:1], w33io, b)
-        d = (y[:1].double() - ref.double()).abs()
-        r = ref.double()
-        parity = ((d.max() / r.abs().max()).item(), (d / (r.abs() + r.pow(2).mean().sqrt())).max().item())
+        parity = c3_oracle_parity(y[0].cpu().numpy(), x_host[0], w33io, b)
     sampler = ClockSampler(local) if (rank == 0 and not summary) else None
     if sampler:
         sampler.start()
@@ -489,11 +560,8 @@ def run_c3(args, world, rank, local, summary=False):
     achieved = c3_bytes(n_img) / (t_kernel / steps) / 1e9
     value = c3_bytes(C3_SHAPE[0]) * steps / t_step / 1e9
     if summary:
-        return {"workload": "BASELINE config 3: Winograd F(2x2,3x3) 8x256x256x64 fp16 -> 64 fp32",
-                "metric": "Winograd GB/s", "value": value, "ms_per_step": t_step / steps * 1e3,
-                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                             "frac": achieved / hbm, "peak_source": f"{peak_kind} hbm_gbs"},
-                "parity_vs_direct": {"normwise": parity[0], "elementwise": parity[1]}}
+        return {"value": _r(value), "unit": "GB/s", "ms": _r(t_step / steps * 1e3), "frac": _r(achieved / hbm, 3),
+                "parity": _r(parity[1], 2)}
     # end to end through the public API with host buffers
     x_pin = x_host.pin_memory()
     y_pin = torch.empty(y.shape, dtype=torch.float32).pin_memory()
@@ -521,7 +589,8 @@ def run_c3(args, world, rank, local, summary=False):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": ncu_traffic("winograd_f23_c3"), "peak_source": f"{peak_kind} hbm_gbs",
                      "bytes_per_launch": c3_bytes(n_img)},
-        "parity": {"against": "on-device fp32 direct conv, image 0", "normwise": parity[0], "elementwise": parity[1]},
+        "parity": {"against": "oracle float64 direct conv, image 0 rows 0-31", "normwise": parity[0],
+                   "elementwise": parity[1]},
         "clocks": clocks,
     }
     if world == 1 and not args.profile_run:
@@ -530,11 +599,25 @@ def run_c3(args, world, rank, local, summary=False):
     return line
 
 
+def c3_oracle_parity(y0, x0, w33io, b, rows=32):
+    """(normwise, elementwise) error of output rows [0, rows) of one image
+    against the oracle's float64 direct convolution (the reference's
+    Conv2DTensorOp arithmetic, conv2d_tensor_op.h:21-87) of the same
+    float16-rounded input; input rows [0, rows] feed those outputs."""
+    from oracle import mlp as omlp
+    from oracle import winograd as owg
+
+    xs = x0[:rows + 1].float().numpy()[None]
+    ref = owg.conv3x3_direct(xs, w33io.numpy(), b.numpy())[0, :rows]
+    return omlp.rel_errors(np.asarray(y0[:rows], dtype=np.float64), ref)
+
+
 def c3_cpu_baseline(x_all, w33io, b, seconds=6.0):
     """torch CPU fp32 conv2d (the direct convolution the reference's op
     approximates) on float16-rounded images, all host threads."""
     import torch.nn.functional as F
 
+    cores = host_threads()
     wt = w33io.permute(3, 2, 0, 1).contiguous()  # -> [COUT, CIN, 3, 3]
     done, t0 = 0, time.perf_counter()
     while True:
@@ -544,7 +627,7 @@ def c3_cpu_baseline(x_all, w33io, b, seconds=6.0):
         el = time.perf_counter() - t0
         if el >= seconds or done >= x_all.shape[0]:
             break
-    return {"value": c3_bytes(done) / el / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": c3_bytes(done) / el / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
             "sample": f"{done} of {x_all.shape[0]} images ({el:.1f} s), torch CPU fp32 conv2d on float16-rounded "
                       f"input, algorithmic bytes of those images per second"}
 
@@ -613,12 +696,8 @@ def run_c4(args, world, rank, local, summary=False):
     achieved = hits * 128 * flops_sample / (t_kernel / steps) / 1e12
     fps = steps / t_step
     if summary:
-        return {"workload": "BASELINE config 4: ray-march 1920x1080, 128 samples/ray, MLP 3-64-64-4 fp16",
-                "metric": "frames/s", "value": fps, "ms_per_frame": t_step / steps * 1e3, "rays_hit": hits,
-                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                             "frac": achieved / peak, "peak_source": f"{peak_kind} bf16_tflops",
-                             "note": "flops of the samples of rays that hit the box"},
-                "parity_vs_oracle_rows_537_539": {"normwise": parity[0], "elementwise": parity[1]}}
+        return {"value": _r(fps), "unit": "frames/s", "ms": _r(t_step / steps * 1e3), "frac": _r(achieved / peak, 3),
+                "parity": _r(parity[1], 2)}
     if rank != 0:
         return None
     line = {
@@ -662,12 +741,13 @@ def c4_cpu_baseline(layers, rows=4):
     rows through the middle of the image, extrapolated to frames/s."""
     from oracle import raymarch as orm
 
+    cores = host_threads()
     lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
     t0 = time.perf_counter()
     orm.render_emission_absorption(orm.orbit_pose(0), C4["width"], C4["height"], 128, lay_np, row_begin=538,
                                    row_end=538 + rows)
     el = time.perf_counter() - t0
-    return {"value": rows / el / C4["height"], "unit": "frames/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": rows / el / C4["height"], "unit": "frames/s", "cores": cores, "kind": "port",
             "sample": f"{rows} full-width rows through the cube ({el:.1f} s, numpy/BLAS), extrapolated to 1080 rows "
                       f"(the middle rows hit the box more than the frame average, so this favours the CPU)"}
 
@@ -814,11 +894,8 @@ def run_trm(args, world, rank, local, summary=False):
                "h2d_bytes_per_step": int(rays_pin.numel() * 4) * world,
                "d2h_bytes_per_step": int(T_pin.numel() * 4) * world}
     if summary:
-        return {"workload": "RaymarchingTransmittance, 1920x1080 camera rays (orbit pose 0), extinction "
-                            "ReLU(MLP 3->64->64->1) LinearFast (tensor-core march), step 0.01",
-                "metric": "extinction evaluations/s", "value": value, "ms_per_step": t_step / steps * 1e3,
-                "evaluations_per_step": evals_total, "rays": n_all, "roofline": roof,
-                "parity_vs_oracle_2048_rays": {"normwise": parity[0], "elementwise": parity[1]}}
+        return {"value": _r(value), "unit": "evaluations/s", "ms": _r(t_step / steps * 1e3),
+                "frac": _r(achieved / peak, 3), "parity": _r(parity[1], 2)}
     if rank != 0:
         return None
     roof["traffic"] = ncu_traffic("mlp_tc_march_trm")
@@ -853,6 +930,7 @@ def trm_cpu_baseline(layers, n=65536):
     exit, float16-staged MLP) on n rays through the image middle."""
     from oracle import raymarch as orm
 
+    cores = host_threads()
     lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
     rays = trm_rays()
     mid = (TRM["height"] // 2) * TRM["width"]
@@ -861,7 +939,7 @@ def trm_cpu_baseline(layers, n=65536):
     _, evals = orm.raymarching_transmittance(sample[:, :3], sample[:, 3:], TRM["step"], TRM["scale"],
                                              orm.mlp_extinction(lay_np), return_evaluations=True)
     el = time.perf_counter() - t0
-    return {"value": evals / el, "unit": "evaluations/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": evals / el, "unit": "evaluations/s", "cores": cores, "kind": "port",
             "sample": f"{n} rays through the image middle ({evals} evaluations, {el:.1f} s, numpy/BLAS)"}
 
 
@@ -916,14 +994,8 @@ def ratiotracking_summary(steps=3):
                                                 orm.mlp_extinction(lay_np), grid.numpy(), seeds,
                                                 index=np.arange(mid, mid + n_cpu), return_evaluations=True)
     el = time.perf_counter() - t0
-    return {"workload": "RatiotrackingTransmittance, 1920x1080 rays (config-4 camera), ReLU(MLP 3->64->64->1) "
-                        "LinearFast extinction, 16^3 voxel majorant",
-            "ms": t * 1e3, "rays_per_s": rays.shape[0] / t, "evaluations": evals, "evaluations_per_s": evals / t,
-            "roofline": {"bound": "fp32 CUDA-core FMA", "achieved": flop / t / 1e12, "unit": "TFLOP/s",
-                         "peak": nominal, "frac": flop / t / 1e12 / nominal,
-                         "peak_source": "nominal: 148 SMs x 128 lanes x 2 x 1.965 GHz"},
-            "cpu_baseline": {"value": ev_cpu / el, "unit": "evaluations/s", "cores": torch.get_num_threads(),
-                             "kind": "port", "sample": f"{n_cpu} middle rays ({ev_cpu} evaluations, {el:.1f} s)"}}
+    return {"value": _r(evals / t), "unit": "evaluations/s", "ms": _r(t * 1e3), "rays_per_s": _r(rays.shape[0] / t),
+            "frac_fp32_nominal": _r(flop / t / 1e12 / nominal, 3), "cpu": _r(ev_cpu / el)}
 
 
 def chain_summary(rows=1 << 20, steps=3):
@@ -960,10 +1032,14 @@ def chain_summary(rows=1 << 20, steps=3):
     torch.cuda.synchronize()
     t_fused = time_steps(final.evaluate_chain, steps)
     same = bool(torch.equal(final.as_type("torch"), ref))
-    return {"workload": f"config-2 architecture as {len(ops)} TensorOperations (LinearTensorOpSmall, "
-                        f"ReLUTensorOp), {rows} rows",
-            "per_op_ms": t_ops / steps * 1e3, "evaluate_chain_ms": t_fused / steps * 1e3,
-            "speedup": t_ops / t_fused, "bit_identical": same}
+    from oracle import mlp as omlp
+    idx = np.sort(np.random.default_rng(3).choice(rows, size=2048, replace=False))
+    x_np = make_input(spec, rows, seed=0).numpy()[idx]
+    lay_np = [{"W": l["W"].numpy(), "b": l["b"].numpy(), "math": "f16", "relu": l["relu"]} for l in layers]
+    got = final.as_type("torch")[torch.from_numpy(idx).to(dev)].cpu().numpy()
+    parity = omlp.rel_errors(got, omlp.mlp_forward(x_np, lay_np))
+    return {"ms": _r(t_fused / steps * 1e3), "per_op_ms": _r(t_ops / steps * 1e3), "speedup": _r(t_ops / t_fused, 3),
+            "exact_vs_per_op": same, "parity": _r(parity[1], 2)}
 
 
 def conv_family_summary(steps=5):
@@ -993,19 +1069,18 @@ def conv_family_summary(steps=5):
                                               bd.data_ptr(), N.RDVB_MATH_F16, 1, y.data_ptr(), None),
                 "rdvb_conv2d_direct_staged")
 
-    out = {"workload": "3x3 direct conv, float16 operands / fp32 accumulation, 8x256x256x64 -> 64 (config 3 shape)"}
+    out = {}
     flops = 2 * n * h * w * c * c * 9
-    for name, fn, k in (("tensor_core", tc, steps), ("cuda_cores", cuda_cores, 1)):
+    for name, fn, k in (("tc", tc, steps), ("cuda_cores", cuda_cores, 1)):
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
-        t = time_steps(fn, k, flush=flush) / k
-        out[name] = {"ms": t * 1e3, "tflops": flops / t / 1e12}
+        out[name] = time_steps(fn, k, flush=flush) / k
     peaks, peak_kind = measured_peaks()
     peak = float(peaks.get("bf16_tflops", 1590.0))
-    out["roofline"] = {"bound": "tensor", "achieved": out["tensor_core"]["tflops"], "peak": peak, "unit": "TFLOP/s",
-                       "frac": out["tensor_core"]["tflops"] / peak, "peak_source": f"{peak_kind} bf16_tflops"}
-    return out
+    tf = flops / out["tc"] / 1e12
+    return {"ms": _r(out["tc"] * 1e3), "tflops": _r(tf), "frac": _r(tf / peak, 3),
+            "cuda_core_ms": _r(out["cuda_cores"] * 1e3)}
 
 
 def mlp_summary(spec, steps=5):
@@ -1023,14 +1098,11 @@ def mlp_summary(spec, steps=5):
     t = time_steps(lambda: m(x), steps)
     peaks, peak_kind = measured_peaks()
     achieved = flops_per_row(spec["dims"]) * spec["rows"] / (t / steps) / 1e12
-    out = {"workload": spec["workload"], "metric": METRIC, "value": spec["rows"] * len(layers) * steps / t,
-           "ms_per_step": t / steps * 1e3, "rows": spec["rows"]}
+    out = {"value": _r(spec["rows"] * len(layers) * steps / t), "unit": UNIT, "ms": _r(t / steps * 1e3)}
     if spec["math"] != "f32":
-        peak = float(peaks.get("bf16_tflops", 1590.0))
-        out["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                           "frac": achieved / peak, "peak_source": f"{peak_kind} bf16_tflops"}
+        out["frac"] = _r(achieved / float(peaks.get("bf16_tflops", 1590.0)), 3)
     else:
-        out["achieved_tflops_fp32"] = achieved
+        out["tflops_fp32"] = _r(achieved)
     return out
 
 
@@ -1040,7 +1112,13 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5", "trm"], default="c2")
+    ap.add_argument("--workload", choices=["c5", "c2", "c1", "c3", "c4", "trm"], default="c5")
+    ap.add_argument("--chunks", type=int, default=0,
+                    help="slabs of the sharded config-5 step (default 8 at N > 1, 1 at N = 1)")
+    ap.add_argument("--reserve-ctas", type=int, default=16,
+                    help="SMs left free of the persistent MLP kernel for the overlapped all-gather (N > 1)")
+    ap.add_argument("--e2e-chunks", type=int, default=16,
+                    help="pieces of the end-to-end leg's host-streaming pipeline")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows per GPU instead of the config's (small cases for ncu captures)")
     ap.add_argument("--no-secondary", action="store_true",

@@ -109,6 +109,30 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
                      const float* const* weights, const float* const* biases, const int* layer_flags,
                      int input_relu, int tail_exact, const void* packed, float* y, void* stream);
 
+/* Which kernel rdvb_mlp_forward runs for these arguments (no reference
+ * counterpart: the reference picks between its fp16 and fp32 paths inside the
+ * shader, linear_fast.h:44,102-108). Returns RDVB_PATH_TENSOR_CORE when its
+ * whole 32-row groups run on the tcgen05 kernel, RDVB_PATH_CUDA_CORE when the
+ * call runs on the CUDA cores -- then rdvb_last_error() names the reason (an
+ * fp32 layer, a misaligned x or packed image, a chain too wide ...) -- or a
+ * negative RDVB_ERR_* for invalid arguments. Launches nothing; the decision
+ * depends on the current device's shared-memory limit. A float16 chain whose
+ * x is misaligned (e.g. a row slice x[1:] of a 3-wide fp32 tensor) runs on
+ * the CUDA cores, tens of times slower: callers can check here first. */
+#define RDVB_PATH_CUDA_CORE 0
+#define RDVB_PATH_TENSOR_CORE 1
+int rdvb_mlp_forward_path(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
+                          const int* layer_flags, const void* packed, const float* y);
+
+/* Caps the CTAs of the persistent tensor-core MLP kernel at max_ctas (0, the
+ * default, = one CTA per SM), for every later launch in this process (no
+ * reference counterpart). A persistent CTA holds its SM's registers, so a
+ * collective launched concurrently on another stream (the NCCL all-gather
+ * that overlaps a sharded map's next chunk) gets SMs only if some are left
+ * free. rdvb_get_max_ctas returns the current cap. */
+int rdvb_set_max_ctas(int max_ctas);
+int rdvb_get_max_ctas(void);
+
 /* Allocation-free rdvb_mlp_forward (no reference counterpart: the reference
  * re-stages weights inside every dispatch). Same arguments minus `packed`:
  * the packed weight image is written into a static device array of
@@ -121,7 +145,12 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
  * callers on a device: two calls whose work overlaps on the device (other
  * streams, other threads) race on it, so order them (one stream, or events).
  * The array's address is looked up (cudaGetSymbolAddress) on the first call
- * on each device; make that first call before any stream capture. */
+ * on each device; make that first call before any stream capture. The
+ * address belongs to the device's context: after cudaDeviceReset the library
+ * must be reloaded (as for its other per-device state, e.g. kernel
+ * attributes). A call rejected for its arguments never writes the array, and
+ * the array is written only when the tensor-core kernel will read it
+ * (rdvb_mlp_forward_path). */
 int64_t rdvb_mlp_static_capacity(void);
 int rdvb_mlp_forward_static(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
                             const float* const* weights, const float* const* biases, const int* layer_flags,

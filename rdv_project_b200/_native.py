@@ -20,6 +20,7 @@ RDVB_F32, RDVB_F16, RDVB_BF16 = 0, 1, 2
 RDVB_MATH_F32, RDVB_MATH_F16, RDVB_MATH_BF16 = 0, 1, 2
 RDVB_LAYER_RELU = 4
 RDVB_WINOGRAD_F2X2, RDVB_WINOGRAD_F4X4 = 0, 1
+RDVB_PATH_CUDA_CORE, RDVB_PATH_TENSOR_CORE = 0, 1
 
 _c_int, _c_i64, _vp, _c_u32, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float
 
@@ -34,6 +35,9 @@ SIGNATURES = {
     "rdvb_mlp_forward": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp]),
     "rdvb_mlp_static_capacity": (_c_i64, []),
     "rdvb_mlp_forward_static": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp]),
+    "rdvb_mlp_forward_path": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp]),
+    "rdvb_set_max_ctas": (_c_int, [_c_int]),
+    "rdvb_get_max_ctas": (_c_int, []),
     "rdvb_relu": (_c_int, [_vp, _vp, _c_i64, _vp]),
     "rdvb_winograd_packed_bytes": (_c_i64, [_c_int, _c_int, _c_int]),
     "rdvb_winograd_filter_transform": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
@@ -102,7 +106,7 @@ def check(rc: int, what: str) -> None:
         raise RdvbError(f"{what} failed ({rc}): {last_error()}")
 
 
-RDVB_ERR_DEVICE_STATUS = -4
+RDVB_ERR_INVALID_ARG, RDVB_ERR_UNSUPPORTED, RDVB_ERR_CUDA, RDVB_ERR_DEVICE_STATUS = -1, -2, -3, -4
 
 
 def device_status(clear: bool = True) -> int:
@@ -117,6 +121,14 @@ def device_status(clear: bool = True) -> int:
 
 def launch_count() -> int:
     return int(lib().rdvb_launch_count())
+
+
+def set_max_ctas(n: int) -> int:
+    """Caps the persistent tensor-core MLP kernel at n CTAs (0 = one per SM)
+    for later launches; returns the previous cap."""
+    prev = int(lib().rdvb_get_max_ctas())
+    check(lib().rdvb_set_max_ctas(int(n)), "rdvb_set_max_ctas")
+    return prev
 
 
 def int_array(values):

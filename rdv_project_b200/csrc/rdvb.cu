@@ -148,13 +148,42 @@ int check_chain(int n_layers, const int* dims, const int* flags) {
     return RDVB_OK;
 }
 
+// Upper bound on the CTAs of the persistent MLP kernel (0 = one per SM);
+// see rdvb_set_max_ctas.
+std::atomic<int> g_max_ctas{0};
+
+// Persistent-grid size on `dev` under the rdvb_set_max_ctas cap.
+int persistent_ctas(const DeviceInfo* dev) {
+    const int cap = g_max_ctas.load(std::memory_order_relaxed);
+    return (cap > 0 && cap < dev->sm_count) ? cap : dev->sm_count;
+}
+
+// Why the tcgen05 kernel does not take a rows-mode chain, or nullptr when
+// it does as far as the arguments go (the shared-memory plan, which depends
+// on the device, is checked by the launcher).
+const char* mlp_tc_decline(const void* x, int n_layers, const int* dims, const int* flags, const void* packed,
+                           const float* y) {
+    using namespace rdvb::mlp_tc;
+    if (!pack_layout(n_layers, dims).ok) return "the chain has more than 16 layers or a width above 128";
+    const int math = flags[0] & 3;
+    if (math == RDVB_MATH_F32) return "the chain has exact fp32 (Linear) layers";
+    for (int l = 1; l < n_layers; ++l)
+        if ((flags[l] & 3) != math) return "the chain mixes float16, bfloat16 and fp32 layers";
+    if (packed == nullptr) return "no packed weight image was given";
+    if (!aligned(packed, 256)) return "the packed weight image is not 256-byte aligned";
+    if (!aligned(x, 16)) return "x is not 16-byte aligned";
+    if (!aligned(y, 4)) return "y is not 4-byte aligned";
+    return nullptr;
+}
+
 // --------------------------------------------------- tensor-core launcher
 // Launches the tcgen05 fused-MLP kernel on rows [0, n_rows) of x, or, with
 // `ray` set, in ray-march mode (tiles = the rays of ray->hit_list, count on
-// the device). Sets *taken when the chain fits the kernel and it launched.
+// the device). Sets *taken when the chain fits the kernel and it launched;
+// with `dry_run` it only decides (*taken) and launches nothing.
 int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims, const int* flags,
                   int input_relu, const void* packed, float* y, cudaStream_t stream, DeviceInfo* dev, bool* taken,
-                  const rdvb::mlp_tc::RayParams* ray = nullptr) {
+                  const rdvb::mlp_tc::RayParams* ray = nullptr, bool dry_run = false) {
     using namespace rdvb::mlp_tc;
     *taken = false;
     if (!ray && n_rows <= 0) return RDVB_OK;
@@ -258,6 +287,10 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
         }
     }
     if (!slots) return RDVB_OK;  // does not fit: CUDA-core path
+    if (dry_run) {
+        *taken = true;
+        return RDVB_OK;
+    }
 
     int rc = RDVB_OK;
     const int ri = ray ? (ray->march ? kModeMarch : kModeRender) : kModeRows;
@@ -281,7 +314,8 @@ int launch_mlp_tc(const void* x, int x_dtype, int64_t n_rows, int n_layers, cons
         // ray mode: the tile count is only known on the device; a CTA with
         // no tile exits after loading the weights
         const int groups = (p.n_tiles + sl - 1) / sl;
-        const int grid = ray ? dev->sm_count : std::min(dev->sm_count, groups);
+        const int ctas = persistent_ctas(dev);
+        const int grid = ray ? ctas : std::min(ctas, groups);
         kernel<<<grid, cta_threads(iss), smem, stream>>>(p);
     };
 #define RDVB_GO(S, B, R)                                                         \
@@ -537,6 +571,42 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
     return launch_mlp_simt(x, x_dtype, 0, n_rows, n_layers, dims, weights, biases, layer_flags, false, input_relu, y,
                            st, dev);
 }
+
+int rdvb_mlp_forward_path(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
+                          const int* layer_flags, const void* packed, const float* y) {
+    if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
+    if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16 && x_dtype != RDVB_BF16)
+        return fail(RDVB_ERR_INVALID_ARG, "x_dtype %d is not RDVB_F32/F16/BF16", x_dtype);
+    if (n_rows < 0) return fail(RDVB_ERR_INVALID_ARG, "n_rows must be >= 0");
+    g_last_error.clear();
+    if (const char* why = mlp_tc_decline(x, n_layers, dims, layer_flags, packed, y)) {
+        fail(RDVB_OK, "CUDA-core path: %s", why);
+        return RDVB_PATH_CUDA_CORE;
+    }
+    if (n_rows < 32) {
+        fail(RDVB_OK, "CUDA-core path: fewer than 32 rows (no whole 32-row group)");
+        return RDVB_PATH_CUDA_CORE;
+    }
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    bool taken = false;
+    if (int rc = launch_mlp_tc(x, x_dtype, (n_rows / 32) * 32, n_layers, dims, layer_flags, 0, packed,
+                               const_cast<float*>(y), nullptr, dev, &taken, nullptr, true))
+        return rc;
+    if (!taken) {
+        fail(RDVB_OK, "CUDA-core path: no shared-memory plan of the tensor-core kernel fits this chain");
+        return RDVB_PATH_CUDA_CORE;
+    }
+    return RDVB_PATH_TENSOR_CORE;
+}
+
+int rdvb_set_max_ctas(int max_ctas) {
+    if (max_ctas < 0) return fail(RDVB_ERR_INVALID_ARG, "max_ctas must be >= 0 (0 = one CTA per SM)");
+    g_max_ctas.store(max_ctas, std::memory_order_relaxed);
+    return RDVB_OK;
+}
+
+int rdvb_get_max_ctas(void) { return g_max_ctas.load(std::memory_order_relaxed); }
 
 int rdvb_relu(const float* x, float* y, int64_t n, void* stream) {
     if (n < 0) return fail(RDVB_ERR_INVALID_ARG, "n must be >= 0");
@@ -1593,25 +1663,41 @@ int64_t rdvb_mlp_static_capacity(void) { return static_cast<int64_t>(kStaticPack
 int rdvb_mlp_forward_static(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
                             const float* const* weights, const float* const* biases, const int* layer_flags,
                             int input_relu, int tail_exact, float* y, void* stream) {
+    // The same argument checks as rdvb_mlp_forward, before anything touches
+    // the shared array: a rejected call leaves it as the last good call left it.
     if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
+    if (x_dtype != RDVB_F32 && x_dtype != RDVB_F16 && x_dtype != RDVB_BF16)
+        return fail(RDVB_ERR_INVALID_ARG, "x_dtype %d is not RDVB_F32/F16/BF16", x_dtype);
+    if (n_rows < 0) return fail(RDVB_ERR_INVALID_ARG, "n_rows must be >= 0");
+    if (n_rows == 0) return RDVB_OK;
+    if (!x || !y) return fail(RDVB_ERR_INVALID_ARG, "x and y must not be NULL");
+    if (!weights || !biases) return fail(RDVB_ERR_INVALID_ARG, "weights/biases must not be NULL");
+    for (int l = 0; l < n_layers; ++l)
+        if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "weights[%d]/biases[%d] is NULL", l, l);
     const int math = layer_flags[0] & 3;
     bool uniform = true;
     for (int l = 1; l < n_layers; ++l) uniform &= (layer_flags[l] & 3) == math;
     void* packed = nullptr;
-    // a packed image is used only by chains the tensor-core kernel takes:
-    // every layer float16 or every layer bfloat16, widths <= 128
-    if (uniform && math != RDVB_MATH_F32 && n_rows >= 32) {
-        const int64_t need = rdvb_mlp_packed_bytes(n_layers, dims);
-        if (need > 0) {
-            if (need > static_cast<int64_t>(kStaticPackBytes))
-                return fail(RDVB_ERR_UNSUPPORTED,
-                            "packed weights need %lld bytes; rdvb_mlp_forward_static holds at most %lld "
-                            "(use rdvb_mlp_pack + rdvb_mlp_forward with a caller buffer)",
-                            (long long)need, (long long)kStaticPackBytes);
-            if (int rc = static_pack_address(&packed)) return rc;
+    // The image is written only when the tensor-core kernel will read it:
+    // every layer float16 (or every layer bfloat16), widths <= 128, aligned
+    // x and y, at least one whole 32-row group and a shared-memory plan that
+    // fits. Any other call never touches the array.
+    const int64_t need = rdvb_mlp_packed_bytes(n_layers, dims);
+    if (uniform && math != RDVB_MATH_F32 && need > 0 && n_rows >= 32) {
+        if (need > static_cast<int64_t>(kStaticPackBytes))
+            return fail(RDVB_ERR_UNSUPPORTED,
+                        "packed weights need %lld bytes; rdvb_mlp_forward_static holds at most %lld "
+                        "(use rdvb_mlp_pack + rdvb_mlp_forward with a caller buffer)",
+                        (long long)need, (long long)kStaticPackBytes);
+        void* addr = nullptr;
+        if (int rc = static_pack_address(&addr)) return rc;
+        const int path = rdvb_mlp_forward_path(x, x_dtype, n_rows, n_layers, dims, layer_flags, addr, y);
+        if (path < 0) return path;
+        if (path == RDVB_PATH_TENSOR_CORE) {
             if (int rc = rdvb_mlp_pack(n_layers, dims, weights, biases,
-                                       math == RDVB_MATH_BF16 ? RDVB_BF16 : RDVB_F16, packed, stream))
+                                       math == RDVB_MATH_BF16 ? RDVB_BF16 : RDVB_F16, addr, stream))
                 return rc;
+            packed = addr;
         }
     }
     return rdvb_mlp_forward(x, x_dtype, n_rows, n_layers, dims, weights, biases, layer_flags, input_relu, tail_exact,

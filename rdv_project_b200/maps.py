@@ -374,27 +374,72 @@ def run_chain(plan: _ChainPlan, x2d: torch.Tensor, y2d: torch.Tensor, tail_exact
     N.check(rc, "rdvb_mlp_forward")
 
 
-def _evaluate(m: Map, owner: Map, x):
-    dev = current_device()
-    xt = x._tensor if isinstance(x, RDVObject) else wrap(x)._tensor
+def _device_tensor(x) -> torch.Tensor:
+    return x._tensor if isinstance(x, RDVObject) else wrap(x)._tensor
+
+
+def _as_rows(m: Map, xt: torch.Tensor) -> torch.Tensor:
+    """xt as a contiguous [rows, IN] tensor. The tensor-core kernel reads x
+    with 16-byte bulk copies; a misaligned view (a row slice such as x[1:] of
+    a 3-wide fp32 tensor) is copied to an aligned buffer instead of sending
+    the chain to the CUDA cores."""
     if xt.dtype not in _DTYPES:
         xt = xt.to(torch.float32)
-    lead = list(xt.shape[:-1])
     x2d = xt.reshape(-1, m.IN)
-    if not x2d.is_contiguous():
-        x2d = x2d.contiguous()
-    cache = owner.__dict__.setdefault("_out_cache", {})
-    key = (dev.index, tuple(lead), m.OUT)
-    out = cache.get(key)
-    if out is None:
-        out = RDVObject(torch.empty(lead + [m.OUT], dtype=torch.float32, device=dev))
-        cache[key] = out
+    if not x2d.is_contiguous() or x2d.data_ptr() % 16:
+        x2d = x2d.contiguous() if not x2d.is_contiguous() else x2d.clone()
+    return x2d
+
+
+def _plan_of(m: Map, owner: Map, dev) -> _ChainPlan:
     plans = owner.__dict__.setdefault("_plans", {})
     pkey = (dev.index, m.IN)
     plan = plans.get(pkey)
     if plan is None:
         plan = _ChainPlan(m, dev)
         plans[pkey] = plan
+    return plan
+
+
+def _bound(m: Map, in_size: int) -> Map:
+    b = m._bind(in_size=in_size) if m.__is_generic__ else m
+    if b.__is_generic__:
+        raise RuntimeError("Generic arguments could not be deduced from input data. You must explicitly cast.")
+    assert in_size == b.IN, f"input's last dimension ({in_size}) must match the map's IN ({b.IN})"
+    return b
+
+
+def _evaluate(m: Map, owner: Map, x):
+    dev = current_device()
+    xt = _device_tensor(x)
+    x2d = _as_rows(m, xt)
+    lead = list(xt.shape[:-1])
+    cache = owner.__dict__.setdefault("_out_cache", {})
+    key = (dev.index, tuple(lead), m.OUT)
+    out = cache.get(key)
+    if out is None:
+        out = RDVObject(torch.empty(lead + [m.OUT], dtype=torch.float32, device=dev))
+        cache[key] = out
+    plan = _plan_of(m, owner, dev)
     with _timed():
         run_chain(plan, x2d, out._tensor.view(-1, m.OUT), tail_exact=True)
+    return out
+
+
+def evaluate_into(m: Map, x, out: torch.Tensor) -> torch.Tensor:
+    """m(x) written into `out` (a [rows, OUT] fp32 view on the current
+    device, e.g. a slice of a larger buffer) instead of the map's cached
+    output object; the same launches and results as ``m(x)``. Used by the
+    sharded and host-streaming evaluators, which place each chunk's rows
+    straight into the final buffer."""
+    dev = current_device()
+    xt = _device_tensor(x)
+    b = _bound(m, xt.shape[-1])
+    x2d = _as_rows(b, xt)
+    y2d = out.view(-1, b.OUT)
+    if y2d.dtype != torch.float32 or y2d.device != dev or y2d.shape[0] != x2d.shape[0]:
+        raise ValueError(f"out must be a float32 [{x2d.shape[0]}, {b.OUT}] tensor on {dev}")
+    plan = _plan_of(b, m, dev)
+    with _timed():
+        run_chain(plan, x2d, y2d, tail_exact=True)
     return out

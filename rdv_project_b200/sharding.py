@@ -7,6 +7,12 @@ The reference has no multi-device execution at all; this is the B200
 scale-out of its data-parallel operators. Nothing here touches device
 memory of another GPU: each rank's kernels read only local tensors, and the
 exchange is a library collective.
+
+``sharded_map_overlapped`` is the pipelined form used for large batches: the
+rows are cut into slabs, every slab is split evenly over the ranks, and the
+all-gather of slab k runs (on NCCL's stream) while slab k + 1 computes.
+Given pinned host buffers it also streams its input in and its rows out on
+copy streams, overlapping PCIe with the kernels.
 """
 from __future__ import annotations
 
@@ -84,3 +90,178 @@ def sharded_render(renderer, pose9, width: int, height: int, group=None, **kw) -
     b, e = shard_range(height, world, rank)
     band = renderer.render(pose9, width, height, row_begin=b, row_end=e, **kw)
     return all_gather_rows(band, height, group=group)
+
+
+# ------------------------------------------------------------ overlapped form
+def slab_bounds(n: int, world: int, chunks: int, align: int = 128) -> list[tuple[int, int]]:
+    """[begin, end) global row ranges of the slabs of a pipelined sharded
+    map: `chunks` slabs (fewer when n is small) whose size is a multiple of
+    world * align, so that every rank's piece of every slab but the last is
+    the same whole number of `align`-row tiles."""
+    if n < 0 or world < 1 or chunks < 1 or align < 1:
+        raise ValueError("n >= 0, world >= 1, chunks >= 1 and align >= 1 are required")
+    if n == 0:
+        return []
+    unit = world * align
+    size = -(-n // chunks)
+    size = -(-size // unit) * unit
+    return [(b, min(n, b + size)) for b in range(0, n, size)]
+
+
+def piece_bounds(n: int, world: int, rank: int, chunks: int, align: int = 128) -> list[tuple[int, int]]:
+    """The global row ranges rank `rank` computes: its shard_range share of
+    every slab."""
+    out = []
+    for b, e in slab_bounds(n, world, chunks, align):
+        pb, pe = shard_range(e - b, world, rank)
+        out.append((b + pb, b + pe))
+    return out
+
+
+class _Ring:
+    """Device staging buffers (two, reused call after call) for pieces of a
+    host input, cached per (device, dtype, columns, rows)."""
+
+    _cache: dict = {}
+
+    @classmethod
+    def get(cls, dev, dtype, cols, rows):
+        key = (str(dev), dtype, cols, rows)
+        bufs = cls._cache.get(key)
+        if bufs is None:
+            bufs = [torch.empty(rows, cols, dtype=dtype, device=dev) for _ in range(2)]
+            cls._cache[key] = bufs
+        return bufs
+
+
+def _rank_world(group):
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return 0, 1
+
+
+def sharded_map_overlapped(m, x: torch.Tensor | None = None, *, group=None, out: torch.Tensor | None = None,
+                           chunks: int = 8, x_host: torch.Tensor | None = None,
+                           y_host: torch.Tensor | None = None, evaluate=None, reserve_ctas: int = 0,
+                           align: int = 128, shard: bool = True) -> torch.Tensor:
+    """Map `m` over n rows, split over the ranks of `group` (or this process
+    alone when no process group is initialised), every rank ending with the
+    full [n, OUT] result in `out`.
+
+    The rows are cut into `chunks` slabs (``slab_bounds``); each rank
+    evaluates its piece of slab k straight into `out` at the piece's global
+    rows, then starts an in-place all-gather of slab k (async, NCCL stream),
+    so the exchange of slab k overlaps the kernel of slab k + 1.
+
+    Input: `x`, the full [n, IN] batch on the device (a rank reads only its
+    pieces), or `x_host`, the full batch in (pinned) host memory: each rank
+    then copies its pieces in on a copy stream, one piece ahead of the
+    kernels, through two device staging buffers. `y_host` (pinned host
+    [n, OUT]), if given, receives the rows this rank computed, copied back on
+    a second copy stream as each piece finishes -- the union over ranks is
+    the whole result.
+
+    `reserve_ctas` leaves that many SMs free of the persistent MLP kernel
+    while the call runs (``rdvb_set_max_ctas``), so the all-gather's NCCL
+    kernels, which cannot share an SM with it, start at once.
+
+    `evaluate(x_piece, y_piece)` replaces the map evaluation (it must write
+    y_piece from x_piece); by default it is ``maps.evaluate_into(m, ...)``.
+    With ``shard=False`` the whole batch is this process's own (no split, no
+    exchange): the host-streaming pipeline alone.
+    """
+    import torch.distributed as dist
+
+    rank, world = _rank_world(group) if shard else (0, 1)
+    src = x if x is not None else x_host
+    if src is None:
+        raise ValueError("give x (device) or x_host (host) input rows")
+    n = src.shape[0]
+    if out is None:
+        raise ValueError("out ([n, OUT] on this rank's device) is required")
+    if out.shape[0] != n:
+        raise ValueError(f"out has {out.shape[0]} rows, the input {n}")
+    if y_host is not None and y_host.shape[0] != n:
+        raise ValueError(f"y_host has {y_host.shape[0]} rows, the input {n}")
+    if evaluate is None:
+        from .maps import evaluate_into
+
+        def evaluate(xs, ys):
+            evaluate_into(m, xs, ys)
+
+    cuda = out.device.type == "cuda"
+    slabs = slab_bounds(n, world, chunks, align)
+    pieces = piece_bounds(n, world, rank, chunks, align)
+    comp = torch.cuda.current_stream(out.device) if cuda else None
+    h2d = d2h = None
+    ring = None
+    free_ev = [None, None]
+    if x_host is not None and x is None:
+        rows_max = max((e - b for b, e in pieces), default=0)
+        if cuda:
+            h2d = torch.cuda.Stream(out.device)
+            ring = _Ring.get(out.device, x_host.dtype, x_host.shape[1], max(rows_max, 1))
+    if y_host is not None and cuda:
+        d2h = torch.cuda.Stream(out.device)
+    prev_cap = None
+    if cuda and reserve_ctas > 0 and world > 1:
+        from . import _native as N
+
+        sms = torch.cuda.get_device_properties(out.device).multi_processor_count
+        prev_cap = N.set_max_ctas(max(1, sms - reserve_ctas))
+    works = []
+    try:
+        for k, ((sb, se), (pb, pe)) in enumerate(zip(slabs, pieces)):
+            rows = pe - pb
+            # ---- input piece
+            if x is not None:
+                xs = x[pb:pe]
+            elif cuda:
+                buf = ring[k % 2][:rows]
+                with torch.cuda.stream(h2d):
+                    if free_ev[k % 2] is not None:
+                        h2d.wait_event(free_ev[k % 2])
+                    buf.copy_(x_host[pb:pe], non_blocking=True)
+                    ready = torch.cuda.Event()
+                    ready.record(h2d)
+                comp.wait_event(ready)
+                xs = buf
+            else:
+                xs = x_host[pb:pe]
+            # ---- kernel: the piece's rows straight into `out`
+            if rows:
+                evaluate(xs, out[pb:pe])
+            if cuda:
+                done = torch.cuda.Event()
+                done.record(comp)
+                if ring is not None:
+                    free_ev[k % 2] = done
+                if d2h is not None and rows:
+                    d2h.wait_event(done)
+                    with torch.cuda.stream(d2h):
+                        y_host[pb:pe].copy_(out[pb:pe], non_blocking=True)
+            elif y_host is not None and rows:
+                y_host[pb:pe].copy_(out[pb:pe])
+            # ---- exchange of the slab, in place
+            if world > 1:
+                if (se - sb) % world == 0:
+                    works.append(dist.all_gather_into_tensor(out[sb:se], out[pb:pe], group=group, async_op=True))
+                else:
+                    # ragged last slab: padded all-gather (pieces differ by a row)
+                    local = out[pb:pe].clone()
+                    all_gather_rows(local, se - sb, group=group, out=out[sb:se])
+    finally:
+        if prev_cap is not None:
+            from . import _native as N
+
+            N.set_max_ctas(prev_cap)
+    for w in works:
+        w.wait()
+    if cuda:
+        if d2h is not None:
+            comp.wait_stream(d2h)
+        if h2d is not None:
+            comp.wait_stream(h2d)
+    return out

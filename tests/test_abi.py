@@ -132,3 +132,43 @@ def test_volume_nodes_host_side():
     node = rdv.RatiotrackingTransmittance(ext, torch.ones(1, 1, 1, 1), density_scale=2.0)
     assert node.IN == 6 and node.OUT == 1 and node.density_scale == 2.0
     assert not hasattr(node, "step_size")
+
+
+def test_forward_path_reasons_without_a_device(lib):
+    """rdvb_mlp_forward_path names why a chain would run on the CUDA cores;
+    every case here is decided from the arguments alone."""
+    import rdv_project_b200._native as N
+
+    dims = N.int_array([3, 64, 64, 4])
+    f16 = N.int_array([N.RDVB_MATH_F16 | N.RDVB_LAYER_RELU] * 2 + [N.RDVB_MATH_F16])
+    good_x, good_p, good_y = 0x10000, 0x20000, 0x30000
+
+    def path(x, flags, packed, y, d=dims, n=3, rows=4096):
+        return lib.rdvb_mlp_forward_path(x, N.RDVB_F32, rows, n, d, flags, packed, y)
+
+    assert path(good_x, N.int_array([0, 0, 0]), good_p, good_y) == N.RDVB_PATH_CUDA_CORE
+    assert "fp32" in N.last_error()
+    mixed = N.int_array([N.RDVB_MATH_F16, N.RDVB_MATH_BF16, N.RDVB_MATH_F16])
+    assert path(good_x, mixed, good_p, good_y) == N.RDVB_PATH_CUDA_CORE and "mixes" in N.last_error()
+    assert path(good_x, f16, None, good_y) == N.RDVB_PATH_CUDA_CORE and "packed" in N.last_error()
+    assert path(good_x, f16, good_p + 16, good_y) == N.RDVB_PATH_CUDA_CORE and "256-byte" in N.last_error()
+    # x[1:] of a 3-wide fp32 tensor: 12 bytes past an aligned base
+    assert path(good_x + 12, f16, good_p, good_y) == N.RDVB_PATH_CUDA_CORE
+    assert "x is not 16-byte aligned" in N.last_error()
+    assert path(good_x, f16, good_p, good_y + 2) == N.RDVB_PATH_CUDA_CORE and "y is not" in N.last_error()
+    wide = N.int_array([3, 200, 4])
+    assert path(good_x, f16, good_p, good_y, d=wide, n=2) == N.RDVB_PATH_CUDA_CORE
+    assert "width above 128" in N.last_error()
+    assert path(good_x, f16, good_p, good_y, rows=31) == N.RDVB_PATH_CUDA_CORE and "32 rows" in N.last_error()
+    assert lib.rdvb_mlp_forward_path(good_x, 9, 4096, 3, dims, f16, good_p, good_y) == N.RDVB_ERR_INVALID_ARG
+
+
+def test_max_ctas_setting(lib):
+    import rdv_project_b200._native as N
+
+    assert lib.rdvb_get_max_ctas() == 0
+    assert N.set_max_ctas(100) == 0
+    assert lib.rdvb_get_max_ctas() == 100
+    assert N.set_max_ctas(0) == 100
+    assert lib.rdvb_set_max_ctas(-1) == N.RDVB_ERR_INVALID_ARG and "max_ctas" in N.last_error()
+    assert lib.rdvb_get_max_ctas() == 0
