@@ -8,10 +8,15 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "_build", "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_shaders.so")
-REFERENCE_ROOT = os.environ.get("RDV_REFERENCE_ROOT", "/root/reference")
+REF_COOPMAT_LIB = os.path.join(HERE, "_ref", "libref_coopmat.so")
+# The reference checkout: $RDV_REFERENCE_ROOT, else a checkout named
+# `reference` beside this repository.
+REFERENCE_ROOT = os.environ.get("RDV_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                      "reference")
 
 _oracle = None
 _ref = None
+_ref_cm = None
 
 
 def build_oracle(verbose: bool = False) -> None:
@@ -84,6 +89,31 @@ def ref_lib() -> ctypes.CDLL:
             getattr(lib, name).restype = None
         _ref = lib
     return _ref
+
+
+def ref_coopmat_lib() -> ctypes.CDLL:
+    """The reference's cooperative-matrix (float16) code paths executed on
+    the CPU (ref_shim/ref_coopmat.cpp)."""
+    global _ref_cm
+    if _ref_cm is None:
+        if not os.path.exists(REF_COOPMAT_LIB) and not ref_lib_available():
+            raise FileNotFoundError(
+                f"{REF_COOPMAT_LIB} is missing and the reference checkout is not present to build it")
+        lib = ctypes.CDLL(REF_COOPMAT_LIB)
+        vp, lg, i32 = ctypes.c_void_p, ctypes.c_long, ctypes.c_int
+        for name in ("ref_cm_mlp_c5", "ref_cm_mlp_c2"):
+            getattr(lib, name).argtypes = [vp, lg, vp, vp, vp]
+        for name in ("ref_cm_small_32_48", "ref_cm_small_64_32", "ref_cm_simple_32_64", "ref_cm_fast_32_64",
+                     "ref_cm_mine_32_48"):
+            getattr(lib, name).argtypes = [vp, i32, vp, vp, vp]
+        for name in ("ref_cm_winograd_16", "ref_cm_winograd_48"):
+            getattr(lib, name).argtypes = [vp, vp, vp, vp]
+        for name in ("ref_cm_mlp_c5", "ref_cm_mlp_c2", "ref_cm_small_32_48", "ref_cm_small_64_32",
+                     "ref_cm_simple_32_64", "ref_cm_fast_32_64", "ref_cm_mine_32_48", "ref_cm_winograd_16",
+                     "ref_cm_winograd_48"):
+            getattr(lib, name).restype = None
+        _ref_cm = lib
+    return _ref_cm
 
 
 def ptr(a) -> int:

@@ -14,6 +14,11 @@
  *       (_output[o] = _SH_Y[...] + bias[o], :97-98)
  *   bf16 operands: same as fp16 with bfloat16 staging (a B200 extension; the
  *       reference has no bf16 path)
+ *   bias first (flag bit 3): the accumulator starts from the bias and the
+ *       staged products are added to it in ascending k -- the order of
+ *       LinearTensorOpSmall / LinearTensorOpSimple, whose cooperative-matrix
+ *       accumulators are seeded with a stride-0 load of the bias
+ *       (tensors/linear_tensor_op_small.h:99, linear_tensor_op_simple.h)
  *   ReLU (maps/relu.h:1-5): max(x, 0) in fp32.
  *
  * LinearFast's workgroup fallback (linear_fast.h:44 / :102-108, and
@@ -32,6 +37,7 @@
 enum { ORACLE_MATH_F32 = 0, ORACLE_MATH_F16 = 1, ORACLE_MATH_BF16 = 2 };
 #define ORACLE_FLAG_MATH_MASK 3
 #define ORACLE_FLAG_RELU 4
+#define ORACLE_FLAG_BIAS_FIRST 8
 
 static float round_f16(float v) { return (float)(_Float16)v; }
 
@@ -86,12 +92,13 @@ void oracle_mlp_forward(const float* x, int64_t n_rows, int n_layers, const int*
                         c[o] = acc;
                     }
                 } else {
+                    const int bias_first = (flags[l] & ORACLE_FLAG_BIAS_FIRST) != 0;
                     for (int k = 0; k < IN; ++k) ws[k] = stage(a[k], math);
                     for (int o = 0; o < OUT; ++o) {
-                        float acc = 0.0f;
+                        float acc = bias_first ? b[l][o] : 0.0f;
                         for (int k = 0; k < IN; ++k)
                             acc += ws[k] * stage(W[l][(int64_t)o * IN + k], math);
-                        c[o] = acc + b[l][o];
+                        c[o] = bias_first ? acc : acc + b[l][o];
                     }
                 }
                 if (flags[l] & ORACLE_FLAG_RELU)

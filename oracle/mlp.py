@@ -10,7 +10,9 @@ bias added after)). A trailing partial 32-row workgroup runs exact fp32
 
 Layer description used throughout: a list of dicts
 ``{"W": [out, in] float32, "b": [out] float32, "math": "f32"|"f16"|"bf16",
-"relu": bool}``.
+"relu": bool}``, optionally ``"bias_first": True`` for the float16 layers of
+LinearTensorOpSmall / LinearTensorOpSimple, whose accumulators start from
+the bias (rdv/shaders/tensors/linear_tensor_op_small.h:99).
 """
 from __future__ import annotations
 
@@ -23,10 +25,12 @@ from ._clib import oracle_lib, ptr, ptr_array
 
 MATH_CODES = {"f32": 0, "f16": 1, "bf16": 2}
 FLAG_RELU = 4
+FLAG_BIAS_FIRST = 8
 
 
 def layer_flags(layers) -> np.ndarray:
-    return np.array([MATH_CODES[l["math"]] | (FLAG_RELU if l["relu"] else 0) for l in layers], dtype=np.int32)
+    return np.array([MATH_CODES[l["math"]] | (FLAG_RELU if l["relu"] else 0)
+                     | (FLAG_BIAS_FIRST if l.get("bias_first") else 0) for l in layers], dtype=np.int32)
 
 
 def mlp_forward(x: np.ndarray, layers, input_relu: bool = False, tail_exact: bool = False,

@@ -200,3 +200,39 @@ def conv3x3_winograd(x_nhwc: np.ndarray, w_33io: np.ndarray, bias: np.ndarray,
     Y = np.einsum("pi,nxyijd,qj->nxypqd", AT, M, AT)  # n, th, tw, m, m, cout
     Y = Y.transpose(0, 1, 3, 2, 4, 5).reshape(n, H, W, cout)
     return Y + np.asarray(bias, dtype=np.float64)
+
+
+def conv3x3_winograd_f23_ordered(x_nhwc: np.ndarray, u16: np.ndarray, bias: np.ndarray) -> np.ndarray:
+    """Conv2DTensorOpWinograd3x3.forward in the reference's own fp32
+    operation order (conv2d_tensor_op_winograd3x3.h:95-177), for the
+    reference's shapes (H and W even): per 2x2 tile the zero-padded 4x4
+    patch of every input channel, V = _winograd_fwd(patch) in fp32 staged
+    float16 (:123-137); per domain position p an fp32 accumulator from 0
+    with the float16 products V[c] * U[p][c][o] added in ascending c
+    (:140-161; each product is exact in fp32, each sum rounded); the 16
+    sums through _winograd_inv in fp32, then + bias (:164-174).
+
+    `u16` is the float16 filter image [16][CIN][COUT] (any float dtype
+    holding float16 values). Returns float32 NHWC."""
+    x = np.asarray(x_nhwc, dtype=np.float32)
+    n, H, W, cin = x.shape
+    assert H % 2 == 0 and W % 2 == 0
+    U = np.asarray(u16, dtype=np.float32).reshape(16, cin, -1)
+    cout = U.shape[2]
+    th, tw = H // 2, W // 2
+    xp = np.zeros((n, H + 2, W + 2, cin), dtype=np.float32)
+    xp[:, 1:H + 1, 1:W + 1, :] = x
+    idx_h = (np.arange(th) * 2)[:, None] + np.arange(4)[None, :]
+    idx_w = (np.arange(tw) * 2)[:, None] + np.arange(4)[None, :]
+    d = xp[:, idx_h][:, :, :, idx_w]                        # n, th, 4, tw, 4, cin
+    d = np.ascontiguousarray(d.transpose(0, 1, 3, 5, 2, 4))  # n, th, tw, cin, 4, 4
+    V = winograd_fwd_f23(d.reshape(-1, 16)).reshape(n * th * tw, cin, 16)
+    V = stage(V, "f16")
+    M = np.zeros((n * th * tw, 16, cout), dtype=np.float32)
+    for c in range(cin):
+        # M[t, p, o] += V[t, c, p] * U[p, c, o], one fp32 rounding per term
+        M += V[:, c, :, None] * U[None, :, c, :]
+    Mt = np.ascontiguousarray(M.transpose(0, 2, 1)).reshape(-1, 16)   # (tile, o) rows of 16 positions
+    Y = winograd_inv_f23(Mt).reshape(n, th, tw, cout, 2, 2)
+    Y = Y + np.asarray(bias, dtype=np.float32)[None, None, None, :, None, None]
+    return np.ascontiguousarray(Y.transpose(0, 1, 4, 2, 5, 3)).reshape(n, H, W, cout)

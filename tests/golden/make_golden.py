@@ -3,9 +3,10 @@
 Run where the reference checkout is present (its path: RDV_REFERENCE_ROOT, else
 the default in oracle/_clib.py):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py            # every fixture
+    python tests/golden/make_golden.py coopmat    # coopmat.npz only
 
-Two sources, both the reference's own code:
+Three sources, all the reference's own code:
 
 * ``oracle/_ref/libref_shaders.so`` -- the reference's scalar GLSL functions
   (maps/linear.h, relu.h, composite.h, tensors/linear_tensor_op.h,
@@ -13,11 +14,18 @@ Two sources, both the reference's own code:
   volumes/raymarching_transmittance_trait.h, libraries/random_library.h and
   volumes/ratiotracking_transmittance_trait.h) compiled as C++ from the
   reference checkout by ``make -C oracle ref``;
-* ``rdv/domain/nn.py``'s torch helper ``_winograd_transform_weight`` and its
-  ``_WINOGRAD_G`` table, executed from the reference source. The package
-  itself cannot be imported (it needs the external ``vk`` module at import
-  time), so the two definitions are lifted out of the file with ``ast`` and
-  executed on their own.
+* ``oracle/_ref/libref_coopmat.so`` -- the reference's cooperative-matrix
+  (float16 tensor-core) bodies: maps/linear_fast.h in Map chains of the
+  config-5 and config-2 architectures, tensors/linear_tensor_op_{small,
+  simple,fast,mine}.h and tensors/conv2d_tensor_op_winograd3x3.h, executed
+  on the CPU by 32-thread workgroups (oracle/ref_shim/coopmat_prelude.hpp
+  gives coopMatMulAdd its ascending-k fp32 summation);
+* ``rdv/domain/nn.py``'s torch helpers ``_winograd_transform_weight``,
+  ``_tile_weight_fp16`` and ``_cast_fp16`` and its ``_WINOGRAD_G`` table,
+  executed from the reference source. The package itself cannot be
+  imported (it needs the external ``vk`` module at import time), so these
+  definitions are lifted out of the file with ``ast`` and executed on
+  their own.
 
 The fixtures are small ``.npz`` files; the CPU tests compare the oracle's
 restatements against them, so they keep pinning the oracle where the
@@ -36,7 +44,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from oracle._clib import REFERENCE_ROOT, ptr, ptr_array, ref_lib  # noqa: E402
+from oracle._clib import REFERENCE_ROOT, ptr, ptr_array, ref_coopmat_lib, ref_lib  # noqa: E402
 
 
 def xavier_uniform(rng, out_f, in_f):
@@ -49,7 +57,7 @@ def reference_python_helpers():
     reference's nn.py in an isolated namespace."""
     path = os.path.join(REFERENCE_ROOT, "src", "rdv", "domain", "nn.py")
     tree = ast.parse(open(path).read(), filename=path)
-    wanted = {"_WINOGRAD_G", "_winograd_transform_weight"}
+    wanted = {"_WINOGRAD_G", "_winograd_transform_weight", "_tile_weight_fp16", "_cast_fp16"}
     body = []
     for node in tree.body:
         if isinstance(node, ast.FunctionDef) and node.name in wanted:
@@ -188,8 +196,80 @@ def main():
     np.savez_compressed(os.path.join(HERE, "ratiotracking.npz"), seeds=seeds, rng_index=rng_index,
                         rng_draws=rng_draws, media=media, x=rt_x, w=rt_w, d=rt_d, index=rt_index, grids=grids,
                         T=rt_T)
+    coopmat_goldens()
     print("golden fixtures written to", HERE)
 
 
+def _f16(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float16)).view(np.uint16)
+
+
+def coopmat_goldens():
+    """coopmat.npz: inputs, weights and outputs of the reference's float16
+    (cooperative-matrix) code paths. Float16 weight images are made by the
+    reference's own torch helpers."""
+    import torch
+
+    lib = ref_coopmat_lib()
+    ns = reference_python_helpers()
+    rng = np.random.default_rng(20261202)
+    out = {}
+
+    def kaiming(o, i):
+        return (rng.standard_normal((o, i)) * np.sqrt(2.0 / i)).astype(np.float32)
+
+    # Map chains: 3 full 32-row workgroups + a partial one (scalar fp32 path)
+    for name, dims, rows in (("c5", [3, 64, 64, 64, 64, 4], 112), ("c2", [32] + [128] * 8 + [16], 80)):
+        Ws = [kaiming(dims[i + 1], dims[i]) for i in range(len(dims) - 1)]
+        if name == "c2":
+            # multiples of 2^-7 stored as int8 codes, to keep the fixture
+            # small (exact in float16, so staged and fallback rows see the
+            # same weights)
+            Ws = [np.clip(np.round(w * 128.0), -127, 127).astype(np.float32) / 128.0 for w in Ws]
+        bs = [(rng.standard_normal(dims[i + 1]) * 0.1).astype(np.float32) for i in range(len(dims) - 1)]
+        x = (rng.uniform(-1, 1, (rows, dims[0])) if name == "c5" else rng.standard_normal((rows, dims[0])))
+        x = x.astype(np.float32)
+        y = np.zeros((rows, dims[-1]), np.float32)
+        getattr(lib, f"ref_cm_mlp_{name}")(ptr(x), rows, ptr_array(Ws), ptr_array(bs), ptr(y))
+        out[f"{name}_x"], out[f"{name}_y"] = x, y
+        for i, (w, b) in enumerate(zip(Ws, bs)):
+            out[f"{name}_W{i}"] = (w * 128.0).astype(np.int8) if name == "c2" else w
+            out[f"{name}_b{i}"] = b
+
+    # TensorOps
+    for name, inf, outf, batch, image in (("small_32_48", 32, 48, 64, "f32"), ("small_64_32", 64, 32, 64, "f32"),
+                                          ("simple_32_64", 32, 64, 64, "cast"), ("fast_32_64", 32, 64, 64, "tiled"),
+                                          ("mine_32_48", 32, 48, 64, "f32")):
+        x = rng.standard_normal((batch, inf)).astype(np.float32)
+        W = kaiming(outf, inf)
+        b = (rng.standard_normal(outf) * 0.1).astype(np.float32)
+        if image == "cast":
+            img = _f16(ns["_cast_fp16"](_TorchHolder(torch.from_numpy(W))).numpy())
+        elif image == "tiled":
+            img = _f16(ns["_tile_weight_fp16"](_TorchHolder(torch.from_numpy(W)), outf, inf).numpy())
+        else:
+            img = W
+        y = np.zeros((batch, outf), np.float32)
+        getattr(lib, f"ref_cm_{name}")(ptr(x), batch, ptr(img), ptr(b), ptr(y))
+        out.update({f"{name}_x": x, f"{name}_W": W, f"{name}_b": b, f"{name}_y": y})
+
+    # Conv2DTensorOpWinograd3x3, one 16x16 image
+    for c in (16, 48):
+        x = rng.standard_normal((16, 16, c)).astype(np.float32)
+        # float16 values (stored as float16)
+        w = (rng.standard_normal((3, 3, c, c)) * np.sqrt(2.0 / (9 * c))).astype(np.float16).astype(np.float32)
+        b = (rng.standard_normal(c) * 0.1).astype(np.float32)
+        U = ns["_winograd_transform_weight"](_TorchHolder(torch.from_numpy(w)), c, c).numpy()
+        U16 = _f16(U)
+        y = np.zeros((256, c), np.float32)
+        getattr(lib, f"ref_cm_winograd_{c}")(ptr(np.ascontiguousarray(x.reshape(256, c))), ptr(U16), ptr(b), ptr(y))
+        out.update({f"wino{c}_x": x, f"wino{c}_w": w.astype(np.float16), f"wino{c}_b": b,
+                    f"wino{c}_y": y.reshape(16, 16, c)})
+    np.savez_compressed(os.path.join(HERE, "coopmat.npz"), **out)
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["coopmat"]:
+        coopmat_goldens()
+    else:
+        main()

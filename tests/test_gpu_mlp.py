@@ -231,3 +231,36 @@ def test_profiling_accumulates_device_time(rdv, cuda_device):
     finally:
         rdv.profiling(False)
     assert rdv.profiling_submit_times() > 0.0
+
+
+# ---------------------------------------------------------------------------
+# Against the reference's own float16 (cooperative-matrix) bodies executed on
+# the CPU (tests/golden/coopmat.npz, see tests/golden/make_golden.py): the
+# oracle restatements reproduce those outputs bit for bit
+# (tests/test_oracle_golden.py); the tensor-core kernels must meet them within
+# the float16 tolerance and the tight bound.
+def _cm_layers(g, name):
+    n = len([k for k in g if k.startswith(f"{name}_W")])
+    Ws = [g[f"{name}_W{i}"] for i in range(n)]
+    Ws = [w.astype(np.float32) / 128.0 if w.dtype == np.int8 else w for w in Ws]
+    return [{"W": Ws[i], "b": g[f"{name}_b{i}"], "math": "f16", "relu": i < n - 1} for i in range(n)]
+
+
+@pytest.mark.parametrize("name", ["c5", "c2"])
+def test_linearfast_chain_vs_reference_coopmat(rdv, cuda_device, golden, name):
+    g = golden("coopmat.npz")
+    m = _build(rdv, _cm_layers(g, name), cuda_device)
+    y = m(rdv.wrap(torch.from_numpy(g[f"{name}_x"]).to(cuda_device))).as_tensor("torch").cpu().numpy()
+    _check(y, g[f"{name}_y"], TOL_F16, TIGHT_F16)
+    # the partial 32-row workgroup ran in exact fp32, as the reference's did
+    full = (y.shape[0] // 32) * 32
+    _check(y[full:], g[f"{name}_y"][full:], TOL_F32)
+
+
+@pytest.mark.parametrize("cls_name,key", [("LinearTensorOpSmall", "small_32_48"), ("LinearTensorOpSmall", "small_64_32"),
+                                          ("LinearTensorOpSimple", "simple_32_64"),
+                                          ("LinearTensorOpFast", "fast_32_64"), ("LinearTensorOpMine", "mine_32_48")])
+def test_fp16_tensor_ops_vs_reference_coopmat(rdv, cuda_device, golden, cls_name, key):
+    g = golden("coopmat.npz")
+    op = getattr(rdv, cls_name)(*(torch.from_numpy(g[f"{key}_{t}"]).to(cuda_device) for t in ("x", "W", "b")))
+    _check(op.as_type("torch").cpu().numpy(), g[f"{key}_y"], TOL_F16, TIGHT_F16)

@@ -224,3 +224,18 @@ def test_tma_fed_kernel_equals_global_load_kernel(rdv, cuda_device, monkeypatch,
     if n * h * wd <= 20000:
         _check(y_tma.cpu().numpy(), _oracle_staged(x, w, b), TIGHT)
     assert rdv.device_status() == 0
+
+
+@pytest.mark.parametrize("c", [16, 48])
+def test_reference_winograd_op_vs_reference_coopmat(rdv, cuda_device, golden, c):
+    """Conv2DTensorOpWinograd3x3 against the reference's own
+    cooperative-matrix body executed on the CPU (tests/golden/coopmat.npz):
+    same float16 staging of U and V, so only the fp32 summation order
+    differs -- within the tight Winograd bound."""
+    g = golden("coopmat.npz")
+    x = torch.from_numpy(g[f"wino{c}_x"].reshape(256, c))
+    w = torch.from_numpy(g[f"wino{c}_w"].astype(np.float32))
+    b = torch.from_numpy(g[f"wino{c}_b"])
+    op = rdv.Conv2DTensorOpWinograd3x3(x, w, b, 16, 16)
+    y = op.as_type("torch").cpu().numpy().reshape(16, 16, c)
+    _check(y, g[f"wino{c}_y"], TIGHT)

@@ -205,3 +205,92 @@ def test_tensor_sampler_restatement_matches_torch_grid_sample(in_dim, clamp, ali
                         padding_mode="border" if clamp else "zeros", align_corners=aligned)
     ref = ref.reshape(t.shape[-1], 500).T.numpy()
     np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+
+
+# ---------------------------------------------------------------------------
+# The float16 (cooperative-matrix) paths: tests/golden/coopmat.npz holds the
+# outputs of the reference's own coopmat bodies executed on the CPU
+# (oracle/ref_shim/ref_coopmat.cpp; coopMatMulAdd sums in ascending k in
+# fp32). The restatements must reproduce them bit for bit.
+def _cm_chain(g, name):
+    n = len([k for k in g if k.startswith(f"{name}_W")])
+    Ws = [g[f"{name}_W{i}"] for i in range(n)]
+    Ws = [w.astype(np.float32) / 128.0 if w.dtype == np.int8 else w for w in Ws]
+    return [{"W": Ws[i], "b": g[f"{name}_b{i}"], "math": "f16", "relu": i < n - 1} for i in range(n)]
+
+
+@pytest.mark.parametrize("name", ["c5", "c2"])
+def test_linear_fast_chain_bit_exact_vs_reference_coopmat(golden, name):
+    """LinearFast >> relu >> ... (maps/linear_fast.h:39-98 through
+    cooperative_library.h's gate): float16 staging, fp32 sums from 0, bias
+    after; the trailing partial workgroup in exact fp32."""
+    g = golden("coopmat.npz")
+    layers = _cm_chain(g, name)
+    x = g[f"{name}_x"]
+    assert x.shape[0] % 32 != 0  # the fixture includes a partial workgroup
+    y = omlp.mlp_forward(x, layers, tail_exact=True)
+    np.testing.assert_array_equal(y, g[f"{name}_y"])
+    # without the tail rule the partial workgroup's rows differ (they are the
+    # reference's scalar fp32 rows), the full workgroups' do not
+    full = (x.shape[0] // 32) * 32
+    y2 = omlp.mlp_forward(x, layers, tail_exact=False)
+    np.testing.assert_array_equal(y2[:full], g[f"{name}_y"][:full])
+    assert not np.array_equal(y2[full:], g[f"{name}_y"][full:])
+
+
+@pytest.mark.parametrize("name,bias_first", [("small_32_48", True), ("small_64_32", True), ("simple_32_64", True),
+                                             ("fast_32_64", False), ("mine_32_48", False)])
+def test_linear_tensor_ops_bit_exact_vs_reference_coopmat(golden, name, bias_first):
+    """LinearTensorOpSmall/Simple seed their accumulators with the bias
+    (linear_tensor_op_small.h:99, linear_tensor_op_simple.h); Fast/Mine add
+    it after (linear_tensor_op_fast.h, linear_tensor_op_mine.h)."""
+    g = golden("coopmat.npz")
+    layer = {"W": g[f"{name}_W"], "b": g[f"{name}_b"], "math": "f16", "relu": False, "bias_first": bias_first}
+    y = omlp.mlp_forward(g[f"{name}_x"], [layer])
+    np.testing.assert_array_equal(y, g[f"{name}_y"])
+    # the other order is a different (fp32-rounding-level) result
+    other = dict(layer, bias_first=not bias_first)
+    y2 = omlp.mlp_forward(g[f"{name}_x"], [other])
+    assert not np.array_equal(y2, g[f"{name}_y"])
+    assert omlp.within_tolerance(y2, g[f"{name}_y"], 1e-6)
+
+
+@pytest.mark.parametrize("c", [16, 48])
+def test_winograd_op_bit_exact_vs_reference_coopmat(golden, c):
+    """Conv2DTensorOpWinograd3x3.forward (conv2d_tensor_op_winograd3x3.h:
+    95-177) with the float16 filter image of the reference's own
+    _winograd_transform_weight: the ordered fp32 restatement reproduces it
+    bit for bit, the float64-GEMM restatement within 1e-6."""
+    g = golden("coopmat.npz")
+    x, w, b = g[f"wino{c}_x"][None], g[f"wino{c}_w"].astype(np.float32), g[f"wino{c}_b"]
+    U = owg.filter_transform(w, "F2x2")
+    y = owg.conv3x3_winograd_f23_ordered(x, U, b)[0]
+    np.testing.assert_array_equal(y, g[f"wino{c}_y"])
+    y64 = owg.conv3x3_winograd(x, w, b, "F2x2", staged=True)[0]
+    assert omlp.within_tolerance(y64, g[f"wino{c}_y"], 1e-6)
+    # and the float16 Winograd is within the BASELINE fp16 tolerance of the direct convolution
+    assert omlp.within_tolerance(g[f"wino{c}_y"], owg.conv3x3_direct(x, w, b)[0], 1e-2)
+
+
+def test_live_reference_coopmat_library_agrees_with_fixture(golden):
+    """Where the reference checkout is present, its coopmat bodies rerun on
+    the fixture's inputs give the stored outputs."""
+    if not ref_lib_available():
+        pytest.skip("reference checkout not present")
+    from oracle._clib import ptr, ptr_array, ref_coopmat_lib
+
+    g = golden("coopmat.npz")
+    lib = ref_coopmat_lib()
+    for name in ("c5", "c2"):
+        layers = _cm_chain(g, name)
+        x = g[f"{name}_x"]
+        y = np.zeros_like(g[f"{name}_y"])
+        Ws = [np.ascontiguousarray(l["W"], dtype=np.float32) for l in layers]
+        bs = [np.ascontiguousarray(l["b"]) for l in layers]
+        getattr(lib, f"ref_cm_mlp_{name}")(ptr(x), x.shape[0], ptr_array(Ws), ptr_array(bs), ptr(y))
+        np.testing.assert_array_equal(y, g[f"{name}_y"])
+    x, b = g["small_64_32_x"], g["small_64_32_b"]
+    W = np.ascontiguousarray(g["small_64_32_W"])
+    y = np.zeros_like(g["small_64_32_y"])
+    lib.ref_cm_small_64_32(ptr(x), x.shape[0], ptr(W), ptr(b), ptr(y))
+    np.testing.assert_array_equal(y, g["small_64_32_y"])
