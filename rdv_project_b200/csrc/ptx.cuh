@@ -220,17 +220,19 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (f16 or bf16 inputs,
-// f32 accumulate), issued by one thread. No "memory" clobber: the operands
-// are ordered by the mbarrier waits and tcgen05 fences around the issue, and
-// a clobber would stop the compiler from scheduling descriptor arithmetic
-// around the (volatile, so still in-order) MMA instructions.
+// f32 accumulate), issued by one thread; only a tcgen05.commit from that same
+// thread tracks it (a commit from another lane arrives at once). The MMA
+// reads shared memory and TMEM written by other threads and by bulk copies,
+// so it carries a "memory" clobber: no load or store of the issuing thread
+// moves across it, whatever the surrounding code.
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
 // Same with the A operand read from tensor memory (M=128 rows = lanes, 16-bit
@@ -241,7 +243,8 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
 // Arrive once on `bar` when every previously issued tcgen05 op of this
@@ -260,12 +263,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
 // The registers of a tcgen05.ld hold the data only after tcgen05.wait::ld,
-// but the compiler sees them defined at the load. These forms make the wait
-// (or an empty statement placed after it) redefine the registers, so no use
-// of them can be scheduled between the load and the wait.
+// but the compiler sees them defined at the load, and a wait with only a
+// "memory" clobber does not stop it from scheduling arithmetic on them
+// before the wait (register uses are not memory accesses). So the only wait
+// offered here redefines the loaded registers (and reg_barrier, placed
+// after it, those of a second load waited on by the same instruction): no
+// use of them can move above the wait.
 __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),

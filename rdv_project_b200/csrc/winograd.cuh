@@ -263,7 +263,7 @@ __device__ __forceinline__ void store_block(const Params& p, int t, bool valid, 
     for (int q = 0; q < 4; ++q) {
         uint32_t r[16];
         tmem_ld16(td + static_cast<uint32_t>(q * kMaxChannels), r);
-        tmem_wait_ld();
+        tmem_wait_ld(r);
         const int oh = 2 * ty + (q >> 1), ow = 2 * tx + (q & 1);
         if (!valid || oh >= p.h || ow >= p.w) continue;  // past the end; odd h or w
         const long long o = ((static_cast<long long>(img) * p.h + oh) * p.w + ow) * p.cout + 16 * grp;
@@ -559,7 +559,7 @@ __device__ __forceinline__ void store_block_tma(const TmaParams& p, int img, int
     for (int q = 0; q < 4; ++q) {
         uint32_t r[16];
         tmem_ld16(td + static_cast<uint32_t>(q * kMaxChannels), r);
-        tmem_wait_ld();
+        tmem_wait_ld(r);
         const int oh = 2 * ty + (q >> 1), ow = 2 * tx + (q & 1);
         if (!in_block || oh >= p.h || ow >= p.w) continue;
         const long long o = ((static_cast<long long>(img) * p.h + oh) * p.w + ow) * p.cout + 16 * grp;
