@@ -3,8 +3,11 @@
 run as one fused kernel launch, and must give bit for bit the results of
 dispatching the ops one by one (the eager dispatch every op does at
 construction). Ops inside a fused run materialise on first use."""
+import numpy as np
 import pytest
 import torch
+
+from oracle import mlp as omlp
 
 pytestmark = pytest.mark.gpu
 
@@ -56,6 +59,19 @@ def test_fused_chain_equals_per_op_dispatch(rdv, cuda_device, kinds):
     for op, ref in zip(ops[:-1], ref_ops[:-1]):
         assert torch.equal(op.as_type("torch"), ref.as_type("torch"))
         assert not op._stale
+    # and the fused result meets the oracle (each op's own arithmetic:
+    # float16 staging for the coopmat ops, with the bias first for Small and
+    # Simple; exact fp32 for LinearTensorOp)
+    dims = [32, 64, 64, 16]
+    layers = []
+    for i, cls in enumerate(kinds):
+        W, b = _w(dims[i + 1], dims[i], 100 + i)
+        layers.append({"W": W.numpy(), "b": b.numpy(), "math": "f32" if cls == "LinearTensorOp" else "f16",
+                       "relu": i < len(kinds) - 1, "bias_first": cls in ("LinearTensorOpSmall", "LinearTensorOpSimple")})
+    ref = omlp.mlp_forward(x.cpu().numpy(), layers)
+    tol = 1e-5 if all(k == "LinearTensorOp" for k in kinds) else 2e-3
+    nw, el = omlp.rel_errors(got.cpu().numpy(), ref)
+    assert nw <= tol and el <= tol, (nw, el)
 
 
 def test_mixed_precision_pipeline_is_not_fused_across_arithmetics(rdv, cuda_device):

@@ -155,14 +155,20 @@ def test_evaluate_chain_sees_in_place_input_edit(rdv, cuda_device):
 
 def test_config3_full_size_vs_direct(rdv, cuda_device):
     # x [8, 256, 256, 64] float16 ~N(0,1), Kaiming-normal
-    # weights, zero bias, fp32 output; compared against a direct convolution
-    # (here the on-device fp32 one, itself checked against the oracle above)
+    # weights, zero bias, fp32 output; compared against a direct convolution:
+    # the oracle's float64 one (conv2d_tensor_op.h:21-87 semantics) on output
+    # rows 0-31 of images 0 and 7, and the on-device fp32 one on every pixel
     g = torch.Generator().manual_seed(0)
-    x = torch.randn((8, 256, 256, 64), generator=g).half().to(cuda_device)
+    x_host = torch.randn((8, 256, 256, 64), generator=g).half()
+    x = x_host.to(cuda_device)
     w = torch.randn((64, 64, 3, 3), generator=torch.Generator().manual_seed(1000)) * np.sqrt(2.0 / 576)
     w33io = w.permute(2, 3, 1, 0).contiguous()
     conv = rdv.Conv3x3Winograd(w33io, torch.zeros(64))
     y = conv(x)
+    y_host = y.cpu().numpy()
+    for img in (0, 7):
+        band = owg.conv3x3_direct(x_host[img:img + 1, :33].float().numpy(), w33io.numpy(), np.zeros(64))[0, :32]
+        _check(y_host[img, :32], band, TOL_F16)
     ref = rdv.conv2d_direct(x, w33io, torch.zeros(64))
     torch.cuda.synchronize()
     d = (y.double() - ref.double()).abs()
