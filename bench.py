@@ -475,6 +475,7 @@ def secondary_summaries(args, local, headline):
     out["c4"] = run_c4(args, 1, 0, local, summary=True)
     out["trm"] = run_trm(args, 1, 0, local, summary=True)
     out["rt"] = ratiotracking_summary()
+    out["pbvr"] = pbvr_summary()
     out["chain"] = chain_summary()
     out["conv_tc"] = conv_family_summary()
     return out
@@ -996,6 +997,64 @@ def ratiotracking_summary(steps=3):
     el = time.perf_counter() - t0
     return {"value": _r(evals / t), "unit": "evaluations/s", "ms": _r(t * 1e3), "rays_per_s": _r(rays.shape[0] / t),
             "frac_fp32_nominal": _r(flop / t / 1e12 / nominal, 3), "cpu": _r(ev_cpu / el)}
+
+
+def sphere_from_voxel(g):
+    """A SphereMajorantField grid [D, H, W, 2] from a voxel majorant grid
+    [D, H, W]: radius 1.5 voxels, the majorant the largest voxel majorant of
+    the 3x3x3 neighbourhood (edge-clamped)."""
+    p = np.pad(g, 1, mode="edge")
+    D, H, W = g.shape
+    m = np.full_like(g, -np.inf)
+    for a in range(3):
+        for b in range(3):
+            for c in range(3):
+                m = np.maximum(m, p[a:a + D, b:b + H, c:c + W])
+    return np.stack([m, np.full_like(m, 1.5)], -1).astype(np.float32)
+
+
+def pbvr_summary(steps=3):
+    """PBVR over the config-4 camera's rays (1920x1080, orbit pose 0): the
+    transmittance workload's extinction chain, its 16^3 voxel majorant (and
+    a sphere field built from it, radius 1.5 voxels), a constant
+    environment, albedo 0.8, g = 0.3, at most 8 bounces, fixed seeds;
+    CUDA-core kernel, one thread per path. The oracle restatement on 8,192
+    middle rays is the CPU figure."""
+    import rdv_project_b200 as rdv
+    from oracle import raymarch as orm
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = trm_layers()
+    grid, lay_np = trm_majorant(layers)
+    ext = build_map(rdv, layers, dev)
+    env = rdv.Constant([0.8, 0.9, 1.0])
+    kw = dict(albedo=(0.8, 0.8, 0.8), g=0.3, max_bounces=8)
+    node = rdv.PBVR(ext, env, grid.to(dev), **kw)
+    sph = sphere_from_voxel(grid.numpy()[..., 0])
+    node_s = rdv.PBVR(ext, env, rdv.SphereMajorantField(torch.from_numpy(sph).to(dev)), **kw)
+    rays = trm_rays().to(dev)
+    seeds = (1234567, 7654321, 1357911, 2468024)
+    res = {}
+    for name, nd in (("voxel", node), ("sphere", node_s)):
+        for _ in range(2):
+            nd(rays, seeds=seeds)
+        torch.cuda.synchronize()
+        res[name] = (time_steps(lambda: nd(rays, seeds=seeds), steps) / steps, nd.last_evaluations())
+    t, evals = res["voxel"]
+    flop = trm_flop() * evals
+    nominal = 148 * 128 * 2 * 1.965e9 / 1e12
+    n_cpu = 8192
+    mid = (TRM["height"] // 2) * TRM["width"]
+    sample = trm_rays()[mid:mid + n_cpu].numpy()
+    t0 = time.perf_counter()
+    _, ev_cpu = orm.pbvr(sample[:, :3], sample[:, 3:], orm.mlp_extinction(lay_np),
+                         orm.constant_environment([0.8, 0.9, 1.0]),
+                         lambda x, w: orm.voxel_majorant(grid.numpy()[..., 0], x, w), seeds,
+                         index=np.arange(mid, mid + n_cpu), return_evaluations=True, **kw)
+    el = time.perf_counter() - t0
+    return {"value": _r(evals / t), "unit": "evaluations/s", "ms": _r(t * 1e3), "rays_per_s": _r(rays.shape[0] / t),
+            "frac_fp32_nominal": _r(flop / t / 1e12 / nominal, 3), "sphere_ms": _r(res["sphere"][0] * 1e3),
+            "sphere_evals": int(res["sphere"][1]), "cpu": _r(ev_cpu / el)}
 
 
 def chain_summary(rows=1 << 20, steps=3):

@@ -48,6 +48,17 @@ extern "C" {
 #define RDVB_WINOGRAD_F2X2 0 /* F(2x2,3x3), the reference's algorithm */
 #define RDVB_WINOGRAD_F4X4 1 /* F(4x4,3x3), B200 extension */
 
+/* Majorant fields of the ray trackers (rdv/domain/volumes.py:172-242). */
+#define RDVB_MAJORANT_VOXEL 0  /* VoxelMajorantField: grid [D, H, W] of majorants */
+#define RDVB_MAJORANT_SPHERE 1 /* SphereMajorantField: grid [D, H, W, 2] of (majorant, radius in voxels) */
+
+/* PBVR environments and the 2-D sampler flags of an equirectangular one. */
+#define RDVB_ENV_CONSTANT 0 /* a Constant map: one RGB radiance for every direction */
+#define RDVB_ENV_EQUIRECT 1 /* XRProject() >> TensorSampler(image [H, W, 3]) */
+#define RDVB_SAMPLER_CLAMP 1
+#define RDVB_SAMPLER_ALIGNED 2
+#define RDVB_SAMPLER_LINEAR 4
+
 /* Library version (major*10000 + minor*100 + patch). */
 int rdvb_version(void);
 
@@ -352,7 +363,8 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
 /* RatiotrackingTransmittance (rdv/domain/volumes.py:144-170;
  * rdv/shaders/volumes/ratiotracking_transmittance.h and
  * ratiotracking_transmittance_trait.h) with a VoxelMajorantField
- * (volumes.py:196-212, rdv/shaders/volumes/voxel_majorant_field.h):
+ * (volumes.py:196-212, rdv/shaders/volumes/voxel_majorant_field.h) or a
+ * SphereMajorantField (volumes.py:215-224, sphere_majorant_field.h):
  * out[i] = the ratio-tracking estimate of the transmittance along ray i of
  * rays [n_rays, 6]. Object space, box clip and misses as
  * rdvb_transmittance_rm; then from the entry point, at most 1024 times while
@@ -360,9 +372,13 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
  * -log(1 - random()) / (majorant * density_scale)); on a collision inside the
  * cell T *= 1 - extinction(x) / majorant, and below 0.05 Russian roulette
  * (random() >= T gives 0, else T = 1).
- * majorant: fp32 device grid [D, H, W] (z, y, x; the Grid[3, 1]'s tensor
- * without its channel), majorant_dims = {D, H, W} (host); the cell of x is
- * clamp(int((x * 0.5 + 0.5) * (W, H, D)), 0, dims - 1).
+ * majorant: fp32 device grid, majorant_dims = {D, H, W} (host); the cell of
+ * x is clamp(int((x * 0.5 + 0.5) * (W, H, D)), 0, dims - 1).
+ * majorant_kind RDVB_MAJORANT_VOXEL: grid [D, H, W] (z, y, x; the
+ * Grid[3, 1]'s tensor without its channel); the cell's majorant, up to the
+ * cell's exit. RDVB_MAJORANT_SPHERE: grid [D, H, W, 2] of (majorant, radius
+ * r in voxels; 8-byte aligned); the majorant up to the exit of the box of
+ * half-width r voxels around the cell's centre, at least 1e-6 ahead.
  * seeds: 4 host uint32, the dispatch's generator seeds (the reference draws
  * them per dispatch, core/_common.py:66-75); ray i draws from the seeds
  * spawned by index i (libraries/random_library.h:44-49, :256-268), the
@@ -375,10 +391,47 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
  * bytes, 256-byte aligned; bytes 8-15 hold the number of extinction
  * evaluations of the call. */
 int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
-                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int draws_before,
-                          int n_layers, const int* dims, const float* const* weights, const float* const* biases,
-                          const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, float* out,
-                          void* stream);
+                          const float* majorant, const int* majorant_dims, int majorant_kind, const uint32_t* seeds,
+                          int draws_before, int n_layers, const int* dims, const float* const* weights,
+                          const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+                          size_t workspace_bytes, float* out, void* stream);
+
+/* XRProject (rdv/domain/rendering.py:150-160, rdv/shaders/rendering/
+ * xr_project.h): out[i] = dir2xr(dirs[i]) = (atan(w.x, w.z) / pi,
+ * asin(clamp(w.y, -1, 1)) * 2 / pi) for dirs [n, 3] -> out [n, 2] (fp32
+ * device; math_library.h:265-276, w.x nudged by 1e-7 when w.x = w.z = 0). */
+int rdvb_xr_project(const float* dirs, int64_t n, float* out, void* stream);
+
+/* PBVR (rdv/domain/volumes.py:257-326, rdv/shaders/volumes/pbvr.h):
+ * out[i] (RGB, [n_rays, 3] fp32 device) = one delta-tracking path sample of
+ * the radiance arriving along ray i of rays [n_rays, 6] -- unbiased, to be
+ * averaged over dispatches. Object space and box clip as
+ * rdvb_transmittance_rm; a ray that misses the box returns
+ * environment(w). Then at most 8192 times while the segment lasts: the
+ * field's (majorant, max step) at (x, w_object) -- majorant floored at
+ * 1e-12 and NOT scaled (PBVR has no density scale) --, a free flight
+ * -log(1 - random()) / majorant, clipped to the max step and the segment;
+ * a clipped flight that used up the segment escapes, any other starts a new
+ * cell; at a tentative collision random() >= extinction(x) / majorant is a
+ * null collision, else a real one: throughput *= albedo (3 host floats),
+ * the path ends with 0 below 1e-4 or after max_bounces real collisions, else
+ * w <- Henyey-Greenstein sample around w with anisotropy g
+ * (random_library.h:224-239; two draws: azimuth, then cosine) and the
+ * segment restarts at x up to the box exit. An escaped path returns
+ * throughput * environment(w), a path out of iterations 0.
+ * Environment: env_kind RDVB_ENV_CONSTANT (env_rgb: 3 host floats) or
+ * RDVB_ENV_EQUIRECT (env_image: fp32 device [H, W, 3], env_dims = {H, W}
+ * host, env_flags a mask of RDVB_SAMPLER_*), looked up at
+ * (atan(w.x, w.z) / pi, asin(w.y) * 2 / pi) as XRProject() >>
+ * TensorSampler (math_library.h:265-276, tensor_sampler.h).
+ * Majorant field, generator (seeds, draws_before), extinction chain and
+ * workspace as rdvb_transmittance_rt (bytes 8-15: extinction evaluations). */
+int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const float* majorant,
+              const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
+              int env_kind, const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
+              const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
+              const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+              size_t workspace_bytes, float* out, void* stream);
 
 #ifdef __cplusplus
 }

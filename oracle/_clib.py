@@ -9,6 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "_build", "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_shaders.so")
 REF_COOPMAT_LIB = os.path.join(HERE, "_ref", "libref_coopmat.so")
+REF_PBVR_LIB = os.path.join(HERE, "_ref", "libref_pbvr.so")
 # The reference checkout: $RDV_REFERENCE_ROOT, else a checkout named
 # `reference` beside this repository.
 REFERENCE_ROOT = os.environ.get("RDV_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
@@ -17,6 +18,7 @@ REFERENCE_ROOT = os.environ.get("RDV_REFERENCE_ROOT") or os.path.join(os.path.di
 _oracle = None
 _ref = None
 _ref_cm = None
+_ref_pbvr = None
 
 
 def build_oracle(verbose: bool = False) -> None:
@@ -114,6 +116,24 @@ def ref_coopmat_lib() -> ctypes.CDLL:
             getattr(lib, name).restype = None
         _ref_cm = lib
     return _ref_cm
+
+
+def ref_pbvr_lib() -> ctypes.CDLL:
+    """The reference's PBVR body and Henyey-Greenstein sampler compiled as
+    C++ (ref_shim/ref_pbvr.cpp)."""
+    global _ref_pbvr
+    if _ref_pbvr is None:
+        if not os.path.exists(REF_PBVR_LIB) and not ref_lib_available():
+            raise FileNotFoundError(
+                f"{REF_PBVR_LIB} is missing and the reference checkout is not present to build it")
+        lib = ctypes.CDLL(REF_PBVR_LIB)
+        vp, lg, i32, f32 = ctypes.c_void_p, ctypes.c_long, ctypes.c_int, ctypes.c_float
+        lib.ref_pbvr.argtypes = [f32, f32, i32, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp, lg, vp]
+        lib.ref_pbvr.restype = None
+        lib.ref_hg_phase_sample.argtypes = [vp, i32, i32, vp, f32, vp]
+        lib.ref_hg_phase_sample.restype = None
+        _ref_pbvr = lib
+    return _ref_pbvr
 
 
 def ptr(a) -> int:

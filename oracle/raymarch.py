@@ -395,3 +395,239 @@ def ratiotracking_transmittance(origins, dirs, density_scale, extinction, grid, 
     if return_evaluations:
         return out, int(counts.sum())
     return out
+
+
+# ---------------------------------------------------------------------------
+# PBVR (rdv/domain/volumes.py:257-326, rdv/shaders/volumes/pbvr.h)
+# ---------------------------------------------------------------------------
+_PI = np.float32(3.14159265358979323846)
+_INV_PI = np.float32(0.31830988618379067153776752674503)
+
+
+def _glsl_min(a, b):
+    """GLSL min(a, b) = b < a ? b : a (elementwise, float32)."""
+    return np.where(b < a, b, a).astype(np.float32)
+
+
+def _glsl_max(a, b):
+    """GLSL max(a, b) = a < b ? b : a (elementwise, float32)."""
+    return np.where(a < b, b, a).astype(np.float32)
+
+
+def _f32(fn, v):
+    """A float32 math function, correctly rounded (evaluated in float64)."""
+    return fn(np.asarray(v, dtype=np.float64)).astype(np.float32)
+
+
+def sphere_majorant(grid: np.ndarray, x: np.ndarray, w: np.ndarray):
+    """SphereMajorantField.forward (rdv/shaders/volumes/sphere_majorant_field.h):
+    grid [D, H, W, 2] (z, y, x; majorant, radius in voxels) float32; x, w
+    [R, 3] object space. Returns the cell's majorant and the distance along
+    w to the exit of the box of half-width radius voxels around the cell's
+    centre, at least 1e-6."""
+    dims = np.array([grid.shape[2], grid.shape[1], grid.shape[0]], dtype=np.int64)
+    f = dims.astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        pos = (x * np.float32(0.5) + np.float32(0.5)) * f
+        cell = np.clip(np.trunc(pos).astype(np.int64), 0, dims - 1)
+        value = grid[cell[:, 2], cell[:, 1], cell[:, 0]]
+        maj = value[:, 0].astype(np.float32)
+        radius = value[:, 1].astype(np.float32)
+        vs = np.float32(2.0) / f
+        center = (cell.astype(np.float32) + np.float32(0.5)) * vs - np.float32(1.0)
+        half = radius[:, None] * vs
+        t0 = ((center - half) - x) / w
+        t1 = ((center + half) - x) / w
+        texit = _glsl_max(t0, t1)
+        dist = _glsl_min(_glsl_min(texit[:, 0], texit[:, 1]), texit[:, 2])
+        dist = _glsl_max(dist, np.float32(1e-6))
+    return maj, dist
+
+
+def dir2xr(w: np.ndarray) -> np.ndarray:
+    """dir2xr (rdv/shaders/libraries/math_library.h:265-276) in float32:
+    (atan(w.x, w.z) / pi, asin(clamp(w.y, -1, 1)) * 2 / pi), w.x += 1e-7
+    where w.x = w.z = 0 (and += 0 elsewhere, which turns -0 into +0)."""
+    w = np.asarray(w, dtype=np.float32)
+    nudge = np.where((w[:, 0] == 0) & (w[:, 2] == 0), np.float32(1e-7), np.float32(0.0))
+    wx = (w[:, 0] + nudge).astype(np.float32)
+    beta = _f32(np.arcsin, np.clip(w[:, 1], np.float32(-1.0), np.float32(1.0)))
+    alpha = np.arctan2(wx.astype(np.float64), w[:, 2].astype(np.float64)).astype(np.float32)
+    return np.stack([alpha * _INV_PI, beta * (np.float32(2.0) * _INV_PI)], axis=1).astype(np.float32)
+
+
+def constant_environment(rgb):
+    """A Constant map's environment: the same RGB for every direction."""
+    c = np.asarray(rgb, dtype=np.float32).reshape(1, 3)
+    return lambda w: np.repeat(c, w.shape[0], axis=0)
+
+
+def equirect_environment(image, clamp: bool = True, aligned: bool = False, linear: bool = True):
+    """XRProject() >> TensorSampler(image [H, W, 3]): dir2xr, then the 2-D
+    sampler (oracle/tensors.py tensor_sampler)."""
+    from .tensors import tensor_sampler
+    img = np.asarray(image, dtype=np.float32)
+    return lambda w: tensor_sampler(img, dir2xr(w), clamp=clamp, aligned=aligned, linear=linear)
+
+
+def ortho_basis(n: np.ndarray):
+    """create_ortho_basis (math_library.h:323-330), float32, [R, 3] -> (T, B)."""
+    one = np.float32(1.0)
+    sign = np.where(n[:, 2] >= 0, one, -one).astype(np.float32)
+    a = (-one / (sign + n[:, 2])).astype(np.float32)
+    b = ((n[:, 0] * n[:, 1]) * a).astype(np.float32)
+    T = np.stack([one + ((sign * n[:, 0]) * n[:, 0]) * a, sign * b, -sign * n[:, 0]], axis=1)
+    B = np.stack([b, sign + (n[:, 1] * n[:, 1]) * a, -n[:, 1]], axis=1)
+    return T.astype(np.float32), B.astype(np.float32)
+
+
+def hg_phase_sample(w: np.ndarray, g: float, state: np.ndarray) -> np.ndarray:
+    """hg_phase_sample (rdv/shaders/libraries/random_library.h:224-239) in
+    float32: two draws (azimuth phi, then xi), the inverted Henyey-Greenstein
+    CDF (uniform cosine when |g| < 0.001), the direction around w in
+    create_ortho_basis' frame. `state` advances in place."""
+    one, two = np.float32(1.0), np.float32(2.0)
+    g = np.float32(g)
+    phi = (random_draw(state) * two) * _PI
+    xi = random_draw(state)
+    g2 = g * g
+    with np.errstate(divide="ignore", invalid="ignore"):
+        t = (one - g2) / ((one - g) + (two * g) * xi)
+        invertcdf = (np.float32(0.5) / g) * ((one + g2) - t * t)
+    cos_t = ((two * xi) - one) if abs(float(g)) < 0.001 else invertcdf
+    cos_t = np.asarray(cos_t, dtype=np.float32)
+    sin_t = np.sqrt(np.maximum(np.float32(0.0), one - cos_t * cos_t)).astype(np.float32)
+    t0, t1 = ortho_basis(w)
+    s0 = (sin_t * _f32(np.sin, phi))[:, None]
+    s1 = (sin_t * _f32(np.cos, phi))[:, None]
+    return ((s0 * t0 + s1 * t1) + cos_t[:, None] * w).astype(np.float32)
+
+
+def _inverse3(transform):
+    if transform is None:
+        return np.eye(3, dtype=np.float32)
+    t = np.asarray(transform, dtype=np.float64).reshape(-1)
+    return np.linalg.inv(t[:9].reshape(3, 3).T).astype(np.float32)
+
+
+def _apply3(L, v):
+    out = np.empty_like(v)
+    for i in range(3):
+        acc = (L[i, 0] * v[:, 0]).astype(np.float32) + (L[i, 1] * v[:, 1]).astype(np.float32)
+        out[:, i] = acc.astype(np.float32) + (L[i, 2] * v[:, 2]).astype(np.float32)
+    return out
+
+
+def slab_exit(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """tMax of ray_box_intersection (math_library.h:48-57) from x along w,
+    min(min(c.x, c.y), c.z) with GLSL min, c = -x / w + |1 / w|."""
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.float32(1.0) / w
+        c = (-x * inv + np.abs(inv)).astype(np.float32)
+    return _glsl_min(_glsl_min(c[:, 0], c[:, 1]), c[:, 2])
+
+
+def pbvr(origins, dirs, extinction, environment, majorant, seeds, transform=None, albedo=(1.0, 1.0, 1.0),
+         g: float = 0.0, max_bounces: int = 32, index=None, draws_before: int = 0,
+         return_evaluations: bool = False, safety_cap: int = 8192):
+    """PBVR.forward (rdv/shaders/volumes/pbvr.h:21-110) vectorised over rays
+    in lock step, every operation in float32:
+
+        x, wo <- object space; miss -> environment(w)
+        x <- entry point; d = tMax - tMin; W = 1; bounces = 0
+        for (safety < 8192 while d > 0):
+            maj = max(majorant(x, wo, max_step), 1e-12); max_step = max(max_step, 1e-6)
+            dt = -log(1 - random()) / maj; step = min(dt, min(max_step, d))
+            x += step wo; d -= step
+            step < dt: d <= 0 -> escaped (break), else continue
+            random() >= extinction(x) / maj -> continue (null collision)
+            W *= albedo; max(W) < 1e-4 -> 0; bounces >= max_bounces -> 0
+            w <- hg_phase_sample(w, g); wo <- L w; d <- slab exit from x; bounces++
+        escaped -> W * environment(w), else 0
+
+    `majorant(x, wo)` returns (value, distance) -- voxel_majorant or
+    sphere_majorant; `environment(w)` maps [n, 3] -> [n, 3]. The reference's
+    local_majorant (volumes/majorant_field_precode.h) is absent from its
+    checkout; it is taken as the field's (majorant, distance) with the
+    distance floored at 1e-6, the floor ratiotracking_transmittance_trait.h:14
+    applies (pbvr.h:60-61 names local_majorant's own epsilon)."""
+    o, w_obj = object_space(origins, dirs, transform)
+    w_world = np.asarray(dirs, dtype=np.float32).copy()
+    L = _inverse3(transform)
+    tmin, tmax = ray_box(o, w_obj)
+    miss = (tmax <= 0) | (tmin > tmax)
+    tmin = np.maximum(tmin, np.float32(0.0))
+    n = o.shape[0]
+    out = np.zeros((n, 3), dtype=np.float32)
+    if miss.any():
+        out[miss] = environment(w_world[miss])
+    hit = np.nonzero(~miss)[0]
+    evals = 0
+    if hit.size:
+        idx = np.arange(n) if index is None else np.asarray(index)
+        state = random_spawn(seeds, idx[hit])
+        for _ in range(draws_before):
+            random_step(state)
+        x = (o[hit] + w_obj[hit] * tmin[hit, None]).astype(np.float32)
+        wo = w_obj[hit].copy()
+        w = w_world[hit].copy()
+        d = (tmax[hit] - tmin[hit]).astype(np.float32)
+        m = hit.size
+        W = np.ones((m, 3), dtype=np.float32)
+        bounces = np.zeros(m, dtype=np.int64)
+        running = np.ones(m, dtype=bool)
+        escaped = np.zeros(m, dtype=bool)
+        alb = np.asarray(albedo, dtype=np.float32).reshape(1, 3)
+        for _ in range(safety_cap):
+            running &= d > 0
+            act = np.nonzero(running)[0]
+            if act.size == 0:
+                break
+            maj, max_step = majorant(x[act], wo[act])
+            maj = _glsl_max(maj.astype(np.float32), np.float32(1e-12))
+            max_step = _glsl_max(max_step.astype(np.float32), np.float32(1e-6))
+            st = state[act]
+            u = random_draw(st)
+            with np.errstate(divide="ignore", over="ignore"):
+                dt = ((-_log_f32(np.float32(1.0) - u)) / maj).astype(np.float32)
+            step = _glsl_min(dt, _glsl_min(max_step.astype(np.float32), d[act]))
+            x[act] = (x[act] + step[:, None] * wo[act]).astype(np.float32)
+            d[act] = (d[act] - step).astype(np.float32)
+            free = step < dt
+            esc = free & (d[act] <= 0)
+            escaped[act[esc]] = True
+            running[act[esc]] = False
+            coll = np.nonzero(~free)[0]          # positions inside act
+            if coll.size:
+                ci = act[coll]
+                sigma = np.asarray(extinction(x[ci]), dtype=np.float32)
+                evals += ci.size
+                sub = st[coll]
+                u2 = random_draw(sub)
+                real = ~(u2 >= (sigma / maj[coll]).astype(np.float32))
+                if real.any():
+                    rp = coll[real]                  # positions inside act
+                    ri = act[rp]
+                    W[ri] = (W[ri] * alb).astype(np.float32)
+                    wmax = _glsl_max(_glsl_max(W[ri, 0], W[ri, 1]), W[ri, 2])
+                    stop = (wmax < np.float32(1e-4)) | (bounces[ri] >= max_bounces)
+                    running[ri[stop]] = False
+                    go = ~stop
+                    if go.any():
+                        gi = ri[go]
+                        s2 = sub[real][go]
+                        w[gi] = hg_phase_sample(w[gi], g, s2)
+                        wo[gi] = _apply3(L, w[gi])
+                        d[gi] = slab_exit(x[gi], wo[gi])
+                        bounces[gi] += 1
+                        tmp = sub[real]
+                        tmp[go] = s2
+                        sub[real] = tmp
+                st[coll] = sub
+            state[act] = st
+        if escaped.any():
+            e = np.nonzero(escaped)[0]
+            out[hit[e]] = (W[e] * environment(w[e])).astype(np.float32)
+    if return_evaluations:
+        return out, evals
+    return out

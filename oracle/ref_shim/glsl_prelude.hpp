@@ -44,6 +44,7 @@ struct rdv_vec2 {
 struct rdv_vec3 {
     float x, y, z;
     rdv_vec3() : x(0), y(0), z(0) {}
+    explicit rdv_vec3(float s) : x(s), y(s), z(s) {}
     rdv_vec3(float a, float b, float c) : x(a), y(b), z(c) {}
     rdv_vec3(rdv_vec2 a, float c) : x(a.x), y(a.y), z(c) {}
 };

@@ -10,7 +10,8 @@ Every operator launches hand-written sm_100a kernels from the in-tree
 ``_lib/librdvb.so`` (C ABI in ``include/rdvb.h``); there is no CPU fallback.
 """
 from .core import (RDVObject, wrap, profiling, reset_submit_times, profiling_submit_times)
-from .maps import (Map, Identity, X, ReLU, relu, Linear, LinearFast, LinearFastBF16, linear, Composite, TensorSampler)
+from .maps import (Map, Identity, X, ReLU, relu, Linear, LinearFast, LinearFastBF16, linear, Composite, TensorSampler,
+                   Constant, XRProject, dir2xr)
 from .tensor_ops import (TensorOperation, ReLUTensorOp, LinearTensorOp, LinearTensorOpFast, LinearTensorOpMine,
                          LinearTensorOpSimple, LinearTensorOpSmall, Downsample2xTensorOp, Upsample2xTensorOp,
                          ConcatTensorOp)
@@ -18,18 +19,19 @@ from .conv import (Conv2DTensorOp, Conv2DTensorOpFast, Conv2DTensorOpSimple, Con
                    Conv2DTensorOpWindow3x3, Conv2DTensorOpWinograd3x3, Conv3x3Winograd, conv2d_direct,
                    _winograd_transform_weight)
 from .rendering import Cameras, VolumeRenderer
-from .volumes import RaymarchingTransmittance, RatiotrackingTransmittance, TensorGrid, VoxelMajorantField
+from .volumes import (RaymarchingTransmittance, RatiotrackingTransmittance, TensorGrid, VoxelMajorantField,
+                      SphereMajorantField, PBVR)
 from ._native import RdvbError, device_status
 
 __all__ = [
     "RDVObject", "wrap", "profiling", "reset_submit_times", "profiling_submit_times",
     "Map", "Identity", "X", "ReLU", "relu", "Linear", "LinearFast", "LinearFastBF16", "linear", "Composite",
-    "TensorSampler",
+    "TensorSampler", "Constant", "XRProject", "dir2xr",
     "TensorOperation", "ReLUTensorOp", "LinearTensorOp", "LinearTensorOpFast", "LinearTensorOpMine",
     "LinearTensorOpSimple", "LinearTensorOpSmall", "Downsample2xTensorOp", "Upsample2xTensorOp", "ConcatTensorOp",
     "Conv2DTensorOp", "Conv2DTensorOpFast", "Conv2DTensorOpSimple", "Conv2DTensorOpSimple3x3",
     "Conv2DTensorOpWindow3x3", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
     "Cameras", "VolumeRenderer", "RaymarchingTransmittance", "RatiotrackingTransmittance", "TensorGrid",
-    "VoxelMajorantField",
+    "VoxelMajorantField", "SphereMajorantField", "PBVR",
     "RdvbError", "device_status",
 ]

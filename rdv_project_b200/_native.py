@@ -21,6 +21,9 @@ RDVB_MATH_F32, RDVB_MATH_F16, RDVB_MATH_BF16 = 0, 1, 2
 RDVB_LAYER_RELU = 4
 RDVB_WINOGRAD_F2X2, RDVB_WINOGRAD_F4X4 = 0, 1
 RDVB_PATH_CUDA_CORE, RDVB_PATH_TENSOR_CORE = 0, 1
+RDVB_MAJORANT_VOXEL, RDVB_MAJORANT_SPHERE = 0, 1
+RDVB_ENV_CONSTANT, RDVB_ENV_EQUIRECT = 0, 1
+RDVB_SAMPLER_CLAMP, RDVB_SAMPLER_ALIGNED, RDVB_SAMPLER_LINEAR = 1, 2, 4
 
 _c_int, _c_i64, _vp, _c_u32, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float
 
@@ -63,8 +66,11 @@ SIGNATURES = {
     "rdvb_transmittance_workspace_bytes": (_c_i64, [_c_i64, _c_int, _vp, _vp]),
     "rdvb_transmittance_rm": (_c_int, [_vp, _c_i64, _vp, _c_f, _c_f, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
                                        ctypes.c_size_t, _vp, _vp]),
-    "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp,
-                                       _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
+    "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp,
+                                       _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
+    "rdvb_xr_project": (_c_int, [_vp, _c_i64, _vp, _vp]),
+    "rdvb_pbvr": (_c_int, [_vp, _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int,
+                           _vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
 }
 
 

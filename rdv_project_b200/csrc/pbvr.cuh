@@ -1,0 +1,249 @@
+// PBVR (rdv/domain/volumes.py:257-326, rdv/shaders/volumes/pbvr.h): unbiased
+// volume rendering by delta tracking through a majorant field, with an MLP
+// extinction, Henyey-Greenstein scattering, an albedo, a bounce budget and
+// an environment for escaped paths; one persistent thread per ray, RGB out.
+//
+// Per ray (x, w) -- pbvr.h:21-110:
+//   object space x <- L (x - O), wo <- L w (L formed on the host); slab test
+//   against [-1, 1]^3; a miss returns environment(w);
+//   entry clamp, x <- x + wo tMin, d <- tMax - tMin; W = (1, 1, 1);
+//   for (safety < 8192 while d > 0):
+//     maj = max(majorant(x, wo, max_step), 1e-12)
+//     dt = -log(1 - random()) / maj; step = min(dt, min(max_step, d))
+//     x += step wo; d -= step
+//     step < dt: d <= 0 -> escaped; else next iteration (a new majorant cell)
+//     collision: random() >= extinction(x) / maj -> null collision
+//     real collision: W *= albedo; max(W) < 1e-4 -> 0; bounces >= max -> 0;
+//       w <- hg_phase_sample(w, g); wo <- L w; d <- the slab exit from x
+//   escaped -> W * environment(w), else 0.
+// pbvr.h calls local_majorant(mg, x, w, max_step), defined by
+// volumes/majorant_field_precode.h, which the reference checkout does not
+// contain. It is taken here as the field's Map[6, 2] output (x, w) ->
+// (majorant, distance), read as majorant_trait.h reads it, with the distance
+// floored at 1e-6 as ratiotracking_transmittance_trait.h:14 floors it --
+// the "own epsilon" pbvr.h:60-61 refers to. Without a floor a ray moving
+// toward -x, -y or -z stops on the first voxel face it reaches (the face
+// point maps back to the voxel it leaves, whose exit distance is then 0).
+// hg_phase_sample and create_ortho_basis follow
+// rdv/shaders/libraries/random_library.h:224-239 and math_library.h:323-330.
+// Every march operation is a separately rounded fp32 operation; log, sin,
+// cos, asin and atan2 are CUDA's.
+//
+// Environment: a constant RGB (a Constant map), or an equirectangular image
+// looked up with XRProject >> TensorSampler (math_library.h dir2xr: asin of
+// w.y and atan(w.x, w.z), scaled by 1/pi and 2/pi; then the 2-D sampler).
+//
+// Work is warp-coherent, as in ratiotracking_kernel: each lane runs its ray's
+// free flights until a tentative collision, then the warp evaluates the MLP
+// together.
+#pragma once
+#include "sampler.cuh"
+#include "transmittance.cuh"
+
+namespace rdvb {
+namespace pbvr {
+
+using trm::Params;
+constexpr int kSafety = 8192;  // pbvr.h's loop cap
+constexpr float kPi = 3.14159265358979323846f;
+constexpr float kInvPi = 0.318309886183790671538f;
+
+struct Extra {
+    float albedo[3];
+    float g;
+    int max_bounces;
+    int env_kind;          // 0 constant, 1 equirectangular image
+    float env_rgb[3];
+    const float* env;      // [H, W, 3] fp32 (env_kind 1)
+    int env_h, env_w;
+    int env_clamp, env_aligned, env_linear;
+    float* out;            // [n_rays, 3]
+};
+
+// dir2xr (math_library.h:265-276): a direction's equirectangular
+// coordinates (atan(w.x, w.z) / pi, asin(w.y) * 2 / pi). The reference always
+// adds 0 or 1e-7 to w.x, which turns a -0 x into +0 before atan.
+__device__ __forceinline__ void dir2xr(const float (&w)[3], float& u, float& v) {
+    const float wx = __fadd_rn(w[0], (w[0] == 0.0f && w[2] == 0.0f) ? 1e-7f : 0.0f);
+    const float beta = asinf(fminf(fmaxf(w[1], -1.0f), 1.0f));
+    const float alpha = atan2f(wx, w[2]);
+    u = __fmul_rn(alpha, kInvPi);
+    v = __fmul_rn(beta, __fmul_rn(2.0f, kInvPi));
+}
+
+// XRProject as a map of its own: [n, 3] directions -> [n, 2].
+__global__ void xr_project_kernel(const float* __restrict__ dirs, long long n, float* __restrict__ out) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const float w[3] = {__ldg(dirs + 3 * i), __ldg(dirs + 3 * i + 1), __ldg(dirs + 3 * i + 2)};
+        float u, v;
+        dir2xr(w, u, v);
+        out[2 * i] = u;
+        out[2 * i + 1] = v;
+    }
+}
+
+// world direction -> environment radiance
+__device__ __forceinline__ void environment(const Extra& e, const float (&w)[3], float (&c)[3]) {
+    if (e.env_kind == 0) {
+        c[0] = e.env_rgb[0];
+        c[1] = e.env_rgb[1];
+        c[2] = e.env_rgb[2];
+        return;
+    }
+    float u, v;
+    dir2xr(w, u, v);
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        c[k] = sampler::sample2(e.env, e.env_h, e.env_w, 3, k, u, v, e.env_clamp != 0, e.env_aligned != 0,
+                                e.env_linear != 0);
+}
+
+// create_ortho_basis (math_library.h:323-330)
+__device__ __forceinline__ void ortho_basis(const float (&n)[3], float (&t)[3], float (&b)[3]) {
+    const float sign = n[2] >= 0.0f ? 1.0f : -1.0f;
+    const float a = __fdiv_rn(-1.0f, __fadd_rn(sign, n[2]));
+    const float bb = __fmul_rn(__fmul_rn(n[0], n[1]), a);
+    t[0] = __fadd_rn(1.0f, __fmul_rn(__fmul_rn(__fmul_rn(sign, n[0]), n[0]), a));
+    t[1] = __fmul_rn(sign, bb);
+    t[2] = -__fmul_rn(sign, n[0]);
+    b[0] = bb;
+    b[1] = __fadd_rn(sign, __fmul_rn(__fmul_rn(n[1], n[1]), a));
+    b[2] = -n[1];
+}
+
+// hg_phase_sample (random_library.h:224-239): two draws (phi, then xi).
+__device__ __forceinline__ void hg_sample(Rng& r, float g, float (&w)[3]) {
+    const float phi = __fmul_rn(__fmul_rn(rng_uniform(r), 2.0f), kPi);
+    const float xi = rng_uniform(r);
+    const float g2 = __fmul_rn(g, g);
+    const float one_minus_g2 = __fsub_rn(1.0f, g2);
+    const float one_plus_g2 = __fadd_rn(1.0f, g2);
+    const float one_over_2g = __fdiv_rn(0.5f, g);
+    const float t = __fdiv_rn(one_minus_g2, __fadd_rn(__fsub_rn(1.0f, g), __fmul_rn(__fmul_rn(2.0f, g), xi)));
+    const float invertcdf = __fmul_rn(one_over_2g, __fsub_rn(one_plus_g2, __fmul_rn(t, t)));
+    const float cos_t = fabsf(g) < 0.001f ? __fsub_rn(__fmul_rn(2.0f, xi), 1.0f) : invertcdf;
+    const float sin_t = __fsqrt_rn(fmaxf(0.0f, __fsub_rn(1.0f, __fmul_rn(cos_t, cos_t))));
+    float t0[3], t1[3];
+    ortho_basis(w, t0, t1);
+    const float s0 = __fmul_rn(sin_t, sinf(phi)), s1 = __fmul_rn(sin_t, cosf(phi));
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        w[k] = __fadd_rn(__fadd_rn(__fmul_rn(s0, t0[k]), __fmul_rn(s1, t1[k])), __fmul_rn(cos_t, w[k]));
+}
+
+// wo = L w (the node's inverse 3x3, row-major), each sum rounded in order.
+__device__ __forceinline__ void to_object(const float (&L)[9], const float (&w)[3], float (&wo)[3]) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+        wo[i] = __fadd_rn(__fadd_rn(__fmul_rn(L[3 * i], w[0]), __fmul_rn(L[3 * i + 1], w[1])),
+                          __fmul_rn(L[3 * i + 2], w[2]));
+}
+
+// ray_box_intersection (math_library.h:48-57) from x along w: tMax =
+// min(min(c.x, c.y), c.z) with c = -x / w + |1 / w| (GLSL min(a, b) = b < a ?
+// b : a).
+__device__ __forceinline__ float slab_exit(const float (&x)[3], const float (&w)[3]) {
+    float c[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float inv = __fdiv_rn(1.0f, w[k]);
+        c[k] = __fadd_rn(__fmul_rn(-x[k], inv), fabsf(inv));
+    }
+    const float m = c[1] < c[0] ? c[1] : c[0];
+    return c[2] < m ? c[2] : m;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT) pbvr_kernel(const __grid_constant__ Params p, const __grid_constant__ Extra e) {
+    extern __shared__ float sm[];
+    float* wsm = sm;
+    float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
+    float* act1 = act0 + p.maxw * NT;
+    trm::stage_chain<NT>(p, wsm);
+    const float* bsm = wsm;
+    unsigned long long my_evals = 0;
+    long long ray = -1;  // -1: take the next ray; -2: none left
+    float x[3] = {0.0f, 0.0f, 0.0f}, w[3] = {0.0f, 0.0f, 1.0f}, wo[3] = {0.0f, 0.0f, 1.0f};
+    float d = 0.0f, maj = 1.0f, W[3] = {1.0f, 1.0f, 1.0f};
+    int safety = 0, bounces = 0;
+    Rng r = {0u, 0u, 0u, 0u};
+    auto finish = [&](float c0, float c1, float c2) {
+        e.out[ray * 3 + 0] = c0;
+        e.out[ray * 3 + 1] = c1;
+        e.out[ray * 3 + 2] = c2;
+        ray = -1;
+    };
+    while (true) {
+        bool pending = false;  // a tentative collision at x waits for its extinction
+        while (ray != -2 && !pending) {
+            if (ray < 0) {
+                ray = atomicAdd(p.counter, 1);
+                if (ray >= p.n_rays) {
+                    ray = -2;
+                    break;
+                }
+                const float* rr = p.rays + ray * 6;
+                w[0] = rr[3];
+                w[1] = rr[4];
+                w[2] = rr[5];
+                if (!trm::march_entry(rr, p.L, p.O, x, wo, d)) {
+                    float c[3];
+                    environment(e, w, c);  // the ray never touches the volume
+                    finish(c[0], c[1], c[2]);
+                    continue;
+                }
+                W[0] = W[1] = W[2] = 1.0f;
+                safety = 0;
+                bounces = 0;
+                r = rng_spawn(p.seeds, static_cast<unsigned>(ray));
+                for (int k = 0; k < p.draws_before; ++k) rng_step(r);
+            }
+            if (!(d > 0.0f) || safety >= kSafety) {  // the loop ended without escaping
+                finish(0.0f, 0.0f, 0.0f);
+                continue;
+            }
+            ++safety;
+            float max_step;
+            maj = trm::field_majorant(p, x, wo, max_step);
+            maj = maj < 1e-12f ? 1e-12f : maj;                      // max(majorant, 1e-12)
+            max_step = max_step < 1e-6f ? 1e-6f : max_step;         // local_majorant's floor
+            const float dt = __fdiv_rn(-logf(__fsub_rn(1.0f, rng_uniform(r))), maj);
+            const float m = d < max_step ? d : max_step;    // min(max_step, d)
+            const float step = m < dt ? m : dt;              // min(dt, .)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(step, wo[k]));
+            d = __fsub_rn(d, step);
+            if (step < dt) {
+                if (d <= 0.0f) {  // reached the boundary without a collision
+                    float c[3];
+                    environment(e, w, c);
+                    finish(__fmul_rn(W[0], c[0]), __fmul_rn(W[1], c[1]), __fmul_rn(W[2], c[2]));
+                }
+                continue;  // (or: a new majorant cell)
+            }
+            pending = true;
+        }
+        if (!__any_sync(0xffffffffu, pending)) break;  // no lane has rays left
+        const float sigma = trm::extinction<NT>(p, wsm, bsm, act0, act1, x);
+        if (pending) {
+            ++my_evals;
+            if (rng_uniform(r) >= __fdiv_rn(sigma, maj)) continue;  // null collision
+#pragma unroll
+            for (int k = 0; k < 3; ++k) W[k] = __fmul_rn(W[k], e.albedo[k]);
+            const float wmax = fmaxf(fmaxf(W[0], W[1]), W[2]);
+            if (wmax < 0.0001f || bounces >= e.max_bounces) {
+                finish(0.0f, 0.0f, 0.0f);  // throughput too low, or the bounce budget spent
+                continue;
+            }
+            hg_sample(r, e.g, w);
+            to_object(p.L, w, wo);
+            d = slab_exit(x, wo);
+            ++bounces;
+        }
+    }
+    if (my_evals) atomicAdd(p.evaluations, my_evals);
+}
+
+}  // namespace pbvr
+}  // namespace rdvb

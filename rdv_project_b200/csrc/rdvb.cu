@@ -25,6 +25,7 @@
 #include "resample.cuh"
 #include "conv_tc.cuh"
 #include "sampler.cuh"
+#include "pbvr.cuh"
 
 namespace {
 
@@ -58,6 +59,8 @@ struct DeviceInfo {
     size_t trm_smem_set = 0;
     size_t rt_smem_set = 0;
     size_t rt_wide_smem_set = 0;
+    size_t pbvr_smem_set = 0;
+    size_t pbvr_wide_smem_set = 0;
     size_t rows_smem_set = 0;
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
@@ -1352,9 +1355,11 @@ int trm_object_space(const float* transform, rdvb::trm::Params& p) {
 // The CUDA-core march kernels: the chain's shared-memory weight image, then
 // one launch of as many persistent 128-thread CTAs as fit (rays handed out
 // by the counter at the start of the workspace).
+enum class March { kRaymarch, kRatioTracking, kPbvr };
+
 int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const float* const* weights,
                       const float* const* biases, const int* layer_flags, void* workspace, DeviceInfo* dev,
-                      cudaStream_t st, bool ratio_tracking) {
+                      cudaStream_t st, March kind, const rdvb::pbvr::Extra* extra = nullptr) {
     using namespace rdvb::trm;
     int off = 0;
     for (int l = 0; l < n_layers; ++l) {
@@ -1374,24 +1379,43 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
         off += (dims[l + 1] + 3) & ~3;
     }
     p.w_floats = off;
-    // ratio tracking: 384 rays per CTA when their activation columns fit
-    // (chains at most 64 wide), 128 otherwise -- the per-ray activations
-    // bound how many warps an SM holds
+    // ratio tracking and PBVR: 384 rays per CTA when their activation
+    // columns fit (chains at most 64 wide), 128 otherwise -- the per-ray
+    // activations bound how many warps an SM holds
     const size_t w_bytes = static_cast<size_t>((off + 3) & ~3) * 4;
-    const bool wide = ratio_tracking &&
+    const bool wide = kind != March::kRaymarch &&
                       w_bytes + static_cast<size_t>(2 * p.maxw) * kRtWideThreads * 4 <=
                           static_cast<size_t>(dev->max_smem_optin);
     const int threads = wide ? kRtWideThreads : kThreads;
     const size_t smem = w_bytes + static_cast<size_t>(2 * p.maxw) * threads * 4;
     if (smem > static_cast<size_t>(dev->max_smem_optin))
         return fail(RDVB_ERR_UNSUPPORTED, "the extinction MLP needs %zu bytes of shared memory", smem);
-    auto kernel = !ratio_tracking ? transmittance_kernel
-                                  : (wide ? ratiotracking_kernel<kRtWideThreads> : ratiotracking_kernel<kThreads>);
-    size_t& smem_set = !ratio_tracking ? dev->trm_smem_set : (wide ? dev->rt_wide_smem_set : dev->rt_smem_set);
-    if (smem_set < smem) {
+    const void* kernel = nullptr;
+    size_t* smem_set = nullptr;
+    const char* name = nullptr;
+    switch (kind) {
+        case March::kRaymarch:
+            kernel = reinterpret_cast<const void*>(transmittance_kernel);
+            smem_set = &dev->trm_smem_set;
+            name = "transmittance_kernel";
+            break;
+        case March::kRatioTracking:
+            kernel = wide ? reinterpret_cast<const void*>(ratiotracking_kernel<kRtWideThreads>)
+                          : reinterpret_cast<const void*>(ratiotracking_kernel<kThreads>);
+            smem_set = wide ? &dev->rt_wide_smem_set : &dev->rt_smem_set;
+            name = "ratiotracking_kernel";
+            break;
+        case March::kPbvr:
+            kernel = wide ? reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kRtWideThreads>)
+                          : reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kThreads>);
+            smem_set = wide ? &dev->pbvr_wide_smem_set : &dev->pbvr_smem_set;
+            name = "pbvr_kernel";
+            break;
+    }
+    if (*smem_set < smem) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(march): %s", cudaGetErrorString(e));
-        smem_set = smem;
+        *smem_set = smem;
     }
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
@@ -1402,8 +1426,16 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * dev->sm_count * per_sm)));
     e = cudaMemsetAsync(workspace, 0, 16, st);
     if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    kernel<<<grid, threads, smem, st>>>(p);
-    return check_launch(ratio_tracking ? "ratiotracking_kernel" : "transmittance_kernel");
+    if (kind == March::kPbvr) {
+        void* args[] = {&p, const_cast<rdvb::pbvr::Extra*>(extra)};
+        e = cudaLaunchKernel(kernel, dim3(grid), dim3(threads), args, smem, st);
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
+    } else {
+        void* args[] = {&p};
+        e = cudaLaunchKernel(kernel, dim3(grid), dim3(threads), args, smem, st);
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
+    }
+    return check_launch(name);
 }
 }  // namespace
 
@@ -1522,14 +1554,31 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
         }
         return RDVB_OK;
     }
-    return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev, st, false);
+    return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev, st, March::kRaymarch);
 }
 
-int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
-                          const float* majorant, const int* majorant_dims, const uint32_t* seeds, int draws_before,
-                          int n_layers, const int* dims, const float* const* weights, const float* const* biases,
-                          const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, float* out,
-                          void* stream) {
+int rdvb_xr_project(const float* dirs, int64_t n, float* out, void* stream) {
+    if (n < 0) return fail(RDVB_ERR_INVALID_ARG, "n must be >= 0");
+    if (n == 0) return RDVB_OK;
+    if (!dirs || !out || !aligned(dirs, 4) || !aligned(out, 4))
+        return fail(RDVB_ERR_INVALID_ARG, "dirs and out must be 4-byte aligned device pointers");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const long long blocks = std::min<long long>((n + 255) / 256, 1LL * dev->sm_count * 8);
+    rdvb::pbvr::xr_project_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(dirs, n,
+                                                                                                          out);
+    return check_launch("xr_project_kernel");
+}
+
+namespace {
+// The arguments ratio tracking and PBVR share: the rays, the node's
+// transform, the majorant field, the generator and the extinction chain.
+// Fills p (all but the launch state) and reports whether there is any work.
+int tracking_params(const float* rays, int64_t n_rays, const float* transform, const float* majorant,
+                    const int* majorant_dims, int majorant_kind, const uint32_t* seeds, int draws_before,
+                    int n_layers, const int* dims, const float* const* weights, const float* const* biases,
+                    const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, void* out,
+                    rdvb::trm::Params& p, int out_dim) {
     using namespace rdvb::trm;
     if (draws_before < 0 || draws_before > 64)
         return fail(RDVB_ERR_INVALID_ARG, "draws_before must be in [0, 64], got %d", draws_before);
@@ -1547,6 +1596,9 @@ int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transf
     }
     for (int l = 0; l < n_layers; ++l)
         if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "layer %d has a NULL weight or bias", l);
+    if (majorant_kind != RDVB_MAJORANT_VOXEL && majorant_kind != RDVB_MAJORANT_SPHERE)
+        return fail(RDVB_ERR_INVALID_ARG, "majorant_kind must be RDVB_MAJORANT_VOXEL or RDVB_MAJORANT_SPHERE, got %d",
+                    majorant_kind);
     if (!majorant_dims || !seeds) return fail(RDVB_ERR_INVALID_ARG, "majorant_dims and seeds must not be NULL");
     for (int k = 0; k < 3; ++k)
         if (majorant_dims[k] < 1)
@@ -1557,33 +1609,99 @@ int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transf
         return fail(RDVB_ERR_UNSUPPORTED, "at most %lld rays per call", 0x7fffffffLL - (1LL << 24));
     if (n_rays == 0) return RDVB_OK;
     if (!rays || !out || !majorant) return fail(RDVB_ERR_INVALID_ARG, "rays, majorant and out must not be NULL");
-    if (!aligned(rays, 4) || !aligned(out, 4) || !aligned(majorant, 4))
-        return fail(RDVB_ERR_INVALID_ARG, "rays, majorant and out must be 4-byte aligned");
+    if (!aligned(rays, 4) || !aligned(out, 4) || !aligned(majorant, majorant_kind == RDVB_MAJORANT_SPHERE ? 8 : 4))
+        return fail(RDVB_ERR_INVALID_ARG, "rays and out must be 4-byte aligned, a voxel majorant grid 4-byte and a "
+                                          "sphere majorant grid 8-byte aligned");
     if (!workspace || !aligned(workspace, 256) || workspace_bytes < 256)
         return fail(RDVB_ERR_INVALID_ARG, "workspace must be 256-byte aligned and hold 256 bytes");
-    DeviceInfo* dev = nullptr;
-    if (int rc = current_device(&dev)) return rc;
-    Params p;
     memset(&p, 0, sizeof(p));
     p.rays = rays;
-    p.out = out;
+    p.out = out_dim == 1 ? static_cast<float*>(out) : nullptr;
     p.n_rays = n_rays;
     p.counter = static_cast<int*>(workspace);
     p.evaluations = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + 8);
-    p.scale = density_scale;
+    p.scale = 1.0f;
     p.n_layers = n_layers;
     p.input_relu = input_relu ? 1 : 0;
     p.maxw = maxw;
     p.maj = majorant;
+    p.field = majorant_kind == RDVB_MAJORANT_SPHERE ? 1 : 0;
     p.mdim[0] = majorant_dims[2];  // x: W
     p.mdim[1] = majorant_dims[1];  // y: H
     p.mdim[2] = majorant_dims[0];  // z: D
     for (int k = 0; k < 3; ++k) p.mvs[k] = 2.0f / static_cast<float>(p.mdim[k]);
     for (int k = 0; k < 4; ++k) p.seeds[k] = seeds[k];
     p.draws_before = draws_before;
-    if (int rc = trm_object_space(transform, p)) return rc;
+    return trm_object_space(transform, p);
+}
+}  // namespace
+
+int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
+                          const float* majorant, const int* majorant_dims, int majorant_kind, const uint32_t* seeds,
+                          int draws_before, int n_layers, const int* dims, const float* const* weights,
+                          const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+                          size_t workspace_bytes, float* out, void* stream) {
+    rdvb::trm::Params p;
+    if (int rc = tracking_params(rays, n_rays, transform, majorant, majorant_dims, majorant_kind, seeds, draws_before,
+                                 n_layers, dims, weights, biases, layer_flags, input_relu, workspace, workspace_bytes,
+                                 out, p, 1))
+        return rc;
+    if (n_rays == 0) return RDVB_OK;
+    p.scale = density_scale;
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
     return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev,
-                             static_cast<cudaStream_t>(stream), true);
+                             static_cast<cudaStream_t>(stream), March::kRatioTracking);
+}
+
+int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const float* majorant,
+              const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
+              int env_kind, const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
+              const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
+              const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+              size_t workspace_bytes, float* out, void* stream) {
+    rdvb::trm::Params p;
+    if (int rc = tracking_params(rays, n_rays, transform, majorant, majorant_dims, majorant_kind, seeds, draws_before,
+                                 n_layers, dims, weights, biases, layer_flags, input_relu, workspace, workspace_bytes,
+                                 out, p, 3))
+        return rc;
+    if (!albedo) return fail(RDVB_ERR_INVALID_ARG, "albedo must not be NULL");
+    if (max_bounces < 0) return fail(RDVB_ERR_INVALID_ARG, "max_bounces must be >= 0, got %d", max_bounces);
+    if (!std::isfinite(g)) return fail(RDVB_ERR_INVALID_ARG, "g must be finite");
+    rdvb::pbvr::Extra e;
+    memset(&e, 0, sizeof(e));
+    for (int k = 0; k < 3; ++k) e.albedo[k] = albedo[k];
+    e.g = g;
+    e.max_bounces = max_bounces;
+    if (env_kind == RDVB_ENV_CONSTANT) {
+        if (!env_rgb) return fail(RDVB_ERR_INVALID_ARG, "a constant environment needs env_rgb");
+        for (int k = 0; k < 3; ++k) e.env_rgb[k] = env_rgb[k];
+    } else if (env_kind == RDVB_ENV_EQUIRECT) {
+        if (!env_dims) return fail(RDVB_ERR_INVALID_ARG, "an equirectangular environment needs env_dims");
+        if (env_dims[0] < 1 || env_dims[1] < 1)
+            return fail(RDVB_ERR_INVALID_ARG, "env_dims must be positive, got %d x %d", env_dims[0], env_dims[1]);
+        if (1LL * env_dims[0] * env_dims[1] > (1LL << 28))
+            return fail(RDVB_ERR_UNSUPPORTED, "the environment image must have at most 2^28 pixels");
+        if (env_flags & ~(RDVB_SAMPLER_CLAMP | RDVB_SAMPLER_ALIGNED | RDVB_SAMPLER_LINEAR))
+            return fail(RDVB_ERR_INVALID_ARG, "unknown env_flags bits 0x%x", env_flags);
+        if (n_rays > 0 && (!env_image || !aligned(env_image, 4)))
+            return fail(RDVB_ERR_INVALID_ARG, "env_image must be a 4-byte aligned device pointer");
+        e.env_kind = 1;
+        e.env = env_image;
+        e.env_h = env_dims[0];
+        e.env_w = env_dims[1];
+        e.env_clamp = (env_flags & RDVB_SAMPLER_CLAMP) ? 1 : 0;
+        e.env_aligned = (env_flags & RDVB_SAMPLER_ALIGNED) ? 1 : 0;
+        e.env_linear = (env_flags & RDVB_SAMPLER_LINEAR) ? 1 : 0;
+    } else {
+        return fail(RDVB_ERR_INVALID_ARG, "env_kind must be RDVB_ENV_CONSTANT or RDVB_ENV_EQUIRECT, got %d", env_kind);
+    }
+    if (n_rays == 0) return RDVB_OK;
+    e.out = out;
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev,
+                             static_cast<cudaStream_t>(stream), March::kPbvr, &e);
 }
 
 namespace {

@@ -58,6 +58,42 @@ __device__ __forceinline__ void coord(float xc, int dim, float ac, bool border, 
     chi = min(max(hi, 0), dim - 1);
 }
 
+// Channel k of a 2-D lookup into t [dim0, dim1, out] at (x0, x1) (x1 runs
+// along dim0), with the kernel's arithmetic: the IN = 2 case of
+// tensor_sampler_kernel, and the environment lookup of an equirectangular
+// image (XRProject >> TensorSampler) in the PBVR kernel.
+__device__ __forceinline__ float sample2(const float* __restrict__ t, int dim0, int dim1, int out, int k, float x0,
+                                         float x1, bool border, bool aligned, bool linear) {
+    const float ac = aligned ? 1.0f : 0.0f;
+    int lo[2], clo[2], chi[2];
+    float alpha[2];
+    bool lo_in[2], hi_in[2];
+    coord(x1, dim0, ac, border, lo[0], clo[0], chi[0], alpha[0], lo_in[0], hi_in[0]);
+    coord(x0, dim1, ac, border, lo[1], clo[1], chi[1], alpha[1], lo_in[1], hi_in[1]);
+    const long long st0 = static_cast<long long>(out) * dim1, st1 = out;
+    if (!linear) {
+        bool inside = true;
+        long long off = k;
+        const int dims[2] = {dim0, dim1};
+        const long long st[2] = {st0, st1};
+#pragma unroll
+        for (int d = 0; d < 2; ++d) {
+            int id = lo[d] + (alpha[d] >= 0.5f ? 1 : 0);
+            inside = inside && id >= 0 && id < dims[d];
+            id = min(max(id, 0), dims[d] - 1);
+            off += id * st[d];
+        }
+        return (border || inside) ? __ldg(t + off) : 0.0f;
+    }
+    const long long dl = static_cast<long long>(chi[1] - clo[1]) * st1;
+    const long long base = clo[0] * st0 + clo[1] * st1 + k;
+    const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st0;
+    float v = 0.0f;
+    v = blend_pair(t, base, dl, lo_in[0] && lo_in[1], lo_in[0] && hi_in[1], alpha[1], __fsub_rn(1.0f, alpha[0]), v);
+    v = blend_pair(t, base + d0, dl, hi_in[0] && lo_in[1], hi_in[0] && hi_in[1], alpha[1], alpha[0], v);
+    return v;
+}
+
 template <int IN>
 __global__ void tensor_sampler_kernel(const __grid_constant__ Params p) {
     const long long total = p.n * p.out;
@@ -99,11 +135,8 @@ __global__ void tensor_sampler_kernel(const __grid_constant__ Params p) {
         if constexpr (IN == 1) {
             out = blend_pair(p.t, clo[0] * st[0] + k, dl, lo_in[0], hi_in[0], alpha[0], 1.0f, out);
         } else if constexpr (IN == 2) {
-            const long long base = clo[0] * st[0] + clo[1] * st[1] + k;
-            const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st[0];
-            out = blend_pair(p.t, base, dl, lo_in[0] && lo_in[1], lo_in[0] && hi_in[1], alpha[1],
-                             __fsub_rn(1.0f, alpha[0]), out);
-            out = blend_pair(p.t, base + d0, dl, hi_in[0] && lo_in[1], hi_in[0] && hi_in[1], alpha[1], alpha[0], out);
+            out = sample2(p.t, p.dim[0], p.dim[1], p.out, k, __ldg(p.x + i * 2), __ldg(p.x + i * 2 + 1), border,
+                          p.aligned != 0, true);
         } else {
             long long ptr = clo[0] * st[0] + clo[1] * st[1] + clo[2] * st[2] + k;
             const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st[0];

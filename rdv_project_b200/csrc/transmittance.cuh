@@ -66,10 +66,11 @@ struct Params {
     int maxw;               // widest activation (>= 3)
     int w_floats;           // floats of the shared weight image (weight blocks, then biases)
     Layer layer[kMaxLayers];
-    // ratiotracking_kernel only
-    const float* maj;       // majorant voxels [D, H, W] (z, y, x)
+    // ratiotracking_kernel / pbvr_kernel only
+    const float* maj;       // majorant voxels [D, H, W] (z, y, x), [D, H, W, 2] for a sphere field
     int mdim[3];            // W, H, D: cells along x, y, z
     float mvs[3];           // voxel sizes 2 / mdim (fp32 division, as the reference's vec3(2.0) / dim)
+    int field;              // 0 VoxelMajorantField, 1 SphereMajorantField
     unsigned seeds[4];      // the dispatch's generator seeds
     int draws_before;       // draws of each ray's generator already used upstream (a jittered camera: 2)
     // chain_rows_kernel only
@@ -323,6 +324,43 @@ __device__ __forceinline__ float voxel_majorant(const Params& p, const float (&x
     return __ldg(p.maj + (static_cast<long long>(cell[2]) * p.mdim[1] + cell[1]) * p.mdim[0] + cell[0]);
 }
 
+// SphereMajorantField (rdv/shaders/volumes/sphere_majorant_field.h): the
+// cell holding x stores (majorant, radius in voxel units); the returned
+// distance is to the exit, along w, of the box of that half-width around
+// the cell's centre, at least 1e-6.
+__device__ __forceinline__ float sphere_majorant(const Params& p, const float (&x)[3], const float (&w)[3],
+                                                 float& dist) {
+    int cell[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float f = static_cast<float>(p.mdim[k]);
+        int c = static_cast<int>(__fmul_rn(__fadd_rn(__fmul_rn(x[k], 0.5f), 0.5f), f));
+        cell[k] = min(max(c, 0), p.mdim[k] - 1);
+    }
+    const long long idx = (static_cast<long long>(cell[2]) * p.mdim[1] + cell[1]) * p.mdim[0] + cell[0];
+    const float majv = __ldg(p.maj + 2 * idx), radius = __ldg(p.maj + 2 * idx + 1);
+    float texit[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float vs = p.mvs[k];
+        const float center = __fsub_rn(__fmul_rn(__fadd_rn(static_cast<float>(cell[k]), 0.5f), vs), 1.0f);
+        const float half = __fmul_rn(radius, vs);
+        const float t0 = __fdiv_rn(__fsub_rn(__fsub_rn(center, half), x[k]), w[k]);
+        const float t1 = __fdiv_rn(__fsub_rn(__fadd_rn(center, half), x[k]), w[k]);
+        texit[k] = t0 < t1 ? t1 : t0;  // GLSL max
+    }
+    float dd = texit[1] < texit[0] ? texit[1] : texit[0];  // GLSL min
+    dd = texit[2] < dd ? texit[2] : dd;
+    dist = dd < 1e-6f ? 1e-6f : dd;  // max(dist, 1e-6)
+    return majv;
+}
+
+// The node's majorant field at (x, w): (majorant, max step).
+__device__ __forceinline__ float field_majorant(const Params& p, const float (&x)[3], const float (&w)[3],
+                                                float& dist) {
+    return p.field == 1 ? sphere_majorant(p, x, w, dist) : voxel_majorant(p, x, w, dist);
+}
+
 constexpr int kRtSafety = 1024;  // ratiotracking_transmittance_trait.h's loop cap
 
 // Work is warp-coherent: each lane advances its own ray (free flights across
@@ -371,7 +409,7 @@ __global__ void __launch_bounds__(NT) ratiotracking_kernel(const __grid_constant
             }
             ++safety;
             float dist;
-            maj = voxel_majorant(p, x, w, dist);
+            maj = field_majorant(p, x, w, dist);
             maj = maj < 1e-12f ? 1e-12f : maj;
             dist = dist < 1e-6f ? 1e-6f : dist;
             const float q = __fdiv_rn(-logf(__fsub_rn(1.0f, rng_uniform(r))), __fmul_rn(maj, p.scale));

@@ -218,6 +218,50 @@ class TensorSampler(Map):
         return RDVObject(out)
 
 
+class Constant(Map):
+    """f(x) = data for every x (rdv/maths/__init__.py:1659-1668,
+    rdv/shaders/maps/constant.h): OUT = data's last dimension, IN generic.
+    PBVR takes a Constant[3, 3] as a uniform environment."""
+
+    def __init__(self, data, in_size=None) -> None:
+        t = data._tensor if isinstance(data, RDVObject) else torch.as_tensor(data, dtype=torch.float32)
+        self.data = t.reshape(-1).to(torch.float32)
+        self.IN = in_size
+        self.OUT = int(self.data.numel())
+
+    def _bind(self, in_size=None, out_size=None):
+        if self.IN is not None or in_size is None:
+            return self
+        return Constant(self.data, in_size)
+
+    def __call__(self, *args, **kwargs):
+        if len(args) != 1:
+            raise TypeError("a Map is called with exactly one input tensor")
+        xt = _device_tensor(args[0])
+        dev = current_device()
+        out = self.data.to(dev).expand(list(xt.shape[:-1]) + [self.OUT]).contiguous()
+        return RDVObject(out)
+
+
+class XRProject(Map):
+    """Map[3, 2]: a direction's equirectangular coordinates
+    (rdv/domain/rendering.py:150-160, rdv/shaders/rendering/xr_project.h,
+    dir2xr of rdv/shaders/libraries/math_library.h:265-276):
+    (atan(w.x, w.z) / pi, asin(clamp(w.y, -1, 1)) * 2 / pi) ->
+    rdvb_xr_project. ``XRProject() >> TensorSampler(image [H, W, C])`` looks
+    an environment image up by direction (PBVR's environment)."""
+
+    IN = 3
+    OUT = 2
+
+    def _project(self, x2d: torch.Tensor, y2d: torch.Tensor) -> None:
+        N.check(N.lib().rdvb_xr_project(x2d.data_ptr(), x2d.shape[0], y2d.data_ptr(), stream_handle()),
+                "rdvb_xr_project")
+
+
+dir2xr = XRProject()
+
+
 class Composite(Map):
     """f(g(x)); g's OUT must match f's IN."""
 
@@ -267,8 +311,8 @@ def _lower(m: Map):
     layers = []
     relus = []
     for op in m._ops():
-        if isinstance(op, TensorSampler):
-            raise NotImplementedError("a TensorSampler must come first in the chain (its input encoding)")
+        if isinstance(op, (TensorSampler, XRProject)):
+            raise NotImplementedError(f"a {type(op).__name__} must come first in the chain (its input encoding)")
         if isinstance(op, _LinearBase):
             layers.append(op)
             relus.append(False)
@@ -296,13 +340,17 @@ class _ChainPlan:
 
     def __init__(self, m: Map, dev):
         ops = m._ops()
+        self.project = ops[0] if ops and isinstance(ops[0], XRProject) else None
+        if self.project is not None:
+            ops = ops[1:]
         self.prologue = ops[0] if ops and isinstance(ops[0], TensorSampler) else None
-        rest = m
         if self.prologue is not None:
-            rest = _compose_ops(ops[1:])
+            ops = ops[1:]
+        rest = _compose_ops(ops)
         self.input_relu, self.layers, self.relus = _lower(rest) if rest is not None else (False, [], [])
         self.dev = dev
-        self.dims = [self.prologue.OUT if self.prologue is not None else m.IN] + [l.OUT for l in self.layers]
+        first = self.prologue.OUT if self.prologue is not None else (2 if self.project is not None else m.IN)
+        self.dims = [first] + [l.OUT for l in self.layers]
         self.flags = [l._math | (N.RDVB_LAYER_RELU if r else 0) for l, r in zip(self.layers, self.relus)]
         self.packed = None
         self.packed_key = None
@@ -350,6 +398,14 @@ def run_chain(plan: _ChainPlan, x2d: torch.Tensor, y2d: torch.Tensor, tail_exact
     rows = x2d.shape[0]
     if rows == 0:
         return
+    if plan.project is not None:
+        xs = x2d if x2d.dtype == torch.float32 else x2d.float()
+        last = plan.prologue is None and not plan.layers and not plan.input_relu
+        coords = y2d if last else torch.empty(rows, 2, dtype=torch.float32, device=x2d.device)
+        plan.project._project(xs.contiguous(), coords)
+        if last:
+            return
+        x2d = coords
     if plan.prologue is not None:
         feats = torch.empty(rows, plan.prologue.OUT, dtype=torch.float32, device=x2d.device)
         xs = x2d if x2d.dtype == torch.float32 else x2d.float()

@@ -29,7 +29,7 @@ import torch
 
 from . import _native as N
 from .core import RDVObject, _timed, current_device, stream_handle, wrap
-from .maps import Map, _ChainPlan
+from .maps import Map, XRProject, _ChainPlan, dir2xr
 
 
 class Cameras:
@@ -90,11 +90,12 @@ class _CameraGrid:
     def __call__(self, seeds=None) -> RDVObject:
         """One dispatch of the composition. A node that draws random numbers
         (RatiotrackingTransmittance) continues each pixel's generator after
-        the camera's draws, as the reference's single per-thread state does:
+        the camera's draws, as the reference's single per-thread state does
+        (RatiotrackingTransmittance, PBVR):
         the same seeds, 2 draws already taken when the camera jitters."""
-        from .volumes import RatiotrackingTransmittance, _draw_seeds
+        from .volumes import _draw_seeds
 
-        if isinstance(self.map, RatiotrackingTransmittance):
+        if getattr(self.map, "_draws_random", False):
             seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
             rays = self.cameras(seeds=seeds) if self.cameras.pixel_jitter else self.cameras()
             return self.map(rays, seeds=seeds, draws_before=2 if self.cameras.pixel_jitter else 0)

@@ -36,7 +36,7 @@ import torch
 
 from . import _native as N
 from .core import RDVObject, _timed, current_device, stream_handle, wrap
-from .maps import Map, _lower
+from .maps import Composite, Constant, Map, TensorSampler, XRProject, _lower
 
 _IDENTITY = (1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0)
 
@@ -150,13 +150,39 @@ class VoxelMajorantField:
         self.grid = grid
 
 
-def _as_majorant_field(majorant) -> VoxelMajorantField:
+class SphereMajorantField:
+    """Map[6, 2] (rdv/domain/volumes.py:215-224,
+    rdv/shaders/volumes/sphere_majorant_field.h): ``grid`` is a Grid[3, 2]
+    over [-1, 1]^3 holding per voxel (majorant, radius), the radius a
+    half-width in voxels of the box around the voxel's centre that the
+    majorant bounds. For an object-space position and direction: the
+    majorant of the voxel holding the position and the distance along the
+    direction to that box's exit (at least 1e-6), so one free flight may
+    cross many voxels. A TensorGrid, or its tensor [D, H, W, 2]."""
+
+    def __init__(self, grid):
+        if not isinstance(grid, TensorGrid):
+            grid = TensorGrid(grid)
+        assert grid.IN == 3 and grid.OUT == 2, "the sphere majorant grid must be a Grid[3, 2]"
+        self.grid = grid
+
+
+def _as_majorant_field(majorant):
     """volumes.py:227-242: a field as given, a Grid[3, 1] wrapped as a voxel field."""
-    if isinstance(majorant, VoxelMajorantField):
+    if isinstance(majorant, (VoxelMajorantField, SphereMajorantField)):
         return majorant
     if isinstance(majorant, (TensorGrid, torch.Tensor, RDVObject)):
         return VoxelMajorantField(majorant)
-    raise NotImplementedError("majorant must be a VoxelMajorantField or a Grid[3, 1]")
+    raise NotImplementedError("majorant must be a VoxelMajorantField, a SphereMajorantField or a Grid[3, 1]")
+
+
+def _field_args(field, dev):
+    """(device grid, [D, H, W], RDVB_MAJORANT_*) of a majorant field."""
+    g = field.grid.data
+    if g.device != dev or g.dtype != torch.float32 or not g.is_contiguous():
+        g = g.to(device=dev, dtype=torch.float32).contiguous()
+    kind = N.RDVB_MAJORANT_SPHERE if isinstance(field, SphereMajorantField) else N.RDVB_MAJORANT_VOXEL
+    return g, list(g.shape[:3]), kind
 
 
 def _draw_seeds():
@@ -167,6 +193,8 @@ def _draw_seeds():
 
 class RatiotrackingTransmittance(RaymarchingTransmittance):
     """Map[6, 1]: ray -> ratio-tracking estimate of the transmittance."""
+
+    _draws_random = True
 
     def __init__(self, extinction: Map, majorant, transform=None, density_scale: float = 1.0):
         super().__init__(extinction, transform=transform, density_scale=density_scale)
@@ -184,9 +212,7 @@ class RatiotrackingTransmittance(RaymarchingTransmittance):
             r2 = r2.to(device=dev, dtype=torch.float32).contiguous()
         out = torch.empty(lead + [1], dtype=torch.float32, device=dev)
         st = self._device_state(dev)
-        g = self.majorant.grid.data
-        if g.device != dev or g.dtype != torch.float32 or not g.is_contiguous():
-            g = g.to(device=dev, dtype=torch.float32).contiguous()
+        g, gdims, kind = _field_args(self.majorant, dev)
         seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
         assert len(seeds) == 4, "seeds must be 4 integers"
         self.last_seeds = seeds
@@ -196,9 +222,94 @@ class RatiotrackingTransmittance(RaymarchingTransmittance):
         with _timed():
             N.check(N.lib().rdvb_transmittance_rt(
                 r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.density_scale, g.data_ptr(),
-                N.int_array(list(g.shape[:3])), N.uint32_array(seeds), int(draws_before), n,
+                N.int_array(gdims), kind, N.uint32_array(seeds), int(draws_before), n,
                 N.int_array(st["dims"]),
                 N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
                 N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
                 stream_handle()), "rdvb_transmittance_rt")
+        return RDVObject(out)
+
+
+def _environment_args(env, dev):
+    """(RDVB_ENV_*, rgb, image, [H, W], sampler flags) of a PBVR
+    environment: a Constant of 3 values, or XRProject() >> TensorSampler of
+    a [H, W, 3] image."""
+    if isinstance(env, Constant):
+        assert env.OUT == 3, "a constant environment holds 3 values (RGB)"
+        return N.RDVB_ENV_CONSTANT, [float(v) for v in env.data.tolist()], None, [0, 0], 0
+    if isinstance(env, Composite) and isinstance(env.g, XRProject) and isinstance(env.f, TensorSampler):
+        smp = env.f
+        assert smp.IN == 2 and smp.OUT == 3, "the environment image must be [H, W, 3]"
+        img = smp.t._tensor
+        if img.device != dev or img.dtype != torch.float32 or not img.is_contiguous():
+            img = img.to(device=dev, dtype=torch.float32).contiguous()
+        flags = ((N.RDVB_SAMPLER_CLAMP if smp.clamp else 0) | (N.RDVB_SAMPLER_ALIGNED if smp.aligned else 0) |
+                 (N.RDVB_SAMPLER_LINEAR if smp.linear else 0))
+        return N.RDVB_ENV_EQUIRECT, [0.0, 0.0, 0.0], img, list(img.shape[:2]), flags
+    raise NotImplementedError("the environment must be a Constant[3, 3] or XRProject() >> TensorSampler(image)")
+
+
+class PBVR(RaymarchingTransmittance):
+    """Map[6, 3]: ray -> one unbiased delta-tracking sample of the radiance
+    along it (rdv/domain/volumes.py:257-326, rdv/shaders/volumes/pbvr.h);
+    averaged over dispatches it converges to the volume's rendering.
+
+    ``extinction`` is a Map[3, 1] in the [-1, 1]^3 box (Linear / LinearFast
+    / ReLU chain); ``environment`` a Map[3, 3] from a world direction to RGB
+    radiance: ``Constant((r, g, b))`` or ``XRProject() >> TensorSampler(image
+    [H, W, 3])``; ``majorant`` a VoxelMajorantField, a SphereMajorantField,
+    or a bare Grid[3, 1] wrapped as a voxel field; ``transform`` the node's
+    mat4x3; ``albedo`` (RGB) and ``g`` (Henyey-Greenstein anisotropy) are
+    uniform; ``max_bounces`` bounds the real scattering events of a path.
+    The extinction is used unscaled (PBVR has no density scale). Each call
+    draws fresh generator seeds, as the reference does per dispatch;
+    ``node(rays, seeds=...)`` fixes them (rdvb_pbvr)."""
+
+    OUT = 3
+    _draws_random = True
+
+    def __init__(self, extinction: Map, environment: Map, majorant, transform=None, albedo=(1.0, 1.0, 1.0),
+                 g: float = 0.0, max_bounces: int = 32) -> None:
+        super().__init__(extinction, transform=transform)
+        del self.step_size, self.density_scale
+        env = environment
+        if env.__is_generic__:
+            env = env._bind(in_size=3, out_size=3)
+        assert env.IN == 3 and env.OUT == 3, "environment must be a Map[3, 3]"
+        self.environment = env
+        self.majorant = _as_majorant_field(majorant)
+        a = torch.as_tensor(albedo, dtype=torch.float32).reshape(-1)
+        assert a.numel() == 3, "albedo must hold 3 values"
+        self.albedo = tuple(float(v) for v in a)
+        self.g = float(g)
+        self.max_bounces = int(max_bounces)
+        self.last_seeds = None
+
+    def __call__(self, rays, seeds=None, draws_before: int = 0):
+        dev = current_device()
+        rt = rays._tensor if isinstance(rays, RDVObject) else wrap(rays)._tensor
+        assert rt.shape[-1] == 6, f"input's last dimension ({rt.shape[-1]}) must match the map's IN (6)"
+        lead = list(rt.shape[:-1])
+        r2 = rt.reshape(-1, 6)
+        if r2.device != dev or r2.dtype != torch.float32 or not r2.is_contiguous():
+            r2 = r2.to(device=dev, dtype=torch.float32).contiguous()
+        out = torch.empty(lead + [3], dtype=torch.float32, device=dev)
+        st = self._device_state(dev)
+        g, gdims, kind = _field_args(self.majorant, dev)
+        env_kind, env_rgb, env_img, env_dims, env_flags = _environment_args(self.environment, dev)
+        seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
+        assert len(seeds) == 4, "seeds must be 4 integers"
+        self.last_seeds = seeds
+        if st["ws"] is None:
+            st["ws"] = torch.empty(256, dtype=torch.uint8, device=dev)
+        n = len(st["layers"])
+        with _timed():
+            N.check(N.lib().rdvb_pbvr(
+                r2.data_ptr(), r2.shape[0], N.float_array(self.transform), g.data_ptr(), N.int_array(gdims), kind,
+                N.float_array(self.albedo), self.g, self.max_bounces, env_kind, N.float_array(env_rgb),
+                env_img.data_ptr() if env_img is not None else None, N.int_array(env_dims), env_flags,
+                N.uint32_array(seeds), int(draws_before), n, N.int_array(st["dims"]),
+                N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
+                N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
+                stream_handle()), "rdvb_pbvr")
         return RDVObject(out)

@@ -5,6 +5,7 @@ the default in oracle/_clib.py):
 
     python tests/golden/make_golden.py            # every fixture
     python tests/golden/make_golden.py coopmat    # coopmat.npz only
+    python tests/golden/make_golden.py pbvr       # pbvr.npz only
 
 Three sources, all the reference's own code:
 
@@ -20,6 +21,9 @@ Three sources, all the reference's own code:
   simple,fast,mine}.h and tensors/conv2d_tensor_op_winograd3x3.h, executed
   on the CPU by 32-thread workgroups (oracle/ref_shim/coopmat_prelude.hpp
   gives coopMatMulAdd its ascending-k fp32 summation);
+* ``oracle/_ref/libref_pbvr.so`` -- the reference's PBVR body
+  (volumes/pbvr.h) and its Henyey-Greenstein sampler
+  (libraries/random_library.h) compiled as C++ (oracle/ref_shim/ref_pbvr.cpp);
 * ``rdv/domain/nn.py``'s torch helpers ``_winograd_transform_weight``,
   ``_tile_weight_fp16`` and ``_cast_fp16`` and its ``_WINOGRAD_G`` table,
   executed from the reference source. The package itself cannot be
@@ -44,7 +48,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from oracle._clib import REFERENCE_ROOT, ptr, ptr_array, ref_coopmat_lib, ref_lib  # noqa: E402
+from oracle._clib import REFERENCE_ROOT, ptr, ptr_array, ref_coopmat_lib, ref_lib, ref_pbvr_lib  # noqa: E402
 
 
 def xavier_uniform(rng, out_f, in_f):
@@ -197,6 +201,7 @@ def main():
                         rng_draws=rng_draws, media=media, x=rt_x, w=rt_w, d=rt_d, index=rt_index, grids=grids,
                         T=rt_T)
     coopmat_goldens()
+    pbvr_goldens()
     print("golden fixtures written to", HERE)
 
 
@@ -268,8 +273,68 @@ def coopmat_goldens():
     np.savez_compressed(os.path.join(HERE, "coopmat.npz"), **out)
 
 
+def pbvr_goldens():
+    """pbvr.npz: PBVR.forward of the reference (volumes/pbvr.h) over world
+    rays [n, 6] with the analytic extinction c0 + c1 |x|^2, a constant
+    environment, a voxel and a sphere majorant field, several albedos,
+    anisotropies and bounce budgets, an identity and a scaled + shifted
+    transform (inverse exact in any formula); and hg_phase_sample
+    directions for a few g (the uniform branch |g| < 0.001 included)."""
+    lib = ref_pbvr_lib()
+    rng = np.random.default_rng(424242)
+    n = 384
+    o = rng.uniform(-3, 3, (n, 3)).astype(np.float32)
+    t = rng.uniform(-0.8, 0.8, (n, 3)).astype(np.float32)
+    w = t - o
+    w /= np.linalg.norm(w, axis=1, keepdims=True)
+    w = w.astype(np.float32)
+    w[: n // 8] *= -1.0                       # pointing away: misses
+    o[n // 8: n // 4] *= np.float32(0.2)       # starting inside the box
+    rays = np.ascontiguousarray(np.concatenate([o, w], 1).astype(np.float32))
+    seeds = np.array([123457, 98765432, 5550123, 777777], np.uint32)
+    c0, c1 = np.float32(0.5), np.float32(2.0)
+    D, H, W = 3, 4, 5
+    vox = (rng.uniform(1.0, 1.3, (D, H, W)) * (c0 + 3 * c1)).astype(np.float32)
+    sph = np.stack([vox, rng.uniform(0.5, 2.5, (D, H, W)).astype(np.float32)], -1).astype(np.float32)
+    env = np.array([0.3, 0.6, 0.9], np.float32)
+    identity = np.array([1, 0, 0, 0, 1, 0, 0, 0, 1, 0, 0, 0], np.float32)
+    scaled = np.array([2, 0, 0, 0, 0.5, 0, 0, 0, 4, 0.25, -0.5, 1.0], np.float32)
+    # (field kind, g, albedo, max bounces, transform)
+    cases = [(0, 0.0, (0.9, 0.8, 0.7), 32, 0), (0, 0.6, (0.95, 0.9, 0.99), 8, 0), (0, -0.4, (1, 1, 1), 3, 1),
+             (1, 0.0, (0.9, 0.8, 0.7), 32, 0), (1, 0.6, (0.95, 0.9, 0.99), 8, 1), (1, 0.0005, (0.5, 0.5, 0.5), 0, 0)]
+    kinds = np.array([c[0] for c in cases], np.int32)
+    gs = np.array([c[1] for c in cases], np.float32)
+    albedos = np.array([c[2] for c in cases], np.float32)
+    bounces = np.array([c[3] for c in cases], np.int32)
+    transforms = np.stack([identity, scaled])[[c[4] for c in cases]].astype(np.float32)
+    out = np.zeros((len(cases), n, 3), np.float32)
+    for k, (kind, g, alb, mb, _) in enumerate(cases):
+        grid = vox if kind == 0 else sph
+        lib.ref_pbvr(ctypes.c_float(c0), ctypes.c_float(c1), int(kind), ptr(grid), D, H, W, ptr(env),
+                     ptr(np.ascontiguousarray(transforms[k])), ptr(np.ascontiguousarray(albedos[k])),
+                     ctypes.c_float(g), int(mb), ptr(seeds), ptr(rays), n, ptr(out[k]))
+    hg_g = np.array([0.0, 0.0005, 0.3, -0.7, 0.95], np.float32)
+    hg_w = rng.standard_normal((24, 3)).astype(np.float32)
+    hg_w /= np.linalg.norm(hg_w, axis=1, keepdims=True)
+    hg_w[0] = [0.0, 0.0, 1.0]
+    hg_w[1] = [0.0, 0.0, -1.0]
+    hg_w = hg_w.astype(np.float32)
+    hg_index = rng.integers(0, 1 << 20, size=24).astype(np.int64)
+    hg_out = np.zeros((hg_g.size, 24, 3), np.float32)
+    for a, g in enumerate(hg_g):
+        for i in range(24):
+            lib.ref_hg_phase_sample(ptr(seeds), int(hg_index[i]), 3, ptr(np.ascontiguousarray(hg_w[i])),
+                                    ctypes.c_float(g), ptr(hg_out[a, i]))
+    np.savez_compressed(os.path.join(HERE, "pbvr.npz"), rays=rays, seeds=seeds, c0=c0, c1=c1, vox=vox, sph=sph,
+                        env=env, kinds=kinds, g=gs, albedo=albedos, max_bounces=bounces, transforms=transforms,
+                        out=out, hg_g=hg_g, hg_w=hg_w, hg_index=hg_index, hg_draws_before=np.int32(3),
+                        hg_out=hg_out)
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["coopmat"]:
         coopmat_goldens()
+    elif sys.argv[1:] == ["pbvr"]:
+        pbvr_goldens()
     else:
         main()

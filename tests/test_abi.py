@@ -87,25 +87,70 @@ def test_ratio_tracking_validation_before_any_device_work(lib):
 
     dims, flags = N.int_array([3, 16, 1]), N.int_array([1, 1])
     seeds = N.uint32_array([1, 2, 3, 4])
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 0, 2, dims, None, None,
-                                   flags, 0, None, 256, None, None)
+    vox = N.RDVB_MAJORANT_VOXEL
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), vox, seeds, 0, 2, dims, None,
+                                   None, flags, 0, None, 256, None, None)
     assert rc == -1 and "weights" in N.last_error()
     w = N.ptr_array([1, 1])
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), seeds, 0, 2, dims, w, w, flags,
-                                   0, None, 256, None, None)
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), vox, seeds, 0, 2, dims, w, w,
+                                   flags, 0, None, 256, None, None)
     assert rc == -1 and "majorant_dims" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), None, 0, 2, dims, w, w, flags,
-                                   0, None, 256, None, None)
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, None, 0, 2, dims, w, w,
+                                   flags, 0, None, 256, None, None)
     assert rc == -1 and "seeds" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 0, 2,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, seeds, 0, 2,
                                    N.int_array([3, 16, 2]), w, w, flags, 0, None, 256, None, None)
     assert rc == -1 and "3 -> 1" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), seeds, -1, 2, dims, w, w, flags,
-                                   0, None, 256, None, None)
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, seeds, -1, 2, dims, w, w,
+                                   flags, 0, None, 256, None, None)
     assert rc == -1 and "draws_before" in N.last_error()
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), 7, seeds, 0, 2, dims, w, w,
+                                   flags, 0, None, 256, None, None)
+    assert rc == -1 and "majorant_kind" in N.last_error()
     # nothing to do: no device needed
-    assert lib.rdvb_transmittance_rt(None, 0, None, 1.0, None, N.int_array([2, 2, 2]), seeds, 0, 2, dims, w, w, flags,
-                                     0, None, 256, None, None) == 0
+    for kind in (N.RDVB_MAJORANT_VOXEL, N.RDVB_MAJORANT_SPHERE):
+        assert lib.rdvb_transmittance_rt(None, 0, None, 1.0, None, N.int_array([2, 2, 2]), kind, seeds, 0, 2, dims,
+                                         w, w, flags, 0, None, 256, None, None) == 0
+
+
+def _pbvr(lib, N, *, n=4, kind=0, albedo=(1.0, 1.0, 1.0), g=0.0, max_bounces=4, env_kind=0, env_rgb=(1, 1, 1),
+          env_dims=(4, 8), env_flags=0, seeds=(1, 2, 3, 4), dims=(3, 16, 1), w=(1, 1)):
+    return lib.rdvb_pbvr(None, n, None, None, N.int_array([2, 2, 2]), kind,
+                         N.float_array(albedo) if albedo is not None else None, g, max_bounces, env_kind,
+                         N.float_array(env_rgb) if env_rgb is not None else None, None,
+                         N.int_array(env_dims) if env_dims is not None else None, env_flags,
+                         N.uint32_array(seeds) if seeds is not None else None, 0, len(dims) - 1,
+                         N.int_array(dims), N.ptr_array(w), N.ptr_array(w), N.int_array([1] * (len(dims) - 1)), 0,
+                         None, 256, None, None)
+
+
+def test_pbvr_validation_before_any_device_work(lib):
+    """rdvb_pbvr checks its arguments on the host, before any device work;
+    a call without rays succeeds without a device."""
+    import rdv_project_b200._native as N
+
+    assert _pbvr(lib, N, n=0) == 0
+    assert _pbvr(lib, N, n=0, kind=N.RDVB_MAJORANT_SPHERE, env_kind=N.RDVB_ENV_EQUIRECT, env_rgb=None) == 0
+    cases = [
+        (dict(kind=3), "majorant_kind"),
+        (dict(seeds=None), "seeds"),
+        (dict(dims=(3, 16, 3)), "3 -> 1"),
+        (dict(albedo=None, n=0), "albedo"),
+        (dict(max_bounces=-1, n=0), "max_bounces"),
+        (dict(g=float("nan"), n=0), "g must be finite"),
+        (dict(env_kind=5, n=0), "env_kind"),
+        (dict(env_rgb=None, n=0), "env_rgb"),
+        (dict(env_kind=N.RDVB_ENV_EQUIRECT, env_dims=None, n=0), "env_dims"),
+        (dict(env_kind=N.RDVB_ENV_EQUIRECT, env_dims=(0, 8), n=0), "env_dims"),
+        (dict(env_kind=N.RDVB_ENV_EQUIRECT, env_flags=8, n=0), "env_flags"),
+        (dict(env_kind=N.RDVB_ENV_EQUIRECT), "rays, majorant and out"),
+    ]
+    for kw, msg in cases:
+        rc = _pbvr(lib, N, **kw)
+        assert rc == -1 and msg in N.last_error(), (kw, rc, N.last_error())
+    assert lib.rdvb_xr_project(None, 0, None, None) == 0
+    assert lib.rdvb_xr_project(None, -1, None, None) == -1
+    assert lib.rdvb_xr_project(None, 3, None, None) == -1 and "aligned" in N.last_error()
 
 
 def test_volume_nodes_host_side():

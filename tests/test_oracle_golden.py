@@ -294,3 +294,78 @@ def test_live_reference_coopmat_library_agrees_with_fixture(golden):
     y = np.zeros_like(g["small_64_32_y"])
     lib.ref_cm_small_64_32(ptr(x), x.shape[0], ptr(W), ptr(b), ptr(y))
     np.testing.assert_array_equal(y, g["small_64_32_y"])
+
+
+def _pbvr_case(g, k):
+    c0, c1 = np.float32(g["c0"]), np.float32(g["c1"])
+
+    def ext(p):
+        return (c0 + c1 * ((p[:, 0] * p[:, 0] + p[:, 1] * p[:, 1]) + p[:, 2] * p[:, 2])).astype(np.float32)
+
+    if int(g["kinds"][k]) == 0:
+        field = lambda x, w: orm.voxel_majorant(g["vox"], x, w)  # noqa: E731
+    else:
+        field = lambda x, w: orm.sphere_majorant(g["sph"], x, w)  # noqa: E731
+    rays = g["rays"]
+    return orm.pbvr(rays[:, :3], rays[:, 3:], ext, orm.constant_environment(g["env"]), field, g["seeds"],
+                    transform=g["transforms"][k], albedo=g["albedo"][k], g=float(g["g"][k]),
+                    max_bounces=int(g["max_bounces"][k]))
+
+
+@pytest.mark.parametrize("k", range(6))
+def test_pbvr_restatement_bit_exact_vs_reference(golden, k):
+    """PBVR.forward (volumes/pbvr.h) of the oracle against the reference's
+    own body compiled as C++ (voxel and sphere majorant fields, isotropic
+    and forward/backward scattering, bounce budgets 0..32, an identity and
+    a scaled + shifted transform): the same draws, collisions, directions
+    and radiance on every ray."""
+    g = golden("pbvr.npz")
+    got = _pbvr_case(g, k)
+    np.testing.assert_array_equal(got, g["out"][k])
+    o, w = orm.object_space(g["rays"][:, :3], g["rays"][:, 3:], g["transforms"][k])
+    tmin, tmax = orm.ray_box(o, w)
+    miss = (tmax <= 0) | (tmin > tmax)
+    assert miss.any()
+    np.testing.assert_array_equal(g["out"][k][miss], np.broadcast_to(g["env"], (int(miss.sum()), 3)))
+
+
+def test_pbvr_fixture_covers_the_path_outcomes(golden):
+    """The fixture's paths reach every outcome: misses (environment), escapes
+    after scattering (attenuated environment) and terminations (0)."""
+    g = golden("pbvr.npz")
+    out, env = g["out"], g["env"]
+    assert (out == 0).all(axis=2).any()
+    assert (out == env).all(axis=2).any()
+    partial = (out > 0).all(axis=2) & (out < env).all(axis=2)
+    assert partial.any()
+    assert (out[5] <= env).all()   # max_bounces 0: no scattering survives
+
+
+def test_hg_phase_sample_bit_exact_vs_reference(golden):
+    """hg_phase_sample (random_library.h:224-239) of the oracle against the
+    reference's own function, after 3 draws of each invocation's generator."""
+    g = golden("pbvr.npz")
+    for a, gg in enumerate(g["hg_g"]):
+        st = orm.random_spawn(g["seeds"], g["hg_index"])
+        for _ in range(int(g["hg_draws_before"])):
+            orm.random_step(st)
+        got = orm.hg_phase_sample(g["hg_w"], float(gg), st)
+        np.testing.assert_array_equal(got, g["hg_out"][a])
+        np.testing.assert_allclose(np.linalg.norm(got.astype(np.float64), axis=1), 1.0, atol=1e-5)
+
+
+def test_live_reference_pbvr_library_agrees_with_fixture(golden):
+    """Where the reference checkout is present, its PBVR body rerun on the
+    fixture's first case gives the stored radiance."""
+    if not ref_lib_available():
+        pytest.skip("reference checkout not present")
+    from oracle._clib import ptr, ref_pbvr_lib
+    import ctypes
+
+    g = golden("pbvr.npz")
+    out = np.zeros_like(g["out"][0])
+    ref_pbvr_lib().ref_pbvr(ctypes.c_float(g["c0"]), ctypes.c_float(g["c1"]), 0, ptr(g["vox"]), 3, 4, 5,
+                            ptr(g["env"]), ptr(np.ascontiguousarray(g["transforms"][0])),
+                            ptr(np.ascontiguousarray(g["albedo"][0])), ctypes.c_float(g["g"][0]),
+                            int(g["max_bounces"][0]), ptr(g["seeds"]), ptr(g["rays"]), g["rays"].shape[0], ptr(out))
+    np.testing.assert_array_equal(out, g["out"][0])
