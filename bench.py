@@ -478,6 +478,7 @@ def secondary_summaries(args, local, headline):
     out["pbvr"] = pbvr_summary()
     out["chain"] = chain_summary()
     out["conv_tc"] = conv_family_summary()
+    out["samplers"] = sampler_summary()
     return out
 
 
@@ -1099,6 +1100,29 @@ def chain_summary(rows=1 << 20, steps=3):
     parity = omlp.rel_errors(got, omlp.mlp_forward(x_np, lay_np))
     return {"ms": _r(t_fused / steps * 1e3), "per_op_ms": _r(t_ops / steps * 1e3), "speedup": _r(t_ops / t_fused, 3),
             "exact_vs_per_op": same, "parity": _r(parity[1], 2)}
+
+
+def sampler_summary(points=1 << 24, steps=5):
+    """TensorSampler and GridSampler, trilinear with clamp, on a 64^3 x 8
+    fp32 grid (8 MiB, L2-resident) at 2^24 uniform points: points/s and the
+    HBM rate of the per-point stream (12 B of coordinates in, 32 B of
+    features out); the corner gathers hit L2."""
+    import rdv_project_b200 as rdv
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device="cpu").manual_seed(7)
+    t = torch.randn(64, 64, 64, 8, generator=g).to(dev)
+    x = (torch.rand(points, 3, generator=g) * 2 - 1).to(dev)
+    out = {}
+    for name, smp in (("tensor", rdv.TensorSampler(t)), ("grid", rdv.GridSampler(t))):
+        for _ in range(2):
+            smp(x)
+        torch.cuda.synchronize()
+        ms = time_steps(lambda: smp(x), steps) / steps * 1e3
+        out[name + "_ms"] = _r(ms)
+        out[name + "_gbs"] = _r(points * (12 + 32) / (ms * 1e-3) / 1e9)
+    out["points_per_s"] = _r(points / (out["grid_ms"] * 1e-3))
+    return out
 
 
 def conv_family_summary(steps=5):

@@ -264,6 +264,20 @@ int rdvb_conv2d_tc(const void* x, int x_dtype, int n, int h, int w, int cin, int
 int rdvb_tensor_sampler(const float* t, int in_dim, const int* shape, int out_dim, const float* x, int64_t n,
                         int clamp, int aligned, int linear, float* y, void* stream);
 
+/* GridSampler (rdv/maths/__init__.py:2018-2047,
+ * rdv/shaders/samplers/grid_sampler.h) over a dense grid (a TensorGrid,
+ * grids/tensor_grid.h): grid [shape[0], ..., shape[in_dim-1], out_dim] fp32
+ * row-major, x [n, in_dim] fp32 in [-1, 1]^in_dim (coordinate in_dim-1-d
+ * along dimension d) -> y [n, out_dim] fp32. Per dimension t = x * 0.5 +
+ * 0.5, pos = aligned ? t (D - 1) : t D - 0.5, voxel = floor(pos), alpha =
+ * pos - voxel; linear: the 2^in_dim corners in bit-mask order, weight the
+ * product of alpha / (1 - alpha) over the dimensions, corners outside the
+ * grid skipped unless clamp; nearest: voxel + (alpha >= 0.5). in_dim 1..4.
+ * (The TensorSampler computes its positions and blends differently, so the
+ * two samplers round differently on the same tensor.) */
+int rdvb_grid_sampler(const float* grid, int in_dim, const int* shape, int out_dim, const float* x, int64_t n,
+                      int clamp, int aligned, int linear, float* y, void* stream);
+
 /* 2x2 average pool, stride 2 (Downsample2xTensorOp, rdv/domain/nn.py:1090-1107,
  * rdv/shaders/tensors/downsample2x_tensor_op.h): x [h, w, c] fp32 -> y
  * [h/2, w/2, c], each output ((x00 + x01) + x10) + x11, times 0.25. h, w even;

@@ -10,6 +10,7 @@ ORACLE_LIB = os.path.join(HERE, "_build", "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_shaders.so")
 REF_COOPMAT_LIB = os.path.join(HERE, "_ref", "libref_coopmat.so")
 REF_PBVR_LIB = os.path.join(HERE, "_ref", "libref_pbvr.so")
+REF_SAMPLERS_LIB = os.path.join(HERE, "_ref", "libref_samplers.so")
 # The reference checkout: $RDV_REFERENCE_ROOT, else a checkout named
 # `reference` beside this repository.
 REFERENCE_ROOT = os.environ.get("RDV_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
@@ -19,6 +20,7 @@ _oracle = None
 _ref = None
 _ref_cm = None
 _ref_pbvr = None
+_ref_samplers = None
 
 
 def build_oracle(verbose: bool = False) -> None:
@@ -134,6 +136,22 @@ def ref_pbvr_lib() -> ctypes.CDLL:
         lib.ref_hg_phase_sample.restype = None
         _ref_pbvr = lib
     return _ref_pbvr
+
+
+def ref_samplers_lib() -> ctypes.CDLL:
+    """The reference's GridSampler body compiled as C++
+    (ref_shim/ref_samplers.cpp)."""
+    global _ref_samplers
+    if _ref_samplers is None:
+        if not os.path.exists(REF_SAMPLERS_LIB) and not ref_lib_available():
+            raise FileNotFoundError(
+                f"{REF_SAMPLERS_LIB} is missing and the reference checkout is not present to build it")
+        lib = ctypes.CDLL(REF_SAMPLERS_LIB)
+        vp, i32 = ctypes.c_void_p, ctypes.c_int
+        lib.ref_grid_sampler.argtypes = [i32, i32, vp, vp, i32, i32, i32, vp, ctypes.c_long, vp]
+        lib.ref_grid_sampler.restype = i32
+        _ref_samplers = lib
+    return _ref_samplers
 
 
 def ptr(a) -> int:

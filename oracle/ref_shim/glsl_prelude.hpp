@@ -97,6 +97,7 @@ static inline float max(int a, double b) { return (float)a > (float)b ? (float)a
 static inline float max(float a, double b) { return a > (float)b ? a : (float)b; }
 static inline float max(double a, float b) { return (float)a > b ? (float)a : b; }
 static inline float max(float a, float b) { return a > b ? a : b; }
+static inline float max(int a, float b) { return (float)a < b ? b : (float)a; }
 static inline int min(int a, int b) { return a < b ? a : b; }
 
 #define vec3 rdv_vec3

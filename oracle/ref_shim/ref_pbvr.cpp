@@ -38,7 +38,6 @@ static inline rdv_farr_t<sizeof...(T)> rdv_farr(T... a) { return {{static_cast<f
 static inline rdv_vec3 operator-(rdv_vec3 a, rdv_vec3 b) { return rdv_vec3(a.x - b.x, a.y - b.y, a.z - b.z); }
 static inline rdv_vec3 operator-(rdv_vec3 a) { return rdv_vec3(-a.x, -a.y, -a.z); }
 static inline rdv_vec3& operator*=(rdv_vec3& a, rdv_vec3 b) { a.x *= b.x; a.y *= b.y; a.z *= b.z; return a; }
-static inline float max(int a, float b) { return (float)a < b ? b : (float)a; }
 
 struct rdv_mat4x3 {
     rdv_vec3 c[4];

@@ -117,3 +117,60 @@ def tensor_sampler(t: np.ndarray, x: np.ndarray, clamp: bool = True, aligned: bo
              (a0 * a1).astype(np.float32), y)
     return pair([chi[0], clo[1]], hi_in[0] & lo_in[1] & lo_in[2], hi_in[0] & lo_in[1] & hi_in[2],
                 (a0 * (one - a1)).astype(np.float32), y)
+
+
+def grid_sampler(t: np.ndarray, x: np.ndarray, clamp: bool = True, aligned: bool = False,
+                 linear: bool = True) -> np.ndarray:
+    """GridSampler (rdv/shaders/samplers/grid_sampler.h) over a dense grid
+    t [D0, .., D(IN-1), OUT], restated in float32 and vectorised over
+    points x [n, IN] -> [n, OUT]. Dimension i takes coordinate x[:, IN-1-i]:
+    t_i = x * 0.5 + 0.5; pos = aligned ? t_i (D - 1) : t_i D - 0.5;
+    voxel = floor(pos); alpha = pos - voxel. Linear: the 2^IN corners in
+    bit-mask order (bit i: +1 along dimension i), weight the product over i
+    ascending (from 1) of alpha_i or 1 - alpha_i, out += w * value, corners
+    outside skipped unless clamp (clamped then). Nearest: voxel +
+    (alpha >= 0.5), outside -> 0 unless clamp."""
+    t = np.asarray(t, dtype=np.float32)
+    x = np.asarray(x, dtype=np.float32)
+    IN = t.ndim - 1
+    dims = t.shape[:IN]
+    half, one = np.float32(0.5), np.float32(1.0)
+    voxel, alpha = [], []
+    for i in range(IN):
+        ti = (x[:, IN - 1 - i] * half + half).astype(np.float32)
+        if aligned:
+            pos = (ti * np.float32(dims[i] - 1)).astype(np.float32)
+        else:
+            pos = ((ti * np.float32(dims[i])).astype(np.float32) - half).astype(np.float32)
+        fv = np.floor(pos)
+        voxel.append(fv.astype(np.int64))
+        alpha.append((pos - fv).astype(np.float32))
+    n = x.shape[0]
+    out = np.zeros((n, t.shape[-1]), dtype=np.float32)
+    if not linear:
+        idx, inside = [], np.ones(n, dtype=bool)
+        for i in range(IN):
+            c = voxel[i] + (alpha[i] >= half)
+            if clamp:
+                c = np.clip(c, 0, dims[i] - 1)
+            inside &= (c >= 0) & (c < dims[i])
+            idx.append(np.clip(c, 0, dims[i] - 1))
+        y = t[tuple(idx)]
+        return (y if clamp else np.where(inside[:, None], y, np.float32(0.0))).astype(np.float32)
+    for bits in range(1 << IN):
+        idx, inside = [], np.ones(n, dtype=bool)
+        w = np.ones(n, dtype=np.float32)
+        for i in range(IN):
+            up = (bits >> i) & 1
+            c = voxel[i] + up
+            if clamp:
+                c = np.clip(c, 0, dims[i] - 1)
+            inside &= (c >= 0) & (c < dims[i])
+            idx.append(np.clip(c, 0, dims[i] - 1))
+            w = (w * (alpha[i] if up else (one - alpha[i]))).astype(np.float32)
+        v = t[tuple(idx)]
+        add = (w[:, None] * v).astype(np.float32)
+        if not clamp:
+            add = np.where(inside[:, None], add, np.float32(0.0))
+        out = (out + add).astype(np.float32)
+    return out

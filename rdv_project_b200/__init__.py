@@ -11,7 +11,7 @@ Every operator launches hand-written sm_100a kernels from the in-tree
 """
 from .core import (RDVObject, wrap, profiling, reset_submit_times, profiling_submit_times)
 from .maps import (Map, Identity, X, ReLU, relu, Linear, LinearFast, LinearFastBF16, linear, Composite, TensorSampler,
-                   Constant, XRProject, dir2xr)
+                   GridSampler, Constant, XRProject, dir2xr)
 from .tensor_ops import (TensorOperation, ReLUTensorOp, LinearTensorOp, LinearTensorOpFast, LinearTensorOpMine,
                          LinearTensorOpSimple, LinearTensorOpSmall, Downsample2xTensorOp, Upsample2xTensorOp,
                          ConcatTensorOp)
@@ -26,7 +26,7 @@ from ._native import RdvbError, device_status
 __all__ = [
     "RDVObject", "wrap", "profiling", "reset_submit_times", "profiling_submit_times",
     "Map", "Identity", "X", "ReLU", "relu", "Linear", "LinearFast", "LinearFastBF16", "linear", "Composite",
-    "TensorSampler", "Constant", "XRProject", "dir2xr",
+    "TensorSampler", "GridSampler", "Constant", "XRProject", "dir2xr",
     "TensorOperation", "ReLUTensorOp", "LinearTensorOp", "LinearTensorOpFast", "LinearTensorOpMine",
     "LinearTensorOpSimple", "LinearTensorOpSmall", "Downsample2xTensorOp", "Upsample2xTensorOp", "ConcatTensorOp",
     "Conv2DTensorOp", "Conv2DTensorOpFast", "Conv2DTensorOpSimple", "Conv2DTensorOpSimple3x3",

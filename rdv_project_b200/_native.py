@@ -69,6 +69,7 @@ SIGNATURES = {
     "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp,
                                        _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
     "rdvb_xr_project": (_c_int, [_vp, _c_i64, _vp, _vp]),
+    "rdvb_grid_sampler": (_c_int, [_vp, _c_int, _vp, _c_int, _vp, _c_i64, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_pbvr": (_c_int, [_vp, _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int,
                            _vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
 }

@@ -176,7 +176,10 @@ __global__ void __launch_bounds__(NT) pbvr_kernel(const __grid_constant__ Params
     };
     while (true) {
         bool pending = false;  // a tentative collision at x waits for its extinction
-        while (ray != -2 && !pending) {
+        // at most kYieldFlights free flights per lane between two extinction
+        // rounds, so that a lane stuck in a long run of free flights does
+        // not hold the warp's colliding lanes back
+        for (int flights = 0; ray != -2 && !pending && flights < trm::kYieldFlights; ++flights) {
             if (ray < 0) {
                 ray = atomicAdd(p.counter, 1);
                 if (ray >= p.n_rays) {
@@ -224,7 +227,10 @@ __global__ void __launch_bounds__(NT) pbvr_kernel(const __grid_constant__ Params
             }
             pending = true;
         }
-        if (!__any_sync(0xffffffffu, pending)) break;  // no lane has rays left
+        if (!__any_sync(0xffffffffu, pending)) {
+            if (__all_sync(0xffffffffu, ray == -2)) break;  // no lane has rays left
+            continue;
+        }
         const float sigma = trm::extinction<NT>(p, wsm, bsm, act0, act1, x);
         if (pending) {
             ++my_evals;

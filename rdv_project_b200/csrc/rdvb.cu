@@ -1154,6 +1154,48 @@ int rdvb_tensor_sampler(const float* t, int in_dim, const int* shape, int out_di
     return check_launch("tensor_sampler_kernel");
 }
 
+int rdvb_grid_sampler(const float* grid, int in_dim, const int* shape, int out_dim, const float* x, int64_t n,
+                      int clamp, int aligned_centres, int linear, float* y, void* stream) {
+    if (in_dim < 1 || in_dim > 4) return fail(RDVB_ERR_UNSUPPORTED, "in_dim must be 1, 2, 3 or 4 (got %d)", in_dim);
+    if (!shape) return fail(RDVB_ERR_INVALID_ARG, "shape must not be NULL");
+    long long cells = 1;
+    for (int d = 0; d < in_dim; ++d) {
+        if (shape[d] < 1) return fail(RDVB_ERR_INVALID_ARG, "shape[%d] = %d must be positive", d, shape[d]);
+        cells *= shape[d];
+    }
+    if (out_dim < 1) return fail(RDVB_ERR_INVALID_ARG, "out_dim must be positive");
+    if (cells * out_dim > (1LL << 40)) return fail(RDVB_ERR_UNSUPPORTED, "the grid must hold at most 2^40 values");
+    if (n < 0) return fail(RDVB_ERR_INVALID_ARG, "n must be >= 0");
+    if (n == 0) return RDVB_OK;
+    if (!grid || !x || !y) return fail(RDVB_ERR_INVALID_ARG, "grid, x and y must not be NULL");
+    if (!aligned(grid, 4) || !aligned(x, 4) || !aligned(y, 4))
+        return fail(RDVB_ERR_INVALID_ARG, "grid, x and y must be 4-byte aligned");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    rdvb::sampler::GridParams p;
+    memset(&p, 0, sizeof(p));
+    p.t = grid;
+    p.x = x;
+    p.y = y;
+    p.n = n;
+    p.out = out_dim;
+    for (int d = 0; d < in_dim; ++d) p.dim[d] = shape[d];
+    p.clamp = clamp ? 1 : 0;
+    p.aligned = aligned_centres ? 1 : 0;
+    p.linear = linear ? 1 : 0;
+    const long long total = n * out_dim;
+    const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + 255) / 256,
+                                                                               dev->sm_count * 16LL)));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (in_dim) {
+        case 1: rdvb::sampler::grid_sampler_kernel<1><<<blocks, 256, 0, st>>>(p); break;
+        case 2: rdvb::sampler::grid_sampler_kernel<2><<<blocks, 256, 0, st>>>(p); break;
+        case 3: rdvb::sampler::grid_sampler_kernel<3><<<blocks, 256, 0, st>>>(p); break;
+        default: rdvb::sampler::grid_sampler_kernel<4><<<blocks, 256, 0, st>>>(p); break;
+    }
+    return check_launch("grid_sampler_kernel");
+}
+
 int rdvb_downsample2x(const float* x, int h, int w, int c, float* y, void* stream) {
     if (h < 0 || w < 0 || h % 2 || w % 2) return fail(RDVB_ERR_INVALID_ARG, "h and w must be even and >= 0");
     if (h == 0 || w == 0) return RDVB_OK;

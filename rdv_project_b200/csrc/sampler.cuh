@@ -158,5 +158,82 @@ __global__ void tensor_sampler_kernel(const __grid_constant__ Params p) {
     }
 }
 
+// GridSampler (rdv/maths/__init__.py:2018-2047, rdv/shaders/samplers/
+// grid_sampler.h) over a dense grid (a TensorGrid, grids/tensor_grid.h:
+// row-major [D0, ..., D(IN-1), OUT]). Its arithmetic differs from the
+// TensorSampler's: per dimension i (coordinate x[IN-1-i])
+//   t = x * 0.5 + 0.5
+//   pos = aligned ? t * (D - 1) : t * D - 0.5
+//   voxel = floor(pos), alpha = pos - voxel
+// linear: the 2^IN corners in the order of their bit masks (bit i: +1 along
+// dimension i), each weighted by the product, over i ascending and starting
+// from 1, of alpha_i or 1 - alpha_i, accumulated as out += w * value; a
+// corner outside the grid is skipped unless clamp (then clamped).
+// nearest: voxel + (alpha >= 0.5), skipped outside unless clamp.
+struct GridParams {
+    const float* t;
+    const float* x;   // [n, IN]
+    float* y;         // [n, OUT]
+    long long n;
+    int out;
+    int dim[4];
+    int clamp, aligned, linear;
+};
+
+template <int IN>
+__global__ void grid_sampler_kernel(const __grid_constant__ GridParams p) {
+    const long long total = p.n * p.out;
+    const bool clamp = p.clamp != 0;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long i = idx / p.out;
+        const int k = static_cast<int>(idx - i * p.out);
+        int voxel[IN];
+        float alpha[IN];
+#pragma unroll
+        for (int d = 0; d < IN; ++d) {
+            const float x = __ldg(p.x + i * IN + (IN - 1 - d));
+            const float t = __fadd_rn(__fmul_rn(x, 0.5f), 0.5f);
+            const float pos = p.aligned ? __fmul_rn(t, static_cast<float>(p.dim[d] - 1))
+                                        : __fsub_rn(__fmul_rn(t, static_cast<float>(p.dim[d])), 0.5f);
+            const float fv = floorf(pos);
+            voxel[d] = static_cast<int>(fv);
+            alpha[d] = __fsub_rn(pos, fv);
+        }
+        float out = 0.0f;
+        if (!p.linear) {
+            bool inside = true;
+            long long off = 0;
+#pragma unroll
+            for (int d = 0; d < IN; ++d) {
+                int c = voxel[d] + (alpha[d] >= 0.5f ? 1 : 0);
+                if (clamp) c = min(max(c, 0), p.dim[d] - 1);
+                inside = inside && c >= 0 && c < p.dim[d];
+                off = off * p.dim[d] + c;
+            }
+            if (clamp || inside) out = __ldg(p.t + off * p.out + k);
+        } else {
+#pragma unroll
+            for (int bits = 0; bits < (1 << IN); ++bits) {
+                bool inside = true;
+                long long off = 0;
+                float w = 1.0f;
+#pragma unroll
+                for (int d = 0; d < IN; ++d) {
+                    const int up = (bits >> d) & 1;
+                    int c = voxel[d] + up;
+                    if (clamp) c = min(max(c, 0), p.dim[d] - 1);
+                    inside = inside && c >= 0 && c < p.dim[d];
+                    off = off * p.dim[d] + c;
+                    w = __fmul_rn(w, up ? alpha[d] : __fsub_rn(1.0f, alpha[d]));
+                }
+                if (!clamp && !inside) continue;
+                out = __fadd_rn(out, __fmul_rn(w, __ldg(p.t + off * p.out + k)));
+            }
+        }
+        p.y[idx] = out;
+    }
+}
+
 }  // namespace sampler
 }  // namespace rdvb

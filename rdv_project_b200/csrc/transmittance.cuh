@@ -362,6 +362,12 @@ __device__ __forceinline__ float field_majorant(const Params& p, const float (&x
 }
 
 constexpr int kRtSafety = 1024;  // ratiotracking_transmittance_trait.h's loop cap
+// free flights per lane between two warp-wide extinction rounds (a
+// compile-time tuning constant)
+#ifndef RDVB_YIELD_FLIGHTS
+#define RDVB_YIELD_FLIGHTS 16
+#endif
+constexpr int kYieldFlights = RDVB_YIELD_FLIGHTS;
 
 // Work is warp-coherent: each lane advances its own ray (free flights across
 // majorant cells, taking the next ray when one ends) until it reaches a
@@ -385,7 +391,10 @@ __global__ void __launch_bounds__(NT) ratiotracking_kernel(const __grid_constant
     Rng r = {0u, 0u, 0u, 0u};
     while (true) {
         bool pending = false;  // a collision at x waits for its extinction
-        while (ray != -2 && !pending) {
+        // at most kYieldFlights free flights per lane between two extinction
+        // rounds, so that a lane stuck in a long run of free flights does
+        // not hold the warp's colliding lanes back
+        for (int flights = 0; ray != -2 && !pending && flights < kYieldFlights; ++flights) {
             if (ray < 0) {
                 ray = atomicAdd(p.counter, 1);
                 if (ray >= p.n_rays) {
@@ -425,7 +434,10 @@ __global__ void __launch_bounds__(NT) ratiotracking_kernel(const __grid_constant
             }
             pending = true;
         }
-        if (!__any_sync(0xffffffffu, pending)) break;  // no lane has rays left
+        if (!__any_sync(0xffffffffu, pending)) {
+            if (__all_sync(0xffffffffu, ray == -2)) break;  // no lane has rays left
+            continue;
+        }
         const float sigma = extinction<NT>(p, wsm, bsm, act0, act1, x);
         if (pending) {
             ++my_evals;

@@ -218,6 +218,44 @@ class TensorSampler(Map):
         return RDVObject(out)
 
 
+class GridSampler(Map):
+    """Multilinear (linear=True) or nearest lookup of a grid at points in
+    [-1, 1]^IN (rdv/maths/__init__.py:2018-2047,
+    rdv/shaders/samplers/grid_sampler.h): clamp clamps out-of-range corners
+    (else they are skipped), aligned ties -1/+1 to the first/last cell
+    centres (else to the outer edges). ``g`` is a dense grid: a TensorGrid
+    (rdv_project_b200.volumes) or its tensor [D0, ..., D(IN-1), OUT], IN 1
+    to 4 -> rdvb_grid_sampler. Its position and corner arithmetic is the
+    GridSampler's, not the TensorSampler's, so the two round differently on
+    the same tensor, as in the reference. Composed before a Linear chain
+    (``sampler >> mlp``) it is the chain's input encoding, like the
+    TensorSampler."""
+
+    def __init__(self, g, clamp: bool = True, aligned: bool = False, linear: bool = True) -> None:
+        data = getattr(g, "data", g)     # a TensorGrid holds its tensor in .data
+        t = data if isinstance(data, RDVObject) else wrap(data)
+        n = len(t.shape)
+        assert 2 <= n <= 5, "GridSampler supports 1- to 4-dimensional grids (a [D0, ..., OUT] tensor)"
+        self.g = g
+        self.t = t
+        self.IN = n - 1
+        self.OUT = t.shape[n - 1]
+        self.clamp = 1 if clamp else 0
+        self.aligned = 1 if aligned else 0
+        self.linear = 1 if linear else 0
+
+    def _sample(self, x2d: torch.Tensor, y2d: torch.Tensor) -> None:
+        t = self.t._tensor
+        if t.device != x2d.device or t.dtype != torch.float32 or not t.is_contiguous():
+            t = t.to(device=x2d.device, dtype=torch.float32).contiguous()
+        N.check(N.lib().rdvb_grid_sampler(
+            t.data_ptr(), self.IN, N.int_array(list(t.shape[:self.IN])), self.OUT, x2d.data_ptr(), x2d.shape[0],
+            self.clamp, self.aligned, self.linear, y2d.data_ptr(), stream_handle()), "rdvb_grid_sampler")
+
+    def __call__(self, *args, **kwargs):
+        return TensorSampler.__call__(self, *args, **kwargs)
+
+
 class Constant(Map):
     """f(x) = data for every x (rdv/maths/__init__.py:1659-1668,
     rdv/shaders/maps/constant.h): OUT = data's last dimension, IN generic.
@@ -311,7 +349,7 @@ def _lower(m: Map):
     layers = []
     relus = []
     for op in m._ops():
-        if isinstance(op, (TensorSampler, XRProject)):
+        if isinstance(op, (TensorSampler, GridSampler, XRProject)):
             raise NotImplementedError(f"a {type(op).__name__} must come first in the chain (its input encoding)")
         if isinstance(op, _LinearBase):
             layers.append(op)
@@ -343,7 +381,7 @@ class _ChainPlan:
         self.project = ops[0] if ops and isinstance(ops[0], XRProject) else None
         if self.project is not None:
             ops = ops[1:]
-        self.prologue = ops[0] if ops and isinstance(ops[0], TensorSampler) else None
+        self.prologue = ops[0] if ops and isinstance(ops[0], (TensorSampler, GridSampler)) else None
         if self.prologue is not None:
             ops = ops[1:]
         rest = _compose_ops(ops)

@@ -6,6 +6,7 @@ the default in oracle/_clib.py):
     python tests/golden/make_golden.py            # every fixture
     python tests/golden/make_golden.py coopmat    # coopmat.npz only
     python tests/golden/make_golden.py pbvr       # pbvr.npz only
+    python tests/golden/make_golden.py samplers   # grid_sampler.npz only
 
 Three sources, all the reference's own code:
 
@@ -24,6 +25,8 @@ Three sources, all the reference's own code:
 * ``oracle/_ref/libref_pbvr.so`` -- the reference's PBVR body
   (volumes/pbvr.h) and its Henyey-Greenstein sampler
   (libraries/random_library.h) compiled as C++ (oracle/ref_shim/ref_pbvr.cpp);
+* ``oracle/_ref/libref_samplers.so`` -- the reference's GridSampler
+  (samplers/grid_sampler.h) compiled as C++ (oracle/ref_shim/ref_samplers.cpp);
 * ``rdv/domain/nn.py``'s torch helpers ``_winograd_transform_weight``,
   ``_tile_weight_fp16`` and ``_cast_fp16`` and its ``_WINOGRAD_G`` table,
   executed from the reference source. The package itself cannot be
@@ -48,7 +51,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from oracle._clib import REFERENCE_ROOT, ptr, ptr_array, ref_coopmat_lib, ref_lib, ref_pbvr_lib  # noqa: E402
+from oracle._clib import (REFERENCE_ROOT, ptr, ptr_array, ref_coopmat_lib, ref_lib, ref_pbvr_lib,  # noqa: E402
+                          ref_samplers_lib)
 
 
 def xavier_uniform(rng, out_f, in_f):
@@ -202,6 +206,7 @@ def main():
                         T=rt_T)
     coopmat_goldens()
     pbvr_goldens()
+    sampler_goldens()
     print("golden fixtures written to", HERE)
 
 
@@ -331,10 +336,39 @@ def pbvr_goldens():
                         hg_out=hg_out)
 
 
+GRID_CASES = ((1, 3, (7,)), (2, 3, (5, 9)), (3, 3, (4, 5, 6)), (4, 3, (3, 4, 2, 5)), (3, 5, (2, 3, 1)))
+
+
+def sampler_goldens():
+    """grid_sampler.npz: GridSampler.forward of the reference
+    (samplers/grid_sampler.h) over dense grids, for every (clamp, aligned,
+    linear) and the (IN, OUT) pairs of GRID_CASES; points in [-1.3, 1.3]^IN
+    (outside the grid too) with the exact -1, 0, 1 and cell-centre
+    coordinates first."""
+    lib = ref_samplers_lib()
+    rng = np.random.default_rng(2027)
+    out = {}
+    n = 256
+    for c, (IN, OUT, shape) in enumerate(GRID_CASES):
+        t = rng.standard_normal(tuple(shape) + (OUT,)).astype(np.float32)
+        x = rng.uniform(-1.3, 1.3, (n, IN)).astype(np.float32)
+        x[:8] = np.float32([-1, 1, 0, -1.0, 1.0, 0.5, -0.5, 0.25])[:, None]
+        ys = np.zeros((8, n, OUT), np.float32)
+        for f in range(8):
+            clamp, aligned, linear = f & 1, (f >> 1) & 1, (f >> 2) & 1
+            rc = lib.ref_grid_sampler(IN, OUT, ptr(np.array(shape, np.int32)), ptr(t), clamp, aligned, linear,
+                                      ptr(x), n, ptr(ys[f]))
+            assert rc == 0
+        out.update({f"t{c}": t, f"x{c}": x, f"y{c}": ys})
+    np.savez_compressed(os.path.join(HERE, "grid_sampler.npz"), **out)
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["coopmat"]:
         coopmat_goldens()
     elif sys.argv[1:] == ["pbvr"]:
         pbvr_goldens()
+    elif sys.argv[1:] == ["samplers"]:
+        sampler_goldens()
     else:
         main()

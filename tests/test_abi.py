@@ -217,3 +217,16 @@ def test_max_ctas_setting(lib):
     assert N.set_max_ctas(0) == 100
     assert lib.rdvb_set_max_ctas(-1) == N.RDVB_ERR_INVALID_ARG and "max_ctas" in N.last_error()
     assert lib.rdvb_get_max_ctas() == 0
+
+
+def test_grid_sampler_validation(lib):
+    import rdv_project_b200._native as N
+
+    shape = N.int_array([4, 4, 4, 4, 4])
+    assert lib.rdvb_grid_sampler(None, 3, shape, 2, None, 0, 1, 0, 1, None, None) == 0
+    assert lib.rdvb_grid_sampler(None, 5, shape, 2, None, 4, 1, 0, 1, None, None) == -2
+    assert "in_dim" in N.last_error()
+    assert lib.rdvb_grid_sampler(None, 3, N.int_array([4, 0, 4]), 2, None, 4, 1, 0, 1, None, None) == -1
+    assert lib.rdvb_grid_sampler(None, 3, shape, 0, None, 4, 1, 0, 1, None, None) == -1
+    assert lib.rdvb_grid_sampler(None, 3, shape, 2, None, 4, 1, 0, 1, None, None) == -1
+    assert "must not be NULL" in N.last_error()

@@ -69,3 +69,67 @@ def test_sampler_shapes_and_empty(rdv, cuda_device):
     v = rdv.TensorSampler(one)(torch.zeros(1, 2, device=cuda_device)).as_tensor("torch")
     assert torch.equal(v.cpu(), torch.arange(6.0).reshape(1, 6))
     assert rdv.device_status() == 0
+
+
+# ------------------------------------------------------------- GridSampler
+_GRID_PAIRS = ((1, 3), (2, 3), (3, 3), (4, 3), (3, 5))
+
+
+@pytest.mark.parametrize("c", range(len(_GRID_PAIRS)))
+def test_grid_sampler_bit_exact_vs_reference_fixture(rdv, cuda_device, golden, c):
+    """GridSampler over a TensorGrid against the reference's own
+    grid_sampler.h outputs (tests/golden/grid_sampler.npz): every (clamp,
+    aligned, linear), IN 1..4, bit for bit (both round every product and
+    sum separately in the same order)."""
+    g = golden("grid_sampler.npz")
+    t, x, ys = g[f"t{c}"], g[f"x{c}"], g[f"y{c}"]
+    grid = rdv.TensorGrid(torch.from_numpy(t).to(cuda_device))
+    for f in range(8):
+        s = rdv.GridSampler(grid, clamp=bool(f & 1), aligned=bool(f & 2), linear=bool(f & 4))
+        assert (s.IN, s.OUT) == _GRID_PAIRS[c]
+        got = s(torch.from_numpy(x).to(cuda_device)).as_tensor("torch").cpu().numpy()
+        np.testing.assert_array_equal(got, ys[f], err_msg=f"flags {f}")
+    assert rdv.device_status() == 0
+
+
+def test_grid_sampler_full_size_against_oracle(rdv, cuda_device):
+    """A 64^3 x 8 grid at 2^22 points: bit-exact to the oracle on every 97th
+    point; constant grids return the constant (partition of unity of the
+    corner weights, up to rounding) wherever all corners are inside."""
+    rng = np.random.default_rng(17)
+    t = rng.standard_normal((64, 64, 64, 8)).astype(np.float32)
+    x = rng.uniform(-1.05, 1.05, (1 << 22, 3)).astype(np.float32)
+    dev_t = torch.from_numpy(t).to(cuda_device)
+    xs = torch.from_numpy(x).to(cuda_device)
+    for clamp, aligned in ((True, False), (False, True)):
+        got = rdv.GridSampler(dev_t, clamp=clamp, aligned=aligned)(xs).as_tensor("torch")
+        sub = np.arange(0, x.shape[0], 97)
+        np.testing.assert_array_equal(got.cpu().numpy()[sub], oten.grid_sampler(t, x[sub], clamp, aligned))
+    ones = torch.full((64, 64, 64, 2), 2.5, device=cuda_device)
+    v = rdv.GridSampler(ones, clamp=True)(xs).as_tensor("torch").cpu().numpy()
+    np.testing.assert_allclose(v, 2.5, rtol=1e-6)
+    assert rdv.device_status() == 0
+
+
+def test_grid_sampler_feeds_fused_mlp(rdv, cuda_device):
+    """GridSampler >> LinearFast chain: the sampler launch, then the fused
+    tensor-core MLP on its features."""
+    rng = np.random.default_rng(5)
+    grid = rng.standard_normal((8, 8, 8, 16)).astype(np.float32)
+    dims = [16, 64, 4]
+    layers = [{"W": (rng.standard_normal((dims[i + 1], dims[i])) * np.sqrt(2.0 / dims[i])).astype(np.float32),
+               "b": (rng.standard_normal(dims[i + 1]) * 0.1).astype(np.float32), "math": "f16", "relu": i < 1}
+              for i in range(2)]
+    m = rdv.GridSampler(rdv.TensorGrid(torch.from_numpy(grid).to(cuda_device)), aligned=True)
+    for l in layers:
+        m = m >> rdv.linear(torch.from_numpy(l["W"]).to(cuda_device), torch.from_numpy(l["b"]).to(cuda_device),
+                            f16=True)
+        if l["relu"]:
+            m = m >> rdv.relu
+    x = rng.uniform(-1, 1, size=(5000, 3)).astype(np.float32)
+    got = m(rdv.wrap(torch.from_numpy(x).to(cuda_device))).as_tensor("torch").cpu().numpy()
+    ref = omlp.mlp_forward(oten.grid_sampler(grid, x, aligned=True), layers, tail_exact=True)
+    nw, el = omlp.rel_errors(got, ref)
+    assert nw <= 1e-2 and el <= 1e-2, (nw, el)
+    empty = rdv.GridSampler(torch.from_numpy(grid).to(cuda_device))(torch.zeros(0, 3, device=cuda_device))
+    assert tuple(empty.as_tensor("torch").shape) == (0, 16)

@@ -115,9 +115,9 @@ def test_generator_restatement_is_bit_exact(golden):
 
 def test_ratiotracking_restatement_matches_reference(golden):
     """transmittance_rt over the fixture's ray segments: the same random
-    draws, collisions and Russian-roulette outcomes as the reference's own
-    loop (which evaluates 1 - sigma / maj in double, so values may differ
-    in the last bits)."""
+    draws, collisions, Russian-roulette outcomes and values, bit for bit, as
+    the reference's own loop (compiled with its floating literals as float,
+    as GLSL reads them)."""
     g = golden("ratiotracking.npz")
     for m, (c0, c1, _, ds) in enumerate(g["media"]):
         def ext(p, c0=c0, c1=c1):
@@ -129,7 +129,7 @@ def test_ratiotracking_restatement_matches_reference(golden):
         T = orm.transmittance_rt(g["x"][m], g["w"][m], g["d"][m], ds, ext,
                                  lambda x, w: orm.voxel_majorant(grid, x, w), state)
         ref = g["T"][m]
-        np.testing.assert_allclose(T, ref, rtol=0, atol=1e-6)
+        np.testing.assert_array_equal(T, ref)
         np.testing.assert_array_equal(T == 0, ref == 0)
         np.testing.assert_array_equal(T == 1, ref == 1)
     assert (g["T"] == 0).any() and ((g["T"] > 0) & (g["T"] < 1)).any()
@@ -369,3 +369,43 @@ def test_live_reference_pbvr_library_agrees_with_fixture(golden):
                             ptr(np.ascontiguousarray(g["albedo"][0])), ctypes.c_float(g["g"][0]),
                             int(g["max_bounces"][0]), ptr(g["seeds"]), ptr(g["rays"]), g["rays"].shape[0], ptr(out))
     np.testing.assert_array_equal(out, g["out"][0])
+
+
+_GRID_PAIRS = ((1, 3), (2, 3), (3, 3), (4, 3), (3, 5))
+
+
+@pytest.mark.parametrize("c", range(len(_GRID_PAIRS)))
+def test_grid_sampler_restatement_bit_exact_vs_reference(golden, c):
+    """GridSampler.forward (samplers/grid_sampler.h) of the oracle against
+    the reference's own body, every (clamp, aligned, linear), IN 1..4."""
+    g = golden("grid_sampler.npz")
+    t, x, ys = g[f"t{c}"], g[f"x{c}"], g[f"y{c}"]
+    assert (t.ndim - 1, t.shape[-1]) == _GRID_PAIRS[c]
+    for f in range(8):
+        got = oten.grid_sampler(t, x, clamp=bool(f & 1), aligned=bool(f & 2), linear=bool(f & 4))
+        np.testing.assert_array_equal(got, ys[f], err_msg=f"flags {f}")
+
+
+def test_grid_and_tensor_samplers_round_differently(golden):
+    """The two samplers agree to rounding on the same tensor but are not the
+    same arithmetic (positions t D - 0.5 against (x (D - a) + D) 0.5 - 0.5,
+    bit-mask corner weights against paired lerps), as in the reference."""
+    g = golden("grid_sampler.npz")
+    t, x = g["t2"], g["x2"]
+    a = oten.grid_sampler(t, x)
+    b = oten.tensor_sampler(t, x)
+    np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-5)
+    assert not np.array_equal(a, b)
+
+
+def test_live_reference_samplers_library_agrees_with_fixture(golden):
+    if not ref_lib_available():
+        pytest.skip("reference checkout not present")
+    from oracle._clib import ptr, ref_samplers_lib
+
+    g = golden("grid_sampler.npz")
+    t, x = g["t2"], g["x2"]
+    y = np.zeros_like(g["y2"][7])
+    assert ref_samplers_lib().ref_grid_sampler(3, 3, ptr(np.array(t.shape[:3], np.int32)), ptr(t), 1, 1, 1, ptr(x),
+                                               x.shape[0], ptr(y)) == 0
+    np.testing.assert_array_equal(y, g["y2"][7])
