@@ -562,8 +562,15 @@ def run_c3(args, world, rank, local, summary=False):
     achieved = c3_bytes(n_img) / (t_kernel / steps) / 1e9
     value = c3_bytes(C3_SHAPE[0]) * steps / t_step / 1e9
     if summary:
+        # the F(4x4,3x3) extension (CUDA cores, fp32 operands) on the same input
+        conv43 = rdv.Conv3x3Winograd(w33io, b, variant="F4x4")
+        for _ in range(3):
+            conv43(x, out=y)
+        torch.cuda.synchronize()
+        t43 = time_steps(lambda: conv43(x, out=y), steps, flush) / steps
+        p43 = c3_oracle_parity(y[0].cpu().numpy(), x_host[0], w33io, b)
         return {"value": _r(value), "unit": "GB/s", "ms": _r(t_step / steps * 1e3), "frac": _r(achieved / hbm, 3),
-                "parity": _r(parity[1], 2)}
+                "parity": _r(parity[1], 2), "f4x4_ms": _r(t43 * 1e3), "f4x4_parity": _r(p43[1], 2)}
     # end to end through the public API with host buffers
     x_pin = x_host.pin_memory()
     y_pin = torch.empty(y.shape, dtype=torch.float32).pin_memory()

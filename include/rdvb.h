@@ -196,9 +196,9 @@ int64_t rdvb_winograd_packed_bytes(int variant, int cin, int cout);
  *            rdvb_conv3x3_winograd, rdvb_winograd_packed_bytes() bytes,
  *            256-byte aligned; requires cin, cout multiples of 16, <= 64
  * RDVB_WINOGRAD_F4X4 (a B200 extension): U = G g G^T with the 6x3 Toom-Cook
- * G of the points {0, 1, -1, 2, -1/2, inf}; u_plain and u_packed are both
- * the plain float16 array [36][cin][cout] (2-byte aligned), cin and cout in
- * [1, 128]. */
+ * G of the points {0, 1, -1, 2, -1/2, inf}, kept fp32; u_plain and u_packed
+ * are both the plain fp32 array [36][cin][cout] (4-byte aligned), cin and
+ * cout in [1, 128]. */
 int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int variant, void* u_plain,
                                    void* u_packed, void* stream);
 
@@ -210,9 +210,10 @@ int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int v
  *  bias      [cout] fp32, or NULL for zero
  *  y_dtype   RDVB_F32 (the reference's output type) or RDVB_F16
  *            (y 16-byte aligned)
- * variant RDVB_WINOGRAD_F4X4: the same recipe with 6x6 transforms and the 36
- * per-position reductions on CUDA cores (fp32), one fused kernel; cin, cout
- * in [1, 128]; x, y aligned to their element size. */
+ * variant RDVB_WINOGRAD_F4X4: 6x6 transforms with every operand fp32 (U, V,
+ * the 36 per-position reductions on CUDA cores, the inverse transform), one
+ * fused kernel; cin, cout in [1, 128]; x, y aligned to their element size.
+ * (float16 U and V would put F(4x4) above the 1e-2 tolerance.) */
 int rdvb_conv3x3_winograd(const void* x, int x_dtype, int n, int h, int w, int cin, int cout,
                           const void* u_packed, int variant, const float* bias, void* y, int y_dtype,
                           void* stream);

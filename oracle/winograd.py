@@ -102,10 +102,13 @@ def winograd_inv_f23(M: np.ndarray) -> np.ndarray:
     return Y.reshape(-1, 4)
 
 
-def filter_transform(w_33io: np.ndarray, variant: str = "F2x2") -> np.ndarray:
+def filter_transform(w_33io: np.ndarray, variant: str = "F2x2", staged: bool | None = None) -> np.ndarray:
     """U = G g G^T per (cin, cout) filter, computed in float32 like the
-    reference's torch code (nn.py:533-538), returned float16-staged as float32
-    values with layout [a*a, CIN, COUT]."""
+    reference's torch code (nn.py:533-538), with layout [a*a, CIN, COUT];
+    float16-staged (as float32 values) when `staged`, by default for F2x2
+    only (the F4x4 extension keeps U fp32)."""
+    if staged is None:
+        staged = variant == "F2x2"
     v = VARIANTS[variant]
     w = np.asarray(w_33io, dtype=np.float32)
     g = np.transpose(w, (2, 3, 0, 1))  # [CIN, COUT, 3, 3]
@@ -113,8 +116,8 @@ def filter_transform(w_33io: np.ndarray, variant: str = "F2x2") -> np.ndarray:
     U = G @ g @ G.T  # [CIN, COUT, a, a]
     a = v["a"]
     cin, cout = g.shape[0], g.shape[1]
-    U = U.reshape(cin, cout, a * a).transpose(2, 0, 1)
-    return stage(np.ascontiguousarray(U), "f16")
+    U = np.ascontiguousarray(U.reshape(cin, cout, a * a).transpose(2, 0, 1))
+    return stage(U, "f16") if staged else U.astype(np.float32)
 
 
 def conv3x3_direct(x_nhwc: np.ndarray, w_33io: np.ndarray, bias: np.ndarray) -> np.ndarray:
@@ -190,7 +193,7 @@ def conv3x3_winograd(x_nhwc: np.ndarray, w_33io: np.ndarray, bias: np.ndarray,
         if staged:
             V = stage(V.astype(np.float32), "f16").astype(np.float64)
     if staged:
-        U = filter_transform(w_33io, variant).astype(np.float64)  # [a*a, cin, cout]
+        U = filter_transform(w_33io, variant, staged=True).astype(np.float64)  # [a*a, cin, cout]
     else:
         g = np.transpose(np.asarray(w_33io, dtype=np.float64), (2, 3, 0, 1))
         U = (v["G"] @ g @ v["G"].T).reshape(cin, cout, a * a).transpose(2, 0, 1)

@@ -57,7 +57,8 @@ def _filter_transform(w33io: torch.Tensor, cin: int, cout: int, plain: bool, pac
     lib = N.lib()
     code = _variant(variant)
     positions = _VARIANTS[variant][1]
-    u_plain = torch.empty(positions * cin * cout, dtype=torch.float16, device=w33io.device) if plain else None
+    u_dtype = torch.float32 if variant == "F4x4" else torch.float16   # F(4x4) keeps U fp32
+    u_plain = torch.empty(positions * cin * cout, dtype=u_dtype, device=w33io.device) if plain else None
     u_packed = None
     if packed:
         nbytes = lib.rdvb_winograd_packed_bytes(code, cin, cout)
@@ -321,8 +322,8 @@ class Conv3x3Winograd:
 
     variant "F2x2": the fused tcgen05 kernel, channels multiples of 16 up to
     64 (the reference operator's transform). variant "F4x4": F(4x4,3x3) on
-    CUDA cores, channels 1..128 (a B200 extension; with float16 staging its
-    error against the direct convolution is ~6x that of F(2x2))."""
+    CUDA cores with fp32 operands, channels 1..128 (a B200 extension; with
+    float16 U and V its error would exceed the 1e-2 tolerance)."""
 
     def __init__(self, weight, bias=None, variant: str = "F2x2") -> None:
         w = _dev_f32(weight)

@@ -65,7 +65,7 @@ struct DeviceInfo {
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
     size_t wino_tma_smem_set = 0;
-    size_t wino43_smem_set[2] = {};
+    size_t wino43_smem_set[4] = {};
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
@@ -651,7 +651,7 @@ int conv3x3_winograd_f43(const void* x, int x_dtype, int n, int h, int w, int ci
     if (n == 0 || h == 0 || w == 0) return RDVB_OK;
     if (!x || !y || !u) return fail(RDVB_ERR_INVALID_ARG, "x, y and u_packed must not be NULL");
     const uintptr_t xa = x_dtype == RDVB_F16 ? 2 : 4, ya = y_dtype == RDVB_F16 ? 2 : 4;
-    if (!aligned(x, xa) || !aligned(y, ya) || !aligned(u, 2) || (bias && !aligned(bias, 4)))
+    if (!aligned(x, xa) || !aligned(y, ya) || !aligned(u, 4) || (bias && !aligned(bias, 4)))
         return fail(RDVB_ERR_INVALID_ARG, "x, y, u_packed and bias must be aligned to their element size");
     const long long tiles_h = (h + kM - 1) / kM, tiles_w = (w + kM - 1) / kM;
     if (tiles_h * tiles_w > 0x7fffffffLL) return fail(RDVB_ERR_UNSUPPORTED, "image too large (%d x %d)", h, w);
@@ -661,7 +661,7 @@ int conv3x3_winograd_f43(const void* x, int x_dtype, int n, int h, int w, int ci
     memset(&p, 0, sizeof(p));
     p.x = x;
     p.y = y;
-    p.u = static_cast<const __half*>(u);
+    p.u = static_cast<const float*>(u);
     p.bias = bias;
     p.h = h;
     p.w = w;
@@ -671,23 +671,34 @@ int conv3x3_winograd_f43(const void* x, int x_dtype, int n, int h, int w, int ci
     p.tiles_w = static_cast<int>(tiles_w);
     p.tiles_per_img = static_cast<int>(tiles_h * tiles_w);
     p.n_tiles = static_cast<long long>(n) * p.tiles_per_img;
-    const size_t smem = smem_bytes(cin, cout);
+    // 8 tiles per block when their V and M fit in shared memory, else 4
+    const int bt = smem_bytes(cin, cout, 8) <= static_cast<size_t>(dev->max_smem_optin) ? 8 : 4;
+    const size_t smem = smem_bytes(cin, cout, bt);
     if (smem > static_cast<size_t>(dev->max_smem_optin))
         return fail(RDVB_ERR_UNSUPPORTED, "F4X4 kernel needs %zu bytes of shared memory", smem);
     const int xi = x_dtype == RDVB_F16 ? 1 : 0;
-    auto kernel = xi ? winograd_f43_kernel<true> : winograd_f43_kernel<false>;
-    if (dev->wino43_smem_set[xi] < smem) {
+    const int ki = 2 * xi + (bt == 8 ? 1 : 0);
+    const void* kernel = nullptr;
+    switch (ki) {
+        case 0: kernel = reinterpret_cast<const void*>(winograd_f43_kernel<false, 4>); break;
+        case 1: kernel = reinterpret_cast<const void*>(winograd_f43_kernel<false, 8>); break;
+        case 2: kernel = reinterpret_cast<const void*>(winograd_f43_kernel<true, 4>); break;
+        default: kernel = reinterpret_cast<const void*>(winograd_f43_kernel<true, 8>); break;
+    }
+    if (dev->wino43_smem_set[ki] < smem) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaFuncSetAttribute(winograd_f43): %s", cudaGetErrorString(e));
-        dev->wino43_smem_set[xi] = smem;
+        dev->wino43_smem_set[ki] = smem;
     }
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
     if (e != cudaSuccess)
         return fail(RDVB_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s", cudaGetErrorString(e));
-    const long long blocks = (p.n_tiles + kBlockTiles - 1) / kBlockTiles;
+    const long long blocks = (p.n_tiles + bt - 1) / bt;
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(blocks, 1LL * dev->sm_count * std::max(per_sm, 1))));
-    kernel<<<grid, kThreads, smem, stream>>>(p);
+    void* args[] = {&p};
+    e = cudaLaunchKernel(kernel, dim3(grid), dim3(kThreads), args, smem, stream);
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "winograd_f43_kernel launch: %s", cudaGetErrorString(e));
     return check_launch("winograd_f43_kernel");
 }
 
@@ -697,7 +708,7 @@ extern "C" {
 
 int64_t rdvb_winograd_packed_bytes(int variant, int cin, int cout) {
     if (variant == RDVB_WINOGRAD_F4X4)
-        return wino43_channels_ok(cin, cout) ? 36LL * cin * cout * static_cast<int64_t>(sizeof(__half)) : 0;
+        return wino43_channels_ok(cin, cout) ? 36LL * cin * cout * static_cast<int64_t>(sizeof(float)) : 0;
     if (variant != RDVB_WINOGRAD_F2X2 || !wino_channels_ok(cin, cout)) return 0;
     return 16LL * cout * 128;
 }
@@ -709,12 +720,12 @@ int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int v
     if (cin < 1 || cout < 1) return fail(RDVB_ERR_INVALID_ARG, "cin (%d) and cout (%d) must be positive", cin, cout);
     if (!w_33io) return fail(RDVB_ERR_INVALID_ARG, "w_33io must not be NULL");
     if (variant == RDVB_WINOGRAD_F4X4) {
-        // the packed operand of F(4x4) is the plain [36][cin][cout] float16 array
+        // the packed operand of F(4x4) is the plain [36][cin][cout] fp32 array
         if (!wino43_channels_ok(cin, cout))
             return fail(RDVB_ERR_UNSUPPORTED, "F4X4 needs cin, cout in [1, %d] (got %d, %d)",
                         rdvb::wino43::kMaxChannels, cin, cout);
-        if ((u_plain && !aligned(u_plain, 2)) || (u_packed && !aligned(u_packed, 2)))
-            return fail(RDVB_ERR_INVALID_ARG, "u_plain and u_packed must be 2-byte aligned");
+        if ((u_plain && !aligned(u_plain, 4)) || (u_packed && !aligned(u_packed, 4)))
+            return fail(RDVB_ERR_INVALID_ARG, "u_plain and u_packed must be 4-byte aligned");
         if (!u_plain && !u_packed) return RDVB_OK;
         DeviceInfo* dev = nullptr;
         if (int rc = current_device(&dev)) return rc;
@@ -726,7 +737,7 @@ int rdvb_winograd_filter_transform(const float* w_33io, int cin, int cout, int v
         for (void* dst : {u_plain, u_packed}) {
             if (!dst) continue;
             rdvb::wino43::winograd_f43_filter_kernel<<<blocks, threads, 0, st>>>(w_33io, cin, cout,
-                                                                                 static_cast<__half*>(dst));
+                                                                                 static_cast<float*>(dst));
             if (int rc = check_launch("winograd_f43_filter_kernel")) return rc;
         }
         return RDVB_OK;

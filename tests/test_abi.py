@@ -74,7 +74,7 @@ def test_validation_before_any_device_work(lib):
     rc = lib.rdvb_conv3x3_winograd(None, N.RDVB_F16, 1, 8, 8, 24, 40, None, N.RDVB_WINOGRAD_F4X4, None, None,
                                    N.RDVB_F32, None)
     assert rc == -1 and "NULL" in N.last_error()
-    assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F4X4, 24, 40) == 36 * 24 * 40 * 2
+    assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F4X4, 24, 40) == 36 * 24 * 40 * 4
     assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F4X4, 0, 40) == 0
     rc = lib.rdvb_raymarch_render(N.float_array([3, 0.5, 0, 0, 0, 0, 0, 1, 0]), 8, 8, 0.0, 0.0, 64, 3,
                                   N.int_array([3, 64, 64, 4]), N.int_array([5, 5, 1]), None, 0, 8, None, 0, None,

@@ -183,7 +183,7 @@ def test_errors_and_empty(rdv, cuda_device):
     lib = N.lib()
     assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F2X2, 64, 64) == 16 * 64 * 128
     assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F2X2, 80, 64) == 0
-    assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F4X4, 64, 64) == 36 * 64 * 64 * 2
+    assert lib.rdvb_winograd_packed_bytes(N.RDVB_WINOGRAD_F4X4, 64, 64) == 36 * 64 * 64 * 4
     dummy = torch.zeros(1 << 16, device=cuda_device)
     # n = 0: nothing to do, no launch
     before = N.launch_count()
