@@ -1026,8 +1026,9 @@ def pbvr_summary(steps=3):
     transmittance workload's extinction chain, its 16^3 voxel majorant (and
     a sphere field built from it, radius 1.5 voxels), a constant
     environment, albedo 0.8, g = 0.3, at most 8 bounces, fixed seeds;
-    CUDA-core kernel, one thread per path. The oracle restatement on 8,192
-    middle rays is the CPU figure."""
+    CUDA-core kernel, one thread per path; and PBVRT (next-event estimation
+    toward a directional light) on the voxel field. The oracle restatement
+    on 8,192 middle rays is the CPU figure."""
     import rdv_project_b200 as rdv
     from oracle import raymarch as orm
 
@@ -1040,10 +1041,12 @@ def pbvr_summary(steps=3):
     node = rdv.PBVR(ext, env, grid.to(dev), **kw)
     sph = sphere_from_voxel(grid.numpy()[..., 0])
     node_s = rdv.PBVR(ext, env, rdv.SphereMajorantField(torch.from_numpy(sph).to(dev)), **kw)
+    node_t = rdv.PBVRT(ext, grid.to(dev), env, rdv.Constant([0.8, 0.8, 0.8]), light_direction=(0.3, 1.0, -0.2),
+                       light_intensity=(2.0, 2.0, 2.0), g=0.3, max_bounces=8)
     rays = trm_rays().to(dev)
     seeds = (1234567, 7654321, 1357911, 2468024)
     res = {}
-    for name, nd in (("voxel", node), ("sphere", node_s)):
+    for name, nd in (("voxel", node), ("sphere", node_s), ("pbvrt", node_t)):
         for _ in range(2):
             nd(rays, seeds=seeds)
         torch.cuda.synchronize()
@@ -1062,7 +1065,8 @@ def pbvr_summary(steps=3):
     el = time.perf_counter() - t0
     return {"value": _r(evals / t), "unit": "evaluations/s", "ms": _r(t * 1e3), "rays_per_s": _r(rays.shape[0] / t),
             "frac_fp32_nominal": _r(flop / t / 1e12 / nominal, 3), "sphere_ms": _r(res["sphere"][0] * 1e3),
-            "sphere_evals": int(res["sphere"][1]), "cpu": _r(ev_cpu / el)}
+            "sphere_evals": int(res["sphere"][1]), "pbvrt_ms": _r(res["pbvrt"][0] * 1e3),
+            "pbvrt_evals": int(res["pbvrt"][1]), "cpu": _r(ev_cpu / el)}
 
 
 def chain_summary(rows=1 << 20, steps=3):

@@ -59,6 +59,10 @@ extern "C" {
 #define RDVB_SAMPLER_ALIGNED 2
 #define RDVB_SAMPLER_LINEAR 4
 
+/* rdvb_pbvrt variants */
+#define RDVB_PBVRT 0    /* PBVRT: RGB + alpha, the environment after scattering */
+#define RDVB_PBVR_NEE 1 /* PBVR_NEE: RGB, next-event estimation only */
+
 /* Library version (major*10000 + minor*100 + patch). */
 int rdvb_version(void);
 
@@ -447,6 +451,36 @@ int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const f
               const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
               const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
               size_t workspace_bytes, float* out, void* stream);
+
+/* PBVRT and PBVR_NEE (rdv/domain/volumes.py:326-442,
+ * rdv/shaders/volumes/pbvrt.h, pbvr_nee.h): delta tracking with
+ * next-event estimation toward a directional light. Per ray: object space;
+ * a ray that misses the box returns 0 (PBVRT: alpha 1); entry at
+ * max(0, tMin) + 1e-5; at most 16384 times: the field's raw (majorant,
+ * distance), majorant + 1e-5, distance floored at 1e-5, free flight
+ * -log(1 - random()) / (density_scale * majorant) clipped to the distance
+ * and the segment; segment below 1e-7 ends the loop; a tentative collision
+ * is null when random() >= extinction / majorant; a real one counts a
+ * bounce (past max_bounces: PBVRT zeroes the throughput and ends the loop,
+ * NEE returns what it has), multiplies the throughput by albedo (3 host
+ * floats; the loop ends when no channel is above 1e-4), adds throughput *
+ * transmittance_rt(shadow ray toward the light) * hg_phase_eval(w . l, g),
+ * then scatters (hg_phase_sample). light_direction: 3 host floats,
+ * normalized here (l / sqrt((x x + y y) + z z)). PBVRT (variant
+ * RDVB_PBVRT, out [n_rays, 4]): after the loop, when the ray scattered,
+ * alpha 0 and RGB = NEE sum * light_intensity (3 host floats) + throughput *
+ * environment(w) (environment arguments as rdvb_pbvr); else RGB 0, alpha 1.
+ * PBVR_NEE (RDVB_PBVR_NEE, out [n_rays, 3]): the NEE sum; the environment
+ * and light_intensity are not read. Majorant field, generator, chain and
+ * workspace as rdvb_transmittance_rt (bytes 8-15: extinction evaluations,
+ * shadow rays included). */
+int rdvb_pbvrt(const float* rays, int64_t n_rays, const float* transform, float density_scale, const float* majorant,
+               const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
+               const float* light_direction, const float* light_intensity, int variant, int env_kind,
+               const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
+               const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
+               const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+               size_t workspace_bytes, float* out, void* stream);
 
 #ifdef __cplusplus
 }

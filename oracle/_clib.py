@@ -132,6 +132,9 @@ def ref_pbvr_lib() -> ctypes.CDLL:
         vp, lg, i32, f32 = ctypes.c_void_p, ctypes.c_long, ctypes.c_int, ctypes.c_float
         lib.ref_pbvr.argtypes = [f32, f32, i32, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, vp, lg, vp]
         lib.ref_pbvr.restype = None
+        lib.ref_pbvrt.argtypes = [i32, f32, f32, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp, f32, f32, i32, vp, vp,
+                                  lg, vp]
+        lib.ref_pbvrt.restype = None
         lib.ref_hg_phase_sample.argtypes = [vp, i32, i32, vp, f32, vp]
         lib.ref_hg_phase_sample.restype = None
         _ref_pbvr = lib

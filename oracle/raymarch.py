@@ -631,3 +631,231 @@ def pbvr(origins, dirs, extinction, environment, majorant, seeds, transform=None
     if return_evaluations:
         return out, evals
     return out
+
+
+def hg_phase_eval(cos_t: np.ndarray, g: float) -> np.ndarray:
+    """hg_phase_eval (random_library.h:241-249) in float32:
+    (0.25 / pi) (1 - g^2) / (1 + g^2 - 2 g cos)^1.5, or 0.25 / pi when
+    |g| < 0.001."""
+    cos_t = np.asarray(cos_t, dtype=np.float32)
+    g = np.float32(g)
+    quarter_pi = np.float32(np.float32(0.25) / _PI)
+    if abs(float(g)) < 0.001:
+        return np.full(cos_t.shape, quarter_pi, dtype=np.float32)
+    g2 = g * g
+    base = ((np.float32(1.0) + g2) - (np.float32(2.0) * g) * cos_t).astype(np.float32)
+    powed = np.power(base.astype(np.float64), 1.5).astype(np.float32)
+    return ((quarter_pi * (np.float32(1.0) - g2)) / powed).astype(np.float32)
+
+
+def normalize3(v) -> np.ndarray:
+    """v / sqrt((x x + y y) + z z) in float32."""
+    v = np.asarray(v, dtype=np.float32).reshape(3)
+    sq = np.float32(np.float32(v[0] * v[0] + v[1] * v[1]) + v[2] * v[2])
+    return (v / np.float32(np.sqrt(np.float64(sq)))).astype(np.float32)
+
+
+def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, light_intensity=(1.0, 1.0, 1.0),
+          environment=None, transform=None, density_scale: float = 1.0, g: float = 0.0, max_bounces: int = 32,
+          variant: str = "pbvrt", index=None, draws_before: int = 0, return_evaluations: bool = False):
+    """PBVRT.forward (rdv/shaders/volumes/pbvrt.h:21-149) and, with
+    variant="nee", PBVR_NEE.forward (pbvr_nee.h), vectorised over rays, each
+    ray a state machine of the main path and its shadow ray run in lock step,
+    every operation in float32:
+
+        object space; miss (tMax <= 0 or tMin >= tMax) -> 0 (PBVRT: alpha 1)
+        x <- entry at max(0, tMin) + 1e-5; d = tMax - tMin; W = 1
+        for (safety < 16384):
+            maj = majorant(x, wo, dist) + 1e-5; dist <= 1e-5 -> 1e-5
+            dt = min(min(d, dist), -log(1 - random()) / (density_scale maj))
+            x += dt wo; d -= dt; dt >= dist -> continue; d <= 1e-7 -> break
+            random() >= extinction(x) / maj -> continue
+            ++bounces > max_bounces -> PBVRT: W = 0, break; NEE: return
+            W *= albedo; no W > 1e-4 -> PBVRT: break; NEE: return
+            out += W transmittance_rt(x, L l, slab exit) hg_phase_eval(w . l, g)
+            w <- hg_phase_sample(w, g); wo <- L w; d <- slab exit from x
+        PBVRT: bounces > 0 -> alpha 0, out = out light_intensity + W env(w)
+
+    `majorant(x, w)` returns the field's raw (value, distance);
+    transmittance_rt is ratiotracking_transmittance_trait.h's loop (as
+    transmittance_rt above). Returns [n, 4] (PBVRT) or [n, 3] (NEE)."""
+    nee = variant == "nee"
+    o, w_obj = object_space(origins, dirs, transform)
+    w_world = np.asarray(dirs, dtype=np.float32).copy()
+    L = _inverse3(transform)
+    n = o.shape[0]
+    n_out = 3 if nee else 4
+    out = np.zeros((n, n_out), dtype=np.float32)
+    if not nee:
+        out[:, 3] = 1.0
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.float32(1.0) / w_obj
+        xc = -o * inv
+        sa = np.abs(inv)
+        lo = xc - sa
+        hi = xc + sa
+    tmin = _glsl_max(_glsl_max(lo[:, 0], lo[:, 1]), lo[:, 2])
+    tmax = _glsl_min(_glsl_min(hi[:, 0], hi[:, 1]), hi[:, 2])
+    miss = (tmax <= 0) | (tmin >= tmax)
+    hit = np.nonzero(~miss)[0]
+    evals = 0
+    if hit.size == 0:
+        return (out, 0) if return_evaluations else out
+    idx = np.arange(n) if index is None else np.asarray(index)
+    state = random_spawn(seeds, idx[hit])
+    for _ in range(draws_before):
+        random_step(state)
+    m = hit.size
+    t0 = (_glsl_max(np.float32(0.0), tmin[hit]) + np.float32(1e-5)).astype(np.float32)
+    x = (o[hit] + w_obj[hit] * t0[:, None]).astype(np.float32)
+    d = (tmax[hit] - t0).astype(np.float32)
+    wo = w_obj[hit].copy()
+    w = w_world[hit].copy()
+    W = np.ones((m, 3), dtype=np.float32)
+    acc = np.zeros((m, 3), dtype=np.float32)
+    alb = np.asarray(albedo, dtype=np.float32).reshape(1, 3)
+    light = normalize3(light_direction)
+    lo_dir = _apply3(L, light[None].astype(np.float32))[0]
+    bounces = np.zeros(m, dtype=np.int64)
+    safety = np.zeros(m, dtype=np.int64)
+    mode = np.zeros(m, dtype=np.int64)          # 0 main, 1 shadow
+    xs = np.zeros((m, 3), dtype=np.float32)
+    ds = np.zeros(m, dtype=np.float32)
+    T = np.ones(m, dtype=np.float32)
+    phase = np.zeros(m, dtype=np.float32)
+    s_safety = np.zeros(m, dtype=np.int64)
+    maj = np.ones(m, dtype=np.float32)
+    running = np.ones(m, dtype=bool)
+    ended = np.zeros(m, dtype=bool)             # main loop over: resolve the outputs
+    f32 = np.float32
+    dsc = f32(density_scale)
+
+    def shadow_end(rows, t):
+        tr = (t.astype(np.float32) * phase[rows]).astype(np.float32)
+        acc[rows] = (acc[rows] + W[rows] * tr[:, None]).astype(np.float32)
+        sub = state[rows]
+        w[rows] = hg_phase_sample(w[rows], g, sub)
+        state[rows] = sub
+        wo[rows] = _apply3(L, w[rows])
+        d[rows] = slab_exit(x[rows], wo[rows])
+        mode[rows] = 0
+
+    while running.any():
+        pend = np.zeros(m, dtype=bool)
+        # -- main-path steps
+        mm = np.nonzero(running & (mode == 0))[0]
+        if mm.size:
+            cap = safety[mm] >= 16384
+            ended[mm[cap]] = True
+            running[mm[cap]] = False
+            mm = mm[~cap]
+            safety[mm] += 1
+            mv, dist = majorant(x[mm], wo[mm])
+            mj = (mv.astype(np.float32) + f32(1e-5)).astype(np.float32)
+            dist = np.where(dist <= f32(1e-5), f32(1e-5), dist).astype(np.float32)
+            sub = state[mm]
+            u = random_draw(sub)
+            state[mm] = sub
+            with np.errstate(divide="ignore", over="ignore"):
+                q = ((-_log_f32(f32(1.0) - u)) / (dsc * mj)).astype(np.float32)
+            dt = _glsl_min(_glsl_min(d[mm], dist), q)
+            x[mm] = (x[mm] + dt[:, None] * wo[mm]).astype(np.float32)
+            d[mm] = (d[mm] - dt).astype(np.float32)
+            moved = dt >= dist
+            brk = ~moved & (d[mm] <= f32(1e-7))
+            ended[mm[brk]] = True
+            running[mm[brk]] = False
+            coll = ~moved & ~brk
+            maj[mm[coll]] = mj[coll]
+            pend[mm[coll]] = True
+        # -- shadow-ray steps
+        ss = np.nonzero(running & (mode == 1))[0]
+        if ss.size:
+            done = ~(ds[ss] > 0) | (s_safety[ss] >= 1024)
+            if done.any():
+                shadow_end(ss[done], T[ss[done]])
+            ss = ss[~done]
+        if ss.size:
+            s_safety[ss] += 1
+            mv, dist = majorant(xs[ss], np.broadcast_to(lo_dir, (ss.size, 3)).astype(np.float32))
+            mj = _glsl_max(mv.astype(np.float32), f32(1e-12))
+            dist = _glsl_max(dist.astype(np.float32), f32(1e-6))
+            sub = state[ss]
+            u = random_draw(sub)
+            state[ss] = sub
+            with np.errstate(divide="ignore", over="ignore"):
+                q = ((-_log_f32(f32(1.0) - u)) / (mj * dsc)).astype(np.float32)
+            dt = _glsl_min(dist, q)
+            ds[ss] = (ds[ss] - dt).astype(np.float32)
+            xs[ss] = (xs[ss] + dt[:, None] * lo_dir[None]).astype(np.float32)
+            moved = dt >= dist
+            fin = ~moved & (ds[ss] <= 0)
+            if fin.any():
+                shadow_end(ss[fin], T[ss[fin]])
+            coll = ~moved & ~fin
+            maj[ss[coll]] = mj[coll]
+            pend[ss[coll]] = True
+        # -- collisions: the extinction at the main or shadow point
+        pi_ = np.nonzero(pend)[0]
+        if pi_.size == 0:
+            continue
+        pts = np.where((mode[pi_] == 0)[:, None], x[pi_], xs[pi_]).astype(np.float32)
+        sigma = np.asarray(extinction(pts), dtype=np.float32)
+        evals += pi_.size
+        ratio = (sigma / maj[pi_]).astype(np.float32)
+        sh = mode[pi_] == 1
+        if sh.any():
+            rows = pi_[sh]
+            T[rows] = (T[rows] * (f32(1.0) - ratio[sh])).astype(np.float32)
+            low = rows[T[rows] < f32(0.05)]
+            if low.size:
+                sub = state[low]
+                u2 = random_draw(sub)
+                state[low] = sub
+                kill = u2 >= T[low]
+                if kill.any():
+                    shadow_end(low[kill], np.zeros(int(kill.sum()), dtype=np.float32))
+                T[low[~kill]] = 1.0
+        mn = ~sh
+        if mn.any():
+            rows = pi_[mn]
+            sub = state[rows]
+            u2 = random_draw(sub)
+            state[rows] = sub
+            real = rows[~(u2 >= ratio[mn])]
+            if real.size:
+                bounces[real] += 1
+                over = real[bounces[real] > max_bounces]
+                if over.size:
+                    if not nee:
+                        W[over] = 0.0
+                    ended[over] = True
+                    running[over] = False
+                go = real[bounces[real] <= max_bounces]
+                W[go] = (W[go] * alb).astype(np.float32)
+                low_w = ~np.any(W[go] > f32(1e-4), axis=1)
+                ended[go[low_w]] = True
+                running[go[low_w]] = False
+                go = go[~low_w]
+                if go.size:
+                    cos_t = ((w[go, 0] * light[0] + w[go, 1] * light[1]).astype(np.float32) + w[go, 2] * light[2])
+                    phase[go] = hg_phase_eval(cos_t.astype(np.float32), g)
+                    xs[go] = x[go]
+                    ds[go] = slab_exit(x[go], np.broadcast_to(lo_dir, (go.size, 3)).astype(np.float32))
+                    T[go] = 1.0
+                    s_safety[go] = 0
+                    mode[go] = 1
+    if nee:
+        out[hit] = acc
+    else:
+        scat = bounces > 0
+        res = np.zeros((m, 4), dtype=np.float32)
+        res[:, 3] = 1.0
+        if scat.any():
+            e = np.nonzero(scat)[0]
+            env = environment(w[e]).astype(np.float32)
+            li = np.asarray(light_intensity, dtype=np.float32).reshape(1, 3)
+            res[e, :3] = ((acc[e] * li).astype(np.float32) + (W[e] * env).astype(np.float32)).astype(np.float32)
+            res[e, 3] = 0.0
+        out[hit] = res
+    return (out, evals) if return_evaluations else out

@@ -89,7 +89,10 @@ static inline rdv_vec3 operator*(rdv_vec3 a, rdv_vec3 b) { return rdv_vec3(a.x *
 static inline rdv_vec3 operator*(double s, rdv_vec3 v) { return (float)s * v; }
 static inline float dot(rdv_vec3 a, rdv_vec3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
 // GLSL's float log: C++ would widen `1.0 - random()` and evaluate in double.
-static inline float rdv_log(double v) { return std::log((float)v); }
+// Transcendentals of a float argument are evaluated in double and rounded
+// once (the correctly rounded float result in practice), as the numpy
+// restatements do; the pins then compare operation order, not two libm's.
+static inline float rdv_log(double v) { return (float)std::log((double)(float)v); }
 static inline float min(float a, double b) { return a < (float)b ? a : (float)b; }
 static inline float max(int a, double b) { return (float)a > (float)b ? (float)a : (float)b; }
 

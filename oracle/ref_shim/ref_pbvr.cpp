@@ -119,16 +119,19 @@ static void create_ortho_basis(rdv_vec3 N, rdv_vec3& T, rdv_vec3& B) {
 #define random rdv_random  // stdlib's long random(void) has the same name
 static float min(float a, float b) { return a < b ? a : b; }
 static inline float abs(float v) { return std::fabs(v); }
-// GLSL's sin / cos / sqrt of a float are float: without these the global
-// double overloads would round sinTheta * sin(phi) once, in double
-#define sin(x) std::sin(static_cast<float>(x))
-#define cos(x) std::cos(static_cast<float>(x))
+// GLSL's sin / cos / sqrt / pow of a float are float: without these the
+// global double overloads would round sinTheta * sin(phi) once, in double.
+// Each is evaluated in double and rounded to float once (see rdv_log).
+#define sin(x) static_cast<float>(std::sin(static_cast<double>(static_cast<float>(x))))
+#define cos(x) static_cast<float>(std::cos(static_cast<double>(static_cast<float>(x))))
 #define sqrt(x) std::sqrt(static_cast<float>(x))
+#define pow(a, b) static_cast<float>(std::pow(static_cast<double>(static_cast<float>(a)), \
+                                              static_cast<double>(static_cast<float>(b))))
 #define RDV_NODE rdv_random_init
 #include "random_library.h"
 #undef RDV_NODE
 
-// -- the majorant fields (Map[6, 2] contract: (x, w) -> majorant, max step) --
+// -- the majorant fields (Map[6, 2]: (x, w) -> majorant, distance) ----------
 struct VoxelField {
     const float* grid;  // [D, H, W]
     int gd, gh, gw;
@@ -221,6 +224,89 @@ typedef PbvrNode<SphereField> PbvrSphere;
 #define RDV_NODE PbvrSphere
 #include "pbvr.h"
 #undef RDV_NODE
+
+// -- PBVRT and PBVR_NEE (volumes/pbvrt.h, pbvr_nee.h) -------------------------
+// Their trait helpers (extinction_trait.h, majorant_trait.h,
+// scattering_albedo_trait.h, environment_trait.h: one forward() each, with
+// GLSL array constructors) are restated per node below; the shadow ray is
+// ratiotracking_transmittance_trait.h itself (the float-literal copy of
+// libref_shaders.so), instantiated per node.
+static inline rdv_vec3 normalize(rdv_vec3 v) {
+    const float len = sqrt((v.x * v.x + v.y * v.y) + v.z * v.z);
+    return rdv_vec3(v.x / len, v.y / len, v.z / len);
+}
+#define SPECTRAL_DIM 3
+template <typename MG>
+struct PbvrtNode {
+    ExtNode ext;
+    MG mg;
+    EnvConst env;
+    float sa[3];
+    rdv_mat4x3 transform;
+    rdv_vec3 light_direction;
+    float light_intensity[3];
+    float g;
+    float density_scale;
+    int max_bounces;
+};
+typedef PbvrtNode<VoxelField> PbvrtVoxel;
+typedef PbvrtNode<SphereField> PbvrtSphere;
+template <typename MG>
+static float extinction(PbvrtNode<MG> node, rdv_vec3 x) {
+    float in_[3] = {x.x, x.y, x.z}, v[1];
+    forward(node.ext, in_, v);
+    return v[0];
+}
+// majorant_trait.h: the field's raw (majorant, distance)
+static float majorant(PbvrtNode<VoxelField> node, rdv_vec3 x, rdv_vec3 w, float& distance) {
+    return voxel_field(node.mg, x, w, distance);
+}
+static float majorant(PbvrtNode<SphereField> node, rdv_vec3 x, rdv_vec3 w, float& distance) {
+    return sphere_field(node.mg, x, w, distance);
+}
+template <typename MG>
+static void scattering_albedo(PbvrtNode<MG> node, rdv_vec3, float* sa) {
+    for (int i = 0; i < 3; ++i) sa[i] = node.sa[i];
+}
+template <typename MG>
+static void environment(PbvrtNode<MG> node, rdv_vec3, float* env) {
+    env[0] = node.env.r;
+    env[1] = node.env.g;
+    env[2] = node.env.b;
+}
+#define RDV_NODE PbvrtVoxel
+#include "volumes/ratiotracking_transmittance_trait.h"
+#define OUT 4
+#include "pbvrt.h"
+#undef OUT
+#undef RDV_NODE
+#define RDV_NODE PbvrtSphere
+#include "volumes/ratiotracking_transmittance_trait.h"
+#define OUT 4
+#include "pbvrt.h"
+#undef OUT
+#undef RDV_NODE
+// PBVR_NEE: the same node fields (environment and light_intensity unused)
+struct NeeVoxel : PbvrtVoxel {};
+struct NeeSphere : PbvrtSphere {};
+static float extinction(NeeVoxel n, rdv_vec3 x) { return extinction(static_cast<PbvrtVoxel>(n), x); }
+static float extinction(NeeSphere n, rdv_vec3 x) { return extinction(static_cast<PbvrtSphere>(n), x); }
+static float majorant(NeeVoxel n, rdv_vec3 x, rdv_vec3 w, float& d) { return majorant(static_cast<PbvrtVoxel>(n), x, w, d); }
+static float majorant(NeeSphere n, rdv_vec3 x, rdv_vec3 w, float& d) { return majorant(static_cast<PbvrtSphere>(n), x, w, d); }
+static void scattering_albedo(NeeVoxel n, rdv_vec3 x, float* sa) { scattering_albedo(static_cast<PbvrtVoxel>(n), x, sa); }
+static void scattering_albedo(NeeSphere n, rdv_vec3 x, float* sa) { scattering_albedo(static_cast<PbvrtSphere>(n), x, sa); }
+#define RDV_NODE NeeVoxel
+#include "volumes/ratiotracking_transmittance_trait.h"
+#define OUT 3
+#include "pbvr_nee.h"
+#undef OUT
+#undef RDV_NODE
+#define RDV_NODE NeeSphere
+#include "volumes/ratiotracking_transmittance_trait.h"
+#define OUT 3
+#include "pbvr_nee.h"
+#undef OUT
+#undef RDV_NODE
 #undef log
 #undef random
 
@@ -265,6 +351,48 @@ void ref_pbvr(float c0, float c1, int field_kind, const float* grid, int gd, int
         setup(node, c0, c1, env_rgb, transform, albedo, g, max_bounces);
         node.mg = SphereField{grid, gd, gh, gw};
         run(node, seeds, rays, n, dst);
+    }
+}
+
+// PBVRT.forward (variant 0, dst [n, 4]) or PBVR_NEE.forward (variant 1,
+// dst [n, 3]) for rays [n, 6]; fields, extinction and the constant albedo /
+// environment as ref_pbvr.
+void ref_pbvrt(int variant, float c0, float c1, int field_kind, const float* grid, int gd, int gh, int gw,
+               const float* env_rgb, const float* transform, const float* albedo, const float* light_direction,
+               const float* light_intensity, float g, float density_scale, int max_bounces, const unsigned* seeds,
+               const float* rays, long n, float* dst) {
+    auto fill = [&](auto& node) {
+        node.ext = ExtNode{c0, c1};
+        node.env = EnvConst{env_rgb[0], env_rgb[1], env_rgb[2]};
+        for (int k = 0; k < 3; ++k) {
+            node.sa[k] = albedo[k];
+            node.light_intensity[k] = light_intensity[k];
+        }
+        for (int j = 0; j < 4; ++j)
+            node.transform.c[j] = rdv_vec3(transform[3 * j], transform[3 * j + 1], transform[3 * j + 2]);
+        node.light_direction = rdv_vec3(light_direction[0], light_direction[1], light_direction[2]);
+        node.g = g;
+        node.density_scale = density_scale;
+        node.max_bounces = max_bounces;
+    };
+    const int n_out = variant == 0 ? 4 : 3;
+    auto run_rays = [&](auto node) {
+        for (long r = 0; r < n; ++r) {
+            random_seeds.seeds = rdv_uvec4(seeds[0], seeds[1], seeds[2], seeds[3]);
+            rdv_random_init(rdv_uvec3{(unsigned)r, 0u, 0u});
+            float in6[6];
+            for (int k = 0; k < 6; ++k) in6[k] = rays[r * 6 + k];
+            forward(node, in6, dst + r * n_out);
+        }
+    };
+    if (variant == 0 && field_kind == 0) {
+        PbvrtVoxel node; fill(node); node.mg = VoxelField{grid, gd, gh, gw}; run_rays(node);
+    } else if (variant == 0) {
+        PbvrtSphere node; fill(node); node.mg = SphereField{grid, gd, gh, gw}; run_rays(node);
+    } else if (field_kind == 0) {
+        NeeVoxel node; fill(node); node.mg = VoxelField{grid, gd, gh, gw}; run_rays(node);
+    } else {
+        NeeSphere node; fill(node); node.mg = SphereField{grid, gd, gh, gw}; run_rays(node);
     }
 }
 

@@ -251,5 +251,246 @@ __global__ void __launch_bounds__(NT) pbvr_kernel(const __grid_constant__ Params
     if (my_evals) atomicAdd(p.evaluations, my_evals);
 }
 
+// ---------------------------------------------------------------------------
+// PBVRT and PBVR_NEE (rdv/domain/volumes.py:326-442, rdv/shaders/volumes/
+// pbvrt.h, pbvr_nee.h): delta tracking with next-event estimation toward a
+// directional light, RGB. Per ray -- pbvrt.h:21-149:
+//   object space; slab test (miss: tMax <= 0 or tMin >= tMax) -> 0 (PBVRT:
+//   alpha 1); entry x <- x + w_o (max(0, tMin) + 1e-5), d <- tMax - tMin;
+//   for (safety < 16384):
+//     maj = majorant(x, w_o, dist) + 1e-5; dist <= 1e-5 -> 1e-5
+//     dt = min(min(d, dist), -log(1 - random()) / (density_scale * maj))
+//     x += dt w_o; d -= dt; dt >= dist -> continue; d <= 1e-7 -> break
+//     random() >= extinction(x) / maj -> continue (null collision)
+//     ++bounces > max_bounces -> PBVRT: W = 0, break; NEE: return
+//     W *= albedo; no W[i] > 1e-4 -> PBVRT: break; NEE: return
+//     out += W * transmittance_rt(x, L l, tMax from x) * hg_phase_eval(w . l, g)
+//       (a ratio-tracking shadow ray: ratiotracking_transmittance_trait.h)
+//     w <- hg_phase_sample(w, g); w_o <- L w; d <- slab exit from x
+//   PBVRT after the loop, if bounces > 0: alpha 0,
+//     out = out * light_intensity + W * environment(w).
+// The majorant here is the field's raw (majorant, distance), as
+// majorant_trait.h reads it. Each lane is a small state machine: the main
+// path or its shadow ray; both stop at tentative collisions, where the warp
+// evaluates the extinction together at each lane's point.
+struct ExtraT {
+    float albedo[3];
+    float g;
+    float density_scale;
+    int max_bounces;
+    int variant;             // 0 PBVRT ([n, 4]: RGB, alpha), 1 PBVR_NEE ([n, 3])
+    float light[3];          // normalize(light_direction), world space (host)
+    float intensity[3];      // PBVRT: light_intensity
+    Extra env;               // environment (PBVRT) and the output pointer
+};
+
+constexpr int kSafetyT = 16384;   // pbvrt.h / pbvr_nee.h loop cap
+
+// hg_phase_eval (random_library.h:241-249) at cos_theta
+__device__ __forceinline__ float hg_eval(float cos_t, float g) {
+    if (fabsf(g) < 0.001f) return __fdiv_rn(0.25f, kPi);
+    const float g2 = __fmul_rn(g, g);
+    const float omg2 = __fsub_rn(1.0f, g2), opg2 = __fadd_rn(1.0f, g2);
+    const float base = __fsub_rn(opg2, __fmul_rn(__fmul_rn(2.0f, g), cos_t));
+    return __fdiv_rn(__fmul_rn(__fdiv_rn(0.25f, kPi), omg2), powf(base, 1.5f));
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT) pbvrt_kernel(const __grid_constant__ Params p, const __grid_constant__ ExtraT e) {
+    extern __shared__ float sm[];
+    float* wsm = sm;
+    float* act0 = sm + ((p.w_floats + 3) & ~3) + threadIdx.x;
+    float* act1 = act0 + p.maxw * NT;
+    trm::stage_chain<NT>(p, wsm);
+    const float* bsm = wsm;
+    const int n_out = e.variant == 0 ? 4 : 3;
+    float* out_ptr = e.env.out;
+    // the light in object space (L l, each sum rounded in order) and its
+    // slab exit from a point are per ray below
+    float lo[3];
+    to_object(p.L, e.light, lo);
+    unsigned long long my_evals = 0;
+    long long ray = -1;  // -1: take the next ray; -2: none left
+    float x[3] = {0.0f, 0.0f, 0.0f}, w[3] = {0.0f, 0.0f, 1.0f}, wo[3] = {0.0f, 0.0f, 1.0f};
+    float d = 0.0f, maj = 1.0f, W[3] = {1.0f, 1.0f, 1.0f}, acc[3] = {0.0f, 0.0f, 0.0f};
+    int safety = 0, bounces = 0;
+    // shadow ray (mode 1): point, remaining distance, transmittance, its own cap, the phase
+    int mode = 0;
+    float xs[3] = {0.0f, 0.0f, 0.0f}, ds = 0.0f, T = 1.0f, phase = 0.0f;
+    int s_safety = 0;
+    Rng r = {0u, 0u, 0u, 0u};
+    auto store = [&](float a0, float a1, float a2, float alpha) {
+        out_ptr[ray * n_out + 0] = a0;
+        out_ptr[ray * n_out + 1] = a1;
+        out_ptr[ray * n_out + 2] = a2;
+        if (n_out == 4) out_ptr[ray * n_out + 3] = alpha;
+        ray = -1;
+    };
+    // the main loop ended (cap, break): PBVRT resolves the escape term
+    auto loop_end = [&]() {
+        if (e.variant == 1) {
+            store(acc[0], acc[1], acc[2], 0.0f);
+            return;
+        }
+        if (bounces > 0) {
+            float c[3];
+            environment(e.env, w, c);
+            store(__fadd_rn(__fmul_rn(acc[0], e.intensity[0]), __fmul_rn(W[0], c[0])),
+                  __fadd_rn(__fmul_rn(acc[1], e.intensity[1]), __fmul_rn(W[1], c[1])),
+                  __fadd_rn(__fmul_rn(acc[2], e.intensity[2]), __fmul_rn(W[2], c[2])), 0.0f);
+        } else {
+            store(0.0f, 0.0f, 0.0f, 1.0f);
+        }
+    };
+    // the shadow ray ended with transmittance t: add its NEE term, scatter
+    auto shadow_end = [&](float t) {
+        const float tr = __fmul_rn(t, phase);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(W[k], tr));
+        hg_sample(r, e.g, w);
+        to_object(p.L, w, wo);
+        d = slab_exit(x, wo);
+        mode = 0;
+    };
+    while (true) {
+        bool pending = false;
+        for (int flights = 0; ray != -2 && !pending && flights < trm::kYieldFlights; ++flights) {
+            if (ray < 0) {
+                ray = atomicAdd(p.counter, 1);
+                if (ray >= p.n_rays) {
+                    ray = -2;
+                    break;
+                }
+                const float* rr = p.rays + ray * 6;
+                w[0] = rr[3];
+                w[1] = rr[4];
+                w[2] = rr[5];
+                // object space and slab test (pbvrt.h:25-41)
+                float xr[3];
+#pragma unroll
+                for (int k = 0; k < 3; ++k) xr[k] = __fsub_rn(rr[k], p.O[k]);
+                to_object(p.L, xr, x);
+                to_object(p.L, w, wo);
+                float tmin = -INFINITY, tmax = INFINITY;
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    const float inv = __fdiv_rn(1.0f, wo[k]);
+                    const float xc = __fmul_rn(-x[k], inv);
+                    const float sabs = fabsf(inv);
+                    const float lo_k = __fsub_rn(xc, sabs), hi_k = __fadd_rn(xc, sabs);
+                    tmin = tmin < lo_k ? lo_k : tmin;   // GLSL max
+                    tmax = hi_k < tmax ? hi_k : tmax;   // GLSL min
+                }
+                if (tmax <= 0.0f || tmin >= tmax) {
+                    store(0.0f, 0.0f, 0.0f, 1.0f);
+                    continue;
+                }
+                tmin = __fadd_rn(0.0f < tmin ? tmin : 0.0f, 1e-5f);
+#pragma unroll
+                for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(wo[k], tmin));
+                d = __fsub_rn(tmax, tmin);
+                W[0] = W[1] = W[2] = 1.0f;
+                acc[0] = acc[1] = acc[2] = 0.0f;
+                safety = 0;
+                bounces = 0;
+                mode = 0;
+                r = rng_spawn(p.seeds, static_cast<unsigned>(ray));
+                for (int k = 0; k < p.draws_before; ++k) rng_step(r);
+            }
+            if (mode == 0) {
+                if (safety >= kSafetyT) {  // the loop ran out
+                    loop_end();
+                    continue;
+                }
+                ++safety;
+                float dist;
+                maj = __fadd_rn(trm::field_majorant(p, x, wo, dist), 1e-5f);
+                if (dist <= 1e-5f) dist = 1e-5f;
+                const float q = __fdiv_rn(-logf(__fsub_rn(1.0f, rng_uniform(r))), __fmul_rn(e.density_scale, maj));
+                const float m = dist < d ? dist : d;      // min(d, dist)
+                const float dt = q < m ? q : m;           // min(., q)
+#pragma unroll
+                for (int k = 0; k < 3; ++k) x[k] = __fadd_rn(x[k], __fmul_rn(dt, wo[k]));
+                d = __fsub_rn(d, dt);
+                if (dt >= dist) continue;
+                if (d <= 1e-7f) {
+                    loop_end();
+                    continue;
+                }
+                pending = true;
+            } else {
+                // transmittance_rt (ratiotracking_transmittance_trait.h:1-31) along the light
+                if (!(ds > 0.0f) || s_safety >= trm::kRtSafety) {
+                    shadow_end(T);
+                    continue;
+                }
+                ++s_safety;
+                float dist;
+                float mj = trm::field_majorant(p, xs, lo, dist);
+                mj = mj < 1e-12f ? 1e-12f : mj;
+                dist = dist < 1e-6f ? 1e-6f : dist;
+                maj = mj;
+                const float q = __fdiv_rn(-logf(__fsub_rn(1.0f, rng_uniform(r))), __fmul_rn(mj, e.density_scale));
+                const float dt = q < dist ? q : dist;     // min(dist, q)
+                ds = __fsub_rn(ds, dt);
+#pragma unroll
+                for (int k = 0; k < 3; ++k) xs[k] = __fadd_rn(xs[k], __fmul_rn(dt, lo[k]));
+                if (dt >= dist) continue;
+                if (ds <= 0.0f) {
+                    shadow_end(T);
+                    continue;
+                }
+                pending = true;
+            }
+        }
+        if (!__any_sync(0xffffffffu, pending)) {
+            if (__all_sync(0xffffffffu, ray == -2)) break;  // no lane has rays left
+            continue;
+        }
+        float pt[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) pt[k] = mode == 0 ? x[k] : xs[k];
+        const float sigma = trm::extinction<NT>(p, wsm, bsm, act0, act1, pt);
+        if (!pending) continue;
+        ++my_evals;
+        if (mode == 1) {
+            T = __fmul_rn(T, __fsub_rn(1.0f, __fdiv_rn(sigma, maj)));
+            if (T < 0.05f) {
+                if (rng_uniform(r) >= T) {
+                    shadow_end(0.0f);
+                    continue;
+                }
+                T = 1.0f;
+            }
+            continue;
+        }
+        if (rng_uniform(r) >= __fdiv_rn(sigma, maj)) continue;  // null collision
+        ++bounces;
+        if (bounces > e.max_bounces) {
+            if (e.variant == 0) W[0] = W[1] = W[2] = 0.0f;
+            loop_end();
+            continue;
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k) W[k] = __fmul_rn(W[k], e.albedo[k]);
+        if (!(W[0] > 0.0001f || W[1] > 0.0001f || W[2] > 0.0001f)) {
+            loop_end();
+            continue;
+        }
+        // next-event estimation toward the light: phase, then the shadow ray
+        const float cos_t = __fadd_rn(__fadd_rn(__fmul_rn(w[0], e.light[0]), __fmul_rn(w[1], e.light[1])),
+                                      __fmul_rn(w[2], e.light[2]));
+        phase = hg_eval(cos_t, e.g);
+        xs[0] = x[0];
+        xs[1] = x[1];
+        xs[2] = x[2];
+        ds = slab_exit(x, lo);
+        T = 1.0f;
+        s_safety = 0;
+        mode = 1;
+    }
+    if (my_evals) atomicAdd(p.evaluations, my_evals);
+}
+
 }  // namespace pbvr
 }  // namespace rdvb

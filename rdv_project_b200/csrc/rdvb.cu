@@ -61,6 +61,8 @@ struct DeviceInfo {
     size_t rt_wide_smem_set = 0;
     size_t pbvr_smem_set = 0;
     size_t pbvr_wide_smem_set = 0;
+    size_t pbvrt_smem_set = 0;
+    size_t pbvrt_wide_smem_set = 0;
     size_t rows_smem_set = 0;
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
@@ -1408,11 +1410,13 @@ int trm_object_space(const float* transform, rdvb::trm::Params& p) {
 // The CUDA-core march kernels: the chain's shared-memory weight image, then
 // one launch of as many persistent 128-thread CTAs as fit (rays handed out
 // by the counter at the start of the workspace).
-enum class March { kRaymarch, kRatioTracking, kPbvr };
+enum class March { kRaymarch, kRatioTracking, kPbvr, kPbvrt };
 
+// extra: the kernel's second argument (rdvb::pbvr::Extra for kPbvr,
+// rdvb::pbvr::ExtraT for kPbvrt), else null.
 int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const float* const* weights,
                       const float* const* biases, const int* layer_flags, void* workspace, DeviceInfo* dev,
-                      cudaStream_t st, March kind, const rdvb::pbvr::Extra* extra = nullptr) {
+                      cudaStream_t st, March kind, const void* extra = nullptr) {
     using namespace rdvb::trm;
     int off = 0;
     for (int l = 0; l < n_layers; ++l) {
@@ -1464,6 +1468,12 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
             smem_set = wide ? &dev->pbvr_wide_smem_set : &dev->pbvr_smem_set;
             name = "pbvr_kernel";
             break;
+        case March::kPbvrt:
+            kernel = wide ? reinterpret_cast<const void*>(rdvb::pbvr::pbvrt_kernel<kRtWideThreads>)
+                          : reinterpret_cast<const void*>(rdvb::pbvr::pbvrt_kernel<kThreads>);
+            smem_set = wide ? &dev->pbvrt_wide_smem_set : &dev->pbvrt_smem_set;
+            name = "pbvrt_kernel";
+            break;
     }
     if (*smem_set < smem) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -1479,8 +1489,8 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * dev->sm_count * per_sm)));
     e = cudaMemsetAsync(workspace, 0, 16, st);
     if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    if (kind == March::kPbvr) {
-        void* args[] = {&p, const_cast<rdvb::pbvr::Extra*>(extra)};
+    if (kind == March::kPbvr || kind == March::kPbvrt) {
+        void* args[] = {&p, const_cast<void*>(extra)};
         e = cudaLaunchKernel(kernel, dim3(grid), dim3(threads), args, smem, st);
         if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
     } else {
@@ -1687,6 +1697,35 @@ int tracking_params(const float* rays, int64_t n_rays, const float* transform, c
     p.draws_before = draws_before;
     return trm_object_space(transform, p);
 }
+
+// The PBVR environment: a constant RGB or an equirectangular image [H, W, 3].
+int environment_args(int env_kind, const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
+                     int64_t n_rays, rdvb::pbvr::Extra& e) {
+    if (env_kind == RDVB_ENV_CONSTANT) {
+        if (!env_rgb) return fail(RDVB_ERR_INVALID_ARG, "a constant environment needs env_rgb");
+        for (int k = 0; k < 3; ++k) e.env_rgb[k] = env_rgb[k];
+    } else if (env_kind == RDVB_ENV_EQUIRECT) {
+        if (!env_dims) return fail(RDVB_ERR_INVALID_ARG, "an equirectangular environment needs env_dims");
+        if (env_dims[0] < 1 || env_dims[1] < 1)
+            return fail(RDVB_ERR_INVALID_ARG, "env_dims must be positive, got %d x %d", env_dims[0], env_dims[1]);
+        if (1LL * env_dims[0] * env_dims[1] > (1LL << 28))
+            return fail(RDVB_ERR_UNSUPPORTED, "the environment image must have at most 2^28 pixels");
+        if (env_flags & ~(RDVB_SAMPLER_CLAMP | RDVB_SAMPLER_ALIGNED | RDVB_SAMPLER_LINEAR))
+            return fail(RDVB_ERR_INVALID_ARG, "unknown env_flags bits 0x%x", env_flags);
+        if (n_rays > 0 && (!env_image || !aligned(env_image, 4)))
+            return fail(RDVB_ERR_INVALID_ARG, "env_image must be a 4-byte aligned device pointer");
+        e.env_kind = 1;
+        e.env = env_image;
+        e.env_h = env_dims[0];
+        e.env_w = env_dims[1];
+        e.env_clamp = (env_flags & RDVB_SAMPLER_CLAMP) ? 1 : 0;
+        e.env_aligned = (env_flags & RDVB_SAMPLER_ALIGNED) ? 1 : 0;
+        e.env_linear = (env_flags & RDVB_SAMPLER_LINEAR) ? 1 : 0;
+    } else {
+        return fail(RDVB_ERR_INVALID_ARG, "env_kind must be RDVB_ENV_CONSTANT or RDVB_ENV_EQUIRECT, got %d", env_kind);
+    }
+    return RDVB_OK;
+}
 }  // namespace
 
 int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
@@ -1726,29 +1765,7 @@ int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const f
     for (int k = 0; k < 3; ++k) e.albedo[k] = albedo[k];
     e.g = g;
     e.max_bounces = max_bounces;
-    if (env_kind == RDVB_ENV_CONSTANT) {
-        if (!env_rgb) return fail(RDVB_ERR_INVALID_ARG, "a constant environment needs env_rgb");
-        for (int k = 0; k < 3; ++k) e.env_rgb[k] = env_rgb[k];
-    } else if (env_kind == RDVB_ENV_EQUIRECT) {
-        if (!env_dims) return fail(RDVB_ERR_INVALID_ARG, "an equirectangular environment needs env_dims");
-        if (env_dims[0] < 1 || env_dims[1] < 1)
-            return fail(RDVB_ERR_INVALID_ARG, "env_dims must be positive, got %d x %d", env_dims[0], env_dims[1]);
-        if (1LL * env_dims[0] * env_dims[1] > (1LL << 28))
-            return fail(RDVB_ERR_UNSUPPORTED, "the environment image must have at most 2^28 pixels");
-        if (env_flags & ~(RDVB_SAMPLER_CLAMP | RDVB_SAMPLER_ALIGNED | RDVB_SAMPLER_LINEAR))
-            return fail(RDVB_ERR_INVALID_ARG, "unknown env_flags bits 0x%x", env_flags);
-        if (n_rays > 0 && (!env_image || !aligned(env_image, 4)))
-            return fail(RDVB_ERR_INVALID_ARG, "env_image must be a 4-byte aligned device pointer");
-        e.env_kind = 1;
-        e.env = env_image;
-        e.env_h = env_dims[0];
-        e.env_w = env_dims[1];
-        e.env_clamp = (env_flags & RDVB_SAMPLER_CLAMP) ? 1 : 0;
-        e.env_aligned = (env_flags & RDVB_SAMPLER_ALIGNED) ? 1 : 0;
-        e.env_linear = (env_flags & RDVB_SAMPLER_LINEAR) ? 1 : 0;
-    } else {
-        return fail(RDVB_ERR_INVALID_ARG, "env_kind must be RDVB_ENV_CONSTANT or RDVB_ENV_EQUIRECT, got %d", env_kind);
-    }
+    if (int rc = environment_args(env_kind, env_rgb, env_image, env_dims, env_flags, n_rays, e)) return rc;
     if (n_rays == 0) return RDVB_OK;
     e.out = out;
     DeviceInfo* dev = nullptr;
@@ -1756,6 +1773,53 @@ int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const f
     return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev,
                              static_cast<cudaStream_t>(stream), March::kPbvr, &e);
 }
+
+int rdvb_pbvrt(const float* rays, int64_t n_rays, const float* transform, float density_scale, const float* majorant,
+               const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
+               const float* light_direction, const float* light_intensity, int variant, int env_kind,
+               const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
+               const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
+               const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+               size_t workspace_bytes, float* out, void* stream) {
+    rdvb::trm::Params p;
+    if (int rc = tracking_params(rays, n_rays, transform, majorant, majorant_dims, majorant_kind, seeds, draws_before,
+                                 n_layers, dims, weights, biases, layer_flags, input_relu, workspace, workspace_bytes,
+                                 out, p, 3))
+        return rc;
+    if (variant != RDVB_PBVRT && variant != RDVB_PBVR_NEE)
+        return fail(RDVB_ERR_INVALID_ARG, "variant must be RDVB_PBVRT or RDVB_PBVR_NEE, got %d", variant);
+    if (!albedo || !light_direction || (variant == RDVB_PBVRT && !light_intensity))
+        return fail(RDVB_ERR_INVALID_ARG, "albedo, light_direction and (PBVRT) light_intensity must not be NULL");
+    if (max_bounces < 0) return fail(RDVB_ERR_INVALID_ARG, "max_bounces must be >= 0, got %d", max_bounces);
+    if (!std::isfinite(g) || !std::isfinite(density_scale))
+        return fail(RDVB_ERR_INVALID_ARG, "g and density_scale must be finite");
+    rdvb::pbvr::ExtraT e;
+    memset(&e, 0, sizeof(e));
+    for (int k = 0; k < 3; ++k) e.albedo[k] = albedo[k];
+    e.g = g;
+    e.density_scale = density_scale;
+    e.max_bounces = max_bounces;
+    e.variant = variant == RDVB_PBVRT ? 0 : 1;
+    // normalize(light_direction) = l / length(l), length = sqrt((x x + y y) + z z)
+    const float l0 = light_direction[0], l1 = light_direction[1], l2 = light_direction[2];
+    const float sq = (l0 * l0 + l1 * l1) + l2 * l2;
+    const float len = std::sqrt(sq);
+    if (!(len > 0.0f) || !std::isfinite(len)) return fail(RDVB_ERR_INVALID_ARG, "light_direction must be a finite nonzero vector");
+    e.light[0] = l0 / len;
+    e.light[1] = l1 / len;
+    e.light[2] = l2 / len;
+    for (int k = 0; k < 3; ++k) e.intensity[k] = variant == RDVB_PBVRT ? light_intensity[k] : 0.0f;
+    if (variant == RDVB_PBVRT) {
+        if (int rc = environment_args(env_kind, env_rgb, env_image, env_dims, env_flags, n_rays, e.env)) return rc;
+    }
+    if (n_rays == 0) return RDVB_OK;
+    e.env.out = out;
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    return launch_simt_march(p, n_layers, dims, weights, biases, layer_flags, workspace, dev,
+                             static_cast<cudaStream_t>(stream), March::kPbvrt, &e);
+}
+
 
 namespace {
 int camera_rays(const float* poses, int n_cameras, int width, int height, float aspect, float fov, int jitter,

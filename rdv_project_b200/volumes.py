@@ -313,3 +313,119 @@ class PBVR(RaymarchingTransmittance):
                 N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
                 stream_handle()), "rdvb_pbvr")
         return RDVObject(out)
+
+
+def _albedo_of(scattering_albedo):
+    """The 3 values of a uniform scattering albedo: a Constant[3, 3] map (the
+    form this library evaluates), or 3 numbers."""
+    if isinstance(scattering_albedo, Constant):
+        assert scattering_albedo.OUT == 3, "the scattering albedo must hold 3 values (RGB)"
+        return tuple(float(v) for v in scattering_albedo.data.tolist())
+    if isinstance(scattering_albedo, Map):
+        raise NotImplementedError("the scattering albedo must be a Constant (a spatially uniform albedo)")
+    a = torch.as_tensor(scattering_albedo, dtype=torch.float32).reshape(-1)
+    assert a.numel() == 3, "the scattering albedo must hold 3 values (RGB)"
+    return tuple(float(v) for v in a)
+
+
+class _PBVRLight(RaymarchingTransmittance):
+    """Shared part of PBVRT and PBVR_NEE (rdvb_pbvrt)."""
+
+    _draws_random = True
+    _variant = None
+
+    def __init__(self, extinction, majorant, scattering_albedo, transform, light_direction, density_scale, g,
+                 max_bounces, environment=None, light_intensity=None):
+        super().__init__(extinction, transform=transform, density_scale=density_scale)
+        del self.step_size
+        self.majorant = _as_majorant_field(majorant)
+        self.albedo = _albedo_of(scattering_albedo)
+        ld = torch.as_tensor(light_direction, dtype=torch.float32).reshape(-1)
+        assert ld.numel() == 3, "light_direction must hold 3 values"
+        self.light_direction = tuple(float(v) for v in ld)
+        self.light_intensity = (1.0, 1.0, 1.0) if light_intensity is None else \
+            tuple(float(v) for v in torch.as_tensor(light_intensity, dtype=torch.float32).reshape(-1))
+        assert len(self.light_intensity) == 3, "light_intensity must hold 3 values"
+        self.environment = environment
+        if environment is not None:
+            env = environment._bind(in_size=3, out_size=3) if environment.__is_generic__ else environment
+            assert env.IN == 3 and env.OUT == 3, "environment must be a Map[3, 3]"
+            self.environment = env
+        self.g = float(g)
+        self.max_bounces = int(max_bounces)
+        self.last_seeds = None
+
+    def __call__(self, rays, seeds=None, draws_before: int = 0):
+        dev = current_device()
+        rt = rays._tensor if isinstance(rays, RDVObject) else wrap(rays)._tensor
+        assert rt.shape[-1] == 6, f"input's last dimension ({rt.shape[-1]}) must match the map's IN (6)"
+        lead = list(rt.shape[:-1])
+        r2 = rt.reshape(-1, 6)
+        if r2.device != dev or r2.dtype != torch.float32 or not r2.is_contiguous():
+            r2 = r2.to(device=dev, dtype=torch.float32).contiguous()
+        out = torch.empty(lead + [self.OUT], dtype=torch.float32, device=dev)
+        st = self._device_state(dev)
+        g, gdims, kind = _field_args(self.majorant, dev)
+        if self.environment is not None:
+            env_kind, env_rgb, env_img, env_dims, env_flags = _environment_args(self.environment, dev)
+        else:
+            env_kind, env_rgb, env_img, env_dims, env_flags = N.RDVB_ENV_CONSTANT, [0.0, 0.0, 0.0], None, [0, 0], 0
+        seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
+        assert len(seeds) == 4, "seeds must be 4 integers"
+        self.last_seeds = seeds
+        if st["ws"] is None:
+            st["ws"] = torch.empty(256, dtype=torch.uint8, device=dev)
+        n = len(st["layers"])
+        with _timed():
+            N.check(N.lib().rdvb_pbvrt(
+                r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.density_scale, g.data_ptr(),
+                N.int_array(gdims), kind, N.float_array(self.albedo), self.g, self.max_bounces,
+                N.float_array(self.light_direction), N.float_array(self.light_intensity), self._variant, env_kind,
+                N.float_array(env_rgb), env_img.data_ptr() if env_img is not None else None, N.int_array(env_dims),
+                env_flags, N.uint32_array(seeds), int(draws_before), n, N.int_array(st["dims"]),
+                N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
+                N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
+                stream_handle()), "rdvb_pbvrt")
+        return RDVObject(out)
+
+
+class PBVRT(_PBVRLight):
+    """Map[6, 4]: ray -> one sample of (RGB radiance, alpha) by delta
+    tracking with next-event estimation toward a directional light
+    (rdv/domain/volumes.py:326-387, rdv/shaders/volumes/pbvrt.h). alpha is 1
+    while the ray has not scattered (fully background, for compositing over
+    a backdrop rendered elsewhere), 0 once it has; then RGB is the NEE sum
+    times ``light_intensity`` plus the throughput times ``environment`` in
+    the escape direction. ``extinction`` a Map[3, 1] chain, ``majorant`` a
+    voxel or sphere majorant field (or a bare Grid[3, 1]), ``environment``
+    a Map[3, 3] (``Constant`` or ``XRProject() >> TensorSampler(image)``),
+    ``scattering_albedo`` a ``Constant`` of 3 values (or 3 numbers),
+    ``light_direction`` normalized here, ``density_scale`` scales the
+    extinction and the majorant, ``g`` the Henyey-Greenstein anisotropy,
+    ``max_bounces`` the real scattering events (rdvb_pbvrt)."""
+
+    OUT = 4
+    _variant = N.RDVB_PBVRT
+
+    def __init__(self, extinction: Map, majorant, environment: Map, scattering_albedo, transform=None,
+                 light_direction=(0.0, 1.0, 0.0), light_intensity=None, density_scale: float = 1.0, g: float = 0.0,
+                 max_bounces: int = 32) -> None:
+        super().__init__(extinction, majorant, scattering_albedo, transform, light_direction, density_scale, g,
+                         max_bounces, environment=environment, light_intensity=light_intensity)
+
+
+class PBVR_NEE(_PBVRLight):
+    """Map[6, 3]: ray -> the next-event-estimation part of delta tracking
+    toward a directional light (rdv/domain/volumes.py:390-442,
+    rdv/shaders/volumes/pbvr_nee.h): the sum over real collisions of
+    throughput * shadow transmittance * phase; no environment, no light
+    intensity, no alpha. Arguments as PBVRT (rdvb_pbvrt)."""
+
+    OUT = 3
+    _variant = N.RDVB_PBVR_NEE
+
+    def __init__(self, extinction: Map, majorant, scattering_albedo, transform=None,
+                 light_direction=(0.0, 1.0, 0.0), density_scale: float = 1.0, g: float = 0.0,
+                 max_bounces: int = 32) -> None:
+        super().__init__(extinction, majorant, scattering_albedo, transform, light_direction, density_scale, g,
+                         max_bounces)

@@ -279,7 +279,8 @@ def coopmat_goldens():
 
 
 def pbvr_goldens():
-    """pbvr.npz: PBVR.forward of the reference (volumes/pbvr.h) over world
+    """pbvr.npz: PBVR.forward of the reference (volumes/pbvr.h), and
+    PBVRT / PBVR_NEE (volumes/pbvrt.h, pbvr_nee.h) as t_*, over world
     rays [n, 6] with the analytic extinction c0 + c1 |x|^2, a constant
     environment, a voxel and a sphere majorant field, several albedos,
     anisotropies and bounce budgets, an identity and a scaled + shifted
@@ -330,10 +331,30 @@ def pbvr_goldens():
         for i in range(24):
             lib.ref_hg_phase_sample(ptr(seeds), int(hg_index[i]), 3, ptr(np.ascontiguousarray(hg_w[i])),
                                     ctypes.c_float(g), ptr(hg_out[a, i]))
+    # PBVRT (variant 0, [n, 4]) and PBVR_NEE (variant 1, [n, 3]) on the same
+    # rays, fields and media: (variant, field kind, g, albedo, max bounces,
+    # density scale, transform)
+    light_dir = np.array([0.3, 1.0, -0.2], np.float32)
+    light_int = np.array([2.0, 1.5, 1.0], np.float32)
+    t_cases = [(0, 0, 0.0, (0.9, 0.8, 0.7), 32, 1.0, 0), (0, 1, 0.6, (0.95, 0.9, 0.99), 3, 0.5, 1),
+               (0, 0, -0.4, (1, 1, 1), 0, 2.0, 0), (1, 1, 0.0, (0.9, 0.8, 0.7), 32, 1.0, 0),
+               (1, 0, 0.3, (0.8, 0.8, 0.8), 6, 1.5, 1)]
+    t_out = np.zeros((len(t_cases), n, 4), np.float32)
+    for k, (var, kind, g, alb, mb, dsc, ti) in enumerate(t_cases):
+        grid = vox if kind == 0 else sph
+        dst = np.zeros((n, 4 if var == 0 else 3), np.float32)
+        lib.ref_pbvrt(int(var), ctypes.c_float(c0), ctypes.c_float(c1), int(kind), ptr(grid), D, H, W, ptr(env),
+                      ptr(np.ascontiguousarray([identity, scaled][ti])), ptr(np.array(alb, np.float32)),
+                      ptr(light_dir), ptr(light_int), ctypes.c_float(g), ctypes.c_float(dsc), int(mb), ptr(seeds),
+                      ptr(rays), n, ptr(dst))
+        t_out[k, :, :dst.shape[1]] = dst
+    t_params = np.array([[c[0], c[1], c[2], c[4], c[5], c[6]] for c in t_cases], np.float32)
+    t_albedo = np.array([c[3] for c in t_cases], np.float32)
     np.savez_compressed(os.path.join(HERE, "pbvr.npz"), rays=rays, seeds=seeds, c0=c0, c1=c1, vox=vox, sph=sph,
                         env=env, kinds=kinds, g=gs, albedo=albedos, max_bounces=bounces, transforms=transforms,
                         out=out, hg_g=hg_g, hg_w=hg_w, hg_index=hg_index, hg_draws_before=np.int32(3),
-                        hg_out=hg_out)
+                        hg_out=hg_out, t_params=t_params, t_albedo=t_albedo, t_transforms=np.stack([identity, scaled]),
+                        t_light_dir=light_dir, t_light_int=light_int, t_out=t_out)
 
 
 GRID_CASES = ((1, 3, (7,)), (2, 3, (5, 9)), (3, 3, (4, 5, 6)), (4, 3, (3, 4, 2, 5)), (3, 5, (2, 3, 1)))

@@ -230,3 +230,22 @@ def test_grid_sampler_validation(lib):
     assert lib.rdvb_grid_sampler(None, 3, shape, 0, None, 4, 1, 0, 1, None, None) == -1
     assert lib.rdvb_grid_sampler(None, 3, shape, 2, None, 4, 1, 0, 1, None, None) == -1
     assert "must not be NULL" in N.last_error()
+
+
+def test_pbvrt_validation(lib):
+    import rdv_project_b200._native as N
+
+    def call(n=0, variant=0, albedo=(1, 1, 1), light=(0, 1, 0), intensity=(1, 1, 1), g=0.0, mb=4, scale=1.0):
+        return lib.rdvb_pbvrt(None, n, None, scale, None, N.int_array([2, 2, 2]), 0,
+                              N.float_array(albedo) if albedo else None, g, mb,
+                              N.float_array(light) if light else None, N.float_array(intensity) if intensity else None,
+                              variant, 0, N.float_array([1, 1, 1]), None, N.int_array([1, 1]), 0,
+                              N.uint32_array([1, 2, 3, 4]), 0, 2, N.int_array([3, 16, 1]), N.ptr_array([1, 1]),
+                              N.ptr_array([1, 1]), N.int_array([1, 1]), 0, None, 256, None, None)
+
+    assert call() == 0
+    assert call(variant=N.RDVB_PBVR_NEE, intensity=None) == 0     # NEE reads no light intensity
+    for kw, msg in ((dict(variant=2), "variant"), (dict(albedo=None), "albedo"), (dict(light=None), "light"),
+                    (dict(intensity=None), "light_intensity"), (dict(mb=-1), "max_bounces"),
+                    (dict(scale=float("inf")), "finite"), (dict(light=(0, 0, 0)), "nonzero")):
+        assert call(**kw) == -1 and msg in N.last_error(), (kw, N.last_error())

@@ -57,11 +57,17 @@ def _env_image(seed=3, h=8, w=16):
 
 
 def _agree(got, ref, frac=0.98):
-    d = np.abs(np.asarray(got, np.float64) - np.asarray(ref, np.float64))
-    tol = 2e-5 + 1e-4 * np.abs(np.asarray(ref, np.float64))
+    """Ray-by-ray agreement on at least `frac` of the rays, and means within
+    5 standard errors of the per-ray spread (the rays that part are
+    independent samples of the same estimator)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.abs(got - ref)
+    tol = 2e-5 + 1e-4 * np.abs(ref)
     close = float(np.mean(np.all(d <= tol, axis=1)))
     assert close >= frac, (close, np.nonzero(~np.all(d <= tol, axis=1))[0][:8])
-    assert np.abs(got.mean(axis=0) - ref.mean(axis=0)).max() <= 5e-3
+    sem = ref.std(axis=0) / np.sqrt(ref.shape[0])
+    assert np.all(np.abs(got.mean(axis=0) - ref.mean(axis=0)) <= 5 * sem + 1e-6), (got.mean(0), ref.mean(0), sem)
     return close
 
 
@@ -263,4 +269,107 @@ def test_empty_and_jittered_camera_composition(rdv, cuda_device):
                    lambda x, ww: orm.voxel_majorant(vox[..., 0], x, ww), SEEDS, albedo=(0.7, 0.8, 0.9), g=0.2,
                    draws_before=2)
     _agree(img.reshape(-1, 3), ref)
+    assert rdv.device_status() == 0
+
+
+# ------------------------------------------------------------ PBVRT, PBVR_NEE
+LIGHT = (0.3, 1.0, -0.2)
+
+
+@pytest.mark.parametrize("variant,math_,field,g,bounces,scale", [
+    ("pbvrt", "f32", "voxel", 0.0, 32, 1.0),
+    ("pbvrt", "f16", "sphere", 0.6, 4, 0.5),
+    ("nee", "f16", "voxel", -0.3, 8, 1.5),
+    ("nee", "bf16", "sphere", 0.0, 32, 1.0),
+])
+def test_pbvrt_and_nee_match_oracle(rdv, cuda_device, variant, math_, field, g, bounces, scale):
+    n = 4000
+    layers = _layers([3, 32, 1] if math_ != "f16" else [3, 64, 64, 1], math_, seed=bounces * 3 + len(variant))
+    vox = _majorant(layers, (4, 3, 5))
+    rays = _rays(n, seed=n + bounces)
+    if field == "voxel":
+        fld = rdv.VoxelMajorantField(torch.from_numpy(vox).to(cuda_device))
+        maj = lambda x, w: orm.voxel_majorant(vox[..., 0], x, w)  # noqa: E731
+    else:
+        sph = _sphere_grid(vox)
+        fld = rdv.SphereMajorantField(torch.from_numpy(sph).to(cuda_device))
+        maj = lambda x, w: orm.sphere_majorant(sph, x, w)  # noqa: E731
+    albedo = (0.9, 0.8, 0.7)
+    rgb = np.array([0.3, 0.6, 0.9], np.float32)
+    chain = _chain(rdv, layers, cuda_device)
+    if variant == "pbvrt":
+        node = rdv.PBVRT(chain, fld, rdv.Constant(rgb), rdv.Constant(albedo), light_direction=LIGHT,
+                         light_intensity=(2.0, 1.5, 1.0), density_scale=scale, g=g, max_bounces=bounces)
+    else:
+        node = rdv.PBVR_NEE(chain, fld, rdv.Constant(albedo), light_direction=LIGHT, density_scale=scale, g=g,
+                            max_bounces=bounces)
+    got = node(torch.from_numpy(rays).to(cuda_device), seeds=SEEDS).as_tensor("torch")
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    ref, evals = orm.pbvrt(rays[:, :3], rays[:, 3:], _extinction(layers), maj, SEEDS, albedo, LIGHT, (2.0, 1.5, 1.0),
+                           orm.constant_environment(rgb), density_scale=scale, g=g, max_bounces=bounces,
+                           variant=variant, return_evaluations=True)
+    assert got.shape == ref.shape == (n, 4 if variant == "pbvrt" else 3)
+    # paths here are long (each real collision adds a ratio-tracking shadow
+    # ray) and Henyey-Greenstein sampling with g != 0 magnifies last-bit
+    # differences of the transcendentals: measured 2.2 % of rays parting
+    # with 32 bounces (g = 0), 5.8-6.5 % with the denser 64-wide medium and
+    # g = -0.3 (float16 and exact chains alike), the means within a tenth of
+    # their standard error, every alpha equal
+    _agree(got[:, :3], ref[:, :3], frac=0.9)
+    miss = _miss_mask(rays)
+    assert np.all(got[miss, :3] == 0)
+    if variant == "pbvrt":
+        assert np.mean(got[:, 3] == ref[:, 3]) >= 0.99
+        assert np.all(got[miss, 3] == 1.0) and (got[:, 3] == 0).any()
+    assert (ref[~miss, :3].sum(1) > 0).any()
+    assert abs(node.last_evaluations() - evals) <= max(50, 0.03 * evals), (node.last_evaluations(), evals)
+    assert rdv.device_status() == 0
+
+
+def test_pbvrt_alpha_is_an_unbiased_transmittance(rdv, cuda_device):
+    """PBVRT's alpha is 1 exactly when the path leaves the box without a real
+    collision, so its mean is the transmittance along the ray: the
+    fixed-step march's value for the same medium and density scale (both
+    fields)."""
+    layers = _layers([3, 32, 1], "f32", seed=21, out_bias=0.3)
+    ext = _chain(rdv, layers, cuda_device)
+    vox = _majorant(layers, (3, 3, 3), margin=2.0)
+    sph = _sphere_grid(vox, seed=8)
+    base = _rays(64, seed=3)[16:]
+    reps = 4096
+    rays = torch.from_numpy(np.repeat(base, reps, axis=0)).to(cuda_device)
+    rm = rdv.RaymarchingTransmittance(ext, step_size=0.001, density_scale=1.3)
+    T = rm(torch.from_numpy(base).to(cuda_device)).as_tensor("torch").cpu().numpy()[:, 0]
+    for fld in (rdv.VoxelMajorantField(torch.from_numpy(vox).to(cuda_device)),
+                rdv.SphereMajorantField(torch.from_numpy(sph).to(cuda_device))):
+        node = rdv.PBVRT(ext, fld, rdv.Constant([0.5, 0.5, 0.5]), rdv.Constant([0.8, 0.8, 0.8]), density_scale=1.3,
+                         g=0.2, max_bounces=4)
+        alpha = node(rays, seeds=SEEDS).as_tensor("torch").cpu().numpy()[:, 3].reshape(-1, reps)
+        mean = alpha.mean(axis=1)
+        sem = alpha.std(axis=1) / np.sqrt(reps)
+        z = (mean - T) / np.maximum(sem, 1e-4)
+        assert np.all(np.abs(z) < 5.0), z
+        assert np.abs(z).mean() < 1.5
+    assert rdv.device_status() == 0
+
+
+def test_nee_jittered_camera_composition(rdv, cuda_device):
+    layers = _layers([3, 32, 1], "f32", seed=31)
+    vox = _majorant(layers, (2, 2, 2))
+    node = rdv.PBVR_NEE(_chain(rdv, layers, cuda_device), torch.from_numpy(vox).to(cuda_device),
+                        (0.7, 0.8, 0.9), light_direction=LIGHT, g=0.2)
+    pose = orm.orbit_pose(1)
+    cams = rdv.Cameras(40, 30, torch.from_numpy(pose[None]), jitter=True)
+    img = (cams >> node)(seeds=SEEDS).as_tensor("torch").cpu().numpy()
+    assert img.shape == (1, 30, 40, 3)
+    # the oracle follows the camera's own rays (the jittered camera itself is
+    # checked against the oracle in test_gpu_ratiotracking.py), each ray's
+    # generator two draws in
+    r = cams(seeds=SEEDS).as_tensor("torch").cpu().numpy().reshape(-1, 6)
+    ref = orm.pbvrt(r[:, :3], r[:, 3:], _extinction(layers), lambda x, ww: orm.voxel_majorant(vox[..., 0], x, ww),
+                    SEEDS, (0.7, 0.8, 0.9), LIGHT, g=0.2, variant="nee", draws_before=2)
+    _agree(img.reshape(-1, 3), ref, frac=0.9)
+    empty = node(torch.zeros(0, 6, device=cuda_device)).as_tensor("torch")
+    assert tuple(empty.shape) == (0, 3)
     assert rdv.device_status() == 0
