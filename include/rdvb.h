@@ -59,6 +59,23 @@ extern "C" {
 #define RDVB_SAMPLER_ALIGNED 2
 #define RDVB_SAMPLER_LINEAR 4
 
+/* Input encoding of a volume node's extinction: a sampler of a dense 3-D
+ * grid in front of the chain (GridSampler / TensorSampler >> Linear ...,
+ * rdv/maths/__init__.py:2018-2083), evaluated per extinction query on the
+ * CUDA cores. grid: device fp32 [dims[0], dims[1], dims[2], features]
+ * (z, y, x, channel); flags: RDVB_SAMPLER_* (clamp, aligned, linear). With an
+ * encoding the chain maps features -> 1 (dims[0] = features), or is empty
+ * (n_layers 0, features 1: the sampled value is the extinction). */
+#define RDVB_ENCODING_TENSOR_SAMPLER 1
+#define RDVB_ENCODING_GRID_SAMPLER 2
+typedef struct rdvb_encoding {
+    int kind;
+    const float* grid;
+    int dims[3];
+    int features;
+    int flags;
+} rdvb_encoding;
+
 /* rdvb_pbvrt variants */
 #define RDVB_PBVRT 0    /* PBVRT: RGB + alpha, the environment after scattering */
 #define RDVB_PBVR_NEE 1 /* PBVR_NEE: RGB, next-event estimation only */
@@ -373,9 +390,12 @@ int64_t rdvb_transmittance_workspace_bytes(int64_t n_rays, int n_layers, const i
  * ray per CUDA thread exactly like the reference's loop; float16 / bfloat16
  * chains evaluate every step of a ray in 128-step chunks on the tensor cores
  * (fused MLP kernel) and combine the chunks in step order -- same result,
- * steps past an early exit are evaluated too. */
+ * steps past an early exit are evaluated too. encoding: NULL, or a sampler
+ * in front of the chain (rdvb_encoding; then every chain runs on the CUDA
+ * cores). */
 int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transform, float step_size,
-                          float density_scale, int n_layers, const int* dims, const float* const* weights,
+                          float density_scale, const rdvb_encoding* encoding, int n_layers, const int* dims,
+                          const float* const* weights,
                           const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
                           size_t workspace_bytes, float* out, void* stream);
 
@@ -411,9 +431,9 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
  * evaluations of the call. */
 int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
                           const float* majorant, const int* majorant_dims, int majorant_kind, const uint32_t* seeds,
-                          int draws_before, int n_layers, const int* dims, const float* const* weights,
-                          const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
-                          size_t workspace_bytes, float* out, void* stream);
+                          int draws_before, const rdvb_encoding* encoding, int n_layers, const int* dims,
+                          const float* const* weights, const float* const* biases, const int* layer_flags,
+                          int input_relu, void* workspace, size_t workspace_bytes, float* out, void* stream);
 
 /* XRProject (rdv/domain/rendering.py:150-160, rdv/shaders/rendering/
  * xr_project.h): out[i] = dir2xr(dirs[i]) = (atan(w.x, w.z) / pi,
@@ -448,9 +468,9 @@ int rdvb_xr_project(const float* dirs, int64_t n, float* out, void* stream);
 int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const float* majorant,
               const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
               int env_kind, const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
-              const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
-              const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
-              size_t workspace_bytes, float* out, void* stream);
+              const uint32_t* seeds, int draws_before, const rdvb_encoding* encoding, int n_layers, const int* dims,
+              const float* const* weights, const float* const* biases, const int* layer_flags, int input_relu,
+              void* workspace, size_t workspace_bytes, float* out, void* stream);
 
 /* PBVRT and PBVR_NEE (rdv/domain/volumes.py:326-442,
  * rdv/shaders/volumes/pbvrt.h, pbvr_nee.h): delta tracking with
@@ -478,9 +498,9 @@ int rdvb_pbvrt(const float* rays, int64_t n_rays, const float* transform, float 
                const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
                const float* light_direction, const float* light_intensity, int variant, int env_kind,
                const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
-               const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
-               const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
-               size_t workspace_bytes, float* out, void* stream);
+               const uint32_t* seeds, int draws_before, const rdvb_encoding* encoding, int n_layers,
+               const int* dims, const float* const* weights, const float* const* biases, const int* layer_flags,
+               int input_relu, void* workspace, size_t workspace_bytes, float* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -25,6 +25,7 @@ RDVB_MAJORANT_VOXEL, RDVB_MAJORANT_SPHERE = 0, 1
 RDVB_ENV_CONSTANT, RDVB_ENV_EQUIRECT = 0, 1
 RDVB_SAMPLER_CLAMP, RDVB_SAMPLER_ALIGNED, RDVB_SAMPLER_LINEAR = 1, 2, 4
 RDVB_PBVRT, RDVB_PBVR_NEE = 0, 1
+RDVB_ENCODING_TENSOR_SAMPLER, RDVB_ENCODING_GRID_SAMPLER = 1, 2
 
 _c_int, _c_i64, _vp, _c_u32, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float
 
@@ -65,18 +66,24 @@ SIGNATURES = {
     "rdvb_raymarch_render": (_c_int, [_vp, _c_int, _c_int, _c_f, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int, _c_int,
                                       _vp, ctypes.c_size_t, _vp, _vp]),
     "rdvb_transmittance_workspace_bytes": (_c_i64, [_c_i64, _c_int, _vp, _vp]),
-    "rdvb_transmittance_rm": (_c_int, [_vp, _c_i64, _vp, _c_f, _c_f, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
+    "rdvb_transmittance_rm": (_c_int, [_vp, _c_i64, _vp, _c_f, _c_f, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
                                        ctypes.c_size_t, _vp, _vp]),
-    "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp,
-                                       _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
+    "rdvb_transmittance_rt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _c_int, _vp, _c_int, _vp, _c_int, _vp, _vp,
+                                       _vp, _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
     "rdvb_xr_project": (_c_int, [_vp, _c_i64, _vp, _vp]),
     "rdvb_pbvrt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _c_int, _vp, _c_f, _c_int, _vp, _vp, _c_int, _c_int,
-                            _vp, _vp, _vp, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
+                            _vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
                             ctypes.c_size_t, _vp, _vp]),
     "rdvb_grid_sampler": (_c_int, [_vp, _c_int, _vp, _c_int, _vp, _c_i64, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_pbvr": (_c_int, [_vp, _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int,
-                           _vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
+                           _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
 }
+
+
+class Encoding(ctypes.Structure):
+    """rdvb_encoding: a sampler of a dense 3-D grid in front of a volume
+    node's extinction chain."""
+    _fields_ = [("kind", _c_int), ("grid", _vp), ("dims", _c_int * 3), ("features", _c_int), ("flags", _c_int)]
 
 
 class RdvbError(RuntimeError):

@@ -1407,6 +1407,64 @@ int trm_object_space(const float* transform, rdvb::trm::Params& p) {
     return RDVB_OK;
 }
 
+// The extinction of a volume node: an optional input encoding (a sampler of
+// a dense 3-D grid) and a chain of n_layers layers mapping 3 (or the
+// encoding's features) to 1. Sets maxw, the widest activation column.
+int check_extinction(const rdvb_encoding* enc, int n_layers, const int* dims, const float* const* weights,
+                     const float* const* biases, const int* layer_flags, int& maxw) {
+    using rdvb::trm::kMaxLayers;
+    using rdvb::trm::kMaxWidth;
+    const int min_layers = enc ? 0 : 1;
+    if (n_layers < min_layers || n_layers > kMaxLayers)
+        return fail(RDVB_ERR_INVALID_ARG, "n_layers must be in [%d, %d], got %d", min_layers, kMaxLayers, n_layers);
+    if (!dims) return fail(RDVB_ERR_INVALID_ARG, "dims must not be NULL");
+    int in = 3;
+    if (enc) {
+        if (enc->kind != RDVB_ENCODING_TENSOR_SAMPLER && enc->kind != RDVB_ENCODING_GRID_SAMPLER)
+            return fail(RDVB_ERR_INVALID_ARG, "encoding kind must be RDVB_ENCODING_TENSOR_SAMPLER or "
+                                              "RDVB_ENCODING_GRID_SAMPLER, got %d", enc->kind);
+        if (!enc->grid || !aligned(enc->grid, 4))
+            return fail(RDVB_ERR_INVALID_ARG, "the encoding grid must be a 4-byte aligned device pointer");
+        long long cells = 1;
+        for (int k = 0; k < 3; ++k) {
+            if (enc->dims[k] < 1)
+                return fail(RDVB_ERR_INVALID_ARG, "encoding dims must be positive, got %d", enc->dims[k]);
+            cells *= enc->dims[k];
+        }
+        if (enc->features < 1 || enc->features > kMaxWidth)
+            return fail(RDVB_ERR_UNSUPPORTED, "encoding features must be in [1, %d], got %d", kMaxWidth, enc->features);
+        if (cells * enc->features > (1LL << 40)) return fail(RDVB_ERR_UNSUPPORTED, "encoding grid too large");
+        if (enc->flags & ~(RDVB_SAMPLER_CLAMP | RDVB_SAMPLER_ALIGNED | RDVB_SAMPLER_LINEAR))
+            return fail(RDVB_ERR_INVALID_ARG, "unknown encoding flag bits 0x%x", enc->flags);
+        in = enc->features;
+    }
+    if (n_layers > 0) {
+        if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
+        if (!weights || !biases) return fail(RDVB_ERR_INVALID_ARG, "weights and biases must not be NULL");
+        for (int l = 0; l < n_layers; ++l)
+            if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "layer %d has a NULL weight or bias", l);
+    }
+    if (dims[0] != in || dims[n_layers] != 1)
+        return fail(RDVB_ERR_INVALID_ARG, "the extinction must map %d -> 1, got %d -> %d", in, dims[0], dims[n_layers]);
+    maxw = 3;
+    for (int l = 0; l <= n_layers; ++l) {
+        if (dims[l] > kMaxWidth) return fail(RDVB_ERR_UNSUPPORTED, "widths must be <= %d, got %d", kMaxWidth, dims[l]);
+        maxw = std::max(maxw, dims[l]);
+    }
+    return RDVB_OK;
+}
+
+void fill_encoding(const rdvb_encoding* enc, rdvb::trm::Params& p) {
+    if (!enc) return;
+    p.enc = enc->kind == RDVB_ENCODING_TENSOR_SAMPLER ? 1 : 2;
+    p.enc_t = enc->grid;
+    for (int k = 0; k < 3; ++k) p.enc_dim[k] = enc->dims[k];
+    p.enc_out = enc->features;
+    p.enc_clamp = (enc->flags & RDVB_SAMPLER_CLAMP) ? 1 : 0;
+    p.enc_aligned = (enc->flags & RDVB_SAMPLER_ALIGNED) ? 1 : 0;
+    p.enc_linear = (enc->flags & RDVB_SAMPLER_LINEAR) ? 1 : 0;
+}
+
 // The CUDA-core march kernels: the chain's shared-memory weight image, then
 // one launch of as many persistent 128-thread CTAs as fit (rays handed out
 // by the counter at the start of the workspace).
@@ -1510,31 +1568,20 @@ int64_t rdvb_transmittance_workspace_bytes(int64_t n_rays, int n_layers, const i
 }
 
 int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transform, float step_size,
-                          float density_scale, int n_layers, const int* dims, const float* const* weights,
-                          const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
-                          size_t workspace_bytes, float* out, void* stream) {
+                          float density_scale, const rdvb_encoding* encoding, int n_layers, const int* dims,
+                          const float* const* weights, const float* const* biases, const int* layer_flags,
+                          int input_relu, void* workspace, size_t workspace_bytes, float* out, void* stream) {
     using namespace rdvb::trm;
     if (n_rays < 0) return fail(RDVB_ERR_INVALID_ARG, "n_rays must be >= 0");
-    if (n_layers < 1 || n_layers > kMaxLayers)
-        return fail(RDVB_ERR_INVALID_ARG, "n_layers must be in [1, %d], got %d", kMaxLayers, n_layers);
-    if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
-    if (dims[0] != 3 || dims[n_layers] != 1)
-        return fail(RDVB_ERR_INVALID_ARG, "the extinction must map 3 -> 1, got %d -> %d", dims[0], dims[n_layers]);
-    if (!weights || !biases) return fail(RDVB_ERR_INVALID_ARG, "weights and biases must not be NULL");
     int maxw = 3;
-    for (int l = 0; l <= n_layers; ++l) {
-        if (dims[l] > kMaxWidth) return fail(RDVB_ERR_UNSUPPORTED, "widths must be <= %d, got %d", kMaxWidth, dims[l]);
-        maxw = std::max(maxw, dims[l]);
-    }
-    for (int l = 0; l < n_layers; ++l)
-        if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "layer %d has a NULL weight or bias", l);
+    if (int rc = check_extinction(encoding, n_layers, dims, weights, biases, layer_flags, maxw)) return rc;
     if (!(step_size > 0.0f)) return fail(RDVB_ERR_INVALID_ARG, "step_size must be > 0");
     if (n_rays > 0x7fffffffLL - (1LL << 24))
         return fail(RDVB_ERR_UNSUPPORTED, "at most %lld rays per call", 0x7fffffffLL - (1LL << 24));
     if (n_rays == 0) return RDVB_OK;
     if (!rays || !out) return fail(RDVB_ERR_INVALID_ARG, "rays and out must not be NULL");
     if (!aligned(rays, 4) || !aligned(out, 4)) return fail(RDVB_ERR_INVALID_ARG, "rays and out must be 4-byte aligned");
-    const bool tc = march_on_tensor_cores(n_layers, dims, layer_flags);
+    const bool tc = !encoding && march_on_tensor_cores(n_layers, dims, layer_flags);
     const int64_t need = tc ? march_workspace(n_rays, n_layers, dims).total : 256;
     if (!workspace || !aligned(workspace, 256) || static_cast<int64_t>(workspace_bytes) < need)
         return fail(RDVB_ERR_INVALID_ARG, "workspace must be 256-byte aligned and hold %lld bytes", (long long)need);
@@ -1554,6 +1601,7 @@ int rdvb_transmittance_rm(const float* rays, int64_t n_rays, const float* transf
     p.n_layers = n_layers;
     p.input_relu = input_relu ? 1 : 0;
     p.maxw = maxw;
+    fill_encoding(encoding, p);
     if (int rc = trm_object_space(transform, p)) return rc;
     if (tc) {
         // tensor-core march: pack the chain into the workspace, then per
@@ -1639,26 +1687,15 @@ namespace {
 // Fills p (all but the launch state) and reports whether there is any work.
 int tracking_params(const float* rays, int64_t n_rays, const float* transform, const float* majorant,
                     const int* majorant_dims, int majorant_kind, const uint32_t* seeds, int draws_before,
-                    int n_layers, const int* dims, const float* const* weights, const float* const* biases,
-                    const int* layer_flags, int input_relu, void* workspace, size_t workspace_bytes, void* out,
-                    rdvb::trm::Params& p, int out_dim) {
+                    const rdvb_encoding* encoding, int n_layers, const int* dims, const float* const* weights,
+                    const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+                    size_t workspace_bytes, void* out, rdvb::trm::Params& p, int out_dim) {
     using namespace rdvb::trm;
     if (draws_before < 0 || draws_before > 64)
         return fail(RDVB_ERR_INVALID_ARG, "draws_before must be in [0, 64], got %d", draws_before);
     if (n_rays < 0) return fail(RDVB_ERR_INVALID_ARG, "n_rays must be >= 0");
-    if (n_layers < 1 || n_layers > kMaxLayers)
-        return fail(RDVB_ERR_INVALID_ARG, "n_layers must be in [1, %d], got %d", kMaxLayers, n_layers);
-    if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;
-    if (dims[0] != 3 || dims[n_layers] != 1)
-        return fail(RDVB_ERR_INVALID_ARG, "the extinction must map 3 -> 1, got %d -> %d", dims[0], dims[n_layers]);
-    if (!weights || !biases) return fail(RDVB_ERR_INVALID_ARG, "weights and biases must not be NULL");
     int maxw = 3;
-    for (int l = 0; l <= n_layers; ++l) {
-        if (dims[l] > kMaxWidth) return fail(RDVB_ERR_UNSUPPORTED, "widths must be <= %d, got %d", kMaxWidth, dims[l]);
-        maxw = std::max(maxw, dims[l]);
-    }
-    for (int l = 0; l < n_layers; ++l)
-        if (!weights[l] || !biases[l]) return fail(RDVB_ERR_INVALID_ARG, "layer %d has a NULL weight or bias", l);
+    if (int rc = check_extinction(encoding, n_layers, dims, weights, biases, layer_flags, maxw)) return rc;
     if (majorant_kind != RDVB_MAJORANT_VOXEL && majorant_kind != RDVB_MAJORANT_SPHERE)
         return fail(RDVB_ERR_INVALID_ARG, "majorant_kind must be RDVB_MAJORANT_VOXEL or RDVB_MAJORANT_SPHERE, got %d",
                     majorant_kind);
@@ -1695,6 +1732,7 @@ int tracking_params(const float* rays, int64_t n_rays, const float* transform, c
     for (int k = 0; k < 3; ++k) p.mvs[k] = 2.0f / static_cast<float>(p.mdim[k]);
     for (int k = 0; k < 4; ++k) p.seeds[k] = seeds[k];
     p.draws_before = draws_before;
+    fill_encoding(encoding, p);
     return trm_object_space(transform, p);
 }
 
@@ -1730,12 +1768,13 @@ int environment_args(int env_kind, const float* env_rgb, const float* env_image,
 
 int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transform, float density_scale,
                           const float* majorant, const int* majorant_dims, int majorant_kind, const uint32_t* seeds,
-                          int draws_before, int n_layers, const int* dims, const float* const* weights,
-                          const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
-                          size_t workspace_bytes, float* out, void* stream) {
+                          int draws_before, const rdvb_encoding* encoding, int n_layers, const int* dims,
+                          const float* const* weights, const float* const* biases, const int* layer_flags,
+                          int input_relu, void* workspace, size_t workspace_bytes, float* out, void* stream) {
     rdvb::trm::Params p;
     if (int rc = tracking_params(rays, n_rays, transform, majorant, majorant_dims, majorant_kind, seeds, draws_before,
-                                 n_layers, dims, weights, biases, layer_flags, input_relu, workspace, workspace_bytes,
+                                 encoding, n_layers, dims, weights, biases, layer_flags, input_relu, workspace,
+                                 workspace_bytes,
                                  out, p, 1))
         return rc;
     if (n_rays == 0) return RDVB_OK;
@@ -1749,12 +1788,13 @@ int rdvb_transmittance_rt(const float* rays, int64_t n_rays, const float* transf
 int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const float* majorant,
               const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
               int env_kind, const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
-              const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
-              const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
-              size_t workspace_bytes, float* out, void* stream) {
+              const uint32_t* seeds, int draws_before, const rdvb_encoding* encoding, int n_layers, const int* dims,
+              const float* const* weights, const float* const* biases, const int* layer_flags, int input_relu,
+              void* workspace, size_t workspace_bytes, float* out, void* stream) {
     rdvb::trm::Params p;
     if (int rc = tracking_params(rays, n_rays, transform, majorant, majorant_dims, majorant_kind, seeds, draws_before,
-                                 n_layers, dims, weights, biases, layer_flags, input_relu, workspace, workspace_bytes,
+                                 encoding, n_layers, dims, weights, biases, layer_flags, input_relu, workspace,
+                                 workspace_bytes,
                                  out, p, 3))
         return rc;
     if (!albedo) return fail(RDVB_ERR_INVALID_ARG, "albedo must not be NULL");
@@ -1778,12 +1818,13 @@ int rdvb_pbvrt(const float* rays, int64_t n_rays, const float* transform, float 
                const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
                const float* light_direction, const float* light_intensity, int variant, int env_kind,
                const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
-               const uint32_t* seeds, int draws_before, int n_layers, const int* dims, const float* const* weights,
-               const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
-               size_t workspace_bytes, float* out, void* stream) {
+               const uint32_t* seeds, int draws_before, const rdvb_encoding* encoding, int n_layers,
+               const int* dims, const float* const* weights, const float* const* biases, const int* layer_flags,
+               int input_relu, void* workspace, size_t workspace_bytes, float* out, void* stream) {
     rdvb::trm::Params p;
     if (int rc = tracking_params(rays, n_rays, transform, majorant, majorant_dims, majorant_kind, seeds, draws_before,
-                                 n_layers, dims, weights, biases, layer_flags, input_relu, workspace, workspace_bytes,
+                                 encoding, n_layers, dims, weights, biases, layer_flags, input_relu, workspace,
+                                 workspace_bytes,
                                  out, p, 3))
         return rc;
     if (variant != RDVB_PBVRT && variant != RDVB_PBVR_NEE)

@@ -94,67 +94,76 @@ __device__ __forceinline__ float sample2(const float* __restrict__ t, int dim0, 
     return v;
 }
 
+// Channel k of the TensorSampler at the point x (x[0] the first
+// coordinate, addressing the last dimension), t [dim[0], ..., dim[IN-1], out].
+template <int IN>
+__device__ __forceinline__ float tensor_sample(const float* __restrict__ t, const int* dim, int out, int k,
+                                               const float* x, bool border, bool aligned, bool linear) {
+    if constexpr (IN == 2) {
+        return sample2(t, dim[0], dim[1], out, k, x[0], x[1], border, aligned, linear);
+    } else {
+    const float ac = aligned ? 1.0f : 0.0f;
+    int lo[IN], clo[IN], chi[IN];
+    float alpha[IN];
+    bool lo_in[IN], hi_in[IN];
+#pragma unroll
+    for (int d = 0; d < IN; ++d)
+        coord(x[IN - 1 - d], dim[d], ac, border, lo[d], clo[d], chi[d], alpha[d], lo_in[d], hi_in[d]);
+    // element strides of the spatial dimensions
+    long long st[IN];
+    st[IN - 1] = out;
+#pragma unroll
+    for (int d = IN - 2; d >= 0; --d) st[d] = st[d + 1] * dim[d + 1];
+    float v = 0.0f;
+    if (!linear) {
+        bool inside = true;
+        long long off = k;
+#pragma unroll
+        for (int d = 0; d < IN; ++d) {
+            int id = lo[d] + (alpha[d] >= 0.5f ? 1 : 0);
+            inside = inside && id >= 0 && id < dim[d];
+            id = min(max(id, 0), dim[d] - 1);
+            off += id * st[d];
+        }
+        return (border || inside) ? __ldg(t + off) : 0.0f;
+    }
+    const int L = IN - 1;  // innermost (fastest) dimension
+    const long long dl = static_cast<long long>(chi[L] - clo[L]) * st[L];
+    if constexpr (IN == 1) {
+        v = blend_pair(t, clo[0] * st[0] + k, dl, lo_in[0], hi_in[0], alpha[0], 1.0f, v);
+    } else {
+        long long ptr = clo[0] * st[0] + clo[1] * st[1] + clo[2] * st[2] + k;
+        const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st[0];
+        const long long d1 = static_cast<long long>(chi[1] - clo[1]) * st[1];
+        const float a0 = alpha[0], a1 = alpha[1];
+        v = blend_pair(t, ptr, dl, lo_in[0] && lo_in[1] && lo_in[2], lo_in[0] && lo_in[1] && hi_in[2], alpha[2],
+                       __fmul_rn(__fsub_rn(1.0f, a0), __fsub_rn(1.0f, a1)), v);
+        ptr += d1;
+        v = blend_pair(t, ptr, dl, lo_in[0] && hi_in[1] && lo_in[2], lo_in[0] && hi_in[1] && hi_in[2], alpha[2],
+                       __fmul_rn(__fsub_rn(1.0f, a0), a1), v);
+        ptr += d0;
+        v = blend_pair(t, ptr, dl, hi_in[0] && hi_in[1] && lo_in[2], hi_in[0] && hi_in[1] && hi_in[2], alpha[2],
+                       __fmul_rn(a0, a1), v);
+        ptr -= d1;
+        v = blend_pair(t, ptr, dl, hi_in[0] && lo_in[1] && lo_in[2], hi_in[0] && lo_in[1] && hi_in[2], alpha[2],
+                       __fmul_rn(a0, __fsub_rn(1.0f, a1)), v);
+    }
+    return v;
+    }
+}
+
 template <int IN>
 __global__ void tensor_sampler_kernel(const __grid_constant__ Params p) {
     const long long total = p.n * p.out;
-    const float ac = p.aligned ? 1.0f : 0.0f;
     const bool border = p.clamp != 0;
     for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<long long>(gridDim.x) * blockDim.x) {
         const long long i = idx / p.out;
         const int k = static_cast<int>(idx - i * p.out);
-        int lo[IN], clo[IN], chi[IN];
-        float alpha[IN];
-        bool lo_in[IN], hi_in[IN];
+        float x[IN];
 #pragma unroll
-        for (int d = 0; d < IN; ++d)
-            coord(__ldg(p.x + i * IN + (IN - 1 - d)), p.dim[d], ac, border, lo[d], clo[d], chi[d], alpha[d],
-                  lo_in[d], hi_in[d]);
-        // element strides of the spatial dimensions
-        long long st[IN];
-        st[IN - 1] = p.out;
-#pragma unroll
-        for (int d = IN - 2; d >= 0; --d) st[d] = st[d + 1] * p.dim[d + 1];
-        float out = 0.0f;
-        if (!p.linear) {
-            bool inside = true;
-            long long off = k;
-#pragma unroll
-            for (int d = 0; d < IN; ++d) {
-                int id = lo[d] + (alpha[d] >= 0.5f ? 1 : 0);
-                inside = inside && id >= 0 && id < p.dim[d];
-                id = min(max(id, 0), p.dim[d] - 1);
-                off += id * st[d];
-            }
-            if (border || inside) out = __ldg(p.t + off);
-            p.y[idx] = out;
-            continue;
-        }
-        const int L = IN - 1;  // innermost (fastest) dimension
-        const long long dl = static_cast<long long>(chi[L] - clo[L]) * st[L];
-        if constexpr (IN == 1) {
-            out = blend_pair(p.t, clo[0] * st[0] + k, dl, lo_in[0], hi_in[0], alpha[0], 1.0f, out);
-        } else if constexpr (IN == 2) {
-            out = sample2(p.t, p.dim[0], p.dim[1], p.out, k, __ldg(p.x + i * 2), __ldg(p.x + i * 2 + 1), border,
-                          p.aligned != 0, true);
-        } else {
-            long long ptr = clo[0] * st[0] + clo[1] * st[1] + clo[2] * st[2] + k;
-            const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st[0];
-            const long long d1 = static_cast<long long>(chi[1] - clo[1]) * st[1];
-            const float a0 = alpha[0], a1 = alpha[1];
-            out = blend_pair(p.t, ptr, dl, lo_in[0] && lo_in[1] && lo_in[2], lo_in[0] && lo_in[1] && hi_in[2],
-                             alpha[2], __fmul_rn(__fsub_rn(1.0f, a0), __fsub_rn(1.0f, a1)), out);
-            ptr += d1;
-            out = blend_pair(p.t, ptr, dl, lo_in[0] && hi_in[1] && lo_in[2], lo_in[0] && hi_in[1] && hi_in[2],
-                             alpha[2], __fmul_rn(__fsub_rn(1.0f, a0), a1), out);
-            ptr += d0;
-            out = blend_pair(p.t, ptr, dl, hi_in[0] && hi_in[1] && lo_in[2], hi_in[0] && hi_in[1] && hi_in[2],
-                             alpha[2], __fmul_rn(a0, a1), out);
-            ptr -= d1;
-            out = blend_pair(p.t, ptr, dl, hi_in[0] && lo_in[1] && lo_in[2], hi_in[0] && lo_in[1] && hi_in[2],
-                             alpha[2], __fmul_rn(a0, __fsub_rn(1.0f, a1)), out);
-        }
-        p.y[idx] = out;
+        for (int d = 0; d < IN; ++d) x[d] = __ldg(p.x + i * IN + d);
+        p.y[idx] = tensor_sample<IN>(p.t, p.dim, p.out, k, x, border, p.aligned != 0, p.linear != 0);
     }
 }
 
@@ -180,58 +189,66 @@ struct GridParams {
     int clamp, aligned, linear;
 };
 
+// Channel k of the GridSampler at the point x (x[0] the first coordinate,
+// addressing the last dimension), t [dim[0], ..., dim[IN-1], out].
+template <int IN>
+__device__ __forceinline__ float grid_sample(const float* __restrict__ t, const int* dim, int out, int k,
+                                             const float* x, bool clamp, bool aligned, bool linear) {
+    int voxel[IN];
+    float alpha[IN];
+#pragma unroll
+    for (int d = 0; d < IN; ++d) {
+        const float tc = __fadd_rn(__fmul_rn(x[IN - 1 - d], 0.5f), 0.5f);
+        const float pos = aligned ? __fmul_rn(tc, static_cast<float>(dim[d] - 1))
+                                  : __fsub_rn(__fmul_rn(tc, static_cast<float>(dim[d])), 0.5f);
+        const float fv = floorf(pos);
+        voxel[d] = static_cast<int>(fv);
+        alpha[d] = __fsub_rn(pos, fv);
+    }
+    float v = 0.0f;
+    if (!linear) {
+        bool inside = true;
+        long long off = 0;
+#pragma unroll
+        for (int d = 0; d < IN; ++d) {
+            int c = voxel[d] + (alpha[d] >= 0.5f ? 1 : 0);
+            if (clamp) c = min(max(c, 0), dim[d] - 1);
+            inside = inside && c >= 0 && c < dim[d];
+            off = off * dim[d] + c;
+        }
+        return (clamp || inside) ? __ldg(t + off * out + k) : 0.0f;
+    }
+#pragma unroll
+    for (int bits = 0; bits < (1 << IN); ++bits) {
+        bool inside = true;
+        long long off = 0;
+        float w = 1.0f;
+#pragma unroll
+        for (int d = 0; d < IN; ++d) {
+            const int up = (bits >> d) & 1;
+            int c = voxel[d] + up;
+            if (clamp) c = min(max(c, 0), dim[d] - 1);
+            inside = inside && c >= 0 && c < dim[d];
+            off = off * dim[d] + c;
+            w = __fmul_rn(w, up ? alpha[d] : __fsub_rn(1.0f, alpha[d]));
+        }
+        if (!clamp && !inside) continue;
+        v = __fadd_rn(v, __fmul_rn(w, __ldg(t + off * out + k)));
+    }
+    return v;
+}
+
 template <int IN>
 __global__ void grid_sampler_kernel(const __grid_constant__ GridParams p) {
     const long long total = p.n * p.out;
-    const bool clamp = p.clamp != 0;
     for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<long long>(gridDim.x) * blockDim.x) {
         const long long i = idx / p.out;
         const int k = static_cast<int>(idx - i * p.out);
-        int voxel[IN];
-        float alpha[IN];
+        float x[IN];
 #pragma unroll
-        for (int d = 0; d < IN; ++d) {
-            const float x = __ldg(p.x + i * IN + (IN - 1 - d));
-            const float t = __fadd_rn(__fmul_rn(x, 0.5f), 0.5f);
-            const float pos = p.aligned ? __fmul_rn(t, static_cast<float>(p.dim[d] - 1))
-                                        : __fsub_rn(__fmul_rn(t, static_cast<float>(p.dim[d])), 0.5f);
-            const float fv = floorf(pos);
-            voxel[d] = static_cast<int>(fv);
-            alpha[d] = __fsub_rn(pos, fv);
-        }
-        float out = 0.0f;
-        if (!p.linear) {
-            bool inside = true;
-            long long off = 0;
-#pragma unroll
-            for (int d = 0; d < IN; ++d) {
-                int c = voxel[d] + (alpha[d] >= 0.5f ? 1 : 0);
-                if (clamp) c = min(max(c, 0), p.dim[d] - 1);
-                inside = inside && c >= 0 && c < p.dim[d];
-                off = off * p.dim[d] + c;
-            }
-            if (clamp || inside) out = __ldg(p.t + off * p.out + k);
-        } else {
-#pragma unroll
-            for (int bits = 0; bits < (1 << IN); ++bits) {
-                bool inside = true;
-                long long off = 0;
-                float w = 1.0f;
-#pragma unroll
-                for (int d = 0; d < IN; ++d) {
-                    const int up = (bits >> d) & 1;
-                    int c = voxel[d] + up;
-                    if (clamp) c = min(max(c, 0), p.dim[d] - 1);
-                    inside = inside && c >= 0 && c < p.dim[d];
-                    off = off * p.dim[d] + c;
-                    w = __fmul_rn(w, up ? alpha[d] : __fsub_rn(1.0f, alpha[d]));
-                }
-                if (!clamp && !inside) continue;
-                out = __fadd_rn(out, __fmul_rn(w, __ldg(p.t + off * p.out + k)));
-            }
-        }
-        p.y[idx] = out;
+        for (int d = 0; d < IN; ++d) x[d] = __ldg(p.x + i * IN + d);
+        p.y[idx] = grid_sample<IN>(p.t, p.dim, p.out, k, x, p.clamp != 0, p.aligned != 0, p.linear != 0);
     }
 }
 

@@ -31,6 +31,7 @@
 #pragma once
 #include "mlp_tc.cuh"
 #include "rng.cuh"
+#include "sampler.cuh"
 
 namespace rdvb {
 namespace trm {
@@ -66,6 +67,12 @@ struct Params {
     int maxw;               // widest activation (>= 3)
     int w_floats;           // floats of the shared weight image (weight blocks, then biases)
     Layer layer[kMaxLayers];
+    // input encoding (a sampler of a dense 3-D grid in front of the chain)
+    int enc;                // 0 none, 1 TensorSampler, 2 GridSampler
+    const float* enc_t;     // [D, H, W, F] fp32
+    int enc_dim[3];         // D, H, W
+    int enc_out;            // F (the chain's input width, or 1 without layers)
+    int enc_clamp, enc_aligned, enc_linear;
     // ratiotracking_kernel / pbvr_kernel only
     const float* maj;       // majorant voxels [D, H, W] (z, y, x), [D, H, W, 2] for a sphere field
     int mdim[3];            // W, H, D: cells along x, y, z
@@ -157,17 +164,30 @@ __device__ __forceinline__ const float* eval_chain(const Params& p, const float*
     return ain;
 }
 
-// extinction(x) for this thread: the chain on the 3-vector x.
+// extinction(x) for this thread: the chain on the 3-vector x, or on the
+// F features the input encoding samples at x (the sampler's own arithmetic,
+// sampler.cuh); an encoding without layers is the extinction itself.
 template <int T = kThreads>
 __device__ __forceinline__ float extinction(const Params& p, const float* __restrict__ wsm,
                                             const float* __restrict__ bsm, float* act0, float* act1,
                                             const float (&x)[3]) {
-    const int m0 = p.layer[0].math;
+    const int m0 = p.n_layers > 0 ? p.layer[0].math : 0;
+    if (p.enc) {
+        for (int k = 0; k < p.enc_out; ++k) {
+            float v = p.enc == 1 ? sampler::tensor_sample<3>(p.enc_t, p.enc_dim, p.enc_out, k, x, p.enc_clamp != 0,
+                                                              p.enc_aligned != 0, p.enc_linear != 0)
+                                 : sampler::grid_sample<3>(p.enc_t, p.enc_dim, p.enc_out, k, x, p.enc_clamp != 0,
+                                                            p.enc_aligned != 0, p.enc_linear != 0);
+            if (p.input_relu) v = fmaxf(v, 0.0f);
+            act0[k * T] = stage_val(v, m0);
+        }
+    } else {
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        float v = x[k];
-        if (p.input_relu) v = fmaxf(v, 0.0f);
-        act0[k * T] = stage_val(v, m0);
+        for (int k = 0; k < 3; ++k) {
+            float v = x[k];
+            if (p.input_relu) v = fmaxf(v, 0.0f);
+            act0[k * T] = stage_val(v, m0);
+        }
     }
     return eval_chain<T>(p, wsm, bsm, act0, act1)[0];
 }

@@ -30,13 +30,14 @@ composition returns ``[num_cameras, height, width, 1]``.
 """
 from __future__ import annotations
 
+import ctypes
 import random as _random
 
 import torch
 
 from . import _native as N
 from .core import RDVObject, _timed, current_device, stream_handle, wrap
-from .maps import Composite, Constant, Map, TensorSampler, XRProject, _lower
+from .maps import Composite, Constant, GridSampler, Map, TensorSampler, XRProject, _lower
 
 _IDENTITY = (1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0)
 
@@ -50,6 +51,41 @@ def _mat4x3(transform) -> tuple:
         t = t.reshape(-1)
     assert t.numel() == 12, "transform must be a mat4x3 (12 values, column-major)"
     return tuple(float(v) for v in t.reshape(-1))
+
+
+def _split_encoding(extinction: Map):
+    """(leading TensorSampler / GridSampler of a 3-D grid or None, the rest
+    of the chain or None): the sampler becomes the kernels' input encoding."""
+    ops = extinction._ops()
+    if ops and isinstance(ops[0], (TensorSampler, GridSampler)):
+        smp = ops[0]
+        assert smp.IN == 3, "a volume's extinction encoding samples a 3-D grid"
+        rest = None
+        for op in ops[1:]:
+            rest = op if rest is None else Composite(op, rest)
+        return smp, rest
+    return None, extinction
+
+
+def _encoding(smp, dev):
+    """rdvb_encoding of a sampler (its grid kept alive on the struct)."""
+    t = smp.t._tensor
+    if t.device != dev or t.dtype != torch.float32 or not t.is_contiguous():
+        t = t.to(device=dev, dtype=torch.float32).contiguous()
+    e = N.Encoding()
+    e.kind = N.RDVB_ENCODING_GRID_SAMPLER if isinstance(smp, GridSampler) else N.RDVB_ENCODING_TENSOR_SAMPLER
+    e.grid = t.data_ptr()
+    for k in range(3):
+        e.dims[k] = int(t.shape[k])
+    e.features = int(t.shape[3])
+    e.flags = ((N.RDVB_SAMPLER_CLAMP if smp.clamp else 0) | (N.RDVB_SAMPLER_ALIGNED if smp.aligned else 0) |
+               (N.RDVB_SAMPLER_LINEAR if smp.linear else 0))
+    e._keep = t
+    return e
+
+
+def _enc_arg(st):
+    return ctypes.byref(st["enc"]) if st["enc"] is not None else None
 
 
 class RaymarchingTransmittance(Map):
@@ -75,19 +111,24 @@ class RaymarchingTransmittance(Map):
     def _device_state(self, dev):
         st = self._state.get(dev.index)
         if st is None:
-            input_relu, layers, relus = _lower(self.extinction)
-            if not layers:
-                raise NotImplementedError("the extinction needs at least one Linear layer")
+            sampler, rest = _split_encoding(self.extinction)
+            input_relu, layers, relus = _lower(rest) if rest is not None else (False, [], [])
+            if not layers and sampler is None:
+                raise NotImplementedError("the extinction needs at least one Linear layer or a sampler")
+            if sampler is not None and not layers:
+                assert sampler.OUT == 1, "a sampler alone as the extinction must have OUT = 1"
             st = {
                 "input_relu": int(input_relu),
                 "layers": layers,
-                "dims": [3] + [l.OUT for l in layers],
+                "dims": [sampler.OUT if sampler is not None else 3] + [l.OUT for l in layers],
                 "flags": [l._math | (N.RDVB_LAYER_RELU if r else 0) for l, r in zip(layers, relus)],
+                "sampler": sampler,
                 "ws": None,
             }
             self._state[dev.index] = st
         st["W"] = [l._fp32(l.weight, dev) for l in st["layers"]]
         st["b"] = [l._fp32(l.bias, dev) for l in st["layers"]]
+        st["enc"] = _encoding(st["sampler"], dev) if st["sampler"] is not None else None
         return st
 
     def __call__(self, rays):
@@ -107,7 +148,8 @@ class RaymarchingTransmittance(Map):
             st["ws"] = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
         with _timed():
             N.check(N.lib().rdvb_transmittance_rm(
-                r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.step_size, self.density_scale, n,
+                r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.step_size, self.density_scale,
+                _enc_arg(st), n,
                 N.int_array(st["dims"]), N.ptr_array([w.data_ptr() for w in st["W"]]),
                 N.ptr_array([b.data_ptr() for b in st["b"]]), N.int_array(st["flags"]), st["input_relu"],
                 st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(), stream_handle()), "rdvb_transmittance_rm")
@@ -222,7 +264,7 @@ class RatiotrackingTransmittance(RaymarchingTransmittance):
         with _timed():
             N.check(N.lib().rdvb_transmittance_rt(
                 r2.data_ptr(), r2.shape[0], N.float_array(self.transform), self.density_scale, g.data_ptr(),
-                N.int_array(gdims), kind, N.uint32_array(seeds), int(draws_before), n,
+                N.int_array(gdims), kind, N.uint32_array(seeds), int(draws_before), _enc_arg(st), n,
                 N.int_array(st["dims"]),
                 N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
                 N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
@@ -308,7 +350,7 @@ class PBVR(RaymarchingTransmittance):
                 r2.data_ptr(), r2.shape[0], N.float_array(self.transform), g.data_ptr(), N.int_array(gdims), kind,
                 N.float_array(self.albedo), self.g, self.max_bounces, env_kind, N.float_array(env_rgb),
                 env_img.data_ptr() if env_img is not None else None, N.int_array(env_dims), env_flags,
-                N.uint32_array(seeds), int(draws_before), n, N.int_array(st["dims"]),
+                N.uint32_array(seeds), int(draws_before), _enc_arg(st), n, N.int_array(st["dims"]),
                 N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
                 N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
                 stream_handle()), "rdvb_pbvr")
@@ -382,7 +424,7 @@ class _PBVRLight(RaymarchingTransmittance):
                 N.int_array(gdims), kind, N.float_array(self.albedo), self.g, self.max_bounces,
                 N.float_array(self.light_direction), N.float_array(self.light_intensity), self._variant, env_kind,
                 N.float_array(env_rgb), env_img.data_ptr() if env_img is not None else None, N.int_array(env_dims),
-                env_flags, N.uint32_array(seeds), int(draws_before), n, N.int_array(st["dims"]),
+                env_flags, N.uint32_array(seeds), int(draws_before), _enc_arg(st), n, N.int_array(st["dims"]),
                 N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
                 N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
                 stream_handle()), "rdvb_pbvrt")

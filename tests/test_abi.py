@@ -88,28 +88,28 @@ def test_ratio_tracking_validation_before_any_device_work(lib):
     dims, flags = N.int_array([3, 16, 1]), N.int_array([1, 1])
     seeds = N.uint32_array([1, 2, 3, 4])
     vox = N.RDVB_MAJORANT_VOXEL
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), vox, seeds, 0, 2, dims, None,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), vox, seeds, 0, None, 2, dims, None,
                                    None, flags, 0, None, 256, None, None)
     assert rc == -1 and "weights" in N.last_error()
     w = N.ptr_array([1, 1])
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), vox, seeds, 0, 2, dims, w, w,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 0]), vox, seeds, 0, None, 2, dims, w, w,
                                    flags, 0, None, 256, None, None)
     assert rc == -1 and "majorant_dims" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, None, 0, 2, dims, w, w,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, None, 0, None, 2, dims, w, w,
                                    flags, 0, None, 256, None, None)
     assert rc == -1 and "seeds" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, seeds, 0, 2,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, seeds, 0, None, 2,
                                    N.int_array([3, 16, 2]), w, w, flags, 0, None, 256, None, None)
     assert rc == -1 and "3 -> 1" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, seeds, -1, 2, dims, w, w,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), vox, seeds, -1, None, 2, dims, w, w,
                                    flags, 0, None, 256, None, None)
     assert rc == -1 and "draws_before" in N.last_error()
-    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), 7, seeds, 0, 2, dims, w, w,
+    rc = lib.rdvb_transmittance_rt(None, 4, None, 1.0, None, N.int_array([2, 2, 2]), 7, seeds, 0, None, 2, dims, w, w,
                                    flags, 0, None, 256, None, None)
     assert rc == -1 and "majorant_kind" in N.last_error()
     # nothing to do: no device needed
     for kind in (N.RDVB_MAJORANT_VOXEL, N.RDVB_MAJORANT_SPHERE):
-        assert lib.rdvb_transmittance_rt(None, 0, None, 1.0, None, N.int_array([2, 2, 2]), kind, seeds, 0, 2, dims,
+        assert lib.rdvb_transmittance_rt(None, 0, None, 1.0, None, N.int_array([2, 2, 2]), kind, seeds, 0, None, 2, dims,
                                          w, w, flags, 0, None, 256, None, None) == 0
 
 
@@ -119,7 +119,7 @@ def _pbvr(lib, N, *, n=4, kind=0, albedo=(1.0, 1.0, 1.0), g=0.0, max_bounces=4, 
                          N.float_array(albedo) if albedo is not None else None, g, max_bounces, env_kind,
                          N.float_array(env_rgb) if env_rgb is not None else None, None,
                          N.int_array(env_dims) if env_dims is not None else None, env_flags,
-                         N.uint32_array(seeds) if seeds is not None else None, 0, len(dims) - 1,
+                         N.uint32_array(seeds) if seeds is not None else None, 0, None, len(dims) - 1,
                          N.int_array(dims), N.ptr_array(w), N.ptr_array(w), N.int_array([1] * (len(dims) - 1)), 0,
                          None, 256, None, None)
 
@@ -240,7 +240,7 @@ def test_pbvrt_validation(lib):
                               N.float_array(albedo) if albedo else None, g, mb,
                               N.float_array(light) if light else None, N.float_array(intensity) if intensity else None,
                               variant, 0, N.float_array([1, 1, 1]), None, N.int_array([1, 1]), 0,
-                              N.uint32_array([1, 2, 3, 4]), 0, 2, N.int_array([3, 16, 1]), N.ptr_array([1, 1]),
+                              N.uint32_array([1, 2, 3, 4]), 0, None, 2, N.int_array([3, 16, 1]), N.ptr_array([1, 1]),
                               N.ptr_array([1, 1]), N.int_array([1, 1]), 0, None, 256, None, None)
 
     assert call() == 0
@@ -249,3 +249,32 @@ def test_pbvrt_validation(lib):
                     (dict(intensity=None), "light_intensity"), (dict(mb=-1), "max_bounces"),
                     (dict(scale=float("inf")), "finite"), (dict(light=(0, 0, 0)), "nonzero")):
         assert call(**kw) == -1 and msg in N.last_error(), (kw, N.last_error())
+
+
+def test_extinction_encoding_validation(lib):
+    """A sampler in front of a volume node's chain (rdvb_encoding): checked
+    on the host; with it the chain maps features -> 1, or is empty."""
+    import ctypes
+    import rdv_project_b200._native as N
+
+    def rm(enc, n_layers, dims, n=0):
+        return lib.rdvb_transmittance_rm(None, n, None, 0.01, 1.0, ctypes.byref(enc) if enc is not None else None,
+                                         n_layers, N.int_array(dims), N.ptr_array([1] * max(n_layers, 1)),
+                                         N.ptr_array([1] * max(n_layers, 1)), N.int_array([1] * max(n_layers, 1)), 0,
+                                         None, 256, None, None)
+
+    e = N.Encoding()
+    e.kind, e.grid, e.features, e.flags = N.RDVB_ENCODING_GRID_SAMPLER, 256, 4, N.RDVB_SAMPLER_LINEAR
+    for k in range(3):
+        e.dims[k] = 8
+    assert rm(e, 1, [4, 1]) == 0              # sampler (4 features) >> Linear 4 -> 1
+    assert rm(e, 0, [4]) == -1 and "4 -> 1" in N.last_error()
+    e.features = 1
+    assert rm(e, 0, [1]) == 0                 # the sampled density is the extinction
+    assert rm(None, 0, [3]) == -1 and "n_layers" in N.last_error()
+    e.kind = 9
+    assert rm(e, 0, [1]) == -1 and "encoding kind" in N.last_error()
+    e.kind, e.dims[1] = N.RDVB_ENCODING_TENSOR_SAMPLER, 0
+    assert rm(e, 0, [1]) == -1 and "encoding dims" in N.last_error()
+    e.dims[1], e.flags = 8, 16
+    assert rm(e, 0, [1]) == -1 and "flag" in N.last_error()
