@@ -79,6 +79,7 @@ typedef struct rdvb_encoding {
 /* rdvb_pbvrt variants */
 #define RDVB_PBVRT 0    /* PBVRT: RGB + alpha, the environment after scattering */
 #define RDVB_PBVR_NEE 1 /* PBVR_NEE: RGB, next-event estimation only */
+#define RDVB_PBVR_ENV 2 /* PBVR_ENV: RGB, next-event estimation toward importance-sampled environment directions */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int rdvb_version(void);
@@ -491,16 +492,26 @@ int rdvb_pbvr(const float* rays, int64_t n_rays, const float* transform, const f
  * alpha 0 and RGB = NEE sum * light_intensity (3 host floats) + throughput *
  * environment(w) (environment arguments as rdvb_pbvr); else RGB 0, alpha 1.
  * PBVR_NEE (RDVB_PBVR_NEE, out [n_rays, 3]): the NEE sum; the environment
- * and light_intensity are not read. Majorant field, generator, chain and
+ * and light_intensity are not read. PBVR_ENV (RDVB_PBVR_ENV, out
+ * [n_rays, 3], rdv/domain/volumes.py:445-502, pbvr_env.h): at each real
+ * collision the NEE direction and its radiance / pdf come from an
+ * XREnvironmentSampler (rendering.py:281-323, xr_environment_sampler.h):
+ * env_densities (device) holds its quadtree of env_levels levels (1..12),
+ * 4 cumulative child probabilities per node, child c of node n being node
+ * 4 n + 1 + c; one draw walks it, two more place the direction in the leaf
+ * pixel; the environment arguments are the sampler's environment map; the
+ * term is (transmittance * phase * throughput) * radiance / pdf;
+ * light_direction and light_intensity are not read. Majorant field, generator, chain and
  * workspace as rdvb_transmittance_rt (bytes 8-15: extinction evaluations,
  * shadow rays included). */
 int rdvb_pbvrt(const float* rays, int64_t n_rays, const float* transform, float density_scale, const float* majorant,
                const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
                const float* light_direction, const float* light_intensity, int variant, int env_kind,
                const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
-               const uint32_t* seeds, int draws_before, const rdvb_encoding* encoding, int n_layers,
-               const int* dims, const float* const* weights, const float* const* biases, const int* layer_flags,
-               int input_relu, void* workspace, size_t workspace_bytes, float* out, void* stream);
+               const float* env_densities, int env_levels, const uint32_t* seeds, int draws_before,
+               const rdvb_encoding* encoding, int n_layers, const int* dims, const float* const* weights,
+               const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+               size_t workspace_bytes, float* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -135,6 +135,9 @@ def ref_pbvr_lib() -> ctypes.CDLL:
         lib.ref_pbvrt.argtypes = [i32, f32, f32, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp, f32, f32, i32, vp, vp,
                                   lg, vp]
         lib.ref_pbvrt.restype = None
+        lib.ref_pbvr_env.argtypes = [f32, f32, i32, vp, i32, i32, i32, vp, vp, vp, vp, i32, f32, f32, i32, vp, vp,
+                                     lg, vp]
+        lib.ref_pbvr_env.restype = None
         lib.ref_hg_phase_sample.argtypes = [vp, i32, i32, vp, f32, vp]
         lib.ref_hg_phase_sample.restype = None
         _ref_pbvr = lib

@@ -655,9 +655,105 @@ def normalize3(v) -> np.ndarray:
     return (v / np.float32(np.sqrt(np.float64(sq)))).astype(np.float32)
 
 
+def xr_env_sample(densities: np.ndarray, levels: int, environment, state: np.ndarray):
+    """XREnvironmentSampler.forward (rdv/shaders/rendering/
+    xr_environment_sampler.h) in float32 for every row of `state` (advanced
+    in place): one draw walks the quadtree (rescaled to [0, 1) per level),
+    prob the product of the chosen children's probabilities; two more draws
+    place the direction uniformly in solid angle inside the leaf pixel
+    (usc2dir, math_library.h:256-263). Returns (directions [R, 3],
+    environment / pdf [R, 3])."""
+    f32 = np.float32
+    dens = np.asarray(densities, dtype=np.float32)
+    n = state.shape[0]
+    node = np.zeros(n, dtype=np.int64)
+    u0 = np.zeros(n, f32); u1 = np.ones(n, f32); v0 = np.zeros(n, f32); v1 = np.ones(n, f32)
+    prob = np.ones(n, f32)
+    sel = random_draw(state)
+    for _ in range(levels):
+        cdf = dens[node[:, None] * 4 + np.arange(4)[None, :]]
+        child = np.full(n, 3, dtype=np.int64)
+        lo = np.zeros(n, f32)
+        hi = cdf[:, 3].copy()
+        decided = np.zeros(n, dtype=bool)
+        for c in range(3):
+            take = ~decided & (sel < cdf[:, c])
+            child[take] = c
+            hi[take] = cdf[take, c]
+            decided |= take
+            lo = np.where(decided, lo, cdf[:, c]).astype(f32)
+        span = (hi - lo).astype(f32)
+        prob = (prob * _glsl_max(f32(0.0), span)).astype(f32)
+        q = ((sel - lo) / _glsl_max(f32(1e-9), span)).astype(f32)
+        sel = _glsl_min(_glsl_max(q, f32(0.0)), f32(1.0))
+        umed = ((u0 + u1) * f32(0.5)).astype(f32)
+        vmed = ((v0 + v1) * f32(0.5)).astype(f32)
+        even = child % 2 == 0
+        u1 = np.where(even, umed, u1); u0 = np.where(even, u0, umed)
+        top = child // 2 == 0
+        v1 = np.where(top, vmed, v1); v0 = np.where(top, v0, vmed)
+        node = node * 4 + 1 + child
+    pi_, half_pi = _PI, np.float32(1.5707963267948966)
+    a0 = ((u0 * f32(2.0) - f32(1.0)) * pi_).astype(f32)
+    a1 = ((u1 * f32(2.0) - f32(1.0)) * pi_).astype(f32)
+    b0 = ((v0 * f32(2.0) - f32(1.0)) * half_pi).astype(f32)
+    b1 = ((v1 * f32(2.0) - f32(1.0)) * half_pi).astype(f32)
+    sb0, sb1 = _f32(np.sin, b0), _f32(np.sin, b1)
+    solid = ((a1 - a0) * (sb1 - sb0)).astype(f32)
+    pdf = (prob / _glsl_max(f32(1e-9), solid)).astype(f32)
+    weight = (f32(1.0) / _glsl_max(f32(1e-9), pdf)).astype(f32)
+    ta = random_draw(state)
+    alpha = ((a0 * (f32(1.0) - ta)) + (a1 * ta)).astype(f32)
+    ts = random_draw(state)
+    sv = ((sb0 * (f32(1.0) - ts)) + (sb1 * ts)).astype(f32)
+    beta = _f32(np.arcsin, np.clip(sv, f32(-1.0), f32(1.0)))
+    rr = _f32(np.cos, beta)
+    d = np.stack([_f32(np.sin, alpha) * rr, _f32(np.sin, beta), _f32(np.cos, alpha) * rr], axis=1).astype(f32)
+    env = np.asarray(environment(d), dtype=np.float32)
+    return d, (env * weight[:, None]).astype(f32)
+
+
+def xr_quadtree(density: np.ndarray, levels: int) -> np.ndarray:
+    """The quadtree of rdv/domain/rendering.py:175-278 from an already
+    resampled, channel-summed density [2^levels, 2^levels] (float32): row
+    solid-angle weights sin(beta1) - sin(beta0), normalisation, the mass
+    pyramid, per node (Morton order) the cumulative child probabilities
+    (0.25 each under an empty parent), the last forced to 1 -- in float64
+    here, so the GPU build agrees within float32 rounding."""
+    res = 1 << levels
+    d = np.maximum(np.asarray(density, dtype=np.float64), 0.0)
+    v0 = np.arange(res) / res
+    v1 = (np.arange(res) + 1) / res
+    w = np.sin((v1 * 2 - 1) * np.pi / 2) - np.sin((v0 * 2 - 1) * np.pi / 2)
+    d = np.maximum(d * w[:, None], 0.0)
+    d = d / max(d.sum(), 1e-12)
+    pyr = [d]
+    for _ in range(levels):
+        g = pyr[-1]
+        pyr.append(g.reshape(g.shape[0] // 2, 2, g.shape[1] // 2, 2).sum(axis=(1, 3)))
+    pyr.reverse()
+
+    def morton(t, dd):
+        if dd == 0:
+            return t.reshape(1)
+        order = [a for i in range(dd) for a in (i, dd + i)]
+        return t.reshape([2] * (2 * dd)).transpose(order).reshape(-1)
+
+    out = []
+    for dd in range(levels):
+        parent = morton(pyr[dd], dd)
+        kids = morton(pyr[dd + 1], dd + 1).reshape(-1, 4)
+        p = np.where(parent[:, None] > 1e-12, kids / np.maximum(parent, 1e-12)[:, None], 0.25)
+        cum = np.cumsum(p, axis=1)
+        cum[:, 3] = 1.0
+        out.append(cum.reshape(-1))
+    return np.concatenate(out)
+
+
 def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, light_intensity=(1.0, 1.0, 1.0),
           environment=None, transform=None, density_scale: float = 1.0, g: float = 0.0, max_bounces: int = 32,
-          variant: str = "pbvrt", index=None, draws_before: int = 0, return_evaluations: bool = False):
+          variant: str = "pbvrt", index=None, draws_before: int = 0, return_evaluations: bool = False,
+          env_densities=None, env_levels: int = 0):
     """PBVRT.forward (rdv/shaders/volumes/pbvrt.h:21-149) and, with
     variant="nee", PBVR_NEE.forward (pbvr_nee.h), vectorised over rays, each
     ray a state machine of the main path and its shadow ray run in lock step,
@@ -678,8 +774,12 @@ def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, l
 
     `majorant(x, w)` returns the field's raw (value, distance);
     transmittance_rt is ratiotracking_transmittance_trait.h's loop (as
-    transmittance_rt above). Returns [n, 4] (PBVRT) or [n, 3] (NEE)."""
-    nee = variant == "nee"
+    transmittance_rt above). Returns [n, 4] (PBVRT) or [n, 3] (NEE, ENV).
+    variant="env" is PBVR_ENV (pbvr_env.h): each NEE direction and its
+    radiance / pdf come from xr_env_sample over (env_densities, env_levels)
+    and `environment`, the term (tr W) * radiance / pdf."""
+    env_nee = variant == "env"
+    nee = variant in ("nee", "env")
     o, w_obj = object_space(origins, dirs, transform)
     w_world = np.asarray(dirs, dtype=np.float32).copy()
     L = _inverse3(transform)
@@ -714,8 +814,11 @@ def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, l
     W = np.ones((m, 3), dtype=np.float32)
     acc = np.zeros((m, 3), dtype=np.float32)
     alb = np.asarray(albedo, dtype=np.float32).reshape(1, 3)
-    light = normalize3(light_direction)
+    light = normalize3(light_direction) if not env_nee else np.array([0.0, 1.0, 0.0], np.float32)
     lo_dir = _apply3(L, light[None].astype(np.float32))[0]
+    l_rows = np.broadcast_to(light, (m, 3)).astype(np.float32).copy()     # NEE direction per ray
+    lo_rows = np.broadcast_to(lo_dir, (m, 3)).astype(np.float32).copy()
+    ew = np.ones((m, 3), dtype=np.float32)
     bounces = np.zeros(m, dtype=np.int64)
     safety = np.zeros(m, dtype=np.int64)
     mode = np.zeros(m, dtype=np.int64)          # 0 main, 1 shadow
@@ -732,7 +835,8 @@ def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, l
 
     def shadow_end(rows, t):
         tr = (t.astype(np.float32) * phase[rows]).astype(np.float32)
-        acc[rows] = (acc[rows] + W[rows] * tr[:, None]).astype(np.float32)
+        term = ((tr[:, None] * W[rows]).astype(np.float32) * ew[rows]).astype(np.float32)
+        acc[rows] = (acc[rows] + term).astype(np.float32)
         sub = state[rows]
         w[rows] = hg_phase_sample(w[rows], g, sub)
         state[rows] = sub
@@ -777,7 +881,7 @@ def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, l
             ss = ss[~done]
         if ss.size:
             s_safety[ss] += 1
-            mv, dist = majorant(xs[ss], np.broadcast_to(lo_dir, (ss.size, 3)).astype(np.float32))
+            mv, dist = majorant(xs[ss], lo_rows[ss])
             mj = _glsl_max(mv.astype(np.float32), f32(1e-12))
             dist = _glsl_max(dist.astype(np.float32), f32(1e-6))
             sub = state[ss]
@@ -787,7 +891,7 @@ def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, l
                 q = ((-_log_f32(f32(1.0) - u)) / (mj * dsc)).astype(np.float32)
             dt = _glsl_min(dist, q)
             ds[ss] = (ds[ss] - dt).astype(np.float32)
-            xs[ss] = (xs[ss] + dt[:, None] * lo_dir[None]).astype(np.float32)
+            xs[ss] = (xs[ss] + dt[:, None] * lo_rows[ss]).astype(np.float32)
             moved = dt >= dist
             fin = ~moved & (ds[ss] <= 0)
             if fin.any():
@@ -838,10 +942,16 @@ def pbvrt(origins, dirs, extinction, majorant, seeds, albedo, light_direction, l
                 running[go[low_w]] = False
                 go = go[~low_w]
                 if go.size:
-                    cos_t = ((w[go, 0] * light[0] + w[go, 1] * light[1]).astype(np.float32) + w[go, 2] * light[2])
+                    if env_nee:
+                        sub = state[go]
+                        l_rows[go], ew[go] = xr_env_sample(env_densities, env_levels, environment, sub)
+                        state[go] = sub
+                        lo_rows[go] = _apply3(L, l_rows[go])
+                    lg = l_rows[go]
+                    cos_t = ((w[go, 0] * lg[:, 0] + w[go, 1] * lg[:, 1]).astype(np.float32) + w[go, 2] * lg[:, 2])
                     phase[go] = hg_phase_eval(cos_t.astype(np.float32), g)
                     xs[go] = x[go]
-                    ds[go] = slab_exit(x[go], np.broadcast_to(lo_dir, (go.size, 3)).astype(np.float32))
+                    ds[go] = slab_exit(x[go], lo_rows[go])
                     T[go] = 1.0
                     s_safety[go] = 0
                     mode[go] = 1

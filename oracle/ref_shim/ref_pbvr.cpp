@@ -307,6 +307,67 @@ static void scattering_albedo(NeeSphere n, rdv_vec3 x, float* sa) { scattering_a
 #include "pbvr_nee.h"
 #undef OUT
 #undef RDV_NODE
+// -- PBVR_ENV (volumes/pbvr_env.h) with its XREnvironmentSampler
+// (rendering/xr_environment_sampler.h; copy: `float[3](` -> `rdv_farr(`,
+// float literals). usc2dir (math_library.h:256-263) and the
+// environment_sampler trait helper (environment_sampler_trait.h) are
+// restated; GLSL mix(a, b, t) = a (1 - t) + b t, clamp = min(max(x, lo), hi).
+#define piOverTwo 1.5707963267948966192313216916398f
+#define asin(x) static_cast<float>(std::asin(static_cast<double>(static_cast<float>(x))))
+static inline float mix(float a, float b, float t) { return a * (1.0f - t) + b * t; }
+static inline float clamp(float x, float lo, float hi) { return gmin(gmax(x, lo), hi); }
+static rdv_vec3 usc2dir(rdv_vec2 angles) {
+    const float y = sin(angles.y);
+    const float r = cos(angles.y);
+    const float x = sin(angles.x) * r;
+    const float z = cos(angles.x) * r;
+    return rdv_vec3(x, y, z);
+}
+struct XrEnvNode {
+    EnvConst environment;
+    const float* densities;
+};
+#define RDV_NODE XrEnvNode
+#define IN 6
+#define OUT 7
+#define LEVELS g_env_levels
+static int g_env_levels = 8;
+#include "xr_environment_sampler.h"
+#undef LEVELS
+#undef OUT
+#undef IN
+#undef RDV_NODE
+template <typename MG>
+struct EnvNodeT : PbvrtNode<MG> {
+    XrEnvNode environment_sampler;
+};
+typedef EnvNodeT<VoxelField> EnvVoxel;
+typedef EnvNodeT<SphereField> EnvSphere;
+static float extinction(EnvVoxel n, rdv_vec3 x) { return extinction(static_cast<PbvrtVoxel>(n), x); }
+static float extinction(EnvSphere n, rdv_vec3 x) { return extinction(static_cast<PbvrtSphere>(n), x); }
+static float majorant(EnvVoxel n, rdv_vec3 x, rdv_vec3 w, float& d) { return majorant(static_cast<PbvrtVoxel>(n), x, w, d); }
+static float majorant(EnvSphere n, rdv_vec3 x, rdv_vec3 w, float& d) { return majorant(static_cast<PbvrtSphere>(n), x, w, d); }
+static void scattering_albedo(EnvVoxel n, rdv_vec3 x, float* sa) { scattering_albedo(static_cast<PbvrtVoxel>(n), x, sa); }
+static void scattering_albedo(EnvSphere n, rdv_vec3 x, float* sa) { scattering_albedo(static_cast<PbvrtSphere>(n), x, sa); }
+template <typename MG>
+static rdv_vec3 environment_sampler(EnvNodeT<MG> node, rdv_vec3 x, rdv_vec3 win, float* env) {
+    float in6[6] = {x.x, x.y, x.z, win.x, win.y, win.z}, result[7];
+    forward(node.environment_sampler, in6, result);
+    for (int i = 0; i < SPECTRAL_DIM; i++) env[i] = result[3 + i];
+    return rdv_vec3(result[0], result[1], result[2]);
+}
+#define RDV_NODE EnvVoxel
+#include "volumes/ratiotracking_transmittance_trait.h"
+#define OUT 3
+#include "pbvr_env.h"
+#undef OUT
+#undef RDV_NODE
+#define RDV_NODE EnvSphere
+#include "volumes/ratiotracking_transmittance_trait.h"
+#define OUT 3
+#include "pbvr_env.h"
+#undef OUT
+#undef RDV_NODE
 #undef log
 #undef random
 
@@ -393,6 +454,44 @@ void ref_pbvrt(int variant, float c0, float c1, int field_kind, const float* gri
         NeeVoxel node; fill(node); node.mg = VoxelField{grid, gd, gh, gw}; run_rays(node);
     } else {
         NeeSphere node; fill(node); node.mg = SphereField{grid, gd, gh, gw}; run_rays(node);
+    }
+}
+
+// PBVR_ENV.forward for rays [n, 6] -> dst [n, 3]: as ref_pbvrt, the NEE
+// directions from an XREnvironmentSampler over `densities` (levels deep)
+// whose environment is the constant env_rgb.
+void ref_pbvr_env(float c0, float c1, int field_kind, const float* grid, int gd, int gh, int gw, const float* env_rgb,
+                  const float* transform, const float* albedo, const float* densities, int levels, float g,
+                  float density_scale, int max_bounces, const unsigned* seeds, const float* rays, long n, float* dst) {
+    g_env_levels = levels;
+    auto fill = [&](auto& node) {
+        node.ext = ExtNode{c0, c1};
+        node.env = EnvConst{env_rgb[0], env_rgb[1], env_rgb[2]};
+        node.environment_sampler = XrEnvNode{EnvConst{env_rgb[0], env_rgb[1], env_rgb[2]}, densities};
+        for (int k = 0; k < 3; ++k) {
+            node.sa[k] = albedo[k];
+            node.light_intensity[k] = 1.0f;
+        }
+        for (int j = 0; j < 4; ++j)
+            node.transform.c[j] = rdv_vec3(transform[3 * j], transform[3 * j + 1], transform[3 * j + 2]);
+        node.light_direction = rdv_vec3(0.0f, 1.0f, 0.0f);
+        node.g = g;
+        node.density_scale = density_scale;
+        node.max_bounces = max_bounces;
+    };
+    auto run_rays = [&](auto node) {
+        for (long r = 0; r < n; ++r) {
+            random_seeds.seeds = rdv_uvec4(seeds[0], seeds[1], seeds[2], seeds[3]);
+            rdv_random_init(rdv_uvec3{(unsigned)r, 0u, 0u});
+            float in6[6];
+            for (int k = 0; k < 6; ++k) in6[k] = rays[r * 6 + k];
+            forward(node, in6, dst + r * 3);
+        }
+    };
+    if (field_kind == 0) {
+        EnvVoxel node; fill(node); node.mg = VoxelField{grid, gd, gh, gw}; run_rays(node);
+    } else {
+        EnvSphere node; fill(node); node.mg = SphereField{grid, gd, gh, gw}; run_rays(node);
     }
 }
 

@@ -20,7 +20,7 @@ from .conv import (Conv2DTensorOp, Conv2DTensorOpFast, Conv2DTensorOpSimple, Con
                    _winograd_transform_weight)
 from .rendering import Cameras, VolumeRenderer
 from .volumes import (RaymarchingTransmittance, RatiotrackingTransmittance, TensorGrid, VoxelMajorantField,
-                      SphereMajorantField, PBVR, PBVRT, PBVR_NEE)
+                      SphereMajorantField, PBVR, PBVRT, PBVR_NEE, PBVR_ENV, XREnvironmentSampler)
 from ._native import RdvbError, device_status
 
 __all__ = [
@@ -32,6 +32,6 @@ __all__ = [
     "Conv2DTensorOp", "Conv2DTensorOpFast", "Conv2DTensorOpSimple", "Conv2DTensorOpSimple3x3",
     "Conv2DTensorOpWindow3x3", "Conv2DTensorOpWinograd3x3", "Conv3x3Winograd", "conv2d_direct",
     "Cameras", "VolumeRenderer", "RaymarchingTransmittance", "RatiotrackingTransmittance", "TensorGrid",
-    "VoxelMajorantField", "SphereMajorantField", "PBVR", "PBVRT", "PBVR_NEE",
+    "VoxelMajorantField", "SphereMajorantField", "PBVR", "PBVRT", "PBVR_NEE", "PBVR_ENV", "XREnvironmentSampler",
     "RdvbError", "device_status",
 ]

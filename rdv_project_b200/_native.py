@@ -24,7 +24,7 @@ RDVB_PATH_CUDA_CORE, RDVB_PATH_TENSOR_CORE = 0, 1
 RDVB_MAJORANT_VOXEL, RDVB_MAJORANT_SPHERE = 0, 1
 RDVB_ENV_CONSTANT, RDVB_ENV_EQUIRECT = 0, 1
 RDVB_SAMPLER_CLAMP, RDVB_SAMPLER_ALIGNED, RDVB_SAMPLER_LINEAR = 1, 2, 4
-RDVB_PBVRT, RDVB_PBVR_NEE = 0, 1
+RDVB_PBVRT, RDVB_PBVR_NEE, RDVB_PBVR_ENV = 0, 1, 2
 RDVB_ENCODING_TENSOR_SAMPLER, RDVB_ENCODING_GRID_SAMPLER = 1, 2
 
 _c_int, _c_i64, _vp, _c_u32, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float
@@ -72,8 +72,8 @@ SIGNATURES = {
                                        _vp, _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
     "rdvb_xr_project": (_c_int, [_vp, _c_i64, _vp, _vp]),
     "rdvb_pbvrt": (_c_int, [_vp, _c_i64, _vp, _c_f, _vp, _vp, _c_int, _vp, _c_f, _c_int, _vp, _vp, _c_int, _c_int,
-                            _vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp,
-                            ctypes.c_size_t, _vp, _vp]),
+                            _vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp,
+                            _c_int, _vp, ctypes.c_size_t, _vp, _vp]),
     "rdvb_grid_sampler": (_c_int, [_vp, _c_int, _vp, _c_int, _vp, _c_i64, _c_int, _c_int, _c_int, _vp, _vp]),
     "rdvb_pbvr": (_c_int, [_vp, _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_f, _c_int, _c_int, _vp, _vp, _vp, _c_int,
                            _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, ctypes.c_size_t, _vp, _vp]),

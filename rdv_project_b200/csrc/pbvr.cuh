@@ -252,9 +252,10 @@ __global__ void __launch_bounds__(NT) pbvr_kernel(const __grid_constant__ Params
 }
 
 // ---------------------------------------------------------------------------
-// PBVRT and PBVR_NEE (rdv/domain/volumes.py:326-442, rdv/shaders/volumes/
-// pbvrt.h, pbvr_nee.h): delta tracking with next-event estimation toward a
-// directional light, RGB. Per ray -- pbvrt.h:21-149:
+// PBVRT, PBVR_NEE and PBVR_ENV (rdv/domain/volumes.py:326-502,
+// rdv/shaders/volumes/pbvrt.h, pbvr_nee.h, pbvr_env.h): delta tracking with
+// next-event estimation toward a directional light (PBVR_ENV: toward a
+// direction importance-sampled from the environment, env_sample), RGB. Per ray -- pbvrt.h:21-149:
 //   object space; slab test (miss: tMax <= 0 or tMin >= tMax) -> 0 (PBVRT:
 //   alpha 1); entry x <- x + w_o (max(0, tMin) + 1e-5), d <- tMax - tMin;
 //   for (safety < 16384):
@@ -278,11 +279,74 @@ struct ExtraT {
     float g;
     float density_scale;
     int max_bounces;
-    int variant;             // 0 PBVRT ([n, 4]: RGB, alpha), 1 PBVR_NEE ([n, 3])
+    int variant;             // 0 PBVRT ([n, 4]: RGB, alpha), 1 PBVR_NEE ([n, 3]), 2 PBVR_ENV ([n, 3])
     float light[3];          // normalize(light_direction), world space (host)
     float intensity[3];      // PBVRT: light_intensity
-    Extra env;               // environment (PBVRT) and the output pointer
+    Extra env;               // environment (PBVRT; PBVR_ENV: the sampler's) and the output pointer
+    const float* densities;  // PBVR_ENV: the quadtree's cumulative child probabilities, 4 per node
+    int levels;              // PBVR_ENV: its depth
 };
+
+constexpr float kPiOverTwo = 1.57079632679489661923f;
+
+// XREnvironmentSampler.forward (rdv/domain/rendering.py:281-323,
+// rdv/shaders/rendering/xr_environment_sampler.h): one draw walks the
+// quadtree (rescaled to [0, 1) at every level), the leaf's probability is
+// the product of the chosen children's; two more draws place the direction
+// uniformly in solid angle inside the leaf pixel (usc2dir,
+// math_library.h:256-263); returns the direction and the environment there
+// times 1 / pdf. GLSL mix(a, b, t) = a (1 - t) + b t.
+__device__ __forceinline__ void env_sample(const ExtraT& e, Rng& r, float (&dir)[3], float (&val)[3]) {
+    int node = 0;
+    float u0 = 0.0f, u1 = 1.0f, v0 = 0.0f, v1 = 1.0f, prob = 1.0f;
+    float sel = rng_uniform(r);
+    for (int i = 0; i < e.levels; ++i) {
+        const float* cdf = e.densities + node * 4;
+        int child = 3;
+        float lo = 0.0f, hi = __ldg(cdf + 3);
+        for (int c = 0; c < 3; ++c) {
+            const float cc = __ldg(cdf + c);
+            if (sel < cc) {
+                child = c;
+                hi = cc;
+                break;
+            }
+            lo = cc;
+        }
+        const float span = __fsub_rn(hi, lo);
+        prob = __fmul_rn(prob, 0.0f < span ? span : 0.0f);               // max(0, hi - lo)
+        float q = __fdiv_rn(__fsub_rn(sel, lo), 1e-9f < span ? span : 1e-9f);
+        q = q < 0.0f ? 0.0f : q;                                         // clamp(., 0, 1)
+        sel = 1.0f < q ? 1.0f : q;
+        const float umed = __fmul_rn(__fadd_rn(u0, u1), 0.5f), vmed = __fmul_rn(__fadd_rn(v0, v1), 0.5f);
+        if (child % 2 == 0) u1 = umed; else u0 = umed;
+        if (child / 2 == 0) v1 = vmed; else v0 = vmed;
+        node = node * 4 + 1 + child;
+    }
+    const float a0 = __fmul_rn(__fsub_rn(__fmul_rn(u0, 2.0f), 1.0f), kPi);
+    const float a1 = __fmul_rn(__fsub_rn(__fmul_rn(u1, 2.0f), 1.0f), kPi);
+    const float b0 = __fmul_rn(__fsub_rn(__fmul_rn(v0, 2.0f), 1.0f), kPiOverTwo);
+    const float b1 = __fmul_rn(__fsub_rn(__fmul_rn(v1, 2.0f), 1.0f), kPiOverTwo);
+    const float sb0 = sinf(b0), sb1 = sinf(b1);
+    const float solid = __fmul_rn(__fsub_rn(a1, a0), __fsub_rn(sb1, sb0));
+    const float pdf = __fdiv_rn(prob, 1e-9f < solid ? solid : 1e-9f);
+    const float weight = __fdiv_rn(1.0f, 1e-9f < pdf ? pdf : 1e-9f);
+    const float ta = rng_uniform(r);
+    const float alpha = __fadd_rn(__fmul_rn(a0, __fsub_rn(1.0f, ta)), __fmul_rn(a1, ta));
+    const float ts = rng_uniform(r);
+    float sv = __fadd_rn(__fmul_rn(sb0, __fsub_rn(1.0f, ts)), __fmul_rn(sb1, ts));
+    sv = sv < -1.0f ? -1.0f : sv;
+    sv = 1.0f < sv ? 1.0f : sv;
+    const float beta = asinf(sv);
+    const float rr = cosf(beta);
+    dir[0] = __fmul_rn(sinf(alpha), rr);
+    dir[1] = sinf(beta);
+    dir[2] = __fmul_rn(cosf(alpha), rr);
+    float c[3];
+    environment(e.env, dir, c);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) val[k] = __fmul_rn(c[k], weight);
+}
 
 constexpr int kSafetyT = 16384;   // pbvrt.h / pbvr_nee.h loop cap
 
@@ -305,10 +369,11 @@ __global__ void __launch_bounds__(NT) pbvrt_kernel(const __grid_constant__ Param
     const float* bsm = wsm;
     const int n_out = e.variant == 0 ? 4 : 3;
     float* out_ptr = e.env.out;
-    // the light in object space (L l, each sum rounded in order) and its
-    // slab exit from a point are per ray below
-    float lo[3];
-    to_object(p.L, e.light, lo);
+    // the NEE direction (world, object space) and the weight its term takes:
+    // the directional light of PBVRT / PBVR_NEE (weight 1), or each
+    // collision's environment sample of PBVR_ENV (radiance / pdf)
+    float ld[3] = {e.light[0], e.light[1], e.light[2]}, lo[3], ew[3] = {1.0f, 1.0f, 1.0f};
+    to_object(p.L, ld, lo);
     unsigned long long my_evals = 0;
     long long ray = -1;  // -1: take the next ray; -2: none left
     float x[3] = {0.0f, 0.0f, 0.0f}, w[3] = {0.0f, 0.0f, 1.0f}, wo[3] = {0.0f, 0.0f, 1.0f};
@@ -328,7 +393,7 @@ __global__ void __launch_bounds__(NT) pbvrt_kernel(const __grid_constant__ Param
     };
     // the main loop ended (cap, break): PBVRT resolves the escape term
     auto loop_end = [&]() {
-        if (e.variant == 1) {
+        if (e.variant != 0) {
             store(acc[0], acc[1], acc[2], 0.0f);
             return;
         }
@@ -345,8 +410,9 @@ __global__ void __launch_bounds__(NT) pbvrt_kernel(const __grid_constant__ Param
     // the shadow ray ended with transmittance t: add its NEE term, scatter
     auto shadow_end = [&](float t) {
         const float tr = __fmul_rn(t, phase);
+        // PBVRT / NEE: out += W tr; ENV: out += (tr W) env (ew = 1 for the former)
 #pragma unroll
-        for (int k = 0; k < 3; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(W[k], tr));
+        for (int k = 0; k < 3; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(__fmul_rn(tr, W[k]), ew[k]));
         hg_sample(r, e.g, w);
         to_object(p.L, w, wo);
         d = slab_exit(x, wo);
@@ -477,9 +543,14 @@ __global__ void __launch_bounds__(NT) pbvrt_kernel(const __grid_constant__ Param
             loop_end();
             continue;
         }
-        // next-event estimation toward the light: phase, then the shadow ray
-        const float cos_t = __fadd_rn(__fadd_rn(__fmul_rn(w[0], e.light[0]), __fmul_rn(w[1], e.light[1])),
-                                      __fmul_rn(w[2], e.light[2]));
+        // next-event estimation toward the light (or the environment
+        // sample): phase, then the shadow ray
+        if (e.variant == 2) {
+            env_sample(e, r, ld, ew);
+            to_object(p.L, ld, lo);
+        }
+        const float cos_t = __fadd_rn(__fadd_rn(__fmul_rn(w[0], ld[0]), __fmul_rn(w[1], ld[1])),
+                                      __fmul_rn(w[2], ld[2]));
         phase = hg_eval(cos_t, e.g);
         xs[0] = x[0];
         xs[1] = x[1];

@@ -1818,19 +1818,27 @@ int rdvb_pbvrt(const float* rays, int64_t n_rays, const float* transform, float 
                const int* majorant_dims, int majorant_kind, const float* albedo, float g, int max_bounces,
                const float* light_direction, const float* light_intensity, int variant, int env_kind,
                const float* env_rgb, const float* env_image, const int* env_dims, int env_flags,
-               const uint32_t* seeds, int draws_before, const rdvb_encoding* encoding, int n_layers,
-               const int* dims, const float* const* weights, const float* const* biases, const int* layer_flags,
-               int input_relu, void* workspace, size_t workspace_bytes, float* out, void* stream) {
+               const float* env_densities, int env_levels, const uint32_t* seeds, int draws_before,
+               const rdvb_encoding* encoding, int n_layers, const int* dims, const float* const* weights,
+               const float* const* biases, const int* layer_flags, int input_relu, void* workspace,
+               size_t workspace_bytes, float* out, void* stream) {
     rdvb::trm::Params p;
     if (int rc = tracking_params(rays, n_rays, transform, majorant, majorant_dims, majorant_kind, seeds, draws_before,
                                  encoding, n_layers, dims, weights, biases, layer_flags, input_relu, workspace,
                                  workspace_bytes,
                                  out, p, 3))
         return rc;
-    if (variant != RDVB_PBVRT && variant != RDVB_PBVR_NEE)
-        return fail(RDVB_ERR_INVALID_ARG, "variant must be RDVB_PBVRT or RDVB_PBVR_NEE, got %d", variant);
-    if (!albedo || !light_direction || (variant == RDVB_PBVRT && !light_intensity))
-        return fail(RDVB_ERR_INVALID_ARG, "albedo, light_direction and (PBVRT) light_intensity must not be NULL");
+    if (variant != RDVB_PBVRT && variant != RDVB_PBVR_NEE && variant != RDVB_PBVR_ENV)
+        return fail(RDVB_ERR_INVALID_ARG, "variant must be RDVB_PBVRT, RDVB_PBVR_NEE or RDVB_PBVR_ENV, got %d",
+                    variant);
+    const bool env_nee = variant == RDVB_PBVR_ENV;
+    if (!albedo || (!env_nee && !light_direction) || (variant == RDVB_PBVRT && !light_intensity))
+        return fail(RDVB_ERR_INVALID_ARG, "albedo, light_direction (PBVRT, NEE) and light_intensity (PBVRT) must "
+                                          "not be NULL");
+    if (env_nee && (env_levels < 1 || env_levels > 12))
+        return fail(RDVB_ERR_INVALID_ARG, "env_levels must be in [1, 12], got %d", env_levels);
+    if (env_nee && n_rays > 0 && (!env_densities || !aligned(env_densities, 4)))
+        return fail(RDVB_ERR_INVALID_ARG, "env_densities must be a 4-byte aligned device pointer");
     if (max_bounces < 0) return fail(RDVB_ERR_INVALID_ARG, "max_bounces must be >= 0, got %d", max_bounces);
     if (!std::isfinite(g) || !std::isfinite(density_scale))
         return fail(RDVB_ERR_INVALID_ARG, "g and density_scale must be finite");
@@ -1840,17 +1848,24 @@ int rdvb_pbvrt(const float* rays, int64_t n_rays, const float* transform, float 
     e.g = g;
     e.density_scale = density_scale;
     e.max_bounces = max_bounces;
-    e.variant = variant == RDVB_PBVRT ? 0 : 1;
-    // normalize(light_direction) = l / length(l), length = sqrt((x x + y y) + z z)
-    const float l0 = light_direction[0], l1 = light_direction[1], l2 = light_direction[2];
-    const float sq = (l0 * l0 + l1 * l1) + l2 * l2;
-    const float len = std::sqrt(sq);
-    if (!(len > 0.0f) || !std::isfinite(len)) return fail(RDVB_ERR_INVALID_ARG, "light_direction must be a finite nonzero vector");
-    e.light[0] = l0 / len;
-    e.light[1] = l1 / len;
-    e.light[2] = l2 / len;
+    e.variant = variant == RDVB_PBVRT ? 0 : (variant == RDVB_PBVR_NEE ? 1 : 2);
+    if (!env_nee) {
+        // normalize(light_direction) = l / length(l), length = sqrt((x x + y y) + z z)
+        const float l0 = light_direction[0], l1 = light_direction[1], l2 = light_direction[2];
+        const float sq = (l0 * l0 + l1 * l1) + l2 * l2;
+        const float len = std::sqrt(sq);
+        if (!(len > 0.0f) || !std::isfinite(len))
+            return fail(RDVB_ERR_INVALID_ARG, "light_direction must be a finite nonzero vector");
+        e.light[0] = l0 / len;
+        e.light[1] = l1 / len;
+        e.light[2] = l2 / len;
+    } else {
+        e.light[1] = 1.0f;  // unused: every NEE direction is sampled
+        e.densities = env_densities;
+        e.levels = env_levels;
+    }
     for (int k = 0; k < 3; ++k) e.intensity[k] = variant == RDVB_PBVRT ? light_intensity[k] : 0.0f;
-    if (variant == RDVB_PBVRT) {
+    if (variant != RDVB_PBVR_NEE) {
         if (int rc = environment_args(env_kind, env_rgb, env_image, env_dims, env_flags, n_rays, e.env)) return rc;
     }
     if (n_rays == 0) return RDVB_OK;

@@ -412,6 +412,12 @@ class _PBVRLight(RaymarchingTransmittance):
             env_kind, env_rgb, env_img, env_dims, env_flags = _environment_args(self.environment, dev)
         else:
             env_kind, env_rgb, env_img, env_dims, env_flags = N.RDVB_ENV_CONSTANT, [0.0, 0.0, 0.0], None, [0, 0], 0
+        dens, levels = None, 0
+        sampler = getattr(self, "environment_sampler", None)
+        if sampler is not None:
+            dens, levels = sampler.densities, sampler.levels
+            if dens.device != dev:
+                dens = dens.to(dev)
         seeds = _draw_seeds() if seeds is None else tuple(int(v) for v in seeds)
         assert len(seeds) == 4, "seeds must be 4 integers"
         self.last_seeds = seeds
@@ -424,7 +430,8 @@ class _PBVRLight(RaymarchingTransmittance):
                 N.int_array(gdims), kind, N.float_array(self.albedo), self.g, self.max_bounces,
                 N.float_array(self.light_direction), N.float_array(self.light_intensity), self._variant, env_kind,
                 N.float_array(env_rgb), env_img.data_ptr() if env_img is not None else None, N.int_array(env_dims),
-                env_flags, N.uint32_array(seeds), int(draws_before), _enc_arg(st), n, N.int_array(st["dims"]),
+                env_flags, dens.data_ptr() if dens is not None else None, levels, N.uint32_array(seeds),
+                int(draws_before), _enc_arg(st), n, N.int_array(st["dims"]),
                 N.ptr_array([w.data_ptr() for w in st["W"]]), N.ptr_array([b.data_ptr() for b in st["b"]]),
                 N.int_array(st["flags"]), st["input_relu"], st["ws"].data_ptr(), st["ws"].numel(), out.data_ptr(),
                 stream_handle()), "rdvb_pbvrt")
@@ -471,3 +478,105 @@ class PBVR_NEE(_PBVRLight):
                  max_bounces: int = 32) -> None:
         super().__init__(extinction, majorant, scattering_albedo, transform, light_direction, density_scale, g,
                          max_bounces)
+
+
+def _xr_quadtree(image: torch.Tensor, levels: int) -> torch.Tensor:
+    """The XREnvironmentSampler's quadtree (the layout of
+    rdv/domain/rendering.py:175-278): the image resampled to 2^levels x
+    2^levels cell centres by the GridSampler (clamp, not aligned, linear,
+    rdvb_grid_sampler), its channels summed, each row weighted by the solid
+    angle sin(beta1) - sin(beta0) of its band of the equirectangular
+    parametrisation, normalised to 1; then per depth d and node (Morton
+    order: child c = 2 row bit + column bit, node 4 n + 1 + c) the
+    cumulative probabilities of its 4 children (0.25 each under an empty
+    parent), the last forced to 1. Returns a flat fp32 tensor of
+    4 (4^levels - 1) / 3 values on the image's device."""
+    assert 1 <= levels <= 12, "levels must be in [1, 12]"
+    dev = image.device
+    res = 1 << levels
+    idx = torch.arange(res, dtype=torch.float32, device=dev)
+    c = (idx + 0.5) / res * 2 - 1                         # RegularGrid cell centres (mode 1)
+    yy, xx = torch.meshgrid(c, c, indexing="ij")
+    pts = torch.stack([xx, yy], -1).reshape(-1, 2).contiguous()
+    img = image.to(torch.float32).contiguous()
+    resized = torch.empty(res * res, img.shape[-1], dtype=torch.float32, device=dev)
+    GridSampler(img, clamp=True, aligned=False, linear=True)._sample(pts, resized)
+    resized = resized.reshape(res, res, -1).cpu()
+    dens = resized[..., 0].clone()
+    for k in range(1, resized.shape[-1]):
+        dens = dens + resized[..., k]
+    dens = dens.clamp_min(0)
+    v0 = torch.arange(res, dtype=torch.float32) / res
+    v1 = (torch.arange(res, dtype=torch.float32) + 1) / res
+    half_pi = torch.tensor(3.14159265358979 / 2, dtype=torch.float32)
+    w_row = torch.sin((v1 * 2 - 1) * half_pi) - torch.sin((v0 * 2 - 1) * half_pi)
+    dens = (dens * w_row[:, None]).clamp_min(0)
+    dens = dens / dens.sum().clamp_min(1e-12)
+    pyramid = [dens]
+    for _ in range(levels):
+        g = pyramid[-1]
+        pyramid.append(g.reshape(g.shape[0] // 2, 2, g.shape[1] // 2, 2).sum(dim=(1, 3)))
+    pyramid.reverse()                                     # pyramid[d]: 2^d x 2^d
+
+    def morton(t, d):
+        if d == 0:
+            return t.reshape(1)
+        bits = t.reshape([2] * (2 * d))                   # row bits, then column bits (MSB first)
+        order = [a for i in range(d) for a in (i, d + i)]
+        return bits.permute(order).reshape(-1)
+
+    parts = []
+    for d in range(levels):
+        parent = morton(pyramid[d], d)
+        kids = morton(pyramid[d + 1], d + 1).reshape(-1, 4)
+        p = torch.where(parent[:, None] > 1e-12, kids / parent.clamp_min(1e-12)[:, None],
+                        torch.full_like(kids, 0.25))
+        cum = torch.cumsum(p, dim=1)
+        cum[:, 3] = 1.0
+        parts.append(cum.reshape(-1))
+    return torch.cat(parts).to(dev).contiguous()
+
+
+class XREnvironmentSampler:
+    """Map[6, 3 + 3 + 1] (rdv/domain/rendering.py:281-323,
+    rdv/shaders/rendering/xr_environment_sampler.h): importance-samples a
+    world direction from an equirectangular environment by a quadtree of
+    its solid-angle-weighted pixel densities (built once here from
+    ``image``); returns the direction, the environment there divided by the
+    pdf, and the pdf. ``environment`` is the Map[3, 3] looked up at the
+    sampled direction (``XRProject() >> TensorSampler(image)`` or a
+    ``Constant``); ``image`` [H, W, C] the data the densities come from.
+    Evaluated inside PBVR_ENV's kernel."""
+
+    IN = 6
+    OUT = 7
+
+    def __init__(self, environment: Map, image, levels: int = 8) -> None:
+        env = environment._bind(in_size=3, out_size=3) if environment.__is_generic__ else environment
+        assert env.IN == 3 and env.OUT == 3, "environment must be a Map[3, 3]"
+        self.environment = env
+        self.levels = int(levels)
+        img = image._tensor if isinstance(image, RDVObject) else torch.as_tensor(image)
+        if img.device.type != "cuda":
+            img = img.to(current_device())
+        self.densities = _xr_quadtree(img, self.levels)
+
+
+class PBVR_ENV(_PBVRLight):
+    """Map[6, 3]: ray -> the next-event-estimation sum of delta tracking
+    where each real collision's NEE direction is importance-sampled from the
+    environment (rdv/domain/volumes.py:445-502,
+    rdv/shaders/volumes/pbvr_env.h): throughput * shadow transmittance *
+    phase * environment / pdf. ``environment_sampler`` an
+    ``XREnvironmentSampler``; other arguments as PBVR_NEE (rdvb_pbvrt)."""
+
+    OUT = 3
+    _variant = N.RDVB_PBVR_ENV
+
+    def __init__(self, extinction: Map, majorant, scattering_albedo, environment_sampler, transform=None,
+                 density_scale: float = 1.0, g: float = 0.0, max_bounces: int = 32) -> None:
+        assert isinstance(environment_sampler, XREnvironmentSampler), \
+            "environment_sampler must be an XREnvironmentSampler"
+        super().__init__(extinction, majorant, scattering_albedo, transform, (0.0, 1.0, 0.0), density_scale, g,
+                         max_bounces, environment=environment_sampler.environment)
+        self.environment_sampler = environment_sampler

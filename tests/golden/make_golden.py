@@ -348,13 +348,28 @@ def pbvr_goldens():
                       ptr(light_dir), ptr(light_int), ctypes.c_float(g), ctypes.c_float(dsc), int(mb), ptr(seeds),
                       ptr(rays), n, ptr(dst))
         t_out[k, :, :dst.shape[1]] = dst
+    # PBVR_ENV: an XREnvironmentSampler quadtree (4 levels, from a skewed
+    # density image) over the constant environment; (field kind, g, max
+    # bounces, density scale)
+    e_levels = 4
+    e_image = (rng.uniform(0, 1, (1 << e_levels, 1 << e_levels)) ** 4).astype(np.float32)
+    from oracle.raymarch import xr_quadtree
+    e_tree = xr_quadtree(e_image, e_levels).astype(np.float32)
+    e_cases = [(0, 0.0, 32, 1.0), (1, 0.5, 4, 0.7)]
+    e_out = np.zeros((len(e_cases), n, 3), np.float32)
+    for k, (kind, g, mb, dsc) in enumerate(e_cases):
+        grid = vox if kind == 0 else sph
+        lib.ref_pbvr_env(ctypes.c_float(c0), ctypes.c_float(c1), int(kind), ptr(grid), D, H, W, ptr(env),
+                         ptr(identity), ptr(np.array((0.9, 0.8, 0.7), np.float32)), ptr(e_tree), e_levels,
+                         ctypes.c_float(g), ctypes.c_float(dsc), int(mb), ptr(seeds), ptr(rays), n, ptr(e_out[k]))
     t_params = np.array([[c[0], c[1], c[2], c[4], c[5], c[6]] for c in t_cases], np.float32)
     t_albedo = np.array([c[3] for c in t_cases], np.float32)
     np.savez_compressed(os.path.join(HERE, "pbvr.npz"), rays=rays, seeds=seeds, c0=c0, c1=c1, vox=vox, sph=sph,
                         env=env, kinds=kinds, g=gs, albedo=albedos, max_bounces=bounces, transforms=transforms,
                         out=out, hg_g=hg_g, hg_w=hg_w, hg_index=hg_index, hg_draws_before=np.int32(3),
                         hg_out=hg_out, t_params=t_params, t_albedo=t_albedo, t_transforms=np.stack([identity, scaled]),
-                        t_light_dir=light_dir, t_light_int=light_int, t_out=t_out)
+                        t_light_dir=light_dir, t_light_int=light_int, t_out=t_out, e_levels=np.int32(e_levels),
+                        e_image=e_image, e_tree=e_tree, e_params=np.array(e_cases, np.float32), e_out=e_out)
 
 
 GRID_CASES = ((1, 3, (7,)), (2, 3, (5, 9)), (3, 3, (4, 5, 6)), (4, 3, (3, 4, 2, 5)), (3, 5, (2, 3, 1)))

@@ -240,12 +240,12 @@ def test_pbvrt_validation(lib):
                               N.float_array(albedo) if albedo else None, g, mb,
                               N.float_array(light) if light else None, N.float_array(intensity) if intensity else None,
                               variant, 0, N.float_array([1, 1, 1]), None, N.int_array([1, 1]), 0,
-                              N.uint32_array([1, 2, 3, 4]), 0, None, 2, N.int_array([3, 16, 1]), N.ptr_array([1, 1]),
+                              None, 0, N.uint32_array([1, 2, 3, 4]), 0, None, 2, N.int_array([3, 16, 1]), N.ptr_array([1, 1]),
                               N.ptr_array([1, 1]), N.int_array([1, 1]), 0, None, 256, None, None)
 
     assert call() == 0
     assert call(variant=N.RDVB_PBVR_NEE, intensity=None) == 0     # NEE reads no light intensity
-    for kw, msg in ((dict(variant=2), "variant"), (dict(albedo=None), "albedo"), (dict(light=None), "light"),
+    for kw, msg in ((dict(variant=3), "variant"), (dict(albedo=None), "albedo"), (dict(light=None), "light"),
                     (dict(intensity=None), "light_intensity"), (dict(mb=-1), "max_bounces"),
                     (dict(scale=float("inf")), "finite"), (dict(light=(0, 0, 0)), "nonzero")):
         assert call(**kw) == -1 and msg in N.last_error(), (kw, N.last_error())
@@ -278,3 +278,17 @@ def test_extinction_encoding_validation(lib):
     assert rm(e, 0, [1]) == -1 and "encoding dims" in N.last_error()
     e.dims[1], e.flags = 8, 16
     assert rm(e, 0, [1]) == -1 and "flag" in N.last_error()
+
+
+def test_pbvr_env_validation(lib):
+    import rdv_project_b200._native as N
+
+    def call(levels=4, dens=None, n=0):
+        return lib.rdvb_pbvrt(None, n, None, 1.0, None, N.int_array([2, 2, 2]), 0, N.float_array([1, 1, 1]), 0.0, 4,
+                              None, None, N.RDVB_PBVR_ENV, 0, N.float_array([1, 1, 1]), None, N.int_array([1, 1]), 0,
+                              dens, levels, N.uint32_array([1, 2, 3, 4]), 0, None, 2, N.int_array([3, 16, 1]),
+                              N.ptr_array([1, 1]), N.ptr_array([1, 1]), N.int_array([1, 1]), 0, None, 256, None, None)
+
+    assert call() == 0                                      # no light direction or intensity needed
+    assert call(levels=0) == -1 and "env_levels" in N.last_error()
+    assert call(levels=13) == -1 and "env_levels" in N.last_error()

@@ -438,3 +438,52 @@ def test_pbvrt_and_nee_restatement_bit_exact_vs_reference(golden, k):
     np.testing.assert_array_equal(got, ref)
     if int(var) == 0:
         assert set(np.unique(ref[:, 3])) <= {0.0, 1.0}
+
+
+@pytest.mark.parametrize("k", range(2))
+def test_pbvr_env_restatement_bit_exact_vs_reference(golden, k):
+    """PBVR_ENV.forward (volumes/pbvr_env.h) with the XREnvironmentSampler
+    (rendering/xr_environment_sampler.h) of the oracle against the
+    reference's own bodies, on the fixture's quadtree: bit for bit."""
+    g = golden("pbvr.npz")
+    kind, gg, mb, dsc = g["e_params"][k]
+    c0, c1 = np.float32(g["c0"]), np.float32(g["c1"])
+
+    def ext(p):
+        return (c0 + c1 * ((p[:, 0] * p[:, 0] + p[:, 1] * p[:, 1]) + p[:, 2] * p[:, 2])).astype(np.float32)
+
+    field = (lambda x, w: orm.voxel_majorant(g["vox"], x, w)) if int(kind) == 0 else \
+        (lambda x, w: orm.sphere_majorant(g["sph"], x, w))
+    rays = g["rays"]
+    got = orm.pbvrt(rays[:, :3], rays[:, 3:], ext, field, g["seeds"], (0.9, 0.8, 0.7), None,
+                    environment=orm.constant_environment(g["env"]), density_scale=float(dsc), g=float(gg),
+                    max_bounces=int(mb), variant="env", env_densities=g["e_tree"], env_levels=int(g["e_levels"]))
+    np.testing.assert_array_equal(got, g["e_out"][k])
+    assert (got.sum(1) > 0).mean() > 0.5
+
+
+def test_xr_quadtree_layout():
+    """The quadtree of rendering.py:175-278: 4 (4^L - 1) / 3 values,
+    cumulative per node (non-decreasing, the last exactly 1), and the
+    product of the chosen children's probabilities along each leaf's path
+    equal to that leaf's normalised, solid-angle-weighted mass."""
+    rng = np.random.default_rng(3)
+    levels = 3
+    img = rng.uniform(0, 1, (8, 8)) ** 3
+    tree = orm.xr_quadtree(img, levels)
+    assert tree.size == 4 * (4 ** levels - 1) // 3
+    cum = tree.reshape(-1, 4)
+    assert np.all(np.diff(cum, axis=1) >= -1e-15) and np.all(cum[:, 3] == 1.0)
+    res = 1 << levels
+    w = np.sin(((np.arange(res) + 1) / res * 2 - 1) * np.pi / 2) - np.sin((np.arange(res) / res * 2 - 1) * np.pi / 2)
+    mass = img * w[:, None]
+    mass = mass / mass.sum()
+    for row in range(res):
+        for col in range(res):
+            node, prob = 0, 1.0
+            for d in range(levels - 1, -1, -1):
+                c = 2 * ((row >> d) & 1) + ((col >> d) & 1)
+                cdf = tree[node * 4:node * 4 + 4]
+                prob *= cdf[c] - (cdf[c - 1] if c else 0.0)
+                node = node * 4 + 1 + c
+            assert abs(prob - mass[row, col]) <= 1e-12
