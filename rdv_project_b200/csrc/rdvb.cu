@@ -1135,7 +1135,7 @@ int check_rows_channels(const void* a, const void* b, int c) {
 }  // namespace
 
 int rdvb_tensor_sampler(const float* t, int in_dim, const int* shape, int out_dim, const float* x, int64_t n,
-                        int clamp, int aligned, int linear, float* y, void* stream) {
+                        int clamp, int aligned_centres, int linear, float* y, void* stream) {
     if (in_dim < 1 || in_dim > 3) return fail(RDVB_ERR_UNSUPPORTED, "in_dim must be 1, 2 or 3 (got %d)", in_dim);
     if (!shape) return fail(RDVB_ERR_INVALID_ARG, "shape must not be NULL");
     for (int d = 0; d < in_dim; ++d)
@@ -1155,12 +1155,30 @@ int rdvb_tensor_sampler(const float* t, int in_dim, const int* shape, int out_di
     p.out = out_dim;
     for (int d = 0; d < in_dim; ++d) p.dim[d] = shape[d];
     p.clamp = clamp ? 1 : 0;
-    p.aligned = aligned ? 1 : 0;
+    p.aligned = aligned_centres ? 1 : 0;
     p.linear = linear ? 1 : 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (in_dim == 3 && out_dim % 4 == 0 && aligned(t, 16) && aligned(y, 16)) {
+        rdvb::sampler::GridParams q;
+        memset(&q, 0, sizeof(q));
+        q.t = t;
+        q.x = x;
+        q.y = y;
+        q.n = n;
+        q.out = out_dim;
+        for (int d = 0; d < 3; ++d) q.dim[d] = shape[d];
+        q.clamp = p.clamp;
+        q.aligned = p.aligned;
+        q.linear = p.linear;
+        const long long items = n * (out_dim / 4);
+        const int vb = static_cast<int>(std::max<long long>(1, std::min<long long>((items + 255) / 256,
+                                                                                 dev->sm_count * 16LL)));
+        rdvb::sampler::sampler3_vec4_kernel<false><<<vb, 256, 0, st>>>(q);
+        return check_launch("sampler3_vec4_kernel");
+    }
     const long long total = n * out_dim;
     const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + 255) / 256,
                                                                                dev->sm_count * 16LL)));
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (in_dim == 1) rdvb::sampler::tensor_sampler_kernel<1><<<blocks, 256, 0, st>>>(p);
     else if (in_dim == 2) rdvb::sampler::tensor_sampler_kernel<2><<<blocks, 256, 0, st>>>(p);
     else rdvb::sampler::tensor_sampler_kernel<3><<<blocks, 256, 0, st>>>(p);
@@ -1196,10 +1214,17 @@ int rdvb_grid_sampler(const float* grid, int in_dim, const int* shape, int out_d
     p.clamp = clamp ? 1 : 0;
     p.aligned = aligned_centres ? 1 : 0;
     p.linear = linear ? 1 : 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (in_dim == 3 && out_dim % 4 == 0 && aligned(grid, 16) && aligned(y, 16)) {
+        const long long items = n * (out_dim / 4);
+        const int vb = static_cast<int>(std::max<long long>(1, std::min<long long>((items + 255) / 256,
+                                                                                 dev->sm_count * 16LL)));
+        rdvb::sampler::sampler3_vec4_kernel<true><<<vb, 256, 0, st>>>(p);
+        return check_launch("sampler3_vec4_kernel");
+    }
     const long long total = n * out_dim;
     const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((total + 255) / 256,
                                                                                dev->sm_count * 16LL)));
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (in_dim) {
         case 1: rdvb::sampler::grid_sampler_kernel<1><<<blocks, 256, 0, st>>>(p); break;
         case 2: rdvb::sampler::grid_sampler_kernel<2><<<blocks, 256, 0, st>>>(p); break;

@@ -238,6 +238,152 @@ __device__ __forceinline__ float grid_sample(const float* __restrict__ t, const 
     return v;
 }
 
+// Four consecutive channels k0..k0+3 of a 3-D sampler at x in one pass
+// (16-byte loads: out % 4 == 0 and t 16-byte aligned), each channel with
+// exactly the arithmetic of tensor_sample<3> / grid_sample<3> (used by
+// sampler3_vec4_kernel below).
+__device__ __forceinline__ float4 f4_fma_lerp(float4 l, float4 r, float xw) {
+    const float omx = __fsub_rn(1.0f, xw);
+    return make_float4(__fadd_rn(__fmul_rn(l.x, omx), __fmul_rn(r.x, xw)),
+                       __fadd_rn(__fmul_rn(l.y, omx), __fmul_rn(r.y, xw)),
+                       __fadd_rn(__fmul_rn(l.z, omx), __fmul_rn(r.z, xw)),
+                       __fadd_rn(__fmul_rn(l.w, omx), __fmul_rn(r.w, xw)));
+}
+__device__ __forceinline__ float4 f4_add_scaled(float4 d, float s, float4 v) {
+    return make_float4(__fadd_rn(d.x, __fmul_rn(s, v.x)), __fadd_rn(d.y, __fmul_rn(s, v.y)),
+                       __fadd_rn(d.z, __fmul_rn(s, v.z)), __fadd_rn(d.w, __fmul_rn(s, v.w)));
+}
+// blend of a loaded pair for 4 channels: dst + rest mix(l, r, xw), or a
+// single side, or nothing (blend_pair's cases)
+__device__ __forceinline__ float4 blend_loaded4(float4 l, float4 r, bool left_in, bool right_in, float xw, float rest,
+                                                float4 dst) {
+    if (left_in && right_in) return f4_add_scaled(dst, rest, f4_fma_lerp(l, r, xw));
+    if (left_in) return f4_add_scaled(dst, __fmul_rn(rest, __fsub_rn(1.0f, xw)), l);
+    if (right_in) return f4_add_scaled(dst, __fmul_rn(rest, xw), r);
+    return dst;
+}
+
+// The 8 corner loads are issued before any blending (they are independent;
+// the clamped corner indices are always inside the tensor, and a corner
+// that does not count is loaded and then skipped).
+__device__ __forceinline__ float4 tensor_sample3_4(const float* __restrict__ t, const int* dim, int out, int k0,
+                                                   const float* x, bool border, bool aligned, bool linear) {
+    const float ac = aligned ? 1.0f : 0.0f;
+    int lo[3], clo[3], chi[3];
+    float alpha[3];
+    bool lo_in[3], hi_in[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) coord(x[2 - d], dim[d], ac, border, lo[d], clo[d], chi[d], alpha[d], lo_in[d], hi_in[d]);
+    const long long st2 = out, st1 = st2 * dim[2], st0 = st1 * dim[1];
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (!linear) {
+        bool inside = true;
+        long long off = k0;
+        const long long st[3] = {st0, st1, st2};
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            int id = lo[d] + (alpha[d] >= 0.5f ? 1 : 0);
+            inside = inside && id >= 0 && id < dim[d];
+            id = min(max(id, 0), dim[d] - 1);
+            off += id * st[d];
+        }
+        return (border || inside) ? __ldg(reinterpret_cast<const float4*>(t + off)) : v;
+    }
+    const long long dl = static_cast<long long>(chi[2] - clo[2]) * st2;
+    const long long p00 = clo[0] * st0 + clo[1] * st1 + clo[2] * st2 + k0;
+    const long long d0 = static_cast<long long>(chi[0] - clo[0]) * st0;
+    const long long d1 = static_cast<long long>(chi[1] - clo[1]) * st1;
+    // the pairs in the reference's order: (lo, lo), (lo, hi), (hi, hi), (hi, lo) of dims 0 and 1
+    const long long base[4] = {p00, p00 + d1, p00 + d1 + d0, p00 + d0};
+    float4 l[4], r[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        l[q] = __ldg(reinterpret_cast<const float4*>(t + base[q]));
+        r[q] = __ldg(reinterpret_cast<const float4*>(t + base[q] + dl));
+    }
+    const float a0 = alpha[0], a1 = alpha[1];
+    v = blend_loaded4(l[0], r[0], lo_in[0] && lo_in[1] && lo_in[2], lo_in[0] && lo_in[1] && hi_in[2], alpha[2],
+                      __fmul_rn(__fsub_rn(1.0f, a0), __fsub_rn(1.0f, a1)), v);
+    v = blend_loaded4(l[1], r[1], lo_in[0] && hi_in[1] && lo_in[2], lo_in[0] && hi_in[1] && hi_in[2], alpha[2],
+                      __fmul_rn(__fsub_rn(1.0f, a0), a1), v);
+    v = blend_loaded4(l[2], r[2], hi_in[0] && hi_in[1] && lo_in[2], hi_in[0] && hi_in[1] && hi_in[2], alpha[2],
+                      __fmul_rn(a0, a1), v);
+    v = blend_loaded4(l[3], r[3], hi_in[0] && lo_in[1] && lo_in[2], hi_in[0] && lo_in[1] && hi_in[2], alpha[2],
+                      __fmul_rn(a0, __fsub_rn(1.0f, a1)), v);
+    return v;
+}
+
+__device__ __forceinline__ float4 grid_sample3_4(const float* __restrict__ t, const int* dim, int out, int k0,
+                                                 const float* x, bool clamp, bool aligned, bool linear) {
+    int voxel[3];
+    float alpha[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+        const float tc = __fadd_rn(__fmul_rn(x[2 - d], 0.5f), 0.5f);
+        const float pos = aligned ? __fmul_rn(tc, static_cast<float>(dim[d] - 1))
+                                  : __fsub_rn(__fmul_rn(tc, static_cast<float>(dim[d])), 0.5f);
+        const float fv = floorf(pos);
+        voxel[d] = static_cast<int>(fv);
+        alpha[d] = __fsub_rn(pos, fv);
+    }
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (!linear) {
+        bool inside = true;
+        long long off = 0;
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            int c = voxel[d] + (alpha[d] >= 0.5f ? 1 : 0);
+            if (clamp) c = min(max(c, 0), dim[d] - 1);
+            inside = inside && c >= 0 && c < dim[d];
+            off = off * dim[d] + c;
+        }
+        return (clamp || inside) ? __ldg(reinterpret_cast<const float4*>(t + off * out + k0)) : v;
+    }
+    float4 val[8];
+    bool use[8];
+#pragma unroll
+    for (int bits = 0; bits < 8; ++bits) {
+        bool inside = true;
+        long long off = 0;
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            const int c = voxel[d] + ((bits >> d) & 1);
+            inside = inside && c >= 0 && c < dim[d];
+            off = off * dim[d] + min(max(c, 0), dim[d] - 1);  // clamped: a valid address either way
+        }
+        use[bits] = clamp || inside;
+        val[bits] = __ldg(reinterpret_cast<const float4*>(t + off * out + k0));
+    }
+#pragma unroll
+    for (int bits = 0; bits < 8; ++bits) {
+        float w = 1.0f;
+#pragma unroll
+        for (int d = 0; d < 3; ++d) w = __fmul_rn(w, ((bits >> d) & 1) ? alpha[d] : __fsub_rn(1.0f, alpha[d]));
+        if (use[bits]) v = f4_add_scaled(v, w, val[bits]);
+    }
+    return v;
+}
+
+// 3-D samplers with out % 4 == 0 (16-byte aligned tensor and output): one
+// thread per (point, 4 channels), the corner indices and weights computed
+// once per 4 channels and 16-byte gathers -- the same per-channel
+// arithmetic as the kernels above (tensor_sample3_4 / grid_sample3_4).
+template <bool GRID>
+__global__ void sampler3_vec4_kernel(const __grid_constant__ GridParams p) {
+    const int quads = p.out >> 2;
+    const long long total = p.n * quads;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long i = idx / quads;
+        const int k0 = static_cast<int>(idx - i * quads) * 4;
+        const float x[3] = {__ldg(p.x + i * 3), __ldg(p.x + i * 3 + 1), __ldg(p.x + i * 3 + 2)};
+        const float4 v = GRID ? grid_sample3_4(p.t, p.dim, p.out, k0, x, p.clamp != 0, p.aligned != 0, p.linear != 0)
+                              : tensor_sample3_4(p.t, p.dim, p.out, k0, x, p.clamp != 0, p.aligned != 0,
+                                                 p.linear != 0);
+        *reinterpret_cast<float4*>(p.y + i * p.out + k0) = v;
+    }
+}
+
 template <int IN>
 __global__ void grid_sampler_kernel(const __grid_constant__ GridParams p) {
     const long long total = p.n * p.out;

@@ -133,3 +133,32 @@ def test_grid_sampler_feeds_fused_mlp(rdv, cuda_device):
     assert nw <= 1e-2 and el <= 1e-2, (nw, el)
     empty = rdv.GridSampler(torch.from_numpy(grid).to(cuda_device))(torch.zeros(0, 3, device=cuda_device))
     assert tuple(empty.as_tensor("torch").shape) == (0, 16)
+
+
+@pytest.mark.parametrize("entry", ["rdvb_grid_sampler", "rdvb_tensor_sampler"])
+@pytest.mark.parametrize("flags", [(1, 0, 1), (0, 1, 1), (0, 0, 0), (1, 1, 0)])
+def test_vec4_sampler_kernel_matches_per_channel_kernel(rdv, cuda_device, entry, flags):
+    """3-D samplers with out % 4 == 0 and 16-byte aligned operands run the
+    4-channel kernel (one thread per point and 4 channels, 16-byte corner
+    loads); an output 4 bytes off alignment takes the per-channel kernel.
+    Both restate the same per-channel arithmetic: equal bit for bit."""
+    import rdv_project_b200._native as N
+    clamp, aligned, linear = flags
+    g = torch.Generator().manual_seed(sum(flags) + len(entry))
+    grid = torch.randn(11, 7, 13, 12, generator=g).to(cuda_device)
+    n = 30001
+    x = (torch.rand(n, 3, generator=g) * 2.6 - 1.3).to(cuda_device)
+    shape = N.int_array([11, 7, 13])
+    fast = torch.empty(n, 12, device=cuda_device)
+    slow_buf = torch.empty(n * 12 + 1, device=cuda_device)
+    slow = slow_buf[1:].view(n, 12)
+    fn = getattr(N.lib(), entry)
+    for y in (fast, slow):
+        N.check(fn(grid.data_ptr(), 3, shape, 12, x.data_ptr(), n, clamp, aligned, linear, y.data_ptr(),
+                   torch.cuda.current_stream().cuda_stream), entry)
+    torch.cuda.synchronize()
+    assert torch.equal(fast, slow)
+    ref = (oten.grid_sampler if entry == "rdvb_grid_sampler" else oten.tensor_sampler)(
+        grid.cpu().numpy(), x.cpu().numpy(), bool(clamp), bool(aligned), bool(linear))
+    nw, el = omlp.rel_errors(fast.cpu().numpy(), ref)
+    assert nw <= 1e-5 and el <= 1e-5, (nw, el)
