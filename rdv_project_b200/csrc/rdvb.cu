@@ -61,8 +61,8 @@ struct DeviceInfo {
     size_t rt_wide_smem_set = 0;
     size_t pbvr_smem_set = 0;
     size_t pbvr_wide_smem_set = 0;
-    size_t pbvrt_smem_set = 0;
-    size_t pbvrt_wide_smem_set = 0;
+    size_t pbvrt_smem_set[3] = {};       // per variant
+    size_t pbvrt_wide_smem_set[3] = {};
     size_t rows_smem_set = 0;
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
@@ -1551,12 +1551,21 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
             smem_set = wide ? &dev->pbvr_wide_smem_set : &dev->pbvr_smem_set;
             name = "pbvr_kernel";
             break;
-        case March::kPbvrt:
-            kernel = wide ? reinterpret_cast<const void*>(rdvb::pbvr::pbvrt_kernel<kRtWideThreads>)
-                          : reinterpret_cast<const void*>(rdvb::pbvr::pbvrt_kernel<kThreads>);
-            smem_set = wide ? &dev->pbvrt_wide_smem_set : &dev->pbvrt_smem_set;
+        case March::kPbvrt: {
+            using rdvb::pbvr::pbvrt_kernel;
+            const int v = static_cast<const rdvb::pbvr::ExtraT*>(extra)->variant;
+            const void* const kernels[2][3] = {
+                {reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 0>),
+                 reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 1>),
+                 reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 2>)},
+                {reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 0>),
+                 reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 1>),
+                 reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 2>)}};
+            kernel = kernels[wide ? 1 : 0][v];
+            smem_set = wide ? &dev->pbvrt_wide_smem_set[v] : &dev->pbvrt_smem_set[v];
             name = "pbvrt_kernel";
             break;
+        }
     }
     if (*smem_set < smem) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
