@@ -74,6 +74,7 @@ def test_linearfast_chain_matches_oracle(rdv, cuda_device, dims, n_rows):
     y = m(rdv.wrap(torch.from_numpy(x).to(cuda_device))).as_tensor("torch").cpu().numpy()
     ref = omlp.mlp_forward(x, layers, tail_exact=True)
     _check(y, ref, TOL_F16, TIGHT_F16)
+    assert rdv.device_status() == 0
     n_full = (n_rows // 32) * 32
     if n_full < n_rows:
         # the trailing partial 32-row group is exact fp32, like the reference
@@ -264,3 +265,32 @@ def test_fp16_tensor_ops_vs_reference_coopmat(rdv, cuda_device, golden, cls_name
     g = golden("coopmat.npz")
     op = getattr(rdv, cls_name)(*(torch.from_numpy(g[f"{key}_{t}"]).to(cuda_device) for t in ("x", "W", "b")))
     _check(op.as_type("torch").cpu().numpy(), g[f"{key}_y"], TOL_F16, TIGHT_F16)
+
+
+@pytest.mark.parametrize("dims,math_,x_dtype,input_relu", [
+    ([3, 64, 64, 64, 64, 4], "f16", torch.float32, False),
+    ([4, 32, 16], "bf16", torch.float32, True),
+    ([2, 128, 64, 8], "f16", torch.float16, False),
+    ([1, 64, 4], "bf16", torch.bfloat16, False),
+])
+def test_narrow_inputs_dtypes_and_input_relu(rdv, cuda_device, dims, math_, x_dtype, input_relu):
+    """Chains of 1-4 inputs (layer 0 a single K = 16 step), float16 and
+    bfloat16 operands, float16 / bfloat16 input tensors and a leading ReLU,
+    over several rounds per CTA with a partial last tile: within the float16
+    tolerance of the oracle, device status clean."""
+    layers = _layers(dims, math_, seed=len(dims) + dims[0])
+    n_rows = 128 * (148 * 4 * 3 + 11) + 64
+    rng = np.random.default_rng(dims[0])
+    x = rng.standard_normal((n_rows, dims[0])).astype(np.float32)
+    xt = torch.from_numpy(x).to(cuda_device).to(x_dtype)
+    m = _build(rdv, layers, cuda_device)
+    if input_relu:
+        m = rdv.relu >> m
+    y = m(rdv.wrap(xt)).as_tensor("torch").cpu().numpy()
+    xs = xt.float().cpu().numpy()
+    if input_relu:
+        xs = np.maximum(xs, 0.0)
+    sel = np.arange(0, n_rows, 7)
+    ref = omlp.mlp_forward(xs[sel], layers)
+    _check(y[sel], ref, TOL_F16, TIGHT_F16)
+    assert rdv.device_status() == 0
