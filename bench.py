@@ -312,7 +312,7 @@ def run_reference(args, spec, world, rank):
 def run_ours(args, spec, world, rank, local):
     import rdv_project_b200 as rdv
     from rdv_project_b200 import _native as N
-    from rdv_project_b200.sharding import piece_bounds, sharded_map_overlapped
+    from rdv_project_b200.sharding import PeerBuffer, piece_bounds, sharded_map_overlapped, sharded_map_p2p
 
     dev = torch.device("cuda", torch.cuda.current_device())
     layers = make_weights(spec)
@@ -322,6 +322,7 @@ def run_ours(args, spec, world, rank, local):
     out_dim = spec["dims"][-1]
     chunks = args.chunks if args.chunks else (8 if world > 1 else 1)
     reserve = args.reserve_ctas if world > 1 else 0
+    p2p = sharded and world > 1 and args.gather == "p2p"
     if sharded:
         n = spec["rows"]
         x_host = make_input(spec, n, seed=0)
@@ -333,11 +334,14 @@ def run_ours(args, spec, world, rank, local):
         pieces = [(0, n)]
         rows_rank = n
     x_dev = x_host.to(dev)
-    y_all = torch.empty(n, out_dim, device=dev)
+    peer_buf = PeerBuffer(n, out_dim) if p2p else None
+    y_all = peer_buf.tensor if p2p else torch.empty(n, out_dim, device=dev)
     stream = torch.cuda.current_stream()
 
     def step():
-        if sharded:
+        if p2p:
+            sharded_map_p2p(m, x_dev, peer_buf, chunks=chunks)
+        elif sharded:
             sharded_map_overlapped(m, x_dev, out=y_all, chunks=chunks, reserve_ctas=reserve)
         else:
             rdv.maps.evaluate_into(m, x_dev, y_all)
@@ -418,6 +422,8 @@ def run_ours(args, spec, world, rank, local):
         torch.cuda.synchronize()
         t_e2e = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world)
 
+    if peer_buf is not None:
+        peer_buf.close()  # collective: every rank, before rank 0 reports
     if rank != 0:
         return
     units_per_step = (n if sharded else n * world) * n_layers
@@ -447,8 +453,10 @@ def run_ours(args, spec, world, rank, local):
         "parity": {"rows": 2048, "normwise": parity[0], "elementwise": parity[1]},
         "clocks": clocks,
     }
-    if sharded and world > 1:
-        line["overlap"] = {"chunks": chunks, "reserve_ctas": reserve}
+    if p2p:
+        line["overlap"] = {"gather": "p2p: copy engines into peer-mapped buffers, slab by slab", "chunks": chunks}
+    elif sharded and world > 1:
+        line["overlap"] = {"gather": "nccl", "chunks": chunks, "reserve_ctas": reserve}
     if world == 1 and not args.profile_run:
         line["cpu_baseline"] = cpu_baseline(spec, layers)
         if not args.no_secondary:
@@ -1207,6 +1215,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c5", "c2", "c1", "c3", "c4", "trm"], default="c5")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="config 5 at N > 1: p2p = slabs whose rows are copied into every rank's mapped buffer by "
+                         "the copy engines over NVLink while the next slab computes; nccl = slabs with overlapped "
+                         "NCCL all-gathers")
     ap.add_argument("--chunks", type=int, default=0,
                     help="slabs of the sharded config-5 step (default 8 at N > 1, 1 at N = 1)")
     ap.add_argument("--reserve-ctas", type=int, default=16,

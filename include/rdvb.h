@@ -142,6 +142,27 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
                      const float* const* weights, const float* const* biases, const int* layer_flags,
                      int input_relu, int tail_exact, const void* packed, float* y, void* stream);
 
+/* The exchange step of a sharded evaluation (B200 extension: the reference
+ * runs Map.__call__, rdv/maths/__init__.py:1451-1487, on one device):
+ * `bytes` from src to each of dst[0..n_dst) on `stream`, one
+ * cudaMemcpyAsync per destination (n_dst 0..7). dst are other GPUs'
+ * buffers mapped by rdvb_ipc_open, so the copies run on the copy engines
+ * over NVLink and leave every SM to the kernels they overlap. The caller
+ * orders the step with a cross-GPU barrier before any rank reads rows it
+ * did not compute. */
+int rdvb_peer_copy(const void* src, void* const* dst, int n_dst, int64_t bytes, void* stream);
+
+/* Buffers other processes on this node can map (the output buffers of a
+ * sharded evaluation, filled by rdvb_peer_copy). rdvb_ipc_alloc: `bytes` of device memory on the
+ * current device and its RDVB_IPC_HANDLE_BYTES-byte handle, to pass to the
+ * other ranks; rdvb_ipc_free releases it. rdvb_ipc_open: another process's
+ * buffer mapped into this one (peer access enabled); rdvb_ipc_close unmaps. */
+#define RDVB_IPC_HANDLE_BYTES 64
+int rdvb_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+int rdvb_ipc_free(void* ptr);
+int rdvb_ipc_open(const void* handle, void** ptr);
+int rdvb_ipc_close(void* ptr);
+
 /* Which kernel rdvb_mlp_forward runs for these arguments (no reference
  * counterpart: the reference picks between its fp16 and fp32 paths inside the
  * shader, linear_fast.h:44,102-108). Returns RDVB_PATH_TENSOR_CORE when its

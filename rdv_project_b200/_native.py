@@ -26,6 +26,8 @@ RDVB_ENV_CONSTANT, RDVB_ENV_EQUIRECT = 0, 1
 RDVB_SAMPLER_CLAMP, RDVB_SAMPLER_ALIGNED, RDVB_SAMPLER_LINEAR = 1, 2, 4
 RDVB_PBVRT, RDVB_PBVR_NEE, RDVB_PBVR_ENV = 0, 1, 2
 RDVB_ENCODING_TENSOR_SAMPLER, RDVB_ENCODING_GRID_SAMPLER = 1, 2
+RDVB_IPC_HANDLE_BYTES = 64
+RDVB_MAX_PEERS = 7
 
 _c_int, _c_i64, _vp, _c_u32, _c_f = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float
 
@@ -38,6 +40,11 @@ SIGNATURES = {
     "rdvb_mlp_packed_bytes": (_c_i64, [_c_int, _vp]),
     "rdvb_mlp_pack": (_c_int, [_c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),
     "rdvb_mlp_forward": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp]),
+    "rdvb_peer_copy": (_c_int, [_vp, _vp, _c_int, _c_i64, _vp]),
+    "rdvb_ipc_alloc": (_c_int, [_c_i64, ctypes.POINTER(_vp), _vp]),
+    "rdvb_ipc_free": (_c_int, [_vp]),
+    "rdvb_ipc_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "rdvb_ipc_close": (_c_int, [_vp]),
     "rdvb_mlp_static_capacity": (_c_i64, []),
     "rdvb_mlp_forward_static": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp]),
     "rdvb_mlp_forward_path": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp]),

@@ -577,6 +577,67 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
                            st, dev);
 }
 
+constexpr int kMaxPeers = 7;  // peer buffers per rdvb_peer_copy call (8 GPUs per node)
+
+int rdvb_peer_copy(const void* src, void* const* dst, int n_dst, int64_t bytes, void* stream) {
+    if (n_dst < 0 || n_dst > kMaxPeers)
+        return fail(RDVB_ERR_INVALID_ARG, "n_dst must be 0..%d, got %d", kMaxPeers, n_dst);
+    if (bytes < 0) return fail(RDVB_ERR_INVALID_ARG, "bytes must be >= 0");
+    if (bytes == 0 || n_dst == 0) return RDVB_OK;
+    if (!src || !dst) return fail(RDVB_ERR_INVALID_ARG, "src and dst must not be NULL");
+    for (int k = 0; k < n_dst; ++k) {
+        if (!dst[k]) return fail(RDVB_ERR_INVALID_ARG, "dst[%d] is NULL", k);
+        // one copy per destination (a peer GPU's memory, mapped by rdvb_ipc_open)
+        cudaError_t e = cudaMemcpyAsync(dst[k], src, static_cast<size_t>(bytes), cudaMemcpyDeviceToDevice,
+                                        static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMemcpyAsync to peer %d: %s", k, cudaGetErrorString(e));
+    }
+    return RDVB_OK;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == RDVB_IPC_HANDLE_BYTES, "IPC handle size");
+
+int rdvb_ipc_alloc(int64_t bytes, void** ptr, void* handle) {
+    if (bytes <= 0 || !ptr || !handle) return fail(RDVB_ERR_INVALID_ARG, "bytes > 0, ptr and handle are required");
+    *ptr = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaMalloc(%lld): %s", (long long)bytes, cudaGetErrorString(e));
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(RDVB_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    }
+    memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return RDVB_OK;
+}
+
+int rdvb_ipc_free(void* ptr) {
+    if (!ptr) return RDVB_OK;
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? RDVB_OK : fail(RDVB_ERR_CUDA, "cudaFree: %s", cudaGetErrorString(e));
+}
+
+int rdvb_ipc_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return fail(RDVB_ERR_INVALID_ARG, "handle and ptr are required");
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fail(RDVB_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+    *ptr = p;
+    return RDVB_OK;
+}
+
+int rdvb_ipc_close(void* ptr) {
+    if (!ptr) return RDVB_OK;
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? RDVB_OK : fail(RDVB_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+}
+
 int rdvb_mlp_forward_path(const void* x, int x_dtype, int64_t n_rows, int n_layers, const int* dims,
                           const int* layer_flags, const void* packed, const float* y) {
     if (int rc = check_chain(n_layers, dims, layer_flags)) return rc;

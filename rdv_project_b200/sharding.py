@@ -4,17 +4,23 @@ range with no cross-rank traffic, and one all-gather of the results at the
 end (NCCL over NVLink on GPUs; gloo in the CPU tests).
 
 The reference has no multi-device execution at all; this is the B200
-scale-out of its data-parallel operators. Nothing here touches device
-memory of another GPU: each rank's kernels read only local tensors, and the
-exchange is a library collective.
+scale-out of its data-parallel operators. Kernels read only local tensors.
 
-``sharded_map_overlapped`` is the pipelined form used for large batches: the
+``sharded_map_p2p`` does the exchange without NCCL: the output buffers
+(``PeerBuffer``) are mapped into every rank's process, and each rank copies
+the rows it computed into all of them with the copy engines over NVLink,
+slab by slab, while the next slab's kernel runs on every SM; a one-element
+all-reduce orders the step.
+
+``sharded_map_overlapped`` is the pipelined library-collective form: the
 rows are cut into slabs, every slab is split evenly over the ranks, and the
-all-gather of slab k runs (on NCCL's stream) while slab k + 1 computes.
-Given pinned host buffers it also streams its input in and its rows out on
-copy streams, overlapping PCIe with the kernels.
+NCCL all-gather of slab k runs (on NCCL's stream) while slab k + 1
+computes. Given pinned host buffers it also streams its input in and its
+rows out on copy streams, overlapping PCIe with the kernels.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -265,3 +271,157 @@ def sharded_map_overlapped(m, x: torch.Tensor | None = None, *, group=None, out:
         if h2d is not None:
             comp.wait_stream(h2d)
     return out
+
+
+class _DeviceArray:
+    """A raw device allocation seen as an array (__cuda_array_interface__),
+    so torch.as_tensor wraps it without a copy."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerBuffer:
+    """An [n, cols] fp32 buffer on every rank of `group`, each rank's buffer
+    mapped into every other rank's process (CUDA IPC over NVLink), so a
+    rank can copy rows straight into all of them: the output of
+    ``sharded_map_p2p``. Collective to create (every rank of the group
+    calls it with the same n and cols); ``close()`` (also collective) unmaps
+    and frees.
+
+    ``tensor``: this rank's buffer as a torch tensor; ``peer_ptrs``: the
+    device addresses of the other ranks' buffers in this process, in rank
+    order without this rank."""
+
+    def __init__(self, n: int, cols: int, group=None):
+        import torch.distributed as dist
+
+        from . import _native as N
+
+        self.group = group
+        self.rank, self.world = _rank_world(group)
+        if self.world - 1 > N.RDVB_MAX_PEERS:
+            raise ValueError(f"at most {N.RDVB_MAX_PEERS + 1} ranks share a PeerBuffer, got {self.world}")
+        self.n, self.cols = int(n), int(cols)
+        lib = N.lib()
+        nbytes = max(1, self.n * self.cols) * 4
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * N.RDVB_IPC_HANDLE_BYTES)()
+        N.check(lib.rdvb_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "rdvb_ipc_alloc")
+        self._ptr = int(ptr.value)
+        self._opened = []
+        self.tensor = torch.as_tensor(_DeviceArray(self._ptr, (self.n, self.cols)), device="cuda")
+        mine = bytes(handle)
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, mine, group=group)
+        else:
+            handles = [mine]
+        self.peer_ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                continue
+            hb = (ctypes.c_ubyte * N.RDVB_IPC_HANDLE_BYTES).from_buffer_copy(h)
+            pp = ctypes.c_void_p()
+            N.check(lib.rdvb_ipc_open(hb, ctypes.byref(pp)), "rdvb_ipc_open")
+            self._opened.append(int(pp.value))
+            self.peer_ptrs.append(int(pp.value))
+
+    def rows_of_peers(self, begin: int) -> list[int]:
+        """The peers' addresses of row `begin` (same offset as in this rank's buffer)."""
+        off = int(begin) * self.cols * 4
+        return [p + off for p in self.peer_ptrs]
+
+    def close(self) -> None:
+        """Collective: every rank unmaps the others' buffers, waits for the
+        group, then frees its own."""
+        import torch.distributed as dist
+
+        from . import _native as N
+
+        if self._ptr is None:
+            return
+        torch.cuda.synchronize()
+        for p in self._opened:
+            N.check(N.lib().rdvb_ipc_close(p), "rdvb_ipc_close")
+        self._opened = []
+        self.peer_ptrs = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.tensor = None
+        N.check(N.lib().rdvb_ipc_free(self._ptr), "rdvb_ipc_free")
+        self._ptr = None
+
+
+def sharded_map_p2p(m, x: torch.Tensor, buf: PeerBuffer, group=None, chunks: int = 8, align: int = 128,
+                    evaluate=None) -> torch.Tensor:
+    """Map `m` over the n rows of `x` (the full batch on this rank's device;
+    a rank reads only its rows), split over the ranks of `group`, every rank
+    ending with the full [n, OUT] result in ``buf.tensor``.
+
+    The rows are cut into `chunks` slabs (``slab_bounds``). Each rank
+    evaluates its piece of slab k into its own buffer with every SM, then
+    copies those rows into every peer's buffer on a copy stream
+    (``rdvb_peer_copy``: one cudaMemcpyAsync per peer, the copy engines over
+    NVLink into memory the peers mapped to this process) while slab k + 1
+    computes. A one-element all-reduce on the compute stream, after the last
+    copy, orders the step: no rank reads another rank's rows before they
+    landed. Unlike an NCCL all-gather this takes no SM from the kernels.
+    `evaluate(x_piece, y_piece)` replaces the map evaluation (default
+    ``maps.evaluate_into``)."""
+    import torch.distributed as dist
+
+    from . import _native as N
+
+    if evaluate is None:
+        from .maps import evaluate_into
+
+        def evaluate(xs, ys):
+            evaluate_into(m, xs, ys)
+
+    rank, world = _rank_world(group)
+    n = x.shape[0]
+    if buf.n != n:
+        raise ValueError(f"the buffer holds {buf.n} rows, the input {n}")
+    out = buf.tensor
+    comp = torch.cuda.current_stream(out.device)
+    cs = _copy_stream(out.device) if world > 1 else None
+    row_bytes = buf.cols * 4
+    for pb, pe in piece_bounds(n, world, rank, chunks, align):
+        if pe <= pb:
+            continue
+        evaluate(x[pb:pe], out[pb:pe])
+        if cs is not None:
+            done = torch.cuda.Event()
+            done.record(comp)
+            cs.wait_event(done)
+            peers = buf.rows_of_peers(pb)
+            N.check(N.lib().rdvb_peer_copy(out[pb:pe].data_ptr(), N.ptr_array(peers), len(peers),
+                                           (pe - pb) * row_bytes, cs.cuda_stream), "rdvb_peer_copy")
+    if world > 1:
+        comp.wait_stream(cs)
+        dist.all_reduce(_barrier_flag(out.device), group=group)
+    return out
+
+
+_copy_streams: dict = {}
+
+
+def _copy_stream(dev) -> torch.cuda.Stream:
+    s = _copy_streams.get(str(dev))
+    if s is None:
+        s = torch.cuda.Stream(dev)
+        _copy_streams[str(dev)] = s
+    return s
+
+
+_flags: dict = {}
+
+
+def _barrier_flag(dev) -> torch.Tensor:
+    t = _flags.get(str(dev))
+    if t is None:
+        t = torch.zeros(1, dtype=torch.float32, device=dev)
+        _flags[str(dev)] = t
+    return t

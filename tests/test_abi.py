@@ -292,3 +292,24 @@ def test_pbvr_env_validation(lib):
     assert call() == 0                                      # no light direction or intensity needed
     assert call(levels=0) == -1 and "env_levels" in N.last_error()
     assert call(levels=13) == -1 and "env_levels" in N.last_error()
+
+
+def test_peer_copy_and_ipc_validation(lib):
+    """The peer copy and the IPC helpers check their arguments before
+    touching a device."""
+    import ctypes
+
+    import rdv_project_b200._native as N
+
+    rc = lib.rdvb_peer_copy(None, None, 9, 16, None)
+    assert rc == -1 and "n_dst" in N.last_error()
+    rc = lib.rdvb_peer_copy(None, None, 1, -1, None)
+    assert rc == -1 and "bytes" in N.last_error()
+    rc = lib.rdvb_peer_copy(None, N.ptr_array([0]), 1, 16, None)
+    assert rc == -1 and "NULL" in N.last_error()
+    assert lib.rdvb_peer_copy(None, None, 0, 16, None) == 0  # nothing to copy
+    ptr = ctypes.c_void_p()
+    assert lib.rdvb_ipc_alloc(0, ctypes.byref(ptr), None) == -1
+    assert lib.rdvb_ipc_open(None, ctypes.byref(ptr)) == -1
+    assert lib.rdvb_ipc_free(None) == 0 and lib.rdvb_ipc_close(None) == 0
+    assert N.RDVB_IPC_HANDLE_BYTES == 64 and N.RDVB_MAX_PEERS == 7
