@@ -322,7 +322,8 @@ def run_ours(args, spec, world, rank, local):
     out_dim = spec["dims"][-1]
     chunks = args.chunks if args.chunks else (8 if world > 1 else 1)
     reserve = args.reserve_ctas if world > 1 else 0
-    p2p = sharded and world > 1 and args.gather == "p2p"
+    gather = args.gather if args.gather != "auto" else ("p2p" if world == 2 else "nccl")
+    p2p = sharded and world > 1 and gather == "p2p"
     if sharded:
         n = spec["rows"]
         x_host = make_input(spec, n, seed=0)
@@ -1215,10 +1216,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c5", "c2", "c1", "c3", "c4", "trm"], default="c5")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+    ap.add_argument("--gather", choices=["auto", "p2p", "nccl"], default="auto",
                     help="config 5 at N > 1: p2p = slabs whose rows are copied into every rank's mapped buffer by "
                          "the copy engines over NVLink while the next slab computes; nccl = slabs with overlapped "
-                         "NCCL all-gathers")
+                         "NCCL all-gathers; auto (default) = p2p on 2 GPUs, nccl on more (measured: 2 B200s "
+                         "2.94 vs 3.20 ms, 8 B200s 3.28 vs 2.15 ms)")
     ap.add_argument("--chunks", type=int, default=0,
                     help="slabs of the sharded config-5 step (default 8 at N > 1, 1 at N = 1)")
     ap.add_argument("--reserve-ctas", type=int, default=16,

@@ -386,34 +386,40 @@ def sharded_map_p2p(m, x: torch.Tensor, buf: PeerBuffer, group=None, chunks: int
         raise ValueError(f"the buffer holds {buf.n} rows, the input {n}")
     out = buf.tensor
     comp = torch.cuda.current_stream(out.device)
-    cs = _copy_stream(out.device) if world > 1 else None
+    # the peers split over up to 4 copy streams, so several copy engines
+    # send at once (one stream would queue the copies to 7 peers)
+    n_cs = min(len(buf.peer_ptrs), 4)
+    streams = _copy_streams(out.device, n_cs)
     row_bytes = buf.cols * 4
     for pb, pe in piece_bounds(n, world, rank, chunks, align):
         if pe <= pb:
             continue
         evaluate(x[pb:pe], out[pb:pe])
-        if cs is not None:
+        if streams:
             done = torch.cuda.Event()
             done.record(comp)
-            cs.wait_event(done)
             peers = buf.rows_of_peers(pb)
-            N.check(N.lib().rdvb_peer_copy(out[pb:pe].data_ptr(), N.ptr_array(peers), len(peers),
-                                           (pe - pb) * row_bytes, cs.cuda_stream), "rdvb_peer_copy")
-    if world > 1:
+            for j, cs in enumerate(streams):
+                mine = peers[j::n_cs]
+                cs.wait_event(done)
+                N.check(N.lib().rdvb_peer_copy(out[pb:pe].data_ptr(), N.ptr_array(mine), len(mine),
+                                               (pe - pb) * row_bytes, cs.cuda_stream), "rdvb_peer_copy")
+    for cs in streams:
         comp.wait_stream(cs)
+    if world > 1:
         dist.all_reduce(_barrier_flag(out.device), group=group)
     return out
 
 
-_copy_streams: dict = {}
+_streams: dict = {}
 
 
-def _copy_stream(dev) -> torch.cuda.Stream:
-    s = _copy_streams.get(str(dev))
-    if s is None:
-        s = torch.cuda.Stream(dev)
-        _copy_streams[str(dev)] = s
-    return s
+def _copy_streams(dev, k: int) -> list:
+    """k side streams of `dev` (created once, reused)."""
+    have = _streams.setdefault(str(dev), [])
+    while len(have) < k:
+        have.append(torch.cuda.Stream(dev))
+    return have[:k]
 
 
 _flags: dict = {}
