@@ -355,7 +355,7 @@ class PeerBuffer:
 
 
 def sharded_map_p2p(m, x: torch.Tensor, buf: PeerBuffer, group=None, chunks: int = 8, align: int = 128,
-                    evaluate=None) -> torch.Tensor:
+                    evaluate=None, copy_streams: int = 7) -> torch.Tensor:
     """Map `m` over the n rows of `x` (the full batch on this rank's device;
     a rank reads only its rows), split over the ranks of `group`, every rank
     ending with the full [n, OUT] result in ``buf.tensor``.
@@ -369,7 +369,8 @@ def sharded_map_p2p(m, x: torch.Tensor, buf: PeerBuffer, group=None, chunks: int
     copy, orders the step: no rank reads another rank's rows before they
     landed. Unlike an NCCL all-gather this takes no SM from the kernels.
     `evaluate(x_piece, y_piece)` replaces the map evaluation (default
-    ``maps.evaluate_into``)."""
+    ``maps.evaluate_into``). The peers are split over `copy_streams` side
+    streams (at most one per peer)."""
     import torch.distributed as dist
 
     from . import _native as N
@@ -386,9 +387,9 @@ def sharded_map_p2p(m, x: torch.Tensor, buf: PeerBuffer, group=None, chunks: int
         raise ValueError(f"the buffer holds {buf.n} rows, the input {n}")
     out = buf.tensor
     comp = torch.cuda.current_stream(out.device)
-    # the peers split over up to 4 copy streams, so several copy engines
+    # the peers split over several copy streams, so several copy engines
     # send at once (one stream would queue the copies to 7 peers)
-    n_cs = min(len(buf.peer_ptrs), 4)
+    n_cs = max(1, min(len(buf.peer_ptrs), copy_streams)) if buf.peer_ptrs else 0
     streams = _copy_streams(out.device, n_cs)
     row_bytes = buf.cols * 4
     for pb, pe in piece_bounds(n, world, rank, chunks, align):
