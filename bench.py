@@ -321,8 +321,9 @@ def run_ours(args, spec, world, rank, local):
     sharded = spec["name"] == "c5"
     out_dim = spec["dims"][-1]
     chunks = args.chunks if args.chunks else (8 if world > 1 else 1)
-    reserve = (args.reserve_ctas if args.reserve_ctas >= 0 else (16 if world <= 2 else 32)) if world > 1 else 0
-    gather = args.gather if args.gather != "auto" else ("p2p" if world == 2 else "nccl")
+    auto_reserve = 16 if world <= 2 else (32 if world <= 4 else 48)
+    reserve = (args.reserve_ctas if args.reserve_ctas >= 0 else auto_reserve) if world > 1 else 0
+    gather = args.gather if args.gather != "auto" else ("p2p" if world <= 4 else "nccl")
     p2p = sharded and world > 1 and gather == "p2p"
     if sharded:
         n = spec["rows"]
@@ -1219,14 +1220,15 @@ def main():
     ap.add_argument("--gather", choices=["auto", "p2p", "nccl"], default="auto",
                     help="config 5 at N > 1: p2p = slabs whose rows are copied into every rank's mapped buffer by "
                          "the copy engines over NVLink while the next slab computes; nccl = slabs with overlapped "
-                         "NCCL all-gathers; auto (default) = p2p on 2 GPUs, nccl on more (measured: 2 B200s "
-                         "2.94 vs 3.20 ms, 8 B200s 3.28 vs 2.15 ms)")
+                         "NCCL all-gathers; auto (default) = p2p on 2 and 4 GPUs, nccl on 8 (measured ms per step, "
+                         "p2p vs nccl: 2 B200s 2.94 vs 3.20, 4: 2.10 vs 2.14, 8: 2.62 vs 1.85)")
     ap.add_argument("--chunks", type=int, default=0,
                     help="slabs of the sharded config-5 step (default 8 at N > 1, 1 at N = 1)")
     ap.add_argument("--reserve-ctas", type=int, default=-1,
                     help="SMs left free of the persistent MLP kernel for the overlapped NCCL all-gather (N > 1); "
-                         "default 16 on 2 GPUs, 32 on more (measured on 8 B200s: 2.13 ms with 16, 2.00 with 32; "
-                         "on 2: 3.19 with 16, 3.58 with 32)")
+                         "default 16 on 2 GPUs, 32 on 4, 48 on 8 (measured ms per step, 8 slabs: 2 B200s 3.19 "
+                         "with 16, 3.58 with 32; 4: 2.33 / 2.25 / 2.14 / 2.19 with 16 / 24 / 32 / 48; 8: 2.13 / "
+                         "1.98 / 1.85 / 1.98 with 16 / 32 / 48 / 64)")
     ap.add_argument("--e2e-chunks", type=int, default=16,
                     help="pieces of the end-to-end leg's host-streaming pipeline")
     ap.add_argument("--rows", type=int, default=None,
