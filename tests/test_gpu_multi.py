@@ -39,3 +39,36 @@ def test_peer_copy_gather_matches_nccl_gather():
         assert c["status"] == 0, c
         tol = 1e-5 if c["math"] == "f32" else 1e-2
         assert c["normwise"] <= tol and c["elementwise"] <= tol, c
+
+
+def test_single_rank_peer_buffer_and_peer_copy(cuda_device):
+    """One process: PeerBuffer allocates through rdvb_ipc_alloc (no peers to
+    map), sharded_map_p2p over one rank equals the map itself bit for bit,
+    and rdvb_peer_copy sends a buffer to two destinations."""
+    import rdv_project_b200 as rdv
+    import rdv_project_b200._native as N
+    from rdv_project_b200.sharding import PeerBuffer, sharded_map_p2p
+
+    g = torch.Generator().manual_seed(4)
+    dims = [3, 64, 64, 4]
+    m = None
+    for i in range(3):
+        f = rdv.LinearFast((torch.randn(dims[i + 1], dims[i], generator=g) * 0.5).to(cuda_device),
+                           (torch.randn(dims[i + 1], generator=g) * 0.1).to(cuda_device))
+        m = f if m is None else m >> f
+        if i < 2:
+            m = m >> rdv.relu
+    n = 100_003
+    x = (torch.rand(n, 3, generator=g) * 2 - 1).to(cuda_device)
+    buf = PeerBuffer(n, 4)
+    assert buf.peer_ptrs == [] and tuple(buf.tensor.shape) == (n, 4)
+    sharded_map_p2p(m, x, buf, chunks=3)
+    want = m(rdv.wrap(x)).as_tensor("torch")
+    assert torch.equal(buf.tensor, want)
+    a, b = torch.empty_like(want), torch.empty_like(want)
+    N.check(N.lib().rdvb_peer_copy(buf.tensor.data_ptr(), N.ptr_array([a.data_ptr(), b.data_ptr()]), 2,
+                                   want.numel() * 4, torch.cuda.current_stream().cuda_stream), "rdvb_peer_copy")
+    torch.cuda.synchronize()
+    assert torch.equal(a, want) and torch.equal(b, want)
+    buf.close()
+    assert rdv.device_status() == 0
