@@ -312,7 +312,8 @@ def run_reference(args, spec, world, rank):
 def run_ours(args, spec, world, rank, local):
     import rdv_project_b200 as rdv
     from rdv_project_b200 import _native as N
-    from rdv_project_b200.sharding import PeerBuffer, piece_bounds, sharded_map_overlapped, sharded_map_p2p
+    from rdv_project_b200.sharding import MulticastBuffer, PeerBuffer, piece_bounds, sharded_map_nvls, \
+        sharded_map_overlapped, sharded_map_p2p
 
     dev = torch.device("cuda", torch.cuda.current_device())
     layers = make_weights(spec)
@@ -323,7 +324,13 @@ def run_ours(args, spec, world, rank, local):
     chunks = args.chunks if args.chunks else (8 if world > 1 else 1)
     auto_reserve = 16 if world <= 2 else (32 if world <= 4 else 48)
     reserve = (args.reserve_ctas if args.reserve_ctas >= 0 else auto_reserve) if world > 1 else 0
-    gather = args.gather if args.gather != "auto" else ("p2p" if world <= 4 else "nccl")
+    gather = args.gather if args.gather != "auto" else ("p2p" if world <= 4 else "nvls")
+    mc_buf = None
+    if sharded and world > 1 and gather == "nvls":
+        try:
+            mc_buf = MulticastBuffer(spec["rows"], out_dim)
+        except RuntimeError:
+            gather = "nccl"  # no NVLink multicast on these GPUs
     p2p = sharded and world > 1 and gather == "p2p"
     if sharded:
         n = spec["rows"]
@@ -337,11 +344,17 @@ def run_ours(args, spec, world, rank, local):
         rows_rank = n
     x_dev = x_host.to(dev)
     peer_buf = PeerBuffer(n, out_dim) if p2p else None
-    y_all = peer_buf.tensor if p2p else torch.empty(n, out_dim, device=dev)
+    if mc_buf is not None:
+        y_all = mc_buf.tensor
+    else:
+        y_all = peer_buf.tensor if p2p else torch.empty(n, out_dim, device=dev)
+    nvls_reserve = args.reserve_ctas if args.reserve_ctas >= 0 else 16
     stream = torch.cuda.current_stream()
 
     def step():
-        if p2p:
+        if mc_buf is not None:
+            sharded_map_nvls(m, x_dev, mc_buf, chunks=chunks, reserve_ctas=nvls_reserve)
+        elif p2p:
             sharded_map_p2p(m, x_dev, peer_buf, chunks=chunks)
         elif sharded:
             sharded_map_overlapped(m, x_dev, out=y_all, chunks=chunks, reserve_ctas=reserve)
@@ -426,6 +439,8 @@ def run_ours(args, spec, world, rank, local):
 
     if peer_buf is not None:
         peer_buf.close()  # collective: every rank, before rank 0 reports
+    if mc_buf is not None:
+        mc_buf.close()
     if rank != 0:
         return
     units_per_step = (n if sharded else n * world) * n_layers
@@ -455,7 +470,10 @@ def run_ours(args, spec, world, rank, local):
         "parity": {"rows": 2048, "normwise": parity[0], "elementwise": parity[1]},
         "clocks": clocks,
     }
-    if p2p:
+    if mc_buf is not None:
+        line["overlap"] = {"gather": "nvls: multimem.st copy kernel into a multicast symmetric buffer, slab by slab",
+                           "chunks": chunks, "reserve_ctas": nvls_reserve}
+    elif p2p:
         line["overlap"] = {"gather": "p2p: copy engines into peer-mapped buffers, slab by slab", "chunks": chunks}
     elif sharded and world > 1:
         line["overlap"] = {"gather": "nccl", "chunks": chunks, "reserve_ctas": reserve}
@@ -1217,11 +1235,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c5", "c2", "c1", "c3", "c4", "trm"], default="c5")
-    ap.add_argument("--gather", choices=["auto", "p2p", "nccl"], default="auto",
+    ap.add_argument("--gather", choices=["auto", "p2p", "nvls", "nccl"], default="auto",
                     help="config 5 at N > 1: p2p = slabs whose rows are copied into every rank's mapped buffer by "
                          "the copy engines over NVLink while the next slab computes; nccl = slabs with overlapped "
-                         "NCCL all-gathers; auto (default) = p2p on 2 and 4 GPUs, nccl on 8 (measured ms per step, "
-                         "p2p vs nccl: 2 B200s 2.94 vs 3.20, 4: 2.10 vs 2.14, 8: 2.62 vs 1.85)")
+                         "NCCL all-gathers; nvls = slabs whose rows a 16-SM copy kernel writes once to the NVLink "
+                         "multicast address of a symmetric buffer (multimem.st); auto (default) = p2p on 2 and 4 "
+                         "GPUs, nvls on 8 (nccl where the GPUs offer no multicast). Measured ms per step: 2 B200s "
+                         "p2p 2.94, nvls 3.21, nccl 3.20; 4: p2p 2.10, nccl 2.14; 8: p2p 2.62, nvls 1.64, nccl 1.85")
     ap.add_argument("--chunks", type=int, default=0,
                     help="slabs of the sharded config-5 step (default 8 at N > 1, 1 at N = 1)")
     ap.add_argument("--reserve-ctas", type=int, default=-1,

@@ -152,6 +152,14 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
  * did not compute. */
 int rdvb_peer_copy(const void* src, void* const* dst, int n_dst, int64_t bytes, void* stream);
 
+/* The same exchange through the NVLink switch: `bytes` (a multiple of 16)
+ * of this GPU's rows at src written once to mc_dst, the multicast (NVLS)
+ * address of the same rows in a symmetric buffer every rank of the group
+ * bound, so the switch delivers them to every GPU. A kernel of at most
+ * max_ctas CTAs (the caller keeps that many SMs free of its other kernels);
+ * the caller orders the step with a cross-GPU barrier after it. */
+int rdvb_multicast_copy(const void* src, uint64_t mc_dst, int64_t bytes, int max_ctas, void* stream);
+
 /* Buffers other processes on this node can map (the output buffers of a
  * sharded evaluation, filled by rdvb_peer_copy). rdvb_ipc_alloc: `bytes` of device memory on the
  * current device and its RDVB_IPC_HANDLE_BYTES-byte handle, to pass to the

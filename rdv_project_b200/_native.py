@@ -41,6 +41,7 @@ SIGNATURES = {
     "rdvb_mlp_pack": (_c_int, [_c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),
     "rdvb_mlp_forward": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp]),
     "rdvb_peer_copy": (_c_int, [_vp, _vp, _c_int, _c_i64, _vp]),
+    "rdvb_multicast_copy": (_c_int, [_vp, ctypes.c_uint64, _c_i64, _c_int, _vp]),
     "rdvb_ipc_alloc": (_c_int, [_c_i64, ctypes.POINTER(_vp), _vp]),
     "rdvb_ipc_free": (_c_int, [_vp]),
     "rdvb_ipc_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),

@@ -19,7 +19,8 @@ LIB_DIR = os.path.join(PKG, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "librdvb.so")
 SOURCES = ["rdvb.cu"]
 HEADERS = ["ptx.cuh", "rng.cuh", "mlp_tc.cuh", "mlp_simt.cuh", "winograd.cuh", "winograd_f43.cuh", "raymarch.cuh", "transmittance.cuh",
-           "resample.cuh", "conv_tc.cuh", "sampler.cuh", "pbvr.cuh"]
+           "resample.cuh", "conv_tc.cuh", "sampler.cuh", "pbvr.cuh",
+           "exchange.cuh"]
 
 
 def nvcc_path() -> str:

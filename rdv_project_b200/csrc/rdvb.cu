@@ -24,6 +24,7 @@
 #include "transmittance.cuh"
 #include "resample.cuh"
 #include "conv_tc.cuh"
+#include "exchange.cuh"
 #include "sampler.cuh"
 #include "pbvr.cuh"
 
@@ -578,6 +579,23 @@ int rdvb_mlp_forward(const void* x, int x_dtype, int64_t n_rows, int n_layers, c
 }
 
 constexpr int kMaxPeers = 7;  // peer buffers per rdvb_peer_copy call (8 GPUs per node)
+
+int rdvb_multicast_copy(const void* src, uint64_t mc_dst, int64_t bytes, int max_ctas, void* stream) {
+    if (bytes < 0 || bytes % 16) return fail(RDVB_ERR_INVALID_ARG, "bytes must be a non-negative multiple of 16");
+    if (bytes == 0) return RDVB_OK;
+    if (!src || !mc_dst) return fail(RDVB_ERR_INVALID_ARG, "src and mc_dst must not be NULL");
+    if (!aligned(src, 16) || mc_dst % 16) return fail(RDVB_ERR_INVALID_ARG, "src and mc_dst must be 16-byte aligned");
+    if (max_ctas < 1) return fail(RDVB_ERR_INVALID_ARG, "max_ctas must be >= 1");
+    DeviceInfo* dev = nullptr;
+    if (int rc = current_device(&dev)) return rc;
+    const long long n16 = bytes / 16;
+    const int threads = 512;
+    const int blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((n16 + threads - 1) / threads,
+                                                                                 max_ctas)));
+    rdvb::exchange::multicast_copy_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(src), mc_dst, n16);
+    return check_launch("multicast_copy_kernel");
+}
 
 int rdvb_peer_copy(const void* src, void* const* dst, int n_dst, int64_t bytes, void* stream) {
     if (n_dst < 0 || n_dst > kMaxPeers)

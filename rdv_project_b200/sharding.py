@@ -432,3 +432,93 @@ def _barrier_flag(dev) -> torch.Tensor:
         t = torch.zeros(1, dtype=torch.float32, device=dev)
         _flags[str(dev)] = t
     return t
+
+
+class MulticastBuffer:
+    """An [n, cols] fp32 buffer on every rank of `group`, allocated as torch
+    symmetric memory and bound to an NVLink multicast (NVLS) object: a store
+    to ``mc_ptr`` + offset reaches every rank's buffer through the switch.
+    Collective to create and to ``close()``. Raises RuntimeError where the
+    GPUs offer no multicast."""
+
+    def __init__(self, n: int, cols: int, group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank, self.world = _rank_world(group)
+        self.n, self.cols = int(n), int(cols)
+        if self.cols % 4:
+            raise ValueError("the multicast exchange moves 16-byte chunks: cols must be a multiple of 4")
+        full = symm.empty(max(1, self.n), self.cols, dtype=torch.float32, device="cuda")
+        self.handle = symm.rendezvous(full, self.group)
+        self.tensor = full[: self.n]
+        mc = int(self.handle.multicast_ptr or 0)
+        if not mc:
+            self.close()
+            raise RuntimeError("these GPUs offer no NVLink multicast (NVLS) for symmetric memory")
+        # the tensor's place in the symmetric allocation, in the multicast mapping
+        self.mc_ptr = mc + (self.tensor.data_ptr() - int(self.handle.buffer_ptrs[self.rank]))
+
+    def close(self) -> None:
+        """Collective: every rank waits for the group, then drops the buffer."""
+        import torch.distributed as dist
+
+        if self.tensor is None:
+            return
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.handle = None
+        self.tensor = None
+
+
+def sharded_map_nvls(m, x: torch.Tensor, buf: MulticastBuffer, group=None, chunks: int = 8, align: int = 128,
+                     reserve_ctas: int = 32, evaluate=None) -> torch.Tensor:
+    """``sharded_map_p2p`` with the exchange through the NVLink switch: after
+    each piece's kernel, a copy kernel of `reserve_ctas` CTAs (the MLP kernel
+    leaves that many SMs free, ``rdvb_set_max_ctas``) writes the piece's rows
+    once to the buffer's multicast address (``rdvb_multicast_copy``,
+    multimem.st) and the switch delivers them to every rank, while the next
+    piece computes. A one-element all-reduce then orders the step."""
+    import torch.distributed as dist
+
+    from . import _native as N
+
+    if evaluate is None:
+        from .maps import evaluate_into
+
+        def evaluate(xs, ys):
+            evaluate_into(m, xs, ys)
+
+    rank, world = _rank_world(group)
+    n = x.shape[0]
+    if buf.n != n:
+        raise ValueError(f"the buffer holds {buf.n} rows, the input {n}")
+    out = buf.tensor
+    comp = torch.cuda.current_stream(out.device)
+    cs = _copy_streams(out.device, 1)[0] if world > 1 else None
+    row_bytes = buf.cols * 4
+    prev_cap = None
+    if cs is not None and reserve_ctas > 0:
+        sms = torch.cuda.get_device_properties(out.device).multi_processor_count
+        prev_cap = N.set_max_ctas(max(1, sms - reserve_ctas))
+    try:
+        for pb, pe in piece_bounds(n, world, rank, chunks, align):
+            if pe <= pb:
+                continue
+            evaluate(x[pb:pe], out[pb:pe])
+            if cs is not None:
+                done = torch.cuda.Event()
+                done.record(comp)
+                cs.wait_event(done)
+                N.check(N.lib().rdvb_multicast_copy(out[pb:pe].data_ptr(), buf.mc_ptr + pb * row_bytes,
+                                                    (pe - pb) * row_bytes, max(1, reserve_ctas), cs.cuda_stream),
+                        "rdvb_multicast_copy")
+    finally:
+        if prev_cap is not None:
+            N.set_max_ctas(prev_cap)
+    if cs is not None:
+        comp.wait_stream(cs)
+        dist.all_reduce(_barrier_flag(out.device), group=group)
+    return out

@@ -4,7 +4,9 @@ output buffer (PeerBuffer) and evaluates its pieces of the slabs, copying
 each piece into every peer's buffer with the copy engines
 (sharding.sharded_map_p2p); the gathered result must equal, bit for bit, the
 same pieces evaluated and gathered by NCCL (sharding.sharded_map_overlapped),
-and agree with the oracle on sampled rows. Rank 0 prints one JSON line."""
+and agree with the oracle on sampled rows. Where the GPUs offer NVLink
+multicast, the exchange through the switch (sharding.sharded_map_nvls) must
+equal it too. Rank 0 prints one JSON line."""
 import datetime
 import json
 import os
@@ -49,7 +51,8 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     import rdv_project_b200 as rdv
     from oracle import mlp as omlp
-    from rdv_project_b200.sharding import PeerBuffer, sharded_map_overlapped, sharded_map_p2p
+    from rdv_project_b200.sharding import MulticastBuffer, PeerBuffer, sharded_map_nvls, sharded_map_overlapped, \
+        sharded_map_p2p
 
     out = []
     for ci, (dims, math, n) in enumerate(CASES):
@@ -69,10 +72,25 @@ def main():
         sel = np.arange(0, n, max(1, n // 2000))
         nw, el = omlp.rel_errors(got[0][torch.from_numpy(sel).to(dev)].cpu().numpy(),
                                  omlp.mlp_forward(x.cpu().numpy()[sel], layers, tail_exact=True))
-        out.append({"dims": dims, "math": math, "rows": n, "equal_nccl": bool(torch.equal(got[0], ref)),
-                    "equal_again": bool(torch.equal(got[0], got[1])), "finite": bool(torch.isfinite(got[0]).all()),
-                    "normwise": float(nw), "elementwise": float(el), "status": int(rdv.device_status())})
+        rec = {"dims": dims, "math": math, "rows": n, "equal_nccl": bool(torch.equal(got[0], ref)),
+               "equal_again": bool(torch.equal(got[0], got[1])), "finite": bool(torch.isfinite(got[0]).all()),
+               "normwise": float(nw), "elementwise": float(el), "status": int(rdv.device_status())}
         buf.close()
+        if dims[-1] % 4 == 0:
+            # the same through the NVLink switch (multimem.st), where the GPUs offer multicast
+            try:
+                mb = MulticastBuffer(n, dims[-1])
+            except RuntimeError:
+                mb = None
+            if mb is not None:
+                mb.tensor.fill_(float("nan"))
+                dist.barrier()
+                sharded_map_nvls(m, x, mb, chunks=4, reserve_ctas=16)
+                torch.cuda.synchronize()
+                rec["nvls_equal_nccl"] = bool(torch.equal(mb.tensor, ref))
+                rec["status"] = max(rec["status"], int(rdv.device_status()))
+                mb.close()
+        out.append(rec)
     if rank == 0:
         print(json.dumps({"world": world, "cases": out}), flush=True)
     dist.barrier()

@@ -313,3 +313,13 @@ def test_peer_copy_and_ipc_validation(lib):
     assert lib.rdvb_ipc_open(None, ctypes.byref(ptr)) == -1
     assert lib.rdvb_ipc_free(None) == 0 and lib.rdvb_ipc_close(None) == 0
     assert N.RDVB_IPC_HANDLE_BYTES == 64 and N.RDVB_MAX_PEERS == 7
+
+
+def test_multicast_copy_validation(lib):
+    import rdv_project_b200._native as N
+
+    rc = lib.rdvb_multicast_copy(None, 0, 24, 16, None)
+    assert rc == -1 and "multiple of 16" in N.last_error()
+    rc = lib.rdvb_multicast_copy(None, 0, 32, 16, None)
+    assert rc == -1 and "NULL" in N.last_error()
+    assert lib.rdvb_multicast_copy(None, 0, 0, 16, None) == 0

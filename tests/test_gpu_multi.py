@@ -36,6 +36,7 @@ def test_peer_copy_gather_matches_nccl_gather():
     assert rep["world"] == world
     for c in rep["cases"]:
         assert c["equal_nccl"] and c["equal_again"] and c["finite"], c
+        assert c.get("nvls_equal_nccl", True), c
         assert c["status"] == 0, c
         tol = 1e-5 if c["math"] == "f32" else 1e-2
         assert c["normwise"] <= tol and c["elementwise"] <= tol, c
