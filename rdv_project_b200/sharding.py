@@ -1,7 +1,8 @@
 """Multi-GPU sharding of the hot path: one process per GPU, the batch (MLP
 rows, image row bands) split into contiguous ranges, each rank computing its
-range with no cross-rank traffic, and one all-gather of the results at the
-end (NCCL over NVLink on GPUs; gloo in the CPU tests).
+range with no cross-rank traffic, and one all-gather of the results (NCCL
+over NVLink, the copy engines, or NVLink multicast stores on GPUs; gloo in
+the CPU tests).
 
 The reference has no multi-device execution at all; this is the B200
 scale-out of its data-parallel operators. Kernels read only local tensors.
@@ -10,7 +11,10 @@ scale-out of its data-parallel operators. Kernels read only local tensors.
 (``PeerBuffer``) are mapped into every rank's process, and each rank copies
 the rows it computed into all of them with the copy engines over NVLink,
 slab by slab, while the next slab's kernel runs on every SM; a one-element
-all-reduce orders the step.
+all-reduce orders the step. ``sharded_map_nvls`` sends each rank's rows once,
+through the NVLink switch: a small copy kernel stores them to the multicast
+address of a symmetric buffer (``MulticastBuffer``) and the switch delivers
+them to every rank.
 
 ``sharded_map_overlapped`` is the pipelined library-collective form: the
 rows are cut into slabs, every slab is split evenly over the ranks, and the
