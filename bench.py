@@ -329,8 +329,18 @@ def run_ours(args, spec, world, rank, local):
     if sharded and world > 1 and gather == "nvls":
         try:
             mc_buf = MulticastBuffer(spec["rows"], out_dim)
-        except RuntimeError:
-            gather = "nccl"  # no NVLink multicast on these GPUs
+        except Exception:  # no NVLink multicast (or no symmetric memory) on these GPUs
+            mc_buf = None
+        # every rank takes the same exchange: NCCL unless all have the buffer
+        import torch.distributed as dist
+
+        ok = torch.tensor([1.0 if mc_buf is not None else 0.0], device=torch.device("cuda", local))
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if ok.item() < 1.0:
+            if mc_buf is not None:
+                mc_buf.close()
+            mc_buf = None
+            gather = "nccl"
     p2p = sharded and world > 1 and gather == "p2p"
     if sharded:
         n = spec["rows"]

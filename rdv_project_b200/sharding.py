@@ -442,8 +442,8 @@ class MulticastBuffer:
     """An [n, cols] fp32 buffer on every rank of `group`, allocated as torch
     symmetric memory and bound to an NVLink multicast (NVLS) object: a store
     to ``mc_ptr`` + offset reaches every rank's buffer through the switch.
-    Collective to create and to ``close()``. Raises RuntimeError where the
-    GPUs offer no multicast."""
+    Collective to create and to ``close()``, in an initialised process group
+    (NCCL). Raises RuntimeError where the GPUs offer no multicast."""
 
     def __init__(self, n: int, cols: int, group=None):
         import torch.distributed as dist
