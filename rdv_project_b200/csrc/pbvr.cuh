@@ -359,12 +359,14 @@ __device__ __forceinline__ float hg_eval(float cos_t, float g) {
     return __fdiv_rn(__fmul_rn(__fdiv_rn(0.25f, kPi), omg2), powf(base, 1.5f));
 }
 
+// ENC: whether the launch has an input encoding (its sampler code is
+// compiled only into those instantiations).
 // VAR = e.variant at compile time: each variant keeps only its own code
 // (PBVRT's escape term, PBVR_ENV's environment sampling), and every path
 // end (loop_end, shadow_end) is taken at one site at the top of the flight
 // loop -- the kernel measured instruction-cache bound (75 % hit rate) with
 // all three variants and these ends inlined at each of their 7 call sites.
-template <int NT, int VAR>
+template <int NT, int VAR, bool ENC>
 __global__ void __launch_bounds__(NT) pbvrt_kernel(const __grid_constant__ Params p, const __grid_constant__ ExtraT e) {
     extern __shared__ float sm[];
     float* wsm = sm;
@@ -545,7 +547,7 @@ __global__ void __launch_bounds__(NT) pbvrt_kernel(const __grid_constant__ Param
         float pt[3];
 #pragma unroll
         for (int k = 0; k < 3; ++k) pt[k] = mode == 0 ? x[k] : xs[k];
-        const float sigma = trm::extinction<NT>(p, wsm, bsm, act0, act1, pt);
+        const float sigma = trm::extinction<NT, ENC>(p, wsm, bsm, act0, act1, pt);
         if (!pending) continue;
         ++my_evals;
         if (mode == 1) {

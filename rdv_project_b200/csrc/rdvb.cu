@@ -62,8 +62,8 @@ struct DeviceInfo {
     size_t rt_wide_smem_set = 0;
     size_t pbvr_smem_set = 0;
     size_t pbvr_wide_smem_set = 0;
-    size_t pbvrt_smem_set[3] = {};       // per variant
-    size_t pbvrt_wide_smem_set[3] = {};
+    size_t pbvrt_smem_set[2][3] = {};    // per (encoding, variant)
+    size_t pbvrt_wide_smem_set[2][3] = {};
     size_t rows_smem_set = 0;
     size_t conv_tc_smem_set = 0;
     size_t conv_tma_smem_set = 0;
@@ -1633,15 +1633,22 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
         case March::kPbvrt: {
             using rdvb::pbvr::pbvrt_kernel;
             const int v = static_cast<const rdvb::pbvr::ExtraT*>(extra)->variant;
-            const void* const kernels[2][3] = {
-                {reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 0>),
-                 reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 1>),
-                 reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 2>)},
-                {reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 0>),
-                 reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 1>),
-                 reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 2>)}};
-            kernel = kernels[wide ? 1 : 0][v];
-            smem_set = wide ? &dev->pbvrt_wide_smem_set[v] : &dev->pbvrt_smem_set[v];
+            const int enc = p.enc ? 1 : 0;
+            const void* const kernels[2][2][3] = {
+                {{reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 0, false>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 1, false>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 2, false>)},
+                 {reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 0, true>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 1, true>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kThreads, 2, true>)}},
+                {{reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 0, false>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 1, false>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 2, false>)},
+                 {reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 0, true>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 1, true>),
+                  reinterpret_cast<const void*>(pbvrt_kernel<kRtWideThreads, 2, true>)}}};
+            kernel = kernels[wide ? 1 : 0][enc][v];
+            smem_set = wide ? &dev->pbvrt_wide_smem_set[enc][v] : &dev->pbvrt_smem_set[enc][v];
             name = "pbvrt_kernel";
             break;
         }

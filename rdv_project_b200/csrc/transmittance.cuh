@@ -166,13 +166,15 @@ __device__ __forceinline__ const float* eval_chain(const Params& p, const float*
 
 // extinction(x) for this thread: the chain on the 3-vector x, or on the
 // F features the input encoding samples at x (the sampler's own arithmetic,
-// sampler.cuh); an encoding without layers is the extinction itself.
-template <int T = kThreads>
+// sampler.cuh); an encoding without layers is the extinction itself. ENC =
+// false compiles the kernel without the encoding's sampler code (for
+// launches whose Params have none: a smaller instruction footprint).
+template <int T = kThreads, bool ENC = true>
 __device__ __forceinline__ float extinction(const Params& p, const float* __restrict__ wsm,
                                             const float* __restrict__ bsm, float* act0, float* act1,
                                             const float (&x)[3]) {
     const int m0 = p.n_layers > 0 ? p.layer[0].math : 0;
-    if (p.enc) {
+    if (ENC && p.enc) {
         for (int k = 0; k < p.enc_out; ++k) {
             float v = p.enc == 1 ? sampler::tensor_sample<3>(p.enc_t, p.enc_dim, p.enc_out, k, x, p.enc_clamp != 0,
                                                               p.enc_aligned != 0, p.enc_linear != 0)
