@@ -154,7 +154,7 @@ __device__ __forceinline__ float slab_exit(const float (&x)[3], const float (&w)
     return c[2] < m ? c[2] : m;
 }
 
-template <int NT>
+template <int NT, bool ENC>
 __global__ void __launch_bounds__(NT) pbvr_kernel(const __grid_constant__ Params p, const __grid_constant__ Extra e) {
     extern __shared__ float sm[];
     float* wsm = sm;
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(NT) pbvr_kernel(const __grid_constant__ Params
             if (__all_sync(0xffffffffu, ray == -2)) break;  // no lane has rays left
             continue;
         }
-        const float sigma = trm::extinction<NT>(p, wsm, bsm, act0, act1, x);
+        const float sigma = trm::extinction<NT, ENC>(p, wsm, bsm, act0, act1, x);
         if (pending) {
             ++my_evals;
             if (rng_uniform(r) >= __fdiv_rn(sigma, maj)) continue;  // null collision

@@ -58,10 +58,10 @@ struct DeviceInfo {
     size_t simt_smem_set = 0;
     size_t wino_smem_set[2] = {};
     size_t trm_smem_set = 0;
-    size_t rt_smem_set = 0;
-    size_t rt_wide_smem_set = 0;
-    size_t pbvr_smem_set = 0;
-    size_t pbvr_wide_smem_set = 0;
+    size_t rt_smem_set[2] = {};          // per encoding (absent, present)
+    size_t rt_wide_smem_set[2] = {};
+    size_t pbvr_smem_set[2] = {};
+    size_t pbvr_wide_smem_set[2] = {};
     size_t pbvrt_smem_set[2][3] = {};    // per (encoding, variant)
     size_t pbvrt_wide_smem_set[2][3] = {};
     size_t rows_smem_set = 0;
@@ -1618,18 +1618,29 @@ int launch_simt_march(rdvb::trm::Params& p, int n_layers, const int* dims, const
             smem_set = &dev->trm_smem_set;
             name = "transmittance_kernel";
             break;
-        case March::kRatioTracking:
-            kernel = wide ? reinterpret_cast<const void*>(ratiotracking_kernel<kRtWideThreads>)
-                          : reinterpret_cast<const void*>(ratiotracking_kernel<kThreads>);
-            smem_set = wide ? &dev->rt_wide_smem_set : &dev->rt_smem_set;
+        case March::kRatioTracking: {
+            // instantiations without the encoding's sampler code when there is none
+            const void* const k[2][2] = {
+                {reinterpret_cast<const void*>(ratiotracking_kernel<kThreads, false>),
+                 reinterpret_cast<const void*>(ratiotracking_kernel<kThreads, true>)},
+                {reinterpret_cast<const void*>(ratiotracking_kernel<kRtWideThreads, false>),
+                 reinterpret_cast<const void*>(ratiotracking_kernel<kRtWideThreads, true>)}};
+            kernel = k[wide ? 1 : 0][p.enc ? 1 : 0];
+            smem_set = wide ? &dev->rt_wide_smem_set[p.enc ? 1 : 0] : &dev->rt_smem_set[p.enc ? 1 : 0];
             name = "ratiotracking_kernel";
             break;
-        case March::kPbvr:
-            kernel = wide ? reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kRtWideThreads>)
-                          : reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kThreads>);
-            smem_set = wide ? &dev->pbvr_wide_smem_set : &dev->pbvr_smem_set;
+        }
+        case March::kPbvr: {
+            const void* const k[2][2] = {
+                {reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kThreads, false>),
+                 reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kThreads, true>)},
+                {reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kRtWideThreads, false>),
+                 reinterpret_cast<const void*>(rdvb::pbvr::pbvr_kernel<kRtWideThreads, true>)}};
+            kernel = k[wide ? 1 : 0][p.enc ? 1 : 0];
+            smem_set = wide ? &dev->pbvr_wide_smem_set[p.enc ? 1 : 0] : &dev->pbvr_smem_set[p.enc ? 1 : 0];
             name = "pbvr_kernel";
             break;
+        }
         case March::kPbvrt: {
             using rdvb::pbvr::pbvrt_kernel;
             const int v = static_cast<const rdvb::pbvr::ExtraT*>(extra)->variant;

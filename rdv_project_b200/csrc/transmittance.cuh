@@ -398,7 +398,7 @@ constexpr int kYieldFlights = RDVB_YIELD_FLIGHTS;
 // point and discard it), and applies the collision. The MLP -- nearly all of
 // the arithmetic -- thus runs with the lanes converged instead of once per
 // colliding lane.
-template <int NT>
+template <int NT, bool ENC>
 __global__ void __launch_bounds__(NT) ratiotracking_kernel(const __grid_constant__ Params p) {
     extern __shared__ float sm[];
     float* wsm = sm;
@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(NT) ratiotracking_kernel(const __grid_constant
             if (__all_sync(0xffffffffu, ray == -2)) break;  // no lane has rays left
             continue;
         }
-        const float sigma = extinction<NT>(p, wsm, bsm, act0, act1, x);
+        const float sigma = extinction<NT, ENC>(p, wsm, bsm, act0, act1, x);
         if (pending) {
             ++my_evals;
             T = __fmul_rn(T, __fsub_rn(1.0f, __fdiv_rn(sigma, maj)));
